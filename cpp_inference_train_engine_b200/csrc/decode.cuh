@@ -1,0 +1,141 @@
+// Batched rollout decoding over the compressed latent cache (CpuDecoder, inference.cpp:47-174,
+// absorbed form), on-device sampling (sample_token, inference.cpp:345-426) and the batched
+// rollout() of trainer.cpp:187-213.
+#pragma once
+#include "passes.cuh"
+
+namespace mm {
+
+inline void ensure_decode(Context& cx, int B, int Sc, int max_new) {
+    DecodeState& d = cx.dec;
+    if (d.B == B && d.Sc >= Sc && d.max_new >= max_new && d.arena.capacity()) return;
+    const Dims& c = cx.c;
+    MM_CUDA_CHECK(cudaStreamSynchronize(cx.stream));
+    auto plan = [&](auto& a) {
+        d.cache = a.template take<__half>(static_cast<long long>(c.L) * B * Sc * c.kvw());
+        d.pos = a.template take<int>(B);
+        d.x = a.template take<float>(static_cast<long long>(B) * c.d);
+        d.h16 = a.template take<__half>(static_cast<long long>(B) * cx.d16(c.d));
+        d.y = a.template take<float>(static_cast<long long>(B) * (c.qr + c.kvw()));
+        d.cq16 = a.template take<__half>(static_cast<long long>(B) * cx.d16(c.qr));
+        d.lat16 = a.template take<__half>(static_cast<long long>(B) * cx.d16(c.kvr));
+        d.k_rope = a.template take<float>(static_cast<long long>(B) * c.rope);
+        d.qf = a.template take<float>(static_cast<long long>(B) * c.H * c.kvw());
+        d.qf2 = a.template take<float>(static_cast<long long>(B) * c.H * c.kvw());
+        d.ctx16 = a.template take<__half>(static_cast<long long>(B) * c.H * c.kvr);
+        d.res = a.template take<float>(static_cast<long long>(B) * c.d);
+        d.h2 = a.template take<__half>(static_cast<long long>(B) * cx.d16(c.d));
+        d.gu = a.template take<__half>(static_cast<long long>(B) * cx.d16(2 * c.dff));
+        d.gated = a.template take<__half>(static_cast<long long>(B) * cx.d16(c.dff));
+        d.hf = a.template take<float>(static_cast<long long>(B) * c.d);
+        d.h3 = a.template take<__half>(static_cast<long long>(B) * cx.d16(3 * c.d));
+        d.logits = a.template take<float>(static_cast<long long>(B) * c.V);
+        d.tok = a.template take<uint16_t>(B);
+        d.seeds = a.template take<uint64_t>(B);
+        d.draw = a.template take<int>(B);
+        d.out_tok = a.template take<uint16_t>(static_cast<long long>(B) * std::max(max_new, 1));
+    };
+    d.B = B;
+    d.Sc = Sc;
+    d.max_new = max_new;
+    Sizer sz;
+    plan(sz);
+    d.arena.release();
+    d.arena.reserve(sz.used() + 4096);
+    plan(d.arena);
+}
+
+// Prefill of rows [0, B) from device prompts [B][P] (already in ws-independent storage):
+// runs the teacher-forced forward in chunks that fit the workspace, writing the cache and
+// the last-position logits into dec.logits.
+inline void prefill_rows(Context& cx, const uint16_t* d_prompts, int B, int P, int chunk_tokens) {
+    DecodeState& d = cx.dec;
+    const int per = std::max(1, chunk_tokens / P);
+    ensure_workspace(cx, std::min(B, per) * P, cx.ws.tape);
+    for (int r0 = 0; r0 < B; r0 += per) {
+        const int bc = std::min(per, B - r0);
+        MM_CUDA_CHECK(cudaMemcpyAsync(cx.ws.tokens, d_prompts + static_cast<long long>(r0) * P,
+                                      sizeof(uint16_t) * bc * P, cudaMemcpyDeviceToDevice, cx.stream));
+        forward_chunk(cx, bc, P, false, kVocabLast, false, d.cache, d.Sc, r0, d.logits + static_cast<long long>(r0) * cx.c.V);
+    }
+    std::vector<int> pos(B, P);
+    MM_CUDA_CHECK(cudaMemcpyAsync(d.pos, pos.data(), sizeof(int) * B, cudaMemcpyHostToDevice, cx.stream));
+}
+
+__global__ void advance_pos_kernel(int* pos, int B) {
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b < B) pos[b] += 1;
+}
+
+// One decode step for every row: dec.tok holds the tokens to append at dec.pos.
+inline void decode_step(Context& cx) {
+    const Dims& c = cx.c;
+    DecodeState& d = cx.dec;
+    const int B = d.B, kvw = c.kvw(), qrk = c.qr + kvw;
+    const int ld_d = cx.d16(c.d), ld_qr = cx.d16(c.qr), ld_kvr = cx.d16(c.kvr);
+    MM_LAUNCH(embed_kernel, warp_rows_grid(B), 256, 0, d.tok, cx.E(), d.x, B, c.d, c.V, cx.d_err);
+    for (int l = 0; l < c.L; ++l) {
+        const PrepLayer& p = cx.prep[l];
+        MM_LAUNCH(rmsnorm_kernel, warp_rows_grid(B), 256, 0, d.x, (long long)c.d, cx.W(l, kAttnNorm), B, c.d, c.eps,
+                  (float*)nullptr, 0LL, d.h16, (long long)ld_d, (float*)nullptr);
+        gemm(cx, B, qrk, c.d, {d.h16, ld_d, false}, {p.Wa, p.lda, true}, {d.y, qrk, kOutF32});
+        MM_LAUNCH(rmsnorm_kernel, warp_rows_grid(B), 256, 0, d.y, (long long)qrk, cx.W(l, kQNorm), B, c.qr, c.eps,
+                  (float*)nullptr, 0LL, d.cq16, (long long)ld_qr, (float*)nullptr);
+        MM_LAUNCH(rmsnorm_kernel, warp_rows_grid(B), 256, 0, d.y + c.qr, (long long)qrk, cx.W(l, kKvNorm), B, c.kvr, c.eps,
+                  (float*)nullptr, 0LL, d.lat16, (long long)ld_kvr, (float*)nullptr);
+        MM_LAUNCH(rope_key_kernel, blocks_for((long long)B * (c.rope / 2), 256), 256, 0, d.y + c.qr, (long long)qrk, c.kvr,
+                  c.rope, B, 1, d.pos, cx.cos_t, cx.sin_t, d.k_rope, (__half*)nullptr, 0LL);
+        __half* cache_l = d.cache + static_cast<long long>(l) * B * d.Sc * kvw;
+        MM_LAUNCH(cache_write_kernel, blocks_for((long long)B * kvw, 256), 256, 0, d.lat16, (long long)ld_kvr, d.k_rope, B, 1,
+                  d.pos, 0, cache_l, d.Sc, c.kvr, c.rope);
+        gemm(cx, B, c.H * kvw, c.qr, {d.cq16, ld_qr, false}, {p.Wq, p.ldq, true}, {d.qf, c.H * kvw, kOutF32});
+        MM_LAUNCH(rope_rows_kernel, warp_rows_grid(B), 256, 0, d.qf, (long long)(c.H * kvw), B, 1, d.pos, c.H, kvw, c.kvr,
+                  c.rope, cx.cos_t, cx.sin_t, 0, d.qf2, (long long)(c.H * kvw), (__half*)nullptr, 0LL);
+        {
+            const float scale = 1.0f / std::sqrt(static_cast<float>(c.qk()));
+            const size_t smem = sizeof(float) * c.H * kvw;
+            // cache rows read once (fp16) + absorbed queries in (fp32) + context out (fp16)
+            const double bytes = static_cast<double>(B) * ((cx.dec_len + 1.0) * kvw * 2 + c.H * kvw * 4.0 + c.H * c.kvr * 2.0);
+            if (c.kvr == 128)
+                MM_LAUNCH_TIMED(kKDecodeAttn, bytes, (decode_attention_kernel<128, 16>), B, 32 * c.H, smem, d.qf2, cache_l,
+                                (long long)d.Sc * kvw, d.pos, c.H, scale, d.ctx16);
+            else
+                MM_LAUNCH_TIMED(kKDecodeAttn, bytes, (decode_attention_kernel<8, 4>), B, 32 * c.H, smem, d.qf2, cache_l,
+                                (long long)d.Sc * kvw, d.pos, c.H, scale, d.ctx16);
+        }
+        {
+            GemmOutSpec o{d.res, c.d, kOutF32};
+            o.residual = d.x;
+            o.ldr = c.d;
+            gemm(cx, B, c.d, c.H * c.kvr, {d.ctx16, c.H * c.kvr, false}, {p.Wo, p.ldo, true}, o);
+        }
+        MM_LAUNCH(rmsnorm_kernel, warp_rows_grid(B), 256, 0, d.res, (long long)c.d, cx.W(l, kFfnNorm), B, c.d, c.eps,
+                  (float*)nullptr, 0LL, d.h2, (long long)ld_d, (float*)nullptr);
+        const int ld_gu = cx.d16(2 * c.dff), ld_ff = cx.d16(c.dff);
+        gemm(cx, B, 2 * c.dff, c.d, {d.h2, ld_d, false}, {p.Wgu, p.ldgu, true}, {d.gu, ld_gu, kOutF16});
+        MM_LAUNCH(swiglu_kernel, blocks_for((long long)B * c.dff, 256), 256, 0, d.gu, d.gu + c.dff, (long long)ld_gu, B,
+                  c.dff, d.gated, (long long)ld_ff);
+        {
+            GemmOutSpec o{d.x, c.d, kOutF32};
+            o.residual = d.res;
+            o.ldr = c.d;
+            gemm(cx, B, c.d, c.dff, {d.gated, ld_ff, false}, {cx.S(l, kWdown), cx.SL(l, kWdown), true}, o);
+        }
+    }
+    MM_LAUNCH(rmsnorm_kernel, warp_rows_grid(B), 256, 0, d.x, (long long)c.d, cx.FinalNorm(), B, c.d, c.eps, d.hf,
+              (long long)c.d, (__half*)nullptr, 0LL, (float*)nullptr);
+    const int ld3 = cx.d16(3 * c.d);
+    MM_LAUNCH(split3_gather_kernel, blocks_for((long long)B * c.d, 256), 256, 0, d.hf, c.d, B, 1, 0, d.h3, (long long)ld3);
+    GemmOutSpec lo{d.logits, c.V, kOutF32};
+    lo.alpha = 1.0f / kVocabScale;
+    gemm(cx, B, c.V, 3 * c.d, {d.h3, ld3, false}, {cx.E3(), cx.E3L(), false}, lo);
+    MM_LAUNCH(advance_pos_kernel, blocks_for(B, 256), 256, 0, d.pos, B);
+}
+
+inline void launch_sample(Context& cx, const float* logits, int B, float temperature, const uint64_t* seeds,
+                          const int* draw, int draw_offset, const int* active, uint16_t* out, long long out_stride) {
+    MM_LAUNCH_TIMED(kKSample, 4.0 * B * cx.c.V, sample_kernel, B, kSampleThreads, 0, logits, (long long)cx.c.V, cx.c.V,
+                    temperature, seeds, draw, draw_offset, active, out, out_stride);
+}
+
+} // namespace mm

@@ -1,0 +1,434 @@
+// C ABI of the sm_100a backend (include/mm_cuda.h, include/mm_cuda_kernels.h). Every
+// entry point validates its arguments, runs on the context's stream, waits for completion
+// and maps failures to 1 + ErrorCode with a message, as the reference's Result does.
+#include <new>
+
+#include "train.cuh"
+
+#include "../../include/mm_cuda_kernels.h"
+
+struct mm_cuda_ctx {
+    mm::Context cx;
+};
+
+namespace {
+
+template <class F> int guarded(mm_cuda_ctx* h, F&& f) {
+    if (!h) return MM_INVALID_ARGUMENT;
+    try {
+        if (h->cx.unusable) mm::fail(MM_GPU_ERROR, "Execution is unusable after a device failure");
+        MM_CUDA_CHECK(cudaSetDevice(h->cx.device));
+        f(h->cx);
+        return MM_OK;
+    } catch (const mm::Failure& e) {
+        h->cx.last_error = e.what();
+        return e.code;
+    } catch (const std::bad_alloc&) {
+        h->cx.last_error = "host allocation failed";
+        return MM_OUT_OF_MEMORY;
+    } catch (const std::exception& e) {
+        h->cx.last_error = e.what();
+        return MM_INVALID_ARGUMENT;
+    }
+}
+
+mm::Dims checked_dims(const mm_model_desc* d) {
+    if (!d) mm::fail(MM_INVALID_ARGUMENT, "null model description");
+    mm::Dims c = mm::dims_from(*d);
+    const int v[] = {c.V, c.maxS, c.L, c.d, c.H, c.nope, c.rope, c.dv, c.qr, c.kvr, c.dff};
+    for (int x : v)
+        if (x < 1 || x > 65535) mm::fail(MM_INVALID_ARGUMENT, "model dimensions must be in [1, 65535]");
+    return c;
+}
+
+// Rng of include/mini_mla/rng.hpp:7-35 (splitmix64; float uniform; Box-Muller normal).
+struct HostRng {
+    uint64_t s;
+    uint64_t next() {
+        uint64_t z = (s += 0x9e3779b97f4a7c15ULL);
+        z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ULL;
+        z = (z ^ (z >> 27)) * 0x94d049bb133111ebULL;
+        return z ^ (z >> 31);
+    }
+    float uniform() { return (static_cast<float>(next() >> 40) + 0.5F) / 16777216.0F; }
+    float normal() {
+        const float u1 = uniform();  // first draw feeds the logarithm, as the reference build does
+        const float u2 = uniform();
+        return std::sqrt(-2.0F * std::log(u1)) * std::cos(2.0F * 3.14159265358979323846F * u2);
+    }
+};
+
+void check_tokens(const mm::Context& cx, const uint16_t* t, long long n) {
+    for (long long i = 0; i < n; ++i)
+        if (t[i] >= cx.c.V) mm::fail(MM_INVALID_ARGUMENT, "Input token exceeds vocabulary");
+}
+
+} // namespace
+
+extern "C" {
+
+int64_t mm_model_parameter_count(const mm_model_desc* desc) {
+    try {
+        return mm::parameter_count(checked_dims(desc));
+    } catch (...) {
+        return -1;
+    }
+}
+
+int mm_model_init_params(const mm_model_desc* desc, uint64_t seed, float* out) {
+    try {
+        const mm::Dims c = checked_dims(desc);
+        if (!out) return MM_INVALID_ARGUMENT;
+        HostRng rng{seed};
+        auto reg = mm::registry(c);
+        long long off = 0;
+        for (size_t i = 0; i < reg.size(); ++i) {
+            auto [rows, cols, role] = reg[i];
+            // w_o and w_down (registry slots 8 and 12 of a layer) carry the residual scale.
+            bool residual = false;
+            if (i >= 2) {
+                const int slot = static_cast<int>((i - 2) % mm::kLayerParams);
+                residual = slot == mm::kWo || slot == mm::kWdown;
+            }
+            const float scale = residual ? 0.02F / std::sqrt(static_cast<float>(2 * c.L)) : 0.02F;
+            for (long long j = 0; j < static_cast<long long>(rows) * cols; ++j)
+                out[off + j] = role == 2 ? 1.0F : rng.normal() * scale;
+            off += static_cast<long long>(rows) * cols;
+        }
+        return MM_OK;
+    } catch (const mm::Failure& e) {
+        return e.code;
+    }
+}
+
+float mm_cosine_learning_rate(uint64_t done, uint64_t total, uint64_t warmup, float peak, float minimum) {
+    if (warmup && done < warmup) return peak * static_cast<float>(done + 1) / static_cast<float>(warmup);
+    if (total <= warmup) return peak;
+    double t = static_cast<double>(done - std::min(done, warmup)) / static_cast<double>(total - warmup);
+    t = std::min(std::max(t, 0.0), 1.0);
+    return peak * static_cast<float>(minimum + (1 - minimum) * 0.5 * (1 + std::cos(3.14159265358979323846 * t)));
+}
+
+int mm_cuda_create(const mm_model_desc* desc, int device, int trainable, const mm_adamw_desc* optimizer,
+                   mm_cuda_ctx** out) {
+    if (!desc || !out) return MM_INVALID_ARGUMENT;
+    *out = nullptr;
+    auto* h = new (std::nothrow) mm_cuda_ctx;
+    if (!h) return MM_OUT_OF_MEMORY;
+    int rc = guarded(h, [&](mm::Context& cx) { mm::create_context(cx, *desc, device, trainable != 0, optimizer); });
+    *out = h;  // returned even on failure so the caller can read the message
+    return rc;
+}
+
+void mm_cuda_destroy(mm_cuda_ctx* h) {
+    if (!h) return;
+    cudaSetDevice(h->cx.device);
+    if (h->cx.stream) cudaStreamSynchronize(h->cx.stream);
+    if (h->cx.nccl_comm) {
+        try {
+            mm::nccl().commDestroy(static_cast<ncclComm_t>(h->cx.nccl_comm));
+        } catch (...) {
+        }
+    }
+    if (h->cx.ev0) cudaEventDestroy(h->cx.ev0);
+    if (h->cx.ev1) cudaEventDestroy(h->cx.ev1);
+    cudaStream_t s = h->cx.stream;
+    delete h;
+    if (s) cudaStreamDestroy(s);
+}
+
+size_t mm_cuda_last_error(const mm_cuda_ctx* h, char* buf, size_t cap) {
+    if (!h) return 0;
+    const std::string& m = h->cx.last_error;
+    if (buf && cap) {
+        const size_t n = std::min(cap - 1, m.size());
+        std::memcpy(buf, m.data(), n);
+        buf[n] = 0;
+    }
+    return m.size();
+}
+
+int mm_cuda_upload_params(mm_cuda_ctx* h, const float* params, const float* m, const float* v, uint64_t steps) {
+    return guarded(h, [&](mm::Context& cx) {
+        if (!params) mm::fail(MM_INVALID_ARGUMENT, "null parameters");
+        mm::upload_params(cx, params, m, v, steps);
+    });
+}
+
+int mm_cuda_download(mm_cuda_ctx* h, float* params, float* grads, float* m, float* v, uint64_t* steps) {
+    return guarded(h, [&](mm::Context& cx) {
+        mm::download(cx, params, grads, m, v);
+        if (steps) *steps = cx.steps;
+    });
+}
+
+int mm_cuda_forward_logits(mm_cuda_ctx* h, const uint16_t* tokens, int batch, int seq, float* logits) {
+    return guarded(h, [&](mm::Context& cx) {
+        if (!tokens || !logits || batch < 1 || seq < 1 || seq > cx.c.maxS)
+            mm::fail(MM_INVALID_ARGUMENT, "Input batch or sequence shape is invalid");
+        check_tokens(cx, tokens, static_cast<long long>(batch) * seq);
+        const int per = std::max(1, mm::chunk_tokens_default() / seq);
+        mm::ensure_workspace(cx, std::min(batch, per) * seq, cx.ws.tape);
+        for (int r0 = 0; r0 < batch; r0 += per) {
+            const int bc = std::min(per, batch - r0);
+            const long long T = static_cast<long long>(bc) * seq;
+            MM_CUDA_CHECK(cudaMemcpyAsync(cx.ws.tokens, tokens + static_cast<long long>(r0) * seq, T * 2,
+                                          cudaMemcpyHostToDevice, cx.stream));
+            mm::forward_chunk(cx, bc, seq, false, mm::kVocabAll, false, nullptr, 0, 0, nullptr);
+            MM_CUDA_CHECK(cudaMemcpyAsync(logits + static_cast<long long>(r0) * seq * cx.c.V, cx.ws.logits,
+                                          T * cx.c.V * 4, cudaMemcpyDeviceToHost, cx.stream));
+        }
+        mm::check_device(cx, "forward");
+    });
+}
+
+int mm_cuda_log_probs(mm_cuda_ctx* h, const uint16_t* input, const uint16_t* target, int batch, int seq, float* out) {
+    return guarded(h, [&](mm::Context& cx) {
+        if (!input || !target || !out || batch < 1 || seq < 1 || seq > cx.c.maxS)
+            mm::fail(MM_INVALID_ARGUMENT, "Input batch or sequence shape is invalid");
+        check_tokens(cx, input, static_cast<long long>(batch) * seq);
+        check_tokens(cx, target, static_cast<long long>(batch) * seq);
+        mm::log_probs_host(cx, input, target, batch, seq, out);
+    });
+}
+
+int mm_cuda_zero_grad(mm_cuda_ctx* h) {
+    return guarded(h, [&](mm::Context& cx) {
+        if (!cx.trainable) mm::fail(MM_INVALID_ARGUMENT, "Inference execution has no optimizer");
+        MM_CUDA_CHECK(cudaMemsetAsync(cx.g, 0, sizeof(float) * cx.P_dev, cx.stream));
+        MM_CUDA_CHECK(cudaStreamSynchronize(cx.stream));
+    });
+}
+
+int mm_cuda_accumulate(mm_cuda_ctx* h, const uint16_t* input, const uint16_t* target, const float* coef, int batch,
+                       int seq, double* loss) {
+    return guarded(h, [&](mm::Context& cx) {
+        if (!cx.trainable) mm::fail(MM_INVALID_ARGUMENT, "Inference execution has no optimizer");
+        if (!input || !target || !coef || batch < 1 || seq < 1 || seq > cx.c.maxS)
+            mm::fail(MM_INVALID_ARGUMENT, "Input batch or sequence shape is invalid");
+        const long long N = static_cast<long long>(batch) * seq;
+        check_tokens(cx, input, N);
+        check_tokens(cx, target, N);
+        for (long long i = 0; i < N; ++i)
+            if (!std::isfinite(coef[i])) mm::fail(MM_INVALID_ARGUMENT, "Invalid target or loss coefficient");
+        const int per = std::max(1, mm::chunk_tokens_default() / seq);
+        mm::ensure_workspace(cx, std::min(batch, per) * seq, true);
+        mm::Workspace& w = cx.ws;
+        double total = 0;
+        std::vector<float> lp;
+        for (int r0 = 0; r0 < batch; r0 += per) {
+            const int bc = std::min(per, batch - r0);
+            const long long T = static_cast<long long>(bc) * seq, off = static_cast<long long>(r0) * seq;
+            MM_CUDA_CHECK(cudaMemcpyAsync(w.tokens, input + off, T * 2, cudaMemcpyHostToDevice, cx.stream));
+            MM_CUDA_CHECK(cudaMemcpyAsync(w.targets, target + off, T * 2, cudaMemcpyHostToDevice, cx.stream));
+            MM_CUDA_CHECK(cudaMemcpyAsync(w.coef, coef + off, T * 4, cudaMemcpyHostToDevice, cx.stream));
+            mm::forward_chunk(cx, bc, seq, true, mm::kVocabAll, true, nullptr, 0, 0, nullptr);
+            lp.resize(static_cast<size_t>(T));
+            MM_CUDA_CHECK(cudaMemcpyAsync(lp.data(), w.lp, T * 4, cudaMemcpyDeviceToHost, cx.stream));
+            MM_CUDA_CHECK(cudaMemsetAsync(&cx.d_sums->max_coef_bits, 0, 4, cx.stream));
+            MM_LAUNCH(mm::absmax_kernel, mm::blocks_for(T, 256), 256, 0, w.coef, static_cast<int>(T),
+                      &cx.d_sums->max_coef_bits);
+            MM_LAUNCH(mm::grad_scale_kernel, 1, 1, 0, cx.d_sums, cx.d_scale);
+            mm::backward_chunk(cx, bc, seq);
+            MM_CUDA_CHECK(cudaStreamSynchronize(cx.stream));
+            for (long long i = 0; i < T; ++i) total += static_cast<double>(coef[off + i]) * -static_cast<double>(lp[i]);
+        }
+        mm::check_device(cx, "accumulate");
+        if (!std::isfinite(total)) mm::fail(MM_NUMERICAL_ERROR, "Nonfinite logits or loss");
+        if (loss) *loss = total;
+    });
+}
+
+int mm_cuda_update(mm_cuda_ctx* h, float lr, double* grad_norm) {
+    return guarded(h, [&](mm::Context& cx) {
+        const double n = mm::adamw_update(cx, lr);
+        if (grad_norm) *grad_norm = n;
+    });
+}
+
+int mm_cuda_prefill_batch(mm_cuda_ctx* h, const uint16_t* prompts, int batch, int prompt_len, float* logits) {
+    return guarded(h, [&](mm::Context& cx) {
+        if (!prompts || batch < 1 || prompt_len < 1 || prompt_len > cx.c.maxS)
+            mm::fail(MM_INVALID_ARGUMENT, "Prompt exceeds context or is empty");
+        check_tokens(cx, prompts, static_cast<long long>(batch) * prompt_len);
+        mm::ensure_decode(cx, batch, cx.c.maxS, 1);
+        uint16_t* d = static_cast<uint16_t*>(cx.stage.get(static_cast<size_t>(batch) * prompt_len * 2));
+        MM_CUDA_CHECK(cudaMemcpyAsync(d, prompts, static_cast<size_t>(batch) * prompt_len * 2, cudaMemcpyHostToDevice, cx.stream));
+        mm::prefill_rows(cx, d, batch, prompt_len, mm::chunk_tokens_default());
+        if (logits)
+            MM_CUDA_CHECK(cudaMemcpyAsync(logits, cx.dec.logits, sizeof(float) * batch * cx.c.V, cudaMemcpyDeviceToHost, cx.stream));
+        cx.dec_len = prompt_len;
+        mm::check_device(cx, "prefill");
+    });
+}
+
+int mm_cuda_decode_batch(mm_cuda_ctx* h, const uint16_t* tokens, int batch, float* logits) {
+    return guarded(h, [&](mm::Context& cx) {
+        if (!tokens || batch != cx.dec.B || cx.dec_len < 1)
+            mm::fail(MM_INVALID_ARGUMENT, "Decode requires current-weight prefill, available context, and a valid token");
+        if (cx.dec_len >= cx.c.maxS) mm::fail(MM_INVALID_ARGUMENT, "Decode requires available context");
+        check_tokens(cx, tokens, batch);
+        MM_CUDA_CHECK(cudaMemcpyAsync(cx.dec.tok, tokens, static_cast<size_t>(batch) * 2, cudaMemcpyHostToDevice, cx.stream));
+        mm::decode_step(cx);
+        if (logits)
+            MM_CUDA_CHECK(cudaMemcpyAsync(logits, cx.dec.logits, sizeof(float) * batch * cx.c.V, cudaMemcpyDeviceToHost, cx.stream));
+        cx.dec_len += 1;
+        mm::check_device(cx, "decode");
+    });
+}
+
+int mm_cuda_sample(mm_cuda_ctx* h, const float* logits, int batch, float temperature, const uint64_t* seeds,
+                   const int32_t* draw_index, uint16_t* out) {
+    return guarded(h, [&](mm::Context& cx) {
+        if (!logits || !seeds || !out || batch < 1 || !std::isfinite(temperature) || temperature < 0)
+            mm::fail(MM_INVALID_ARGUMENT, "Invalid generation settings");
+        for (long long i = 0; i < static_cast<long long>(batch) * cx.c.V; ++i)
+            if (!std::isfinite(logits[i])) mm::fail(MM_NUMERICAL_ERROR, "Invalid sampler logits");
+        const size_t lb = sizeof(float) * batch * cx.c.V;
+        char* base = static_cast<char*>(cx.stage.get(lb + static_cast<size_t>(batch) * 16 + 1024));
+        float* d_log = reinterpret_cast<float*>(base);
+        uint64_t* d_seed = reinterpret_cast<uint64_t*>(base + mm::round_up(static_cast<long long>(lb), 256));
+        int* d_draw = reinterpret_cast<int*>(reinterpret_cast<char*>(d_seed) + mm::round_up(batch * 8LL, 256));
+        uint16_t* d_out = reinterpret_cast<uint16_t*>(reinterpret_cast<char*>(d_draw) + mm::round_up(batch * 4LL, 256));
+        MM_CUDA_CHECK(cudaMemcpyAsync(d_log, logits, lb, cudaMemcpyHostToDevice, cx.stream));
+        MM_CUDA_CHECK(cudaMemcpyAsync(d_seed, seeds, batch * 8, cudaMemcpyHostToDevice, cx.stream));
+        if (draw_index) MM_CUDA_CHECK(cudaMemcpyAsync(d_draw, draw_index, batch * 4, cudaMemcpyHostToDevice, cx.stream));
+        mm::launch_sample(cx, d_log, batch, temperature, d_seed, draw_index ? d_draw : nullptr, 0, nullptr, d_out, 1);
+        MM_CUDA_CHECK(cudaMemcpyAsync(out, d_out, batch * 2, cudaMemcpyDeviceToHost, cx.stream));
+        mm::check_device(cx, "sample");
+    });
+}
+
+int mm_cuda_rollout(mm_cuda_ctx* h, const uint16_t* prompts, int n, int prompt_len, int completion_tokens, int sequence,
+                    uint16_t eos, uint16_t pad, const uint64_t* seeds, float temperature, uint16_t* out_tokens,
+                    int32_t* out_len, uint16_t* out_input, uint16_t* out_target, float* out_mask, float* out_old_lp) {
+    return guarded(h, [&](mm::Context& cx) {
+        if (!prompts || !seeds || !out_tokens || !out_len) mm::fail(MM_INVALID_ARGUMENT, "null rollout buffer");
+        mm::rollout(cx, prompts, n, prompt_len, completion_tokens, sequence, eos, pad, seeds, temperature, out_tokens,
+                    out_len, out_input, out_target, out_mask, out_old_lp);
+        cx.dec_len = 0;
+    });
+}
+
+int mm_cuda_grpo_coefficients(mm_cuda_ctx* h, const float* lp, const float* old_lp, const float* ref_lp,
+                              const float* mask, const float* rewards, int n, int seq, int group_size, int64_t n_total,
+                              float clip, float klc, float* coefficients, float* advantages, double* loss, double* kl) {
+    return guarded(h, [&](mm::Context& cx) {
+        if (!lp || !old_lp || !ref_lp || !mask || !rewards || !coefficients || n < 1 || seq < 1 || group_size < 2 ||
+            n % group_size || n_total < n)
+            mm::fail(MM_INVALID_ARGUMENT, "Invalid reward group");
+        if (!std::isfinite(clip) || clip <= 0 || clip >= 1 || !std::isfinite(klc) || klc < 0)
+            mm::fail(MM_NUMERICAL_ERROR, "Invalid or unbounded GRPO token statistics");
+        const long long T = static_cast<long long>(n) * seq;
+        std::vector<int> sup(n, 0);
+        for (int i = 0; i < n; ++i)
+            for (int t = 0; t < seq; ++t) sup[i] += mask[static_cast<long long>(i) * seq + t] == 1.f ? 1 : 0;
+        const long long fb = mm::round_up(T * 4, 256);
+        char* base = static_cast<char*>(cx.stage.get(static_cast<size_t>(fb * 5 + mm::round_up(n * 4LL, 256) * 3 + 1024)));
+        float* d_lp = reinterpret_cast<float*>(base);
+        float* d_old = reinterpret_cast<float*>(base + fb);
+        float* d_ref = reinterpret_cast<float*>(base + 2 * fb);
+        float* d_mask = reinterpret_cast<float*>(base + 3 * fb);
+        float* d_coef = reinterpret_cast<float*>(base + 4 * fb);
+        float* d_rew = reinterpret_cast<float*>(base + 5 * fb);
+        float* d_adv = d_rew + mm::round_up(n, 64);
+        int* d_sup = reinterpret_cast<int*>(d_adv + mm::round_up(n, 64));
+        MM_CUDA_CHECK(cudaMemcpyAsync(d_lp, lp, T * 4, cudaMemcpyHostToDevice, cx.stream));
+        MM_CUDA_CHECK(cudaMemcpyAsync(d_old, old_lp, T * 4, cudaMemcpyHostToDevice, cx.stream));
+        MM_CUDA_CHECK(cudaMemcpyAsync(d_ref, ref_lp, T * 4, cudaMemcpyHostToDevice, cx.stream));
+        MM_CUDA_CHECK(cudaMemcpyAsync(d_mask, mask, T * 4, cudaMemcpyHostToDevice, cx.stream));
+        MM_CUDA_CHECK(cudaMemcpyAsync(d_rew, rewards, n * 4, cudaMemcpyHostToDevice, cx.stream));
+        MM_CUDA_CHECK(cudaMemcpyAsync(d_sup, sup.data(), n * 4, cudaMemcpyHostToDevice, cx.stream));
+        MM_CUDA_CHECK(cudaMemsetAsync(cx.d_any, 0, 4, cx.stream));
+        MM_CUDA_CHECK(cudaMemsetAsync(cx.d_sums, 0, sizeof(mm::GrpoSums), cx.stream));
+        MM_LAUNCH(mm::advantages_kernel, mm::blocks_for(n / group_size, 128), 128, 0, d_rew, n / group_size, group_size,
+                  1e-6f, d_adv, cx.d_any);
+        MM_LAUNCH(mm::grpo_coef_kernel, mm::blocks_for(T, 256), 256, 0, d_lp, d_old, d_ref, d_mask, d_adv, d_sup,
+                  static_cast<int>(T), seq, static_cast<double>(n_total), clip, klc, d_coef, cx.d_sums);
+        mm::GrpoSums sums{};
+        MM_CUDA_CHECK(cudaMemcpyAsync(coefficients, d_coef, T * 4, cudaMemcpyDeviceToHost, cx.stream));
+        if (advantages) MM_CUDA_CHECK(cudaMemcpyAsync(advantages, d_adv, n * 4, cudaMemcpyDeviceToHost, cx.stream));
+        MM_CUDA_CHECK(cudaMemcpyAsync(&sums, cx.d_sums, sizeof(sums), cudaMemcpyDeviceToHost, cx.stream));
+        mm::check_device(cx, "grpo_coefficients");
+        if (sums.rejected) mm::fail(MM_NUMERICAL_ERROR, "Invalid or unbounded GRPO token statistics");
+        if (loss) *loss = sums.loss;
+        if (kl) *kl = sums.kl;
+    });
+}
+
+int mm_cuda_grpo_step(mm_cuda_ctx* policy, mm_cuda_ctx* reference, const uint16_t* input, const uint16_t* target,
+                      const float* mask, const float* old_lp, const float* rewards, int n, int seq, int group_size,
+                      int64_t n_total, float clip, float klc, float lr, mm_step_result* out) {
+    if (!reference) return MM_INVALID_ARGUMENT;
+    return guarded(policy, [&](mm::Context& cx) {
+        if (!input || !target || !mask || !old_lp || !rewards || !out) mm::fail(MM_INVALID_ARGUMENT, "null GRPO buffer");
+        if (reference->cx.unusable) mm::fail(MM_GPU_ERROR, "reference execution is unusable");
+        *out = mm::grpo_step(cx, reference->cx, input, target, mask, old_lp, rewards, n, seq, group_size, n_total, clip,
+                             klc, lr);
+    });
+}
+
+int mm_cuda_nccl_unique_id(char out[128]) {
+    try {
+        ncclUniqueId id;
+        if (mm::nccl().getUniqueId(&id) != ncclSuccess) return MM_GPU_ERROR;
+        std::memcpy(out, &id, sizeof(id) < 128 ? sizeof(id) : 128);
+        return MM_OK;
+    } catch (const mm::Failure& e) {
+        return e.code;
+    }
+}
+
+int mm_cuda_init_comm(mm_cuda_ctx* h, int rank, int world, const char id[128]) {
+    return guarded(h, [&](mm::Context& cx) {
+        if (world < 1 || rank < 0 || rank >= world || !id) mm::fail(MM_INVALID_ARGUMENT, "invalid rank/world");
+        if (world == 1) return;
+        ncclUniqueId uid;
+        std::memcpy(&uid, id, sizeof(uid));
+        ncclComm_t comm;
+        MM_NCCL_CHECK(mm::nccl().commInitRank(&comm, world, uid, rank));
+        cx.nccl_comm = comm;
+        cx.rank = rank;
+        cx.world = world;
+    });
+}
+
+int64_t mm_cuda_kernel_launches(const mm_cuda_ctx* h) { return h ? h->cx.launches : -1; }
+
+// ---------------------------------------------------------------- include/mm_cuda_kernels.h
+
+int mm_cuda_profile(mm_cuda_ctx* h, int enable, double* ms, int64_t* calls, double* work) {
+    return guarded(h, [&](mm::Context& cx) {
+        cx.prof_resolve();
+        for (int i = 0; i < mm::kProfTags; ++i) {
+            if (ms) ms[i] = cx.prof.ms[i];
+            if (calls) calls[i] = cx.prof.calls[i];
+            if (work) work[i] = cx.prof.work[i];
+        }
+        if (enable >= 0) {
+            cx.profiling = enable != 0;
+            cx.prof = mm::Profile{};
+        }
+    });
+}
+
+int mm_cuda_gemm_f16(mm_cuda_ctx* h, int M, int N, int K, const void* a, int64_t lda, int a_mn, const void* b,
+                     int64_t ldb, int b_mn, void* out, int64_t ldc, int out_kind, float alpha, const float* residual,
+                     int64_t ldr, int bf16) {
+    return guarded(h, [&](mm::Context& cx) {
+        if (M < 1 || N < 1 || K < 1 || !a || !b || !out || out_kind < 0 || out_kind > 3)
+            mm::fail(MM_INVALID_ARGUMENT, "invalid GEMM arguments");
+        mm::GemmOutSpec o{out, ldc, out_kind};
+        o.alpha = alpha;
+        o.residual = residual;
+        o.ldr = ldr;
+        mm::gemm(cx, M, N, K, {a, lda, a_mn != 0}, {b, ldb, b_mn != 0}, o, bf16 != 0);
+        mm::check_device(cx, "gemm");
+    });
+}
+
+int mm_cuda_stream(mm_cuda_ctx* h, void** stream) {
+    return guarded(h, [&](mm::Context& cx) { *stream = cx.stream; });
+}
+
+} // extern "C"

@@ -1,0 +1,359 @@
+// Teacher-forced forward and backward passes over a chunk of whole sequences
+// (Model::forward / Model::backward, src/model/model.cpp:76-245), tensor-core GEMMs with
+// fp16 operands and fp32 accumulation, fp32 residual stream and norms, an FP32-accurate
+// tied vocabulary head.
+#pragma once
+#include "setup.cuh"
+
+namespace mm {
+
+// Writes the normalised latent and rotated rope key of token rows into the decode cache:
+// row t -> sequence row0 + t / S at position (pos ? pos[t / S] : 0) + t % S.
+__global__ void cache_write_kernel(const __half* __restrict__ ckv, long long ldckv,
+                                   const float* __restrict__ k_rope, int T, int S,
+                                   const int* __restrict__ pos, int row0, __half* __restrict__ cache,
+                                   int Sc, int kvr, int rope) {
+    const int kvw = kvr + rope;
+    const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (idx >= static_cast<long long>(T) * kvw) return;
+    const int t = static_cast<int>(idx / kvw), j = static_cast<int>(idx % kvw);
+    const int seq = t / S;
+    const int p = (pos ? pos[seq] : 0) + t % S;
+    if (p >= Sc) return;
+    __half* dst = cache + (static_cast<long long>(row0 + seq) * Sc + p) * kvw;
+    dst[j] = j < kvr ? ckv[t * ldckv + j] : __float2half_rn(k_rope[t * rope + (j - kvr)]);
+}
+
+// h3 rows for the vocabulary head from fp32 rows in[t * mul + add].
+__global__ void split3_gather_kernel(const float* __restrict__ h, int d, int T, int mul, int add,
+                                     __half* __restrict__ h3, long long ld3) {
+    const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (idx >= static_cast<long long>(T) * d) return;
+    const int t = static_cast<int>(idx / d), j = static_cast<int>(idx % d);
+    const float v = h[(static_cast<long long>(t) * mul + add) * d + j];
+    const __half hi = __float2half_rn(v);
+    const __half lo = __float2half_rn(v - __half2float(hi));
+    h3[t * ld3 + j] = hi;
+    h3[t * ld3 + d + j] = lo;
+    h3[t * ld3 + 2 * d + j] = hi;
+}
+
+template <class A> void plan_workspace(Context& cx, A& a, int T, bool tape) {
+    Workspace& w = cx.ws;
+    const Dims& c = cx.c;
+    const long long t = T;
+    const int nl = tape ? c.L : 1;
+    w.T = T;
+    w.tape = tape;
+    w.layers.assign(nl, LayerBuf{});
+    for (int l = 0; l < nl; ++l) {
+        LayerBuf& b = w.layers[l];
+        b.x_in = a.template take<float>(t * c.d);
+        b.h = a.template take<__half>(t * cx.d16(c.d));
+        b.raw_cq = a.template take<float>(t * c.qr);
+        b.cq = a.template take<__half>(t * cx.d16(c.qr));
+        b.q = a.template take<__half>(t * c.H * c.qk());
+        b.kvp = a.template take<float>(t * c.kvw());
+        b.ckv = a.template take<__half>(t * cx.d16(c.kvr));
+        b.k_rope = a.template take<float>(t * c.rope);
+        b.k = a.template take<__half>(t * c.H * c.qk());
+        b.v = a.template take<__half>(t * c.aw());
+        b.ao = a.template take<__half>(t * c.aw());
+        b.lse = a.template take<float>(t * c.H);
+        b.res = a.template take<float>(t * c.d);
+        b.h2 = a.template take<__half>(t * cx.d16(c.d));
+        b.gate = a.template take<__half>(t * cx.d16(c.dff));
+        b.up = a.template take<__half>(t * cx.d16(c.dff));
+        b.gated = a.template take<__half>(t * cx.d16(c.dff));
+    }
+    w.x_out = a.template take<float>(t * c.d);
+    w.hf = a.template take<float>(t * c.d);
+    w.h3 = a.template take<__half>(t * cx.d16(3 * c.d));
+    w.logits = a.template take<float>(t * c.V);
+    w.lp = a.template take<float>(t);
+    w.lse_v = a.template take<float>(t);
+    w.tokens = a.template take<uint16_t>(t);
+    w.targets = a.template take<uint16_t>(t);
+    w.mask = a.template take<float>(t);
+    w.coef = a.template take<float>(t);
+    w.old_lp = a.template take<float>(t);
+    w.ref_lp = a.template take<float>(t);
+    w.q_pre = a.template take<float>(t * c.H * c.qk());
+    w.knope = a.template take<float>(t * c.H * c.nope);
+    if (tape) {
+        w.dy = a.template take<float>(t * c.d);
+        w.dgated = a.template take<float>(t * c.dff);
+        w.dh2 = a.template take<float>(t * c.d);
+        w.dres = a.template take<float>(t * c.d);
+        w.dao = a.template take<float>(t * c.aw());
+        w.dq = a.template take<float>(t * c.H * c.qk());
+        w.dk = a.template take<float>(t * c.H * c.qk());
+        w.dv = a.template take<float>(t * c.aw());
+        w.drope = a.template take<float>(t * c.rope);
+        w.drope2 = a.template take<float>(t * c.rope);
+        w.dckv = a.template take<float>(t * c.kvr);
+        w.dkvraw = a.template take<float>(t * c.kvr);
+        w.dh = a.template take<float>(t * c.d);
+        w.dcq = a.template take<float>(t * c.qr);
+        w.Dd = a.template take<float>(t * c.H);
+        w.dy16 = a.template take<__half>(t * cx.d16(c.d));
+        w.dg16 = a.template take<__half>(t * cx.d16(c.dff));
+        w.du16 = a.template take<__half>(t * cx.d16(c.dff));
+        w.dres16 = a.template take<__half>(t * cx.d16(c.d));
+        w.dq16 = a.template take<__half>(t * cx.d16(c.H * c.qk()));
+        w.dkn16 = a.template take<__half>(t * cx.d16(c.H * c.nope));
+        w.dv16 = a.template take<__half>(t * cx.d16(c.aw()));
+        w.dkvp16 = a.template take<__half>(t * cx.d16(c.kvw()));
+        w.draw16 = a.template take<__half>(t * cx.d16(c.qr));
+        w.g16 = a.template take<__half>(t * c.V);
+    }
+}
+
+// Ensures the chunk workspace holds T tokens (and a tape when requested).
+inline void ensure_workspace(Context& cx, int T, bool tape) {
+    if (cx.ws.T >= T && (cx.ws.tape || !tape) && cx.ws_arena.capacity()) return;
+    if (tape && !cx.trainable) fail(MM_INVALID_ARGUMENT, "backward needs a trainable context");
+    MM_CUDA_CHECK(cudaStreamSynchronize(cx.stream));
+    Sizer sz;
+    plan_workspace(cx, sz, T, tape);
+    cx.ws_arena.release();
+    cx.ws_arena.reserve(sz.used() + 4096);
+    plan_workspace(cx, cx.ws_arena, T, tape);
+}
+
+#define MM_LAUNCH_CX(ctx, kernel, grid, block, smem, ...)                 \
+    do {                                                                 \
+        kernel<<<(grid), (block), (smem), (ctx).stream>>>(__VA_ARGS__);  \
+        ++(ctx).launches;                                                \
+    } while (0)
+#define MM_LAUNCH(kernel, grid, block, smem, ...) MM_LAUNCH_CX(cx, kernel, grid, block, smem, __VA_ARGS__)
+// Launch recorded under a kernel class with its algorithmic work.
+#define MM_LAUNCH_TIMED(tag, work, kernel, grid, block, smem, ...)       \
+    do {                                                                 \
+        cudaEvent_t t0_ = cx.prof_begin();                               \
+        MM_LAUNCH(kernel, grid, block, smem, __VA_ARGS__);               \
+        cx.prof_end(tag, t0_, work);                                     \
+    } while (0)
+
+inline unsigned warp_rows_grid(int rows) { return blocks_for(static_cast<long long>(rows) * 32, 256); }
+
+inline void launch_flash_fwd(Context& cx, const LayerBuf& b, int Bc, int S) {
+    const Dims& c = cx.c;
+    dim3 grid((S + kAttTile - 1) / kAttTile, c.H, Bc);
+    const float scale = 1.0f / std::sqrt(static_cast<float>(c.qk()));
+    // causal pairs x (qk + dv) multiply-adds
+    const double work = 2.0 * Bc * c.H * (S * (S + 1.0) / 2.0) * (c.qk() + c.dv);
+    if (c.qk() == 64) MM_LAUNCH_TIMED(kKFlashFwd, work, (flash_fwd_kernel<64, 64>), grid, 64, 0, b.q, b.k, b.v, S, c.H, scale, b.ao, b.lse);
+    else MM_LAUNCH_TIMED(kKFlashFwd, work, (flash_fwd_kernel<16, 16>), grid, 64, 0, b.q, b.k, b.v, S, c.H, scale, b.ao, b.lse);
+}
+
+enum VocabMode { kVocabNone, kVocabAll, kVocabLast };
+
+// Forward over ws.tokens [Bc*S]. tape: keep every layer's activations. cache: write the
+// latent/rope cache of rows [row0, row0 + Bc) (prefill). Vocabulary head:
+//   kVocabAll  logits [T][V] into ws.logits and, with targets, lp/lse into ws.lp/ws.lse_v;
+//   kVocabLast logits of each sequence's last position into last_logits [Bc][V].
+inline void forward_chunk(Context& cx, int Bc, int S, bool tape, VocabMode vm, bool with_targets,
+                          __half* cache, int Sc, int row0, float* last_logits) {
+    const Dims& c = cx.c;
+    Workspace& w = cx.ws;
+    const int T = Bc * S;
+    const int qk = c.qk(), kvw = c.kvw();
+    const int ld_d = cx.d16(c.d), ld_qr = cx.d16(c.qr), ld_kvr = cx.d16(c.kvr), ld_ff = cx.d16(c.dff);
+    MM_LAUNCH(embed_kernel, warp_rows_grid(T), 256, 0, w.tokens, cx.E(), w.layers[0].x_in, T, c.d, c.V, cx.d_err);
+    for (int l = 0; l < c.L; ++l) {
+        LayerBuf& b = w.layers[tape ? l : 0];
+        float* x_next = tape ? (l + 1 < c.L ? w.layers[l + 1].x_in : w.x_out) : (l + 1 < c.L ? b.x_in : w.x_out);
+        // attention block
+        MM_LAUNCH(rmsnorm_kernel, warp_rows_grid(T), 256, 0, b.x_in, (long long)c.d, cx.W(l, kAttnNorm), T, c.d, c.eps,
+                  (float*)nullptr, 0LL, b.h, (long long)ld_d, (float*)nullptr);
+        gemm(cx, T, c.qr, c.d, {b.h, ld_d, false}, {cx.S(l, kWdq), cx.SL(l, kWdq), true}, {b.raw_cq, c.qr, kOutF32});
+        MM_LAUNCH(rmsnorm_kernel, warp_rows_grid(T), 256, 0, b.raw_cq, (long long)c.qr, cx.W(l, kQNorm), T, c.qr, c.eps,
+                  (float*)nullptr, 0LL, b.cq, (long long)ld_qr, (float*)nullptr);
+        gemm(cx, T, c.H * qk, c.qr, {b.cq, ld_qr, false}, {cx.S(l, kWuq), cx.SL(l, kWuq), true}, {w.q_pre, c.H * qk, kOutF32});
+        MM_LAUNCH(rope_rows_kernel, warp_rows_grid(T), 256, 0, w.q_pre, (long long)(c.H * qk), T, S, (const int*)nullptr,
+                  c.H, qk, c.nope, c.rope, cx.cos_t, cx.sin_t, 0, (float*)nullptr, 0LL, b.q, (long long)(c.H * qk));
+        gemm(cx, T, kvw, c.d, {b.h, ld_d, false}, {cx.S(l, kWdkv), cx.SL(l, kWdkv), true}, {b.kvp, kvw, kOutF32});
+        MM_LAUNCH(rmsnorm_kernel, warp_rows_grid(T), 256, 0, b.kvp, (long long)kvw, cx.W(l, kKvNorm), T, c.kvr, c.eps,
+                  (float*)nullptr, 0LL, b.ckv, (long long)ld_kvr, (float*)nullptr);
+        MM_LAUNCH(rope_key_kernel, blocks_for((long long)T * (c.rope / 2), 256), 256, 0, b.kvp, (long long)kvw, c.kvr,
+                  c.rope, T, S, (const int*)nullptr, cx.cos_t, cx.sin_t, b.k_rope, (__half*)nullptr, 0LL);
+        if (cache)
+            MM_LAUNCH(cache_write_kernel, blocks_for((long long)T * kvw, 256), 256, 0, b.ckv, (long long)ld_kvr, b.k_rope,
+                      T, S, (const int*)nullptr, row0, cache + (long long)l * cx.dec.B * Sc * kvw, Sc, c.kvr, c.rope);
+        gemm(cx, T, c.H * c.nope, c.kvr, {b.ckv, ld_kvr, false}, {cx.S(l, kWuk), cx.SL(l, kWuk), true},
+             {w.knope, c.H * c.nope, kOutF32});
+        MM_LAUNCH(assemble_k_kernel, blocks_for((long long)T * c.H * qk, 256), 256, 0, w.knope, (long long)(c.H * c.nope),
+                  b.k_rope, T, c.H, c.nope, c.rope, b.k, (long long)(c.H * qk));
+        gemm(cx, T, c.aw(), c.kvr, {b.ckv, ld_kvr, false}, {cx.S(l, kWuv), cx.SL(l, kWuv), true}, {b.v, c.aw(), kOutF16});
+        launch_flash_fwd(cx, b, Bc, S);
+        {
+            GemmOutSpec o{b.res, c.d, kOutF32};
+            o.residual = b.x_in;
+            o.ldr = c.d;
+            gemm(cx, T, c.d, c.aw(), {b.ao, c.aw(), false}, {cx.S(l, kWo), cx.SL(l, kWo), true}, o);
+        }
+        // feed-forward block
+        MM_LAUNCH(rmsnorm_kernel, warp_rows_grid(T), 256, 0, b.res, (long long)c.d, cx.W(l, kFfnNorm), T, c.d, c.eps,
+                  (float*)nullptr, 0LL, b.h2, (long long)ld_d, (float*)nullptr);
+        gemm(cx, T, c.dff, c.d, {b.h2, ld_d, false}, {cx.S(l, kWgate), cx.SL(l, kWgate), true}, {b.gate, ld_ff, kOutF16});
+        gemm(cx, T, c.dff, c.d, {b.h2, ld_d, false}, {cx.S(l, kWup), cx.SL(l, kWup), true}, {b.up, ld_ff, kOutF16});
+        MM_LAUNCH(swiglu_kernel, blocks_for((long long)T * c.dff, 256), 256, 0, b.gate, b.up, (long long)ld_ff, T, c.dff,
+                  b.gated, (long long)ld_ff);
+        {
+            GemmOutSpec o{x_next, c.d, kOutF32};
+            o.residual = b.res;
+            o.ldr = c.d;
+            gemm(cx, T, c.d, c.dff, {b.gated, ld_ff, false}, {cx.S(l, kWdown), cx.SL(l, kWdown), true}, o);
+        }
+    }
+    if (vm == kVocabNone) return;
+    MM_LAUNCH(rmsnorm_kernel, warp_rows_grid(T), 256, 0, w.x_out, (long long)c.d, cx.FinalNorm(), T, c.d, c.eps,
+              w.hf, (long long)c.d, (__half*)nullptr, 0LL, (float*)nullptr);
+    const int ld3 = cx.d16(3 * c.d);
+    GemmOutSpec lo{nullptr, c.V, kOutF32};
+    lo.alpha = 1.0f / kVocabScale;
+    if (vm == kVocabAll) {
+        MM_LAUNCH(split3_gather_kernel, blocks_for((long long)T * c.d, 256), 256, 0, w.hf, c.d, T, 1, 0, w.h3, (long long)ld3);
+        lo.out = w.logits;
+        gemm(cx, T, c.V, 3 * c.d, {w.h3, ld3, false}, {cx.E3(), cx.E3L(), false}, lo);
+        if (with_targets)
+            MM_LAUNCH_TIMED(kKLogsoftmax, 4.0 * T * c.V, logsoftmax_rows_kernel, T, 256, 0, w.logits, (long long)c.V, c.V,
+                            w.targets, T, w.lp, w.lse_v, cx.d_err);
+    } else {
+        MM_LAUNCH(split3_gather_kernel, blocks_for((long long)Bc * c.d, 256), 256, 0, w.hf, c.d, Bc, S, S - 1, w.h3,
+                  (long long)ld3);
+        lo.out = last_logits;
+        gemm(cx, Bc, c.V, 3 * c.d, {w.h3, ld3, false}, {cx.E3(), cx.E3L(), false}, lo);
+    }
+}
+
+// Backward of the chunk most recently run forward with tape = true and kVocabAll.
+// ws.coef holds the per-token weighted-NLL coefficients; d_scale[0] is the power-of-two
+// gradient scale for the fp16 operands and d_scale[1] its inverse, applied when a
+// gradient lands in the fp32 accumulator.
+inline void backward_chunk(Context& cx, int Bc, int S) {
+    const Dims& c = cx.c;
+    Workspace& w = cx.ws;
+    const int T = Bc * S;
+    const int qk = c.qk(), kvw = c.kvw(), aw = c.aw();
+    const int ld_d = cx.d16(c.d), ld_qr = cx.d16(c.qr), ld_kvr = cx.d16(c.kvr), ld_ff = cx.d16(c.dff);
+    const int ld3 = cx.d16(3 * c.d);
+    const float* inv_s = cx.d_scale + 1;
+    // vocabulary head: g = s * coef * (softmax - onehot)
+    MM_LAUNCH(vocab_grad_kernel, T, 256, 0, w.logits, (long long)c.V, c.V, w.targets, w.lse_v, w.coef, cx.d_scale, T,
+              w.g16, (long long)c.V);
+    {
+        GemmOutSpec o{w.dh, c.d, kOutF32};
+        o.alpha = 1.0f / kVocabScale;  // E3's hi part holds 64 * E
+        gemm(cx, T, c.d, c.V, {w.g16, c.V, false}, {cx.E3(), cx.E3L(), true}, o);
+    }
+    {
+        GemmOutSpec o{cx.GE(), c.d, kOutF32Acc};
+        o.alpha_ptr = inv_s;
+        gemm(cx, c.V, c.d, T, {w.g16, c.V, true}, {w.h3, ld3, true}, o);  // h_hi = h3[:, :d]
+    }
+    MM_LAUNCH(rmsnorm_backward_kernel, 148 * 4, 256, c.d * 4, w.x_out, (long long)c.d, cx.FinalNorm(), w.dh,
+              (long long)c.d, (const float*)nullptr, 0LL, T, c.d, c.eps, w.dy, (long long)c.d, (__half*)nullptr, 0LL,
+              cx.GFinalNorm(), inv_s);
+    for (int l = c.L - 1; l >= 0; --l) {
+        LayerBuf& b = w.layers[l];
+        // feed-forward block
+        MM_LAUNCH(to_half_kernel, blocks_for((long long)T * c.d, 256), 256, 0, w.dy, (long long)c.d, T, c.d, w.dy16,
+                  (long long)ld_d);
+        {
+            GemmOutSpec o{cx.G(l, kWdown), c.d, kOutF32Acc};
+            o.alpha_ptr = inv_s;
+            gemm(cx, c.dff, c.d, T, {b.gated, ld_ff, true}, {w.dy16, ld_d, true}, o);
+        }
+        gemm(cx, T, c.dff, c.d, {w.dy16, ld_d, false}, {cx.S(l, kWdown), cx.SL(l, kWdown), false}, {w.dgated, c.dff, kOutF32});
+        MM_LAUNCH(swiglu_backward_kernel, blocks_for((long long)T * c.dff, 256), 256, 0, b.gate, b.up, (long long)ld_ff,
+                  w.dgated, (long long)c.dff, T, c.dff, w.dg16, w.du16, (long long)ld_ff);
+        {
+            GemmOutSpec o{cx.G(l, kWgate), c.dff, kOutF32Acc};
+            o.alpha_ptr = inv_s;
+            gemm(cx, c.d, c.dff, T, {b.h2, ld_d, true}, {w.dg16, ld_ff, true}, o);
+            o.out = cx.G(l, kWup);
+            gemm(cx, c.d, c.dff, T, {b.h2, ld_d, true}, {w.du16, ld_ff, true}, o);
+        }
+        gemm(cx, T, c.d, c.dff, {w.dg16, ld_ff, false}, {cx.S(l, kWgate), cx.SL(l, kWgate), false}, {w.dh2, c.d, kOutF32});
+        gemm(cx, T, c.d, c.dff, {w.du16, ld_ff, false}, {cx.S(l, kWup), cx.SL(l, kWup), false}, {w.dh2, c.d, kOutF32Acc});
+        MM_LAUNCH(rmsnorm_backward_kernel, 148 * 4, 256, c.d * 4, b.res, (long long)c.d, cx.W(l, kFfnNorm), w.dh2,
+                  (long long)c.d, w.dy, (long long)c.d, T, c.d, c.eps, w.dres, (long long)c.d, w.dres16, (long long)ld_d,
+                  cx.G(l, kFfnNorm), inv_s);
+        // attention output projection
+        {
+            GemmOutSpec o{cx.G(l, kWo), c.d, kOutF32Acc};
+            o.alpha_ptr = inv_s;
+            gemm(cx, aw, c.d, T, {b.ao, aw, true}, {w.dres16, ld_d, true}, o);
+        }
+        gemm(cx, T, aw, c.d, {w.dres16, ld_d, false}, {cx.S(l, kWo), cx.SL(l, kWo), false}, {w.dao, aw, kOutF32});
+        // attention
+        MM_LAUNCH(attn_bwd_dot_kernel, blocks_for((long long)T * c.H, 256), 256, 0, w.dao, b.ao, T, c.H, c.dv, w.Dd);
+        {
+            dim3 grid((S + kAttTile - 1) / kAttTile, c.H, Bc);
+            const float scale = 1.0f / std::sqrt(static_cast<float>(qk));
+            const double pairs = static_cast<double>(Bc) * c.H * (S * (S + 1.0) / 2.0);
+            const double w_kv = pairs * 4.0 * (qk + c.dv), w_q = pairs * 2.0 * (2 * qk + c.dv);
+            if (qk == 64) {
+                MM_LAUNCH_TIMED(kKFlashBwd, w_kv, (flash_bwd_dkdv_kernel<64, 64>), grid, 64, 0, b.q, b.k, b.v, w.dao, b.lse, w.Dd, S, c.H, scale, w.dk, w.dv);
+                MM_LAUNCH_TIMED(kKFlashBwd, w_q, (flash_bwd_dq_kernel<64, 64>), grid, 64, 0, b.q, b.k, b.v, w.dao, b.lse, w.Dd, S, c.H, scale, w.dq);
+            } else {
+                MM_LAUNCH_TIMED(kKFlashBwd, w_kv, (flash_bwd_dkdv_kernel<16, 16>), grid, 64, 0, b.q, b.k, b.v, w.dao, b.lse, w.Dd, S, c.H, scale, w.dk, w.dv);
+                MM_LAUNCH_TIMED(kKFlashBwd, w_q, (flash_bwd_dq_kernel<16, 16>), grid, 64, 0, b.q, b.k, b.v, w.dao, b.lse, w.Dd, S, c.H, scale, w.dq);
+            }
+        }
+        const int ld_q16 = cx.d16(c.H * qk);
+        MM_LAUNCH(rope_rows_kernel, warp_rows_grid(T), 256, 0, w.dq, (long long)(c.H * qk), T, S, (const int*)nullptr, c.H,
+                  qk, c.nope, c.rope, cx.cos_t, cx.sin_t, 1, (float*)nullptr, 0LL, w.dq16, (long long)ld_q16);
+        const int ld_kn16 = cx.d16(c.H * c.nope);
+        MM_LAUNCH(split_dk_kernel, warp_rows_grid(T), 256, 0, w.dk, T, c.H, c.nope, c.rope, w.dkn16, (long long)ld_kn16, w.drope);
+        MM_LAUNCH(rope_rows_kernel, warp_rows_grid(T), 256, 0, w.drope, (long long)c.rope, T, S, (const int*)nullptr, 1,
+                  c.rope, 0, c.rope, cx.cos_t, cx.sin_t, 1, w.drope2, (long long)c.rope, (__half*)nullptr, 0LL);
+        const int ld_v16 = cx.d16(aw);
+        MM_LAUNCH(to_half_kernel, blocks_for((long long)T * aw, 256), 256, 0, w.dv, (long long)aw, T, aw, w.dv16, (long long)ld_v16);
+        {
+            GemmOutSpec o{cx.G(l, kWuk), c.H * c.nope, kOutF32Acc};
+            o.alpha_ptr = inv_s;
+            gemm(cx, c.kvr, c.H * c.nope, T, {b.ckv, ld_kvr, true}, {w.dkn16, ld_kn16, true}, o);
+            o.out = cx.G(l, kWuv);
+            o.ldc = aw;
+            gemm(cx, c.kvr, aw, T, {b.ckv, ld_kvr, true}, {w.dv16, ld_v16, true}, o);
+        }
+        gemm(cx, T, c.kvr, c.H * c.nope, {w.dkn16, ld_kn16, false}, {cx.S(l, kWuk), cx.SL(l, kWuk), false}, {w.dckv, c.kvr, kOutF32});
+        gemm(cx, T, c.kvr, aw, {w.dv16, ld_v16, false}, {cx.S(l, kWuv), cx.SL(l, kWuv), false}, {w.dckv, c.kvr, kOutF32Acc});
+        MM_LAUNCH(rmsnorm_backward_kernel, 148 * 4, 256, c.kvr * 4, b.kvp, (long long)kvw, cx.W(l, kKvNorm), w.dckv,
+                  (long long)c.kvr, (const float*)nullptr, 0LL, T, c.kvr, c.eps, w.dkvraw, (long long)c.kvr, (__half*)nullptr,
+                  0LL, cx.G(l, kKvNorm), inv_s);
+        const int ld_kvw16 = cx.d16(kvw);
+        MM_LAUNCH(pack_dkv_kernel, blocks_for((long long)T * kvw, 256), 256, 0, w.dkvraw, w.drope2, T, c.kvr, c.rope, w.dkvp16,
+                  (long long)ld_kvw16);
+        {
+            GemmOutSpec o{cx.G(l, kWdkv), kvw, kOutF32Acc};
+            o.alpha_ptr = inv_s;
+            gemm(cx, c.d, kvw, T, {b.h, ld_d, true}, {w.dkvp16, ld_kvw16, true}, o);
+        }
+        gemm(cx, T, c.d, kvw, {w.dkvp16, ld_kvw16, false}, {cx.S(l, kWdkv), cx.SL(l, kWdkv), false}, {w.dh, c.d, kOutF32});
+        {
+            GemmOutSpec o{cx.G(l, kWuq), c.H * qk, kOutF32Acc};
+            o.alpha_ptr = inv_s;
+            gemm(cx, c.qr, c.H * qk, T, {b.cq, ld_qr, true}, {w.dq16, ld_q16, true}, o);
+        }
+        gemm(cx, T, c.qr, c.H * qk, {w.dq16, ld_q16, false}, {cx.S(l, kWuq), cx.SL(l, kWuq), false}, {w.dcq, c.qr, kOutF32});
+        MM_LAUNCH(rmsnorm_backward_kernel, 148 * 4, 256, c.qr * 4, b.raw_cq, (long long)c.qr, cx.W(l, kQNorm), w.dcq,
+                  (long long)c.qr, (const float*)nullptr, 0LL, T, c.qr, c.eps, (float*)nullptr, 0LL, w.draw16, (long long)ld_qr,
+                  cx.G(l, kQNorm), inv_s);
+        {
+            GemmOutSpec o{cx.G(l, kWdq), c.qr, kOutF32Acc};
+            o.alpha_ptr = inv_s;
+            gemm(cx, c.d, c.qr, T, {b.h, ld_d, true}, {w.draw16, ld_qr, true}, o);
+        }
+        gemm(cx, T, c.d, c.qr, {w.draw16, ld_qr, false}, {cx.S(l, kWdq), cx.SL(l, kWdq), false}, {w.dh, c.d, kOutF32Acc});
+        MM_LAUNCH(rmsnorm_backward_kernel, 148 * 4, 256, c.d * 4, b.x_in, (long long)c.d, cx.W(l, kAttnNorm), w.dh,
+                  (long long)c.d, w.dres, (long long)c.d, T, c.d, c.eps, w.dy, (long long)c.d, (__half*)nullptr, 0LL,
+                  cx.G(l, kAttnNorm), inv_s);
+    }
+    MM_LAUNCH(embed_backward_kernel, warp_rows_grid(T), 256, 0, w.tokens, w.dy, T, c.d, cx.GE(), inv_s);
+}
+
+} // namespace mm

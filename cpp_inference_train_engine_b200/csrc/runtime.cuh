@@ -1,0 +1,396 @@
+// Host runtime of the backend: device context, parameter arenas, workspaces, the GEMM
+// launcher and the launch helpers shared by the passes (passes.cu) and the C ABI (api.cu).
+#pragma once
+#include <cudaTypedefs.h>
+
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <stdexcept>
+#include <string>
+#include <tuple>
+#include <vector>
+
+#include "attention.cuh"
+#include "common.cuh"
+#include "gemm_tc.cuh"
+#include "kernels_elem.cuh"
+#include "optim.cuh"
+#include "vocab_grpo.cuh"
+
+#include "../../include/mm_cuda.h"
+
+namespace mm {
+
+// Error carried up to the C ABI as 1 + ErrorCode with a message.
+struct Failure : std::runtime_error {
+    int code;
+    Failure(int c, const std::string& m) : std::runtime_error(m), code(c) {}
+};
+[[noreturn]] inline void fail(int code, const std::string& m) { throw Failure(code, m); }
+
+#define MM_CUDA_CHECK(x)                                                                  \
+    do {                                                                                  \
+        cudaError_t e_ = (x);                                                             \
+        if (e_ != cudaSuccess)                                                            \
+            ::mm::fail(e_ == cudaErrorMemoryAllocation ? MM_OUT_OF_MEMORY : MM_GPU_ERROR, \
+                       std::string(#x) + ": " + cudaGetErrorString(e_));                  \
+    } while (0)
+
+inline long long round_up(long long x, long long a) { return (x + a - 1) / a * a; }
+
+struct Dims {
+    int V, maxS, L, d, H, nope, rope, dv, qr, kvr, dff;
+    float eps, theta;
+    int qk() const { return nope + rope; }
+    int kvw() const { return kvr + rope; }
+    int aw() const { return H * dv; }
+};
+
+// One device allocation with bump sub-allocation (256-byte aligned pieces).
+class Arena {
+  public:
+    ~Arena() { release(); }
+    void reserve(size_t bytes) {
+        release();
+        if (bytes == 0) return;
+        MM_CUDA_CHECK(cudaMalloc(&base_, bytes));
+        cap_ = bytes;
+        used_ = 0;
+    }
+    template <class T> T* take(long long count) {
+        size_t off = static_cast<size_t>(round_up(static_cast<long long>(used_), 256));
+        size_t bytes = static_cast<size_t>(count) * sizeof(T);
+        if (off + bytes > cap_) fail(MM_OUT_OF_MEMORY, "workspace arena exhausted");
+        used_ = off + bytes;
+        return reinterpret_cast<T*>(static_cast<char*>(base_) + off);
+    }
+    void reset() { used_ = 0; }
+    void release() {
+        if (base_) cudaFree(base_);
+        base_ = nullptr;
+        cap_ = used_ = 0;
+    }
+    size_t capacity() const { return cap_; }
+
+  private:
+    void* base_ = nullptr;
+    size_t cap_ = 0, used_ = 0;
+};
+
+// Byte counter used to size an Arena before allocating it: same take() sequence.
+class Sizer {
+  public:
+    template <class T> T* take(long long count) {
+        used_ = static_cast<size_t>(round_up(static_cast<long long>(used_), 256)) + static_cast<size_t>(count) * sizeof(T);
+        return nullptr;
+    }
+    size_t used() const { return used_; }
+
+  private:
+    size_t used_ = 0;
+};
+
+// Reusable device staging buffer for host inputs of one call.
+struct Staging {
+    Arena a;
+    size_t cap = 0;
+    void* get(size_t bytes) {
+        if (bytes > cap) {
+            a.release();
+            a.reserve(bytes + 1024);
+            cap = bytes;
+        }
+        a.reset();
+        return a.take<char>(static_cast<long long>(bytes));
+    }
+};
+
+enum LayerParam { kAttnNorm, kWdq, kQNorm, kWuq, kWdkv, kKvNorm, kWuk, kWuv, kWo, kFfnNorm, kWgate, kWup, kWdown, kLayerParams };
+
+// Per-layer activations of a teacher-forced pass (the reference's LayerTape,
+// include/mini_mla/model.hpp:31-34, in the mixed-precision layout of this backend).
+struct LayerBuf {
+    float* x_in;      // [T][d]     layer input (residual stream)
+    __half* h;        // [T][ld16(d)]
+    float* raw_cq;    // [T][qr]
+    __half* cq;       // [T][ld16(qr)]
+    __half* q;        // [T][H*qk]  rotated
+    float* kvp;       // [T][kvw]   raw latent | raw rope key
+    __half* ckv;      // [T][ld16(kvr)]
+    float* k_rope;    // [T][rope]  rotated
+    __half* k;        // [T][H*qk]
+    __half* v;        // [T][H*dv]
+    __half* ao;       // [T][H*dv]
+    float* lse;       // [T][H]
+    float* res;       // [T][d]
+    __half* h2;       // [T][ld16(d)]
+    __half* gate;     // [T][ld16(dff)]
+    __half* up;       // [T][ld16(dff)]
+    __half* gated;    // [T][ld16(dff)]
+};
+
+struct Workspace {
+    int T = 0;          // token capacity
+    bool tape = false;  // one LayerBuf per layer (training) or one shared
+    std::vector<LayerBuf> layers;
+    float* x_out;       // [T][d] output of the last layer
+    float* hf;          // [T][d] final norm output
+    __half* h3;         // [T][ld16(3d)]
+    float* logits;      // [T][V]
+    float* lp;          // [T]
+    float* lse_v;       // [T]
+    uint16_t* tokens;   // [T]
+    uint16_t* targets;  // [T]
+    float* mask;        // [T]
+    float* coef;        // [T]
+    float* old_lp;      // [T]
+    float* ref_lp;      // [T]
+    // scratch
+    float* q_pre;       // [T][H*qk]
+    float* knope;       // [T][H*nope]
+    // backward scratch (tape only)
+    float *dy, *dgated, *dh2, *dres, *dao, *dq, *dk, *dv, *drope, *drope2, *dckv, *dkvraw, *dh, *dcq, *Dd;
+    __half *dy16, *dg16, *du16, *dres16, *dq16, *dkn16, *dv16, *dkvp16, *draw16, *g16;
+};
+
+struct DecodeState {
+    int B = 0, Sc = 0;  // rows, cache positions per row
+    __half* cache = nullptr;  // [L][B][Sc][kvw]
+    int* pos = nullptr;       // [B] next position to write
+    float* x;                 // [B][d]
+    __half* h16;              // [B][ld16(d)]
+    float* y;                 // [B][qr + kvw]
+    __half* cq16;             // [B][ld16(qr)]
+    __half* lat16;            // [B][ld16(kvr)]
+    float* k_rope;            // [B][rope]
+    float* qf;                // [B][H*kvw]
+    float* qf2;               // [B][H*kvw]
+    __half* ctx16;            // [B][H*kvr]
+    float* res;               // [B][d]
+    __half* h2;               // [B][ld16(d)]
+    __half* gu;               // [B][ld16(2 dff)]
+    __half* gated;            // [B][ld16(dff)]
+    float* hf;                // [B][d]
+    __half* h3;               // [B][ld16(3d)]
+    float* logits;            // [B][V]
+    uint16_t* tok;            // [B]
+    uint64_t* seeds;          // [B]
+    int* draw;                // [B]
+    uint16_t* out_tok;        // [B][max_new]
+    int max_new = 0;
+    Arena arena;
+};
+
+struct PrepLayer {
+    __half *Wa, *Wq, *Wo, *Wgu;
+    int lda, ldq, ldo, ldgu;
+};
+
+// Device-time accounting while profiling is on: event pairs recorded on the context's
+// stream around each phase and around every launch of a kernel class, resolved only when
+// read, so the timed region gains no host synchronisation. Each kernel-class launch also
+// adds its algorithmic work (bytes moved or flops) as computed from the launch shape.
+enum Phase { kPhPrefill, kPhDecode, kPhSample, kPhLogprob, kPhBackward, kPhAdamw, kPhAllreduce, kPhPrep };
+enum KernelClass { kKGemm = 8, kKDecodeAttn, kKFlashFwd, kKFlashBwd, kKSample, kKLogsoftmax, kKAdamw, kKOther };
+constexpr int kProfTags = 16;
+struct Profile {
+    double ms[kProfTags] = {0};
+    long long calls[kProfTags] = {0};
+    double work[kProfTags] = {0};  // flops (GEMM, attention) or bytes (the rest)
+};
+struct EventLog {
+    std::vector<cudaEvent_t> free_events;
+    std::vector<std::tuple<int, cudaEvent_t, cudaEvent_t>> pending;
+    cudaEvent_t take() {
+        if (free_events.empty()) {
+            cudaEvent_t e;
+            cudaEventCreate(&e);
+            return e;
+        }
+        cudaEvent_t e = free_events.back();
+        free_events.pop_back();
+        return e;
+    }
+};
+
+class Context {
+  public:
+    Dims c{};
+    int device = 0;
+    bool trainable = false;
+    mm_adamw_desc opt{0.9f, 0.95f, 1e-8f, 0.1f, 1.0f};
+    uint64_t steps = 0;
+    cudaStream_t stream = nullptr;
+    std::string last_error;
+    bool unusable = false;
+    long long launches = 0;
+
+    // parameters
+    std::vector<ParamDesc> params;      // registry order
+    std::vector<long long> flat_off;    // offsets in the caller's flat array
+    long long P = 0, P_dev = 0;         // logical and padded element counts
+    long long shadow_elems = 0;
+    ParamDesc* d_params = nullptr;
+    Arena weights;                      // master, grad, m, v, shadow, rope tables, prep
+    float *w = nullptr, *g = nullptr, *m = nullptr, *v = nullptr;
+    __half* shadow = nullptr;
+    float *cos_t = nullptr, *sin_t = nullptr;
+    std::vector<PrepLayer> prep;
+
+    // scalars on device
+    int* d_err = nullptr;
+    double* d_partial = nullptr;  // AdamW norm partials
+    int n_partial = 0;
+    double* d_norm = nullptr;
+    float* d_gs = nullptr;
+    int* d_nonfinite = nullptr;
+    int* d_nonfinite_out = nullptr;
+    GrpoSums* d_sums = nullptr;
+    float* d_scale = nullptr;     // [2] gradient scale, inverse
+    int* d_any = nullptr;
+    float* d_one = nullptr;       // constant 1.0f
+    Arena scalars;
+
+    Workspace ws;
+    Arena ws_arena;
+    Staging stage;
+    DecodeState dec;
+    int dec_len = 0;  // positions filled in the decode session (0: no session)
+
+    // NCCL
+    void* nccl_comm = nullptr;
+    int rank = 0, world = 1;
+
+    // timing
+    bool profiling = false;
+    Profile prof;
+    EventLog evlog;
+    cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+
+    // Opens a timed interval for `tag` (no-op unless profiling); close with prof_end.
+    cudaEvent_t prof_begin() {
+        if (!profiling) return nullptr;
+        cudaEvent_t e = evlog.take();
+        cudaEventRecord(e, stream);
+        return e;
+    }
+    void prof_end(int tag, cudaEvent_t start, double work = 0) {
+        if (!start) return;
+        cudaEvent_t e = evlog.take();
+        cudaEventRecord(e, stream);
+        evlog.pending.emplace_back(tag, start, e);
+        prof.work[tag] += work;
+        prof.calls[tag] += 1;
+    }
+    // Waits for the stream and folds every pending interval into prof.ms.
+    void prof_resolve() {
+        if (evlog.pending.empty()) return;
+        cudaStreamSynchronize(stream);
+        for (auto& [tag, a, b] : evlog.pending) {
+            float ms = 0.f;
+            cudaEventElapsedTime(&ms, a, b);
+            prof.ms[tag] += ms;
+            evlog.free_events.push_back(a);
+            evlog.free_events.push_back(b);
+        }
+        evlog.pending.clear();
+    }
+
+    int d16(int n) const { return static_cast<int>(round_up(n, 8)); }
+    int param_index(int l, int which) const { return 2 + l * kLayerParams + which; }
+    float* W(int l, int which) const { return w + params[param_index(l, which)].off; }
+    float* G(int l, int which) const { return g + params[param_index(l, which)].off; }
+    __half* S(int l, int which) const { return shadow + params[param_index(l, which)].shadow_off; }
+    int SL(int l, int which) const { return params[param_index(l, which)].shadow_ld; }
+    float* E() const { return w + params[0].off; }
+    float* GE() const { return g + params[0].off; }
+    __half* E3() const { return shadow + params[0].shadow_off; }
+    int E3L() const { return params[0].shadow_ld; }
+    float* FinalNorm() const { return w + params[1].off; }
+    float* GFinalNorm() const { return g + params[1].off; }
+};
+
+// ------------------------------------------------------------------ tensor maps
+inline PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        cudaDriverEntryPointQueryResult q;
+        void* p = nullptr;
+        MM_CUDA_CHECK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q));
+        if (q != cudaDriverEntryPointSuccess || !p) fail(MM_GPU_ERROR, "cuTensorMapEncodeTiled unavailable");
+        fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    return fn;
+}
+
+// 2-D fp16/bf16 tensor map, 128-byte swizzle, zero fill out of bounds. Cached by
+// (address, shape, pitch, box): buffers are long-lived, so the encode runs once per view.
+inline const CUtensorMap& tensor_map(const void* base, bool bf16, long long dim0, long long dim1,
+                                     long long pitch_elems, int box0, int box1) {
+    using Key = std::tuple<const void*, bool, long long, long long, long long, int, int>;
+    static std::map<Key, CUtensorMap> cache;
+    Key k{base, bf16, dim0, dim1, pitch_elems, box0, box1};
+    auto it = cache.find(k);
+    if (it != cache.end()) return it->second;
+    if ((reinterpret_cast<uintptr_t>(base) & 15) || (pitch_elems * 2) % 16)
+        fail(MM_INVALID_ARGUMENT, "tensor map needs 16-byte aligned base and pitch");
+    CUtensorMap map;
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(dim0), static_cast<cuuint64_t>(dim1)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(pitch_elems * 2)};
+    cuuint32_t box[2] = {static_cast<cuuint32_t>(box0), static_cast<cuuint32_t>(box1)};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = tensor_map_encoder()(&map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                                      2, const_cast<void*>(base), dims, strides, box, estr,
+                                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) fail(MM_GPU_ERROR, "cuTensorMapEncodeTiled failed: " + std::to_string(static_cast<int>(r)));
+    return cache.emplace(k, map).first->second;
+}
+
+// ------------------------------------------------------------------ GEMM launcher
+// Operand views. K-major A: [M][K] rows; MN-major A: [K][M] rows. K-major B: [N][K];
+// MN-major B: [K][N]. `ld` is the row pitch in elements (a multiple of 8).
+struct Opnd {
+    const void* p;
+    long long ld;
+    bool mn;
+};
+
+struct GemmOutSpec {
+    void* out;
+    long long ldc;
+    int kind;
+    const float* residual = nullptr;
+    long long ldr = 0;
+    float alpha = 1.f;
+    const float* alpha_ptr = nullptr;
+};
+
+template <int BN, int STAGES>
+inline void launch_gemm_bn(Context& cx, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& ga) {
+    using C = GemmCfg<BN, STAGES>;
+    static bool configured = false;
+    if (!configured) {
+        MM_CUDA_CHECK(cudaFuncSetAttribute(gemm_tc_kernel<BN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+        configured = true;
+    }
+    dim3 grid(static_cast<unsigned>((ga.N + BN - 1) / BN), static_cast<unsigned>((ga.M + kGemmBM - 1) / kGemmBM));
+    cudaEvent_t t0 = cx.prof_begin();
+    gemm_tc_kernel<BN, STAGES><<<grid, 192, C::SMEM, cx.stream>>>(ta, tb, ga);
+    cx.prof_end(kKGemm, t0, 2.0 * ga.M * static_cast<double>(ga.N) * ga.K);
+    ++cx.launches;
+}
+
+// D[M,N] = alpha * A * B (+ residual | += D). bf16 selects bf16 operands.
+void gemm(Context& cx, int M, int N, int K, Opnd A, Opnd B, const GemmOutSpec& o, bool bf16 = false);
+
+// ------------------------------------------------------------------ small launch helpers
+inline unsigned blocks_for(long long n, int threads) {
+    return static_cast<unsigned>((n + threads - 1) / threads);
+}
+
+} // namespace mm

@@ -1,0 +1,295 @@
+// Context construction, GEMM dispatch, parameter upload/download and the derived fp16
+// weight copies.
+#pragma once
+#include "runtime.cuh"
+
+namespace mm {
+
+inline void gemm(Context& cx, int M, int N, int K, Opnd A, Opnd B, const GemmOutSpec& o, bool bf16) {
+    if (M <= 0 || N <= 0 || K <= 0) return;
+    const long long tiles_m = (M + kGemmBM - 1) / kGemmBM;
+    int BN = 64;
+    if (tiles_m * ((N + 255) / 256) >= 148 && N >= 256) BN = 256;
+    else if (tiles_m * ((N + 127) / 128) >= 120 && N > 64) BN = 128;
+    const CUtensorMap& ta = A.mn ? tensor_map(A.p, bf16, M, K, A.ld, 64, 64)
+                                 : tensor_map(A.p, bf16, K, M, A.ld, 64, kGemmBM);
+    const CUtensorMap& tb = B.mn ? tensor_map(B.p, bf16, N, K, B.ld, 64, 64)
+                                 : tensor_map(B.p, bf16, K, N, B.ld, 64, BN);
+    GemmArgs ga{M, N, K, A.mn ? 1 : 0, B.mn ? 1 : 0, bf16 ? 1 : 0, o.out, o.ldc, o.kind,
+                o.residual, o.ldr, o.alpha, o.alpha_ptr, cx.d_err};
+    if (BN == 256) launch_gemm_bn<256, 4>(cx, ta, tb, ga);
+    else if (BN == 128) launch_gemm_bn<128, 3>(cx, ta, tb, ga);
+    else launch_gemm_bn<64, 4>(cx, ta, tb, ga);
+}
+
+inline Dims dims_from(const mm_model_desc& d) {
+    Dims c;
+    c.V = d.vocab_size; c.maxS = d.max_sequence_length; c.L = d.n_layers; c.d = d.d_model;
+    c.H = d.n_heads; c.nope = d.head_dim_nope; c.rope = d.head_dim_rope; c.dv = d.head_dim_value;
+    c.qr = d.q_lora_rank; c.kvr = d.kv_lora_rank; c.dff = d.d_ff;
+    c.eps = d.norm_epsilon; c.theta = d.rope_theta;
+    return c;
+}
+
+// ModelConfig::validate (src/model/config.cpp:20-48) minus the 1e9-parameter cap, plus
+// the limits of this backend's kernels.
+inline void validate_dims(const Dims& c) {
+    const int v[] = {c.V, c.maxS, c.L, c.d, c.H, c.nope, c.rope, c.dv, c.qr, c.kvr, c.dff};
+    for (int x : v)
+        if (x < 1 || x > 65535) fail(MM_INVALID_ARGUMENT, "model dimensions must be in [1, 65535]");
+    if (c.L > 128 || c.H > 256 || c.d % c.H || c.rope % 2)
+        fail(MM_INVALID_ARGUMENT, "Invalid vocabulary/layer/head count, d_model divisibility, or odd RoPE dimension");
+    if (!std::isfinite(c.eps) || c.eps <= 0 || !std::isfinite(c.theta) || c.theta <= 1)
+        fail(MM_INVALID_ARGUMENT, "Invalid normalization epsilon or RoPE theta");
+    const bool att_ok = (c.qk() == 16 && c.dv == 16) || (c.qk() == 64 && c.dv == 64);
+    if (!att_ok) fail(MM_UNSUPPORTED, "attention kernels are built for (qk, dv) = (16, 16) or (64, 64)");
+    const bool dec_ok = (c.kvr == 8 && c.rope == 4) || (c.kvr == 128 && c.rope == 16);
+    if (!dec_ok) fail(MM_UNSUPPORTED, "decode attention is built for (kv_rank, rope) = (8, 4) or (128, 16)");
+}
+
+inline long long parameter_count(const Dims& c) {
+    const long long d = c.d, h = c.H, q = c.qr, kv = c.kvr;
+    return static_cast<long long>(c.V) * d + d +
+           static_cast<long long>(c.L) *
+               (d * q + q * h * c.qk() + d * c.kvw() + kv * h * (c.nope + c.dv) + h * c.dv * d +
+                3 * d * c.dff + 2 * d + q + kv);
+}
+
+// Registry of Model::create (src/model/model.cpp:40-63): (rows, cols, role) per entry,
+// role 0 hidden matrix, 1 token embedding, 2 norm scale.
+inline std::vector<std::tuple<int, int, int>> registry(const Dims& c) {
+    std::vector<std::tuple<int, int, int>> r;
+    r.emplace_back(c.V, c.d, 1);
+    r.emplace_back(1, c.d, 2);
+    for (int l = 0; l < c.L; ++l) {
+        r.emplace_back(1, c.d, 2);
+        r.emplace_back(c.d, c.qr, 0);
+        r.emplace_back(1, c.qr, 2);
+        r.emplace_back(c.qr, c.H * c.qk(), 0);
+        r.emplace_back(c.d, c.kvw(), 0);
+        r.emplace_back(1, c.kvr, 2);
+        r.emplace_back(c.kvr, c.H * c.nope, 0);
+        r.emplace_back(c.kvr, c.aw(), 0);
+        r.emplace_back(c.aw(), c.d, 0);
+        r.emplace_back(1, c.d, 2);
+        r.emplace_back(c.d, c.dff, 0);
+        r.emplace_back(c.d, c.dff, 0);
+        r.emplace_back(c.dff, c.d, 0);
+    }
+    return r;
+}
+
+// Rope cos/sin tables with the reference's float arithmetic (ops.cpp:92-96):
+// angle = float(t) * pow(theta, -float(j) / float(rope)) for even j.
+inline void rope_tables(const Dims& c, std::vector<float>& cs, std::vector<float>& sn) {
+    const int half_r = c.rope / 2;
+    cs.resize(static_cast<size_t>(c.maxS) * half_r);
+    sn.resize(cs.size());
+    for (int t = 0; t < c.maxS; ++t)
+        for (int p = 0; p < half_r; ++p) {
+            const int j = 2 * p;
+            float angle = static_cast<float>(t) *
+                          std::pow(c.theta, -static_cast<float>(j) / static_cast<float>(c.rope));
+            cs[static_cast<size_t>(t) * half_r + p] = std::cos(angle);
+            sn[static_cast<size_t>(t) * half_r + p] = std::sin(angle);
+        }
+}
+
+inline void create_context(Context& cx, const mm_model_desc& desc, int device, bool trainable,
+                           const mm_adamw_desc* opt) {
+    cx.c = dims_from(desc);
+    validate_dims(cx.c);
+    cx.device = device;
+    cx.trainable = trainable;
+    if (opt) cx.opt = *opt;
+    MM_CUDA_CHECK(cudaSetDevice(device));
+    MM_CUDA_CHECK(cudaStreamCreateWithFlags(&cx.stream, cudaStreamNonBlocking));
+    MM_CUDA_CHECK(cudaEventCreate(&cx.ev0));
+    MM_CUDA_CHECK(cudaEventCreate(&cx.ev1));
+    const Dims& c = cx.c;
+    auto reg = registry(c);
+    long long cur = 0, scur = 0, flat = 0;
+    for (auto& [rows, cols, role] : reg) {
+        ParamDesc p{};
+        p.off = round_up(cur, 64);
+        cur = p.off + static_cast<long long>(rows) * cols;
+        p.rows = rows;
+        p.cols = cols;
+        p.decay = role == 2 ? 0.f : cx.opt.weight_decay;
+        if (role == 0) {
+            p.shadow_kind = kShadowHalf;
+            p.shadow_ld = cx.d16(cols);
+        } else if (role == 1) {
+            p.shadow_kind = kShadowVocab3;
+            p.shadow_ld = cx.d16(3 * cols);
+        } else {
+            p.shadow_kind = kShadowNone;
+            p.shadow_ld = 0;
+        }
+        if (p.shadow_kind != kShadowNone) {
+            p.shadow_off = round_up(scur, 64);
+            scur = p.shadow_off + static_cast<long long>(rows) * p.shadow_ld;
+        }
+        cx.params.push_back(p);
+        cx.flat_off.push_back(flat);
+        flat += static_cast<long long>(rows) * cols;
+    }
+    cx.P = flat;
+    cx.P_dev = round_up(cur, 64);
+    cx.shadow_elems = round_up(scur, 64);
+    // decode-derived weights
+    const int lda = cx.d16(c.qr + c.kvw()), ldq = cx.d16(c.H * c.kvw()), ldo = cx.d16(c.d),
+              ldgu = cx.d16(2 * c.dff);
+    auto plan = [&](auto& a) {
+        cx.w = a.template take<float>(cx.P_dev);
+        if (trainable) {
+            cx.g = a.template take<float>(cx.P_dev);
+            cx.m = a.template take<float>(cx.P_dev);
+            cx.v = a.template take<float>(cx.P_dev);
+        }
+        cx.shadow = a.template take<__half>(cx.shadow_elems);
+        cx.cos_t = a.template take<float>(static_cast<long long>(c.maxS) * (c.rope / 2));
+        cx.sin_t = a.template take<float>(static_cast<long long>(c.maxS) * (c.rope / 2));
+        cx.d_params = a.template take<ParamDesc>(static_cast<long long>(cx.params.size()));
+        cx.prep.resize(c.L);
+        for (int l = 0; l < c.L; ++l) {
+            PrepLayer& p = cx.prep[l];
+            p.lda = lda; p.ldq = ldq; p.ldo = ldo; p.ldgu = ldgu;
+            p.Wa = a.template take<__half>(static_cast<long long>(c.d) * lda);
+            p.Wq = a.template take<__half>(static_cast<long long>(c.qr) * ldq);
+            p.Wo = a.template take<__half>(static_cast<long long>(c.H) * c.kvr * ldo);
+            p.Wgu = a.template take<__half>(static_cast<long long>(c.d) * ldgu);
+        }
+    };
+    Sizer sz;
+    plan(sz);
+    cx.weights.reserve(sz.used() + 4096);
+    plan(cx.weights);
+    MM_CUDA_CHECK(cudaMemsetAsync(cx.w, 0, sizeof(float) * cx.P_dev, cx.stream));
+    if (trainable) {
+        MM_CUDA_CHECK(cudaMemsetAsync(cx.g, 0, sizeof(float) * cx.P_dev, cx.stream));
+        MM_CUDA_CHECK(cudaMemsetAsync(cx.m, 0, sizeof(float) * cx.P_dev, cx.stream));
+        MM_CUDA_CHECK(cudaMemsetAsync(cx.v, 0, sizeof(float) * cx.P_dev, cx.stream));
+    }
+    MM_CUDA_CHECK(cudaMemsetAsync(cx.shadow, 0, sizeof(__half) * cx.shadow_elems, cx.stream));
+    std::vector<float> cs, sn;
+    rope_tables(c, cs, sn);
+    MM_CUDA_CHECK(cudaMemcpyAsync(cx.cos_t, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice, cx.stream));
+    MM_CUDA_CHECK(cudaMemcpyAsync(cx.sin_t, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice, cx.stream));
+    MM_CUDA_CHECK(cudaMemcpyAsync(cx.d_params, cx.params.data(), cx.params.size() * sizeof(ParamDesc),
+                                  cudaMemcpyHostToDevice, cx.stream));
+    // device scalars
+    cx.n_partial = 1184;  // 8 blocks per SM on 148 SMs
+    auto plan_s = [&](auto& a) {
+        cx.d_err = a.template take<int>(4);
+        cx.d_partial = a.template take<double>(cx.n_partial);
+        cx.d_norm = a.template take<double>(1);
+        cx.d_gs = a.template take<float>(1);
+        cx.d_nonfinite = a.template take<int>(1);
+        cx.d_nonfinite_out = a.template take<int>(1);
+        cx.d_sums = a.template take<GrpoSums>(1);
+        cx.d_scale = a.template take<float>(2);
+        cx.d_any = a.template take<int>(1);
+        cx.d_one = a.template take<float>(1);
+    };
+    Sizer s2;
+    plan_s(s2);
+    cx.scalars.reserve(s2.used() + 1024);
+    plan_s(cx.scalars);
+    MM_CUDA_CHECK(cudaMemsetAsync(cx.d_err, 0, 16, cx.stream));
+    const float one = 1.f;
+    MM_CUDA_CHECK(cudaMemcpyAsync(cx.d_one, &one, 4, cudaMemcpyHostToDevice, cx.stream));
+    MM_CUDA_CHECK(cudaStreamSynchronize(cx.stream));
+}
+
+// Reads and clears the device error word; raises gpu_error on anything recorded.
+inline void check_device(Context& cx, const char* where) {
+    MM_CUDA_CHECK(cudaGetLastError());
+    int err = 0;
+    MM_CUDA_CHECK(cudaMemcpyAsync(&err, cx.d_err, 4, cudaMemcpyDeviceToHost, cx.stream));
+    MM_CUDA_CHECK(cudaStreamSynchronize(cx.stream));
+    if (err) {
+        MM_CUDA_CHECK(cudaMemsetAsync(cx.d_err, 0, 4, cx.stream));
+        if (err & kErrBadIndex) fail(MM_INVALID_ARGUMENT, std::string(where) + ": token id out of range");
+        if (err & kErrNonfinite) fail(MM_NUMERICAL_ERROR, std::string(where) + ": nonfinite value");
+        cx.unusable = true;
+        fail(MM_GPU_ERROR, std::string(where) + ": device wait timed out (error word " + std::to_string(err) + ")");
+    }
+}
+
+// fp16 shadow of every matrix and the absorbed decode weights, from the fp32 master.
+inline void refresh_derived(Context& cx, bool shadows) {
+    const Dims& c = cx.c;
+    if (shadows) {
+        dim3 grid(256, static_cast<unsigned>(cx.params.size()));
+        shadow_refresh_kernel<<<grid, 256, 0, cx.stream>>>(cx.d_params, cx.w, cx.shadow);
+        ++cx.launches;
+    }
+    for (int l = 0; l < c.L; ++l) {
+        PrepArgs a;
+        a.w_dq = cx.W(l, kWdq); a.w_dkv = cx.W(l, kWdkv); a.w_uq = cx.W(l, kWuq); a.w_uk = cx.W(l, kWuk);
+        a.w_uv = cx.W(l, kWuv); a.w_o = cx.W(l, kWo); a.w_gate = cx.W(l, kWgate); a.w_up = cx.W(l, kWup);
+        const PrepLayer& p = cx.prep[l];
+        a.Wa = p.Wa; a.Wq = p.Wq; a.Wo = p.Wo; a.Wgu = p.Wgu;
+        a.lda = p.lda; a.ldq = p.ldq; a.ldo = p.ldo; a.ldgu = p.ldgu;
+        a.d = c.d; a.qr = c.qr; a.kvr = c.kvr; a.rope = c.rope; a.nope = c.nope; a.dv = c.dv;
+        a.H = c.H; a.dff = c.dff;
+        decode_prep_kernel<<<592, 256, 0, cx.stream>>>(a);
+        ++cx.launches;
+    }
+}
+
+inline void upload_params(Context& cx, const float* params, const float* m, const float* v, uint64_t steps) {
+    std::vector<float> buf(static_cast<size_t>(cx.P_dev), 0.f);
+    auto scatter = [&](const float* src) {
+        std::fill(buf.begin(), buf.end(), 0.f);
+        for (size_t i = 0; i < cx.params.size(); ++i) {
+            const auto& p = cx.params[i];
+            std::memcpy(buf.data() + p.off, src + cx.flat_off[i], sizeof(float) * p.rows * p.cols);
+        }
+    };
+    for (size_t i = 0; i < static_cast<size_t>(cx.P); ++i)
+        if (!std::isfinite(params[i])) fail(MM_INVALID_ARGUMENT, "nonfinite parameter");
+    scatter(params);
+    MM_CUDA_CHECK(cudaMemcpyAsync(cx.w, buf.data(), sizeof(float) * cx.P_dev, cudaMemcpyHostToDevice, cx.stream));
+    MM_CUDA_CHECK(cudaStreamSynchronize(cx.stream));
+    if (cx.trainable) {
+        if (m) {
+            scatter(m);
+            MM_CUDA_CHECK(cudaMemcpyAsync(cx.m, buf.data(), sizeof(float) * cx.P_dev, cudaMemcpyHostToDevice, cx.stream));
+            MM_CUDA_CHECK(cudaStreamSynchronize(cx.stream));
+        } else {
+            MM_CUDA_CHECK(cudaMemsetAsync(cx.m, 0, sizeof(float) * cx.P_dev, cx.stream));
+        }
+        if (v) {
+            scatter(v);
+            MM_CUDA_CHECK(cudaMemcpyAsync(cx.v, buf.data(), sizeof(float) * cx.P_dev, cudaMemcpyHostToDevice, cx.stream));
+            MM_CUDA_CHECK(cudaStreamSynchronize(cx.stream));
+        } else {
+            MM_CUDA_CHECK(cudaMemsetAsync(cx.v, 0, sizeof(float) * cx.P_dev, cx.stream));
+        }
+        MM_CUDA_CHECK(cudaMemsetAsync(cx.g, 0, sizeof(float) * cx.P_dev, cx.stream));
+    }
+    cx.steps = steps;
+    refresh_derived(cx, true);
+    check_device(cx, "upload");
+}
+
+inline void download(Context& cx, float* params, float* grads, float* m, float* v) {
+    std::vector<float> buf(static_cast<size_t>(cx.P_dev));
+    auto gather = [&](const float* dev, float* dst) {
+        MM_CUDA_CHECK(cudaMemcpyAsync(buf.data(), dev, sizeof(float) * cx.P_dev, cudaMemcpyDeviceToHost, cx.stream));
+        MM_CUDA_CHECK(cudaStreamSynchronize(cx.stream));
+        for (size_t i = 0; i < cx.params.size(); ++i) {
+            const auto& p = cx.params[i];
+            std::memcpy(dst + cx.flat_off[i], buf.data() + p.off, sizeof(float) * p.rows * p.cols);
+        }
+    };
+    if (params) gather(cx.w, params);
+    if ((grads || m || v) && !cx.trainable) fail(MM_INVALID_ARGUMENT, "inference context has no gradients or moments");
+    if (grads) gather(cx.g, grads);
+    if (m) gather(cx.m, m);
+    if (v) gather(cx.v, v);
+}
+
+} // namespace mm

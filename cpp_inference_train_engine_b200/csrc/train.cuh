@@ -1,0 +1,278 @@
+// Optimizer step, gradient all-reduce (NCCL over NVLink), the GRPO update and the batched
+// rollout driver.
+#pragma once
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include "decode.cuh"
+
+namespace mm {
+
+// ------------------------------------------------------------------ NCCL, loaded on demand
+// The library is opened at the first data-parallel call, so single-GPU use carries no
+// NCCL dependency and a process that already loaded one (e.g. through torch) reuses it.
+struct Nccl {
+    void* lib = nullptr;
+    ncclResult_t (*getUniqueId)(ncclUniqueId*) = nullptr;
+    ncclResult_t (*commInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*allReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*commDestroy)(ncclComm_t) = nullptr;
+    const char* (*getErrorString)(ncclResult_t) = nullptr;
+};
+inline Nccl& nccl() {
+    static Nccl n;
+    if (!n.lib) {
+        n.lib = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (!n.lib) fail(MM_UNSUPPORTED, std::string("cannot load libnccl.so.2: ") + dlerror());
+        n.getUniqueId = reinterpret_cast<decltype(n.getUniqueId)>(dlsym(n.lib, "ncclGetUniqueId"));
+        n.commInitRank = reinterpret_cast<decltype(n.commInitRank)>(dlsym(n.lib, "ncclCommInitRank"));
+        n.allReduce = reinterpret_cast<decltype(n.allReduce)>(dlsym(n.lib, "ncclAllReduce"));
+        n.commDestroy = reinterpret_cast<decltype(n.commDestroy)>(dlsym(n.lib, "ncclCommDestroy"));
+        n.getErrorString = reinterpret_cast<decltype(n.getErrorString)>(dlsym(n.lib, "ncclGetErrorString"));
+        if (!n.getUniqueId || !n.commInitRank || !n.allReduce || !n.commDestroy || !n.getErrorString)
+            fail(MM_UNSUPPORTED, "libnccl.so.2 lacks the expected symbols");
+    }
+    return n;
+}
+#define MM_NCCL_CHECK(x)                                                                     \
+    do {                                                                                     \
+        ncclResult_t r_ = (x);                                                               \
+        if (r_ != ncclSuccess) ::mm::fail(MM_GPU_ERROR, std::string(#x) + ": " + ::mm::nccl().getErrorString(r_)); \
+    } while (0)
+
+inline void allreduce(Context& cx, void* buf, size_t count, ncclDataType_t t, ncclRedOp_t op) {
+    if (cx.world <= 1 || !cx.nccl_comm) return;
+    MM_NCCL_CHECK(nccl().allReduce(buf, buf, count, t, op, static_cast<ncclComm_t>(cx.nccl_comm), cx.stream));
+}
+
+// ------------------------------------------------------------------ timing
+struct PhaseTimer {
+    Context& cx;
+    int ph;
+    cudaEvent_t start;
+    PhaseTimer(Context& c, int p) : cx(c), ph(p), start(c.prof_begin()) {}
+    ~PhaseTimer() { cx.prof_end(ph, start); }
+};
+
+// ------------------------------------------------------------------ AdamW
+// Execution::update: all-reduce, then Optimizer::step (optimizer.cpp:105-161).
+inline double adamw_update(Context& cx, float lr) {
+    if (!cx.trainable) fail(MM_INVALID_ARGUMENT, "Inference execution has no optimizer");
+    if (!std::isfinite(lr) || lr < 0) fail(MM_INVALID_ARGUMENT, "Invalid learning rate or uninitialized optimizer");
+    {
+        PhaseTimer t(cx, kPhAllreduce);
+        allreduce(cx, cx.g, static_cast<size_t>(cx.P_dev), ncclFloat32, ncclSum);
+    }
+    PhaseTimer t(cx, kPhAdamw);
+    MM_CUDA_CHECK(cudaMemsetAsync(cx.d_nonfinite, 0, 4, cx.stream));
+    MM_CUDA_CHECK(cudaMemsetAsync(cx.d_nonfinite_out, 0, 4, cx.stream));
+    MM_LAUNCH(adamw_norm_partial_kernel, cx.n_partial, 256, 0, cx.g, cx.P_dev, cx.d_partial, cx.d_nonfinite);
+    MM_LAUNCH(adamw_finalize_kernel, 1, 1024, 0, cx.d_partial, cx.n_partial, cx.opt.clip_norm, cx.d_norm, cx.d_gs);
+    const uint64_t next = cx.steps + 1;
+    const float bc1 = static_cast<float>(1.0 - std::pow(static_cast<double>(cx.opt.beta1), static_cast<double>(next)));
+    const float bc2 = static_cast<float>(1.0 - std::pow(static_cast<double>(cx.opt.beta2), static_cast<double>(next)));
+    dim3 grid(256, static_cast<unsigned>(cx.params.size()));
+    // w, g, m, v read + w, m, v written in fp32 + the fp16 shadow (3 copies for the table)
+    const double bytes = 28.0 * cx.P + 2.0 * cx.P + 4.0 * cx.c.V * cx.c.d;
+    MM_LAUNCH_TIMED(kKAdamw, bytes, adamw_update_kernel, grid, 256, 0, cx.d_params, cx.w, cx.g, cx.m, cx.v, cx.shadow,
+                    cx.d_gs, cx.d_nonfinite, lr, cx.opt.beta1, cx.opt.beta2, cx.opt.epsilon, bc1, bc2, cx.d_nonfinite_out);
+    int flags[2] = {0, 0};
+    double norm = 0;
+    MM_CUDA_CHECK(cudaMemcpyAsync(&flags[0], cx.d_nonfinite, 4, cudaMemcpyDeviceToHost, cx.stream));
+    MM_CUDA_CHECK(cudaMemcpyAsync(&flags[1], cx.d_nonfinite_out, 4, cudaMemcpyDeviceToHost, cx.stream));
+    MM_CUDA_CHECK(cudaMemcpyAsync(&norm, cx.d_norm, 8, cudaMemcpyDeviceToHost, cx.stream));
+    MM_CUDA_CHECK(cudaStreamSynchronize(cx.stream));
+    if (flags[0]) fail(MM_NUMERICAL_ERROR, "Nonfinite gradient before optimizer update");
+    cx.steps = next;
+    refresh_derived(cx, false);
+    if (flags[1]) fail(MM_NUMERICAL_ERROR, "Nonfinite optimizer output");
+    check_device(cx, "update");
+    return norm;
+}
+
+inline int chunk_tokens_default() {
+    static int v = [] {
+        const char* e = std::getenv("MM_CHUNK_TOKENS");
+        int x = e ? std::atoi(e) : 0;
+        return x > 0 ? x : 32768;
+    }();
+    return v;
+}
+
+// Teacher-forced log-probabilities of host batches [B][S] (Execution::log_probabilities),
+// chunked over whole sequences. Result into host `out` [B*S].
+inline void log_probs_host(Context& cx, const uint16_t* input, const uint16_t* target, int B, int S, float* out) {
+    PhaseTimer t(cx, kPhLogprob);
+    const int per = std::max(1, chunk_tokens_default() / S);
+    ensure_workspace(cx, std::min(B, per) * S, cx.ws.tape);
+    Workspace& w = cx.ws;
+    for (int r0 = 0; r0 < B; r0 += per) {
+        const int bc = std::min(per, B - r0);
+        const long long T = static_cast<long long>(bc) * S;
+        MM_CUDA_CHECK(cudaMemcpyAsync(w.tokens, input + r0 * static_cast<long long>(S), T * 2, cudaMemcpyHostToDevice, cx.stream));
+        MM_CUDA_CHECK(cudaMemcpyAsync(w.targets, target + r0 * static_cast<long long>(S), T * 2, cudaMemcpyHostToDevice, cx.stream));
+        forward_chunk(cx, bc, S, false, kVocabAll, true, nullptr, 0, 0, nullptr);
+        MM_CUDA_CHECK(cudaMemcpyAsync(out + r0 * static_cast<long long>(S), w.lp, T * 4, cudaMemcpyDeviceToHost, cx.stream));
+    }
+    check_device(cx, "log_probabilities");
+}
+
+// ------------------------------------------------------------------ GRPO update
+inline mm_step_result grpo_step(Context& pc, Context& rc, const uint16_t* input, const uint16_t* target,
+                                const float* mask, const float* old_lp, const float* rewards, int n, int S, int G,
+                                long long n_total, float clip, float klc, float lr) {
+    if (!pc.trainable) fail(MM_INVALID_ARGUMENT, "policy context must be trainable");
+    if (pc.device != rc.device) fail(MM_INVALID_ARGUMENT, "policy and reference must share a device");
+    if (n < 1 || G < 2 || n % G || S < 1 || S > pc.c.maxS || n_total < n)
+        fail(MM_INVALID_ARGUMENT, "rollouts must form whole groups within the context");
+    if (!std::isfinite(clip) || clip <= 0 || clip >= 1 || !std::isfinite(klc) || klc < 0)
+        fail(MM_NUMERICAL_ERROR, "Invalid or unbounded GRPO token statistics");
+    const long long NS = static_cast<long long>(n) * S;
+    std::vector<int> sup(n, 0);
+    for (int i = 0; i < n; ++i) {
+        for (int t = 0; t < S; ++t) {
+            const float mv = mask[static_cast<long long>(i) * S + t];
+            if (mv != 0.f && mv != 1.f) fail(MM_INVALID_ARGUMENT, "Loss mask must contain zero or one");
+            sup[i] += mv == 1.f ? 1 : 0;
+        }
+        if (sup[i] == 0) fail(MM_INVALID_ARGUMENT, "Batch has no supervised tokens");
+    }
+    for (long long i = 0; i < NS; ++i)
+        if (input[i] >= pc.c.V || target[i] >= pc.c.V) fail(MM_INVALID_ARGUMENT, "Input token exceeds vocabulary");
+    for (int i = 0; i < n; ++i)
+        if (!std::isfinite(rewards[i])) fail(MM_INVALID_ARGUMENT, "Invalid reward group");
+    char* base = static_cast<char*>(pc.stage.get(static_cast<size_t>(n) * 16 + 1024));
+    float* d_rew = reinterpret_cast<float*>(base);
+    float* d_adv = reinterpret_cast<float*>(base + round_up(n * 4LL, 256));
+    int* d_sup = reinterpret_cast<int*>(base + 2 * round_up(n * 4LL, 256));
+    MM_CUDA_CHECK(cudaMemcpyAsync(d_rew, rewards, n * 4, cudaMemcpyHostToDevice, pc.stream));
+    MM_CUDA_CHECK(cudaMemcpyAsync(d_sup, sup.data(), n * 4, cudaMemcpyHostToDevice, pc.stream));
+    MM_CUDA_CHECK(cudaMemsetAsync(pc.d_any, 0, 4, pc.stream));
+    MM_LAUNCH_CX(pc, advantages_kernel, blocks_for(n / G, 128), 128, 0, d_rew, n / G, G, 1e-6f, d_adv, pc.d_any);
+    allreduce(pc, pc.d_any, 1, ncclInt32, ncclMax);
+    int any = 0;
+    MM_CUDA_CHECK(cudaMemcpyAsync(&any, pc.d_any, 4, cudaMemcpyDeviceToHost, pc.stream));
+    MM_CUDA_CHECK(cudaStreamSynchronize(pc.stream));
+    mm_step_result res{};
+    if (!any) {
+        res.skipped = 1;
+        return res;
+    }
+    MM_CUDA_CHECK(cudaMemsetAsync(pc.g, 0, sizeof(float) * pc.P_dev, pc.stream));
+    MM_CUDA_CHECK(cudaMemsetAsync(pc.d_sums, 0, sizeof(GrpoSums), pc.stream));
+    const int per = std::max(1, chunk_tokens_default() / S);
+    ensure_workspace(pc, std::min(n, per) * S, true);
+    ensure_workspace(rc, std::min(n, per) * S, rc.ws.tape);
+    Workspace& w = pc.ws;
+    for (int r0 = 0; r0 < n; r0 += per) {
+        const int bc = std::min(per, n - r0);
+        const long long T = static_cast<long long>(bc) * S, off = static_cast<long long>(r0) * S;
+        {
+            PhaseTimer t(pc, kPhLogprob);
+            MM_CUDA_CHECK(cudaMemcpyAsync(rc.ws.tokens, input + off, T * 2, cudaMemcpyHostToDevice, rc.stream));
+            MM_CUDA_CHECK(cudaMemcpyAsync(rc.ws.targets, target + off, T * 2, cudaMemcpyHostToDevice, rc.stream));
+            forward_chunk(rc, bc, S, false, kVocabAll, true, nullptr, 0, 0, nullptr);
+            MM_CUDA_CHECK(cudaMemcpyAsync(w.tokens, input + off, T * 2, cudaMemcpyHostToDevice, pc.stream));
+            MM_CUDA_CHECK(cudaMemcpyAsync(w.targets, target + off, T * 2, cudaMemcpyHostToDevice, pc.stream));
+            MM_CUDA_CHECK(cudaMemcpyAsync(w.mask, mask + off, T * 4, cudaMemcpyHostToDevice, pc.stream));
+            MM_CUDA_CHECK(cudaMemcpyAsync(w.old_lp, old_lp + off, T * 4, cudaMemcpyHostToDevice, pc.stream));
+            // the reference's log-probs reach the policy stream only after its forward completes
+            MM_CUDA_CHECK(cudaStreamSynchronize(rc.stream));
+            MM_CUDA_CHECK(cudaMemcpyAsync(w.ref_lp, rc.ws.lp, T * 4, cudaMemcpyDeviceToDevice, pc.stream));
+            forward_chunk(pc, bc, S, true, kVocabAll, true, nullptr, 0, 0, nullptr);
+        }
+        PhaseTimer t(pc, kPhBackward);
+        MM_CUDA_CHECK(cudaMemsetAsync(&pc.d_sums->max_coef_bits, 0, 4, pc.stream));
+        MM_LAUNCH_CX(pc, grpo_coef_kernel, blocks_for(T, 256), 256, 0, w.lp, w.old_lp, w.ref_lp, w.mask, d_adv + r0,
+                     d_sup + r0, static_cast<int>(T), S, static_cast<double>(n_total), clip, klc, w.coef, pc.d_sums);
+        MM_LAUNCH_CX(pc, grad_scale_kernel, 1, 1, 0, pc.d_sums, pc.d_scale);
+        backward_chunk(pc, bc, S);
+    }
+    check_device(rc, "reference log_probabilities");
+    check_device(pc, "grpo backward");
+    GrpoSums sums{};
+    MM_CUDA_CHECK(cudaMemcpyAsync(&sums, pc.d_sums, sizeof(GrpoSums), cudaMemcpyDeviceToHost, pc.stream));
+    MM_CUDA_CHECK(cudaStreamSynchronize(pc.stream));
+    if (sums.rejected) fail(MM_NUMERICAL_ERROR, "Invalid or unbounded GRPO token statistics");
+    allreduce(pc, pc.d_sums, 2, ncclFloat64, ncclSum);
+    MM_CUDA_CHECK(cudaMemcpyAsync(&sums, pc.d_sums, sizeof(GrpoSums), cudaMemcpyDeviceToHost, pc.stream));
+    res.grad_norm = adamw_update(pc, lr);
+    res.loss = sums.loss;
+    res.kl = sums.kl;
+    return res;
+}
+
+__global__ void column_gather_kernel(const uint16_t* __restrict__ src, long long stride, int col, int B,
+                                     uint16_t* __restrict__ dst) {
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b < B) dst[b] = src[b * stride + col];
+}
+
+// rollout() for n prompts (trainer.cpp:187-213).
+inline void rollout(Context& cx, const uint16_t* prompts, int n, int P, int completion, int S, uint16_t eos,
+                    uint16_t pad, const uint64_t* seeds, float temperature, uint16_t* out_tokens, int32_t* out_len,
+                    uint16_t* out_input, uint16_t* out_target, float* out_mask, float* out_old_lp) {
+    const Dims& c = cx.c;
+    if (n < 1 || P < 1 || P > c.maxS || completion < 1) fail(MM_INVALID_ARGUMENT, "Prompt exceeds context or is empty");
+    if (!std::isfinite(temperature) || temperature < 0) fail(MM_INVALID_ARGUMENT, "Invalid generation settings");
+    const int length = std::min(completion, S + 1 - P);
+    if (length < 1) fail(MM_INVALID_ARGUMENT, "GRPO prompt leaves no room for a response");
+    if (P + length - 1 > c.maxS) fail(MM_INVALID_ARGUMENT, "Decode requires available context");
+    for (long long i = 0; i < static_cast<long long>(n) * P; ++i)
+        if (prompts[i] >= c.V) fail(MM_INVALID_ARGUMENT, "Input token exceeds vocabulary");
+    const int Sc = P + length - 1;
+    ensure_decode(cx, n, Sc, completion);
+    DecodeState& d = cx.dec;
+    uint16_t* d_prompts = static_cast<uint16_t*>(cx.stage.get(static_cast<size_t>(n) * P * 2));
+    MM_CUDA_CHECK(cudaMemcpyAsync(d_prompts, prompts, static_cast<size_t>(n) * P * 2, cudaMemcpyHostToDevice, cx.stream));
+    MM_CUDA_CHECK(cudaMemcpyAsync(d.seeds, seeds, static_cast<size_t>(n) * 8, cudaMemcpyHostToDevice, cx.stream));
+    {
+        PhaseTimer t(cx, kPhPrefill);
+        prefill_rows(cx, d_prompts, n, P, chunk_tokens_default());
+    }
+    for (int k = 0; k < length; ++k) {
+        if (k > 0) {
+            PhaseTimer t(cx, kPhDecode);
+            MM_LAUNCH(column_gather_kernel, blocks_for(n, 256), 256, 0, d.out_tok, (long long)completion, k - 1, n, d.tok);
+            cx.dec_len = P + k - 1;  // cache entries before this step's write
+            decode_step(cx);
+        }
+        PhaseTimer t(cx, kPhSample);
+        launch_sample(cx, d.logits, n, temperature, d.seeds, nullptr, k, nullptr, d.out_tok + k, completion);
+    }
+    std::vector<uint16_t> toks(static_cast<size_t>(n) * completion);
+    MM_CUDA_CHECK(cudaMemcpyAsync(toks.data(), d.out_tok, toks.size() * 2, cudaMemcpyDeviceToHost, cx.stream));
+    MM_CUDA_CHECK(cudaStreamSynchronize(cx.stream));
+    check_device(cx, "rollout");
+    for (int i = 0; i < n; ++i) {
+        int len = length;
+        for (int k = 0; k < length; ++k)
+            if (toks[static_cast<size_t>(i) * completion + k] == eos) {
+                len = k + 1;
+                break;
+            }
+        out_len[i] = len;
+        for (int k = 0; k < completion; ++k)
+            out_tokens[static_cast<size_t>(i) * completion + k] = k < len ? toks[static_cast<size_t>(i) * completion + k] : eos;
+    }
+    if (!out_old_lp) return;
+    // completion_batch (trainer.cpp:386-408) then the old-policy log-probabilities.
+    std::vector<uint16_t> inp(static_cast<size_t>(n) * S, pad), tgt(static_cast<size_t>(n) * S, pad);
+    std::vector<float> msk(static_cast<size_t>(n) * S, 0.f);
+    for (int i = 0; i < n; ++i) {
+        std::vector<uint16_t> ids(prompts + static_cast<size_t>(i) * P, prompts + static_cast<size_t>(i) * P + P);
+        ids.insert(ids.end(), out_tokens + static_cast<size_t>(i) * completion,
+                   out_tokens + static_cast<size_t>(i) * completion + out_len[i]);
+        for (size_t t = 0; t + 1 < ids.size(); ++t) {
+            inp[static_cast<size_t>(i) * S + t] = ids[t];
+            tgt[static_cast<size_t>(i) * S + t] = ids[t + 1];
+            msk[static_cast<size_t>(i) * S + t] = t + 1 >= static_cast<size_t>(P) ? 1.f : 0.f;
+        }
+    }
+    log_probs_host(cx, inp.data(), tgt.data(), n, S, out_old_lp);
+    if (out_input) std::memcpy(out_input, inp.data(), inp.size() * 2);
+    if (out_target) std::memcpy(out_target, tgt.data(), tgt.size() * 2);
+    if (out_mask) std::memcpy(out_mask, msk.data(), msk.size() * 4);
+}
+
+} // namespace mm

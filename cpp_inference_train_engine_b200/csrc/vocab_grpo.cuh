@@ -1,0 +1,378 @@
+// Vocabulary head, GRPO objective and sampling kernels.
+//
+//   logsoftmax_rows_kernel  weighted_nll's normaliser (ops.cpp:183-201): per row max,
+//                           z = sum exp(l - max) accumulated in double, lp = l_t - max - log z.
+//   vocab_grad_kernel       weighted_nll's gradient (ops.cpp:202-207), pre-scaled by the
+//                           chunk's power-of-two gradient scale, fp16 for the GEMMs.
+//   grpo_coef_kernel        grpo_objective + coefficient assembly (trainer.cpp:351-370,
+//                           827-846) for every supervised token, in double.
+//   advantages_kernel       group_advantages (trainer.cpp:371-385), one thread per group.
+//   sample_kernel           sample_token at top_p = 1, no penalties (inference.cpp:345-426).
+#pragma once
+#include "common.cuh"
+
+namespace mm {
+
+// One block per row. logits fp32 [T][ld]; writes lp[t] (float) and lse[t] = max + log z.
+__global__ void logsoftmax_rows_kernel(const float* __restrict__ logits, long long ld, int V,
+                                       const uint16_t* __restrict__ target, int T,
+                                       float* __restrict__ lp, float* __restrict__ lse, int* err) {
+    __shared__ float red_f[32];
+    __shared__ double red_d[32];
+    const int t = blockIdx.x;
+    if (t >= T) return;
+    const float* row = logits + t * ld;
+    float mx = -INFINITY;
+    for (int j = threadIdx.x; j < V; j += blockDim.x) mx = fmaxf(mx, row[j]);
+    mx = warp_max(mx);
+    if ((threadIdx.x & 31) == 0) red_f[threadIdx.x >> 5] = mx;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float v = threadIdx.x < (blockDim.x >> 5) ? red_f[threadIdx.x] : -INFINITY;
+        v = warp_max(v);
+        if (threadIdx.x == 0) red_f[0] = v;
+    }
+    __syncthreads();
+    mx = red_f[0];
+    double z = 0.0;
+    for (int j = threadIdx.x; j < V; j += blockDim.x) z += static_cast<double>(__expf(row[j] - mx));
+    z = warp_sum(z);
+    if ((threadIdx.x & 31) == 0) red_d[threadIdx.x >> 5] = z;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double s = 0.0;
+        for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) s += red_d[w];
+        const int tg = target ? target[t] : 0;
+        if (tg >= V) raise_error(err, kErrBadIndex);
+        const double l = log(s) + static_cast<double>(mx);
+        if (lse) lse[t] = static_cast<float>(l);
+        if (lp) {
+            const double v = static_cast<double>(row[min(tg, V - 1)]) - l;
+            if (!isfinite(v)) raise_error(err, kErrNonfinite);
+            lp[t] = static_cast<float>(v);
+        }
+    }
+}
+
+// g[t, j] = scale * coef[t] * (exp(l - lse) - [j == target]) in fp16, [T][ldg].
+__global__ void vocab_grad_kernel(const float* __restrict__ logits, long long ld, int V,
+                                  const uint16_t* __restrict__ target, const float* __restrict__ lse,
+                                  const float* __restrict__ coef, const float* __restrict__ scale,
+                                  int T, __half* __restrict__ g, long long ldg) {
+    const int t = blockIdx.x;
+    if (t >= T) return;
+    const float c = coef[t] * *scale;
+    const float L = lse[t];
+    const int tg = target[t];
+    const float* row = logits + t * ld;
+    __half* out = g + t * ldg;
+    if (c == 0.f) {
+        for (int j = threadIdx.x; j < V; j += blockDim.x) out[j] = __float2half_rn(0.f);
+        return;
+    }
+    for (int j = threadIdx.x; j < V; j += blockDim.x) {
+        const float p = __expf(row[j] - L);
+        out[j] = __float2half_rn(c * (p - (j == tg ? 1.f : 0.f)));
+    }
+}
+
+struct GrpoSums {
+    double loss, kl;
+    unsigned int max_coef_bits;  // max |coef| of the current chunk, as float bits
+    int rejected;
+};
+
+// Per token t of a chunk (rows t in [0, T), sequence = t / S): when mask[t] != 0,
+// coef[t] = nll_coefficient / (n_total * supervised[seq]) in float, and loss/kl sums
+// (objective/denominator) accumulate in double. Masked tokens get coef 0.
+__global__ void grpo_coef_kernel(const float* __restrict__ lp, const float* __restrict__ old_lp,
+                                 const float* __restrict__ ref_lp, const float* __restrict__ mask,
+                                 const float* __restrict__ adv, const int* __restrict__ supervised,
+                                 int T, int S, double n_total, float clip, float klc,
+                                 float* __restrict__ coef, GrpoSums* __restrict__ sums) {
+    __shared__ double sl[32], sk[32];
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    double lo = 0.0, kl = 0.0;
+    float cf = 0.f;
+    if (t < T) {
+        if (mask[t] != 0.f) {
+            const float a = lp[t], o = old_lp[t], r = ref_lp[t], A = adv[t / S];
+            if (!isfinite(a) || !isfinite(o) || !isfinite(r) || !isfinite(A) ||
+                fabsf(a - o) > 80.f || fabsf(r - a) > 80.f) {
+                atomicAdd(&sums->rejected, 1);
+            } else {
+                const double ratio = exp(static_cast<double>(a) - static_cast<double>(o));
+                const double clipped = fmin(fmax(ratio, 1.0 - static_cast<double>(clip)), 1.0 + static_cast<double>(clip));
+                const double delta = static_cast<double>(r) - static_cast<double>(a);
+                const double ed = exp(delta);
+                const double k3 = ed - delta - 1.0;
+                const double obj = -fmin(ratio * A, clipped * A) + static_cast<double>(klc) * k3;
+                // 1 + clip is float arithmetic in the reference (trainer.cpp:363).
+                const bool active = A >= 0.f ? ratio <= static_cast<double>(1.f + clip)
+                                             : ratio >= static_cast<double>(1.f - clip);
+                const double c = (active ? ratio * A : 0.0) + static_cast<double>(klc) * (ed - 1.0);
+                const double den = n_total * static_cast<double>(supervised[t / S]);
+                lo = obj / den;
+                kl = k3 / den;
+                cf = static_cast<float>(c / den);
+                if (!isfinite(obj) || !isfinite(c)) atomicAdd(&sums->rejected, 1);
+            }
+        }
+        coef[t] = cf;
+    }
+    lo = warp_sum(lo);
+    kl = warp_sum(kl);
+    float am = fabsf(cf);
+    am = warp_max(am);
+    if ((threadIdx.x & 31) == 0) {
+        sl[threadIdx.x >> 5] = lo;
+        sk[threadIdx.x >> 5] = kl;
+        if (am > 0.f) atomicMax(&sums->max_coef_bits, __float_as_uint(am));
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double a = 0.0, b = 0.0;
+        for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) {
+            a += sl[w];
+            b += sk[w];
+        }
+        atomicAdd(&sums->loss, a);
+        atomicAdd(&sums->kl, b);
+    }
+}
+
+// scale = 2^-floor(log2(max|coef|)) so that the largest scaled coefficient lies in [1, 2);
+// inv = 1 / scale. Exact powers of two: the backward pass is linear in the coefficients.
+__global__ void grad_scale_kernel(const GrpoSums* __restrict__ sums, float* __restrict__ scale_inv) {
+    const float m = __uint_as_float(sums->max_coef_bits);
+    float s = 1.f;
+    if (m > 0.f && isfinite(m)) s = exp2f(-floorf(log2f(m)));
+    scale_inv[0] = s;
+    scale_inv[1] = 1.f / s;
+}
+
+// group_advantages for groups of G consecutive rewards.
+__global__ void advantages_kernel(const float* __restrict__ rewards, int n_groups, int G, float eps,
+                                  float* __restrict__ adv, int* __restrict__ any_nonzero) {
+    const int g = blockIdx.x * blockDim.x + threadIdx.x;
+    if (g >= n_groups) return;
+    const float* r = rewards + g * G;
+    double mean = 0.0;
+    for (int i = 0; i < G; ++i) mean += r[i];
+    mean /= static_cast<double>(G);
+    double sq = 0.0;
+    for (int i = 0; i < G; ++i) sq += (r[i] - mean) * (r[i] - mean);
+    const double scale = sqrt(sq / static_cast<double>(G)) + static_cast<double>(eps);
+    for (int i = 0; i < G; ++i) {
+        const float a = static_cast<float>((r[i] - mean) / scale);
+        adv[g * G + i] = a;
+        if (a != 0.f) atomicOr(any_nonzero, 1);
+    }
+}
+
+// ------------------------------------------------------------------ sampling
+__device__ __forceinline__ uint64_t splitmix_mix(uint64_t z) {
+    z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
+    z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
+    return z ^ (z >> 31);
+}
+// Draw k (0-based) of Rng(seed).uniform() (rng.hpp:10-18): splitmix64 is a counter
+// generator, state after k+1 calls is seed + (k+1) * golden gamma.
+__device__ __forceinline__ float rng_uniform_at(uint64_t seed, uint32_t k) {
+    const uint64_t x = splitmix_mix(seed + static_cast<uint64_t>(k + 1) * 0x9e3779b97f4a7c15ull);
+    return (static_cast<float>(x >> 40) + 0.5f) / 16777216.0f;
+}
+// Order-preserving map of a float to uint32 (larger float -> larger key).
+__device__ __forceinline__ uint32_t float_key(float f) {
+    const uint32_t u = __float_as_uint(f);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+constexpr int kSampleThreads = 512;
+constexpr int kSampleBuckets = 2048;
+constexpr int kSampleCap = 1024;
+
+// One block per sequence row of logits [B][ld] (vocab V <= 65535). Greedy when
+// temperature == 0 (first index of the maximum). Otherwise the exact inverse CDF of
+// sample_token with top_p = 1: scores sorted descending (ties: lower id first), weights
+// w = exp(double(s - s0) / T), draw = u * sum(w), first index where the running
+// remainder reaches <= 0. The sorted order is found without a full sort: a histogram
+// of weight mass over the top bits of the order key locates the bucket holding the
+// crossing, then the next bits, until at most kSampleCap candidates remain, which are
+// sorted in shared memory and walked in order.
+// Rows with active[b] == 0 are skipped. out[b * out_stride] receives the token.
+__global__ void __launch_bounds__(kSampleThreads) sample_kernel(
+    const float* __restrict__ logits, long long ld, int V, float temperature,
+    const uint64_t* __restrict__ seeds, const int* __restrict__ draw_index, int draw_offset,
+    const int* __restrict__ active, uint16_t* __restrict__ out, long long out_stride) {
+    __shared__ double hist[kSampleBuckets];
+    __shared__ int hcount[kSampleBuckets];
+    __shared__ uint32_t cand_key[kSampleCap];
+    __shared__ int cand_id[kSampleCap];
+    __shared__ double cand_w[kSampleCap];
+    __shared__ float red_f[32];
+    __shared__ int red_i[32];
+    __shared__ double red_d[32];
+    __shared__ double s_draw, s_total;
+    __shared__ uint32_t s_prefix;
+    __shared__ int s_bits, s_ncand, s_done, s_choice;
+
+    const int b = blockIdx.x;
+    if (active && !active[b]) return;
+    const float* row = logits + b * ld;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+
+    // max score and its first index
+    float mx = -INFINITY;
+    int mi = 0x7fffffff;
+    for (int j = threadIdx.x; j < V; j += blockDim.x) {
+        const float v = row[j];
+        if (v > mx) { mx = v; mi = j; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, mx, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, mi, o);
+        if (ov > mx || (ov == mx && oi < mi)) { mx = ov; mi = oi; }
+    }
+    if (lane == 0) { red_f[warp] = mx; red_i[warp] = mi; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float bm = red_f[0];
+        int bi = red_i[0];
+        for (int w = 1; w < nw; ++w)
+            if (red_f[w] > bm || (red_f[w] == bm && red_i[w] < bi)) { bm = red_f[w]; bi = red_i[w]; }
+        red_f[0] = bm;
+        red_i[0] = bi;
+    }
+    __syncthreads();
+    const float s0 = red_f[0];
+    if (temperature == 0.f) {
+        if (threadIdx.x == 0) out[b * out_stride] = static_cast<uint16_t>(red_i[0]);
+        return;
+    }
+    const double invT = 1.0 / static_cast<double>(temperature);
+    // total mass
+    double tot = 0.0;
+    for (int j = threadIdx.x; j < V; j += blockDim.x)
+        tot += exp(static_cast<double>(row[j] - s0) * invT);
+    tot = warp_sum(tot);
+    if (lane == 0) red_d[warp] = tot;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double s = 0.0;
+        for (int w = 0; w < nw; ++w) s += red_d[w];
+        s_total = s;
+        const int k = (draw_index ? draw_index[b] : 0) + draw_offset;
+        s_draw = static_cast<double>(rng_uniform_at(seeds[b], static_cast<uint32_t>(k))) * s;
+        s_prefix = 0;
+        s_bits = 0;
+        s_done = 0;
+        s_choice = -1;
+    }
+    __syncthreads();
+    // Radix descent: 11 bits per level over the 32-bit key.
+    while (true) {
+        const int bits = s_bits;
+        const uint32_t prefix = s_prefix;
+        const int width = min(11, 32 - bits);
+        const int nb = 1 << width;
+        for (int i = threadIdx.x; i < nb; i += blockDim.x) { hist[i] = 0.0; hcount[i] = 0; }
+        __syncthreads();
+        for (int j = threadIdx.x; j < V; j += blockDim.x) {
+            const float v = row[j];
+            const uint32_t key = float_key(v);
+            if (bits == 0 || (key >> (32 - bits)) == prefix) {
+                const int bk = static_cast<int>((key >> (32 - bits - width)) & (nb - 1));
+                atomicAdd(&hist[bk], exp(static_cast<double>(v - s0) * invT));
+                atomicAdd(&hcount[bk], 1);
+            }
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            // walk buckets from the highest key down
+            double rem = s_draw;
+            int chosen = -1, last_nonempty = -1;
+            for (int i = nb - 1; i >= 0; --i) {
+                if (hcount[i] == 0) continue;
+                last_nonempty = i;
+                if (rem - hist[i] <= 0.0) { chosen = i; break; }
+                rem -= hist[i];
+            }
+            if (chosen < 0) { chosen = last_nonempty; rem = hist[chosen] * 2.0 + 1.0; }
+            s_draw = rem;
+            s_prefix = (prefix << width) | static_cast<uint32_t>(chosen);
+            s_bits = bits + width;
+            s_ncand = hcount[chosen];
+            s_done = (s_ncand <= kSampleCap || s_bits >= 32) ? 1 : 0;
+        }
+        __syncthreads();
+        if (s_done) break;
+    }
+    // gather candidates of the chosen key prefix
+    if (threadIdx.x == 0) s_ncand = 0;
+    __syncthreads();
+    const int bits = s_bits;
+    const uint32_t prefix = s_prefix;
+    for (int j = threadIdx.x; j < V; j += blockDim.x) {
+        const float v = row[j];
+        const uint32_t key = float_key(v);
+        if ((bits >= 32 ? key : (key >> (32 - bits))) == (bits >= 32 ? prefix : prefix)) {
+            const int slot = atomicAdd(&s_ncand, 1);
+            if (slot < kSampleCap) {
+                cand_key[slot] = key;
+                cand_id[slot] = j;
+                cand_w[slot] = exp(static_cast<double>(v - s0) * invT);
+            }
+        }
+    }
+    __syncthreads();
+    const int n = min(s_ncand, kSampleCap);
+    // bitonic sort of up to kSampleCap candidates: key descending, id ascending
+    for (int i = n + threadIdx.x; i < kSampleCap; i += blockDim.x) {
+        cand_key[i] = 0;
+        cand_id[i] = 0x7fffffff;
+        cand_w[i] = 0.0;
+    }
+    __syncthreads();
+    for (int size = 2; size <= kSampleCap; size <<= 1) {
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            for (int i = threadIdx.x; i < kSampleCap; i += blockDim.x) {
+                const int jx = i ^ stride;
+                if (jx > i) {
+                    const bool desc = (i & size) == 0;
+                    // "before" = larger key, or equal key and smaller id
+                    const bool i_before = cand_key[i] > cand_key[jx] ||
+                                          (cand_key[i] == cand_key[jx] && cand_id[i] < cand_id[jx]);
+                    if (desc != i_before) {
+                        const uint32_t tk = cand_key[i]; cand_key[i] = cand_key[jx]; cand_key[jx] = tk;
+                        const int ti = cand_id[i]; cand_id[i] = cand_id[jx]; cand_id[jx] = ti;
+                        const double tw = cand_w[i]; cand_w[i] = cand_w[jx]; cand_w[jx] = tw;
+                    }
+                }
+            }
+            __syncthreads();
+        }
+    }
+    if (threadIdx.x == 0) {
+        double rem = s_draw;
+        int pick = n > 0 ? cand_id[n - 1] : red_i[0];
+        for (int i = 0; i < n; ++i) {
+            rem -= cand_w[i];
+            if (rem <= 0.0) { pick = cand_id[i]; break; }
+        }
+        out[b * out_stride] = static_cast<uint16_t>(pick);
+    }
+}
+
+} // namespace mm
+
+namespace mm {
+// max |x| over n floats, as float bits into *out (atomicMax on non-negative floats).
+__global__ void absmax_kernel(const float* __restrict__ x, int n, unsigned int* __restrict__ out) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    float v = i < n ? fabsf(x[i]) : 0.f;
+    v = warp_max(v);
+    if ((threadIdx.x & 31) == 0 && v > 0.f) atomicMax(out, __float_as_uint(v));
+}
+} // namespace mm

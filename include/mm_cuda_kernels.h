@@ -1,0 +1,41 @@
+/*
+ * mm_cuda_kernels.h -- kernel-level entry points of the sm_100a backend on DEVICE pointers,
+ * for the parity tests and the benchmark's timing. They have no counterpart in the
+ * reference's Execution interface (the reference's GPU path is MPSGraph programs,
+ * src/backends/mps_backend.mm:1597-1738); they expose single kernels of the same path.
+ */
+#ifndef MM_CUDA_KERNELS_H
+#define MM_CUDA_KERNELS_H
+
+#include <stdint.h>
+
+#include "mm_cuda.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Tensor-core GEMM: out[M][N] = alpha * A * B (+ residual), fp16 (or bf16) operands,
+ * fp32 accumulation. A is [M][K] rows (a_mn = 0) or [K][M] rows (a_mn = 1); B is [N][K]
+ * rows (b_mn = 0) or [K][N] rows (b_mn = 1); pitches in elements, multiples of 8.
+ * out_kind: 0 fp32 store, 1 fp32 accumulate (+=), 2 fp16 store, 3 bf16 store.
+ * residual (fp32 [M][ldr], may be NULL) is added for out_kind 0. */
+int mm_cuda_gemm_f16(mm_cuda_ctx* ctx, int M, int N, int K, const void* a, int64_t lda, int a_mn,
+                     const void* b, int64_t ldb, int b_mn, void* out, int64_t ldc, int out_kind,
+                     float alpha, const float* residual, int64_t ldr, int bf16);
+
+/* Device time (CUDA events on the context's stream, resolved at this call) accumulated
+ * since the last reset, 16 entries each of ms, calls and algorithmic work:
+ *   0-7  phases: prefill, decode, sample, logprob, backward, adamw, allreduce, prep;
+ *   8-15 kernel classes: gemm (flops), decode attention (bytes), flash forward (flops),
+ *        flash backward (flops), sampler (bytes), log-softmax (bytes), adamw (bytes), other.
+ * enable: 1 start/reset, 0 stop/reset, -1 read only. Any pointer may be NULL. */
+int mm_cuda_profile(mm_cuda_ctx* ctx, int enable, double* ms, int64_t* calls, double* work);
+
+/* The context's CUDA stream (cudaStream_t), for events recorded by a caller. */
+int mm_cuda_stream(mm_cuda_ctx* ctx, void** stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MM_CUDA_KERNELS_H */

@@ -1,0 +1,68 @@
+"""Batched latent-cache decode and the on-device sampler against the reference's
+CpuDecoder and sample_token."""
+import numpy as np
+import pytest
+
+import cpp_inference_train_engine_b200 as E
+from cpp_inference_train_engine_b200.config import MLA36M, TINY
+from oracle import mla_oracle as O
+from oracle import ref
+from tests.gpu_util import require_gpu
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module", params=["tiny", "36m"])
+def setup(request):
+    require_gpu()
+    if not ref.available():
+        pytest.skip("oracle/_ref not built")
+    cfg = TINY if request.param == "tiny" else MLA36M
+    W = E.init_params(cfg, 3)
+    return cfg, W, E.make_execution(cfg, W)
+
+
+def test_prefill_and_decode_match_reference_decoder(setup):
+    cfg, W, ex = setup
+    rng = np.random.default_rng(1)
+    B, P, steps = 3, 17, 12
+    prompts = rng.integers(0, min(256, cfg.vocab_size), (B, P)).astype(np.uint16)
+    sessions = [ref.Session(cfg, 3) for _ in range(B)]
+    want = np.stack([s.prefill(prompts[b]) for b, s in enumerate(sessions)])
+    got = ex.prefill_batch(prompts)
+    tol = 5e-3 if cfg is TINY else 2e-2
+    assert np.abs(got - want).max() < tol
+    agree = total = 0
+    for k in range(steps):
+        # teacher-force the reference's greedy choice so one divergence cannot compound
+        tok = want.argmax(axis=1).astype(np.uint16)
+        top2 = np.sort(want, axis=1)[:, -2:]
+        margin = top2[:, 1] - top2[:, 0]
+        mine = got.argmax(axis=1)
+        for b in range(B):
+            if margin[b] > 1e-3:
+                total += 1
+                agree += int(mine[b] == tok[b])
+        want = np.stack([s.decode(tok[b]) for b, s in enumerate(sessions)])
+        got = ex.decode_batch(tok)
+        assert np.abs(got - want).max() < tol, k
+    assert agree == total
+
+
+def test_sampler_matches_reference_sample_token():
+    require_gpu()
+    execs = {264: E.CudaExecution(TINY), 16384: E.CudaExecution(MLA36M)}
+    rng = np.random.default_rng(7)
+    for V in (264, 16384):
+        ex = execs[V]
+        B = 64
+        logits = (rng.normal(size=(B, V)) * rng.uniform(0.2, 3, size=(B, 1))).astype(np.float32)
+        logits[::7, :50] = logits[::7, :50].max()  # ties
+        seeds = rng.integers(0, 2 ** 63, B).astype(np.uint64)
+        draws = rng.integers(0, 300, B).astype(np.int32)
+        for temp in (1.0, 0.7, 0.0):
+            got = ex.sample(logits, temp, seeds, draws)
+            for b in range(B):
+                st = (int(seeds[b]) + int(draws[b]) * 0x9E3779B97F4A7C15) % 2 ** 64
+                tok, _ = ref.sample_token(logits[b], st, temperature=temp)
+                assert got[b] == tok, (V, temp, b)

@@ -1,221 +1,13 @@
-// Attention kernels.
-//
-// Teacher-forced passes (ops::attention / ops::attention_backward, ops.cpp:109-172):
-// causal softmax attention per (sequence, head) with qk = nope + rope and value width dv,
-// computed tile by tile with an online softmax so the [T, T] probability matrix of the
-// reference is never written. Forward stores the output (fp16) and the row log-sum-exp;
-// backward recomputes probabilities from them. Tiles of 64 keys/queries are staged in
-// shared memory; each thread owns one query (forward, dq) or one key (dk, dv).
+// Decode attention.
 //
 // Decode (CpuDecoder::decode, inference.cpp:116-153, absorbed form): every head of a
 // sequence attends over the same compressed cache row [latent kv_rank | rope], so one CTA
 // per sequence stages cache tiles once and its warps (one per head) all read them.
 #pragma once
 #include "common.cuh"
+#include "flash_mma.cuh"
 
 namespace mm {
-
-constexpr int kAttTile = 64;
-
-// Forward. q, k: fp16 [B*S][H*QK]; v: fp16 [B*S][H*DV]. out fp16 [B*S][H*DV],
-// lse fp32 [B*S][H] (natural log). grid (ceil(S/64), H, B), block 64.
-template <int QK, int DV>
-__global__ void __launch_bounds__(64) flash_fwd_kernel(const __half* __restrict__ q,
-                                                       const __half* __restrict__ k,
-                                                       const __half* __restrict__ v, int S, int H,
-                                                       float scale, __half* __restrict__ out,
-                                                       float* __restrict__ lse) {
-    __shared__ float Ks[kAttTile][QK + 1];
-    __shared__ float Vs[kAttTile][DV + 1];
-    const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-    const int i = qt * kAttTile + threadIdx.x;  // query position
-    const long long base = static_cast<long long>(b) * S;
-    const int ldq = H * QK, ldv = H * DV;
-    float qr[QK], o[DV];
-    if (i < S) {
-#pragma unroll
-        for (int c = 0; c < QK; ++c) qr[c] = __half2float(q[(base + i) * ldq + h * QK + c]) * scale;
-    }
-#pragma unroll
-    for (int c = 0; c < DV; ++c) o[c] = 0.f;
-    float m = -INFINITY, l = 0.f;
-    for (int kt = 0; kt <= qt; ++kt) {
-        __syncthreads();
-        for (int e = threadIdx.x; e < kAttTile * QK; e += blockDim.x) {
-            const int r = e / QK, c = e % QK, j = kt * kAttTile + r;
-            Ks[r][c] = j < S ? __half2float(k[(base + j) * ldq + h * QK + c]) : 0.f;
-        }
-        for (int e = threadIdx.x; e < kAttTile * DV; e += blockDim.x) {
-            const int r = e / DV, c = e % DV, j = kt * kAttTile + r;
-            Vs[r][c] = j < S ? __half2float(v[(base + j) * ldv + h * DV + c]) : 0.f;
-        }
-        __syncthreads();
-        if (i < S) {
-            const int jmax = min(kAttTile, i - kt * kAttTile + 1);
-            for (int r = 0; r < jmax; ++r) {
-                float s = 0.f;
-#pragma unroll
-                for (int c = 0; c < QK; ++c) s += qr[c] * Ks[r][c];
-                if (s > m) {
-                    const float corr = __expf(m - s);
-                    l *= corr;
-#pragma unroll
-                    for (int c = 0; c < DV; ++c) o[c] *= corr;
-                    m = s;
-                }
-                const float p = __expf(s - m);
-                l += p;
-#pragma unroll
-                for (int c = 0; c < DV; ++c) o[c] += p * Vs[r][c];
-            }
-        }
-    }
-    if (i < S) {
-        const float inv = 1.0f / l;
-#pragma unroll
-        for (int c = 0; c < DV; ++c) out[(base + i) * ldv + h * DV + c] = __float2half_rn(o[c] * inv);
-        lse[(base + i) * H + h] = m + logf(l);
-    }
-}
-
-// D[t, h] = sum_c dO[t, h, c] * O[t, h, c] (the softmax-backward row term).
-__global__ void attn_bwd_dot_kernel(const float* __restrict__ dout, const __half* __restrict__ out,
-                                    int T, int H, int DV, float* __restrict__ D) {
-    const int idx = blockIdx.x * blockDim.x + threadIdx.x;
-    if (idx >= T * H) return;
-    const int t = idx / H, h = idx % H;
-    const long long o = static_cast<long long>(t) * H * DV + h * DV;
-    float s = 0.f;
-    for (int c = 0; c < DV; ++c) s += dout[o + c] * __half2float(out[o + c]);
-    D[idx] = s;
-}
-
-// dK, dV for one key tile. dout fp32 [B*S][H*DV]. dk fp32 [B*S][H*QK] (already scaled by
-// `scale`), dv fp32 [B*S][H*DV]. grid (ceil(S/64), H, B), block 64 (one key per thread).
-template <int QK, int DV>
-__global__ void __launch_bounds__(64) flash_bwd_dkdv_kernel(
-    const __half* __restrict__ q, const __half* __restrict__ k, const __half* __restrict__ v,
-    const float* __restrict__ dout, const float* __restrict__ lse, const float* __restrict__ D,
-    int S, int H, float scale, float* __restrict__ dk, float* __restrict__ dv) {
-    __shared__ float Qs[kAttTile][QK + 1];
-    __shared__ float Gs[kAttTile][DV + 1];
-    __shared__ float Ls[kAttTile], Ds[kAttTile];
-    const int kt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-    const int j = kt * kAttTile + threadIdx.x;
-    const long long base = static_cast<long long>(b) * S;
-    const int ldq = H * QK, ldv = H * DV;
-    float kr[QK], vr[DV], dkr[QK], dvr[DV];
-#pragma unroll
-    for (int c = 0; c < QK; ++c) {
-        kr[c] = j < S ? __half2float(k[(base + j) * ldq + h * QK + c]) : 0.f;
-        dkr[c] = 0.f;
-    }
-#pragma unroll
-    for (int c = 0; c < DV; ++c) {
-        vr[c] = j < S ? __half2float(v[(base + j) * ldv + h * DV + c]) : 0.f;
-        dvr[c] = 0.f;
-    }
-    const int ntiles = (S + kAttTile - 1) / kAttTile;
-    for (int qt = kt; qt < ntiles; ++qt) {
-        __syncthreads();
-        for (int e = threadIdx.x; e < kAttTile * QK; e += blockDim.x) {
-            const int r = e / QK, c = e % QK, i = qt * kAttTile + r;
-            Qs[r][c] = i < S ? __half2float(q[(base + i) * ldq + h * QK + c]) : 0.f;
-        }
-        for (int e = threadIdx.x; e < kAttTile * DV; e += blockDim.x) {
-            const int r = e / DV, c = e % DV, i = qt * kAttTile + r;
-            Gs[r][c] = i < S ? dout[(base + i) * ldv + h * DV + c] : 0.f;
-        }
-        {
-            const int i = qt * kAttTile + threadIdx.x;
-            Ls[threadIdx.x] = i < S ? lse[(base + i) * H + h] : 0.f;
-            Ds[threadIdx.x] = i < S ? D[(base + i) * H + h] : 0.f;
-        }
-        __syncthreads();
-        if (j < S) {
-            const int rmin = qt == kt ? threadIdx.x : 0;
-            const int rmax = min(kAttTile, S - qt * kAttTile);
-            for (int r = rmin; r < rmax; ++r) {
-                float s = 0.f;
-#pragma unroll
-                for (int c = 0; c < QK; ++c) s += Qs[r][c] * kr[c];
-                const float p = __expf(s * scale - Ls[r]);
-                float dp = 0.f;
-#pragma unroll
-                for (int c = 0; c < DV; ++c) {
-                    dp += Gs[r][c] * vr[c];
-                    dvr[c] += p * Gs[r][c];
-                }
-                const float ds = p * (dp - Ds[r]) * scale;
-#pragma unroll
-                for (int c = 0; c < QK; ++c) dkr[c] += ds * Qs[r][c];
-            }
-        }
-    }
-    if (j < S) {
-#pragma unroll
-        for (int c = 0; c < QK; ++c) dk[(base + j) * ldq + h * QK + c] = dkr[c];
-#pragma unroll
-        for (int c = 0; c < DV; ++c) dv[(base + j) * ldv + h * DV + c] = dvr[c];
-    }
-}
-
-// dQ for one query tile (one query per thread). dq fp32 [B*S][H*QK], scaled by `scale`.
-template <int QK, int DV>
-__global__ void __launch_bounds__(64) flash_bwd_dq_kernel(
-    const __half* __restrict__ q, const __half* __restrict__ k, const __half* __restrict__ v,
-    const float* __restrict__ dout, const float* __restrict__ lse, const float* __restrict__ D,
-    int S, int H, float scale, float* __restrict__ dq) {
-    __shared__ float Ks[kAttTile][QK + 1];
-    __shared__ float Vs[kAttTile][DV + 1];
-    const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-    const int i = qt * kAttTile + threadIdx.x;
-    const long long base = static_cast<long long>(b) * S;
-    const int ldq = H * QK, ldv = H * DV;
-    float qr[QK], gr[DV], dqr[QK];
-    float li = 0.f, di = 0.f;
-    if (i < S) {
-        li = lse[(base + i) * H + h];
-        di = D[(base + i) * H + h];
-    }
-#pragma unroll
-    for (int c = 0; c < QK; ++c) {
-        qr[c] = i < S ? __half2float(q[(base + i) * ldq + h * QK + c]) : 0.f;
-        dqr[c] = 0.f;
-    }
-#pragma unroll
-    for (int c = 0; c < DV; ++c) gr[c] = i < S ? dout[(base + i) * ldv + h * DV + c] : 0.f;
-    for (int kt = 0; kt <= qt; ++kt) {
-        __syncthreads();
-        for (int e = threadIdx.x; e < kAttTile * QK; e += blockDim.x) {
-            const int r = e / QK, c = e % QK, j = kt * kAttTile + r;
-            Ks[r][c] = j < S ? __half2float(k[(base + j) * ldq + h * QK + c]) : 0.f;
-        }
-        for (int e = threadIdx.x; e < kAttTile * DV; e += blockDim.x) {
-            const int r = e / DV, c = e % DV, j = kt * kAttTile + r;
-            Vs[r][c] = j < S ? __half2float(v[(base + j) * ldv + h * DV + c]) : 0.f;
-        }
-        __syncthreads();
-        if (i < S) {
-            const int jmax = min(kAttTile, i - kt * kAttTile + 1);
-            for (int r = 0; r < jmax; ++r) {
-                float s = 0.f, dp = 0.f;
-#pragma unroll
-                for (int c = 0; c < QK; ++c) s += qr[c] * Ks[r][c];
-#pragma unroll
-                for (int c = 0; c < DV; ++c) dp += gr[c] * Vs[r][c];
-                const float p = __expf(s * scale - li);
-                const float ds = p * (dp - di) * scale;
-#pragma unroll
-                for (int c = 0; c < QK; ++c) dqr[c] += ds * Ks[r][c];
-            }
-        }
-    }
-    if (i < S) {
-#pragma unroll
-        for (int c = 0; c < QK; ++c) dq[(base + i) * ldq + h * QK + c] = dqr[c];
-    }
-}
 
 // Absorbed latent decode attention for one new token per sequence.
 // qf fp32 [B][H][KV + R]: per head the absorbed query (W_uk folded in) then the rotated
@@ -282,6 +74,176 @@ __global__ void decode_attention_kernel(const float* __restrict__ qf, const __ha
             const int c = lane + 32 * u;
             if (c < KV) ctx[static_cast<long long>(b) * H * KV + warp * KV + c] = __float2half_rn(acc[u] * inv);
         }
+    }
+}
+
+// Tensor-core form for 8 heads over a [128 latent | 16 rope] cache row (the 35.8M model).
+// The 8 heads are exactly the N = 8 of mma.sync m16n8k16, so per 16 cached positions a warp
+// computes S^T = C[16 x 144] * Q^T (9 MMAs) and O^T += C^T[128 x 16] * P^T (8 MMAs, C^T via
+// transposed ldmatrix). Each warp keeps its own online-softmax state over its share of the
+// positions; the 4 warps of a CTA are merged through shared memory. For few sequences the
+// context is also split over gridDim.y CTAs (flash-decoding): each writes a partial
+// (max, sum, O) to `part` and decode_attention_combine_kernel merges them.
+namespace dec {
+constexpr int H = 8, KV = 128, R = 16, W = KV + R;
+constexpr int LDQ = W + 8;    // padded rows: 16-byte aligned, conflict-free ldmatrix
+constexpr int LDP = 16 + 8;
+constexpr int kWarps = 4;
+}  // namespace dec
+
+__global__ void __launch_bounds__(128) decode_attention_mma_kernel(
+    const float* __restrict__ qf, const __half* __restrict__ cache, long long cache_seq_stride,
+    const int* __restrict__ pos, float scale, __half* __restrict__ ctx, float* __restrict__ part) {
+    using namespace dec;
+    using fa::ldsm_x4;
+    using fa::ldsm_x4_t;
+    using fa::mma16816;
+    __shared__ __align__(16) __half Qs[H][LDQ];
+    __shared__ __align__(16) __half Cw[kWarps][16][LDQ];
+    __shared__ __align__(16) __half Pw[kWarps][H][LDP];
+    __shared__ float Mw[kWarps][H], Lw[kWarps][H];
+    __shared__ float Ow[kWarps][H][KV];
+    const int b = blockIdx.x, sp = blockIdx.y, nsplit = gridDim.y;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const int n = pos[b] + 1;
+    const int tiles = (n + 15) / 16;
+    const int per = (tiles + nsplit - 1) / nsplit;
+    const int t_begin = sp * per, t_end = min(tiles, t_begin + per);
+    const float qscale = scale * fa::kLog2e;
+    for (int e = threadIdx.x; e < H * W; e += blockDim.x)
+        Qs[e / W][e % W] = __float2half_rn(qf[static_cast<long long>(b) * H * W + e] * qscale);
+    __syncthreads();
+    // B fragments of Q^T (k = dims, n = heads) for all 9 k-steps, loaded once.
+    uint32_t qb[W / 16][2];
+#pragma unroll
+    for (int kk = 0; kk < W / 16; ++kk) {
+        uint32_t r[4];
+        ldsm_x4(r, &Qs[lane & 7][kk * 16 + ((lane >> 3) & 1) * 8]);  // lanes 16-31 repeat 0-15
+        qb[kk][0] = r[0];
+        qb[kk][1] = r[1];
+    }
+    const __half* cb = cache + static_cast<long long>(b) * cache_seq_stride;
+    float acc[KV / 16][4];
+#pragma unroll
+    for (int i = 0; i < KV / 16; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;  // heads 2t, 2t+1
+    for (int tile = t_begin + warp; tile < t_end; tile += kWarps) {
+        const int p0 = tile * 16;
+        // 16 rows x 18 16-byte vectors
+        for (int e = lane; e < 16 * (W / 8); e += 32) {
+            const int r = e / (W / 8), cc = (e % (W / 8)) * 8;
+            uint4 v = make_uint4(0, 0, 0, 0);
+            if (p0 + r < n) v = *reinterpret_cast<const uint4*>(cb + static_cast<long long>(p0 + r) * W + cc);
+            *reinterpret_cast<uint4*>(&Cw[warp][r][cc]) = v;
+        }
+        __syncwarp();
+        float s[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int kk = 0; kk < W / 16; ++kk) {
+            uint32_t a[4];
+            ldsm_x4(a, &Cw[warp][lane & 15][kk * 16 + (lane >> 4) * 8]);
+            mma16816(s, a, qb[kk][0], qb[kk][1]);
+        }
+        if (p0 + g >= n) { s[0] = -INFINITY; s[1] = -INFINITY; }
+        if (p0 + g + 8 >= n) { s[2] = -INFINITY; s[3] = -INFINITY; }
+        float mx0 = fmaxf(s[0], s[2]), mx1 = fmaxf(s[1], s[3]);
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) {
+            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+        }
+        const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);  // finite: position p0 is valid
+        const float c0 = exp2f(m0 - n0), c1 = exp2f(m1 - n1);
+        m0 = n0;
+        m1 = n1;
+        l0 *= c0;
+        l1 *= c1;
+#pragma unroll
+        for (int i = 0; i < KV / 16; ++i) {
+            acc[i][0] *= c0; acc[i][2] *= c0;
+            acc[i][1] *= c1; acc[i][3] *= c1;
+        }
+        const float p00 = exp2f(s[0] - n0), p01 = exp2f(s[1] - n1), p10 = exp2f(s[2] - n0), p11 = exp2f(s[3] - n1);
+        l0 += p00 + p10;
+        l1 += p01 + p11;
+        Pw[warp][2 * t][g] = __float2half_rn(p00);
+        Pw[warp][2 * t + 1][g] = __float2half_rn(p01);
+        Pw[warp][2 * t][g + 8] = __float2half_rn(p10);
+        Pw[warp][2 * t + 1][g + 8] = __float2half_rn(p11);
+        __syncwarp();
+        uint32_t bp[4];
+        ldsm_x4(bp, &Pw[warp][lane & 7][((lane >> 3) & 1) * 8]);
+#pragma unroll
+        for (int mt = 0; mt < KV / 16; ++mt) {
+            uint32_t a[4];
+            ldsm_x4_t(a, &Cw[warp][(lane & 7) + ((lane >> 4) << 3)][mt * 16 + ((lane >> 3) & 1) * 8]);
+            mma16816(acc[mt], a, bp[0], bp[1]);
+        }
+        __syncwarp();
+    }
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) {
+        l0 += __shfl_xor_sync(0xffffffffu, l0, o);
+        l1 += __shfl_xor_sync(0xffffffffu, l1, o);
+    }
+    if (g == 0) {
+        Mw[warp][2 * t] = m0; Mw[warp][2 * t + 1] = m1;
+        Lw[warp][2 * t] = l0; Lw[warp][2 * t + 1] = l1;
+    }
+#pragma unroll
+    for (int mt = 0; mt < KV / 16; ++mt) {
+        Ow[warp][2 * t][mt * 16 + g] = acc[mt][0];
+        Ow[warp][2 * t + 1][mt * 16 + g] = acc[mt][1];
+        Ow[warp][2 * t][mt * 16 + g + 8] = acc[mt][2];
+        Ow[warp][2 * t + 1][mt * 16 + g + 8] = acc[mt][3];
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < H * KV; e += blockDim.x) {
+        const int hh = e / KV, c = e % KV;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) M = fmaxf(M, Mw[w][hh]);
+        float L = 0.f, O = 0.f;
+        if (M != -INFINITY) {
+#pragma unroll
+            for (int w = 0; w < kWarps; ++w) {
+                const float f = exp2f(Mw[w][hh] - M);
+                L += f * Lw[w][hh];
+                O += f * Ow[w][hh][c];
+            }
+        }
+        if (nsplit == 1) {
+            ctx[static_cast<long long>(b) * H * KV + hh * KV + c] = __float2half_rn(O / L);
+        } else {
+            float* pp = part + (static_cast<long long>(b) * nsplit + sp) * H * (KV + 2);
+            pp[hh * (KV + 2) + 2 + c] = O;
+            if (c == 0) {
+                pp[hh * (KV + 2)] = M;
+                pp[hh * (KV + 2) + 1] = L;
+            }
+        }
+    }
+}
+
+// Merges the nsplit partials of decode_attention_mma_kernel: grid B, block 128.
+__global__ void decode_attention_combine_kernel(const float* __restrict__ part, int nsplit,
+                                                __half* __restrict__ ctx) {
+    using namespace dec;
+    const int b = blockIdx.x;
+    for (int e = threadIdx.x; e < H * KV; e += blockDim.x) {
+        const int hh = e / KV, c = e % KV;
+        const float* pb = part + static_cast<long long>(b) * nsplit * H * (KV + 2) + hh * (KV + 2);
+        float M = -INFINITY;
+        for (int s = 0; s < nsplit; ++s) M = fmaxf(M, pb[s * H * (KV + 2)]);
+        float L = 0.f, O = 0.f;
+        for (int s = 0; s < nsplit; ++s) {
+            const float m = pb[s * H * (KV + 2)];
+            if (m == -INFINITY) continue;
+            const float f = exp2f(m - M);
+            L += f * pb[s * H * (KV + 2) + 1];
+            O += f * pb[s * H * (KV + 2) + 2 + c];
+        }
+        ctx[static_cast<long long>(b) * H * KV + hh * KV + c] = __float2half_rn(O / L);
     }
 }
 

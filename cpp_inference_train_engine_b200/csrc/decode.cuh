@@ -6,6 +6,16 @@
 
 namespace mm {
 
+// Context splits of the tensor-core decode attention: enough CTAs for ~2 per SM when the
+// batch alone does not provide them, at least 4 tiles of 16 positions per split.
+constexpr int kMaxDecodeSplits = 16;
+inline int decode_splits(int B, int ctx) {
+    if (B >= 296) return 1;
+    const int want = (296 + B - 1) / B;
+    const int by_len = std::max(1, (ctx + 63) / 64);
+    return std::max(1, std::min(std::min(want, by_len), kMaxDecodeSplits));
+}
+
 inline void ensure_decode(Context& cx, int B, int Sc, int max_new) {
     DecodeState& d = cx.dec;
     if (d.B == B && d.Sc >= Sc && d.max_new >= max_new && d.arena.capacity()) return;
@@ -34,6 +44,8 @@ inline void ensure_decode(Context& cx, int B, int Sc, int max_new) {
         d.seeds = a.template take<uint64_t>(B);
         d.draw = a.template take<int>(B);
         d.out_tok = a.template take<uint16_t>(static_cast<long long>(B) * std::max(max_new, 1));
+        // flash-decoding partials (max, sum, O[kv_rank]) per split and head
+        d.part = a.template take<float>(B >= 296 ? 1 : static_cast<long long>(B) * kMaxDecodeSplits * c.H * (c.kvr + 2));
     };
     d.B = B;
     d.Sc = Sc;
@@ -96,7 +108,14 @@ inline void decode_step(Context& cx) {
             const size_t smem = sizeof(float) * c.H * kvw;
             // cache rows read once (fp16) + absorbed queries in (fp32) + context out (fp16)
             const double bytes = static_cast<double>(B) * ((cx.dec_len + 1.0) * kvw * 2 + c.H * kvw * 4.0 + c.H * c.kvr * 2.0);
-            if (c.kvr == 128)
+            if (c.kvr == dec::KV && c.rope == dec::R && c.H == dec::H) {
+                const int ns = decode_splits(B, cx.dec_len + 1);
+                cudaEvent_t t0 = cx.prof_begin();
+                MM_LAUNCH(decode_attention_mma_kernel, dim3(B, ns), 128, 0, d.qf2, cache_l, (long long)d.Sc * kvw, d.pos,
+                          scale, d.ctx16, d.part);
+                if (ns > 1) MM_LAUNCH(decode_attention_combine_kernel, B, 128, 0, d.part, ns, d.ctx16);
+                cx.prof_end(kKDecodeAttn, t0, bytes);
+            } else if (c.kvr == 128)
                 MM_LAUNCH_TIMED(kKDecodeAttn, bytes, (decode_attention_kernel<128, 16>), B, 32 * c.H, smem, d.qf2, cache_l,
                                 (long long)d.Sc * kvw, d.pos, c.H, scale, d.ctx16);
             else

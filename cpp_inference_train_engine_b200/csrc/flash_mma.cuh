@@ -1,0 +1,342 @@
+// Causal attention forward/backward on the tensor pipe for the teacher-forced passes
+// (ops::attention / ops::attention_backward, ops.cpp:109-172), FlashAttention-2 style:
+// 64x64 tiles staged in shared memory, warp-level mma.sync m16n8k16 (fp16 in, fp32
+// accumulate) with ldmatrix fragment loads, online softmax in registers. The [T, T]
+// probability matrix is never materialised; the forward keeps the per-row log-sum-exp
+// (base 2) and the backward recomputes probabilities from it.
+//
+// Backward is two kernels with no atomics (deterministic): dK/dV per key tile iterating
+// over the query tiles at or below the diagonal, and dQ per query tile iterating over the
+// key tiles at or above it.
+#pragma once
+#include "common.cuh"
+
+namespace mm {
+
+namespace fa {
+
+constexpr int kTile = 64;
+constexpr float kLog2e = 1.4426950408889634f;
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void* p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(smem_u32(p)));
+}
+// D = A * B + D, m16n8k16, fp16 inputs, fp32 accumulators.
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
+    const __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// Copies rows [row0, row0 + 64) of a head's [*, D] slice (row pitch ld elements) into a
+// padded shared tile; rows at or beyond `rows` are zero.
+template <int D, int LD>
+__device__ __forceinline__ void load_tile(__half (*dst)[LD], const __half* __restrict__ src, long long ld,
+                                          int rows) {
+    constexpr int VPR = D / 8;  // 16-byte vectors per row
+    for (int e = threadIdx.x; e < kTile * VPR; e += blockDim.x) {
+        const int r = e / VPR, c = (e % VPR) * 8;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (r < rows) v = *reinterpret_cast<const uint4*>(src + r * ld + c);
+        *reinterpret_cast<uint4*>(&dst[r][c]) = v;
+    }
+}
+
+// A fragments (16 rows x D) of rows [r0, r0+16) of a shared tile.
+template <int D, int LD>
+__device__ __forceinline__ void load_a_frags(uint32_t (&a)[D / 16][4], __half (*tile)[LD], int r0, int lane) {
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) ldsm_x4(a[kk], &tile[r0 + (lane & 15)][kk * 16 + (lane >> 4) * 8]);
+}
+
+// acc[64/8 n-tiles] += A(16 x D) * rows[0..64)^T of `tile` (B operand: tile rows are n, cols k).
+template <int D, int LD>
+__device__ __forceinline__ void mma_abt(float (&acc)[kTile / 8][4], const uint32_t (&a)[D / 16][4],
+                                        __half (*tile)[LD], int lane) {
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk)
+#pragma unroll
+        for (int n2 = 0; n2 < kTile / 16; ++n2) {
+            uint32_t b[4];
+            ldsm_x4(b, &tile[n2 * 16 + (lane & 7) + ((lane >> 4) << 3)][kk * 16 + ((lane >> 3) & 1) * 8]);
+            mma16816(acc[2 * n2], a[kk], b[0], b[1]);
+            mma16816(acc[2 * n2 + 1], a[kk], b[2], b[3]);
+        }
+}
+
+// acc[D/8 n-tiles] += P(16 x 64, given as accumulator fragments) * tile(64 x D) (B operand
+// stored with k as rows: transposed ldmatrix).
+template <int D, int LD>
+__device__ __forceinline__ void mma_pb(float (&acc)[D / 8][4], const float (&p)[kTile / 8][4], __half (*tile)[LD],
+                                       int lane) {
+#pragma unroll
+    for (int k2 = 0; k2 < kTile / 16; ++k2) {
+        uint32_t a[4];
+        a[0] = pack_half2(p[2 * k2][0], p[2 * k2][1]);
+        a[1] = pack_half2(p[2 * k2][2], p[2 * k2][3]);
+        a[2] = pack_half2(p[2 * k2 + 1][0], p[2 * k2 + 1][1]);
+        a[3] = pack_half2(p[2 * k2 + 1][2], p[2 * k2 + 1][3]);
+#pragma unroll
+        for (int n2 = 0; n2 < D / 16; ++n2) {
+            uint32_t b[4];
+            ldsm_x4_t(b, &tile[k2 * 16 + (lane & 7) + ((lane >> 3) & 1) * 8][n2 * 16 + (lane >> 4) * 8]);
+            mma16816(acc[2 * n2], a, b[0], b[1]);
+            mma16816(acc[2 * n2 + 1], a, b[2], b[3]);
+        }
+    }
+}
+
+}  // namespace fa
+
+// Forward. q, k, v, out: fp16 [B*S][H*D]; lse2 fp32 [B*S][H] = log2-sum-exp of the scaled
+// scores (base 2). grid (ceil(S/64), H, B), block 128 (4 warps x 16 query rows).
+template <int D>
+__global__ void __launch_bounds__(128) flash_fwd_mma_kernel(const __half* __restrict__ q, const __half* __restrict__ k,
+                                                            const __half* __restrict__ v, int S, int H, float scale,
+                                                            __half* __restrict__ out, float* __restrict__ lse2) {
+    using namespace fa;
+    constexpr int LD = D + 8;
+    __shared__ __align__(16) __half Qs[kTile][LD];
+    __shared__ __align__(16) __half Ks[kTile][LD];
+    __shared__ __align__(16) __half Vs[kTile][LD];
+    const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const long long ld = static_cast<long long>(H) * D;
+    const long long base = static_cast<long long>(b) * S;
+    const float c = scale * kLog2e;
+    load_tile<D, LD>(Qs, q + (base + qt * kTile) * ld + h * D, ld, S - qt * kTile);
+    __syncthreads();
+    uint32_t qa[D / 16][4];
+    load_a_frags<D, LD>(qa, Qs, warp * 16, lane);
+    float o[D / 8][4];
+#pragma unroll
+    for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+    const int row0 = qt * kTile + warp * 16 + g, row1 = row0 + 8;
+    for (int kt = 0; kt <= qt; ++kt) {
+        __syncthreads();
+        load_tile<D, LD>(Ks, k + (base + kt * kTile) * ld + h * D, ld, S - kt * kTile);
+        load_tile<D, LD>(Vs, v + (base + kt * kTile) * ld + h * D, ld, S - kt * kTile);
+        __syncthreads();
+        float s[kTile / 8][4];
+#pragma unroll
+        for (int i = 0; i < kTile / 8; ++i) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.f;
+        mma_abt<D, LD>(s, qa, Ks, lane);
+        float mx0 = m0, mx1 = m1;
+#pragma unroll
+        for (int nt = 0; nt < kTile / 8; ++nt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int key = kt * kTile + nt * 8 + 2 * t + (e & 1);
+                const int row = e < 2 ? row0 : row1;
+                float x = s[nt][e] * c;
+                if (key > row || key >= S) x = -INFINITY;
+                s[nt][e] = x;
+                if (e < 2) mx0 = fmaxf(mx0, x); else mx1 = fmaxf(mx1, x);
+            }
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+        const float b0 = mx0 == -INFINITY ? 0.f : mx0, b1 = mx1 == -INFINITY ? 0.f : mx1;
+        const float corr0 = exp2f(m0 - b0), corr1 = exp2f(m1 - b1);
+        m0 = mx0;
+        m1 = mx1;
+        l0 *= corr0;
+        l1 *= corr1;
+#pragma unroll
+        for (int i = 0; i < D / 8; ++i) {
+            o[i][0] *= corr0; o[i][1] *= corr0;
+            o[i][2] *= corr1; o[i][3] *= corr1;
+        }
+#pragma unroll
+        for (int nt = 0; nt < kTile / 8; ++nt) {
+            s[nt][0] = exp2f(s[nt][0] - b0); s[nt][1] = exp2f(s[nt][1] - b0);
+            s[nt][2] = exp2f(s[nt][2] - b1); s[nt][3] = exp2f(s[nt][3] - b1);
+            l0 += s[nt][0] + s[nt][1];
+            l1 += s[nt][2] + s[nt][3];
+        }
+        mma_pb<D, LD>(o, s, Vs, lane);
+    }
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+    const float inv0 = 1.f / l0, inv1 = 1.f / l1;
+#pragma unroll
+    for (int i = 0; i < D / 8; ++i) {
+        const int col = h * D + i * 8 + 2 * t;
+        if (row0 < S) *reinterpret_cast<__half2*>(out + (base + row0) * ld + col) = __floats2half2_rn(o[i][0] * inv0, o[i][1] * inv0);
+        if (row1 < S) *reinterpret_cast<__half2*>(out + (base + row1) * ld + col) = __floats2half2_rn(o[i][2] * inv1, o[i][3] * inv1);
+    }
+    if (t == 0) {
+        if (row0 < S) lse2[(base + row0) * H + h] = m0 + log2f(l0);
+        if (row1 < S) lse2[(base + row1) * H + h] = m1 + log2f(l1);
+    }
+}
+
+// D[t, h] = sum_c dO[t, h, c] * O[t, h, c] over fp16 rows (the softmax-backward row term).
+__global__ void attn_rowdot_kernel(const __half* __restrict__ dout, const __half* __restrict__ out, int T, int H,
+                                   int DV, float* __restrict__ Dd) {
+    const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= T * H) return;
+    const long long o = static_cast<long long>(idx / H) * H * DV + (idx % H) * DV;
+    float s = 0.f;
+    for (int c = 0; c < DV; ++c) s += __half2float(dout[o + c]) * __half2float(out[o + c]);
+    Dd[idx] = s;
+}
+
+// dQ for one query tile (4 warps x 16 query rows). dout fp16 [B*S][H*D]. dq fp32 [B*S][H*D],
+// including the softmax scale.
+template <int D>
+__global__ void __launch_bounds__(128) flash_bwd_dq_mma_kernel(
+    const __half* __restrict__ q, const __half* __restrict__ k, const __half* __restrict__ v,
+    const __half* __restrict__ dout, const float* __restrict__ lse2, const float* __restrict__ Dd, int S, int H,
+    float scale, float* __restrict__ dq) {
+    using namespace fa;
+    constexpr int LD = D + 8;
+    __shared__ __align__(16) __half Qs[kTile][LD];
+    __shared__ __align__(16) __half Gs[kTile][LD];
+    __shared__ __align__(16) __half Ks[kTile][LD];
+    __shared__ __align__(16) __half Vs[kTile][LD];
+    const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const long long ld = static_cast<long long>(H) * D;
+    const long long base = static_cast<long long>(b) * S;
+    const float c = scale * kLog2e;
+    load_tile<D, LD>(Qs, q + (base + qt * kTile) * ld + h * D, ld, S - qt * kTile);
+    load_tile<D, LD>(Gs, dout + (base + qt * kTile) * ld + h * D, ld, S - qt * kTile);
+    __syncthreads();
+    uint32_t qa[D / 16][4], ga[D / 16][4];
+    load_a_frags<D, LD>(qa, Qs, warp * 16, lane);
+    load_a_frags<D, LD>(ga, Gs, warp * 16, lane);
+    const int row0 = qt * kTile + warp * 16 + g, row1 = row0 + 8;
+    const float L0 = row0 < S ? lse2[(base + row0) * H + h] : 0.f, L1 = row1 < S ? lse2[(base + row1) * H + h] : 0.f;
+    const float D0 = row0 < S ? Dd[(base + row0) * H + h] : 0.f, D1 = row1 < S ? Dd[(base + row1) * H + h] : 0.f;
+    float acc[D / 8][4];
+#pragma unroll
+    for (int i = 0; i < D / 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+    for (int kt = 0; kt <= qt; ++kt) {
+        __syncthreads();
+        load_tile<D, LD>(Ks, k + (base + kt * kTile) * ld + h * D, ld, S - kt * kTile);
+        load_tile<D, LD>(Vs, v + (base + kt * kTile) * ld + h * D, ld, S - kt * kTile);
+        __syncthreads();
+        float s[kTile / 8][4], dp[kTile / 8][4];
+#pragma unroll
+        for (int i = 0; i < kTile / 8; ++i) {
+            s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.f;
+            dp[i][0] = dp[i][1] = dp[i][2] = dp[i][3] = 0.f;
+        }
+        mma_abt<D, LD>(s, qa, Ks, lane);
+        mma_abt<D, LD>(dp, ga, Vs, lane);
+#pragma unroll
+        for (int nt = 0; nt < kTile / 8; ++nt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int key = kt * kTile + nt * 8 + 2 * t + (e & 1);
+                const int row = e < 2 ? row0 : row1;
+                const float p = (key > row || key >= S || row >= S) ? 0.f : exp2f(s[nt][e] * c - (e < 2 ? L0 : L1));
+                s[nt][e] = p * (dp[nt][e] - (e < 2 ? D0 : D1)) * scale;
+            }
+        mma_pb<D, LD>(acc, s, Ks, lane);
+    }
+#pragma unroll
+    for (int i = 0; i < D / 8; ++i) {
+        const int col = h * D + i * 8 + 2 * t;
+        if (row0 < S) *reinterpret_cast<float2*>(dq + (base + row0) * ld + col) = make_float2(acc[i][0], acc[i][1]);
+        if (row1 < S) *reinterpret_cast<float2*>(dq + (base + row1) * ld + col) = make_float2(acc[i][2], acc[i][3]);
+    }
+}
+
+// dK, dV for one key tile (4 warps x 16 keys). dk includes the softmax scale.
+template <int D>
+__global__ void __launch_bounds__(128) flash_bwd_dkdv_mma_kernel(
+    const __half* __restrict__ q, const __half* __restrict__ k, const __half* __restrict__ v,
+    const __half* __restrict__ dout, const float* __restrict__ lse2, const float* __restrict__ Dd, int S, int H,
+    float scale, float* __restrict__ dk, float* __restrict__ dv) {
+    using namespace fa;
+    constexpr int LD = D + 8;
+    __shared__ __align__(16) __half Ks[kTile][LD];
+    __shared__ __align__(16) __half Vs[kTile][LD];
+    __shared__ __align__(16) __half Qs[kTile][LD];
+    __shared__ __align__(16) __half Gs[kTile][LD];
+    __shared__ float Ls[kTile], Ds[kTile];
+    const int kt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const long long ld = static_cast<long long>(H) * D;
+    const long long base = static_cast<long long>(b) * S;
+    const float c = scale * kLog2e;
+    load_tile<D, LD>(Ks, k + (base + kt * kTile) * ld + h * D, ld, S - kt * kTile);
+    load_tile<D, LD>(Vs, v + (base + kt * kTile) * ld + h * D, ld, S - kt * kTile);
+    __syncthreads();
+    uint32_t ka[D / 16][4], va[D / 16][4];
+    load_a_frags<D, LD>(ka, Ks, warp * 16, lane);
+    load_a_frags<D, LD>(va, Vs, warp * 16, lane);
+    const int key0 = kt * kTile + warp * 16 + g, key1 = key0 + 8;
+    float accK[D / 8][4], accV[D / 8][4];
+#pragma unroll
+    for (int i = 0; i < D / 8; ++i) {
+        accK[i][0] = accK[i][1] = accK[i][2] = accK[i][3] = 0.f;
+        accV[i][0] = accV[i][1] = accV[i][2] = accV[i][3] = 0.f;
+    }
+    const int ntiles = (S + kTile - 1) / kTile;
+    for (int qt = kt; qt < ntiles; ++qt) {
+        __syncthreads();
+        load_tile<D, LD>(Qs, q + (base + qt * kTile) * ld + h * D, ld, S - qt * kTile);
+        load_tile<D, LD>(Gs, dout + (base + qt * kTile) * ld + h * D, ld, S - qt * kTile);
+        for (int e = threadIdx.x; e < kTile; e += blockDim.x) {
+            const int r = qt * kTile + e;
+            Ls[e] = r < S ? lse2[(base + r) * H + h] : 0.f;
+            Ds[e] = r < S ? Dd[(base + r) * H + h] : 0.f;
+        }
+        __syncthreads();
+        float st[kTile / 8][4], dpt[kTile / 8][4];
+#pragma unroll
+        for (int i = 0; i < kTile / 8; ++i) {
+            st[i][0] = st[i][1] = st[i][2] = st[i][3] = 0.f;
+            dpt[i][0] = dpt[i][1] = dpt[i][2] = dpt[i][3] = 0.f;
+        }
+        mma_abt<D, LD>(st, ka, Qs, lane);   // S^T: keys x queries
+        mma_abt<D, LD>(dpt, va, Gs, lane);  // dP^T
+#pragma unroll
+        for (int nt = 0; nt < kTile / 8; ++nt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int qi = nt * 8 + 2 * t + (e & 1);
+                const int query = qt * kTile + qi;
+                const int key = e < 2 ? key0 : key1;
+                const float p = (key > query || query >= S || key >= S) ? 0.f : exp2f(st[nt][e] * c - Ls[qi]);
+                st[nt][e] = p;
+                dpt[nt][e] = p * (dpt[nt][e] - Ds[qi]) * scale;
+            }
+        mma_pb<D, LD>(accV, st, Gs, lane);   // dV += P^T dO
+        mma_pb<D, LD>(accK, dpt, Qs, lane);  // dK += dS^T Q * scale
+    }
+#pragma unroll
+    for (int i = 0; i < D / 8; ++i) {
+        const int col = h * D + i * 8 + 2 * t;
+        if (key0 < S) {
+            *reinterpret_cast<float2*>(dk + (base + key0) * ld + col) = make_float2(accK[i][0], accK[i][1]);
+            *reinterpret_cast<float2*>(dv + (base + key0) * ld + col) = make_float2(accV[i][0], accV[i][1]);
+        }
+        if (key1 < S) {
+            *reinterpret_cast<float2*>(dk + (base + key1) * ld + col) = make_float2(accK[i][2], accK[i][3]);
+            *reinterpret_cast<float2*>(dv + (base + key1) * ld + col) = make_float2(accV[i][2], accV[i][3]);
+        }
+    }
+}
+
+} // namespace mm

@@ -106,6 +106,7 @@ template <class A> void plan_workspace(Context& cx, A& a, int T, bool tape) {
         w.dkvp16 = a.template take<__half>(t * cx.d16(c.kvw()));
         w.draw16 = a.template take<__half>(t * cx.d16(c.qr));
         w.g16 = a.template take<__half>(t * c.V);
+        w.dao16 = a.template take<__half>(t * c.aw());
     }
 }
 
@@ -139,12 +140,12 @@ inline unsigned warp_rows_grid(int rows) { return blocks_for(static_cast<long lo
 
 inline void launch_flash_fwd(Context& cx, const LayerBuf& b, int Bc, int S) {
     const Dims& c = cx.c;
-    dim3 grid((S + kAttTile - 1) / kAttTile, c.H, Bc);
+    dim3 grid((S + fa::kTile - 1) / fa::kTile, c.H, Bc);
     const float scale = 1.0f / std::sqrt(static_cast<float>(c.qk()));
     // causal pairs x (qk + dv) multiply-adds
     const double work = 2.0 * Bc * c.H * (S * (S + 1.0) / 2.0) * (c.qk() + c.dv);
-    if (c.qk() == 64) MM_LAUNCH_TIMED(kKFlashFwd, work, (flash_fwd_kernel<64, 64>), grid, 64, 0, b.q, b.k, b.v, S, c.H, scale, b.ao, b.lse);
-    else MM_LAUNCH_TIMED(kKFlashFwd, work, (flash_fwd_kernel<16, 16>), grid, 64, 0, b.q, b.k, b.v, S, c.H, scale, b.ao, b.lse);
+    if (c.qk() == 64) MM_LAUNCH_TIMED(kKFlashFwd, work, flash_fwd_mma_kernel<64>, grid, 128, 0, b.q, b.k, b.v, S, c.H, scale, b.ao, b.lse);
+    else MM_LAUNCH_TIMED(kKFlashFwd, work, flash_fwd_mma_kernel<16>, grid, 128, 0, b.q, b.k, b.v, S, c.H, scale, b.ao, b.lse);
 }
 
 enum VocabMode { kVocabNone, kVocabAll, kVocabLast };
@@ -287,20 +288,21 @@ inline void backward_chunk(Context& cx, int Bc, int S) {
             o.alpha_ptr = inv_s;
             gemm(cx, aw, c.d, T, {b.ao, aw, true}, {w.dres16, ld_d, true}, o);
         }
-        gemm(cx, T, aw, c.d, {w.dres16, ld_d, false}, {cx.S(l, kWo), cx.SL(l, kWo), false}, {w.dao, aw, kOutF32});
+        gemm(cx, T, aw, c.d, {w.dres16, ld_d, false}, {cx.S(l, kWo), cx.SL(l, kWo), false}, {w.dao16, aw, kOutF16});
         // attention
-        MM_LAUNCH(attn_bwd_dot_kernel, blocks_for((long long)T * c.H, 256), 256, 0, w.dao, b.ao, T, c.H, c.dv, w.Dd);
+        MM_LAUNCH(attn_rowdot_kernel, blocks_for((long long)T * c.H, 256), 256, 0, w.dao16, b.ao, T, c.H, c.dv, w.Dd);
         {
-            dim3 grid((S + kAttTile - 1) / kAttTile, c.H, Bc);
+            dim3 grid((S + fa::kTile - 1) / fa::kTile, c.H, Bc);
             const float scale = 1.0f / std::sqrt(static_cast<float>(qk));
             const double pairs = static_cast<double>(Bc) * c.H * (S * (S + 1.0) / 2.0);
-            const double w_kv = pairs * 4.0 * (qk + c.dv), w_q = pairs * 2.0 * (2 * qk + c.dv);
+            // dK/dV: S^T, dP^T, dV, dK products; dQ: S, dP, dQ products (2 flops per MAC)
+            const double w_kv = pairs * 2.0 * (2 * qk + 2 * c.dv), w_q = pairs * 2.0 * (2 * qk + c.dv);
             if (qk == 64) {
-                MM_LAUNCH_TIMED(kKFlashBwd, w_kv, (flash_bwd_dkdv_kernel<64, 64>), grid, 64, 0, b.q, b.k, b.v, w.dao, b.lse, w.Dd, S, c.H, scale, w.dk, w.dv);
-                MM_LAUNCH_TIMED(kKFlashBwd, w_q, (flash_bwd_dq_kernel<64, 64>), grid, 64, 0, b.q, b.k, b.v, w.dao, b.lse, w.Dd, S, c.H, scale, w.dq);
+                MM_LAUNCH_TIMED(kKFlashBwd, w_kv, flash_bwd_dkdv_mma_kernel<64>, grid, 128, 0, b.q, b.k, b.v, w.dao16, b.lse, w.Dd, S, c.H, scale, w.dk, w.dv);
+                MM_LAUNCH_TIMED(kKFlashBwd, w_q, flash_bwd_dq_mma_kernel<64>, grid, 128, 0, b.q, b.k, b.v, w.dao16, b.lse, w.Dd, S, c.H, scale, w.dq);
             } else {
-                MM_LAUNCH_TIMED(kKFlashBwd, w_kv, (flash_bwd_dkdv_kernel<16, 16>), grid, 64, 0, b.q, b.k, b.v, w.dao, b.lse, w.Dd, S, c.H, scale, w.dk, w.dv);
-                MM_LAUNCH_TIMED(kKFlashBwd, w_q, (flash_bwd_dq_kernel<16, 16>), grid, 64, 0, b.q, b.k, b.v, w.dao, b.lse, w.Dd, S, c.H, scale, w.dq);
+                MM_LAUNCH_TIMED(kKFlashBwd, w_kv, flash_bwd_dkdv_mma_kernel<16>, grid, 128, 0, b.q, b.k, b.v, w.dao16, b.lse, w.Dd, S, c.H, scale, w.dk, w.dv);
+                MM_LAUNCH_TIMED(kKFlashBwd, w_q, flash_bwd_dq_mma_kernel<16>, grid, 128, 0, b.q, b.k, b.v, w.dao16, b.lse, w.Dd, S, c.H, scale, w.dq);
             }
         }
         const int ld_q16 = cx.d16(c.H * qk);

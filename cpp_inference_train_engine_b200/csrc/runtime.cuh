@@ -16,6 +16,7 @@
 
 #include "attention.cuh"
 #include "common.cuh"
+#include "flash_mma.cuh"
 #include "gemm_tc.cuh"
 #include "kernels_elem.cuh"
 #include "optim.cuh"
@@ -154,7 +155,7 @@ struct Workspace {
     float* knope;       // [T][H*nope]
     // backward scratch (tape only)
     float *dy, *dgated, *dh2, *dres, *dao, *dq, *dk, *dv, *drope, *drope2, *dckv, *dkvraw, *dh, *dcq, *Dd;
-    __half *dy16, *dg16, *du16, *dres16, *dq16, *dkn16, *dv16, *dkvp16, *draw16, *g16;
+    __half *dy16, *dg16, *du16, *dres16, *dq16, *dkn16, *dv16, *dkvp16, *draw16, *g16, *dao16;
 };
 
 struct DecodeState {
@@ -181,6 +182,7 @@ struct DecodeState {
     uint64_t* seeds;          // [B]
     int* draw;                // [B]
     uint16_t* out_tok;        // [B][max_new]
+    float* part;              // [B][splits][H][kv_rank + 2] decode-attention partials
     int max_new = 0;
     Arena arena;
 };

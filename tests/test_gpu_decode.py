@@ -49,6 +49,31 @@ def test_prefill_and_decode_match_reference_decoder(setup):
     assert agree == total
 
 
+@pytest.mark.parametrize("B,P,steps", [(2, 300, 6), (300, 24, 3)])
+def test_36m_decode_split_and_wide_batches(B, P, steps):
+    """Long contexts over few rows take the split-context path; >= 296 rows the one-CTA-per
+    row path. Rows 0, B/2 and B-1 are checked against the reference decoder."""
+    require_gpu()
+    if not ref.available():
+        pytest.skip("oracle/_ref not built")
+    W = E.init_params(MLA36M, 3)
+    ex = E.make_execution(MLA36M, W)
+    rng = np.random.default_rng(B)
+    prompts = rng.integers(0, 16384, (B, P)).astype(np.uint16)
+    rows = sorted({0, B // 2, B - 1})
+    sessions = {r: ref.Session(MLA36M, 3) for r in rows}
+    got = ex.prefill_batch(prompts)
+    want = {r: s.prefill(prompts[r]) for r, s in sessions.items()}
+    for k in range(steps):
+        for r in rows:
+            assert np.abs(got[r] - want[r]).max() < 2e-2, (k, r)
+        tok = got.argmax(axis=1).astype(np.uint16)
+        for r in rows:
+            tok[r] = np.uint16(want[r].argmax())
+        want = {r: s.decode(tok[r]) for r, s in sessions.items()}
+        got = ex.decode_batch(tok)
+
+
 def test_sampler_matches_reference_sample_token():
     require_gpu()
     execs = {264: E.CudaExecution(TINY), 16384: E.CudaExecution(MLA36M)}

@@ -427,6 +427,23 @@ int mm_cuda_gemm_f16(mm_cuda_ctx* h, int M, int N, int K, const void* a, int64_t
     });
 }
 
+int mm_cuda_decode_attention(mm_cuda_ctx* h, const float* q, const void* cache, int64_t cache_seq_stride,
+                             const int32_t* pos, int batch, int splits, float scale, void* out) {
+    return guarded(h, [&](mm::Context& cx) {
+        if (!q || !cache || !pos || !out || batch < 1 || splits < 1 || splits > mm::kMaxDecodeSplits ||
+            cache_seq_stride < mm::dec::W)
+            mm::fail(MM_INVALID_ARGUMENT, "invalid decode attention arguments");
+        float* part = nullptr;
+        if (splits > 1)
+            part = static_cast<float*>(cx.stage.get(sizeof(float) * static_cast<size_t>(batch) * splits * mm::dec::H *
+                                                    (mm::dec::KV + 2)));
+        MM_LAUNCH(mm::decode_attention_mma_kernel, dim3(batch, splits), 128, 0, q, static_cast<const __half*>(cache),
+                  cache_seq_stride, pos, scale, static_cast<__half*>(out), part);
+        if (splits > 1) MM_LAUNCH(mm::decode_attention_combine_kernel, batch, 128, 0, part, splits, static_cast<__half*>(out));
+        mm::check_device(cx, "decode_attention");
+    });
+}
+
 int mm_cuda_stream(mm_cuda_ctx* h, void** stream) {
     return guarded(h, [&](mm::Context& cx) { *stream = cx.stream; });
 }

@@ -119,6 +119,8 @@ def lib():
                                             ctypes.c_float, _vp, ctypes.c_int64, ctypes.c_int]),
         "mm_cuda_profile": (ctypes.c_int, [_vp, ctypes.c_int, _f64p, _i64p, _f64p]),
         "mm_cuda_stream": (ctypes.c_int, [_vp, ctypes.POINTER(_vp)]),
+        "mm_cuda_decode_attention": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int64, _vp, ctypes.c_int,
+                                                    ctypes.c_int, ctypes.c_float, _vp]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)
@@ -388,6 +390,12 @@ class CudaExecution:
         self._check(lib().mm_cuda_gemm_f16(self.h, M, N, K, a_ptr, lda, int(a_mn), b_ptr, ldb,
                                            int(b_mn), out_ptr, ldc, out_kind, alpha,
                                            residual_ptr, ldr, int(bf16)))
+
+    def decode_attention(self, q_ptr, cache_ptr, cache_seq_stride, pos_ptr, batch, splits, scale,
+                         out_ptr):
+        """Kernel-level latent decode attention on device pointers (mm_cuda_kernels.h)."""
+        self._check(lib().mm_cuda_decode_attention(self.h, q_ptr, cache_ptr, cache_seq_stride,
+                                                   pos_ptr, batch, splits, scale, out_ptr))
 
     def profile(self, enable: int = -1):
         """{tag: (device ms, launches, algorithmic work)}; see PROFILE_TAGS."""

@@ -24,6 +24,18 @@ int mm_cuda_gemm_f16(mm_cuda_ctx* ctx, int M, int N, int K, const void* a, int64
                      const void* b, int64_t ldb, int b_mn, void* out, int64_t ldc, int out_kind,
                      float alpha, const float* residual, int64_t ldr, int bf16);
 
+/* Absorbed latent-cache decode attention (CpuDecoder::decode, src/infer/inference.cpp:116-153)
+ * for the 8-head [128 latent | 16 rope] cache of the 35.8M model, on device pointers:
+ *   q      fp32 [batch][8][144]  absorbed query then rotated rope query, per head
+ *   cache  fp16 rows of 144, row b starts at b * cache_seq_stride elements
+ *   pos    int32 [batch]: positions 0..pos[b] (inclusive) are attended
+ *   out    fp16 [batch][8 * 128] latent context per head
+ * splits in [1, 16] divides each row's context over that many CTAs; the partials live in
+ * scratch owned by the context. Runs on the context's stream and returns when done. */
+int mm_cuda_decode_attention(mm_cuda_ctx* ctx, const float* q, const void* cache,
+                             int64_t cache_seq_stride, const int32_t* pos, int batch, int splits,
+                             float scale, void* out);
+
 /* Device time (CUDA events on the context's stream, resolved at this call) accumulated
  * since the last reset, 16 entries each of ms, calls and algorithmic work:
  *   0-7  phases: prefill, decode, sample, logprob, backward, adamw, allreduce, prep;

@@ -1,6 +1,7 @@
 // C ABI of the sm_100a backend (include/mm_cuda.h, include/mm_cuda_kernels.h). Every
 // entry point validates its arguments, runs on the context's stream, waits for completion
 // and maps failures to 1 + ErrorCode with a message, as the reference's Result does.
+#include <mutex>
 #include <new>
 
 #include "train.cuh"
@@ -61,6 +62,28 @@ struct HostRng {
 void check_tokens(const mm::Context& cx, const uint16_t* t, long long n) {
     for (long long i = 0; i < n; ++i)
         if (t[i] >= cx.c.V) mm::fail(MM_INVALID_ARGUMENT, "Input token exceeds vocabulary");
+}
+
+// Scratch of mm_decode_attention_noalloc: partials (max, sum, 128-wide context) of 8 heads
+// for up to 256 (row, split) pairs, in a static device array instead of an allocation.
+// In host code the symbol is only a handle; the kernel gets the device address resolved by
+// cudaGetSymbolAddress once per device, with that device current.
+constexpr int kStaticPartialSlots = 256;
+__device__ __align__(256) float g_static_partials[kStaticPartialSlots * mm::dec::H * (mm::dec::KV + 2)];
+constexpr int kMaxDevices = 64;
+float* g_static_partials_addr[kMaxDevices] = {};
+std::mutex g_static_partials_mu;
+
+float* static_partials_address() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+    std::lock_guard<std::mutex> lock(g_static_partials_mu);
+    if (!g_static_partials_addr[dev]) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_static_partials) != cudaSuccess || !p) return nullptr;
+        g_static_partials_addr[dev] = static_cast<float*>(p);
+    }
+    return g_static_partials_addr[dev];
 }
 
 } // namespace
@@ -442,6 +465,23 @@ int mm_cuda_decode_attention(mm_cuda_ctx* h, const float* q, const void* cache, 
         if (splits > 1) MM_LAUNCH(mm::decode_attention_combine_kernel, batch, 128, 0, part, splits, static_cast<__half*>(out));
         mm::check_device(cx, "decode_attention");
     });
+}
+
+int mm_decode_attention_noalloc(const float* q, const void* cache, int64_t cache_seq_stride, const int32_t* pos,
+                                int batch, int splits, float scale, void* out, void* stream) {
+    if (!q || !cache || !pos || !out || batch < 1 || splits < 1 || splits > mm::kMaxDecodeSplits ||
+        cache_seq_stride < mm::dec::W)
+        return MM_INVALID_ARGUMENT;
+    if (splits > 1 && static_cast<long long>(batch) * splits > kStaticPartialSlots) return MM_INVALID_ARGUMENT;
+    float* part = static_partials_address();
+    if (!part) return MM_GPU_ERROR;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    mm::decode_attention_mma_kernel<<<dim3(batch, splits), 128, 0, s>>>(
+        q, static_cast<const __half*>(cache), cache_seq_stride, pos, scale, static_cast<__half*>(out), part);
+    if (splits > 1) mm::decode_attention_combine_kernel<<<batch, 128, 0, s>>>(part, splits, static_cast<__half*>(out));
+    if (cudaGetLastError() != cudaSuccess) return MM_GPU_ERROR;
+    if (cudaStreamSynchronize(s) != cudaSuccess) return MM_GPU_ERROR;
+    return MM_OK;
 }
 
 int mm_cuda_stream(mm_cuda_ctx* h, void** stream) {

@@ -36,6 +36,29 @@ int mm_cuda_decode_attention(mm_cuda_ctx* ctx, const float* q, const void* cache
                              int64_t cache_seq_stride, const int32_t* pos, int batch, int splits,
                              float scale, void* out);
 
+/* The same decode attention without any allocation, for callers that may not allocate
+ * device memory: a serving process that hands all device memory to its own pool at
+ * start-up and forbids allocations afterwards, or a plugin host that lends device buffers
+ * for inputs and outputs only. No counterpart in the reference (its decode runs inside a
+ * CpuDecoder or an MPSGraph program).
+ *
+ * Arguments mean what they mean for mm_cuda_decode_attention; `stream` is the caller's
+ * cudaStream_t (NULL = the legacy default stream) and the call returns when that stream
+ * has finished the work. No context, cudaMalloc, cudaFree or allocating library routine is
+ * involved: the split partials live in one static device array of 256 (row, split) slots
+ * (1,064,960 bytes) that every GPU loading this library holds until the process exits.
+ *   - The first call on a device resolves that array's device address (with the device
+ *     current); make this first call before any stream capture on that device.
+ *   - Returns MM_INVALID_ARGUMENT when splits > 1 and batch * splits > 256 (the array's
+ *     capacity), for splits outside [1, 16], a null pointer or a row stride below 144;
+ *     MM_GPU_ERROR when a CUDA call fails.
+ *   - Every call shares the array and it keeps the last call's partials (each call writes
+ *     every slot it reads, so nothing needs clearing). Calls that overlap on the GPU
+ *     (different streams, or threads racing on one device) race on the array. */
+int mm_decode_attention_noalloc(const float* q, const void* cache, int64_t cache_seq_stride,
+                                const int32_t* pos, int batch, int splits, float scale, void* out,
+                                void* stream);
+
 /* Device time (CUDA events on the context's stream, resolved at this call) accumulated
  * since the last reset, 16 entries each of ms, calls and algorithmic work:
  *   0-7  phases: prefill, decode, sample, logprob, backward, adamw, allreduce, prep;

@@ -48,6 +48,8 @@ def parse():
     ap.add_argument("--cpu-rollouts", type=int, default=2,
                     help="rollouts in the bounded CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--gemm-shapes", action="store_true",
+                    help="print per-shape GEMM device time to stderr")
     return ap.parse_args()
 
 
@@ -257,6 +259,13 @@ def main():
         end.record(stream)
         barrier()
     e2e_ms = start.elapsed_time(end)
+    if args.gemm_shapes and rank == 0:
+        for name, ctx in (("policy", pol), ("reference", refm)):
+            for row in ctx.gemm_shapes()[:25]:
+                print(json.dumps({"gemm_shape": row["shape"], "ctx": name,
+                                  "ms_per_step": round(row["ms"] / args.steps, 3),
+                                  "calls_per_step": row["calls"] // args.steps,
+                                  "tflops": row["tflops"]}), file=sys.stderr)
     prof_p = pol.profile(0)
     prof_r = refm.profile(0)
     launches = pol.kernel_launches + refm.kernel_launches - launches0

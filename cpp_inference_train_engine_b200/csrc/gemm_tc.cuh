@@ -33,6 +33,8 @@ struct GemmArgs {
     float alpha;
     const float* alpha_ptr; // optional device scalar multiplied into alpha
     int* err;
+    int k_tiles_per_split;   // split-K: CTA z covers k-tiles [z*per, (z+1)*per); 0 = all
+    long long split_stride;  // split-K: output of CTA z starts at out + z * split_stride
 };
 
 constexpr int kGemmBM = 128;
@@ -95,6 +97,14 @@ __device__ __forceinline__ void gemm_store16(const GemmArgs& g, float alpha, int
     }
 }
 
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Persistent: CTA c processes tiles c, c + gridDim.x, ... of the (m, n, split) tile list,
+// n fastest (consecutive CTAs share the A row tile in L2). The shared-memory ring of
+// STAGES (A, B) stages runs across tile boundaries; two TMEM accumulators of BN columns
+// alternate, so the epilogue of tile j overlaps the MMAs of tile j + 1.
 template <int BN, int STAGES>
 __global__ void __launch_bounds__(192, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -105,13 +115,16 @@ __global__ void __launch_bounds__(192, 1)
                                                ~static_cast<uintptr_t>(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * C::STAGE_BYTES);
     uint64_t* empty = full + STAGES;
-    uint64_t* done = empty + STAGES;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    uint64_t* acc_full = empty + STAGES;  // [2] MMA -> epilogue
+    uint64_t* acc_empty = acc_full + 2;   // [2] epilogue -> MMA (4 warp arrivals)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * kGemmBM;
     const int num_k = (g.K + kGemmBK - 1) / kGemmBK;
-    const int n_mma = min(BN, ((g.N - n0) + 15) / 16 * 16);
+    const int per = g.k_tiles_per_split > 0 ? g.k_tiles_per_split : num_k;
+    const int splits = (num_k + per - 1) / per;
+    const int tiles_n = (g.N + BN - 1) / BN, tiles_m = (g.M + kGemmBM - 1) / kGemmBM;
+    const int tiles = tiles_n * tiles_m * splits;
 
     if (warp == 0) {
         if (lane == 0) {
@@ -119,13 +132,16 @@ __global__ void __launch_bounds__(192, 1)
                 mbar_init(&full[s], 1);
                 mbar_init(&empty[s], 1);
             }
-            mbar_init(done, 1);
+            mbar_init(&acc_full[0], 1);
+            mbar_init(&acc_full[1], 1);
+            mbar_init(&acc_empty[0], 4);
+            mbar_init(&acc_empty[1], 4);
             fence_mbar_init();
             prefetch_tmap(&tmA);
             prefetch_tmap(&tmB);
         }
         __syncwarp();
-        tmem_alloc(tmem_slot, BN);
+        tmem_alloc(tmem_slot, 2 * BN);
         tmem_relinquish();
     }
     tc_fence_before();
@@ -134,58 +150,95 @@ __global__ void __launch_bounds__(192, 1)
     const uint32_t tmem = *tmem_slot;
 
     if (warp == 0 && lane == 0) {
-        for (int kt = 0; kt < num_k; ++kt) {
-            const int s = kt % STAGES;
-            const uint32_t ph = (kt / STAGES) & 1;
-            if (!mbar_wait_bounded(&empty[s], ph ^ 1, g.err)) break;
-            uint8_t* sa = smem + s * C::STAGE_BYTES;
-            uint8_t* sb = sa + C::A_BYTES;
-            mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
-            const int k0 = kt * kGemmBK;
-            if (!g.a_mn) {
-                tma_load_2d(sa, &tmA, &full[s], k0, m0);
-            } else {
-                tma_load_2d(sa, &tmA, &full[s], m0, k0);
-                tma_load_2d(sa + 8192, &tmA, &full[s], m0 + 64, k0);
-            }
-            if (!g.b_mn) {
-                tma_load_2d(sb, &tmB, &full[s], k0, n0);
-            } else {
+        int it = 0;  // ring position across tiles
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+            const int z = tile / (tiles_n * tiles_m), mn = tile % (tiles_n * tiles_m);
+            const int m0 = (mn / tiles_n) * kGemmBM, n0 = (mn % tiles_n) * BN;
+            const int kb = z * per, ke = min(num_k, kb + per);
+            for (int kt = kb; kt < ke; ++kt, ++it) {
+                const int s = it % STAGES;
+                const uint32_t ph = (it / STAGES) & 1;
+                if (!mbar_wait_bounded(&empty[s], ph ^ 1, g.err)) { ok = false; break; }
+                uint8_t* sa = smem + s * C::STAGE_BYTES;
+                uint8_t* sb = sa + C::A_BYTES;
+                mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
+                const int k0 = kt * kGemmBK;
+                if (!g.a_mn) {
+                    tma_load_2d(sa, &tmA, &full[s], k0, m0);
+                } else {
+                    tma_load_2d(sa, &tmA, &full[s], m0, k0);
+                    tma_load_2d(sa + 8192, &tmA, &full[s], m0 + 64, k0);
+                }
+                if (!g.b_mn) {
+                    tma_load_2d(sb, &tmB, &full[s], k0, n0);
+                } else {
 #pragma unroll
-                for (int j = 0; j < BN / 64; ++j)
-                    tma_load_2d(sb + j * 8192, &tmB, &full[s], n0 + 64 * j, k0);
+                    for (int j = 0; j < BN / 64; ++j)
+                        tma_load_2d(sb + j * 8192, &tmB, &full[s], n0 + 64 * j, k0);
+                }
             }
         }
     } else if (warp == 1 && lane == 0) {
-        const uint32_t idesc = umma_idesc_f16(g.bf16 != 0, g.a_mn != 0, g.b_mn != 0, kGemmBM, n_mma);
-        for (int kt = 0; kt < num_k; ++kt) {
-            const int s = kt % STAGES;
-            const uint32_t ph = (kt / STAGES) & 1;
-            if (!mbar_wait_bounded(&full[s], ph, g.err)) break;
+        int it = 0, j = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++j) {
+            const int z = tile / (tiles_n * tiles_m), mn = tile % (tiles_n * tiles_m);
+            const int n0 = (mn % tiles_n) * BN;
+            const int kb = z * per, ke = min(num_k, kb + per);
+            const int n_mma = min(BN, ((g.N - n0) + 15) / 16 * 16);
+            const uint32_t idesc = umma_idesc_f16(g.bf16 != 0, g.a_mn != 0, g.b_mn != 0, kGemmBM, n_mma);
+            const int buf = j & 1;
+            if (!mbar_wait_bounded(&acc_empty[buf], ((j >> 1) & 1) ^ 1, g.err)) break;
             tc_fence_after();
-            const uint32_t sa = smem_u32(smem + s * C::STAGE_BYTES);
-            const uint32_t sb = sa + C::A_BYTES;
+            const uint32_t dst = tmem + static_cast<uint32_t>(buf * BN);
+            for (int kt = kb; kt < ke; ++kt, ++it) {
+                const int s = it % STAGES;
+                const uint32_t ph = (it / STAGES) & 1;
+                if (!mbar_wait_bounded(&full[s], ph, g.err)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t sa = smem_u32(smem + s * C::STAGE_BYTES);
+                const uint32_t sb = sa + C::A_BYTES;
 #pragma unroll
-            for (int k = 0; k < kGemmBK / 16; ++k) {
-                const uint64_t ad = g.a_mn ? umma_desc_sw128(sa + k * 2048, 8192, 1024)
-                                           : umma_desc_sw128(sa + k * 32, 16, 1024);
-                const uint64_t bd = g.b_mn ? umma_desc_sw128(sb + k * 2048, 8192, 1024)
-                                           : umma_desc_sw128(sb + k * 32, 16, 1024);
-                tc_mma_f16(tmem, ad, bd, idesc, (kt | k) != 0 ? 1u : 0u);
+                for (int k = 0; k < kGemmBK / 16; ++k) {
+                    const uint64_t ad = g.a_mn ? umma_desc_sw128(sa + k * 2048, 8192, 1024)
+                                               : umma_desc_sw128(sa + k * 32, 16, 1024);
+                    const uint64_t bd = g.b_mn ? umma_desc_sw128(sb + k * 2048, 8192, 1024)
+                                               : umma_desc_sw128(sb + k * 32, 16, 1024);
+                    tc_mma_f16(dst, ad, bd, idesc, (kt != kb || k != 0) ? 1u : 0u);
+                }
+                tc_commit(&empty[s]);
             }
-            tc_commit(&empty[s]);
+            tc_commit(&acc_full[buf]);
         }
-        tc_commit(done);
     } else if (warp >= 2) {
-        if (mbar_wait_bounded(done, 0, g.err)) {
+        const int q = warp & 3;
+        const float alpha = g.alpha * (g.alpha_ptr ? *g.alpha_ptr : 1.0f);
+        int j = 0;
+        for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++j) {
+            const int z = tile / (tiles_n * tiles_m), mn = tile % (tiles_n * tiles_m);
+            const int m0 = (mn / tiles_n) * kGemmBM, n0 = (mn % tiles_n) * BN;
+            const int n_mma = min(BN, ((g.N - n0) + 15) / 16 * 16);
+            const int buf = j & 1;
+            if (!mbar_wait_bounded(&acc_full[buf], (j >> 1) & 1, g.err)) break;
             tc_fence_after();
-            const int q = warp & 3;
+            GemmArgs gz = g;
+            if (g.k_tiles_per_split > 0)
+                gz.out = static_cast<char*>(g.out) +
+                         z * g.split_stride * (g.out_kind >= kOutF16 ? 2 : 4);
             const int row = m0 + q * 32 + lane;
-            const float alpha = g.alpha * (g.alpha_ptr ? *g.alpha_ptr : 1.0f);
+            const uint32_t src = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * BN);
+            // Drain the whole accumulator into registers in 16-column pieces, store each.
             for (int c = 0; c < n_mma; c += 16) {
                 float v[16];
-                tmem_ld16(tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(c), v);
-                if (row < g.M && n0 + c < g.N) gemm_store16(g, alpha, row, n0 + c, v);
+                tmem_ld16(src + static_cast<uint32_t>(c), v);
+                if (c + 16 >= n_mma) {
+                    // last read of this buffer: hand it back to the MMA warp before storing
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&acc_empty[buf]);
+                }
+                if (row < g.M && n0 + c < g.N) gemm_store16(gz, alpha, row, n0 + c, v);
             }
         }
     }
@@ -193,7 +246,7 @@ __global__ void __launch_bounds__(192, 1)
     __syncthreads();
     if (warp == 0) {
         tc_fence_after();
-        tmem_dealloc(tmem, BN);
+        tmem_dealloc(tmem, 2 * BN);
     }
 }
 

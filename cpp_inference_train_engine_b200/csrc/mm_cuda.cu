@@ -431,6 +431,7 @@ int mm_cuda_profile(mm_cuda_ctx* h, int enable, double* ms, int64_t* calls, doub
         if (enable >= 0) {
             cx.profiling = enable != 0;
             cx.prof = mm::Profile{};
+            cx.evlog.shapes.clear();
         }
     });
 }
@@ -482,6 +483,26 @@ int mm_decode_attention_noalloc(const float* q, const void* cache, int64_t cache
     if (cudaGetLastError() != cudaSuccess) return MM_GPU_ERROR;
     if (cudaStreamSynchronize(s) != cudaSuccess) return MM_GPU_ERROR;
     return MM_OK;
+}
+
+int64_t mm_cuda_profile_gemm_shapes(mm_cuda_ctx* h, char* buf, int64_t cap) {
+    std::string text;
+    int rc = guarded(h, [&](mm::Context& cx) {
+        cx.prof_resolve();
+        for (const auto& [key, st] : cx.evlog.shapes) {
+            char line[192];
+            std::snprintf(line, sizeof line, "%s calls=%lld ms=%.4f tflops=%.2f\n", key.c_str(), st.calls, st.ms,
+                          st.ms > 0 ? st.flops / (st.ms * 1e9) : 0.0);
+            text += line;
+        }
+    });
+    if (rc) return -rc;
+    if (buf && cap > 0) {
+        const size_t n = std::min(static_cast<size_t>(cap - 1), text.size());
+        std::memcpy(buf, text.data(), n);
+        buf[n] = 0;
+    }
+    return static_cast<int64_t>(text.size());
 }
 
 int mm_cuda_stream(mm_cuda_ctx* h, void** stream) {

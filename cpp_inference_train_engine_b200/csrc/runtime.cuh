@@ -204,9 +204,16 @@ struct Profile {
     long long calls[kProfTags] = {0};
     double work[kProfTags] = {0};  // flops (GEMM, attention) or bytes (the rest)
 };
+struct ShapeStat {
+    long long calls = 0;
+    double ms = 0, flops = 0;
+};
 struct EventLog {
     std::vector<cudaEvent_t> free_events;
     std::vector<std::tuple<int, cudaEvent_t, cudaEvent_t>> pending;
+    // GEMM intervals by launch shape: (shape key, start, end)
+    std::vector<std::tuple<std::string, cudaEvent_t, cudaEvent_t>> pending_shapes;
+    std::map<std::string, ShapeStat> shapes;
     cudaEvent_t take() {
         if (free_events.empty()) {
             cudaEvent_t e;
@@ -260,6 +267,7 @@ class Context {
     Workspace ws;
     Arena ws_arena;
     Staging stage;
+    Staging splitk;  // split-K partials of the GEMM
     DecodeState dec;
     int dec_len = 0;  // positions filled in the decode session (0: no session)
 
@@ -288,10 +296,27 @@ class Context {
         prof.work[tag] += work;
         prof.calls[tag] += 1;
     }
+    // Also files the interval opened by `start` (owned by the class log) under a GEMM shape;
+    // the shape log records its own end event.
+    void prof_shape(const std::string& key, cudaEvent_t start, double flops) {
+        if (!start) return;
+        cudaEvent_t b = evlog.take();
+        cudaEventRecord(b, stream);
+        evlog.pending_shapes.emplace_back(key, start, b);
+        evlog.shapes[key].calls += 1;
+        evlog.shapes[key].flops += flops;
+    }
     // Waits for the stream and folds every pending interval into prof.ms.
     void prof_resolve() {
-        if (evlog.pending.empty()) return;
+        if (evlog.pending.empty() && evlog.pending_shapes.empty()) return;
         cudaStreamSynchronize(stream);
+        for (auto& [key, a, b] : evlog.pending_shapes) {
+            float ms = 0.f;
+            cudaEventElapsedTime(&ms, a, b);
+            evlog.shapes[key].ms += ms;
+            evlog.free_events.push_back(b);
+        }
+        evlog.pending_shapes.clear();
         for (auto& [tag, a, b] : evlog.pending) {
             float ms = 0.f;
             cudaEventElapsedTime(&ms, a, b);
@@ -372,6 +397,17 @@ struct GemmOutSpec {
     const float* alpha_ptr = nullptr;
 };
 
+inline int sm_count() {
+    static int n = 0;
+    if (!n) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        if (n <= 0) n = 148;
+    }
+    return n;
+}
+
 template <int BN, int STAGES>
 inline void launch_gemm_bn(Context& cx, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& ga) {
     using C = GemmCfg<BN, STAGES>;
@@ -380,10 +416,23 @@ inline void launch_gemm_bn(Context& cx, const CUtensorMap& ta, const CUtensorMap
         MM_CUDA_CHECK(cudaFuncSetAttribute(gemm_tc_kernel<BN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
         configured = true;
     }
-    dim3 grid(static_cast<unsigned>((ga.N + BN - 1) / BN), static_cast<unsigned>((ga.M + kGemmBM - 1) / kGemmBM));
+    const long long num_k = (ga.K + kGemmBK - 1) / kGemmBK;
+    const long long per = ga.k_tiles_per_split > 0 ? ga.k_tiles_per_split : num_k;
+    const long long tiles = static_cast<long long>((ga.N + BN - 1) / BN) * ((ga.M + kGemmBM - 1) / kGemmBM) *
+                            ((num_k + per - 1) / per);
+    // resident CTAs per SM: two TMEM accumulators of BN columns each out of 512, and smem
+    const int per_sm = std::max(1, std::min(512 / (2 * BN), (227 * 1024) / C::SMEM));
+    dim3 grid(static_cast<unsigned>(std::min<long long>(tiles, static_cast<long long>(sm_count()) * per_sm)));
     cudaEvent_t t0 = cx.prof_begin();
     gemm_tc_kernel<BN, STAGES><<<grid, 192, C::SMEM, cx.stream>>>(ta, tb, ga);
-    cx.prof_end(kKGemm, t0, 2.0 * ga.M * static_cast<double>(ga.N) * ga.K);
+    const double flops = 2.0 * ga.M * static_cast<double>(ga.N) * ga.K;
+    if (t0) {
+        char key[96];
+        std::snprintf(key, sizeof key, "M%d N%d K%d a%s b%s bn%d out%d", ga.M, ga.N, ga.K, ga.a_mn ? "mn" : "k",
+                      ga.b_mn ? "mn" : "k", BN, ga.out_kind);
+        cx.prof_shape(key, t0, flops);
+    }
+    cx.prof_end(kKGemm, t0, flops);
     ++cx.launches;
 }
 

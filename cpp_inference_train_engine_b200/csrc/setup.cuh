@@ -5,6 +5,19 @@
 
 namespace mm {
 
+// out[r][c] += alpha * (*alpha_ptr) * sum_z part[z][r][c], z in order (deterministic split-K).
+__global__ void splitk_reduce_kernel(const float* __restrict__ part, int splits, int M, int N, float* __restrict__ out,
+                                     long long ldc, float alpha, const float* __restrict__ alpha_ptr) {
+    const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const long long MN = static_cast<long long>(M) * N;
+    if (idx >= MN) return;
+    float s = 0.f;
+    for (int z = 0; z < splits; ++z) s += part[z * MN + idx];
+    const float a = alpha * (alpha_ptr ? *alpha_ptr : 1.0f);
+    const int r = static_cast<int>(idx / N), c = static_cast<int>(idx % N);
+    out[r * ldc + c] += a * s;
+}
+
 inline void gemm(Context& cx, int M, int N, int K, Opnd A, Opnd B, const GemmOutSpec& o, bool bf16) {
     if (M <= 0 || N <= 0 || K <= 0) return;
     const long long tiles_m = (M + kGemmBM - 1) / kGemmBM;
@@ -16,10 +29,39 @@ inline void gemm(Context& cx, int M, int N, int K, Opnd A, Opnd B, const GemmOut
     const CUtensorMap& tb = B.mn ? tensor_map(B.p, bf16, N, K, B.ld, 64, 64)
                                  : tensor_map(B.p, bf16, K, N, B.ld, 64, BN);
     GemmArgs ga{M, N, K, A.mn ? 1 : 0, B.mn ? 1 : 0, bf16 ? 1 : 0, o.out, o.ldc, o.kind,
-                o.residual, o.ldr, o.alpha, o.alpha_ptr, cx.d_err};
+                o.residual, o.ldr, o.alpha, o.alpha_ptr, cx.d_err, 0, 0};
+    // Split-K for accumulating products with few output tiles over a long K (the weight
+    // gradients, K = tokens): each K slice stores its fp32 partial, then one reduction adds
+    // them in order into the destination.
+    const long long tiles = tiles_m * ((N + BN - 1) / BN);
+    const int num_k = (K + kGemmBK - 1) / kGemmBK;
+    int splits = 1;
+    if (o.kind == kOutF32Acc && !o.residual && tiles < sm_count() && num_k >= 32) {
+        splits = static_cast<int>(std::min<long long>((2LL * sm_count() + tiles - 1) / tiles, num_k / 8));
+        splits = std::max(1, std::min(splits, 32));
+    }
+    float* part = nullptr;
+    if (splits > 1) {
+        const int per = (num_k + splits - 1) / splits;
+        splits = (num_k + per - 1) / per;
+        part = static_cast<float*>(cx.splitk.get(sizeof(float) * static_cast<size_t>(splits) * M * N));
+        ga.k_tiles_per_split = per;
+        ga.split_stride = static_cast<long long>(M) * N;
+        ga.out = part;
+        ga.ldc = N;
+        ga.out_kind = kOutF32;
+        ga.alpha = 1.f;
+        ga.alpha_ptr = nullptr;
+    }
     if (BN == 256) launch_gemm_bn<256, 4>(cx, ta, tb, ga);
     else if (BN == 128) launch_gemm_bn<128, 3>(cx, ta, tb, ga);
     else launch_gemm_bn<64, 4>(cx, ta, tb, ga);
+    if (splits > 1) {
+        const long long MN = static_cast<long long>(M) * N;
+        splitk_reduce_kernel<<<blocks_for(MN, 256), 256, 0, cx.stream>>>(part, splits, M, N, static_cast<float*>(o.out),
+                                                                          o.ldc, o.alpha, o.alpha_ptr);
+        ++cx.launches;
+    }
 }
 
 inline Dims dims_from(const mm_model_desc& d) {

@@ -121,6 +121,7 @@ def lib():
         "mm_cuda_stream": (ctypes.c_int, [_vp, ctypes.POINTER(_vp)]),
         "mm_cuda_decode_attention": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int64, _vp, ctypes.c_int,
                                                     ctypes.c_int, ctypes.c_float, _vp]),
+        "mm_cuda_profile_gemm_shapes": (ctypes.c_int64, [_vp, ctypes.c_char_p, ctypes.c_int64]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)
@@ -396,6 +397,21 @@ class CudaExecution:
         """Kernel-level latent decode attention on device pointers (mm_cuda_kernels.h)."""
         self._check(lib().mm_cuda_decode_attention(self.h, q_ptr, cache_ptr, cache_seq_stride,
                                                    pos_ptr, batch, splits, scale, out_ptr))
+
+    def gemm_shapes(self):
+        """Per-shape GEMM timing collected while profiling: list of dicts."""
+        n = lib().mm_cuda_profile_gemm_shapes(self.h, None, 0)
+        if n < 0:
+            raise EngineError(-n, self._error())
+        buf = ctypes.create_string_buffer(int(n) + 1)
+        lib().mm_cuda_profile_gemm_shapes(self.h, buf, n + 1)
+        out = []
+        for line in buf.value.decode().splitlines():
+            parts = dict(p.split("=") for p in line.split() if "=" in p)
+            out.append({"shape": " ".join(p for p in line.split() if "=" not in p),
+                        "calls": int(parts["calls"]), "ms": float(parts["ms"]),
+                        "tflops": float(parts["tflops"])})
+        return sorted(out, key=lambda r: -r["ms"])
 
     def profile(self, enable: int = -1):
         """{tag: (device ms, launches, algorithmic work)}; see PROFILE_TAGS."""

@@ -67,6 +67,10 @@ int mm_decode_attention_noalloc(const float* q, const void* cache, int64_t cache
  * enable: 1 start/reset, 0 stop/reset, -1 read only. Any pointer may be NULL. */
 int mm_cuda_profile(mm_cuda_ctx* ctx, int enable, double* ms, int64_t* calls, double* work);
 
+/* While profiling: one text line per GEMM launch shape ("M.. N.. K.. a.. b.. bn.. out..
+ * calls= ms= tflops="), NUL-terminated into buf. Returns the full length, or -(1 + code). */
+int64_t mm_cuda_profile_gemm_shapes(mm_cuda_ctx* ctx, char* buf, int64_t cap);
+
 /* The context's CUDA stream (cudaStream_t), for events recorded by a caller. */
 int mm_cuda_stream(mm_cuda_ctx* ctx, void** stream);
 

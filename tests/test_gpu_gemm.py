@@ -87,6 +87,35 @@ def test_gemm_epilogues(ex, kind):
     assert (out - want).abs().max().item() <= tol * max(1.0, want.abs().max().item())
 
 
+@pytest.mark.parametrize("shape", [(4096, 4096, 256), (2048, 16384, 1536), (4000, 1360, 512)])
+def test_gemm_persistent_multiple_tiles_per_cta(ex, shape):
+    """More output tiles than resident CTAs: each CTA walks several tiles and alternates
+    its two tensor-memory accumulators."""
+    import torch
+    M, N, K = shape
+    A = torch.randn(M, K, device="cuda").half()
+    Bt = torch.randn(N, K, device="cuda").half()
+    out = torch.zeros(M, N, device="cuda")
+    ex.gemm(M, N, K, A.data_ptr(), K, 0, Bt.data_ptr(), K, 0, out.data_ptr(), N, 0)
+    want = A.float() @ Bt.float().t()
+    assert (out - want).abs().max().item() <= 1e-3 * want.abs().max().item()
+
+
+@pytest.mark.parametrize("shape", [(512, 192, 32768), (128, 384, 24576), (1360, 512, 8192)])
+def test_gemm_split_k_accumulate(ex, shape):
+    """Weight-gradient pattern: out += alpha * X^T dY with X, dY stored [tokens][features]
+    (both operands MN-major) and K = tokens: split over K, reduced in order."""
+    import torch
+    M, N, K = shape
+    X = (torch.randn(K, M, device="cuda") * 0.1).half()
+    dY = (torch.randn(K, N, device="cuda") * 0.1).half()
+    R = torch.randn(M, N, device="cuda")
+    out = R.clone()
+    ex.gemm(M, N, K, X.data_ptr(), M, 1, dY.data_ptr(), N, 1, out.data_ptr(), N, 1, alpha=0.5)
+    want = R + 0.5 * (X.float().t() @ dY.float())
+    assert (out - want).abs().max().item() <= 1e-3 * max(1.0, want.abs().max().item())
+
+
 def test_gemm_bf16_operands(ex):
     import torch
     M, N, K = 256, 256, 256

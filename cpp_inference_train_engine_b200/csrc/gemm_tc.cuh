@@ -10,11 +10,15 @@
 // so x*W (W stored [in][out]) is "B MN-major", dY*W^T is "B K-major" and X^T*dY is
 // "A and B MN-major": no transposed copies of weights or activations are ever made.
 //
-// One output tile (128 x BN) per CTA, 6 warps: warp 0 issues TMA (one elected thread),
-// warp 1 issues tcgen05.mma (one thread) and commits each stage back to the producer,
-// warps 2-5 drain tensor memory (lane quarter = warp % 4) and store. Every mbarrier
-// wait is bounded; a timeout sets the device error word and the CTA unwinds, freeing its
-// tensor memory.
+// Persistent: CTA c processes tiles c, c + gridDim.x, ... of the (m, n, k-split) tile
+// list, n fastest (consecutive CTAs share the A row tile in L2). 6 warps: warp 0 issues
+// TMA into a ring of STAGES (A, B) stages that runs across tile boundaries; warp 1 issues
+// tcgen05.mma (one thread) into one of two TMEM accumulators of BN columns, so the
+// epilogue of tile j overlaps the MMAs of tile j + 1; warps 2-5 drain tensor memory
+// (lane quarter = warp % 4) 128 bytes per row at a time into a 128-byte-swizzled shared
+// staging tile and hand it to a TMA bulk tensor store (fp32 += uses the TMA reduce-add),
+// which also clips the ragged edges. Every mbarrier wait is bounded; a timeout sets the
+// device error word and the CTA unwinds, freeing its tensor memory.
 #pragma once
 #include "common.cuh"
 
@@ -25,95 +29,41 @@ enum GemmOut : int { kOutF32 = 0, kOutF32Acc = 1, kOutF16 = 2, kOutBF16 = 3 };
 struct GemmArgs {
     int M, N, K;
     int a_mn, b_mn, bf16;
-    void* out;
-    long long ldc;
     int out_kind;
     const float* residual; // optional, fp32 [M][ldr], added in the kOutF32 epilogue
     long long ldr;
     float alpha;
     const float* alpha_ptr; // optional device scalar multiplied into alpha
     int* err;
-    int k_tiles_per_split;   // split-K: CTA z covers k-tiles [z*per, (z+1)*per); 0 = all
-    long long split_stride;  // split-K: output of CTA z starts at out + z * split_stride
+    int k_tiles_per_split;  // split-K: tiles of split z cover k-tiles [z*per, (z+1)*per); 0 = all
+    int split_rows;         // split-K: rows of the output map per split (M rounded up to 128)
 };
 
 constexpr int kGemmBM = 128;
 constexpr int kGemmBK = 64;
+constexpr int kEpiBytes = 4 * 4096;  // one 32-row x 128-byte staging tile per epilogue warp
 
 template <int BN, int STAGES> struct GemmCfg {
     static constexpr int A_BYTES = kGemmBM * 128;
     static constexpr int B_BYTES = BN * 128;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
+    static constexpr int SMEM = STAGES * STAGE_BYTES + kEpiBytes + 1024 + 256;
 };
-
-__device__ __forceinline__ void gemm_store16(const GemmArgs& g, float alpha, int row, int col0,
-                                             const float (&v)[16]) {
-    const bool full = col0 + 16 <= g.N;
-    if (g.out_kind == kOutF32 || g.out_kind == kOutF32Acc) {
-        float* o = static_cast<float*>(g.out) + static_cast<long long>(row) * g.ldc + col0;
-        const float* r = g.residual ? g.residual + static_cast<long long>(row) * g.ldr + col0 : nullptr;
-        const bool vec = full && (g.ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(o) & 15) == 0) &&
-                         (!r || ((g.ldr % 4 == 0) && ((reinterpret_cast<uintptr_t>(r) & 15) == 0)));
-        if (vec) {
-#pragma unroll
-            for (int i = 0; i < 16; i += 4) {
-                float4 x = make_float4(alpha * v[i], alpha * v[i + 1], alpha * v[i + 2],
-                                       alpha * v[i + 3]);
-                if (g.out_kind == kOutF32Acc) {
-                    float4 y = *reinterpret_cast<const float4*>(o + i);
-                    x.x += y.x; x.y += y.y; x.z += y.z; x.w += y.w;
-                } else if (r) {
-                    float4 y = *reinterpret_cast<const float4*>(r + i);
-                    x.x += y.x; x.y += y.y; x.z += y.z; x.w += y.w;
-                }
-                *reinterpret_cast<float4*>(o + i) = x;
-            }
-        } else {
-            for (int i = 0; i < 16 && col0 + i < g.N; ++i) {
-                float x = alpha * v[i];
-                if (g.out_kind == kOutF32Acc) x += o[i];
-                else if (r) x += r[i];
-                o[i] = x;
-            }
-        }
-    } else {
-        // 16-bit outputs.
-        uint16_t* o = static_cast<uint16_t*>(g.out) + static_cast<long long>(row) * g.ldc + col0;
-        uint16_t h[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-            float x = alpha * v[i];
-            h[i] = g.out_kind == kOutF16 ? __half_as_ushort(__float2half_rn(x))
-                                         : __bfloat16_as_ushort(__float2bfloat16_rn(x));
-        }
-        const bool vec = full && (g.ldc % 8 == 0) && ((reinterpret_cast<uintptr_t>(o) & 15) == 0);
-        if (vec) {
-            *reinterpret_cast<uint4*>(o) = *reinterpret_cast<const uint4*>(h);
-            *reinterpret_cast<uint4*>(o + 8) = *reinterpret_cast<const uint4*>(h + 8);
-        } else {
-            for (int i = 0; i < 16 && col0 + i < g.N; ++i) o[i] = h[i];
-        }
-    }
-}
 
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
-// Persistent: CTA c processes tiles c, c + gridDim.x, ... of the (m, n, split) tile list,
-// n fastest (consecutive CTAs share the A row tile in L2). The shared-memory ring of
-// STAGES (A, B) stages runs across tile boundaries; two TMEM accumulators of BN columns
-// alternate, so the epilogue of tile j overlaps the MMAs of tile j + 1.
 template <int BN, int STAGES>
 __global__ void __launch_bounds__(192, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   GemmArgs g) {
+                   const __grid_constant__ CUtensorMap tmC, GemmArgs g) {
     using C = GemmCfg<BN, STAGES>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~static_cast<uintptr_t>(1023));
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * C::STAGE_BYTES);
+    uint8_t* epi = smem + STAGES * C::STAGE_BYTES;
+    uint64_t* full = reinterpret_cast<uint64_t*>(epi + kEpiBytes);
     uint64_t* empty = full + STAGES;
     uint64_t* acc_full = empty + STAGES;  // [2] MMA -> epilogue
     uint64_t* acc_empty = acc_full + 2;   // [2] epilogue -> MMA (4 warp arrivals)
@@ -139,6 +89,7 @@ __global__ void __launch_bounds__(192, 1)
             fence_mbar_init();
             prefetch_tmap(&tmA);
             prefetch_tmap(&tmB);
+            prefetch_tmap(&tmC);
         }
         __syncwarp();
         tmem_alloc(tmem_slot, 2 * BN);
@@ -213,7 +164,10 @@ __global__ void __launch_bounds__(192, 1)
         }
     } else if (warp >= 2) {
         const int q = warp & 3;
+        uint8_t* stage = epi + (warp - 2) * 4096;
         const float alpha = g.alpha * (g.alpha_ptr ? *g.alpha_ptr : 1.0f);
+        const bool half_out = g.out_kind >= kOutF16;
+        const int CH = half_out ? 64 : 32;  // columns per 128-byte staged row
         int j = 0;
         for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++j) {
             const int z = tile / (tiles_n * tiles_m), mn = tile % (tiles_n * tiles_m);
@@ -222,25 +176,68 @@ __global__ void __launch_bounds__(192, 1)
             const int buf = j & 1;
             if (!mbar_wait_bounded(&acc_full[buf], (j >> 1) & 1, g.err)) break;
             tc_fence_after();
-            GemmArgs gz = g;
-            if (g.k_tiles_per_split > 0)
-                gz.out = static_cast<char*>(g.out) +
-                         z * g.split_stride * (g.out_kind >= kOutF16 ? 2 : 4);
-            const int row = m0 + q * 32 + lane;
+            const int row0 = m0 + q * 32;
+            const int row = row0 + lane;
+            const int map_row0 = row0 + (g.k_tiles_per_split > 0 ? z * g.split_rows : 0);
             const uint32_t src = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * BN);
-            // Drain the whole accumulator into registers in 16-column pieces, store each.
-            for (int c = 0; c < n_mma; c += 16) {
-                float v[16];
-                tmem_ld16(src + static_cast<uint32_t>(c), v);
-                if (c + 16 >= n_mma) {
-                    // last read of this buffer: hand it back to the MMA warp before storing
+            for (int c = 0; c < n_mma; c += CH) {
+                float v[64];
+                tmem_ld32_nowait(src + static_cast<uint32_t>(c), v);
+                if (half_out) tmem_ld32_nowait(src + static_cast<uint32_t>(c + 32), v + 32);
+                tmem_wait_ld();
+                if (c + CH >= n_mma) {
+                    // last read of this accumulator: hand it back to the MMA warp first
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&acc_empty[buf]);
                 }
-                if (row < g.M && n0 + c < g.N) gemm_store16(gz, alpha, row, n0 + c, v);
+                const int col0 = n0 + c;
+#pragma unroll
+                for (int i = 0; i < 64; ++i) v[i] *= alpha;
+                if (g.residual && row < g.M) {
+                    const float* r = g.residual + static_cast<long long>(row) * g.ldr + col0;
+#pragma unroll
+                    for (int i = 0; i < 32; ++i)
+                        if (col0 + i < g.N) v[i] += r[i];
+                }
+                // the previous store from this staging tile must have finished reading it
+                if (lane == 0) bulk_wait_read0();
+                __syncwarp();
+                uint8_t* rowp = stage + lane * 128;
+                if (half_out) {
+#pragma unroll
+                    for (int ch = 0; ch < 8; ++ch) {
+                        uint32_t w[4];
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const float a = v[ch * 8 + 2 * e], b = v[ch * 8 + 2 * e + 1];
+                            if (g.out_kind == kOutF16) {
+                                const __half2 h = __floats2half2_rn(a, b);
+                                w[e] = *reinterpret_cast<const uint32_t*>(&h);
+                            } else {
+                                const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+                                w[e] = *reinterpret_cast<const uint32_t*>(&h);
+                            }
+                        }
+                        *reinterpret_cast<uint4*>(rowp + ((ch ^ (lane & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+                    }
+                } else {
+#pragma unroll
+                    for (int ch = 0; ch < 8; ++ch)
+                        *reinterpret_cast<float4*>(rowp + ((ch ^ (lane & 7)) << 4)) =
+                            make_float4(v[4 * ch], v[4 * ch + 1], v[4 * ch + 2], v[4 * ch + 3]);
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    if (g.out_kind == kOutF32Acc) tma_reduce_add_2d(&tmC, stage, col0, map_row0);
+                    else tma_store_2d(&tmC, stage, col0, map_row0);
+                    bulk_commit();
+                }
             }
         }
+        if (lane == 0) bulk_wait0();
+        __syncwarp();
     }
     tc_fence_before();
     __syncthreads();

@@ -356,26 +356,35 @@ inline PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 
 // 2-D fp16/bf16 tensor map, 128-byte swizzle, zero fill out of bounds. Cached by
 // (address, shape, pitch, box): buffers are long-lived, so the encode runs once per view.
-inline const CUtensorMap& tensor_map(const void* base, bool bf16, long long dim0, long long dim1,
-                                     long long pitch_elems, int box0, int box1) {
-    using Key = std::tuple<const void*, bool, long long, long long, long long, int, int>;
+enum MapType : int { kMapF16 = 0, kMapBF16 = 1, kMapF32 = 2 };
+
+inline const CUtensorMap& tensor_map_t(const void* base, int type, long long dim0, long long dim1,
+                                       long long pitch_elems, int box0, int box1) {
+    using Key = std::tuple<const void*, int, long long, long long, long long, int, int>;
     static std::map<Key, CUtensorMap> cache;
-    Key k{base, bf16, dim0, dim1, pitch_elems, box0, box1};
+    Key k{base, type, dim0, dim1, pitch_elems, box0, box1};
     auto it = cache.find(k);
     if (it != cache.end()) return it->second;
-    if ((reinterpret_cast<uintptr_t>(base) & 15) || (pitch_elems * 2) % 16)
+    const int esize = type == kMapF32 ? 4 : 2;
+    if ((reinterpret_cast<uintptr_t>(base) & 15) || (pitch_elems * esize) % 16)
         fail(MM_INVALID_ARGUMENT, "tensor map needs 16-byte aligned base and pitch");
     CUtensorMap map;
     cuuint64_t dims[2] = {static_cast<cuuint64_t>(dim0), static_cast<cuuint64_t>(dim1)};
-    cuuint64_t strides[1] = {static_cast<cuuint64_t>(pitch_elems * 2)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(pitch_elems * esize)};
     cuuint32_t box[2] = {static_cast<cuuint32_t>(box0), static_cast<cuuint32_t>(box1)};
     cuuint32_t estr[2] = {1, 1};
-    CUresult r = tensor_map_encoder()(&map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-                                      2, const_cast<void*>(base), dims, strides, box, estr,
+    const CUtensorMapDataType dt = type == kMapF32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                   : type == kMapBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                      : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    CUresult r = tensor_map_encoder()(&map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
                                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                                       CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) fail(MM_GPU_ERROR, "cuTensorMapEncodeTiled failed: " + std::to_string(static_cast<int>(r)));
     return cache.emplace(k, map).first->second;
+}
+inline const CUtensorMap& tensor_map(const void* base, bool bf16, long long dim0, long long dim1,
+                                     long long pitch_elems, int box0, int box1) {
+    return tensor_map_t(base, bf16 ? kMapBF16 : kMapF16, dim0, dim1, pitch_elems, box0, box1);
 }
 
 // ------------------------------------------------------------------ GEMM launcher
@@ -409,7 +418,8 @@ inline int sm_count() {
 }
 
 template <int BN, int STAGES>
-inline void launch_gemm_bn(Context& cx, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& ga) {
+inline void launch_gemm_bn(Context& cx, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
+                           const GemmArgs& ga) {
     using C = GemmCfg<BN, STAGES>;
     static bool configured = false;
     if (!configured) {
@@ -424,7 +434,7 @@ inline void launch_gemm_bn(Context& cx, const CUtensorMap& ta, const CUtensorMap
     const int per_sm = std::max(1, std::min(512 / (2 * BN), (227 * 1024) / C::SMEM));
     dim3 grid(static_cast<unsigned>(std::min<long long>(tiles, static_cast<long long>(sm_count()) * per_sm)));
     cudaEvent_t t0 = cx.prof_begin();
-    gemm_tc_kernel<BN, STAGES><<<grid, 192, C::SMEM, cx.stream>>>(ta, tb, ga);
+    gemm_tc_kernel<BN, STAGES><<<grid, 192, C::SMEM, cx.stream>>>(ta, tb, tc, ga);
     const double flops = 2.0 * ga.M * static_cast<double>(ga.N) * ga.K;
     if (t0) {
         char key[96];

@@ -5,14 +5,16 @@
 
 namespace mm {
 
-// out[r][c] += alpha * (*alpha_ptr) * sum_z part[z][r][c], z in order (deterministic split-K).
-__global__ void splitk_reduce_kernel(const float* __restrict__ part, int splits, int M, int N, float* __restrict__ out,
-                                     long long ldc, float alpha, const float* __restrict__ alpha_ptr) {
+// out[r][c] += alpha * (*alpha_ptr) * sum_z part[z][r][c], z in order (deterministic
+// split-K); split z's partial starts at part + z * split_stride.
+__global__ void splitk_reduce_kernel(const float* __restrict__ part, int splits, long long split_stride, int M, int N,
+                                     float* __restrict__ out, long long ldc, float alpha,
+                                     const float* __restrict__ alpha_ptr) {
     const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
     const long long MN = static_cast<long long>(M) * N;
     if (idx >= MN) return;
     float s = 0.f;
-    for (int z = 0; z < splits; ++z) s += part[z * MN + idx];
+    for (int z = 0; z < splits; ++z) s += part[z * split_stride + idx];
     const float a = alpha * (alpha_ptr ? *alpha_ptr : 1.0f);
     const int r = static_cast<int>(idx / N), c = static_cast<int>(idx % N);
     out[r * ldc + c] += a * s;
@@ -28,7 +30,7 @@ inline void gemm(Context& cx, int M, int N, int K, Opnd A, Opnd B, const GemmOut
                                  : tensor_map(A.p, bf16, K, M, A.ld, 64, kGemmBM);
     const CUtensorMap& tb = B.mn ? tensor_map(B.p, bf16, N, K, B.ld, 64, 64)
                                  : tensor_map(B.p, bf16, K, N, B.ld, 64, BN);
-    GemmArgs ga{M, N, K, A.mn ? 1 : 0, B.mn ? 1 : 0, bf16 ? 1 : 0, o.out, o.ldc, o.kind,
+    GemmArgs ga{M, N, K, A.mn ? 1 : 0, B.mn ? 1 : 0, bf16 ? 1 : 0, o.kind,
                 o.residual, o.ldr, o.alpha, o.alpha_ptr, cx.d_err, 0, 0};
     // Split-K for accumulating products with few output tiles over a long K (the weight
     // gradients, K = tokens): each K slice stores its fp32 partial, then one reduction adds
@@ -36,30 +38,43 @@ inline void gemm(Context& cx, int M, int N, int K, Opnd A, Opnd B, const GemmOut
     const long long tiles = tiles_m * ((N + BN - 1) / BN);
     const int num_k = (K + kGemmBK - 1) / kGemmBK;
     int splits = 1;
-    if (o.kind == kOutF32Acc && !o.residual && tiles < sm_count() && num_k >= 32) {
+    if (o.kind == kOutF32Acc && !o.residual && tiles < sm_count() && num_k >= 32 && N % 4 == 0) {
         splits = static_cast<int>(std::min<long long>((2LL * sm_count() + tiles - 1) / tiles, num_k / 8));
         splits = std::max(1, std::min(splits, 32));
     }
+    // Output map: 32-row x 128-byte boxes; fp32 partials of split z occupy rows
+    // [z * Mp, z * Mp + M) with Mp = M rounded up to whole 128-row tiles, so a tile's
+    // clipped edge never reaches the next split.
+    const int map_type = (o.kind == kOutF16) ? kMapF16 : (o.kind == kOutBF16) ? kMapBF16 : kMapF32;
+    const int ch = map_type == kMapF32 ? 32 : 64;
     float* part = nullptr;
+    const CUtensorMap* tc = nullptr;
     if (splits > 1) {
         const int per = (num_k + splits - 1) / splits;
         splits = (num_k + per - 1) / per;
-        part = static_cast<float*>(cx.splitk.get(sizeof(float) * static_cast<size_t>(splits) * M * N));
+        const int Mp = static_cast<int>(tiles_m * kGemmBM);
+        const long long n_pad = N;  // N % 4 == 0: 16-byte row pitch
+        part = static_cast<float*>(cx.splitk.get(sizeof(float) * static_cast<size_t>(splits) * Mp * n_pad));
         ga.k_tiles_per_split = per;
-        ga.split_stride = static_cast<long long>(M) * N;
-        ga.out = part;
-        ga.ldc = N;
+        ga.split_rows = Mp;
         ga.out_kind = kOutF32;
         ga.alpha = 1.f;
         ga.alpha_ptr = nullptr;
+        tc = &tensor_map_t(part, kMapF32, N, static_cast<long long>(splits) * Mp, n_pad, 32, 32);
+    } else {
+        tc = &tensor_map_t(o.out, map_type, N, M, o.ldc, ch, 32);
     }
-    if (BN == 256) launch_gemm_bn<256, 4>(cx, ta, tb, ga);
-    else if (BN == 128) launch_gemm_bn<128, 3>(cx, ta, tb, ga);
-    else launch_gemm_bn<64, 4>(cx, ta, tb, ga);
+    if (BN == 256) launch_gemm_bn<256, 4>(cx, ta, tb, *tc, ga);
+    else if (BN == 128) launch_gemm_bn<128, 3>(cx, ta, tb, *tc, ga);
+    else launch_gemm_bn<64, 4>(cx, ta, tb, *tc, ga);
     if (splits > 1) {
+        // partial of split z, row r: part[(z * Mp + r) * n_pad + c]; reduce over a dense view
+        const int Mp = ga.split_rows;
+        const long long n_pad = N;
         const long long MN = static_cast<long long>(M) * N;
-        splitk_reduce_kernel<<<blocks_for(MN, 256), 256, 0, cx.stream>>>(part, splits, M, N, static_cast<float*>(o.out),
-                                                                          o.ldc, o.alpha, o.alpha_ptr);
+        splitk_reduce_kernel<<<blocks_for(MN, 256), 256, 0, cx.stream>>>(
+            part, splits, static_cast<long long>(Mp) * n_pad, M, N, static_cast<float*>(o.out), o.ldc, o.alpha,
+            o.alpha_ptr);
         ++cx.launches;
     }
 }

@@ -50,10 +50,11 @@ template <class A> void plan_workspace(Context& cx, A& a, int T, bool tape) {
         LayerBuf& b = w.layers[l];
         b.x_in = a.template take<float>(t * c.d);
         b.h = a.template take<__half>(t * cx.d16(c.d));
-        b.raw_cq = a.template take<float>(t * c.qr);
+        // [raw_cq | kv_pack] from one product with [W_dq | W_dkv], row pitch qr + kvw
+        b.raw_cq = a.template take<float>(t * (c.qr + c.kvw()));
+        b.kvp = b.raw_cq ? b.raw_cq + c.qr : nullptr;
         b.cq = a.template take<__half>(t * cx.d16(c.qr));
         b.q = a.template take<__half>(t * c.H * c.qk());
-        b.kvp = a.template take<float>(t * c.kvw());
         b.ckv = a.template take<__half>(t * cx.d16(c.kvr));
         b.k_rope = a.template take<float>(t * c.rope);
         b.k = a.template take<__half>(t * c.H * c.qk());
@@ -62,8 +63,9 @@ template <class A> void plan_workspace(Context& cx, A& a, int T, bool tape) {
         b.lse = a.template take<float>(t * c.H);
         b.res = a.template take<float>(t * c.d);
         b.h2 = a.template take<__half>(t * cx.d16(c.d));
-        b.gate = a.template take<__half>(t * cx.d16(c.dff));
-        b.up = a.template take<__half>(t * cx.d16(c.dff));
+        // [gate | up] from one product with [W_gate | W_up], row pitch ld16(2 d_ff)
+        b.gate = a.template take<__half>(t * cx.d16(2 * c.dff));
+        b.up = b.gate ? b.gate + c.dff : nullptr;
         b.gated = a.template take<__half>(t * cx.d16(c.dff));
     }
     w.x_out = a.template take<float>(t * c.d);
@@ -97,14 +99,16 @@ template <class A> void plan_workspace(Context& cx, A& a, int T, bool tape) {
         w.dcq = a.template take<float>(t * c.qr);
         w.Dd = a.template take<float>(t * c.H);
         w.dy16 = a.template take<__half>(t * cx.d16(c.d));
-        w.dg16 = a.template take<__half>(t * cx.d16(c.dff));
-        w.du16 = a.template take<__half>(t * cx.d16(c.dff));
+        // [d gate | d up], pitch ld16(2 d_ff)
+        w.dg16 = a.template take<__half>(t * cx.d16(2 * c.dff));
+        w.du16 = w.dg16 ? w.dg16 + c.dff : nullptr;
         w.dres16 = a.template take<__half>(t * cx.d16(c.d));
         w.dq16 = a.template take<__half>(t * cx.d16(c.H * c.qk()));
         w.dkn16 = a.template take<__half>(t * cx.d16(c.H * c.nope));
         w.dv16 = a.template take<__half>(t * cx.d16(c.aw()));
-        w.dkvp16 = a.template take<__half>(t * cx.d16(c.kvw()));
-        w.draw16 = a.template take<__half>(t * cx.d16(c.qr));
+        // [d raw_cq | d kv_pack], pitch ld16(qr + kvw)
+        w.draw16 = a.template take<__half>(t * cx.d16(c.qr + c.kvw()));
+        w.dkvp16 = w.draw16 ? w.draw16 + c.qr : nullptr;
         w.g16 = a.template take<__half>(t * c.V);
         w.dao16 = a.template take<__half>(t * c.aw());
     }
@@ -168,16 +172,17 @@ inline void forward_chunk(Context& cx, int Bc, int S, bool tape, VocabMode vm, b
         // attention block
         MM_LAUNCH(rmsnorm_kernel, warp_rows_grid(T), 256, 0, b.x_in, (long long)c.d, cx.W(l, kAttnNorm), T, c.d, c.eps,
                   (float*)nullptr, 0LL, b.h, (long long)ld_d, (float*)nullptr);
-        gemm(cx, T, c.qr, c.d, {b.h, ld_d, false}, {cx.S(l, kWdq), cx.SL(l, kWdq), true}, {b.raw_cq, c.qr, kOutF32});
-        MM_LAUNCH(rmsnorm_kernel, warp_rows_grid(T), 256, 0, b.raw_cq, (long long)c.qr, cx.W(l, kQNorm), T, c.qr, c.eps,
+        const PrepLayer& pw = cx.prep[l];
+        const int qkv = c.qr + kvw;
+        gemm(cx, T, qkv, c.d, {b.h, ld_d, false}, {pw.Wa, pw.lda, true}, {b.raw_cq, qkv, kOutF32});
+        MM_LAUNCH(rmsnorm_kernel, warp_rows_grid(T), 256, 0, b.raw_cq, (long long)qkv, cx.W(l, kQNorm), T, c.qr, c.eps,
                   (float*)nullptr, 0LL, b.cq, (long long)ld_qr, (float*)nullptr);
         gemm(cx, T, c.H * qk, c.qr, {b.cq, ld_qr, false}, {cx.S(l, kWuq), cx.SL(l, kWuq), true}, {w.q_pre, c.H * qk, kOutF32});
         MM_LAUNCH(rope_rows_kernel, warp_rows_grid(T), 256, 0, w.q_pre, (long long)(c.H * qk), T, S, (const int*)nullptr,
                   c.H, qk, c.nope, c.rope, cx.cos_t, cx.sin_t, 0, (float*)nullptr, 0LL, b.q, (long long)(c.H * qk));
-        gemm(cx, T, kvw, c.d, {b.h, ld_d, false}, {cx.S(l, kWdkv), cx.SL(l, kWdkv), true}, {b.kvp, kvw, kOutF32});
-        MM_LAUNCH(rmsnorm_kernel, warp_rows_grid(T), 256, 0, b.kvp, (long long)kvw, cx.W(l, kKvNorm), T, c.kvr, c.eps,
+        MM_LAUNCH(rmsnorm_kernel, warp_rows_grid(T), 256, 0, b.kvp, (long long)qkv, cx.W(l, kKvNorm), T, c.kvr, c.eps,
                   (float*)nullptr, 0LL, b.ckv, (long long)ld_kvr, (float*)nullptr);
-        MM_LAUNCH(rope_key_kernel, blocks_for((long long)T * (c.rope / 2), 256), 256, 0, b.kvp, (long long)kvw, c.kvr,
+        MM_LAUNCH(rope_key_kernel, blocks_for((long long)T * (c.rope / 2), 256), 256, 0, b.kvp, (long long)qkv, c.kvr,
                   c.rope, T, S, (const int*)nullptr, cx.cos_t, cx.sin_t, b.k_rope, (__half*)nullptr, 0LL);
         if (cache)
             MM_LAUNCH(cache_write_kernel, blocks_for((long long)T * kvw, 256), 256, 0, b.ckv, (long long)ld_kvr, b.k_rope,
@@ -197,9 +202,9 @@ inline void forward_chunk(Context& cx, int Bc, int S, bool tape, VocabMode vm, b
         // feed-forward block
         MM_LAUNCH(rmsnorm_kernel, warp_rows_grid(T), 256, 0, b.res, (long long)c.d, cx.W(l, kFfnNorm), T, c.d, c.eps,
                   (float*)nullptr, 0LL, b.h2, (long long)ld_d, (float*)nullptr);
-        gemm(cx, T, c.dff, c.d, {b.h2, ld_d, false}, {cx.S(l, kWgate), cx.SL(l, kWgate), true}, {b.gate, ld_ff, kOutF16});
-        gemm(cx, T, c.dff, c.d, {b.h2, ld_d, false}, {cx.S(l, kWup), cx.SL(l, kWup), true}, {b.up, ld_ff, kOutF16});
-        MM_LAUNCH(swiglu_kernel, blocks_for((long long)T * c.dff, 256), 256, 0, b.gate, b.up, (long long)ld_ff, T, c.dff,
+        const int ld_gu = cx.d16(2 * c.dff);
+        gemm(cx, T, 2 * c.dff, c.d, {b.h2, ld_d, false}, {pw.Wgu, pw.ldgu, true}, {b.gate, ld_gu, kOutF16});
+        MM_LAUNCH(swiglu_kernel, blocks_for((long long)T * c.dff, 256), 256, 0, b.gate, b.up, (long long)ld_gu, T, c.dff,
                   b.gated, (long long)ld_ff);
         {
             GemmOutSpec o{x_next, c.d, kOutF32};
@@ -268,17 +273,19 @@ inline void backward_chunk(Context& cx, int Bc, int S) {
             gemm(cx, c.dff, c.d, T, {b.gated, ld_ff, true}, {w.dy16, ld_d, true}, o);
         }
         gemm(cx, T, c.dff, c.d, {w.dy16, ld_d, false}, {cx.S(l, kWdown), cx.SL(l, kWdown), false}, {w.dgated, c.dff, kOutF32});
-        MM_LAUNCH(swiglu_backward_kernel, blocks_for((long long)T * c.dff, 256), 256, 0, b.gate, b.up, (long long)ld_ff,
-                  w.dgated, (long long)c.dff, T, c.dff, w.dg16, w.du16, (long long)ld_ff);
+        const int ld_gu = cx.d16(2 * c.dff);
+        const PrepLayer& pw = cx.prep[l];
+        MM_LAUNCH(swiglu_backward_kernel, blocks_for((long long)T * c.dff, 256), 256, 0, b.gate, b.up, (long long)ld_gu,
+                  w.dgated, (long long)c.dff, T, c.dff, w.dg16, w.du16, (long long)ld_gu);
         {
             GemmOutSpec o{cx.G(l, kWgate), c.dff, kOutF32Acc};
             o.alpha_ptr = inv_s;
-            gemm(cx, c.d, c.dff, T, {b.h2, ld_d, true}, {w.dg16, ld_ff, true}, o);
+            gemm(cx, c.d, c.dff, T, {b.h2, ld_d, true}, {w.dg16, ld_gu, true}, o);
             o.out = cx.G(l, kWup);
-            gemm(cx, c.d, c.dff, T, {b.h2, ld_d, true}, {w.du16, ld_ff, true}, o);
+            gemm(cx, c.d, c.dff, T, {b.h2, ld_d, true}, {w.du16, ld_gu, true}, o);
         }
-        gemm(cx, T, c.d, c.dff, {w.dg16, ld_ff, false}, {cx.S(l, kWgate), cx.SL(l, kWgate), false}, {w.dh2, c.d, kOutF32});
-        gemm(cx, T, c.d, c.dff, {w.du16, ld_ff, false}, {cx.S(l, kWup), cx.SL(l, kWup), false}, {w.dh2, c.d, kOutF32Acc});
+        // dh2 = [dg | du] . [W_gate | W_up]^T, one product over K = 2 d_ff
+        gemm(cx, T, c.d, 2 * c.dff, {w.dg16, ld_gu, false}, {pw.Wgu, pw.ldgu, false}, {w.dh2, c.d, kOutF32});
         MM_LAUNCH(rmsnorm_backward_kernel, 148 * 4, 256, c.d * 4, b.res, (long long)c.d, cx.W(l, kFfnNorm), w.dh2,
                   (long long)c.d, w.dy, (long long)c.d, T, c.d, c.eps, w.dres, (long long)c.d, w.dres16, (long long)ld_d,
                   cx.G(l, kFfnNorm), inv_s);
@@ -324,33 +331,33 @@ inline void backward_chunk(Context& cx, int Bc, int S) {
         }
         gemm(cx, T, c.kvr, c.H * c.nope, {w.dkn16, ld_kn16, false}, {cx.S(l, kWuk), cx.SL(l, kWuk), false}, {w.dckv, c.kvr, kOutF32});
         gemm(cx, T, c.kvr, aw, {w.dv16, ld_v16, false}, {cx.S(l, kWuv), cx.SL(l, kWuv), false}, {w.dckv, c.kvr, kOutF32Acc});
-        MM_LAUNCH(rmsnorm_backward_kernel, 148 * 4, 256, c.kvr * 4, b.kvp, (long long)kvw, cx.W(l, kKvNorm), w.dckv,
+        const int qkv = c.qr + kvw, ld_qkv16 = cx.d16(qkv);
+        MM_LAUNCH(rmsnorm_backward_kernel, 148 * 4, 256, c.kvr * 4, b.kvp, (long long)qkv, cx.W(l, kKvNorm), w.dckv,
                   (long long)c.kvr, (const float*)nullptr, 0LL, T, c.kvr, c.eps, w.dkvraw, (long long)c.kvr, (__half*)nullptr,
                   0LL, cx.G(l, kKvNorm), inv_s);
-        const int ld_kvw16 = cx.d16(kvw);
         MM_LAUNCH(pack_dkv_kernel, blocks_for((long long)T * kvw, 256), 256, 0, w.dkvraw, w.drope2, T, c.kvr, c.rope, w.dkvp16,
-                  (long long)ld_kvw16);
+                  (long long)ld_qkv16);
         {
             GemmOutSpec o{cx.G(l, kWdkv), kvw, kOutF32Acc};
             o.alpha_ptr = inv_s;
-            gemm(cx, c.d, kvw, T, {b.h, ld_d, true}, {w.dkvp16, ld_kvw16, true}, o);
+            gemm(cx, c.d, kvw, T, {b.h, ld_d, true}, {w.dkvp16, ld_qkv16, true}, o);
         }
-        gemm(cx, T, c.d, kvw, {w.dkvp16, ld_kvw16, false}, {cx.S(l, kWdkv), cx.SL(l, kWdkv), false}, {w.dh, c.d, kOutF32});
         {
             GemmOutSpec o{cx.G(l, kWuq), c.H * qk, kOutF32Acc};
             o.alpha_ptr = inv_s;
             gemm(cx, c.qr, c.H * qk, T, {b.cq, ld_qr, true}, {w.dq16, ld_q16, true}, o);
         }
         gemm(cx, T, c.qr, c.H * qk, {w.dq16, ld_q16, false}, {cx.S(l, kWuq), cx.SL(l, kWuq), false}, {w.dcq, c.qr, kOutF32});
-        MM_LAUNCH(rmsnorm_backward_kernel, 148 * 4, 256, c.qr * 4, b.raw_cq, (long long)c.qr, cx.W(l, kQNorm), w.dcq,
-                  (long long)c.qr, (const float*)nullptr, 0LL, T, c.qr, c.eps, (float*)nullptr, 0LL, w.draw16, (long long)ld_qr,
-                  cx.G(l, kQNorm), inv_s);
+        MM_LAUNCH(rmsnorm_backward_kernel, 148 * 4, 256, c.qr * 4, b.raw_cq, (long long)qkv, cx.W(l, kQNorm), w.dcq,
+                  (long long)c.qr, (const float*)nullptr, 0LL, T, c.qr, c.eps, (float*)nullptr, 0LL, w.draw16,
+                  (long long)ld_qkv16, cx.G(l, kQNorm), inv_s);
         {
             GemmOutSpec o{cx.G(l, kWdq), c.qr, kOutF32Acc};
             o.alpha_ptr = inv_s;
-            gemm(cx, c.d, c.qr, T, {b.h, ld_d, true}, {w.draw16, ld_qr, true}, o);
+            gemm(cx, c.d, c.qr, T, {b.h, ld_d, true}, {w.draw16, ld_qkv16, true}, o);
         }
-        gemm(cx, T, c.d, c.qr, {w.draw16, ld_qr, false}, {cx.S(l, kWdq), cx.SL(l, kWdq), false}, {w.dh, c.d, kOutF32Acc});
+        // dh = [d raw_cq | d kv_pack] . [W_dq | W_dkv]^T, one product over K = qr + kvw
+        gemm(cx, T, c.d, qkv, {w.draw16, ld_qkv16, false}, {cx.prep[l].Wa, cx.prep[l].lda, false}, {w.dh, c.d, kOutF32});
         MM_LAUNCH(rmsnorm_backward_kernel, 148 * 4, 256, c.d * 4, b.x_in, (long long)c.d, cx.W(l, kAttnNorm), w.dh,
                   (long long)c.d, w.dres, (long long)c.d, T, c.d, c.eps, w.dy, (long long)c.d, (__half*)nullptr, 0LL,
                   cx.G(l, kAttnNorm), inv_s);

@@ -20,11 +20,25 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ part, int splits,
     out[r * ldc + c] += a * s;
 }
 
-inline void gemm(Context& cx, int M, int N, int K, Opnd A, Opnd B, const GemmOutSpec& o, bool bf16) {
+inline void gemm(Context& cx, int M, int N, int K, Opnd A, Opnd B, const GemmOutSpec& o_in, bool bf16) {
     if (M <= 0 || N <= 0 || K <= 0) return;
+    GemmOutSpec o = o_in;
+    if (o.residual) {
+        // out = alpha * A B + residual  ==  out := residual, then out += alpha * A B through the
+        // TMA reduce-add epilogue (the residual moves as one coalesced device copy).
+        if (o.kind != kOutF32) fail(MM_INVALID_ARGUMENT, "residual epilogue needs fp32 output");
+        MM_CUDA_CHECK(cudaMemcpy2DAsync(o.out, o.ldc * 4, o.residual, o.ldr * 4, static_cast<size_t>(N) * 4, M,
+                                        cudaMemcpyDeviceToDevice, cx.stream));
+        o.residual = nullptr;
+        o.kind = kOutF32Acc;
+    }
     const long long tiles_m = (M + kGemmBM - 1) / kGemmBM;
+    const int num_k_all = (K + kGemmBK - 1) / kGemmBK;
+    // products that will be split over K (few output tiles, long K) use the widest tile
+    const bool split_candidate = o.kind == kOutF32Acc && num_k_all >= 32 && N % 4 == 0 &&
+                                 tiles_m * ((N + 63) / 64) < sm_count();
     int BN = 64;
-    if (tiles_m * ((N + 255) / 256) >= 148 && N >= 256) BN = 256;
+    if (N >= 256 && (split_candidate || tiles_m * ((N + 255) / 256) >= 148)) BN = 256;
     else if (tiles_m * ((N + 127) / 128) >= 120 && N > 64) BN = 128;
     const CUtensorMap& ta = A.mn ? tensor_map(A.p, bf16, M, K, A.ld, 64, 64)
                                  : tensor_map(A.p, bf16, K, M, A.ld, 64, kGemmBM);

@@ -192,14 +192,41 @@ constexpr int kSampleThreads = 512;
 constexpr int kSampleBuckets = 2048;
 constexpr int kSampleCap = 1024;
 
+// Block-wide inclusive prefix sum of one double per thread (blockDim.x = kSampleThreads).
+__device__ __forceinline__ double block_scan_incl(double v, double* warp_tot) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const double n = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += n;
+    }
+    if (lane == 31) warp_tot[warp] = v;
+    __syncthreads();
+    if (warp == 0) {
+        double t = lane < (kSampleThreads >> 5) ? warp_tot[lane] : 0.0;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const double n = __shfl_up_sync(0xffffffffu, t, o);
+            if (lane >= o) t += n;
+        }
+        if (lane < (kSampleThreads >> 5)) warp_tot[lane] = t;
+    }
+    __syncthreads();
+    const double before = warp > 0 ? warp_tot[warp - 1] : 0.0;
+    __syncthreads();  // warp_tot is reused by the next scan
+    return v + before;
+}
+
 // One block per sequence row of logits [B][ld] (vocab V <= 65535). Greedy when
 // temperature == 0 (first index of the maximum). Otherwise the exact inverse CDF of
 // sample_token with top_p = 1: scores sorted descending (ties: lower id first), weights
-// w = exp(double(s - s0) / T), draw = u * sum(w), first index where the running
-// remainder reaches <= 0. The sorted order is found without a full sort: a histogram
-// of weight mass over the top bits of the order key locates the bucket holding the
-// crossing, then the next bits, until at most kSampleCap candidates remain, which are
-// sorted in shared memory and walked in order.
+// w = exp(double(s - s0) / T), draw = u * sum(w), first position whose running sum reaches
+// the draw. The sorted order is found without a full sort: in one pass every weight goes
+// into a histogram of 2048 buckets keyed by the top 11 bits of the order-preserving score
+// key; a block scan over the buckets (highest key first) locates the bucket holding the
+// crossing; the next key bits refine it while it holds more than kSampleCap scores; the
+// remaining candidates are sorted in shared memory (score desc, id asc) and a block scan
+// finds the crossing among them.
 // Rows with active[b] == 0 are skipped. out[b * out_stride] receives the token.
 __global__ void __launch_bounds__(kSampleThreads) sample_kernel(
     const float* __restrict__ logits, long long ld, int V, float temperature,
@@ -212,10 +239,10 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(
     __shared__ double cand_w[kSampleCap];
     __shared__ float red_f[32];
     __shared__ int red_i[32];
-    __shared__ double red_d[32];
-    __shared__ double s_draw, s_total;
+    __shared__ double warp_tot[32];
+    __shared__ double s_draw;
     __shared__ uint32_t s_prefix;
-    __shared__ int s_bits, s_ncand, s_done, s_choice;
+    __shared__ int s_bits, s_ncand, s_chosen, s_last;
 
     const int b = blockIdx.x;
     if (active && !active[b]) return;
@@ -252,32 +279,19 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(
         return;
     }
     const double invT = 1.0 / static_cast<double>(temperature);
-    // total mass
-    double tot = 0.0;
-    for (int j = threadIdx.x; j < V; j += blockDim.x)
-        tot += exp(static_cast<double>(row[j] - s0) * invT);
-    tot = warp_sum(tot);
-    if (lane == 0) red_d[warp] = tot;
-    __syncthreads();
     if (threadIdx.x == 0) {
-        double s = 0.0;
-        for (int w = 0; w < nw; ++w) s += red_d[w];
-        s_total = s;
-        const int k = (draw_index ? draw_index[b] : 0) + draw_offset;
-        s_draw = static_cast<double>(rng_uniform_at(seeds[b], static_cast<uint32_t>(k))) * s;
         s_prefix = 0;
         s_bits = 0;
-        s_done = 0;
-        s_choice = -1;
     }
     __syncthreads();
-    // Radix descent: 11 bits per level over the 32-bit key.
+    constexpr int PER = kSampleBuckets / kSampleThreads;  // buckets per thread in a scan
+    bool first = true;
     while (true) {
         const int bits = s_bits;
         const uint32_t prefix = s_prefix;
         const int width = min(11, 32 - bits);
         const int nb = 1 << width;
-        for (int i = threadIdx.x; i < nb; i += blockDim.x) { hist[i] = 0.0; hcount[i] = 0; }
+        for (int i = threadIdx.x; i < kSampleBuckets; i += blockDim.x) { hist[i] = 0.0; hcount[i] = 0; }
         __syncthreads();
         for (int j = threadIdx.x; j < V; j += blockDim.x) {
             const float v = row[j];
@@ -289,35 +303,67 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(
             }
         }
         __syncthreads();
-        if (threadIdx.x == 0) {
-            // walk buckets from the highest key down
-            double rem = s_draw;
-            int chosen = -1, last_nonempty = -1;
-            for (int i = nb - 1; i >= 0; --i) {
-                if (hcount[i] == 0) continue;
-                last_nonempty = i;
-                if (rem - hist[i] <= 0.0) { chosen = i; break; }
-                rem -= hist[i];
+        // Scan buckets from the highest key down: thread t owns descending positions
+        // [t*PER, t*PER + PER), position p <-> bucket nb - 1 - p (buckets >= nb are empty).
+        double mine = 0.0;
+#pragma unroll
+        for (int e = 0; e < PER; ++e) {
+            const int bk = nb - 1 - (threadIdx.x * PER + e);
+            if (bk >= 0) mine += hist[bk];
+        }
+        const double incl = block_scan_incl(mine, warp_tot);
+        if (first) {
+            // total mass = the last inclusive sum; draw = u * total
+            if (threadIdx.x == kSampleThreads - 1) {
+                const int k = (draw_index ? draw_index[b] : 0) + draw_offset;
+                s_draw = static_cast<double>(rng_uniform_at(seeds[b], static_cast<uint32_t>(k))) * incl;
             }
-            if (chosen < 0) { chosen = last_nonempty; rem = hist[chosen] * 2.0 + 1.0; }
-            s_draw = rem;
+            __syncthreads();
+            first = false;
+        }
+        if (threadIdx.x == 0) { s_chosen = -1; s_last = 0x7fffffff; }
+        __syncthreads();
+        const double draw = s_draw;
+        double run = incl - mine;  // mass of all higher buckets
+        int last_here = 0x7fffffff;
+        __syncthreads();  // every thread has read the draw before it is rewritten
+#pragma unroll
+        for (int e = 0; e < PER; ++e) {
+            const int bk = nb - 1 - (threadIdx.x * PER + e);
+            if (bk < 0 || hcount[bk] == 0) continue;
+            last_here = bk;
+            // the single bucket where the running mass from the top first reaches the draw
+            if (draw - run > 0.0 && draw - run - hist[bk] <= 0.0) {
+                s_chosen = bk;
+                s_draw = draw - run;
+            }
+            run += hist[bk];
+        }
+        if (last_here != 0x7fffffff) atomicMin(&s_last, last_here);
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            int chosen = s_chosen;
+            if (chosen < 0) {
+                chosen = s_last;  // draw beyond the rounding of the total: the last score
+                s_draw = 1e300;
+            }
             s_prefix = (prefix << width) | static_cast<uint32_t>(chosen);
             s_bits = bits + width;
             s_ncand = hcount[chosen];
-            s_done = (s_ncand <= kSampleCap || s_bits >= 32) ? 1 : 0;
         }
         __syncthreads();
-        if (s_done) break;
+        if (s_ncand <= kSampleCap || s_bits >= 32) break;
     }
     // gather candidates of the chosen key prefix
-    if (threadIdx.x == 0) s_ncand = 0;
-    __syncthreads();
     const int bits = s_bits;
     const uint32_t prefix = s_prefix;
+    __syncthreads();
+    if (threadIdx.x == 0) s_ncand = 0;
+    __syncthreads();
     for (int j = threadIdx.x; j < V; j += blockDim.x) {
         const float v = row[j];
         const uint32_t key = float_key(v);
-        if ((bits >= 32 ? key : (key >> (32 - bits))) == (bits >= 32 ? prefix : prefix)) {
+        if ((bits >= 32 ? key : (key >> (32 - bits))) == prefix) {
             const int slot = atomicAdd(&s_ncand, 1);
             if (slot < kSampleCap) {
                 cand_key[slot] = key;
@@ -328,20 +374,21 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(
     }
     __syncthreads();
     const int n = min(s_ncand, kSampleCap);
-    // bitonic sort of up to kSampleCap candidates: key descending, id ascending
-    for (int i = n + threadIdx.x; i < kSampleCap; i += blockDim.x) {
+    int np2 = 1;
+    while (np2 < n) np2 <<= 1;
+    // bitonic sort of the candidates (padded to a power of two): key descending, id ascending
+    for (int i = n + threadIdx.x; i < np2; i += blockDim.x) {
         cand_key[i] = 0;
         cand_id[i] = 0x7fffffff;
         cand_w[i] = 0.0;
     }
     __syncthreads();
-    for (int size = 2; size <= kSampleCap; size <<= 1) {
+    for (int size = 2; size <= np2; size <<= 1) {
         for (int stride = size >> 1; stride > 0; stride >>= 1) {
-            for (int i = threadIdx.x; i < kSampleCap; i += blockDim.x) {
+            for (int i = threadIdx.x; i < np2; i += blockDim.x) {
                 const int jx = i ^ stride;
                 if (jx > i) {
                     const bool desc = (i & size) == 0;
-                    // "before" = larger key, or equal key and smaller id
                     const bool i_before = cand_key[i] > cand_key[jx] ||
                                           (cand_key[i] == cand_key[jx] && cand_id[i] < cand_id[jx]);
                     if (desc != i_before) {
@@ -354,14 +401,31 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(
             __syncthreads();
         }
     }
-    if (threadIdx.x == 0) {
-        double rem = s_draw;
-        int pick = n > 0 ? cand_id[n - 1] : red_i[0];
-        for (int i = 0; i < n; ++i) {
-            rem -= cand_w[i];
-            if (rem <= 0.0) { pick = cand_id[i]; break; }
+    // first sorted candidate whose running sum reaches the remaining draw
+    const double rem = s_draw;
+    constexpr int CPT = kSampleCap / kSampleThreads;  // candidates per thread
+    double mine = 0.0;
+#pragma unroll
+    for (int e = 0; e < CPT; ++e) {
+        const int i = threadIdx.x * CPT + e;
+        if (i < n) mine += cand_w[i];
+    }
+    const double incl = block_scan_incl(mine, warp_tot);
+    if (threadIdx.x == 0) s_chosen = 0x7fffffff;
+    __syncthreads();
+    double run = incl - mine;
+#pragma unroll
+    for (int e = 0; e < CPT; ++e) {
+        const int i = threadIdx.x * CPT + e;
+        if (i < n) {
+            run += cand_w[i];
+            if (rem - run <= 0.0) { atomicMin(&s_chosen, i); break; }
         }
-        out[b * out_stride] = static_cast<uint16_t>(pick);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const int i = s_chosen == 0x7fffffff ? n - 1 : s_chosen;
+        out[b * out_stride] = static_cast<uint16_t>(n > 0 ? cand_id[i] : red_i[0]);
     }
 }
 

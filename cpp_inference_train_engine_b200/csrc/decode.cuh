@@ -46,7 +46,9 @@ inline void ensure_decode(Context& cx, int B, int Sc, int max_new) {
         d.out_tok = a.template take<uint16_t>(static_cast<long long>(B) * std::max(max_new, 1));
         // flash-decoding partials (max, sum, O[kv_rank]) per split and head
         d.part = a.template take<float>(B >= 296 ? 1 : static_cast<long long>(B) * kMaxDecodeSplits * c.H * (c.kvr + 2));
+        d.step = a.template take<int>(1);
     };
+    d.drop_graph();
     d.B = B;
     d.Sc = Sc;
     d.max_new = max_new;
@@ -152,9 +154,30 @@ inline void decode_step(Context& cx) {
 }
 
 inline void launch_sample(Context& cx, const float* logits, int B, float temperature, const uint64_t* seeds,
-                          const int* draw, int draw_offset, const int* active, uint16_t* out, long long out_stride) {
+                          const int* draw, int draw_offset, const int* active, uint16_t* out, long long out_stride,
+                          const int* counter = nullptr) {
     MM_LAUNCH_TIMED(kKSample, 4.0 * B * cx.c.V, sample_kernel, B, kSampleThreads, 0, logits, (long long)cx.c.V, cx.c.V,
-                    temperature, seeds, draw, draw_offset, active, out, out_stride);
+                    temperature, seeds, draw, draw_offset, counter, active, out, out_stride);
+}
+
+__global__ void counter_add_kernel(int* c, int v) { *c += v; }
+
+// out_tok column (*counter - 1) -> tok, for the token to append at this step.
+__global__ void column_gather_counter_kernel(const uint16_t* __restrict__ src, long long stride,
+                                             const int* __restrict__ counter, int B, uint16_t* __restrict__ dst) {
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b < B) dst[b] = src[b * stride + *counter - 1];
+}
+
+// One rollout decode step as a replayable unit: step += 1; append out_tok[:, step - 1] at
+// every row's position; logits; sample draw `step` into out_tok[:, step].
+inline void decode_sample_step(Context& cx, int completion, float temperature) {
+    DecodeState& d = cx.dec;
+    const int n = d.B;
+    MM_LAUNCH(counter_add_kernel, 1, 1, 0, d.step, 1);
+    MM_LAUNCH(column_gather_counter_kernel, blocks_for(n, 256), 256, 0, d.out_tok, (long long)completion, d.step, n, d.tok);
+    decode_step(cx);
+    launch_sample(cx, d.logits, n, temperature, d.seeds, nullptr, 0, nullptr, d.out_tok, completion, d.step);
 }
 
 } // namespace mm

@@ -183,8 +183,19 @@ struct DecodeState {
     int* draw;                // [B]
     uint16_t* out_tok;        // [B][max_new]
     float* part;              // [B][splits][H][kv_rank + 2] decode-attention partials
+    int* step;                // device step counter of the rollout loop
     int max_new = 0;
     Arena arena;
+    // one captured rollout decode step (decode_sample_step), valid for the buffers above
+    cudaGraphExec_t graph = nullptr;
+    long long graph_launches = 0;  // kernels per replay
+    int graph_completion = 0;
+    float graph_temperature = 0.f;
+    void drop_graph() {
+        if (graph) cudaGraphExecDestroy(graph);
+        graph = nullptr;
+    }
+    ~DecodeState() { drop_graph(); }
 };
 
 struct PrepLayer {

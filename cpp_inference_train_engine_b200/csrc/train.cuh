@@ -90,6 +90,16 @@ inline double adamw_update(Context& cx, float lr) {
     return norm;
 }
 
+// Rollout decode steps replay a captured CUDA graph unless MM_DECODE_GRAPH=0 (then every
+// kernel is launched and timed individually; same work, same results).
+inline bool decode_graphs_enabled() {
+    static int v = [] {
+        const char* e = std::getenv("MM_DECODE_GRAPH");
+        return (e && e[0] == '0') ? 0 : 1;
+    }();
+    return v != 0;
+}
+
 inline int chunk_tokens_default() {
     static int v = [] {
         const char* e = std::getenv("MM_CHUNK_TOKENS");
@@ -230,19 +240,56 @@ inline void rollout(Context& cx, const uint16_t* prompts, int n, int P, int comp
         PhaseTimer t(cx, kPhPrefill);
         prefill_rows(cx, d_prompts, n, P, chunk_tokens_default());
     }
-    for (int k = 0; k < length; ++k) {
-        if (k > 0) {
-            PhaseTimer t(cx, kPhDecode);
-            MM_LAUNCH(column_gather_kernel, blocks_for(n, 256), 256, 0, d.out_tok, (long long)completion, k - 1, n, d.tok);
-            cx.dec_len = P + k - 1;  // cache entries before this step's write
-            decode_step(cx);
-        }
+    MM_CUDA_CHECK(cudaMemsetAsync(d.step, 0, sizeof(int), cx.stream));
+    {
         PhaseTimer t(cx, kPhSample);
-        launch_sample(cx, d.logits, n, temperature, d.seeds, nullptr, k, nullptr, d.out_tok + k, completion);
+        launch_sample(cx, d.logits, n, temperature, d.seeds, nullptr, 0, nullptr, d.out_tok, completion, d.step);
+    }
+    // Steps 1..length-1: the first runs eagerly (it also initialises every kernel and
+    // tensor map it uses); the rest replay one captured graph of a whole step, whose
+    // arguments are all constant because the step index lives in device memory.
+    for (int k = 1; k < length; ++k) {
+        cx.dec_len = P + k - 1;  // cache entries before this step's write
+        PhaseTimer t(cx, kPhDecode);
+        if (k == 1 || !decode_graphs_enabled()) {
+            decode_sample_step(cx, completion, temperature);
+            continue;
+        }
+        if (!d.graph || d.graph_completion != completion || d.graph_temperature != temperature) {
+            d.drop_graph();
+            const bool prof = cx.profiling;
+            const long long before = cx.launches;
+            cx.profiling = false;
+            cudaGraph_t g = nullptr;
+            MM_CUDA_CHECK(cudaStreamBeginCapture(cx.stream, cudaStreamCaptureModeThreadLocal));
+            try {
+                decode_sample_step(cx, completion, temperature);
+            } catch (...) {
+                cudaStreamEndCapture(cx.stream, &g);  // leave the stream usable
+                if (g) cudaGraphDestroy(g);
+                cx.profiling = prof;
+                throw;
+            }
+            const cudaError_t e = cudaStreamEndCapture(cx.stream, &g);
+            cx.profiling = prof;
+            if (e != cudaSuccess || !g) fail(MM_GPU_ERROR, std::string("decode graph capture: ") + cudaGetErrorString(e));
+            const cudaError_t ie = cudaGraphInstantiate(&d.graph, g, 0);
+            cudaGraphDestroy(g);
+            if (ie != cudaSuccess) fail(MM_GPU_ERROR, std::string("decode graph instantiate: ") + cudaGetErrorString(ie));
+            d.graph_completion = completion;
+            d.graph_temperature = temperature;
+            d.graph_launches = cx.launches - before;
+            cx.launches = before;
+        }
+        MM_CUDA_CHECK(cudaGraphLaunch(d.graph, cx.stream));
+        cx.launches += d.graph_launches;
     }
     std::vector<uint16_t> toks(static_cast<size_t>(n) * completion);
     MM_CUDA_CHECK(cudaMemcpyAsync(toks.data(), d.out_tok, toks.size() * 2, cudaMemcpyDeviceToHost, cx.stream));
     MM_CUDA_CHECK(cudaStreamSynchronize(cx.stream));
+    // The graph holds raw pointers (split-K staging, derived weights) that later calls may
+    // reallocate, so it lives for one rollout only.
+    d.drop_graph();
     check_device(cx, "rollout");
     for (int i = 0; i < n; ++i) {
         int len = length;

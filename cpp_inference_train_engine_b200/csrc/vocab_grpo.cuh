@@ -192,55 +192,85 @@ constexpr int kSampleThreads = 512;
 constexpr int kSampleBuckets = 2048;
 constexpr int kSampleCap = 1024;
 
-// Block-wide inclusive prefix sum of one double per thread (blockDim.x = kSampleThreads).
-__device__ __forceinline__ double block_scan_incl(double v, double* warp_tot) {
+// Block-wide inclusive prefix sum of one u64 per thread (blockDim.x = kSampleThreads).
+__device__ __forceinline__ unsigned long long block_scan_incl(unsigned long long v, unsigned long long* warp_tot) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-        const double n = __shfl_up_sync(0xffffffffu, v, o);
+        const unsigned long long n = __shfl_up_sync(0xffffffffu, v, o);
         if (lane >= o) v += n;
     }
     if (lane == 31) warp_tot[warp] = v;
     __syncthreads();
     if (warp == 0) {
-        double t = lane < (kSampleThreads >> 5) ? warp_tot[lane] : 0.0;
+        unsigned long long t = lane < (kSampleThreads >> 5) ? warp_tot[lane] : 0ull;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
-            const double n = __shfl_up_sync(0xffffffffu, t, o);
+            const unsigned long long n = __shfl_up_sync(0xffffffffu, t, o);
             if (lane >= o) t += n;
         }
         if (lane < (kSampleThreads >> 5)) warp_tot[lane] = t;
     }
     __syncthreads();
-    const double before = warp > 0 ? warp_tot[warp - 1] : 0.0;
+    const unsigned long long before = warp > 0 ? warp_tot[warp - 1] : 0ull;
     __syncthreads();  // warp_tot is reused by the next scan
     return v + before;
 }
 
+// Sampling weight in 2^-48 fixed point: w = exp(double(s - s0) / T) <= 1 (s0 is the row
+// maximum), so a row of at most 65535 weights sums below 2^64 and every partial sum is
+// exact and independent of the order of addition.
+__device__ __forceinline__ unsigned long long sample_weight_q(float s, float s0, double invT) {
+    return __double2ull_rn(exp(static_cast<double>(s - s0) * invT) * 281474976710656.0);
+}
+
+// Adds q to hist[bucket] and 1 to hcount[bucket], one atomic per distinct bucket of the
+// warp (the rows' scores crowd into few buckets, so per-lane atomics would serialise).
+__device__ __forceinline__ void warp_bucket_add(unsigned long long* hist, int* hcount, int bucket,
+                                                unsigned long long q, bool valid) {
+    const unsigned active = __ballot_sync(0xffffffffu, valid);
+    if (!valid) return;
+    const unsigned peers = __match_any_sync(active, bucket);
+    unsigned long long sum = 0;
+    for (unsigned m = peers; m; m &= m - 1) sum += __shfl_sync(peers, q, __ffs(m) - 1);
+    if ((threadIdx.x & 31) == __ffs(peers) - 1) {
+        atomicAdd(&hist[bucket], sum);
+        atomicAdd(&hcount[bucket], __popc(peers));
+    }
+}
+
 // One block per sequence row of logits [B][ld] (vocab V <= 65535). Greedy when
-// temperature == 0 (first index of the maximum). Otherwise the exact inverse CDF of
+// temperature == 0 (first index of the maximum). Otherwise the inverse CDF of
 // sample_token with top_p = 1: scores sorted descending (ties: lower id first), weights
-// w = exp(double(s - s0) / T), draw = u * sum(w), first position whose running sum reaches
-// the draw. The sorted order is found without a full sort: in one pass every weight goes
-// into a histogram of 2048 buckets keyed by the top 11 bits of the order-preserving score
-// key; a block scan over the buckets (highest key first) locates the bucket holding the
-// crossing; the next key bits refine it while it holds more than kSampleCap scores; the
-// remaining candidates are sorted in shared memory (score desc, id asc) and a block scan
-// finds the crossing among them.
-// Rows with active[b] == 0 are skipped. out[b * out_stride] receives the token.
+// w = exp(double(s - s0) / T), draw = u * sum(w) with the reference's 24-bit uniform u,
+// first position whose running sum reaches the draw. Weights are summed in exact 2^-48
+// fixed point (the sampled token equals the reference's except when the draw falls within
+// ~1e-10 of a CDF boundary). The sorted order is found without a full sort: one pass
+// histograms the weights over 2048 buckets keyed by the top 11 bits of the
+// order-preserving score key; a block scan over the buckets (highest key first) locates
+// the bucket holding the crossing; the next key bits refine it while it holds more than
+// kSampleCap scores; the remaining candidates are sorted in shared memory (score desc, id
+// asc) and a block scan finds the crossing among them.
+// Rows with active[b] == 0 are skipped. The draw index of row b is draw_index[b] (or 0) +
+// draw_offset + *counter (when given); the token goes to out[b * out_stride + *counter]
+// (counter 0 when null), so a replayed graph can advance both through device memory.
 __global__ void __launch_bounds__(kSampleThreads) sample_kernel(
     const float* __restrict__ logits, long long ld, int V, float temperature,
     const uint64_t* __restrict__ seeds, const int* __restrict__ draw_index, int draw_offset,
-    const int* __restrict__ active, uint16_t* __restrict__ out, long long out_stride) {
-    __shared__ double hist[kSampleBuckets];
+    const int* __restrict__ counter, const int* __restrict__ active, uint16_t* __restrict__ out,
+    long long out_stride) {
+    const int step = counter ? *counter : 0;
+    out += step;
+    draw_offset += step;
+    __shared__ unsigned long long hist[kSampleBuckets];
     __shared__ int hcount[kSampleBuckets];
     __shared__ uint32_t cand_key[kSampleCap];
     __shared__ int cand_id[kSampleCap];
-    __shared__ double cand_w[kSampleCap];
+    __shared__ unsigned long long cand_w[kSampleCap];
     __shared__ float red_f[32];
     __shared__ int red_i[32];
-    __shared__ double warp_tot[32];
-    __shared__ double s_draw;
+    __shared__ unsigned long long warp_tot[32];
+    __shared__ unsigned long long s_draw;
     __shared__ uint32_t s_prefix;
     __shared__ int s_bits, s_ncand, s_chosen, s_last;
 
@@ -271,6 +301,8 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(
             if (red_f[w] > bm || (red_f[w] == bm && red_i[w] < bi)) { bm = red_f[w]; bi = red_i[w]; }
         red_f[0] = bm;
         red_i[0] = bi;
+        s_prefix = 0;
+        s_bits = 0;
     }
     __syncthreads();
     const float s0 = red_f[0];
@@ -279,11 +311,6 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(
         return;
     }
     const double invT = 1.0 / static_cast<double>(temperature);
-    if (threadIdx.x == 0) {
-        s_prefix = 0;
-        s_bits = 0;
-    }
-    __syncthreads();
     constexpr int PER = kSampleBuckets / kSampleThreads;  // buckets per thread in a scan
     bool first = true;
     while (true) {
@@ -291,40 +318,45 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(
         const uint32_t prefix = s_prefix;
         const int width = min(11, 32 - bits);
         const int nb = 1 << width;
-        for (int i = threadIdx.x; i < kSampleBuckets; i += blockDim.x) { hist[i] = 0.0; hcount[i] = 0; }
+        for (int i = threadIdx.x; i < kSampleBuckets; i += blockDim.x) { hist[i] = 0ull; hcount[i] = 0; }
         __syncthreads();
-        for (int j = threadIdx.x; j < V; j += blockDim.x) {
-            const float v = row[j];
+        for (int j0 = 0; j0 < V; j0 += blockDim.x) {
+            const int j = j0 + threadIdx.x;
+            bool valid = j < V;
+            const float v = valid ? row[j] : 0.f;
             const uint32_t key = float_key(v);
-            if (bits == 0 || (key >> (32 - bits)) == prefix) {
-                const int bk = static_cast<int>((key >> (32 - bits - width)) & (nb - 1));
-                atomicAdd(&hist[bk], exp(static_cast<double>(v - s0) * invT));
-                atomicAdd(&hcount[bk], 1);
-            }
+            if (bits > 0) valid = valid && (key >> (32 - bits)) == prefix;
+            const int bk = static_cast<int>((key >> (32 - bits - width)) & (nb - 1));
+            const unsigned long long q = valid ? sample_weight_q(v, s0, invT) : 0ull;
+            warp_bucket_add(hist, hcount, bk, q, valid);
         }
         __syncthreads();
         // Scan buckets from the highest key down: thread t owns descending positions
         // [t*PER, t*PER + PER), position p <-> bucket nb - 1 - p (buckets >= nb are empty).
-        double mine = 0.0;
+        unsigned long long mine = 0;
 #pragma unroll
         for (int e = 0; e < PER; ++e) {
             const int bk = nb - 1 - (threadIdx.x * PER + e);
             if (bk >= 0) mine += hist[bk];
         }
-        const double incl = block_scan_incl(mine, warp_tot);
+        const unsigned long long incl = block_scan_incl(mine, warp_tot);
         if (first) {
-            // total mass = the last inclusive sum; draw = u * total
+            // total = the last inclusive sum; draw = u * total with u = (x + 1/2) / 2^24,
+            // i.e. ((2x + 1) * total) >> 25 computed exactly in 128 bits
             if (threadIdx.x == kSampleThreads - 1) {
                 const int k = (draw_index ? draw_index[b] : 0) + draw_offset;
-                s_draw = static_cast<double>(rng_uniform_at(seeds[b], static_cast<uint32_t>(k))) * incl;
+                const uint64_t x = splitmix_mix(seeds[b] + static_cast<uint64_t>(k + 1) * 0x9e3779b97f4a7c15ull) >> 40;
+                const unsigned long long f = 2ull * x + 1ull;
+                const unsigned long long lo = f * incl, hi = __umul64hi(f, incl);
+                s_draw = (hi << 39) | (lo >> 25);
             }
             __syncthreads();
             first = false;
         }
         if (threadIdx.x == 0) { s_chosen = -1; s_last = 0x7fffffff; }
         __syncthreads();
-        const double draw = s_draw;
-        double run = incl - mine;  // mass of all higher buckets
+        const unsigned long long draw = s_draw;
+        unsigned long long run = incl - mine;  // mass of all higher buckets
         int last_here = 0x7fffffff;
         __syncthreads();  // every thread has read the draw before it is rewritten
 #pragma unroll
@@ -333,7 +365,7 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(
             if (bk < 0 || hcount[bk] == 0) continue;
             last_here = bk;
             // the single bucket where the running mass from the top first reaches the draw
-            if (draw - run > 0.0 && draw - run - hist[bk] <= 0.0) {
+            if (run < draw && run + hist[bk] >= draw) {
                 s_chosen = bk;
                 s_draw = draw - run;
             }
@@ -344,8 +376,8 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(
         if (threadIdx.x == 0) {
             int chosen = s_chosen;
             if (chosen < 0) {
-                chosen = s_last;  // draw beyond the rounding of the total: the last score
-                s_draw = 1e300;
+                chosen = s_last;  // only when every weight rounded to zero below the draw
+                s_draw = ~0ull;
             }
             s_prefix = (prefix << width) | static_cast<uint32_t>(chosen);
             s_bits = bits + width;
@@ -368,7 +400,7 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(
             if (slot < kSampleCap) {
                 cand_key[slot] = key;
                 cand_id[slot] = j;
-                cand_w[slot] = exp(static_cast<double>(v - s0) * invT);
+                cand_w[slot] = sample_weight_q(v, s0, invT);
             }
         }
     }
@@ -380,7 +412,7 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(
     for (int i = n + threadIdx.x; i < np2; i += blockDim.x) {
         cand_key[i] = 0;
         cand_id[i] = 0x7fffffff;
-        cand_w[i] = 0.0;
+        cand_w[i] = 0ull;
     }
     __syncthreads();
     for (int size = 2; size <= np2; size <<= 1) {
@@ -394,7 +426,7 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(
                     if (desc != i_before) {
                         const uint32_t tk = cand_key[i]; cand_key[i] = cand_key[jx]; cand_key[jx] = tk;
                         const int ti = cand_id[i]; cand_id[i] = cand_id[jx]; cand_id[jx] = ti;
-                        const double tw = cand_w[i]; cand_w[i] = cand_w[jx]; cand_w[jx] = tw;
+                        const unsigned long long tw = cand_w[i]; cand_w[i] = cand_w[jx]; cand_w[jx] = tw;
                     }
                 }
             }
@@ -402,24 +434,24 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(
         }
     }
     // first sorted candidate whose running sum reaches the remaining draw
-    const double rem = s_draw;
+    const unsigned long long rem = s_draw;
     constexpr int CPT = kSampleCap / kSampleThreads;  // candidates per thread
-    double mine = 0.0;
+    unsigned long long mine = 0;
 #pragma unroll
     for (int e = 0; e < CPT; ++e) {
         const int i = threadIdx.x * CPT + e;
         if (i < n) mine += cand_w[i];
     }
-    const double incl = block_scan_incl(mine, warp_tot);
+    const unsigned long long incl = block_scan_incl(mine, warp_tot);
     if (threadIdx.x == 0) s_chosen = 0x7fffffff;
     __syncthreads();
-    double run = incl - mine;
+    unsigned long long run = incl - mine;
 #pragma unroll
     for (int e = 0; e < CPT; ++e) {
         const int i = threadIdx.x * CPT + e;
         if (i < n) {
             run += cand_w[i];
-            if (rem - run <= 0.0) { atomicMin(&s_chosen, i); break; }
+            if (run >= rem) { atomicMin(&s_chosen, i); break; }
         }
     }
     __syncthreads();

@@ -246,6 +246,8 @@ def main():
         start = torch.cuda.Event(enable_timing=True)
         end = torch.cuda.Event(enable_timing=True)
         barrier()
+        # A profiler started with --profile-from-start off sees only the timed steps.
+        torch.cuda.profiler.start()
         start.record(stream)
         for i in range(args.steps):
             r, out = one_step(args.warmup + i)
@@ -258,6 +260,7 @@ def main():
             d2h += r["tokens"].nbytes + r["lengths"].nbytes + r["old_lp"].nbytes
         end.record(stream)
         barrier()
+        torch.cuda.profiler.stop()
     e2e_ms = start.elapsed_time(end)
     if args.gemm_shapes and rank == 0:
         for name, ctx in (("policy", pol), ("reference", refm)):

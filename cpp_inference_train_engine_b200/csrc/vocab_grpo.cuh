@@ -218,14 +218,24 @@ __device__ __forceinline__ unsigned long long block_scan_incl(unsigned long long
 }
 
 // Sampling weight in 2^-48 fixed point: w = exp(double(s - s0) / T) <= 1 (s0 is the row
-// maximum), so a row of at most 65535 weights sums below 2^64 and every partial sum is
-// exact and independent of the order of addition.
-__device__ __forceinline__ unsigned long long sample_weight_q(float s, float s0, double invT) {
-    return __double2ull_rn(exp(static_cast<double>(s - s0) * invT) * 281474976710656.0);
+// maximum; the float difference and the double division are those of sample_token,
+// inference.cpp:410-411), so a row of at most 65535 weights sums below 2^64 and every
+// partial sum is exact and independent of the order of addition.
+__device__ __forceinline__ unsigned long long sample_weight_q(float s, float s0, double T) {
+    return __double2ull_rn(exp(static_cast<double>(__fsub_rn(s, s0)) / T) * 281474976710656.0);
+}
+
+// The draw u * total in the same fixed point, with the reference's 24-bit uniform
+// u = (x + 1/2) / 2^24 of draw k (rng.hpp:10-18): ((2x + 1) * total) >> 25, exact in 128 bits.
+__device__ __forceinline__ unsigned long long sample_draw(uint64_t seed, int k, unsigned long long total) {
+    const uint64_t x = splitmix_mix(seed + static_cast<uint64_t>(k + 1) * 0x9e3779b97f4a7c15ull) >> 40;
+    const unsigned long long f = 2ull * x + 1ull;
+    const unsigned long long lo = f * total, hi = __umul64hi(f, total);
+    return (hi << 39) | (lo >> 25);
 }
 
 // Adds q to hist[bucket] and 1 to hcount[bucket], one atomic per distinct bucket of the
-// warp (the rows' scores crowd into few buckets, so per-lane atomics would serialise).
+// warp (scores crowd into few key buckets, so per-lane atomics would serialise).
 __device__ __forceinline__ void warp_bucket_add(unsigned long long* hist, int* hcount, int bucket,
                                                 unsigned long long q, bool valid) {
     const unsigned active = __ballot_sync(0xffffffffu, valid);
@@ -239,180 +249,91 @@ __device__ __forceinline__ void warp_bucket_add(unsigned long long* hist, int* h
     }
 }
 
-// One block per sequence row of logits [B][ld] (vocab V <= 65535). Greedy when
-// temperature == 0 (first index of the maximum). Otherwise the inverse CDF of
-// sample_token with top_p = 1: scores sorted descending (ties: lower id first), weights
-// w = exp(double(s - s0) / T), draw = u * sum(w) with the reference's 24-bit uniform u,
-// first position whose running sum reaches the draw. Weights are summed in exact 2^-48
-// fixed point (the sampled token equals the reference's except when the draw falls within
-// ~1e-10 of a CDF boundary). The sorted order is found without a full sort: one pass
-// histograms the weights over 2048 buckets keyed by the top 11 bits of the
-// order-preserving score key; a block scan over the buckets (highest key first) locates
-// the bucket holding the crossing; the next key bits refine it while it holds more than
-// kSampleCap scores; the remaining candidates are sorted in shared memory (score desc, id
-// asc) and a block scan finds the crossing among them.
-// Rows with active[b] == 0 are skipped. The draw index of row b is draw_index[b] (or 0) +
-// draw_offset + *counter (when given); the token goes to out[b * out_stride + *counter]
-// (counter 0 when null), so a replayed graph can advance both through device memory.
-__global__ void __launch_bounds__(kSampleThreads) sample_kernel(
-    const float* __restrict__ logits, long long ld, int V, float temperature,
-    const uint64_t* __restrict__ seeds, const int* __restrict__ draw_index, int draw_offset,
-    const int* __restrict__ counter, const int* __restrict__ active, uint16_t* __restrict__ out,
-    long long out_stride) {
-    const int step = counter ? *counter : 0;
-    out += step;
-    draw_offset += step;
-    __shared__ unsigned long long hist[kSampleBuckets];
-    __shared__ int hcount[kSampleBuckets];
-    __shared__ uint32_t cand_key[kSampleCap];
-    __shared__ int cand_id[kSampleCap];
-    __shared__ unsigned long long cand_w[kSampleCap];
-    __shared__ float red_f[32];
-    __shared__ int red_i[32];
-    __shared__ unsigned long long warp_tot[32];
-    __shared__ unsigned long long s_draw;
-    __shared__ uint32_t s_prefix;
-    __shared__ int s_bits, s_ncand, s_chosen, s_last;
+struct SampleShared {
+    unsigned long long hist[kSampleBuckets];
+    int hcount[kSampleBuckets];
+    uint32_t cand_key[kSampleCap];
+    int cand_id[kSampleCap];
+    unsigned long long cand_w[kSampleCap];
+    float red_f[32], red_g[32];
+    int red_i[32];
+    unsigned long long warp_tot[32];
+    unsigned long long s_draw;
+    uint32_t s_prefix;
+    int s_bits, s_ncand, s_chosen, s_last;
+};
 
-    const int b = blockIdx.x;
-    if (active && !active[b]) return;
-    const float* row = logits + b * ld;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+// Scan of the bucket masses from the highest bucket (highest scores) down. With `first`,
+// the draw is derived from the row total. Leaves in S.s_chosen the bucket where the running
+// mass first reaches the draw and in S.s_draw the part of the draw left inside it.
+__device__ void sample_locate(SampleShared& S, int nb, bool first, uint64_t seed, int k) {
+    constexpr int PER = kSampleBuckets / kSampleThreads;  // buckets per thread
+    // thread t owns descending positions [t*PER, t*PER + PER); position p <-> bucket nb-1-p
+    unsigned long long mine = 0;
+#pragma unroll
+    for (int e = 0; e < PER; ++e) {
+        const int bk = nb - 1 - (static_cast<int>(threadIdx.x) * PER + e);
+        if (bk >= 0) mine += S.hist[bk];
+    }
+    const unsigned long long incl = block_scan_incl(mine, S.warp_tot);
+    if (first) {
+        if (threadIdx.x == kSampleThreads - 1) S.s_draw = sample_draw(seed, k, incl);
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) { S.s_chosen = -1; S.s_last = 0x7fffffff; }
+    __syncthreads();
+    const unsigned long long draw = S.s_draw;
+    unsigned long long run = incl - mine;  // mass of all higher buckets
+    int last_here = 0x7fffffff;
+    __syncthreads();  // every thread has read the draw before it is rewritten
+#pragma unroll
+    for (int e = 0; e < PER; ++e) {
+        const int bk = nb - 1 - (static_cast<int>(threadIdx.x) * PER + e);
+        if (bk < 0 || S.hcount[bk] == 0) continue;
+        last_here = bk;
+        if (run < draw && run + S.hist[bk] >= draw) {
+            S.s_chosen = bk;
+            S.s_draw = draw - run;
+        }
+        run += S.hist[bk];
+    }
+    if (last_here != 0x7fffffff) atomicMin(&S.s_last, last_here);
+    __syncthreads();
+    if (threadIdx.x == 0 && S.s_chosen < 0) {
+        S.s_chosen = S.s_last;  // only when every weight rounded to zero below the draw
+        S.s_draw = ~0ull;
+    }
+    __syncthreads();
+}
 
-    // max score and its first index
-    float mx = -INFINITY;
-    int mi = 0x7fffffff;
-    for (int j = threadIdx.x; j < V; j += blockDim.x) {
-        const float v = row[j];
-        if (v > mx) { mx = v; mi = j; }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, mx, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, mi, o);
-        if (ov > mx || (ov == mx && oi < mi)) { mx = ov; mi = oi; }
-    }
-    if (lane == 0) { red_f[warp] = mx; red_i[warp] = mi; }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        float bm = red_f[0];
-        int bi = red_i[0];
-        for (int w = 1; w < nw; ++w)
-            if (red_f[w] > bm || (red_f[w] == bm && red_i[w] < bi)) { bm = red_f[w]; bi = red_i[w]; }
-        red_f[0] = bm;
-        red_i[0] = bi;
-        s_prefix = 0;
-        s_bits = 0;
-    }
-    __syncthreads();
-    const float s0 = red_f[0];
-    if (temperature == 0.f) {
-        if (threadIdx.x == 0) out[b * out_stride] = static_cast<uint16_t>(red_i[0]);
-        return;
-    }
-    const double invT = 1.0 / static_cast<double>(temperature);
-    constexpr int PER = kSampleBuckets / kSampleThreads;  // buckets per thread in a scan
-    bool first = true;
-    while (true) {
-        const int bits = s_bits;
-        const uint32_t prefix = s_prefix;
-        const int width = min(11, 32 - bits);
-        const int nb = 1 << width;
-        for (int i = threadIdx.x; i < kSampleBuckets; i += blockDim.x) { hist[i] = 0ull; hcount[i] = 0; }
-        __syncthreads();
-        for (int j0 = 0; j0 < V; j0 += blockDim.x) {
-            const int j = j0 + threadIdx.x;
-            bool valid = j < V;
-            const float v = valid ? row[j] : 0.f;
-            const uint32_t key = float_key(v);
-            if (bits > 0) valid = valid && (key >> (32 - bits)) == prefix;
-            const int bk = static_cast<int>((key >> (32 - bits - width)) & (nb - 1));
-            const unsigned long long q = valid ? sample_weight_q(v, s0, invT) : 0ull;
-            warp_bucket_add(hist, hcount, bk, q, valid);
-        }
-        __syncthreads();
-        // Scan buckets from the highest key down: thread t owns descending positions
-        // [t*PER, t*PER + PER), position p <-> bucket nb - 1 - p (buckets >= nb are empty).
-        unsigned long long mine = 0;
-#pragma unroll
-        for (int e = 0; e < PER; ++e) {
-            const int bk = nb - 1 - (threadIdx.x * PER + e);
-            if (bk >= 0) mine += hist[bk];
-        }
-        const unsigned long long incl = block_scan_incl(mine, warp_tot);
-        if (first) {
-            // total = the last inclusive sum; draw = u * total with u = (x + 1/2) / 2^24,
-            // i.e. ((2x + 1) * total) >> 25 computed exactly in 128 bits
-            if (threadIdx.x == kSampleThreads - 1) {
-                const int k = (draw_index ? draw_index[b] : 0) + draw_offset;
-                const uint64_t x = splitmix_mix(seeds[b] + static_cast<uint64_t>(k + 1) * 0x9e3779b97f4a7c15ull) >> 40;
-                const unsigned long long f = 2ull * x + 1ull;
-                const unsigned long long lo = f * incl, hi = __umul64hi(f, incl);
-                s_draw = (hi << 39) | (lo >> 25);
-            }
-            __syncthreads();
-            first = false;
-        }
-        if (threadIdx.x == 0) { s_chosen = -1; s_last = 0x7fffffff; }
-        __syncthreads();
-        const unsigned long long draw = s_draw;
-        unsigned long long run = incl - mine;  // mass of all higher buckets
-        int last_here = 0x7fffffff;
-        __syncthreads();  // every thread has read the draw before it is rewritten
-#pragma unroll
-        for (int e = 0; e < PER; ++e) {
-            const int bk = nb - 1 - (threadIdx.x * PER + e);
-            if (bk < 0 || hcount[bk] == 0) continue;
-            last_here = bk;
-            // the single bucket where the running mass from the top first reaches the draw
-            if (run < draw && run + hist[bk] >= draw) {
-                s_chosen = bk;
-                s_draw = draw - run;
-            }
-            run += hist[bk];
-        }
-        if (last_here != 0x7fffffff) atomicMin(&s_last, last_here);
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            int chosen = s_chosen;
-            if (chosen < 0) {
-                chosen = s_last;  // only when every weight rounded to zero below the draw
-                s_draw = ~0ull;
-            }
-            s_prefix = (prefix << width) | static_cast<uint32_t>(chosen);
-            s_bits = bits + width;
-            s_ncand = hcount[chosen];
-        }
-        __syncthreads();
-        if (s_ncand <= kSampleCap || s_bits >= 32) break;
-    }
-    // gather candidates of the chosen key prefix
-    const int bits = s_bits;
-    const uint32_t prefix = s_prefix;
-    __syncthreads();
-    if (threadIdx.x == 0) s_ncand = 0;
+// Gathers the scores selected by `in_set` (at most kSampleCap of them), sorts them (score
+// descending, id ascending) and returns the id where their running mass reaches S.s_draw
+// (the last one when none does; `none` when the set is empty).
+template <class Pred>
+__device__ int sample_pick(SampleShared& S, const float* __restrict__ row, int V, float s0, double T, Pred in_set,
+                           int none) {
+    if (threadIdx.x == 0) S.s_ncand = 0;
     __syncthreads();
     for (int j = threadIdx.x; j < V; j += blockDim.x) {
         const float v = row[j];
-        const uint32_t key = float_key(v);
-        if ((bits >= 32 ? key : (key >> (32 - bits))) == prefix) {
-            const int slot = atomicAdd(&s_ncand, 1);
+        if (in_set(v)) {
+            const int slot = atomicAdd(&S.s_ncand, 1);
             if (slot < kSampleCap) {
-                cand_key[slot] = key;
-                cand_id[slot] = j;
-                cand_w[slot] = sample_weight_q(v, s0, invT);
+                S.cand_key[slot] = float_key(v);
+                S.cand_id[slot] = j;
+                S.cand_w[slot] = sample_weight_q(v, s0, T);
             }
         }
     }
     __syncthreads();
-    const int n = min(s_ncand, kSampleCap);
+    const int n = min(S.s_ncand, kSampleCap);
     int np2 = 1;
     while (np2 < n) np2 <<= 1;
     // bitonic sort of the candidates (padded to a power of two): key descending, id ascending
     for (int i = n + threadIdx.x; i < np2; i += blockDim.x) {
-        cand_key[i] = 0;
-        cand_id[i] = 0x7fffffff;
-        cand_w[i] = 0ull;
+        S.cand_key[i] = 0;
+        S.cand_id[i] = 0x7fffffff;
+        S.cand_w[i] = 0ull;
     }
     __syncthreads();
     for (int size = 2; size <= np2; size <<= 1) {
@@ -421,12 +342,12 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(
                 const int jx = i ^ stride;
                 if (jx > i) {
                     const bool desc = (i & size) == 0;
-                    const bool i_before = cand_key[i] > cand_key[jx] ||
-                                          (cand_key[i] == cand_key[jx] && cand_id[i] < cand_id[jx]);
+                    const bool i_before = S.cand_key[i] > S.cand_key[jx] ||
+                                          (S.cand_key[i] == S.cand_key[jx] && S.cand_id[i] < S.cand_id[jx]);
                     if (desc != i_before) {
-                        const uint32_t tk = cand_key[i]; cand_key[i] = cand_key[jx]; cand_key[jx] = tk;
-                        const int ti = cand_id[i]; cand_id[i] = cand_id[jx]; cand_id[jx] = ti;
-                        const unsigned long long tw = cand_w[i]; cand_w[i] = cand_w[jx]; cand_w[jx] = tw;
+                        const uint32_t tk = S.cand_key[i]; S.cand_key[i] = S.cand_key[jx]; S.cand_key[jx] = tk;
+                        const int ti = S.cand_id[i]; S.cand_id[i] = S.cand_id[jx]; S.cand_id[jx] = ti;
+                        const unsigned long long tw = S.cand_w[i]; S.cand_w[i] = S.cand_w[jx]; S.cand_w[jx] = tw;
                     }
                 }
             }
@@ -434,31 +355,199 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(
         }
     }
     // first sorted candidate whose running sum reaches the remaining draw
-    const unsigned long long rem = s_draw;
+    const unsigned long long rem = S.s_draw;
     constexpr int CPT = kSampleCap / kSampleThreads;  // candidates per thread
     unsigned long long mine = 0;
 #pragma unroll
     for (int e = 0; e < CPT; ++e) {
         const int i = threadIdx.x * CPT + e;
-        if (i < n) mine += cand_w[i];
+        if (i < n) mine += S.cand_w[i];
     }
-    const unsigned long long incl = block_scan_incl(mine, warp_tot);
-    if (threadIdx.x == 0) s_chosen = 0x7fffffff;
+    const unsigned long long incl = block_scan_incl(mine, S.warp_tot);
+    if (threadIdx.x == 0) S.s_chosen = 0x7fffffff;
     __syncthreads();
     unsigned long long run = incl - mine;
 #pragma unroll
     for (int e = 0; e < CPT; ++e) {
         const int i = threadIdx.x * CPT + e;
         if (i < n) {
-            run += cand_w[i];
-            if (run >= rem) { atomicMin(&s_chosen, i); break; }
+            run += S.cand_w[i];
+            if (run >= rem) { atomicMin(&S.s_chosen, i); break; }
         }
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-        const int i = s_chosen == 0x7fffffff ? n - 1 : s_chosen;
-        out[b * out_stride] = static_cast<uint16_t>(n > 0 ? cand_id[i] : red_i[0]);
+    const int i = S.s_chosen == 0x7fffffff ? n - 1 : S.s_chosen;
+    return n > 0 ? S.cand_id[i] : none;
+}
+
+// One block per sequence row of logits [B][ld] (vocab V <= 65535). Greedy when
+// temperature == 0 (first index of the maximum). Otherwise the inverse CDF of
+// sample_token with top_p = 1: scores sorted descending (ties: lower id first), weights
+// w = exp(double(s - s0) / T), draw = u * sum(w) with the reference's 24-bit uniform u,
+// first position whose running sum reaches the draw. Weights are summed in exact 2^-48
+// fixed point (the sampled token equals the reference's except when the draw falls within
+// ~1e-10 of a CDF boundary). The sorted order is found without a full sort:
+//  1. one pass histograms the weights over 2048 buckets of equal score width between the
+//     row minimum and maximum (an order-preserving map: a higher score never lands in a
+//     lower bucket, and equal scores share one), so a row of 16384 spreads ~8 per bucket;
+//  2. a block scan over the buckets, highest first, locates the bucket holding the crossing;
+//  3. that bucket's scores are sorted in shared memory and a block scan finds the crossing.
+// When the crossing bucket holds more than kSampleCap scores (a row of near-identical
+// scores beside a distant maximum), the buckets are rebuilt from the order-preserving
+// integer key of each score instead, 11 bits at a time, until the selected prefix holds at
+// most kSampleCap scores (or all 32 bits are fixed).
+// Rows with active[b] == 0 are skipped. The draw index of row b is draw_index[b] (or 0) +
+// draw_offset + *counter (when given); the token goes to out[b * out_stride + *counter]
+// (counter 0 when null), so a replayed graph can advance both through device memory.
+__global__ void __launch_bounds__(kSampleThreads) sample_kernel(
+    const float* __restrict__ logits, long long ld, int V, float temperature,
+    const uint64_t* __restrict__ seeds, const int* __restrict__ draw_index, int draw_offset,
+    const int* __restrict__ counter, const int* __restrict__ active, uint16_t* __restrict__ out,
+    long long out_stride) {
+    __shared__ SampleShared S;
+    const int step = counter ? *counter : 0;
+    out += step;
+    draw_offset += step;
+    const int b = blockIdx.x;
+    if (active && !active[b]) return;
+    const float* row = logits + b * ld;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+
+    // maximum with its first index, and minimum
+    float mx = -INFINITY, mn = INFINITY;
+    int mi = 0x7fffffff;
+    for (int j = threadIdx.x; j < V; j += blockDim.x) {
+        const float v = row[j];
+        if (v > mx) { mx = v; mi = j; }
+        mn = fminf(mn, v);
     }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, mx, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, mi, o);
+        if (ov > mx || (ov == mx && oi < mi)) { mx = ov; mi = oi; }
+        mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+    }
+    if (lane == 0) { S.red_f[warp] = mx; S.red_i[warp] = mi; S.red_g[warp] = mn; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float bm = S.red_f[0], bn = S.red_g[0];
+        int bi = S.red_i[0];
+        for (int w = 1; w < nw; ++w) {
+            if (S.red_f[w] > bm || (S.red_f[w] == bm && S.red_i[w] < bi)) { bm = S.red_f[w]; bi = S.red_i[w]; }
+            bn = fminf(bn, S.red_g[w]);
+        }
+        S.red_f[0] = bm;
+        S.red_i[0] = bi;
+        S.red_g[0] = bn;
+    }
+    __syncthreads();
+    const float s0 = S.red_f[0], smin = S.red_g[0];
+    const int best = S.red_i[0];
+    if (temperature == 0.f) {
+        if (threadIdx.x == 0) out[b * out_stride] = static_cast<uint16_t>(best);
+        return;
+    }
+    const double T = static_cast<double>(temperature);
+    const uint64_t seed = seeds[b];
+    const int k = (draw_index ? draw_index[b] : 0) + draw_offset;
+
+    // 1-3: buckets of equal score width, bucket kSampleBuckets-1 holding the maximum
+    const float range = __fsub_rn(s0, smin);
+    float scale = range > 0.f ? __fdiv_rn(static_cast<float>(kSampleBuckets), range) : 0.f;
+    if (!(scale <= 3.0e38f)) scale = 0.f;
+    if (scale > 0.f) {
+        auto bucket_of = [&](float v) {
+            const float p = fminf(__fmul_rn(__fsub_rn(s0, v), scale), static_cast<float>(kSampleBuckets - 1));
+            return kSampleBuckets - 1 - static_cast<int>(p);
+        };
+        for (int i = threadIdx.x; i < kSampleBuckets; i += blockDim.x) { S.hist[i] = 0ull; S.hcount[i] = 0; }
+        __syncthreads();
+        for (int j = threadIdx.x; j < V; j += blockDim.x) {
+            const float v = row[j];
+            const int bk = bucket_of(v);
+            atomicAdd(&S.hist[bk], sample_weight_q(v, s0, T));
+            atomicAdd(&S.hcount[bk], 1);
+        }
+        __syncthreads();
+        sample_locate(S, kSampleBuckets, true, seed, k);
+        const int chosen = S.s_chosen;
+        if (S.hcount[chosen] <= kSampleCap) {
+            const int tok = sample_pick(S, row, V, s0, T, [&](float v) { return bucket_of(v) == chosen; }, best);
+            if (threadIdx.x == 0) out[b * out_stride] = static_cast<uint16_t>(tok);
+            return;
+        }
+        __syncthreads();
+    }
+
+    // fallback: buckets of the order-preserving key, refined 11 bits at a time
+    if (threadIdx.x == 0) { S.s_prefix = 0; S.s_bits = 0; }
+    __syncthreads();
+    bool first = true;
+    while (true) {
+        const int bits = S.s_bits;
+        const uint32_t prefix = S.s_prefix;
+        const int width = min(11, 32 - bits);
+        const int nb = 1 << width;
+        for (int i = threadIdx.x; i < kSampleBuckets; i += blockDim.x) { S.hist[i] = 0ull; S.hcount[i] = 0; }
+        __syncthreads();
+        for (int j0 = 0; j0 < V; j0 += blockDim.x) {
+            const int j = j0 + threadIdx.x;
+            bool valid = j < V;
+            const float v = valid ? row[j] : 0.f;
+            const uint32_t key = float_key(v);
+            if (bits > 0) valid = valid && (key >> (32 - bits)) == prefix;
+            const int bk = static_cast<int>((key >> (32 - bits - width)) & (nb - 1));
+            const unsigned long long q = valid ? sample_weight_q(v, s0, T) : 0ull;
+            warp_bucket_add(S.hist, S.hcount, bk, q, valid);
+        }
+        __syncthreads();
+        sample_locate(S, nb, first, seed, k);
+        first = false;
+        if (threadIdx.x == 0) {
+            const int chosen = S.s_chosen;
+            S.s_prefix = (prefix << width) | static_cast<uint32_t>(chosen);
+            S.s_bits = bits + width;
+            S.s_ncand = S.hcount[chosen];
+        }
+        __syncthreads();
+        if (S.s_ncand <= kSampleCap || S.s_bits >= 32) break;
+    }
+    const int bits = S.s_bits;
+    const uint32_t prefix = S.s_prefix;
+    const int ncand = S.s_ncand;
+    __syncthreads();
+    if (ncand > kSampleCap) {
+        // More than kSampleCap scores share one exact value (every key bit fixed): equal
+        // weights w, ordered by id, so the crossing is position m = ceil(rem / w) - 1 among
+        // them, found by an id-ordered block scan over the row.
+        const uint32_t u = (prefix & 0x80000000u) ? (prefix & 0x7fffffffu) : ~prefix;
+        const unsigned long long w = sample_weight_q(__uint_as_float(u), s0, T);
+        const unsigned long long rem = S.s_draw;
+        long long m = ncand - 1;
+        if (w > 0 && rem <= static_cast<unsigned long long>(ncand) * w) m = static_cast<long long>((rem + w - 1) / w) - 1;
+        m = max(0LL, min(m, static_cast<long long>(ncand - 1)));
+        long long seen = 0;
+        for (int j0 = 0; j0 < V; j0 += blockDim.x) {
+            const int j = j0 + threadIdx.x;
+            const int hit = (j < V && float_key(row[j]) == prefix) ? 1 : 0;
+            const unsigned long long incl = block_scan_incl(static_cast<unsigned long long>(hit), S.warp_tot);
+            const long long before = seen + static_cast<long long>(incl) - hit;
+            if (hit && before == m) out[b * out_stride] = static_cast<uint16_t>(j);
+            // the block's count for this chunk is the last thread's inclusive sum
+            if (threadIdx.x == kSampleThreads - 1) S.s_last = static_cast<int>(incl);
+            __syncthreads();
+            seen += S.s_last;
+            __syncthreads();
+            if (seen > m) break;
+        }
+        return;
+    }
+    const int tok = sample_pick(S, row, V, s0, T, [&](float v) {
+        const uint32_t key = float_key(v);
+        return (bits >= 32 ? key : (key >> (32 - bits))) == prefix;
+    }, best);
+    if (threadIdx.x == 0) out[b * out_stride] = static_cast<uint16_t>(tok);
 }
 
 } // namespace mm

@@ -1,0 +1,60 @@
+"""Microbenchmark of the tcgen05 GEMM at one shape through the kernel-level entry point
+(mm_cuda_gemm_f16 in include/mm_cuda_kernels.h).
+
+Device time per launch comes from the library's own CUDA-event profile (events recorded on
+the library stream around every GEMM launch), so host gaps between calls do not count.
+The default shape is the vocabulary head of one 32,640-token teacher-forced chunk:
+[T, 3d] x [V, 3d]^T with K = 3 * 512 (the fp32-accurate three-term split), fp32 output.
+
+    python -m cpp_inference_train_engine_b200.gemm_bench --shape 32640,16384,1536
+"""
+import argparse
+import json
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--shape", default="32640,16384,1536", help="M,N,K")
+    ap.add_argument("--a-mn", type=int, default=0, help="A stored [K][M] (1) or [M][K] (0)")
+    ap.add_argument("--b-mn", type=int, default=0, help="B stored [K][N] (1) or [N][K] (0)")
+    ap.add_argument("--out", default="f32", choices=["f32", "f16", "acc"])
+    ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    args = ap.parse_args(argv)
+
+    import torch
+
+    import cpp_inference_train_engine_b200 as E
+
+    M, N, K = (int(v) for v in args.shape.split(","))
+    kind = {"f32": 0, "acc": 1, "f16": 2}[args.out]
+    ex = E.CudaExecution(E.TINY)
+    g = torch.Generator(device="cuda").manual_seed(M + 3 * N + 7 * K)
+    pad = (K + 7) // 8 * 8
+    A = (torch.randn(K, (M + 7) // 8 * 8, device="cuda", generator=g) if args.a_mn
+         else torch.randn(M, pad, device="cuda", generator=g)).half()
+    B = (torch.randn(K, (N + 7) // 8 * 8, device="cuda", generator=g) if args.b_mn
+         else torch.randn(N, pad, device="cuda", generator=g)).half()
+    C = torch.zeros(M, N, device="cuda", dtype=torch.half if kind == 2 else torch.float32)
+    torch.cuda.synchronize()
+
+    def run():
+        ex.gemm(M, N, K, A.data_ptr(), A.shape[1], args.a_mn, B.data_ptr(), B.shape[1],
+                args.b_mn, C.data_ptr(), N, kind)
+
+    for _ in range(args.warmup):
+        run()
+    ex.profile(1)
+    for _ in range(args.iters):
+        run()
+    prof = ex.profile(0)
+    ms, launches, flops = prof["k_gemm"]
+    line = {"shape": [M, N, K], "a_mn": args.a_mn, "b_mn": args.b_mn, "out": args.out,
+            "launches": launches, "ms_per_launch": ms / max(launches, 1),
+            "tflops": flops / (ms / 1e3) / 1e12 if ms else None}
+    print(json.dumps(line))
+    ex.close()
+
+
+if __name__ == "__main__":
+    main()

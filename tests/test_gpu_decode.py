@@ -91,3 +91,39 @@ def test_sampler_matches_reference_sample_token():
                 st = (int(seeds[b]) + int(draws[b]) * 0x9E3779B97F4A7C15) % 2 ** 64
                 tok, _ = ref.sample_token(logits[b], st, temperature=temp)
                 assert got[b] == tok, (V, temp, b)
+
+
+def test_sampler_crowded_and_tied_rows():
+    """Rows whose crossing lands among crowded or exactly tied scores: a distant maximum
+    beside a tight cluster (more than 1024 scores per equal-width bucket), whole rows of one
+    value, and 3000 exact ties inside a spread row."""
+    require_gpu()
+    if not ref.available():
+        pytest.skip("oracle/_ref not built")
+    ex = E.CudaExecution(MLA36M)
+    V, B = 16384, 48
+    rng = np.random.default_rng(11)
+    logits = np.empty((B, V), np.float32)
+    for b in range(B):
+        kind = b % 4
+        if kind == 0:  # distant maximum, cluster of width 1e-3
+            row = rng.uniform(0, 1e-3, V)
+            row[rng.integers(V)] = 3.0
+        elif kind == 1:  # one value everywhere
+            row = np.full(V, 0.25)
+        elif kind == 2:  # 3000 exact ties at a mid-range value
+            row = rng.normal(size=V) * 0.5
+            row[rng.choice(V, 3000, replace=False)] = 0.0
+        else:  # ties at the maximum
+            row = rng.normal(size=V)
+            row[rng.choice(V, 2000, replace=False)] = row.max()
+        logits[b] = row
+    seeds = rng.integers(0, 2 ** 63, B).astype(np.uint64)
+    draws = rng.integers(0, 300, B).astype(np.int32)
+    for temp in (1.0, 0.3):
+        got = ex.sample(logits, temp, seeds, draws)
+        for b in range(B):
+            st = (int(seeds[b]) + int(draws[b]) * 0x9E3779B97F4A7C15) % 2 ** 64
+            tok, _ = ref.sample_token(logits[b], st, temperature=temp)
+            assert got[b] == tok, (temp, b)
+    ex.close()

@@ -197,27 +197,26 @@ def main():
     import torch
 
     import cpp_inference_train_engine_b200 as E
+    from cpp_inference_train_engine_b200 import distributed as D
     from cpp_inference_train_engine_b200.config import MLA36M, AdamWConfig
     from cpp_inference_train_engine_b200.rng import grpo_workload
 
     cfg = MLA36M
     n_total = args.prompts * args.group
-    if n_total % world or (n_total // world) % args.group:
-        raise SystemExit("rollouts must split into whole groups per rank")
-    R = n_total // world
+    try:
+        sl = D.rollout_shard(n_total, args.group, rank, world)
+    except ValueError as e:
+        raise SystemExit(str(e))
     seq = args.prompt_len + args.new_tokens
     prompts, seeds, rewards = grpo_workload(args.prompts, args.group, args.prompt_len,
                                             cfg.vocab_size, 0.3)
-    sl = slice(rank * R, (rank + 1) * R)
     prompts, seeds, rewards = prompts[sl].copy(), seeds[sl].copy(), rewards[sl].copy()
 
     W = E.init_params(cfg, 0)
     pol = E.make_execution(cfg, W, optimizer=AdamWConfig(), device=local)
     refm = E.make_execution(cfg, W, device=local)
     if world > 1:
-        uid = [E.CudaExecution.nccl_unique_id() if rank == 0 else None]
-        dist.broadcast_object_list(uid, src=0)
-        pol.init_comm(rank, world, uid[0])
+        D.init_comm(pol, rank, world)
     stream = torch.cuda.ExternalStream(pol.stream, device=local)
 
     def one_step(step_idx):

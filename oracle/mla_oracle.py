@@ -424,13 +424,14 @@ def completion_batch(prompt, response, seq, pad):
     return inp, tgt, mask
 
 
-def grpo_coefficients(lp, old, ref, mask, advantages, clip, klc):
+def grpo_coefficients(lp, old, ref, mask, advantages, clip, klc, n_total=None):
     """Coefficient assembly of src/train/trainer.cpp:827-846 over rollouts [N, S]:
-    coef = nll_coefficient / (N * supervised_i); loss/kl summed in double."""
-    N = lp.shape[0]
+    coef = nll_coefficient / (N * supervised_i); loss/kl summed in double. ``n_total``
+    replaces N when these rows are one data-parallel shard of a larger step."""
+    N = lp.shape[0] if n_total is None else int(n_total)
     coef = np.zeros_like(lp, dtype=F32)
     loss = kl = 0.0
-    for i in range(N):
+    for i in range(lp.shape[0]):
         sup = int(np.count_nonzero(mask[i] == 1))
         den = float(N * sup)
         for t in np.nonzero(mask[i])[0]:

@@ -90,21 +90,17 @@ inline void decode_step(Context& cx) {
     MM_LAUNCH(embed_kernel, warp_rows_grid(B), 256, 0, d.tok, cx.E(), d.x, B, c.d, c.V, cx.d_err);
     for (int l = 0; l < c.L; ++l) {
         const PrepLayer& p = cx.prep[l];
-        MM_LAUNCH(rmsnorm_kernel, warp_rows_grid(B), 256, 0, d.x, (long long)c.d, cx.W(l, kAttnNorm), B, c.d, c.eps,
-                  (float*)nullptr, 0LL, d.h16, (long long)ld_d, (float*)nullptr);
+        launch_rmsnorm(cx, d.x, c.d, cx.W(l, kAttnNorm), B, c.d, (float*)nullptr, 0LL, d.h16, ld_d);
         gemm(cx, B, qrk, c.d, {d.h16, ld_d, false}, {p.Wa, p.lda, true}, {d.y, qrk, kOutF32});
-        MM_LAUNCH(rmsnorm_kernel, warp_rows_grid(B), 256, 0, d.y, (long long)qrk, cx.W(l, kQNorm), B, c.qr, c.eps,
-                  (float*)nullptr, 0LL, d.cq16, (long long)ld_qr, (float*)nullptr);
-        MM_LAUNCH(rmsnorm_kernel, warp_rows_grid(B), 256, 0, d.y + c.qr, (long long)qrk, cx.W(l, kKvNorm), B, c.kvr, c.eps,
-                  (float*)nullptr, 0LL, d.lat16, (long long)ld_kvr, (float*)nullptr);
+        launch_rmsnorm(cx, d.y, qrk, cx.W(l, kQNorm), B, c.qr, (float*)nullptr, 0LL, d.cq16, ld_qr);
+        launch_rmsnorm(cx, d.y + c.qr, qrk, cx.W(l, kKvNorm), B, c.kvr, (float*)nullptr, 0LL, d.lat16, ld_kvr);
         MM_LAUNCH(rope_key_kernel, blocks_for((long long)B * (c.rope / 2), 256), 256, 0, d.y + c.qr, (long long)qrk, c.kvr,
                   c.rope, B, 1, d.pos, cx.cos_t, cx.sin_t, d.k_rope, (__half*)nullptr, 0LL);
         __half* cache_l = d.cache + static_cast<long long>(l) * B * d.Sc * kvw;
         MM_LAUNCH(cache_write_kernel, blocks_for((long long)B * kvw, 256), 256, 0, d.lat16, (long long)ld_kvr, d.k_rope, B, 1,
                   d.pos, 0, cache_l, d.Sc, c.kvr, c.rope);
         gemm(cx, B, c.H * kvw, c.qr, {d.cq16, ld_qr, false}, {p.Wq, p.ldq, true}, {d.qf, c.H * kvw, kOutF32});
-        MM_LAUNCH(rope_rows_kernel, warp_rows_grid(B), 256, 0, d.qf, (long long)(c.H * kvw), B, 1, d.pos, c.H, kvw, c.kvr,
-                  c.rope, cx.cos_t, cx.sin_t, 0, d.qf2, (long long)(c.H * kvw), (__half*)nullptr, 0LL);
+        launch_rope_rows(cx, d.qf, (c.H * kvw), B, 1, d.pos, c.H, kvw, c.kvr, c.rope, 0, d.qf2, (c.H * kvw), (__half*)nullptr, 0LL);
         {
             const float scale = 1.0f / std::sqrt(static_cast<float>(c.qk()));
             const size_t smem = sizeof(float) * c.H * kvw;
@@ -130,12 +126,10 @@ inline void decode_step(Context& cx) {
             o.ldr = c.d;
             gemm(cx, B, c.d, c.H * c.kvr, {d.ctx16, c.H * c.kvr, false}, {p.Wo, p.ldo, true}, o);
         }
-        MM_LAUNCH(rmsnorm_kernel, warp_rows_grid(B), 256, 0, d.res, (long long)c.d, cx.W(l, kFfnNorm), B, c.d, c.eps,
-                  (float*)nullptr, 0LL, d.h2, (long long)ld_d, (float*)nullptr);
+        launch_rmsnorm(cx, d.res, c.d, cx.W(l, kFfnNorm), B, c.d, (float*)nullptr, 0LL, d.h2, ld_d);
         const int ld_gu = cx.d16(2 * c.dff), ld_ff = cx.d16(c.dff);
         gemm(cx, B, 2 * c.dff, c.d, {d.h2, ld_d, false}, {p.Wgu, p.ldgu, true}, {d.gu, ld_gu, kOutF16});
-        MM_LAUNCH(swiglu_kernel, blocks_for((long long)B * c.dff, 256), 256, 0, d.gu, d.gu + c.dff, (long long)ld_gu, B,
-                  c.dff, d.gated, (long long)ld_ff);
+        launch_swiglu(cx, d.gu, d.gu + c.dff, ld_gu, B, c.dff, d.gated, ld_ff);
         {
             GemmOutSpec o{d.x, c.d, kOutF32};
             o.residual = d.res;
@@ -143,8 +137,7 @@ inline void decode_step(Context& cx) {
             gemm(cx, B, c.d, c.dff, {d.gated, ld_ff, false}, {cx.S(l, kWdown), cx.SL(l, kWdown), true}, o);
         }
     }
-    MM_LAUNCH(rmsnorm_kernel, warp_rows_grid(B), 256, 0, d.x, (long long)c.d, cx.FinalNorm(), B, c.d, c.eps, d.hf,
-              (long long)c.d, (__half*)nullptr, 0LL, (float*)nullptr);
+    launch_rmsnorm(cx, d.x, c.d, cx.FinalNorm(), B, c.d, d.hf, c.d, (__half*)nullptr, 0LL);
     const int ld3 = cx.d16(3 * c.d);
     MM_LAUNCH(split3_gather_kernel, blocks_for((long long)B * c.d, 256), 256, 0, d.hf, c.d, B, 1, 0, d.h3, (long long)ld3);
     GemmOutSpec lo{d.logits, c.V, kOutF32};

@@ -111,6 +111,7 @@ template <class A> void plan_workspace(Context& cx, A& a, int T, bool tape) {
         w.dkvp16 = w.draw16 ? w.draw16 + c.qr : nullptr;
         w.g16 = a.template take<__half>(t * c.V);
         w.dao16 = a.template take<__half>(t * c.aw());
+        w.norm_part = a.template take<float>(static_cast<long long>(kNormBlocks) * std::max(c.d, std::max(c.qr, c.kvr)));
     }
 }
 
@@ -142,6 +143,118 @@ inline void ensure_workspace(Context& cx, int T, bool tape) {
 
 inline unsigned warp_rows_grid(int rows) { return blocks_for(static_cast<long long>(rows) * 32, 256); }
 
+// ------------------------------------------------------------------ elementwise dispatch
+// Vector kernels (kernels_vec.cuh) when pitches and addresses allow 16-byte accesses.
+inline bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+inline bool al8(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 7) == 0; }
+
+inline void launch_rmsnorm(Context& cx, const float* x, long long ldx, const float* w, int T, int n, float* y32,
+                           long long ld32, __half* y16, long long ld16) {
+    const float eps = cx.c.eps;
+    const bool vec = n % 4 == 0 && n <= 1024 && ldx % 4 == 0 && al16(x) && al16(w) &&
+                     (!y32 || (ld32 % 4 == 0 && al16(y32))) && (!y16 || (ld16 % 4 == 0 && al8(y16)));
+    if (vec && n <= 512)
+        MM_LAUNCH(rmsnorm_v4_kernel<4>, warp_rows_grid(T), 256, 0, x, ldx, w, T, n, eps, y32, ld32, y16, ld16,
+                  (float*)nullptr);
+    else if (vec)
+        MM_LAUNCH(rmsnorm_v4_kernel<8>, warp_rows_grid(T), 256, 0, x, ldx, w, T, n, eps, y32, ld32, y16, ld16,
+                  (float*)nullptr);
+    else
+        MM_LAUNCH(rmsnorm_kernel, warp_rows_grid(T), 256, 0, x, ldx, w, T, n, eps, y32, ld32, y16, ld16, (float*)nullptr);
+}
+
+// dx = RMSNorm backward (+ add); dw += scale * sum over rows (fixed-order reduction when
+// vectorised).
+inline void launch_rmsnorm_backward(Context& cx, const float* x, long long ldx, const float* w, const float* dy,
+                                    long long lddy, const float* add, long long ldadd, int T, int n, float* dx32,
+                                    long long lddx, __half* dx16, long long lddx16, float* dw, const float* scale) {
+    const float eps = cx.c.eps;
+    const bool vec = n % 4 == 0 && n <= 1024 && cx.ws.norm_part && ldx % 4 == 0 && lddy % 4 == 0 && al16(x) &&
+                     al16(w) && al16(dy) && (!add || (ldadd % 4 == 0 && al16(add))) &&
+                     (!dx32 || (lddx % 4 == 0 && al16(dx32))) && (!dx16 || (lddx16 % 4 == 0 && al8(dx16)));
+    if (!vec) {
+        MM_LAUNCH(rmsnorm_backward_kernel, 148 * 4, 256, n * 4, x, ldx, w, dy, lddy, add, ldadd, T, n, eps, dx32, lddx,
+                  dx16, lddx16, dw, scale);
+        return;
+    }
+    const size_t smem = sizeof(float) * 8 * n;
+    if (n <= 512)
+        MM_LAUNCH(rmsnorm_backward_v4_kernel<4>, kNormBlocks, 256, smem, x, ldx, w, dy, lddy, add, ldadd, T, n, eps,
+                  dx32, lddx, dx16, lddx16, cx.ws.norm_part);
+    else
+        MM_LAUNCH(rmsnorm_backward_v4_kernel<8>, kNormBlocks, 256, smem, x, ldx, w, dy, lddy, add, ldadd, T, n, eps,
+                  dx32, lddx, dx16, lddx16, cx.ws.norm_part);
+    MM_LAUNCH(colsum_kernel, blocks_for(n, 256), 256, 0, cx.ws.norm_part, kNormBlocks, n, scale, dw);
+}
+
+inline void launch_swiglu(Context& cx, const __half* gate, const __half* up, long long ld, int T, int n, __half* out,
+                          long long ldo) {
+    if (n % 8 == 0 && ld % 8 == 0 && ldo % 8 == 0 && al16(gate) && al16(up) && al16(out))
+        MM_LAUNCH(swiglu_v8_kernel, blocks_for(static_cast<long long>(T) * (n / 8), 256), 256, 0, gate, up, ld, T, n,
+                  out, ldo);
+    else
+        MM_LAUNCH(swiglu_kernel, blocks_for(static_cast<long long>(T) * n, 256), 256, 0, gate, up, ld, T, n, out, ldo);
+}
+
+inline void launch_swiglu_backward(Context& cx, const __half* gate, const __half* up, long long ld, const float* dy,
+                                   long long lddy, int T, int n, __half* dg, __half* du, long long ldo) {
+    if (n % 8 == 0 && ld % 8 == 0 && ldo % 8 == 0 && lddy % 4 == 0 && al16(gate) && al16(up) && al16(dy) && al16(dg) &&
+        al16(du))
+        MM_LAUNCH(swiglu_backward_v8_kernel, blocks_for(static_cast<long long>(T) * (n / 8), 256), 256, 0, gate, up,
+                  ld, dy, lddy, T, n, dg, du, ldo);
+    else
+        MM_LAUNCH(swiglu_backward_kernel, blocks_for(static_cast<long long>(T) * n, 256), 256, 0, gate, up, ld, dy,
+                  lddy, T, n, dg, du, ldo);
+}
+
+inline void launch_to_half(Context& cx, const float* in, long long ldin, int T, int n, __half* out, long long ldo) {
+    if (n % 4 == 0 && ldin % 4 == 0 && ldo % 4 == 0 && al16(in) && al8(out))
+        MM_LAUNCH(to_half_v4_kernel, blocks_for(static_cast<long long>(T) * (n / 4), 256), 256, 0, in, ldin, T, n, out,
+                  ldo);
+    else
+        MM_LAUNCH(to_half_kernel, blocks_for(static_cast<long long>(T) * n, 256), 256, 0, in, ldin, T, n, out, ldo);
+}
+
+inline void launch_assemble_k(Context& cx, const float* k_nope, long long ldn, const float* k_rope, int T,
+                              __half* k, long long ldk) {
+    const Dims& c = cx.c;
+    const int qk = c.qk();
+    if (c.nope % 8 == 0 && c.rope % 8 == 0 && ldn % 4 == 0 && ldk % 8 == 0 && al16(k_nope) && al16(k_rope) && al16(k))
+        MM_LAUNCH(assemble_k_v8_kernel, blocks_for(static_cast<long long>(T) * c.H * qk / 8, 256), 256, 0, k_nope, ldn,
+                  k_rope, T, c.H, c.nope, c.rope, k, ldk);
+    else
+        MM_LAUNCH(assemble_k_kernel, blocks_for(static_cast<long long>(T) * c.H * qk, 256), 256, 0, k_nope, ldn, k_rope,
+                  T, c.H, c.nope, c.rope, k, ldk);
+}
+
+inline void launch_rowdot(Context& cx, const __half* dout, const __half* out, int T, int H, int DV, float* Dd) {
+    if (DV % 8 == 0 && al16(dout) && al16(out))
+        MM_LAUNCH(attn_rowdot_v8_kernel, blocks_for(static_cast<long long>(T) * H, 256), 256, 0, dout, out, T, H, DV, Dd);
+    else
+        MM_LAUNCH(attn_rowdot_kernel, blocks_for(static_cast<long long>(T) * H, 256), 256, 0, dout, out, T, H, DV, Dd);
+}
+
+inline void launch_vocab_grad(Context& cx, const float* logits, long long ld, int V, const uint16_t* target,
+                              const float* lse, const float* coef, const float* scale, int T, __half* g, long long ldg) {
+    if (V % 4 == 0 && ld % 4 == 0 && ldg % 4 == 0 && al16(logits) && al8(g))
+        MM_LAUNCH(vocab_grad_v4_kernel, blocks_for(static_cast<long long>(T) * (V / 4), 256), 256, 0, logits, ld, V,
+                  target, lse, coef, scale, T, g, ldg);
+    else
+        MM_LAUNCH(vocab_grad_kernel, T, 256, 0, logits, ld, V, target, lse, coef, scale, T, g, ldg);
+}
+
+inline void launch_rope_rows(Context& cx,const float* in, long long ldin, int T, int seq, const int* pos_base, int heads,
+                             int width, int begin, int rope, int inverse, float* out32, long long ld32, __half* out16,
+                             long long ld16) {
+    if ((heads * width) % 4 == 0 && width % 2 == 0 && begin % 2 == 0 && rope % 2 == 0 && ldin % 4 == 0 && al16(in) &&
+        (!out32 || (ld32 % 4 == 0 && al16(out32))) && (!out16 || (ld16 % 4 == 0 && al8(out16))))
+        MM_LAUNCH(rope_rows_v4_kernel, blocks_for(static_cast<long long>(T) * heads * width / 4, 256), 256, 0, in, ldin,
+                  T, seq, pos_base, heads, width, begin, rope, cx.cos_t, cx.sin_t, inverse, out32, ld32, out16, ld16);
+    else
+        MM_LAUNCH(rope_rows_kernel, warp_rows_grid(T), 256, 0, in, ldin, T, seq, pos_base, heads, width, begin, rope,
+                  cx.cos_t, cx.sin_t, inverse, out32, ld32, out16, ld16);
+}
+
 inline void launch_flash_fwd(Context& cx, const LayerBuf& b, int Bc, int S) {
     const Dims& c = cx.c;
     dim3 grid((S + fa::kTile - 1) / fa::kTile, c.H, Bc);
@@ -170,18 +283,14 @@ inline void forward_chunk(Context& cx, int Bc, int S, bool tape, VocabMode vm, b
         LayerBuf& b = w.layers[tape ? l : 0];
         float* x_next = tape ? (l + 1 < c.L ? w.layers[l + 1].x_in : w.x_out) : (l + 1 < c.L ? b.x_in : w.x_out);
         // attention block
-        MM_LAUNCH(rmsnorm_kernel, warp_rows_grid(T), 256, 0, b.x_in, (long long)c.d, cx.W(l, kAttnNorm), T, c.d, c.eps,
-                  (float*)nullptr, 0LL, b.h, (long long)ld_d, (float*)nullptr);
+        launch_rmsnorm(cx, b.x_in, c.d, cx.W(l, kAttnNorm), T, c.d, (float*)nullptr, 0LL, b.h, ld_d);
         const PrepLayer& pw = cx.prep[l];
         const int qkv = c.qr + kvw;
         gemm(cx, T, qkv, c.d, {b.h, ld_d, false}, {pw.Wa, pw.lda, true}, {b.raw_cq, qkv, kOutF32});
-        MM_LAUNCH(rmsnorm_kernel, warp_rows_grid(T), 256, 0, b.raw_cq, (long long)qkv, cx.W(l, kQNorm), T, c.qr, c.eps,
-                  (float*)nullptr, 0LL, b.cq, (long long)ld_qr, (float*)nullptr);
+        launch_rmsnorm(cx, b.raw_cq, qkv, cx.W(l, kQNorm), T, c.qr, (float*)nullptr, 0LL, b.cq, ld_qr);
         gemm(cx, T, c.H * qk, c.qr, {b.cq, ld_qr, false}, {cx.S(l, kWuq), cx.SL(l, kWuq), true}, {w.q_pre, c.H * qk, kOutF32});
-        MM_LAUNCH(rope_rows_kernel, warp_rows_grid(T), 256, 0, w.q_pre, (long long)(c.H * qk), T, S, (const int*)nullptr,
-                  c.H, qk, c.nope, c.rope, cx.cos_t, cx.sin_t, 0, (float*)nullptr, 0LL, b.q, (long long)(c.H * qk));
-        MM_LAUNCH(rmsnorm_kernel, warp_rows_grid(T), 256, 0, b.kvp, (long long)qkv, cx.W(l, kKvNorm), T, c.kvr, c.eps,
-                  (float*)nullptr, 0LL, b.ckv, (long long)ld_kvr, (float*)nullptr);
+        launch_rope_rows(cx, w.q_pre, (c.H * qk), T, S, (const int*)nullptr, c.H, qk, c.nope, c.rope, 0, (float*)nullptr, 0LL, b.q, (c.H * qk));
+        launch_rmsnorm(cx, b.kvp, qkv, cx.W(l, kKvNorm), T, c.kvr, (float*)nullptr, 0LL, b.ckv, ld_kvr);
         MM_LAUNCH(rope_key_kernel, blocks_for((long long)T * (c.rope / 2), 256), 256, 0, b.kvp, (long long)qkv, c.kvr,
                   c.rope, T, S, (const int*)nullptr, cx.cos_t, cx.sin_t, b.k_rope, (__half*)nullptr, 0LL);
         if (cache)
@@ -189,8 +298,7 @@ inline void forward_chunk(Context& cx, int Bc, int S, bool tape, VocabMode vm, b
                       T, S, (const int*)nullptr, row0, cache + (long long)l * cx.dec.B * Sc * kvw, Sc, c.kvr, c.rope);
         gemm(cx, T, c.H * c.nope, c.kvr, {b.ckv, ld_kvr, false}, {cx.S(l, kWuk), cx.SL(l, kWuk), true},
              {w.knope, c.H * c.nope, kOutF32});
-        MM_LAUNCH(assemble_k_kernel, blocks_for((long long)T * c.H * qk, 256), 256, 0, w.knope, (long long)(c.H * c.nope),
-                  b.k_rope, T, c.H, c.nope, c.rope, b.k, (long long)(c.H * qk));
+        launch_assemble_k(cx, w.knope, (c.H * c.nope), b.k_rope, T, b.k, (c.H * qk));
         gemm(cx, T, c.aw(), c.kvr, {b.ckv, ld_kvr, false}, {cx.S(l, kWuv), cx.SL(l, kWuv), true}, {b.v, c.aw(), kOutF16});
         launch_flash_fwd(cx, b, Bc, S);
         {
@@ -200,12 +308,10 @@ inline void forward_chunk(Context& cx, int Bc, int S, bool tape, VocabMode vm, b
             gemm(cx, T, c.d, c.aw(), {b.ao, c.aw(), false}, {cx.S(l, kWo), cx.SL(l, kWo), true}, o);
         }
         // feed-forward block
-        MM_LAUNCH(rmsnorm_kernel, warp_rows_grid(T), 256, 0, b.res, (long long)c.d, cx.W(l, kFfnNorm), T, c.d, c.eps,
-                  (float*)nullptr, 0LL, b.h2, (long long)ld_d, (float*)nullptr);
+        launch_rmsnorm(cx, b.res, c.d, cx.W(l, kFfnNorm), T, c.d, (float*)nullptr, 0LL, b.h2, ld_d);
         const int ld_gu = cx.d16(2 * c.dff);
         gemm(cx, T, 2 * c.dff, c.d, {b.h2, ld_d, false}, {pw.Wgu, pw.ldgu, true}, {b.gate, ld_gu, kOutF16});
-        MM_LAUNCH(swiglu_kernel, blocks_for((long long)T * c.dff, 256), 256, 0, b.gate, b.up, (long long)ld_gu, T, c.dff,
-                  b.gated, (long long)ld_ff);
+        launch_swiglu(cx, b.gate, b.up, ld_gu, T, c.dff, b.gated, ld_ff);
         {
             GemmOutSpec o{x_next, c.d, kOutF32};
             o.residual = b.res;
@@ -214,8 +320,7 @@ inline void forward_chunk(Context& cx, int Bc, int S, bool tape, VocabMode vm, b
         }
     }
     if (vm == kVocabNone) return;
-    MM_LAUNCH(rmsnorm_kernel, warp_rows_grid(T), 256, 0, w.x_out, (long long)c.d, cx.FinalNorm(), T, c.d, c.eps,
-              w.hf, (long long)c.d, (__half*)nullptr, 0LL, (float*)nullptr);
+    launch_rmsnorm(cx, w.x_out, c.d, cx.FinalNorm(), T, c.d, w.hf, c.d, (__half*)nullptr, 0LL);
     const int ld3 = cx.d16(3 * c.d);
     GemmOutSpec lo{nullptr, c.V, kOutF32};
     lo.alpha = 1.0f / kVocabScale;
@@ -247,8 +352,7 @@ inline void backward_chunk(Context& cx, int Bc, int S) {
     const int ld3 = cx.d16(3 * c.d);
     const float* inv_s = cx.d_scale + 1;
     // vocabulary head: g = s * coef * (softmax - onehot)
-    MM_LAUNCH(vocab_grad_kernel, T, 256, 0, w.logits, (long long)c.V, c.V, w.targets, w.lse_v, w.coef, cx.d_scale, T,
-              w.g16, (long long)c.V);
+    launch_vocab_grad(cx, w.logits, c.V, c.V, w.targets, w.lse_v, w.coef, cx.d_scale, T, w.g16, c.V);
     {
         GemmOutSpec o{w.dh, c.d, kOutF32};
         o.alpha = 1.0f / kVocabScale;  // E3's hi part holds 64 * E
@@ -259,14 +363,11 @@ inline void backward_chunk(Context& cx, int Bc, int S) {
         o.alpha_ptr = inv_s;
         gemm(cx, c.V, c.d, T, {w.g16, c.V, true}, {w.h3, ld3, true}, o);  // h_hi = h3[:, :d]
     }
-    MM_LAUNCH(rmsnorm_backward_kernel, 148 * 4, 256, c.d * 4, w.x_out, (long long)c.d, cx.FinalNorm(), w.dh,
-              (long long)c.d, (const float*)nullptr, 0LL, T, c.d, c.eps, w.dy, (long long)c.d, (__half*)nullptr, 0LL,
-              cx.GFinalNorm(), inv_s);
+    launch_rmsnorm_backward(cx, w.x_out, c.d, cx.FinalNorm(), w.dh, c.d, (const float*)nullptr, 0LL, T, c.d, w.dy, c.d, (__half*)nullptr, 0LL, cx.GFinalNorm(), inv_s);
     for (int l = c.L - 1; l >= 0; --l) {
         LayerBuf& b = w.layers[l];
         // feed-forward block
-        MM_LAUNCH(to_half_kernel, blocks_for((long long)T * c.d, 256), 256, 0, w.dy, (long long)c.d, T, c.d, w.dy16,
-                  (long long)ld_d);
+        launch_to_half(cx, w.dy, c.d, T, c.d, w.dy16, ld_d);
         {
             GemmOutSpec o{cx.G(l, kWdown), c.d, kOutF32Acc};
             o.alpha_ptr = inv_s;
@@ -275,8 +376,7 @@ inline void backward_chunk(Context& cx, int Bc, int S) {
         gemm(cx, T, c.dff, c.d, {w.dy16, ld_d, false}, {cx.S(l, kWdown), cx.SL(l, kWdown), false}, {w.dgated, c.dff, kOutF32});
         const int ld_gu = cx.d16(2 * c.dff);
         const PrepLayer& pw = cx.prep[l];
-        MM_LAUNCH(swiglu_backward_kernel, blocks_for((long long)T * c.dff, 256), 256, 0, b.gate, b.up, (long long)ld_gu,
-                  w.dgated, (long long)c.dff, T, c.dff, w.dg16, w.du16, (long long)ld_gu);
+        launch_swiglu_backward(cx, b.gate, b.up, ld_gu, w.dgated, c.dff, T, c.dff, w.dg16, w.du16, ld_gu);
         {
             GemmOutSpec o{cx.G(l, kWgate), c.dff, kOutF32Acc};
             o.alpha_ptr = inv_s;
@@ -286,9 +386,7 @@ inline void backward_chunk(Context& cx, int Bc, int S) {
         }
         // dh2 = [dg | du] . [W_gate | W_up]^T, one product over K = 2 d_ff
         gemm(cx, T, c.d, 2 * c.dff, {w.dg16, ld_gu, false}, {pw.Wgu, pw.ldgu, false}, {w.dh2, c.d, kOutF32});
-        MM_LAUNCH(rmsnorm_backward_kernel, 148 * 4, 256, c.d * 4, b.res, (long long)c.d, cx.W(l, kFfnNorm), w.dh2,
-                  (long long)c.d, w.dy, (long long)c.d, T, c.d, c.eps, w.dres, (long long)c.d, w.dres16, (long long)ld_d,
-                  cx.G(l, kFfnNorm), inv_s);
+        launch_rmsnorm_backward(cx, b.res, c.d, cx.W(l, kFfnNorm), w.dh2, c.d, w.dy, c.d, T, c.d, w.dres, c.d, w.dres16, ld_d, cx.G(l, kFfnNorm), inv_s);
         // attention output projection
         {
             GemmOutSpec o{cx.G(l, kWo), c.d, kOutF32Acc};
@@ -297,7 +395,7 @@ inline void backward_chunk(Context& cx, int Bc, int S) {
         }
         gemm(cx, T, aw, c.d, {w.dres16, ld_d, false}, {cx.S(l, kWo), cx.SL(l, kWo), false}, {w.dao16, aw, kOutF16});
         // attention
-        MM_LAUNCH(attn_rowdot_kernel, blocks_for((long long)T * c.H, 256), 256, 0, w.dao16, b.ao, T, c.H, c.dv, w.Dd);
+        launch_rowdot(cx, w.dao16, b.ao, T, c.H, c.dv, w.Dd);
         {
             dim3 grid((S + fa::kTile - 1) / fa::kTile, c.H, Bc);
             const float scale = 1.0f / std::sqrt(static_cast<float>(qk));
@@ -313,14 +411,12 @@ inline void backward_chunk(Context& cx, int Bc, int S) {
             }
         }
         const int ld_q16 = cx.d16(c.H * qk);
-        MM_LAUNCH(rope_rows_kernel, warp_rows_grid(T), 256, 0, w.dq, (long long)(c.H * qk), T, S, (const int*)nullptr, c.H,
-                  qk, c.nope, c.rope, cx.cos_t, cx.sin_t, 1, (float*)nullptr, 0LL, w.dq16, (long long)ld_q16);
+        launch_rope_rows(cx, w.dq, (c.H * qk), T, S, (const int*)nullptr, c.H, qk, c.nope, c.rope, 1, (float*)nullptr, 0LL, w.dq16, ld_q16);
         const int ld_kn16 = cx.d16(c.H * c.nope);
         MM_LAUNCH(split_dk_kernel, warp_rows_grid(T), 256, 0, w.dk, T, c.H, c.nope, c.rope, w.dkn16, (long long)ld_kn16, w.drope);
-        MM_LAUNCH(rope_rows_kernel, warp_rows_grid(T), 256, 0, w.drope, (long long)c.rope, T, S, (const int*)nullptr, 1,
-                  c.rope, 0, c.rope, cx.cos_t, cx.sin_t, 1, w.drope2, (long long)c.rope, (__half*)nullptr, 0LL);
+        launch_rope_rows(cx, w.drope, c.rope, T, S, (const int*)nullptr, 1, c.rope, 0, c.rope, 1, w.drope2, c.rope, (__half*)nullptr, 0LL);
         const int ld_v16 = cx.d16(aw);
-        MM_LAUNCH(to_half_kernel, blocks_for((long long)T * aw, 256), 256, 0, w.dv, (long long)aw, T, aw, w.dv16, (long long)ld_v16);
+        launch_to_half(cx, w.dv, aw, T, aw, w.dv16, ld_v16);
         {
             GemmOutSpec o{cx.G(l, kWuk), c.H * c.nope, kOutF32Acc};
             o.alpha_ptr = inv_s;
@@ -332,9 +428,7 @@ inline void backward_chunk(Context& cx, int Bc, int S) {
         gemm(cx, T, c.kvr, c.H * c.nope, {w.dkn16, ld_kn16, false}, {cx.S(l, kWuk), cx.SL(l, kWuk), false}, {w.dckv, c.kvr, kOutF32});
         gemm(cx, T, c.kvr, aw, {w.dv16, ld_v16, false}, {cx.S(l, kWuv), cx.SL(l, kWuv), false}, {w.dckv, c.kvr, kOutF32Acc});
         const int qkv = c.qr + kvw, ld_qkv16 = cx.d16(qkv);
-        MM_LAUNCH(rmsnorm_backward_kernel, 148 * 4, 256, c.kvr * 4, b.kvp, (long long)qkv, cx.W(l, kKvNorm), w.dckv,
-                  (long long)c.kvr, (const float*)nullptr, 0LL, T, c.kvr, c.eps, w.dkvraw, (long long)c.kvr, (__half*)nullptr,
-                  0LL, cx.G(l, kKvNorm), inv_s);
+        launch_rmsnorm_backward(cx, b.kvp, qkv, cx.W(l, kKvNorm), w.dckv, c.kvr, (const float*)nullptr, 0LL, T, c.kvr, w.dkvraw, c.kvr, (__half*)nullptr, 0LL, cx.G(l, kKvNorm), inv_s);
         MM_LAUNCH(pack_dkv_kernel, blocks_for((long long)T * kvw, 256), 256, 0, w.dkvraw, w.drope2, T, c.kvr, c.rope, w.dkvp16,
                   (long long)ld_qkv16);
         {
@@ -348,9 +442,7 @@ inline void backward_chunk(Context& cx, int Bc, int S) {
             gemm(cx, c.qr, c.H * qk, T, {b.cq, ld_qr, true}, {w.dq16, ld_q16, true}, o);
         }
         gemm(cx, T, c.qr, c.H * qk, {w.dq16, ld_q16, false}, {cx.S(l, kWuq), cx.SL(l, kWuq), false}, {w.dcq, c.qr, kOutF32});
-        MM_LAUNCH(rmsnorm_backward_kernel, 148 * 4, 256, c.qr * 4, b.raw_cq, (long long)qkv, cx.W(l, kQNorm), w.dcq,
-                  (long long)c.qr, (const float*)nullptr, 0LL, T, c.qr, c.eps, (float*)nullptr, 0LL, w.draw16,
-                  (long long)ld_qkv16, cx.G(l, kQNorm), inv_s);
+        launch_rmsnorm_backward(cx, b.raw_cq, qkv, cx.W(l, kQNorm), w.dcq, c.qr, (const float*)nullptr, 0LL, T, c.qr, (float*)nullptr, 0LL, w.draw16, ld_qkv16, cx.G(l, kQNorm), inv_s);
         {
             GemmOutSpec o{cx.G(l, kWdq), c.qr, kOutF32Acc};
             o.alpha_ptr = inv_s;
@@ -358,9 +450,7 @@ inline void backward_chunk(Context& cx, int Bc, int S) {
         }
         // dh = [d raw_cq | d kv_pack] . [W_dq | W_dkv]^T, one product over K = qr + kvw
         gemm(cx, T, c.d, qkv, {w.draw16, ld_qkv16, false}, {cx.prep[l].Wa, cx.prep[l].lda, false}, {w.dh, c.d, kOutF32});
-        MM_LAUNCH(rmsnorm_backward_kernel, 148 * 4, 256, c.d * 4, b.x_in, (long long)c.d, cx.W(l, kAttnNorm), w.dh,
-                  (long long)c.d, w.dres, (long long)c.d, T, c.d, c.eps, w.dy, (long long)c.d, (__half*)nullptr, 0LL,
-                  cx.G(l, kAttnNorm), inv_s);
+        launch_rmsnorm_backward(cx, b.x_in, c.d, cx.W(l, kAttnNorm), w.dh, c.d, w.dres, c.d, T, c.d, w.dy, c.d, (__half*)nullptr, 0LL, cx.G(l, kAttnNorm), inv_s);
     }
     MM_LAUNCH(embed_backward_kernel, warp_rows_grid(T), 256, 0, w.tokens, w.dy, T, c.d, cx.GE(), inv_s);
 }

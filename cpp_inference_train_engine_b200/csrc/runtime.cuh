@@ -18,7 +18,7 @@
 #include "common.cuh"
 #include "flash_mma.cuh"
 #include "gemm_tc.cuh"
-#include "kernels_elem.cuh"
+#include "kernels_vec.cuh"
 #include "optim.cuh"
 #include "vocab_grpo.cuh"
 
@@ -156,7 +156,11 @@ struct Workspace {
     // backward scratch (tape only)
     float *dy, *dgated, *dh2, *dres, *dao, *dq, *dk, *dv, *drope, *drope2, *dckv, *dkvraw, *dh, *dcq, *Dd;
     __half *dy16, *dg16, *du16, *dres16, *dq16, *dkn16, *dv16, *dkvp16, *draw16, *g16, *dao16;
+    float* norm_part;   // [kNormBlocks][max(d, qr, kv_rank)] RMSNorm weight-gradient partials
 };
+
+// Blocks of the RMSNorm backward (2 per SM): one weight-gradient partial row each.
+constexpr int kNormBlocks = 296;
 
 struct DecodeState {
     int B = 0, Sc = 0;  // rows, cache positions per row

@@ -86,9 +86,14 @@ inline void gemm(Context& cx, int M, int N, int K, Opnd A, Opnd B, const GemmOut
         const int Mp = ga.split_rows;
         const long long n_pad = N;
         const long long MN = static_cast<long long>(M) * N;
-        splitk_reduce_kernel<<<blocks_for(MN, 256), 256, 0, cx.stream>>>(
-            part, splits, static_cast<long long>(Mp) * n_pad, M, N, static_cast<float*>(o.out), o.ldc, o.alpha,
-            o.alpha_ptr);
+        if (o.ldc % 4 == 0 && (reinterpret_cast<uintptr_t>(o.out) & 15) == 0)  // N % 4 == 0 here
+            splitk_reduce_v4_kernel<<<blocks_for(MN / 4, 256), 256, 0, cx.stream>>>(
+                part, splits, static_cast<long long>(Mp) * n_pad, M, N, static_cast<float*>(o.out), o.ldc, o.alpha,
+                o.alpha_ptr);
+        else
+            splitk_reduce_kernel<<<blocks_for(MN, 256), 256, 0, cx.stream>>>(
+                part, splits, static_cast<long long>(Mp) * n_pad, M, N, static_cast<float*>(o.out), o.ldc, o.alpha,
+                o.alpha_ptr);
         ++cx.launches;
     }
 }

@@ -78,6 +78,7 @@ __global__ void decode_attention_kernel(const float* __restrict__ qf, const __ha
 }
 
 // Tensor-core form for 8 heads over a [128 latent | 16 rope] cache row (the 35.8M model).
+// Launch with dec::kSmem bytes of dynamic shared memory.
 // The 8 heads are exactly the N = 8 of mma.sync m16n8k16, so per 16 cached positions a warp
 // computes S^T = C[16 x 144] * Q^T (9 MMAs) and O^T += C^T[128 x 16] * P^T (8 MMAs, C^T via
 // transposed ldmatrix). Each warp keeps its own online-softmax state over its share of the
@@ -89,6 +90,9 @@ constexpr int H = 8, KV = 128, R = 16, W = KV + R;
 constexpr int LDQ = W + 8;    // padded rows: 16-byte aligned, conflict-free ldmatrix
 constexpr int LDP = 16 + 8;
 constexpr int kWarps = 4;
+constexpr int kStages = 3;  // cache tiles in flight per warp
+// dynamic shared memory: the per-warp cache-tile rings
+constexpr int kSmem = kWarps * kStages * 16 * LDQ * 2;
 }  // namespace dec
 
 __global__ void __launch_bounds__(128) decode_attention_mma_kernel(
@@ -99,10 +103,14 @@ __global__ void __launch_bounds__(128) decode_attention_mma_kernel(
     using fa::ldsm_x4_t;
     using fa::mma16816;
     __shared__ __align__(16) __half Qs[H][LDQ];
-    __shared__ __align__(16) __half Cw[kWarps][16][LDQ];
+    // per-warp ring of kStages cache tiles (cp.async), reused as Ow [kWarps][H][KV] fp32
+    // for the merge once every warp has left its loop
+    extern __shared__ __align__(16) unsigned char ring_raw[];  // kSmem bytes
     __shared__ __align__(16) __half Pw[kWarps][H][LDP];
     __shared__ float Mw[kWarps][H], Lw[kWarps][H];
-    __shared__ float Ow[kWarps][H][KV];
+    static_assert(sizeof(float) * kWarps * H * KV <= kSmem, "merge buffer fits the ring");
+    auto Cw = reinterpret_cast<__half (*)[kStages][16][LDQ]>(ring_raw);
+    auto Ow = reinterpret_cast<float (*)[H][KV]>(ring_raw);
     const int b = blockIdx.x, sp = blockIdx.y, nsplit = gridDim.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const int n = pos[b] + 1;
@@ -110,6 +118,24 @@ __global__ void __launch_bounds__(128) decode_attention_mma_kernel(
     const int per = (tiles + nsplit - 1) / nsplit;
     const int t_begin = sp * per, t_end = min(tiles, t_begin + per);
     const float qscale = scale * fa::kLog2e;
+    const __half* cb = cache + static_cast<long long>(b) * cache_seq_stride;
+    // the warp's j-th tile (t_begin + warp + kWarps * j) into ring stage j % kStages; one
+    // commit group per call (empty past the end) keeps the group count uniform
+    auto issue = [&](int j) {
+        const int tile = t_begin + warp + kWarps * j;
+        if (tile < t_end) {
+            const int p0 = tile * 16;
+            __half (*dst)[LDQ] = Cw[warp][j % kStages];
+            for (int e = lane; e < 16 * (W / 8); e += 32) {
+                const int r = e / (W / 8), cc = (e % (W / 8)) * 8;
+                const bool ok = p0 + r < n;
+                cp_async16(&dst[r][cc], cb + static_cast<long long>(ok ? p0 + r : 0) * W + cc, ok);
+            }
+        }
+        cp_async_commit();
+    };
+#pragma unroll
+    for (int j = 0; j < kStages - 1; ++j) issue(j);
     for (int e = threadIdx.x; e < H * W; e += blockDim.x)
         Qs[e / W][e % W] = __float2half_rn(qf[static_cast<long long>(b) * H * W + e] * qscale);
     __syncthreads();
@@ -122,26 +148,23 @@ __global__ void __launch_bounds__(128) decode_attention_mma_kernel(
         qb[kk][0] = r[0];
         qb[kk][1] = r[1];
     }
-    const __half* cb = cache + static_cast<long long>(b) * cache_seq_stride;
     float acc[KV / 16][4];
 #pragma unroll
     for (int i = 0; i < KV / 16; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;  // heads 2t, 2t+1
-    for (int tile = t_begin + warp; tile < t_end; tile += kWarps) {
+    for (int j = 0;; ++j) {
+        const int tile = t_begin + warp + kWarps * j;
+        if (tile >= t_end) break;
         const int p0 = tile * 16;
-        // 16 rows x 18 16-byte vectors
-        for (int e = lane; e < 16 * (W / 8); e += 32) {
-            const int r = e / (W / 8), cc = (e % (W / 8)) * 8;
-            uint4 v = make_uint4(0, 0, 0, 0);
-            if (p0 + r < n) v = *reinterpret_cast<const uint4*>(cb + static_cast<long long>(p0 + r) * W + cc);
-            *reinterpret_cast<uint4*>(&Cw[warp][r][cc]) = v;
-        }
+        issue(j + kStages - 1);
+        cp_async_wait<kStages - 1>();  // tile j has landed
         __syncwarp();
+        __half (*Ct)[LDQ] = Cw[warp][j % kStages];
         float s[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int kk = 0; kk < W / 16; ++kk) {
             uint32_t a[4];
-            ldsm_x4(a, &Cw[warp][lane & 15][kk * 16 + (lane >> 4) * 8]);
+            ldsm_x4(a, &Ct[lane & 15][kk * 16 + (lane >> 4) * 8]);
             mma16816(s, a, qb[kk][0], qb[kk][1]);
         }
         if (p0 + g >= n) { s[0] = -INFINITY; s[1] = -INFINITY; }
@@ -176,7 +199,7 @@ __global__ void __launch_bounds__(128) decode_attention_mma_kernel(
 #pragma unroll
         for (int mt = 0; mt < KV / 16; ++mt) {
             uint32_t a[4];
-            ldsm_x4_t(a, &Cw[warp][(lane & 7) + ((lane >> 4) << 3)][mt * 16 + ((lane >> 3) & 1) * 8]);
+            ldsm_x4_t(a, &Ct[(lane & 7) + ((lane >> 4) << 3)][mt * 16 + ((lane >> 3) & 1) * 8]);
             mma16816(acc[mt], a, bp[0], bp[1]);
         }
         __syncwarp();
@@ -190,6 +213,8 @@ __global__ void __launch_bounds__(128) decode_attention_mma_kernel(
         Mw[warp][2 * t] = m0; Mw[warp][2 * t + 1] = m1;
         Lw[warp][2 * t] = l0; Lw[warp][2 * t + 1] = l1;
     }
+    cp_async_wait<0>();
+    __syncthreads();  // every warp is done with its ring before it becomes Ow
 #pragma unroll
     for (int mt = 0; mt < KV / 16; ++mt) {
         Ow[warp][2 * t][mt * 16 + g] = acc[mt][0];
@@ -225,26 +250,36 @@ __global__ void __launch_bounds__(128) decode_attention_mma_kernel(
     }
 }
 
-// Merges the nsplit partials of decode_attention_mma_kernel: grid B, block 128.
-__global__ void decode_attention_combine_kernel(const float* __restrict__ part, int nsplit,
+// Merges the nsplit partials of decode_attention_mma_kernel: one warp per (row, head),
+// 4 context columns per lane; grid ceil(B * H / 4), block 128.
+__global__ void decode_attention_combine_kernel(const float* __restrict__ part, int nsplit, int B,
                                                 __half* __restrict__ ctx) {
     using namespace dec;
-    const int b = blockIdx.x;
-    for (int e = threadIdx.x; e < H * KV; e += blockDim.x) {
-        const int hh = e / KV, c = e % KV;
-        const float* pb = part + static_cast<long long>(b) * nsplit * H * (KV + 2) + hh * (KV + 2);
-        float M = -INFINITY;
-        for (int s = 0; s < nsplit; ++s) M = fmaxf(M, pb[s * H * (KV + 2)]);
-        float L = 0.f, O = 0.f;
-        for (int s = 0; s < nsplit; ++s) {
-            const float m = pb[s * H * (KV + 2)];
-            if (m == -INFINITY) continue;
-            const float f = exp2f(m - M);
-            L += f * pb[s * H * (KV + 2) + 1];
-            O += f * pb[s * H * (KV + 2) + 2 + c];
-        }
-        ctx[static_cast<long long>(b) * H * KV + hh * KV + c] = __float2half_rn(O / L);
+    const int wid = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (wid >= B * H) return;
+    const int b = wid / H, hh = wid % H;
+    const float* pb = part + static_cast<long long>(b) * nsplit * H * (KV + 2) + hh * (KV + 2);
+    const long long stride = static_cast<long long>(H) * (KV + 2);
+    float M = -INFINITY;
+    for (int s = 0; s < nsplit; ++s) M = fmaxf(M, pb[s * stride]);
+    float L = 0.f, o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
+    for (int s = 0; s < nsplit; ++s) {
+        const float* ps = pb + s * stride;
+        const float m = ps[0];
+        if (m == -INFINITY) continue;
+        const float f = exp2f(m - M);
+        L += f * ps[1];
+        const float2 a = *reinterpret_cast<const float2*>(ps + 2 + 4 * lane);
+        const float2 c = *reinterpret_cast<const float2*>(ps + 4 + 4 * lane);
+        o0 += f * a.x;
+        o1 += f * a.y;
+        o2 += f * c.x;
+        o3 += f * c.y;
     }
+    const float inv = 1.f / L;
+    __half* out = ctx + static_cast<long long>(b) * H * KV + hh * KV + 4 * lane;
+    *reinterpret_cast<__half2*>(out) = __floats2half2_rn(o0 * inv, o1 * inv);
+    *reinterpret_cast<__half2*>(out + 2) = __floats2half2_rn(o2 * inv, o3 * inv);
 }
 
 } // namespace mm

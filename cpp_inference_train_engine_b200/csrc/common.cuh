@@ -38,9 +38,30 @@ __device__ __forceinline__ float warp_max(float v) {
     return v;
 }
 
+// ops::sigmoid (ops.cpp:65-70), the two-branch form.
+__device__ __forceinline__ float sigmoid_ref(float x) {
+    if (x >= 0.f) return 1.0f / (1.0f + expf(-x));
+    const float e = expf(x);
+    return e / (1.0f + e);
+}
+
 // ------------------------------------------------------------------ shared-memory addresses
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ------------------------------------------------------------------ cp.async (16-byte)
+// Copies 16 bytes global -> shared without a register round trip; `valid` false writes
+// zeros (src-size 0, nothing is read).
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src),
+                 "r"(valid ? 16 : 0)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
 // ------------------------------------------------------------------ mbarrier

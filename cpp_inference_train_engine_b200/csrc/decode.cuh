@@ -108,10 +108,13 @@ inline void decode_step(Context& cx) {
             const double bytes = static_cast<double>(B) * ((cx.dec_len + 1.0) * kvw * 2 + c.H * kvw * 4.0 + c.H * c.kvr * 2.0);
             if (c.kvr == dec::KV && c.rope == dec::R && c.H == dec::H) {
                 const int ns = decode_splits(B, cx.dec_len + 1);
+                set_dynamic_smem<decode_attention_mma_kernel>(dec::kSmem);
                 cudaEvent_t t0 = cx.prof_begin();
-                MM_LAUNCH(decode_attention_mma_kernel, dim3(B, ns), 128, 0, d.qf2, cache_l, (long long)d.Sc * kvw, d.pos,
-                          scale, d.ctx16, d.part);
-                if (ns > 1) MM_LAUNCH(decode_attention_combine_kernel, B, 128, 0, d.part, ns, d.ctx16);
+                MM_LAUNCH(decode_attention_mma_kernel, dim3(B, ns), 128, dec::kSmem, d.qf2, cache_l, (long long)d.Sc * kvw,
+                          d.pos, scale, d.ctx16, d.part);
+                if (ns > 1)
+                    MM_LAUNCH(decode_attention_combine_kernel, blocks_for(static_cast<long long>(B) * dec::H * 32, 128), 128, 0,
+                              d.part, ns, B, d.ctx16);
                 cx.prof_end(kKDecodeAttn, t0, bytes);
             } else if (c.kvr == 128)
                 MM_LAUNCH_TIMED(kKDecodeAttn, bytes, (decode_attention_kernel<128, 16>), B, 32 * c.H, smem, d.qf2, cache_l,
@@ -128,8 +131,14 @@ inline void decode_step(Context& cx) {
         }
         launch_rmsnorm(cx, d.res, c.d, cx.W(l, kFfnNorm), B, c.d, (float*)nullptr, 0LL, d.h2, ld_d);
         const int ld_gu = cx.d16(2 * c.dff), ld_ff = cx.d16(c.dff);
-        gemm(cx, B, 2 * c.dff, c.d, {d.h2, ld_d, false}, {p.Wgu, p.ldgu, true}, {d.gu, ld_gu, kOutF16});
-        launch_swiglu(cx, d.gu, d.gu + c.dff, ld_gu, B, c.dff, d.gated, ld_ff);
+        if (c.dff % 8) {
+            gemm(cx, B, 2 * c.dff, c.d, {d.h2, ld_d, false}, {p.Wgu, p.ldgu, true}, {d.gu, ld_gu, kOutF16});
+            launch_swiglu(cx, d.gu, d.gu + c.dff, ld_gu, B, c.dff, d.gated, ld_ff);
+        } else {
+            GemmOutSpec o{d.gated, ld_ff, kOutF16};
+            o.glu_n = c.dff;
+            gemm(cx, B, c.dff, c.d, {d.h2, ld_d, false}, {p.Wgu, p.ldgu, true}, o);
+        }
         {
             GemmOutSpec o{d.x, c.d, kOutF32};
             o.residual = d.res;

@@ -37,6 +37,19 @@ struct GemmArgs {
     int* err;
     int k_tiles_per_split;  // split-K: tiles of split z cover k-tiles [z*per, (z+1)*per); 0 = all
     int split_rows;         // split-K: rows of the output map per split (M rounded up to 128)
+    // Row log-sum-exp partials (the vocabulary head, fp32 output, no split): per output
+    // tile and row, (max, sum exp(x - max)) over the tile's columns into
+    // lse_part[n_tile * M + row], and the value in column targets[row] into tgt_logit[row]
+    // (written by the one tile holding that column). no_store skips the output itself.
+    float2* lse_part;
+    const uint16_t* targets;
+    float* tgt_logit;
+    int no_store;
+    // SwiGLU output (B MN-major, fp16 out): B holds [gate | up] with the up half starting
+    // glu_n columns after the gate half; a BN-wide tile multiplies gate columns
+    // [n0, n0 + BN/2) and the matching up columns into one accumulator and stores
+    // gate * sigmoid(gate) * up for output columns [n0, n0 + BN/2). 0 = off.
+    int glu_n;
 };
 
 constexpr int kGemmBM = 128;
@@ -73,7 +86,8 @@ __global__ void __launch_bounds__(192, 1)
     const int num_k = (g.K + kGemmBK - 1) / kGemmBK;
     const int per = g.k_tiles_per_split > 0 ? g.k_tiles_per_split : num_k;
     const int splits = (num_k + per - 1) / per;
-    const int tiles_n = (g.N + BN - 1) / BN, tiles_m = (g.M + kGemmBM - 1) / kGemmBM;
+    const int TW = g.glu_n ? BN / 2 : BN;  // output columns per tile
+    const int tiles_n = (g.N + TW - 1) / TW, tiles_m = (g.M + kGemmBM - 1) / kGemmBM;
     const int tiles = tiles_n * tiles_m * splits;
 
     if (warp == 0) {
@@ -105,7 +119,7 @@ __global__ void __launch_bounds__(192, 1)
         bool ok = true;
         for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
             const int z = tile / (tiles_n * tiles_m), mn = tile % (tiles_n * tiles_m);
-            const int m0 = (mn / tiles_n) * kGemmBM, n0 = (mn % tiles_n) * BN;
+            const int m0 = (mn / tiles_n) * kGemmBM, n0 = (mn % tiles_n) * TW;
             const int kb = z * per, ke = min(num_k, kb + per);
             for (int kt = kb; kt < ke; ++kt, ++it) {
                 const int s = it % STAGES;
@@ -125,8 +139,11 @@ __global__ void __launch_bounds__(192, 1)
                     tma_load_2d(sb, &tmB, &full[s], k0, n0);
                 } else {
 #pragma unroll
-                    for (int j = 0; j < BN / 64; ++j)
-                        tma_load_2d(sb + j * 8192, &tmB, &full[s], n0 + 64 * j, k0);
+                    for (int j = 0; j < BN / 64; ++j) {
+                        const int col = !g.glu_n ? n0 + 64 * j
+                                                 : (j < BN / 128 ? n0 + 64 * j : g.glu_n + n0 + 64 * (j - BN / 128));
+                        tma_load_2d(sb + j * 8192, &tmB, &full[s], col, k0);
+                    }
                 }
             }
         }
@@ -135,9 +152,9 @@ __global__ void __launch_bounds__(192, 1)
         bool ok = true;
         for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++j) {
             const int z = tile / (tiles_n * tiles_m), mn = tile % (tiles_n * tiles_m);
-            const int n0 = (mn % tiles_n) * BN;
+            const int n0 = (mn % tiles_n) * TW;
             const int kb = z * per, ke = min(num_k, kb + per);
-            const int n_mma = min(BN, ((g.N - n0) + 15) / 16 * 16);
+            const int n_mma = g.glu_n ? BN : min(BN, ((g.N - n0) + 15) / 16 * 16);
             const uint32_t idesc = umma_idesc_f16(g.bf16 != 0, g.a_mn != 0, g.b_mn != 0, kGemmBM, n_mma);
             const int buf = j & 1;
             if (!mbar_wait_bounded(&acc_empty[buf], ((j >> 1) & 1) ^ 1, g.err)) break;
@@ -171,7 +188,7 @@ __global__ void __launch_bounds__(192, 1)
         int j = 0;
         for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++j) {
             const int z = tile / (tiles_n * tiles_m), mn = tile % (tiles_n * tiles_m);
-            const int m0 = (mn / tiles_n) * kGemmBM, n0 = (mn % tiles_n) * BN;
+            const int m0 = (mn / tiles_n) * kGemmBM, n0 = (mn % tiles_n) * TW;
             const int n_mma = min(BN, ((g.N - n0) + 15) / 16 * 16);
             const int buf = j & 1;
             if (!mbar_wait_bounded(&acc_full[buf], (j >> 1) & 1, g.err)) break;
@@ -180,6 +197,53 @@ __global__ void __launch_bounds__(192, 1)
             const int row = row0 + lane;
             const int map_row0 = row0 + (g.k_tiles_per_split > 0 ? z * g.split_rows : 0);
             const uint32_t src = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * BN);
+            if (g.glu_n) {
+                // accumulator columns [0, TW) gate, [TW, 2 TW) up; 64 fp16 outputs per staged row
+                for (int c = 0; c < TW; c += 64) {
+                    if (lane == 0) bulk_wait_read0();
+                    __syncwarp();
+                    uint8_t* rowp = stage + lane * 128;
+#pragma unroll
+                    for (int sub = 0; sub < 2; ++sub) {
+                        float gv[32], uv[32];
+                        tmem_ld32_nowait(src + static_cast<uint32_t>(c + 32 * sub), gv);
+                        tmem_ld32_nowait(src + static_cast<uint32_t>(TW + c + 32 * sub), uv);
+                        tmem_wait_ld();
+                        if (sub == 1 && c + 64 >= TW) {
+                            tc_fence_before();
+                            __syncwarp();
+                            if (lane == 0) mbar_arrive(&acc_empty[buf]);
+                        }
+#pragma unroll
+                        for (int ch = 0; ch < 4; ++ch) {
+                            uint32_t w[4];
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                const int i = ch * 8 + 2 * e;
+                                // g * sigmoid(g) = g / (1 + e^-g), branch-free on the SFU
+                                // (the result is rounded to fp16)
+                                const float ga = gv[i] * alpha, gb = gv[i + 1] * alpha;
+                                const float a = __fdividef(ga, 1.f + __expf(-ga)) * (uv[i] * alpha);
+                                const float b = __fdividef(gb, 1.f + __expf(-gb)) * (uv[i + 1] * alpha);
+                                const __half2 h = __floats2half2_rn(a, b);
+                                w[e] = *reinterpret_cast<const uint32_t*>(&h);
+                            }
+                            const int cc = sub * 4 + ch;
+                            *reinterpret_cast<uint4*>(rowp + ((cc ^ (lane & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+                        }
+                    }
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_2d(&tmC, stage, n0 + c, map_row0);
+                        bulk_commit();
+                    }
+                }
+                continue;
+            }
+            // online (max, sum of exp) over this tile's columns of the row, and its target
+            float run_m = -INFINITY, run_s = 0.f, run_t = 0.f;
+            const int tg = (g.lse_part && row < g.M) ? static_cast<int>(g.targets[row]) : -1;
             for (int c = 0; c < n_mma; c += CH) {
                 float v[64];
                 tmem_ld32_nowait(src + static_cast<uint32_t>(c), v);
@@ -199,6 +263,24 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
                     for (int i = 0; i < 32; ++i)
                         if (col0 + i < g.N) v[i] += r[i];
+                }
+                if (g.lse_part) {  // fp32 output: 32 columns per chunk
+                    float cm = -INFINITY;
+#pragma unroll
+                    for (int i = 0; i < 32; ++i)
+                        if (col0 + i < g.N) cm = fmaxf(cm, v[i]);
+                    const float nm = fmaxf(run_m, cm);  // finite: every chunk holds a column < N
+                    float add = 0.f;
+#pragma unroll
+                    for (int i = 0; i < 32; ++i)
+                        if (col0 + i < g.N) add += __expf(v[i] - nm);
+                    run_s = (run_m == -INFINITY ? 0.f : run_s * __expf(run_m - nm)) + add;
+                    run_m = nm;
+                    const int rel = tg - col0;
+#pragma unroll
+                    for (int i = 0; i < 32; ++i)
+                        if (rel == i) run_t = v[i];
+                    if (g.no_store) continue;
                 }
                 // the previous store from this staging tile must have finished reading it
                 if (lane == 0) bulk_wait_read0();
@@ -234,6 +316,10 @@ __global__ void __launch_bounds__(192, 1)
                     else tma_store_2d(&tmC, stage, col0, map_row0);
                     bulk_commit();
                 }
+            }
+            if (g.lse_part && row < g.M) {
+                g.lse_part[static_cast<long long>(n0 / BN) * g.M + row] = make_float2(run_m, run_s);
+                if (tg >= n0 && tg < n0 + BN) g.tgt_logit[row] = run_t;
             }
         }
         if (lane == 0) bulk_wait0();

@@ -162,12 +162,6 @@ __global__ void assemble_k_kernel(const float* __restrict__ k_nope, long long ld
     k[t * ldk + c] = __float2half_rn(v);
 }
 
-// ops::sigmoid (ops.cpp:65-70), the two-branch form.
-__device__ __forceinline__ float sigmoid_ref(float x) {
-    if (x >= 0.f) return 1.0f / (1.0f + expf(-x));
-    const float e = expf(x);
-    return e / (1.0f + e);
-}
 
 // gated = gate * sigmoid(gate) * up (ops.cpp:71-77).
 __global__ void swiglu_kernel(const __half* __restrict__ gate, const __half* __restrict__ up,

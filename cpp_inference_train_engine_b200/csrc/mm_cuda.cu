@@ -461,9 +461,12 @@ int mm_cuda_decode_attention(mm_cuda_ctx* h, const float* q, const void* cache, 
         if (splits > 1)
             part = static_cast<float*>(cx.stage.get(sizeof(float) * static_cast<size_t>(batch) * splits * mm::dec::H *
                                                     (mm::dec::KV + 2)));
-        MM_LAUNCH(mm::decode_attention_mma_kernel, dim3(batch, splits), 128, 0, q, static_cast<const __half*>(cache),
-                  cache_seq_stride, pos, scale, static_cast<__half*>(out), part);
-        if (splits > 1) MM_LAUNCH(mm::decode_attention_combine_kernel, batch, 128, 0, part, splits, static_cast<__half*>(out));
+        mm::set_dynamic_smem<mm::decode_attention_mma_kernel>(mm::dec::kSmem);
+        MM_LAUNCH(mm::decode_attention_mma_kernel, dim3(batch, splits), 128, mm::dec::kSmem, q,
+                  static_cast<const __half*>(cache), cache_seq_stride, pos, scale, static_cast<__half*>(out), part);
+        if (splits > 1)
+            MM_LAUNCH(mm::decode_attention_combine_kernel, mm::blocks_for(static_cast<long long>(batch) * mm::dec::H * 32, 128),
+                      128, 0, part, splits, batch, static_cast<__half*>(out));
         mm::check_device(cx, "decode_attention");
     });
 }
@@ -477,9 +480,16 @@ int mm_decode_attention_noalloc(const float* q, const void* cache, int64_t cache
     float* part = static_partials_address();
     if (!part) return MM_GPU_ERROR;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    mm::decode_attention_mma_kernel<<<dim3(batch, splits), 128, 0, s>>>(
+    try {
+        mm::set_dynamic_smem<mm::decode_attention_mma_kernel>(mm::dec::kSmem);
+    } catch (...) {
+        return MM_GPU_ERROR;
+    }
+    mm::decode_attention_mma_kernel<<<dim3(batch, splits), 128, mm::dec::kSmem, s>>>(
         q, static_cast<const __half*>(cache), cache_seq_stride, pos, scale, static_cast<__half*>(out), part);
-    if (splits > 1) mm::decode_attention_combine_kernel<<<batch, 128, 0, s>>>(part, splits, static_cast<__half*>(out));
+    if (splits > 1)
+        mm::decode_attention_combine_kernel<<<mm::blocks_for(static_cast<long long>(batch) * mm::dec::H * 32, 128), 128, 0, s>>>(
+            part, splits, batch, static_cast<__half*>(out));
     if (cudaGetLastError() != cudaSuccess) return MM_GPU_ERROR;
     if (cudaStreamSynchronize(s) != cudaSuccess) return MM_GPU_ERROR;
     return MM_OK;

@@ -72,6 +72,8 @@ template <class A> void plan_workspace(Context& cx, A& a, int T, bool tape) {
     w.hf = a.template take<float>(t * c.d);
     w.h3 = a.template take<__half>(t * cx.d16(3 * c.d));
     w.logits = a.template take<float>(t * c.V);
+    w.lse_part = a.template take<float2>(t * ((c.V + 63) / 64));
+    w.tgt_logit = a.template take<float>(t);
     w.lp = a.template take<float>(t);
     w.lse_v = a.template take<float>(t);
     w.tokens = a.template take<uint16_t>(t);
@@ -310,8 +312,15 @@ inline void forward_chunk(Context& cx, int Bc, int S, bool tape, VocabMode vm, b
         // feed-forward block
         launch_rmsnorm(cx, b.res, c.d, cx.W(l, kFfnNorm), T, c.d, (float*)nullptr, 0LL, b.h2, ld_d);
         const int ld_gu = cx.d16(2 * c.dff);
-        gemm(cx, T, 2 * c.dff, c.d, {b.h2, ld_d, false}, {pw.Wgu, pw.ldgu, true}, {b.gate, ld_gu, kOutF16});
-        launch_swiglu(cx, b.gate, b.up, ld_gu, T, c.dff, b.gated, ld_ff);
+        if (tape || c.dff % 8) {
+            // the backward needs gate and up themselves
+            gemm(cx, T, 2 * c.dff, c.d, {b.h2, ld_d, false}, {pw.Wgu, pw.ldgu, true}, {b.gate, ld_gu, kOutF16});
+            launch_swiglu(cx, b.gate, b.up, ld_gu, T, c.dff, b.gated, ld_ff);
+        } else {
+            GemmOutSpec o{b.gated, ld_ff, kOutF16};
+            o.glu_n = c.dff;
+            gemm(cx, T, c.dff, c.d, {b.h2, ld_d, false}, {pw.Wgu, pw.ldgu, true}, o);
+        }
         {
             GemmOutSpec o{x_next, c.d, kOutF32};
             o.residual = b.res;
@@ -327,10 +336,18 @@ inline void forward_chunk(Context& cx, int Bc, int S, bool tape, VocabMode vm, b
     if (vm == kVocabAll) {
         MM_LAUNCH(split3_gather_kernel, blocks_for((long long)T * c.d, 256), 256, 0, w.hf, c.d, T, 1, 0, w.h3, (long long)ld3);
         lo.out = w.logits;
-        gemm(cx, T, c.V, 3 * c.d, {w.h3, ld3, false}, {cx.E3(), cx.E3L(), false}, lo);
+        if (with_targets) {
+            // log-softmax fused into the product: per-tile row partials, then one combine;
+            // the logits themselves are stored only for the backward (tape)
+            lo.lse_part = w.lse_part;
+            lo.targets = w.targets;
+            lo.tgt_logit = w.tgt_logit;
+            lo.no_store = !tape;
+        }
+        const int bn = gemm(cx, T, c.V, 3 * c.d, {w.h3, ld3, false}, {cx.E3(), cx.E3L(), false}, lo);
         if (with_targets)
-            MM_LAUNCH_TIMED(kKLogsoftmax, 4.0 * T * c.V, logsoftmax_rows_kernel, T, 256, 0, w.logits, (long long)c.V, c.V,
-                            w.targets, T, w.lp, w.lse_v, cx.d_err);
+            MM_LAUNCH_TIMED(kKLogsoftmax, 8.0 * T * ((c.V + bn - 1) / bn), lse_combine_kernel, blocks_for(T, 256), 256, 0,
+                            w.lse_part, (c.V + bn - 1) / bn, T, w.tgt_logit, w.lp, w.lse_v, cx.d_err);
     } else {
         MM_LAUNCH(split3_gather_kernel, blocks_for((long long)Bc * c.d, 256), 256, 0, w.hf, c.d, Bc, S, S - 1, w.h3,
                   (long long)ld3);

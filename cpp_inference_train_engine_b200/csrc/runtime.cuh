@@ -3,6 +3,8 @@
 #pragma once
 #include <cudaTypedefs.h>
 
+#include <atomic>
+
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
@@ -142,6 +144,8 @@ struct Workspace {
     float* hf;          // [T][d] final norm output
     __half* h3;         // [T][ld16(3d)]
     float* logits;      // [T][V]
+    float2* lse_part;   // [ceil(V / 64)][T] per-tile (max, sum exp) of the vocabulary head
+    float* tgt_logit;   // [T]
     float* lp;          // [T]
     float* lse_v;       // [T]
     uint16_t* tokens;   // [T]
@@ -419,6 +423,15 @@ struct GemmOutSpec {
     long long ldr = 0;
     float alpha = 1.f;
     const float* alpha_ptr = nullptr;
+    // row log-sum-exp partials of an fp32 product (GemmArgs::lse_part); gemm() returns the
+    // tile width, so the partials are [ceil(N / width)][M]
+    float2* lse_part = nullptr;
+    const uint16_t* targets = nullptr;
+    float* tgt_logit = nullptr;
+    bool no_store = false;
+    // SwiGLU output (GemmArgs::glu_n): N = output columns, B holds [gate | up] with the up
+    // half glu_n columns after the gate half; fp16 output, B MN-major
+    int glu_n = 0;
 };
 
 inline int sm_count() {
@@ -432,18 +445,27 @@ inline int sm_count() {
     return n;
 }
 
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) for a kernel, once per device.
+template <auto Kernel>
+inline void set_dynamic_smem(int bytes) {
+    static std::atomic<unsigned long long> done{0};
+    int dev = 0;
+    MM_CUDA_CHECK(cudaGetDevice(&dev));
+    const unsigned long long bit = 1ull << (dev & 63);
+    if (done.load() & bit) return;
+    MM_CUDA_CHECK(cudaFuncSetAttribute(Kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    done.fetch_or(bit);
+}
+
 template <int BN, int STAGES>
 inline void launch_gemm_bn(Context& cx, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
                            const GemmArgs& ga) {
     using C = GemmCfg<BN, STAGES>;
-    static bool configured = false;
-    if (!configured) {
-        MM_CUDA_CHECK(cudaFuncSetAttribute(gemm_tc_kernel<BN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
-        configured = true;
-    }
+    set_dynamic_smem<gemm_tc_kernel<BN, STAGES>>(C::SMEM);
     const long long num_k = (ga.K + kGemmBK - 1) / kGemmBK;
     const long long per = ga.k_tiles_per_split > 0 ? ga.k_tiles_per_split : num_k;
-    const long long tiles = static_cast<long long>((ga.N + BN - 1) / BN) * ((ga.M + kGemmBM - 1) / kGemmBM) *
+    const int tw = ga.glu_n ? BN / 2 : BN;
+    const long long tiles = static_cast<long long>((ga.N + tw - 1) / tw) * ((ga.M + kGemmBM - 1) / kGemmBM) *
                             ((num_k + per - 1) / per);
     // resident CTAs per SM: two TMEM accumulators of BN columns each out of 512, and smem
     const int per_sm = std::max(1, std::min(512 / (2 * BN), (227 * 1024) / C::SMEM));
@@ -462,7 +484,7 @@ inline void launch_gemm_bn(Context& cx, const CUtensorMap& ta, const CUtensorMap
 }
 
 // D[M,N] = alpha * A * B (+ residual | += D). bf16 selects bf16 operands.
-void gemm(Context& cx, int M, int N, int K, Opnd A, Opnd B, const GemmOutSpec& o, bool bf16 = false);
+int gemm(Context& cx, int M, int N, int K, Opnd A, Opnd B, const GemmOutSpec& o, bool bf16 = false);
 
 // ------------------------------------------------------------------ small launch helpers
 inline unsigned blocks_for(long long n, int threads) {

@@ -20,9 +20,13 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ part, int splits,
     out[r * ldc + c] += a * s;
 }
 
-inline void gemm(Context& cx, int M, int N, int K, Opnd A, Opnd B, const GemmOutSpec& o_in, bool bf16) {
-    if (M <= 0 || N <= 0 || K <= 0) return;
+inline int gemm(Context& cx, int M, int N, int K, Opnd A, Opnd B, const GemmOutSpec& o_in, bool bf16) {
+    if (M <= 0 || N <= 0 || K <= 0) return 0;
     GemmOutSpec o = o_in;
+    if (o.lse_part && (o.kind != kOutF32 || o.residual || !o.targets || !o.tgt_logit))
+        fail(MM_INVALID_ARGUMENT, "log-sum-exp epilogue needs a plain fp32 product with targets");
+    if (o.glu_n && (o.kind != kOutF16 || o.residual || o.lse_part || !B.mn || o.glu_n < N))
+        fail(MM_INVALID_ARGUMENT, "SwiGLU epilogue needs an fp16 product with [gate | up] MN-major weights");
     if (o.residual) {
         // out = alpha * A B + residual  ==  out := residual, then out += alpha * A B through the
         // TMA reduce-add epilogue (the residual moves as one coalesced device copy).
@@ -38,21 +42,24 @@ inline void gemm(Context& cx, int M, int N, int K, Opnd A, Opnd B, const GemmOut
     const bool split_candidate = o.kind == kOutF32Acc && num_k_all >= 32 && N % 4 == 0 &&
                                  tiles_m * ((N + 63) / 64) < sm_count();
     int BN = 64;
-    if (N >= 256 && (split_candidate || tiles_m * ((N + 255) / 256) >= 148)) BN = 256;
+    if (o.glu_n) BN = 256;  // 128 gate + 128 up columns per tile
+    else if (N >= 256 && (split_candidate || tiles_m * ((N + 255) / 256) >= 148)) BN = 256;
     else if (tiles_m * ((N + 127) / 128) >= 120 && N > 64) BN = 128;
+    const int nb = o.glu_n ? o.glu_n + N : N;  // columns of B
     const CUtensorMap& ta = A.mn ? tensor_map(A.p, bf16, M, K, A.ld, 64, 64)
                                  : tensor_map(A.p, bf16, K, M, A.ld, 64, kGemmBM);
-    const CUtensorMap& tb = B.mn ? tensor_map(B.p, bf16, N, K, B.ld, 64, 64)
-                                 : tensor_map(B.p, bf16, K, N, B.ld, 64, BN);
+    const CUtensorMap& tb = B.mn ? tensor_map(B.p, bf16, nb, K, B.ld, 64, 64)
+                                 : tensor_map(B.p, bf16, K, nb, B.ld, 64, BN);
     GemmArgs ga{M, N, K, A.mn ? 1 : 0, B.mn ? 1 : 0, bf16 ? 1 : 0, o.kind,
-                o.residual, o.ldr, o.alpha, o.alpha_ptr, cx.d_err, 0, 0};
+                o.residual, o.ldr, o.alpha, o.alpha_ptr, cx.d_err, 0, 0,
+                o.lse_part, o.targets, o.tgt_logit, (o.lse_part && o.no_store) ? 1 : 0, o.glu_n};
     // Split-K for accumulating products with few output tiles over a long K (the weight
     // gradients, K = tokens): each K slice stores its fp32 partial, then one reduction adds
     // them in order into the destination.
     const long long tiles = tiles_m * ((N + BN - 1) / BN);
     const int num_k = (K + kGemmBK - 1) / kGemmBK;
     int splits = 1;
-    if (o.kind == kOutF32Acc && !o.residual && tiles < sm_count() && num_k >= 32 && N % 4 == 0) {
+    if (!o.glu_n && o.kind == kOutF32Acc && !o.residual && tiles < sm_count() && num_k >= 32 && N % 4 == 0) {
         splits = static_cast<int>(std::min<long long>((2LL * sm_count() + tiles - 1) / tiles, num_k / 8));
         splits = std::max(1, std::min(splits, 32));
     }
@@ -96,6 +103,7 @@ inline void gemm(Context& cx, int M, int N, int K, Opnd A, Opnd B, const GemmOut
                 o.alpha_ptr);
         ++cx.launches;
     }
+    return BN;
 }
 
 inline Dims dims_from(const mm_model_desc& d) {

@@ -54,6 +54,30 @@ __global__ void logsoftmax_rows_kernel(const float* __restrict__ logits, long lo
     }
 }
 
+// Combines the per-tile (max, sum exp) partials of the vocabulary GEMM's log-sum-exp
+// epilogue, part[j * T + t] for j < ntiles: lse[t] = M + log(sum_j s_j exp(m_j - M)) with the
+// sum in double, lp[t] = target logit - lse[t]. One thread per row.
+__global__ void lse_combine_kernel(const float2* __restrict__ part, int ntiles, int T,
+                                   const float* __restrict__ tgt_logit, float* __restrict__ lp,
+                                   float* __restrict__ lse, int* err) {
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= T) return;
+    float mx = -INFINITY;
+    for (int j = 0; j < ntiles; ++j) mx = fmaxf(mx, part[static_cast<long long>(j) * T + t].x);
+    double z = 0.0;
+    for (int j = 0; j < ntiles; ++j) {
+        const float2 p = part[static_cast<long long>(j) * T + t];
+        z += static_cast<double>(p.y) * static_cast<double>(__expf(p.x - mx));
+    }
+    const double l = log(z) + static_cast<double>(mx);
+    if (lse) lse[t] = static_cast<float>(l);
+    if (lp) {
+        const double v = static_cast<double>(tgt_logit[t]) - l;
+        if (!isfinite(v)) raise_error(err, kErrNonfinite);
+        lp[t] = static_cast<float>(v);
+    }
+}
+
 // g[t, j] = scale * coef[t] * (exp(l - lse) - [j == target]) in fp16, [T][ldg].
 __global__ void vocab_grad_kernel(const float* __restrict__ logits, long long ld, int V,
                                   const uint16_t* __restrict__ target, const float* __restrict__ lse,

@@ -1,0 +1,118 @@
+"""Rollout decode throughput and the latent decode-attention kernel alone.
+
+Decode mode (default) runs the batched rollout of the 35.8M model without its log-prob
+pass: B random prompts of --prompt ids, prefill, then --new tokens per row (greedy or
+temperature sampling), and reports the decode phase (all steps after the first token,
+which comes from the prefill logits) as tokens/s and against the HBM roofline of
+2·P weight bytes (fp16) plus B·ctx·2880 cache bytes (latent 128 + rope 16 in fp16 over 10
+layers) per step, ctx averaged over the steps. BASELINE config 2 is
+``--batch 1,16,64 --prompt 1024 --new 128``; config 4's decode is ``--batch 2048 --prompt 128
+--new 256``.
+
+Attention mode times one launch of the split latent attention (mm_cuda_decode_attention)
+over a synthetic fp16 cache of --ctx positions per row:
+
+    python -m cpp_inference_train_engine_b200.decode_bench --attention --batch 2048 --ctx 256
+"""
+import argparse
+import json
+
+
+def _peak_hbm():
+    import os
+    p = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+def attention(args):
+    import torch
+
+    import cpp_inference_train_engine_b200 as E
+    H, KV, W = 8, 128, 144
+    ex = E.CudaExecution(E.MLA36M)
+    stream = torch.cuda.ExternalStream(ex.stream)
+    g = torch.Generator(device="cuda").manual_seed(1)
+    for B in args.batch:
+        Sc = args.ctx
+        q = torch.randn(B, H, W, device="cuda", generator=g)
+        cache = (torch.randn(B, Sc, W, device="cuda", generator=g) * 0.5).half()
+        pos = torch.full((B,), args.ctx - 1, device="cuda", dtype=torch.int32)
+        out = torch.empty(B, H * KV, device="cuda", dtype=torch.half)
+        splits = args.splits or max(1, min((296 + B - 1) // B, (args.ctx + 63) // 64, 16))
+        torch.cuda.synchronize()
+        times = []
+        for it in range(args.warmup + args.iters):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            ex.decode_attention(q.data_ptr(), cache.data_ptr(), Sc * W, pos.data_ptr(), B, splits, 0.125,
+                                out.data_ptr())
+            e1.record(stream)
+            torch.cuda.synchronize()
+            if it >= args.warmup:
+                times.append(e0.elapsed_time(e1))
+        ms = sorted(times)[len(times) // 2]
+        byts = B * args.ctx * W * 2 + B * H * W * 4 + B * H * KV * 2
+        peak, src = _peak_hbm()
+        print(json.dumps({"kernel": "decode_attention", "batch": B, "ctx": args.ctx, "splits": splits,
+                          "us": ms * 1e3, "gbs": byts / (ms / 1e3) / 1e9,
+                          "hbm_frac": byts / (ms / 1e3) / 1e9 / peak, "peak_source": src}))
+    ex.close()
+
+
+def decode(args):
+    import numpy as np
+
+    import cpp_inference_train_engine_b200 as E
+    from cpp_inference_train_engine_b200.config import MLA36M
+    from cpp_inference_train_engine_b200.rng import Rng
+
+    cfg = MLA36M
+    P = E.parameter_count(cfg)
+    ex = E.make_execution(cfg, E.init_params(cfg, 0))
+    peak, src = _peak_hbm()
+    for B in args.batch:
+        r = Rng(2)
+        prompts = np.array([[r.bounded(cfg.vocab_size) for _ in range(args.prompt)] for _ in range(B)],
+                           np.uint16)
+        r1 = Rng(1)
+        seeds = np.array([r1.next() for _ in range(B)], np.uint64)
+        S = args.prompt + args.new
+        for temp in args.temperature:
+            for it in range(args.warmup + 1):
+                if it == args.warmup:
+                    ex.profile(1)
+                ex.rollout(prompts, args.new, S, seeds, temp, with_batches=False)
+            prof = ex.profile(0)
+            ms = prof["decode"][0] + prof["sample"][0]
+            steps = args.new - 1
+            ctx = args.prompt + (args.new - 1) / 2.0  # mean positions attended per step
+            byts = steps * (2.0 * P + B * ctx * 2880.0)
+            print(json.dumps({"mode": "decode", "batch": B, "prompt": args.prompt, "new": args.new,
+                              "temperature": temp, "decode_ms": ms, "ms_per_step": ms / steps,
+                              "tok_s": B * steps / (ms / 1e3),
+                              "hbm_roofline_frac": byts / (ms / 1e3) / 1e9 / peak, "peak_source": src,
+                              "prefill_ms": prof["prefill"][0]}))
+    ex.close()
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--attention", action="store_true")
+    ap.add_argument("--batch", type=lambda s: [int(x) for x in s.split(",")], default=[1, 16, 64])
+    ap.add_argument("--prompt", type=int, default=1024)
+    ap.add_argument("--new", type=int, default=128)
+    ap.add_argument("--temperature", type=lambda s: [float(x) for x in s.split(",")], default=[0.0, 1.0])
+    ap.add_argument("--ctx", type=int, default=256)
+    ap.add_argument("--splits", type=int, default=0)
+    ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=2)
+    args = ap.parse_args(argv)
+    attention(args) if args.attention else decode(args)
+
+
+if __name__ == "__main__":
+    main()

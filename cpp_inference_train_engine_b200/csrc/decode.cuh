@@ -124,12 +124,11 @@ inline void decode_step(Context& cx) {
                                 (long long)d.Sc * kvw, d.pos, c.H, scale, d.ctx16);
         }
         {
-            GemmOutSpec o{d.res, c.d, kOutF32};
-            o.residual = d.x;
+            GemmOutSpec o{d.x, c.d, kOutF32Acc};  // residual stream updated in place
             o.ldr = c.d;
             gemm(cx, B, c.d, c.H * c.kvr, {d.ctx16, c.H * c.kvr, false}, {p.Wo, p.ldo, true}, o);
         }
-        launch_rmsnorm(cx, d.res, c.d, cx.W(l, kFfnNorm), B, c.d, (float*)nullptr, 0LL, d.h2, ld_d);
+        launch_rmsnorm(cx, d.x, c.d, cx.W(l, kFfnNorm), B, c.d, (float*)nullptr, 0LL, d.h2, ld_d);
         const int ld_gu = cx.d16(2 * c.dff), ld_ff = cx.d16(c.dff);
         if (c.dff % 8) {
             gemm(cx, B, 2 * c.dff, c.d, {d.h2, ld_d, false}, {p.Wgu, p.ldgu, true}, {d.gu, ld_gu, kOutF16});
@@ -140,15 +139,14 @@ inline void decode_step(Context& cx) {
             gemm(cx, B, c.dff, c.d, {d.h2, ld_d, false}, {p.Wgu, p.ldgu, true}, o);
         }
         {
-            GemmOutSpec o{d.x, c.d, kOutF32};
-            o.residual = d.res;
+            GemmOutSpec o{d.x, c.d, kOutF32Acc};
             o.ldr = c.d;
             gemm(cx, B, c.d, c.dff, {d.gated, ld_ff, false}, {cx.S(l, kWdown), cx.SL(l, kWdown), true}, o);
         }
     }
     launch_rmsnorm(cx, d.x, c.d, cx.FinalNorm(), B, c.d, d.hf, c.d, (__half*)nullptr, 0LL);
     const int ld3 = cx.d16(3 * c.d);
-    MM_LAUNCH(split3_gather_kernel, blocks_for((long long)B * c.d, 256), 256, 0, d.hf, c.d, B, 1, 0, d.h3, (long long)ld3);
+    launch_split3(cx, d.hf, c.d, B, 1, 0, d.h3, ld3);
     GemmOutSpec lo{d.logits, c.V, kOutF32};
     lo.alpha = 1.0f / kVocabScale;
     gemm(cx, B, c.V, 3 * c.d, {d.h3, ld3, false}, {cx.E3(), cx.E3L(), false}, lo);

@@ -54,13 +54,18 @@ struct GemmArgs {
 
 constexpr int kGemmBM = 128;
 constexpr int kGemmBK = 64;
-constexpr int kEpiBytes = 4 * 4096;  // one 32-row x 128-byte staging tile per epilogue warp
+// 32-row x 128-byte staging tiles per epilogue warp: with two, a warp fills one while the
+// TMA store of the other is still reading it (the 256-wide tile, one CTA per SM); the
+// narrower tiles keep one so that two CTAs fit on an SM.
+template <int BN> constexpr int epi_bufs() { return BN == 256 ? 2 : 1; }
 
 template <int BN, int STAGES> struct GemmCfg {
     static constexpr int A_BYTES = kGemmBM * 128;
     static constexpr int B_BYTES = BN * 128;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int SMEM = STAGES * STAGE_BYTES + kEpiBytes + 1024 + 256;
+    static constexpr int EPI_BUFS = epi_bufs<BN>();
+    static constexpr int EPI_BYTES = 4 * EPI_BUFS * 4096;
+    static constexpr int SMEM = STAGES * STAGE_BYTES + EPI_BYTES + 1024 + 256;
 };
 
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
@@ -76,7 +81,7 @@ __global__ void __launch_bounds__(192, 1)
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~static_cast<uintptr_t>(1023));
     uint8_t* epi = smem + STAGES * C::STAGE_BYTES;
-    uint64_t* full = reinterpret_cast<uint64_t*>(epi + kEpiBytes);
+    uint64_t* full = reinterpret_cast<uint64_t*>(epi + C::EPI_BYTES);
     uint64_t* empty = full + STAGES;
     uint64_t* acc_full = empty + STAGES;  // [2] MMA -> epilogue
     uint64_t* acc_empty = acc_full + 2;   // [2] epilogue -> MMA (4 warp arrivals)
@@ -181,7 +186,8 @@ __global__ void __launch_bounds__(192, 1)
         }
     } else if (warp >= 2) {
         const int q = warp & 3;
-        uint8_t* stage = epi + (warp - 2) * 4096;
+        uint8_t* stage_base = epi + (warp - 2) * C::EPI_BUFS * 4096;
+        int sbuf = 0;  // staging tile the next chunk fills
         const float alpha = g.alpha * (g.alpha_ptr ? *g.alpha_ptr : 1.0f);
         const bool half_out = g.out_kind >= kOutF16;
         const int CH = half_out ? 64 : 32;  // columns per 128-byte staged row
@@ -200,7 +206,12 @@ __global__ void __launch_bounds__(192, 1)
             if (g.glu_n) {
                 // accumulator columns [0, TW) gate, [TW, 2 TW) up; 64 fp16 outputs per staged row
                 for (int c = 0; c < TW; c += 64) {
-                    if (lane == 0) bulk_wait_read0();
+                    uint8_t* stage = stage_base + sbuf * 4096;
+                    if (C::EPI_BUFS == 2) sbuf ^= 1;
+                    if (lane == 0) {  // the store that last read `stage` is done
+                        if (C::EPI_BUFS == 2) bulk_wait_read1();
+                        else bulk_wait_read0();
+                    }
                     __syncwarp();
                     uint8_t* rowp = stage + lane * 128;
 #pragma unroll
@@ -282,8 +293,13 @@ __global__ void __launch_bounds__(192, 1)
                         if (rel == i) run_t = v[i];
                     if (g.no_store) continue;
                 }
-                // the previous store from this staging tile must have finished reading it
-                if (lane == 0) bulk_wait_read0();
+                // the store issued two chunks ago (from this staging tile) has finished reading it
+                uint8_t* stage = stage_base + sbuf * 4096;
+                if (C::EPI_BUFS == 2) sbuf ^= 1;
+                if (lane == 0) {
+                    if (C::EPI_BUFS == 2) bulk_wait_read1();
+                    else bulk_wait_read0();
+                }
                 __syncwarp();
                 uint8_t* rowp = stage + lane * 128;
                 if (half_out) {

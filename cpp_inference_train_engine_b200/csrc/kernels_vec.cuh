@@ -150,14 +150,22 @@ __global__ void __launch_bounds__(256) rmsnorm_backward_v4_kernel(
     }
 }
 
-// dw[j] += scale * sum_r part[r][j], r in order.
+// dw[j] += scale * sum_r part[r][j] in a fixed order: block (32, 8) covers 32 columns,
+// row group y sums rows y, y + 8, ... and the 8 group sums are added in order.
 __global__ void colsum_kernel(const float* __restrict__ part, int rows, int n, const float* __restrict__ scale,
                               float* __restrict__ dw) {
-    const int j = blockIdx.x * blockDim.x + threadIdx.x;
-    if (j >= n) return;
+    __shared__ float grp[8][33];
+    const int j = blockIdx.x * 32 + threadIdx.x;
     float s = 0.f;
-    for (int r = 0; r < rows; ++r) s += part[static_cast<long long>(r) * n + j];
-    dw[j] += s * (scale ? *scale : 1.0f);
+    if (j < n)
+        for (int r = threadIdx.y; r < rows; r += 8) s += part[static_cast<long long>(r) * n + j];
+    grp[threadIdx.y][threadIdx.x] = s;
+    __syncthreads();
+    if (threadIdx.y == 0 && j < n) {
+        float t = grp[0][threadIdx.x];
+        for (int y = 1; y < 8; ++y) t += grp[y][threadIdx.x];
+        dw[j] += t * (scale ? *scale : 1.0f);
+    }
 }
 
 // SwiGLU forward, 8 columns per thread.

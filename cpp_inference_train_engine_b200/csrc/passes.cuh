@@ -38,6 +38,28 @@ __global__ void split3_gather_kernel(const float* __restrict__ h, int d, int T, 
     h3[t * ld3 + 2 * d + j] = hi;
 }
 
+// split3_gather_kernel, 4 columns per thread (d % 4 == 0, 8-byte aligned h3 rows).
+__global__ void split3_gather_v4_kernel(const float* __restrict__ h, int d, int T, int mul, int add,
+                                        __half* __restrict__ h3, long long ld3) {
+    const int nv = d >> 2;
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= T * nv) return;
+    const int t = i / nv, j = (i - t * nv) << 2;
+    const float4 v = *reinterpret_cast<const float4*>(h + (static_cast<long long>(t) * mul + add) * d + j);
+    const float f[4] = {v.x, v.y, v.z, v.w};
+    __half hi[4], lo[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        hi[k] = __float2half_rn(f[k]);
+        lo[k] = __float2half_rn(f[k] - __half2float(hi[k]));
+    }
+    __half* row = h3 + t * ld3;
+    const uint2 H = *reinterpret_cast<const uint2*>(hi), L = *reinterpret_cast<const uint2*>(lo);
+    *reinterpret_cast<uint2*>(row + j) = H;
+    *reinterpret_cast<uint2*>(row + d + j) = L;
+    *reinterpret_cast<uint2*>(row + 2 * d + j) = H;
+}
+
 template <class A> void plan_workspace(Context& cx, A& a, int T, bool tape) {
     Workspace& w = cx.ws;
     const Dims& c = cx.c;
@@ -186,7 +208,7 @@ inline void launch_rmsnorm_backward(Context& cx, const float* x, long long ldx, 
     else
         MM_LAUNCH(rmsnorm_backward_v4_kernel<8>, kNormBlocks, 256, smem, x, ldx, w, dy, lddy, add, ldadd, T, n, eps,
                   dx32, lddx, dx16, lddx16, cx.ws.norm_part);
-    MM_LAUNCH(colsum_kernel, blocks_for(n, 256), 256, 0, cx.ws.norm_part, kNormBlocks, n, scale, dw);
+    MM_LAUNCH(colsum_kernel, (n + 31) / 32, dim3(32, 8), 0, cx.ws.norm_part, kNormBlocks, n, scale, dw);
 }
 
 inline void launch_swiglu(Context& cx, const __half* gate, const __half* up, long long ld, int T, int n, __half* out,
@@ -227,6 +249,15 @@ inline void launch_assemble_k(Context& cx, const float* k_nope, long long ldn, c
     else
         MM_LAUNCH(assemble_k_kernel, blocks_for(static_cast<long long>(T) * c.H * qk, 256), 256, 0, k_nope, ldn, k_rope,
                   T, c.H, c.nope, c.rope, k, ldk);
+}
+
+inline void launch_split3(Context& cx, const float* h, int d, int T, int mul, int add, __half* h3, long long ld3) {
+    if (d % 4 == 0 && ld3 % 4 == 0 && al16(h) && al8(h3))
+        MM_LAUNCH(split3_gather_v4_kernel, blocks_for(static_cast<long long>(T) * (d / 4), 256), 256, 0, h, d, T, mul,
+                  add, h3, ld3);
+    else
+        MM_LAUNCH(split3_gather_kernel, blocks_for(static_cast<long long>(T) * d, 256), 256, 0, h, d, T, mul, add, h3,
+                  ld3);
 }
 
 inline void launch_rowdot(Context& cx, const __half* dout, const __half* out, int T, int H, int DV, float* Dd) {
@@ -283,7 +314,10 @@ inline void forward_chunk(Context& cx, int Bc, int S, bool tape, VocabMode vm, b
     MM_LAUNCH(embed_kernel, warp_rows_grid(T), 256, 0, w.tokens, cx.E(), w.layers[0].x_in, T, c.d, c.V, cx.d_err);
     for (int l = 0; l < c.L; ++l) {
         LayerBuf& b = w.layers[tape ? l : 0];
-        float* x_next = tape ? (l + 1 < c.L ? w.layers[l + 1].x_in : w.x_out) : (l + 1 < c.L ? b.x_in : w.x_out);
+        // tape: every layer keeps its input and mid-block residual; otherwise the residual
+        // stream is one buffer updated in place by the reduce-add epilogues
+        float* x_next = tape ? (l + 1 < c.L ? w.layers[l + 1].x_in : w.x_out) : b.x_in;
+        float* res = tape ? b.res : b.x_in;
         // attention block
         launch_rmsnorm(cx, b.x_in, c.d, cx.W(l, kAttnNorm), T, c.d, (float*)nullptr, 0LL, b.h, ld_d);
         const PrepLayer& pw = cx.prep[l];
@@ -304,13 +338,13 @@ inline void forward_chunk(Context& cx, int Bc, int S, bool tape, VocabMode vm, b
         gemm(cx, T, c.aw(), c.kvr, {b.ckv, ld_kvr, false}, {cx.S(l, kWuv), cx.SL(l, kWuv), true}, {b.v, c.aw(), kOutF16});
         launch_flash_fwd(cx, b, Bc, S);
         {
-            GemmOutSpec o{b.res, c.d, kOutF32};
-            o.residual = b.x_in;
+            GemmOutSpec o{res, c.d, tape ? kOutF32 : kOutF32Acc};
+            if (tape) o.residual = b.x_in;
             o.ldr = c.d;
             gemm(cx, T, c.d, c.aw(), {b.ao, c.aw(), false}, {cx.S(l, kWo), cx.SL(l, kWo), true}, o);
         }
         // feed-forward block
-        launch_rmsnorm(cx, b.res, c.d, cx.W(l, kFfnNorm), T, c.d, (float*)nullptr, 0LL, b.h2, ld_d);
+        launch_rmsnorm(cx, res, c.d, cx.W(l, kFfnNorm), T, c.d, (float*)nullptr, 0LL, b.h2, ld_d);
         const int ld_gu = cx.d16(2 * c.dff);
         if (tape || c.dff % 8) {
             // the backward needs gate and up themselves
@@ -322,19 +356,19 @@ inline void forward_chunk(Context& cx, int Bc, int S, bool tape, VocabMode vm, b
             gemm(cx, T, c.dff, c.d, {b.h2, ld_d, false}, {pw.Wgu, pw.ldgu, true}, o);
         }
         {
-            GemmOutSpec o{x_next, c.d, kOutF32};
-            o.residual = b.res;
+            GemmOutSpec o{x_next, c.d, tape ? kOutF32 : kOutF32Acc};
+            if (tape) o.residual = b.res;
             o.ldr = c.d;
             gemm(cx, T, c.d, c.dff, {b.gated, ld_ff, false}, {cx.S(l, kWdown), cx.SL(l, kWdown), true}, o);
         }
     }
     if (vm == kVocabNone) return;
-    launch_rmsnorm(cx, w.x_out, c.d, cx.FinalNorm(), T, c.d, w.hf, c.d, (__half*)nullptr, 0LL);
+    launch_rmsnorm(cx, tape ? w.x_out : w.layers[0].x_in, c.d, cx.FinalNorm(), T, c.d, w.hf, c.d, (__half*)nullptr, 0LL);
     const int ld3 = cx.d16(3 * c.d);
     GemmOutSpec lo{nullptr, c.V, kOutF32};
     lo.alpha = 1.0f / kVocabScale;
     if (vm == kVocabAll) {
-        MM_LAUNCH(split3_gather_kernel, blocks_for((long long)T * c.d, 256), 256, 0, w.hf, c.d, T, 1, 0, w.h3, (long long)ld3);
+        launch_split3(cx, w.hf, c.d, T, 1, 0, w.h3, ld3);
         lo.out = w.logits;
         if (with_targets) {
             // log-softmax fused into the product: per-tile row partials, then one combine;

@@ -17,6 +17,7 @@ template <int KV, int R>
 __global__ void decode_attention_kernel(const float* __restrict__ qf, const __half* __restrict__ cache,
                                         long long cache_seq_stride, const int* __restrict__ pos,
                                         int H, float scale, __half* __restrict__ ctx) {
+    MM_PDL_ENTRY();
     constexpr int W = KV + R;
     constexpr int TILE = 32;
     __shared__ float Cs[TILE][W + 1];
@@ -98,6 +99,7 @@ constexpr int kSmem = kWarps * kStages * 16 * LDQ * 2;
 __global__ void __launch_bounds__(128) decode_attention_mma_kernel(
     const float* __restrict__ qf, const __half* __restrict__ cache, long long cache_seq_stride,
     const int* __restrict__ pos, float scale, __half* __restrict__ ctx, float* __restrict__ part) {
+    MM_PDL_ENTRY();
     using namespace dec;
     using fa::ldsm_x4;
     using fa::ldsm_x4_t;
@@ -254,6 +256,7 @@ __global__ void __launch_bounds__(128) decode_attention_mma_kernel(
 // 4 context columns per lane; grid ceil(B * H / 4), block 128.
 __global__ void decode_attention_combine_kernel(const float* __restrict__ part, int nsplit, int B,
                                                 __half* __restrict__ ctx) {
+    MM_PDL_ENTRY();
     using namespace dec;
     const int wid = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (wid >= B * H) return;

@@ -21,6 +21,20 @@ __device__ __forceinline__ void raise_error(int* err, int code) {
     if (err) atomicOr(err, code);
 }
 
+// ------------------------------------------------------------------ programmatic dependent launch
+// Every kernel of this backend is launched with programmatic stream serialization, so it
+// may start while its predecessor in the stream is still running. It first waits for the
+// predecessor to complete and flush (a no-op without a programmatic dependency), then
+// lets its own successor begin launching: successive kernels overlap launch latency and
+// block scheduling, never memory accesses.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+#define MM_PDL_ENTRY()                 \
+    do {                               \
+        ::mm::pdl_wait();              \
+        ::mm::pdl_launch_dependents(); \
+    } while (0)
+
 // ------------------------------------------------------------------ warp helpers
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll

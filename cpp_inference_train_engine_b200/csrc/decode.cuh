@@ -77,6 +77,7 @@ inline void prefill_rows(Context& cx, const uint16_t* d_prompts, int B, int P, i
 }
 
 __global__ void advance_pos_kernel(int* pos, int B) {
+    MM_PDL_ENTRY();
     const int b = blockIdx.x * blockDim.x + threadIdx.x;
     if (b < B) pos[b] += 1;
 }
@@ -160,11 +161,13 @@ inline void launch_sample(Context& cx, const float* logits, int B, float tempera
                     temperature, seeds, draw, draw_offset, counter, active, out, out_stride);
 }
 
-__global__ void counter_add_kernel(int* c, int v) { *c += v; }
+__global__ void counter_add_kernel(int* c, int v) {
+    MM_PDL_ENTRY(); *c += v; }
 
 // out_tok column (*counter - 1) -> tok, for the token to append at this step.
 __global__ void column_gather_counter_kernel(const uint16_t* __restrict__ src, long long stride,
                                              const int* __restrict__ counter, int B, uint16_t* __restrict__ dst) {
+    MM_PDL_ENTRY();
     const int b = blockIdx.x * blockDim.x + threadIdx.x;
     if (b < B) dst[b] = src[b * stride + *counter - 1];
 }

@@ -107,6 +107,7 @@ template <int D>
 __global__ void __launch_bounds__(128) flash_fwd_mma_kernel(const __half* __restrict__ q, const __half* __restrict__ k,
                                                             const __half* __restrict__ v, int S, int H, float scale,
                                                             __half* __restrict__ out, float* __restrict__ lse2) {
+    MM_PDL_ENTRY();
     using namespace fa;
     constexpr int LD = D + 8;
     __shared__ __align__(16) __half Qs[kTile][LD];
@@ -191,6 +192,7 @@ __global__ void __launch_bounds__(128) flash_fwd_mma_kernel(const __half* __rest
 // D[t, h] = sum_c dO[t, h, c] * O[t, h, c] over fp16 rows (the softmax-backward row term).
 __global__ void attn_rowdot_kernel(const __half* __restrict__ dout, const __half* __restrict__ out, int T, int H,
                                    int DV, float* __restrict__ Dd) {
+    MM_PDL_ENTRY();
     const int idx = blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= T * H) return;
     const long long o = static_cast<long long>(idx / H) * H * DV + (idx % H) * DV;
@@ -206,6 +208,7 @@ __global__ void __launch_bounds__(128) flash_bwd_dq_mma_kernel(
     const __half* __restrict__ q, const __half* __restrict__ k, const __half* __restrict__ v,
     const __half* __restrict__ dout, const float* __restrict__ lse2, const float* __restrict__ Dd, int S, int H,
     float scale, float* __restrict__ dq) {
+    MM_PDL_ENTRY();
     using namespace fa;
     constexpr int LD = D + 8;
     __shared__ __align__(16) __half Qs[kTile][LD];
@@ -267,6 +270,7 @@ __global__ void __launch_bounds__(128) flash_bwd_dkdv_mma_kernel(
     const __half* __restrict__ q, const __half* __restrict__ k, const __half* __restrict__ v,
     const __half* __restrict__ dout, const float* __restrict__ lse2, const float* __restrict__ Dd, int S, int H,
     float scale, float* __restrict__ dk, float* __restrict__ dv) {
+    MM_PDL_ENTRY();
     using namespace fa;
     constexpr int LD = D + 8;
     __shared__ __align__(16) __half Ks[kTile][LD];

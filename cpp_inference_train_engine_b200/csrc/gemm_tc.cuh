@@ -118,6 +118,8 @@ __global__ void __launch_bounds__(192, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    // barriers, tensor memory and descriptor prefetch overlap the predecessor's tail
+    MM_PDL_ENTRY();
 
     if (warp == 0 && lane == 0) {
         int it = 0;  // ring position across tiles

@@ -13,6 +13,7 @@ __device__ __forceinline__ int warp_row() { return (blockIdx.x * blockDim.x + th
 // x[t, :] = E[token[t], :] (fp32 master table), ops-equivalent of model.cpp:94-98.
 __global__ void embed_kernel(const uint16_t* __restrict__ tokens, const float* __restrict__ E,
                              float* __restrict__ x, int T, int d, int V, int* err) {
+    MM_PDL_ENTRY();
     const int t = warp_row(), lane = threadIdx.x & 31;
     if (t >= T) return;
     const int tok = tokens[t];
@@ -30,6 +31,7 @@ __global__ void embed_kernel(const uint16_t* __restrict__ tokens, const float* _
 __global__ void rmsnorm_kernel(const float* __restrict__ x, long long ldx, const float* __restrict__ w,
                                int T, int n, float eps, float* __restrict__ y32, long long ld32,
                                __half* __restrict__ y16, long long ld16, float* __restrict__ inv_out) {
+    MM_PDL_ENTRY();
     const int t = warp_row(), lane = threadIdx.x & 31;
     if (t >= T) return;
     const float* xr = x + t * ldx;
@@ -54,6 +56,7 @@ __global__ void rmsnorm_backward_kernel(const float* __restrict__ x, long long l
                                         int T, int n, float eps, float* __restrict__ dx32,
                                         long long lddx, __half* __restrict__ dx16, long long lddx16,
                                         float* __restrict__ dw, const float* __restrict__ grad_scale) {
+    MM_PDL_ENTRY();
     extern __shared__ float dw_acc[];  // [n]
     for (int j = threadIdx.x; j < n; j += blockDim.x) dw_acc[j] = 0.f;
     __syncthreads();
@@ -96,6 +99,7 @@ __global__ void rope_rows_kernel(const float* __restrict__ in, long long ldin, i
                                  const float* __restrict__ sin_t, int inverse,
                                  float* __restrict__ out32, long long ld32,
                                  __half* __restrict__ out16, long long ld16) {
+    MM_PDL_ENTRY();
     const int t = warp_row(), lane = threadIdx.x & 31;
     if (t >= T) return;
     const int p = (pos_base ? pos_base[t / seq] : 0) + t % seq;
@@ -130,6 +134,7 @@ __global__ void rope_key_kernel(const float* __restrict__ kvp, long long ldkvp, 
                                 const float* __restrict__ cos_t, const float* __restrict__ sin_t,
                                 float* __restrict__ k_rope, __half* __restrict__ cache_rope,
                                 long long cache_ld) {
+    MM_PDL_ENTRY();
     const int idx = blockIdx.x * blockDim.x + threadIdx.x;
     const int half_r = rope / 2;
     if (idx >= T * half_r) return;
@@ -152,6 +157,7 @@ __global__ void rope_key_kernel(const float* __restrict__ kvp, long long ldkvp, 
 __global__ void assemble_k_kernel(const float* __restrict__ k_nope, long long ldn,
                                   const float* __restrict__ k_rope, int T, int H, int nope, int rope,
                                   __half* __restrict__ k, long long ldk) {
+    MM_PDL_ENTRY();
     const int qk = nope + rope;
     const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (idx >= static_cast<long long>(T) * H * qk) return;
@@ -166,6 +172,7 @@ __global__ void assemble_k_kernel(const float* __restrict__ k_nope, long long ld
 // gated = gate * sigmoid(gate) * up (ops.cpp:71-77).
 __global__ void swiglu_kernel(const __half* __restrict__ gate, const __half* __restrict__ up,
                               long long ld, int T, int n, __half* __restrict__ out, long long ldo) {
+    MM_PDL_ENTRY();
     const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (idx >= static_cast<long long>(T) * n) return;
     const int t = static_cast<int>(idx / n), j = static_cast<int>(idx % n);
@@ -178,6 +185,7 @@ __global__ void swiglu_backward_kernel(const __half* __restrict__ gate, const __
                                        long long ld, const float* __restrict__ dy, long long lddy,
                                        int T, int n, __half* __restrict__ dg, __half* __restrict__ du,
                                        long long ldo) {
+    MM_PDL_ENTRY();
     const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (idx >= static_cast<long long>(T) * n) return;
     const int t = static_cast<int>(idx / n), j = static_cast<int>(idx % n);
@@ -191,6 +199,7 @@ __global__ void swiglu_backward_kernel(const __half* __restrict__ gate, const __
 // fp32 -> fp16 copy of a [T][n] block (optionally scaled).
 __global__ void to_half_kernel(const float* __restrict__ in, long long ldin, int T, int n,
                                __half* __restrict__ out, long long ldo) {
+    MM_PDL_ENTRY();
     const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (idx >= static_cast<long long>(T) * n) return;
     const int t = static_cast<int>(idx / n), j = static_cast<int>(idx % n);
@@ -202,6 +211,7 @@ __global__ void to_half_kernel(const float* __restrict__ in, long long ldin, int
 // a float32-accurate h * E^T on the fp16 tensor pipe.
 __global__ void split3_rows_kernel(const float* __restrict__ h, long long ldh, int T, int d,
                                    __half* __restrict__ h3, long long ld3) {
+    MM_PDL_ENTRY();
     const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (idx >= static_cast<long long>(T) * d) return;
     const int t = static_cast<int>(idx / d), j = static_cast<int>(idx % d);
@@ -217,6 +227,7 @@ __global__ void split3_rows_kernel(const float* __restrict__ h, long long ldh, i
 __global__ void embed_backward_kernel(const uint16_t* __restrict__ tokens, const float* __restrict__ dy,
                                       int T, int d, float* __restrict__ dE,
                                       const float* __restrict__ grad_scale) {
+    MM_PDL_ENTRY();
     const int t = warp_row(), lane = threadIdx.x & 31;
     if (t >= T) return;
     const float s = grad_scale ? *grad_scale : 1.0f;
@@ -228,6 +239,7 @@ __global__ void embed_backward_kernel(const uint16_t* __restrict__ tokens, const
 // gradient summed over heads (fp32), before its inverse rotation.
 __global__ void split_dk_kernel(const float* __restrict__ dk, int T, int H, int nope, int rope,
                                 __half* __restrict__ dkn, long long lddkn, float* __restrict__ drope) {
+    MM_PDL_ENTRY();
     const int t = warp_row(), lane = threadIdx.x & 31;
     if (t >= T) return;
     const int qk = nope + rope;
@@ -246,6 +258,7 @@ __global__ void split_dk_kernel(const float* __restrict__ dk, int T, int H, int 
 // kv_pack gradient = [d(raw latent) | d(rope key)] in fp16 (model.cpp:221-227).
 __global__ void pack_dkv_kernel(const float* __restrict__ dlat, const float* __restrict__ drope,
                                 int T, int kv_rank, int rope, __half* __restrict__ out, long long ldo) {
+    MM_PDL_ENTRY();
     const int w = kv_rank + rope;
     const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (idx >= static_cast<long long>(T) * w) return;

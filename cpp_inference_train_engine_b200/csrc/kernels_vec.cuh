@@ -40,6 +40,7 @@ template <int MAXV>
 __global__ void rmsnorm_v4_kernel(const float* __restrict__ x, long long ldx, const float* __restrict__ w, int T,
                                   int n, float eps, float* __restrict__ y32, long long ld32, __half* __restrict__ y16,
                                   long long ld16, float* __restrict__ inv_out) {
+    MM_PDL_ENTRY();
     const int t = warp_row(), lane = threadIdx.x & 31;
     if (t >= T) return;
     const float* xr = x + t * ldx;
@@ -79,6 +80,7 @@ __global__ void __launch_bounds__(256) rmsnorm_backward_v4_kernel(
     long long lddy, const float* __restrict__ add, long long ldadd, int T, int n, float eps,
     float* __restrict__ dx32, long long lddx, __half* __restrict__ dx16, long long lddx16,
     float* __restrict__ dw_part) {
+    MM_PDL_ENTRY();
     extern __shared__ float4 acc_sh[];  // [warps][n / 4]
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
     const int nq = n >> 2;
@@ -154,6 +156,7 @@ __global__ void __launch_bounds__(256) rmsnorm_backward_v4_kernel(
 // row group y sums rows y, y + 8, ... and the 8 group sums are added in order.
 __global__ void colsum_kernel(const float* __restrict__ part, int rows, int n, const float* __restrict__ scale,
                               float* __restrict__ dw) {
+    MM_PDL_ENTRY();
     __shared__ float grp[8][33];
     const int j = blockIdx.x * 32 + threadIdx.x;
     float s = 0.f;
@@ -171,6 +174,7 @@ __global__ void colsum_kernel(const float* __restrict__ part, int rows, int n, c
 // SwiGLU forward, 8 columns per thread.
 __global__ void swiglu_v8_kernel(const __half* __restrict__ gate, const __half* __restrict__ up, long long ld, int T,
                                  int n, __half* __restrict__ out, long long ldo) {
+    MM_PDL_ENTRY();
     const int nv = n >> 3;
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= T * nv) return;
@@ -187,6 +191,7 @@ __global__ void swiglu_v8_kernel(const __half* __restrict__ gate, const __half* 
 __global__ void swiglu_backward_v8_kernel(const __half* __restrict__ gate, const __half* __restrict__ up,
                                           long long ld, const float* __restrict__ dy, long long lddy, int T, int n,
                                           __half* __restrict__ dg, __half* __restrict__ du, long long ldo) {
+    MM_PDL_ENTRY();
     const int nv = n >> 3;
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= T * nv) return;
@@ -210,6 +215,7 @@ __global__ void swiglu_backward_v8_kernel(const __half* __restrict__ gate, const
 // fp32 -> fp16, 4 columns per thread.
 __global__ void to_half_v4_kernel(const float* __restrict__ in, long long ldin, int T, int n, __half* __restrict__ out,
                                   long long ldo) {
+    MM_PDL_ENTRY();
     const int nv = n >> 2;
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= T * nv) return;
@@ -221,6 +227,7 @@ __global__ void to_half_v4_kernel(const float* __restrict__ in, long long ldin, 
 // k = [k_nope_h | k_rope] per head, 8 output columns per thread (nope % 8 == 0, rope % 8 == 0).
 __global__ void assemble_k_v8_kernel(const float* __restrict__ k_nope, long long ldn, const float* __restrict__ k_rope,
                                      int T, int H, int nope, int rope, __half* __restrict__ k, long long ldk) {
+    MM_PDL_ENTRY();
     const int qk = nope + rope, nv = (H * qk) >> 3;
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= T * nv) return;
@@ -239,6 +246,7 @@ __global__ void rope_rows_v4_kernel(const float* __restrict__ in, long long ldin
                                     const float* __restrict__ cos_t, const float* __restrict__ sin_t, int inverse,
                                     float* __restrict__ out32, long long ld32, __half* __restrict__ out16,
                                     long long ld16) {
+    MM_PDL_ENTRY();
     const int nv = (heads * width) >> 2;
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= T * nv) return;
@@ -266,6 +274,7 @@ __global__ void rope_rows_v4_kernel(const float* __restrict__ in, long long ldin
 // D[t, h] = sum_c dout[t, h, c] * out[t, h, c] in column order, 8 columns per load.
 __global__ void attn_rowdot_v8_kernel(const __half* __restrict__ dout, const __half* __restrict__ out, int T, int H,
                                       int DV, float* __restrict__ Dd) {
+    MM_PDL_ENTRY();
     const int idx = blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= T * H) return;
     const long long o = static_cast<long long>(idx) * DV;  // rows are H * DV wide
@@ -285,6 +294,7 @@ __global__ void vocab_grad_v4_kernel(const float* __restrict__ logits, long long
                                      const uint16_t* __restrict__ target, const float* __restrict__ lse,
                                      const float* __restrict__ coef, const float* __restrict__ scale, int T,
                                      __half* __restrict__ g, long long ldg) {
+    MM_PDL_ENTRY();
     const int nv = V >> 2;
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= T * nv) return;
@@ -307,6 +317,7 @@ __global__ void vocab_grad_v4_kernel(const float* __restrict__ logits, long long
 __global__ void splitk_reduce_v4_kernel(const float* __restrict__ part, int splits, long long split_stride, int M,
                                         int N, float* __restrict__ out, long long ldc, float alpha,
                                         const float* __restrict__ alpha_ptr) {
+    MM_PDL_ENTRY();
     const int nv = N >> 2;
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= M * nv) return;

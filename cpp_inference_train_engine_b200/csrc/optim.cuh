@@ -29,6 +29,7 @@ constexpr float kVocabScale = 64.0f;
 
 __global__ void adamw_norm_partial_kernel(const float* __restrict__ g, long long n,
                                           double* __restrict__ partial, int* __restrict__ nonfinite) {
+    MM_PDL_ENTRY();
     __shared__ double red[32];
     double s = 0.0;
     bool bad = false;
@@ -52,6 +53,7 @@ __global__ void adamw_norm_partial_kernel(const float* __restrict__ g, long long
 // out[0] = norm (double), gs (float) written to gs_out. clip <= 0 disables clipping.
 __global__ void adamw_finalize_kernel(const double* __restrict__ partial, int nparts, float clip,
                                       double* __restrict__ norm_out, float* __restrict__ gs_out) {
+    MM_PDL_ENTRY();
     __shared__ double red[32];
     double s = 0.0;
     for (int i = threadIdx.x; i < nparts; i += blockDim.x) s += partial[i];
@@ -75,6 +77,7 @@ __global__ void adamw_update_kernel(const ParamDesc* __restrict__ params, float*
                                     const float* __restrict__ gs_ptr, const int* __restrict__ skip,
                                     float lr, float beta1, float beta2, float eps, float bc1,
                                     float bc2, int* __restrict__ nonfinite_out) {
+    MM_PDL_ENTRY();
     if (*skip) return;
     const ParamDesc p = params[blockIdx.y];
     const long long n = static_cast<long long>(p.rows) * p.cols;
@@ -114,6 +117,7 @@ __global__ void adamw_update_kernel(const ParamDesc* __restrict__ params, float*
 // Shadow refresh without an update (after an upload): same layout as the update writes.
 __global__ void shadow_refresh_kernel(const ParamDesc* __restrict__ params, const float* __restrict__ w,
                                       __half* __restrict__ shadow) {
+    MM_PDL_ENTRY();
     const ParamDesc p = params[blockIdx.y];
     const long long n = static_cast<long long>(p.rows) * p.cols;
     for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
@@ -147,6 +151,7 @@ struct PrepArgs {
 };
 
 __global__ void decode_prep_kernel(PrepArgs a) {
+    MM_PDL_ENTRY();
     const int qk = a.nope + a.rope;
     const int kvw = a.kvr + a.rope;
     const long long nWa = static_cast<long long>(a.d) * (a.qr + kvw);

@@ -13,6 +13,7 @@ __global__ void cache_write_kernel(const __half* __restrict__ ckv, long long ldc
                                    const float* __restrict__ k_rope, int T, int S,
                                    const int* __restrict__ pos, int row0, __half* __restrict__ cache,
                                    int Sc, int kvr, int rope) {
+    MM_PDL_ENTRY();
     const int kvw = kvr + rope;
     const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (idx >= static_cast<long long>(T) * kvw) return;
@@ -27,6 +28,7 @@ __global__ void cache_write_kernel(const __half* __restrict__ ckv, long long ldc
 // h3 rows for the vocabulary head from fp32 rows in[t * mul + add].
 __global__ void split3_gather_kernel(const float* __restrict__ h, int d, int T, int mul, int add,
                                      __half* __restrict__ h3, long long ld3) {
+    MM_PDL_ENTRY();
     const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (idx >= static_cast<long long>(T) * d) return;
     const int t = static_cast<int>(idx / d), j = static_cast<int>(idx % d);
@@ -41,6 +43,7 @@ __global__ void split3_gather_kernel(const float* __restrict__ h, int d, int T, 
 // split3_gather_kernel, 4 columns per thread (d % 4 == 0, 8-byte aligned h3 rows).
 __global__ void split3_gather_v4_kernel(const float* __restrict__ h, int d, int T, int mul, int add,
                                         __half* __restrict__ h3, long long ld3) {
+    MM_PDL_ENTRY();
     const int nv = d >> 2;
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= T * nv) return;
@@ -153,7 +156,7 @@ inline void ensure_workspace(Context& cx, int T, bool tape) {
 
 #define MM_LAUNCH_CX(ctx, kernel, grid, block, smem, ...)                 \
     do {                                                                 \
-        kernel<<<(grid), (block), (smem), (ctx).stream>>>(__VA_ARGS__);  \
+        ::mm::launch_k((ctx).stream, kernel, dim3(grid), dim3(block), (smem), __VA_ARGS__); \
         ++(ctx).launches;                                                \
     } while (0)
 #define MM_LAUNCH(kernel, grid, block, smem, ...) MM_LAUNCH_CX(cx, kernel, grid, block, smem, __VA_ARGS__)

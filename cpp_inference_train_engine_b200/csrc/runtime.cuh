@@ -445,6 +445,32 @@ inline int sm_count() {
     return n;
 }
 
+// Programmatic dependent launch for every kernel (MM_PDL=0 turns it off).
+inline bool pdl_enabled() {
+    static const bool on = [] {
+        const char* e = std::getenv("MM_PDL");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
+// Launches `kernel` on stream s with programmatic stream serialization (the kernel enters
+// through MM_PDL_ENTRY, so it touches no memory before its predecessor completes).
+template <typename... KArgs, typename... Args>
+inline void launch_k(cudaStream_t s, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    MM_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
+}
+
 // cudaFuncSetAttribute(MaxDynamicSharedMemorySize) for a kernel, once per device.
 template <auto Kernel>
 inline void set_dynamic_smem(int bytes) {
@@ -471,7 +497,7 @@ inline void launch_gemm_bn(Context& cx, const CUtensorMap& ta, const CUtensorMap
     const int per_sm = std::max(1, std::min(512 / (2 * BN), (227 * 1024) / C::SMEM));
     dim3 grid(static_cast<unsigned>(std::min<long long>(tiles, static_cast<long long>(sm_count()) * per_sm)));
     cudaEvent_t t0 = cx.prof_begin();
-    gemm_tc_kernel<BN, STAGES><<<grid, 192, C::SMEM, cx.stream>>>(ta, tb, tc, ga);
+    launch_k(cx.stream, gemm_tc_kernel<BN, STAGES>, grid, dim3(192), C::SMEM, ta, tb, tc, ga);
     const double flops = 2.0 * ga.M * static_cast<double>(ga.N) * ga.K;
     if (t0) {
         char key[96];

@@ -10,6 +10,7 @@ namespace mm {
 __global__ void splitk_reduce_kernel(const float* __restrict__ part, int splits, long long split_stride, int M, int N,
                                      float* __restrict__ out, long long ldc, float alpha,
                                      const float* __restrict__ alpha_ptr) {
+    MM_PDL_ENTRY();
     const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
     const long long MN = static_cast<long long>(M) * N;
     if (idx >= MN) return;
@@ -94,11 +95,11 @@ inline int gemm(Context& cx, int M, int N, int K, Opnd A, Opnd B, const GemmOutS
         const long long n_pad = N;
         const long long MN = static_cast<long long>(M) * N;
         if (o.ldc % 4 == 0 && (reinterpret_cast<uintptr_t>(o.out) & 15) == 0)  // N % 4 == 0 here
-            splitk_reduce_v4_kernel<<<blocks_for(MN / 4, 256), 256, 0, cx.stream>>>(
+            launch_k(cx.stream, splitk_reduce_v4_kernel, dim3(blocks_for(MN / 4, 256)), dim3(256), 0,
                 part, splits, static_cast<long long>(Mp) * n_pad, M, N, static_cast<float*>(o.out), o.ldc, o.alpha,
                 o.alpha_ptr);
         else
-            splitk_reduce_kernel<<<blocks_for(MN, 256), 256, 0, cx.stream>>>(
+            launch_k(cx.stream, splitk_reduce_kernel, dim3(blocks_for(MN, 256)), dim3(256), 0,
                 part, splits, static_cast<long long>(Mp) * n_pad, M, N, static_cast<float*>(o.out), o.ldc, o.alpha,
                 o.alpha_ptr);
         ++cx.launches;
@@ -306,7 +307,7 @@ inline void refresh_derived(Context& cx, bool shadows) {
     const Dims& c = cx.c;
     if (shadows) {
         dim3 grid(256, static_cast<unsigned>(cx.params.size()));
-        shadow_refresh_kernel<<<grid, 256, 0, cx.stream>>>(cx.d_params, cx.w, cx.shadow);
+        launch_k(cx.stream, shadow_refresh_kernel, grid, dim3(256), 0, cx.d_params, cx.w, cx.shadow);
         ++cx.launches;
     }
     for (int l = 0; l < c.L; ++l) {
@@ -318,7 +319,7 @@ inline void refresh_derived(Context& cx, bool shadows) {
         a.lda = p.lda; a.ldq = p.ldq; a.ldo = p.ldo; a.ldgu = p.ldgu;
         a.d = c.d; a.qr = c.qr; a.kvr = c.kvr; a.rope = c.rope; a.nope = c.nope; a.dv = c.dv;
         a.H = c.H; a.dff = c.dff;
-        decode_prep_kernel<<<592, 256, 0, cx.stream>>>(a);
+        launch_k(cx.stream, decode_prep_kernel, dim3(592), dim3(256), 0, a);
         ++cx.launches;
     }
 }

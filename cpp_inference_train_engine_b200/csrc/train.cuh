@@ -214,6 +214,7 @@ inline mm_step_result grpo_step(Context& pc, Context& rc, const uint16_t* input,
 
 __global__ void column_gather_kernel(const uint16_t* __restrict__ src, long long stride, int col, int B,
                                      uint16_t* __restrict__ dst) {
+    MM_PDL_ENTRY();
     const int b = blockIdx.x * blockDim.x + threadIdx.x;
     if (b < B) dst[b] = src[b * stride + col];
 }

@@ -17,6 +17,7 @@ namespace mm {
 __global__ void logsoftmax_rows_kernel(const float* __restrict__ logits, long long ld, int V,
                                        const uint16_t* __restrict__ target, int T,
                                        float* __restrict__ lp, float* __restrict__ lse, int* err) {
+    MM_PDL_ENTRY();
     __shared__ float red_f[32];
     __shared__ double red_d[32];
     const int t = blockIdx.x;
@@ -60,6 +61,7 @@ __global__ void logsoftmax_rows_kernel(const float* __restrict__ logits, long lo
 __global__ void lse_combine_kernel(const float2* __restrict__ part, int ntiles, int T,
                                    const float* __restrict__ tgt_logit, float* __restrict__ lp,
                                    float* __restrict__ lse, int* err) {
+    MM_PDL_ENTRY();
     const int t = blockIdx.x * blockDim.x + threadIdx.x;
     if (t >= T) return;
     float mx = -INFINITY;
@@ -83,6 +85,7 @@ __global__ void vocab_grad_kernel(const float* __restrict__ logits, long long ld
                                   const uint16_t* __restrict__ target, const float* __restrict__ lse,
                                   const float* __restrict__ coef, const float* __restrict__ scale,
                                   int T, __half* __restrict__ g, long long ldg) {
+    MM_PDL_ENTRY();
     const int t = blockIdx.x;
     if (t >= T) return;
     const float c = coef[t] * *scale;
@@ -114,6 +117,7 @@ __global__ void grpo_coef_kernel(const float* __restrict__ lp, const float* __re
                                  const float* __restrict__ adv, const int* __restrict__ supervised,
                                  int T, int S, double n_total, float clip, float klc,
                                  float* __restrict__ coef, GrpoSums* __restrict__ sums) {
+    MM_PDL_ENTRY();
     __shared__ double sl[32], sk[32];
     const int t = blockIdx.x * blockDim.x + threadIdx.x;
     double lo = 0.0, kl = 0.0;
@@ -168,6 +172,7 @@ __global__ void grpo_coef_kernel(const float* __restrict__ lp, const float* __re
 // scale = 2^-floor(log2(max|coef|)) so that the largest scaled coefficient lies in [1, 2);
 // inv = 1 / scale. Exact powers of two: the backward pass is linear in the coefficients.
 __global__ void grad_scale_kernel(const GrpoSums* __restrict__ sums, float* __restrict__ scale_inv) {
+    MM_PDL_ENTRY();
     const float m = __uint_as_float(sums->max_coef_bits);
     float s = 1.f;
     if (m > 0.f && isfinite(m)) s = exp2f(-floorf(log2f(m)));
@@ -178,6 +183,7 @@ __global__ void grad_scale_kernel(const GrpoSums* __restrict__ sums, float* __re
 // group_advantages for groups of G consecutive rewards.
 __global__ void advantages_kernel(const float* __restrict__ rewards, int n_groups, int G, float eps,
                                   float* __restrict__ adv, int* __restrict__ any_nonzero) {
+    MM_PDL_ENTRY();
     const int g = blockIdx.x * blockDim.x + threadIdx.x;
     if (g >= n_groups) return;
     const float* r = rewards + g * G;
@@ -428,6 +434,7 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(
     const uint64_t* __restrict__ seeds, const int* __restrict__ draw_index, int draw_offset,
     const int* __restrict__ counter, const int* __restrict__ active, uint16_t* __restrict__ out,
     long long out_stride) {
+    MM_PDL_ENTRY();
     __shared__ SampleShared S;
     const int step = counter ? *counter : 0;
     out += step;
@@ -579,6 +586,7 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(
 namespace mm {
 // max |x| over n floats, as float bits into *out (atomicMax on non-negative floats).
 __global__ void absmax_kernel(const float* __restrict__ x, int n, unsigned int* __restrict__ out) {
+    MM_PDL_ENTRY();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     float v = i < n ? fabsf(x[i]) : 0.f;
     v = warp_max(v);

@@ -79,74 +79,83 @@ __global__ void decode_attention_kernel(const float* __restrict__ qf, const __ha
 }
 
 // Tensor-core form for 8 heads over a [128 latent | 16 rope] cache row (the 35.8M model).
-// Launch with dec::kSmem bytes of dynamic shared memory.
 // The 8 heads are exactly the N = 8 of mma.sync m16n8k16, so per 16 cached positions a warp
 // computes S^T = C[16 x 144] * Q^T (9 MMAs) and O^T += C^T[128 x 16] * P^T (8 MMAs, C^T via
-// transposed ldmatrix). Each warp keeps its own online-softmax state over its share of the
-// positions; the 4 warps of a CTA are merged through shared memory. For few sequences the
-// context is also split over gridDim.y CTAs (flash-decoding): each writes a partial
-// (max, sum, O) to `part` and decode_attention_combine_kernel merges them.
+// transposed ldmatrix). For few sequences the context is also split over several warps
+// (flash-decoding): each writes a partial (max, sum, O) to `part` and
+// decode_attention_combine_kernel merges them.
 namespace dec {
 constexpr int H = 8, KV = 128, R = 16, W = KV + R;
 constexpr int LDQ = W + 8;    // padded rows: 16-byte aligned, conflict-free ldmatrix
 constexpr int LDP = 16 + 8;
 constexpr int kWarps = 4;
-constexpr int kStages = 3;  // cache tiles in flight per warp
-// dynamic shared memory: the per-warp cache-tile rings
-constexpr int kSmem = kWarps * kStages * 16 * LDQ * 2;
+constexpr int kStages = 2;  // cache tiles per warp ring: one computing, one landing
+// per warp: a tile ring, its row's query (fp16) and P
+constexpr int kRingBytes = kStages * 16 * LDQ * 2;
+constexpr int kWarpSmem = kRingBytes + H * LDQ * 2 + H * LDP * 2;
+constexpr int kRowSmem = kWarps * kWarpSmem;
+// warps wanted in flight for the whole batch (8 per SM) when choosing context splits
+constexpr int kTargetWarps = 148 * 8;
 }  // namespace dec
 
-__global__ void __launch_bounds__(128) decode_attention_mma_kernel(
+// Latent decode attention with one warp per (sequence row, context split): the warp
+// streams its row's cache tiles through its own cp.async ring (kStages deep) and keeps
+// one online-softmax state, so no cross-warp merge is needed. Work item
+// blockIdx.x * kWarps + warp = b * nsplit + split covers tiles [split * per, ...) of row b.
+// With nsplit == 1 the normalised context goes to ctx (fp16 [B][H * KV]); otherwise the
+// partial (max, sum, O) of each split goes to part for decode_attention_combine_kernel.
+// Launch: ceil(B * nsplit / kWarps) blocks of 128 threads, dec::kRowSmem dynamic smem.
+__global__ void __launch_bounds__(128) decode_attention_row_kernel(
     const float* __restrict__ qf, const __half* __restrict__ cache, long long cache_seq_stride,
-    const int* __restrict__ pos, float scale, __half* __restrict__ ctx, float* __restrict__ part) {
+    const int* __restrict__ pos, int B, int nsplit, float scale, __half* __restrict__ ctx, float* __restrict__ part) {
     MM_PDL_ENTRY();
     using namespace dec;
     using fa::ldsm_x4;
     using fa::ldsm_x4_t;
     using fa::mma16816;
-    __shared__ __align__(16) __half Qs[H][LDQ];
-    // per-warp ring of kStages cache tiles (cp.async), reused as Ow [kWarps][H][KV] fp32
-    // for the merge once every warp has left its loop
-    extern __shared__ __align__(16) unsigned char ring_raw[];  // kSmem bytes
-    __shared__ __align__(16) __half Pw[kWarps][H][LDP];
-    __shared__ float Mw[kWarps][H], Lw[kWarps][H];
-    static_assert(sizeof(float) * kWarps * H * KV <= kSmem, "merge buffer fits the ring");
-    auto Cw = reinterpret_cast<__half (*)[kStages][16][LDQ]>(ring_raw);
-    auto Ow = reinterpret_cast<float (*)[H][KV]>(ring_raw);
-    const int b = blockIdx.x, sp = blockIdx.y, nsplit = gridDim.y;
+    extern __shared__ __align__(16) unsigned char row_smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const int item = blockIdx.x * kWarps + warp;
+    if (item >= B * nsplit) return;  // no block-wide barrier follows
+    const int b = item / nsplit, sp = item - b * nsplit;
+    unsigned char* mine = row_smem + warp * kWarpSmem;
+    auto ring = reinterpret_cast<__half (*)[16][LDQ]>(mine);
+    auto Qs = reinterpret_cast<__half (*)[LDQ]>(mine + kRingBytes);
+    auto Pw = reinterpret_cast<__half (*)[LDP]>(mine + kRingBytes + H * LDQ * 2);
     const int n = pos[b] + 1;
     const int tiles = (n + 15) / 16;
     const int per = (tiles + nsplit - 1) / nsplit;
     const int t_begin = sp * per, t_end = min(tiles, t_begin + per);
-    const float qscale = scale * fa::kLog2e;
     const __half* cb = cache + static_cast<long long>(b) * cache_seq_stride;
-    // the warp's j-th tile (t_begin + warp + kWarps * j) into ring stage j % kStages; one
-    // commit group per call (empty past the end) keeps the group count uniform
     auto issue = [&](int j) {
-        const int tile = t_begin + warp + kWarps * j;
+        const int tile = t_begin + j;
         if (tile < t_end) {
             const int p0 = tile * 16;
-            __half (*dst)[LDQ] = Cw[warp][j % kStages];
             for (int e = lane; e < 16 * (W / 8); e += 32) {
                 const int r = e / (W / 8), cc = (e % (W / 8)) * 8;
                 const bool ok = p0 + r < n;
-                cp_async16(&dst[r][cc], cb + static_cast<long long>(ok ? p0 + r : 0) * W + cc, ok);
+                cp_async16(&ring[j % kStages][r][cc], cb + static_cast<long long>(ok ? p0 + r : 0) * W + cc, ok);
             }
         }
         cp_async_commit();
     };
 #pragma unroll
     for (int j = 0; j < kStages - 1; ++j) issue(j);
-    for (int e = threadIdx.x; e < H * W; e += blockDim.x)
-        Qs[e / W][e % W] = __float2half_rn(qf[static_cast<long long>(b) * H * W + e] * qscale);
-    __syncthreads();
-    // B fragments of Q^T (k = dims, n = heads) for all 9 k-steps, loaded once.
+    // the row's absorbed queries, pre-scaled into the base-2 domain, as fp16
+    const float qscale = scale * fa::kLog2e;
+    const float4* q4 = reinterpret_cast<const float4*>(qf + static_cast<long long>(b) * H * W);
+    for (int e = lane; e < H * W / 4; e += 32) {
+        const float4 v = q4[e];
+        const int hh = (4 * e) / W, c = (4 * e) % W;
+        *reinterpret_cast<__half2*>(&Qs[hh][c]) = __floats2half2_rn(v.x * qscale, v.y * qscale);
+        *reinterpret_cast<__half2*>(&Qs[hh][c + 2]) = __floats2half2_rn(v.z * qscale, v.w * qscale);
+    }
+    __syncwarp();
     uint32_t qb[W / 16][2];
 #pragma unroll
     for (int kk = 0; kk < W / 16; ++kk) {
         uint32_t r[4];
-        ldsm_x4(r, &Qs[lane & 7][kk * 16 + ((lane >> 3) & 1) * 8]);  // lanes 16-31 repeat 0-15
+        ldsm_x4(r, &Qs[lane & 7][kk * 16 + ((lane >> 3) & 1) * 8]);
         qb[kk][0] = r[0];
         qb[kk][1] = r[1];
     }
@@ -155,13 +164,13 @@ __global__ void __launch_bounds__(128) decode_attention_mma_kernel(
     for (int i = 0; i < KV / 16; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;  // heads 2t, 2t+1
     for (int j = 0;; ++j) {
-        const int tile = t_begin + warp + kWarps * j;
+        const int tile = t_begin + j;
         if (tile >= t_end) break;
         const int p0 = tile * 16;
         issue(j + kStages - 1);
-        cp_async_wait<kStages - 1>();  // tile j has landed
+        cp_async_wait<kStages - 1>();
         __syncwarp();
-        __half (*Ct)[LDQ] = Cw[warp][j % kStages];
+        __half (*Ct)[LDQ] = ring[j % kStages];
         float s[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int kk = 0; kk < W / 16; ++kk) {
@@ -191,13 +200,13 @@ __global__ void __launch_bounds__(128) decode_attention_mma_kernel(
         const float p00 = exp2f(s[0] - n0), p01 = exp2f(s[1] - n1), p10 = exp2f(s[2] - n0), p11 = exp2f(s[3] - n1);
         l0 += p00 + p10;
         l1 += p01 + p11;
-        Pw[warp][2 * t][g] = __float2half_rn(p00);
-        Pw[warp][2 * t + 1][g] = __float2half_rn(p01);
-        Pw[warp][2 * t][g + 8] = __float2half_rn(p10);
-        Pw[warp][2 * t + 1][g + 8] = __float2half_rn(p11);
+        Pw[2 * t][g] = __float2half_rn(p00);
+        Pw[2 * t + 1][g] = __float2half_rn(p01);
+        Pw[2 * t][g + 8] = __float2half_rn(p10);
+        Pw[2 * t + 1][g + 8] = __float2half_rn(p11);
         __syncwarp();
         uint32_t bp[4];
-        ldsm_x4(bp, &Pw[warp][lane & 7][((lane >> 3) & 1) * 8]);
+        ldsm_x4(bp, &Pw[lane & 7][((lane >> 3) & 1) * 8]);
 #pragma unroll
         for (int mt = 0; mt < KV / 16; ++mt) {
             uint32_t a[4];
@@ -206,53 +215,42 @@ __global__ void __launch_bounds__(128) decode_attention_mma_kernel(
         }
         __syncwarp();
     }
+    cp_async_wait<0>();
 #pragma unroll
     for (int o = 4; o < 32; o <<= 1) {
         l0 += __shfl_xor_sync(0xffffffffu, l0, o);
         l1 += __shfl_xor_sync(0xffffffffu, l1, o);
     }
-    if (g == 0) {
-        Mw[warp][2 * t] = m0; Mw[warp][2 * t + 1] = m1;
-        Lw[warp][2 * t] = l0; Lw[warp][2 * t + 1] = l1;
-    }
-    cp_async_wait<0>();
-    __syncthreads();  // every warp is done with its ring before it becomes Ow
+    if (nsplit == 1) {
+        const float i0 = 1.f / l0, i1 = 1.f / l1;
+        __half* o0 = ctx + static_cast<long long>(b) * H * KV + (2 * t) * KV;
+        __half* o1 = o0 + KV;
 #pragma unroll
-    for (int mt = 0; mt < KV / 16; ++mt) {
-        Ow[warp][2 * t][mt * 16 + g] = acc[mt][0];
-        Ow[warp][2 * t + 1][mt * 16 + g] = acc[mt][1];
-        Ow[warp][2 * t][mt * 16 + g + 8] = acc[mt][2];
-        Ow[warp][2 * t + 1][mt * 16 + g + 8] = acc[mt][3];
-    }
-    __syncthreads();
-    for (int e = threadIdx.x; e < H * KV; e += blockDim.x) {
-        const int hh = e / KV, c = e % KV;
-        float M = -INFINITY;
-#pragma unroll
-        for (int w = 0; w < kWarps; ++w) M = fmaxf(M, Mw[w][hh]);
-        float L = 0.f, O = 0.f;
-        if (M != -INFINITY) {
-#pragma unroll
-            for (int w = 0; w < kWarps; ++w) {
-                const float f = exp2f(Mw[w][hh] - M);
-                L += f * Lw[w][hh];
-                O += f * Ow[w][hh][c];
-            }
+        for (int mt = 0; mt < KV / 16; ++mt) {
+            o0[mt * 16 + g] = __float2half_rn(acc[mt][0] * i0);
+            o1[mt * 16 + g] = __float2half_rn(acc[mt][1] * i1);
+            o0[mt * 16 + g + 8] = __float2half_rn(acc[mt][2] * i0);
+            o1[mt * 16 + g + 8] = __float2half_rn(acc[mt][3] * i1);
         }
-        if (nsplit == 1) {
-            ctx[static_cast<long long>(b) * H * KV + hh * KV + c] = __float2half_rn(O / L);
-        } else {
-            float* pp = part + (static_cast<long long>(b) * nsplit + sp) * H * (KV + 2);
-            pp[hh * (KV + 2) + 2 + c] = O;
-            if (c == 0) {
-                pp[hh * (KV + 2)] = M;
-                pp[hh * (KV + 2) + 1] = L;
-            }
+    } else {
+        float* pp = part + static_cast<long long>(item) * H * (KV + 2);
+        float* q0 = pp + (2 * t) * (KV + 2);
+        float* q1 = q0 + (KV + 2);
+        if (g == 0) {
+            q0[0] = m0; q0[1] = l0;
+            q1[0] = m1; q1[1] = l1;
+        }
+#pragma unroll
+        for (int mt = 0; mt < KV / 16; ++mt) {
+            q0[2 + mt * 16 + g] = acc[mt][0];
+            q1[2 + mt * 16 + g] = acc[mt][1];
+            q0[2 + mt * 16 + g + 8] = acc[mt][2];
+            q1[2 + mt * 16 + g + 8] = acc[mt][3];
         }
     }
 }
 
-// Merges the nsplit partials of decode_attention_mma_kernel: one warp per (row, head),
+// Merges the nsplit partials of decode_attention_row_kernel: one warp per (row, head),
 // 4 context columns per lane; grid ceil(B * H / 4), block 128.
 __global__ void decode_attention_combine_kernel(const float* __restrict__ part, int nsplit, int B,
                                                 __half* __restrict__ ctx) {

@@ -9,11 +9,25 @@ namespace mm {
 // Context splits of the tensor-core decode attention: enough CTAs for ~2 per SM when the
 // batch alone does not provide them, at least 4 tiles of 16 positions per split.
 constexpr int kMaxDecodeSplits = 16;
+// Context splits of the latent decode attention (one warp per row and split): enough warps
+// for ~8 per SM when the batch alone does not provide them, at least 4 tiles of 16
+// positions per split.
 inline int decode_splits(int B, int ctx) {
-    if (B >= 296) return 1;
-    const int want = (296 + B - 1) / B;
+    if (B >= dec::kTargetWarps) return 1;
+    const int want = (dec::kTargetWarps + B - 1) / B;
     const int by_len = std::max(1, (ctx + 63) / 64);
     return std::max(1, std::min(std::min(want, by_len), kMaxDecodeSplits));
+}
+
+// Latent decode attention (+ split combine) on the context stream.
+inline void launch_decode_attention(Context& cx, const float* q, const __half* cache, long long seq_stride,
+                                    const int* pos, int B, int ns, float scale, __half* out, float* part) {
+    set_dynamic_smem<decode_attention_row_kernel>(dec::kRowSmem);
+    MM_LAUNCH(decode_attention_row_kernel, blocks_for(static_cast<long long>(B) * ns, dec::kWarps), 32 * dec::kWarps,
+              dec::kRowSmem, q, cache, seq_stride, pos, B, ns, scale, out, part);
+    if (ns > 1)
+        MM_LAUNCH(decode_attention_combine_kernel, blocks_for(static_cast<long long>(B) * dec::H * 32, 128), 128, 0, part,
+                  ns, B, out);
 }
 
 inline void ensure_decode(Context& cx, int B, int Sc, int max_new) {
@@ -45,7 +59,7 @@ inline void ensure_decode(Context& cx, int B, int Sc, int max_new) {
         d.draw = a.template take<int>(B);
         d.out_tok = a.template take<uint16_t>(static_cast<long long>(B) * std::max(max_new, 1));
         // flash-decoding partials (max, sum, O[kv_rank]) per split and head
-        d.part = a.template take<float>(B >= 296 ? 1 : static_cast<long long>(B) * kMaxDecodeSplits * c.H * (c.kvr + 2));
+        d.part = a.template take<float>(B >= dec::kTargetWarps ? 1 : static_cast<long long>(B) * kMaxDecodeSplits * c.H * (c.kvr + 2));
         d.step = a.template take<int>(1);
     };
     d.drop_graph();
@@ -109,13 +123,8 @@ inline void decode_step(Context& cx) {
             const double bytes = static_cast<double>(B) * ((cx.dec_len + 1.0) * kvw * 2 + c.H * kvw * 4.0 + c.H * c.kvr * 2.0);
             if (c.kvr == dec::KV && c.rope == dec::R && c.H == dec::H) {
                 const int ns = decode_splits(B, cx.dec_len + 1);
-                set_dynamic_smem<decode_attention_mma_kernel>(dec::kSmem);
                 cudaEvent_t t0 = cx.prof_begin();
-                MM_LAUNCH(decode_attention_mma_kernel, dim3(B, ns), 128, dec::kSmem, d.qf2, cache_l, (long long)d.Sc * kvw,
-                          d.pos, scale, d.ctx16, d.part);
-                if (ns > 1)
-                    MM_LAUNCH(decode_attention_combine_kernel, blocks_for(static_cast<long long>(B) * dec::H * 32, 128), 128, 0,
-                              d.part, ns, B, d.ctx16);
+                launch_decode_attention(cx, d.qf2, cache_l, (long long)d.Sc * kvw, d.pos, B, ns, scale, d.ctx16, d.part);
                 cx.prof_end(kKDecodeAttn, t0, bytes);
             } else if (c.kvr == 128)
                 MM_LAUNCH_TIMED(kKDecodeAttn, bytes, (decode_attention_kernel<128, 16>), B, 32 * c.H, smem, d.qf2, cache_l,

@@ -461,12 +461,8 @@ int mm_cuda_decode_attention(mm_cuda_ctx* h, const float* q, const void* cache, 
         if (splits > 1)
             part = static_cast<float*>(cx.stage.get(sizeof(float) * static_cast<size_t>(batch) * splits * mm::dec::H *
                                                     (mm::dec::KV + 2)));
-        mm::set_dynamic_smem<mm::decode_attention_mma_kernel>(mm::dec::kSmem);
-        MM_LAUNCH(mm::decode_attention_mma_kernel, dim3(batch, splits), 128, mm::dec::kSmem, q,
-                  static_cast<const __half*>(cache), cache_seq_stride, pos, scale, static_cast<__half*>(out), part);
-        if (splits > 1)
-            MM_LAUNCH(mm::decode_attention_combine_kernel, mm::blocks_for(static_cast<long long>(batch) * mm::dec::H * 32, 128),
-                      128, 0, part, splits, batch, static_cast<__half*>(out));
+        mm::launch_decode_attention(cx, q, static_cast<const __half*>(cache), cache_seq_stride, pos, batch, splits, scale,
+                                    static_cast<__half*>(out), part);
         mm::check_device(cx, "decode_attention");
     });
 }
@@ -481,12 +477,14 @@ int mm_decode_attention_noalloc(const float* q, const void* cache, int64_t cache
     if (!part) return MM_GPU_ERROR;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     try {
-        mm::set_dynamic_smem<mm::decode_attention_mma_kernel>(mm::dec::kSmem);
+        mm::set_dynamic_smem<mm::decode_attention_row_kernel>(mm::dec::kRowSmem);
     } catch (...) {
         return MM_GPU_ERROR;
     }
-    mm::decode_attention_mma_kernel<<<dim3(batch, splits), 128, mm::dec::kSmem, s>>>(
-        q, static_cast<const __half*>(cache), cache_seq_stride, pos, scale, static_cast<__half*>(out), part);
+    mm::decode_attention_row_kernel<<<mm::blocks_for(static_cast<long long>(batch) * splits, mm::dec::kWarps),
+                                      32 * mm::dec::kWarps, mm::dec::kRowSmem, s>>>(
+        q, static_cast<const __half*>(cache), cache_seq_stride, pos, batch, splits, scale, static_cast<__half*>(out),
+        part);
     if (splits > 1)
         mm::decode_attention_combine_kernel<<<mm::blocks_for(static_cast<long long>(batch) * mm::dec::H * 32, 128), 128, 0, s>>>(
             part, splits, batch, static_cast<__half*>(out));

@@ -42,7 +42,7 @@ def attention(args):
         cache = (torch.randn(B, Sc, W, device="cuda", generator=g) * 0.5).half()
         pos = torch.full((B,), args.ctx - 1, device="cuda", dtype=torch.int32)
         out = torch.empty(B, H * KV, device="cuda", dtype=torch.half)
-        splits = args.splits or max(1, min((296 + B - 1) // B, (args.ctx + 63) // 64, 16))
+        splits = args.splits or (1 if B >= 1184 else max(1, min((1184 + B - 1) // B, (args.ctx + 63) // 64, 16)))
         torch.cuda.synchronize()
         times = []
         for it in range(args.warmup + args.iters):

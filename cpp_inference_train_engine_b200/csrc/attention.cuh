@@ -104,10 +104,13 @@ constexpr int kTargetWarps = 148 * 8;
 // blockIdx.x * kWarps + warp = b * nsplit + split covers tiles [split * per, ...) of row b.
 // With nsplit == 1 the normalised context goes to ctx (fp16 [B][H * KV]); otherwise the
 // partial (max, sum, O) of each split goes to part for decode_attention_combine_kernel.
+// With cos_t/sin_t, the rope part of each head's query is rotated to position pos[b] as
+// it is loaded (the step's query comes straight from the W_uq product).
 // Launch: ceil(B * nsplit / kWarps) blocks of 128 threads, dec::kRowSmem dynamic smem.
 __global__ void __launch_bounds__(128) decode_attention_row_kernel(
     const float* __restrict__ qf, const __half* __restrict__ cache, long long cache_seq_stride,
-    const int* __restrict__ pos, int B, int nsplit, float scale, __half* __restrict__ ctx, float* __restrict__ part) {
+    const int* __restrict__ pos, int B, int nsplit, float scale, __half* __restrict__ ctx, float* __restrict__ part,
+    const float* __restrict__ cos_t, const float* __restrict__ sin_t) {
     MM_PDL_ENTRY();
     using namespace dec;
     using fa::ldsm_x4;
@@ -144,9 +147,21 @@ __global__ void __launch_bounds__(128) decode_attention_row_kernel(
     // the row's absorbed queries, pre-scaled into the base-2 domain, as fp16
     const float qscale = scale * fa::kLog2e;
     const float4* q4 = reinterpret_cast<const float4*>(qf + static_cast<long long>(b) * H * W);
+    const int p = n - 1;  // position of this step's token
     for (int e = lane; e < H * W / 4; e += 32) {
-        const float4 v = q4[e];
+        float4 v = q4[e];
         const int hh = (4 * e) / W, c = (4 * e) % W;
+        if (cos_t && c >= KV) {  // adjacent-pair RoPE of the rope query (rope_rows_kernel's arithmetic)
+            float* f = reinterpret_cast<float*>(&v);
+#pragma unroll
+            for (int k = 0; k < 4; k += 2) {
+                const int pair = (c - KV + k) >> 1;
+                const float cs = cos_t[p * (R / 2) + pair], sn = sin_t[p * (R / 2) + pair];
+                const float a = f[k], bb = f[k + 1];
+                f[k] = a * cs - bb * sn;
+                f[k + 1] = a * sn + bb * cs;
+            }
+        }
         *reinterpret_cast<__half2*>(&Qs[hh][c]) = __floats2half2_rn(v.x * qscale, v.y * qscale);
         *reinterpret_cast<__half2*>(&Qs[hh][c + 2]) = __floats2half2_rn(v.z * qscale, v.w * qscale);
     }

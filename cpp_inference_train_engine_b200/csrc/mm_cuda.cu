@@ -484,7 +484,7 @@ int mm_decode_attention_noalloc(const float* q, const void* cache, int64_t cache
     mm::decode_attention_row_kernel<<<mm::blocks_for(static_cast<long long>(batch) * splits, mm::dec::kWarps),
                                       32 * mm::dec::kWarps, mm::dec::kRowSmem, s>>>(
         q, static_cast<const __half*>(cache), cache_seq_stride, pos, batch, splits, scale, static_cast<__half*>(out),
-        part);
+        part, static_cast<const float*>(nullptr), static_cast<const float*>(nullptr));
     if (splits > 1)
         mm::decode_attention_combine_kernel<<<mm::blocks_for(static_cast<long long>(batch) * mm::dec::H * 32, 128), 128, 0, s>>>(
             part, splits, batch, static_cast<__half*>(out));

@@ -72,6 +72,12 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src, bool vali
                  "r"(valid ? 16 : 0)
                  : "memory");
 }
+// 4-byte form (L1-allocating), for gathers of strided scalars.
+__device__ __forceinline__ void cp_async4(void* dst, const void* src, bool valid) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(dst)), "l"(src),
+                 "r"(valid ? 4 : 0)
+                 : "memory");
+}
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void cp_async_wait() {

@@ -55,6 +55,18 @@ __device__ __forceinline__ void load_tile(__half (*dst)[LD], const __half* __res
     }
 }
 
+// load_tile through cp.async (no register round trip); the caller commits and waits.
+template <int D, int LD>
+__device__ __forceinline__ void load_tile_async(__half (*dst)[LD], const __half* __restrict__ src, long long ld,
+                                                int rows) {
+    constexpr int VPR = D / 8;
+    for (int e = threadIdx.x; e < kTile * VPR; e += blockDim.x) {
+        const int r = e / VPR, c = (e % VPR) * 8;
+        const bool ok = r < rows;
+        cp_async16(&dst[r][c], src + (ok ? r : 0) * ld + c, ok);
+    }
+}
+
 // A fragments (16 rows x D) of rows [r0, r0+16) of a shared tile.
 template <int D, int LD>
 __device__ __forceinline__ void load_a_frags(uint32_t (&a)[D / 16][4], __half (*tile)[LD], int r0, int lane) {
@@ -62,14 +74,15 @@ __device__ __forceinline__ void load_a_frags(uint32_t (&a)[D / 16][4], __half (*
     for (int kk = 0; kk < D / 16; ++kk) ldsm_x4(a[kk], &tile[r0 + (lane & 15)][kk * 16 + (lane >> 4) * 8]);
 }
 
-// acc[64/8 n-tiles] += A(16 x D) * rows[0..64)^T of `tile` (B operand: tile rows are n, cols k).
-template <int D, int LD>
-__device__ __forceinline__ void mma_abt(float (&acc)[kTile / 8][4], const uint32_t (&a)[D / 16][4],
-                                        __half (*tile)[LD], int lane) {
+// acc[NT n-tiles of 8] += A(16 x D) * rows[0..8 NT)^T of `tile` (B operand: tile rows are n,
+// cols k). NT = kTile / 8 covers a whole tile; pass tile + r0 for rows [r0, r0 + 8 NT).
+template <int D, int LD, int NT = kTile / 8>
+__device__ __forceinline__ void mma_abt(float (&acc)[NT][4], const uint32_t (&a)[D / 16][4], __half (*tile)[LD],
+                                        int lane) {
 #pragma unroll
     for (int kk = 0; kk < D / 16; ++kk)
 #pragma unroll
-        for (int n2 = 0; n2 < kTile / 16; ++n2) {
+        for (int n2 = 0; n2 < NT / 2; ++n2) {
             uint32_t b[4];
             ldsm_x4(b, &tile[n2 * 16 + (lane & 7) + ((lane >> 4) << 3)][kk * 16 + ((lane >> 3) & 1) * 8]);
             mma16816(acc[2 * n2], a[kk], b[0], b[1]);
@@ -77,13 +90,13 @@ __device__ __forceinline__ void mma_abt(float (&acc)[kTile / 8][4], const uint32
         }
 }
 
-// acc[D/8 n-tiles] += P(16 x 64, given as accumulator fragments) * tile(64 x D) (B operand
-// stored with k as rows: transposed ldmatrix).
-template <int D, int LD>
-__device__ __forceinline__ void mma_pb(float (&acc)[D / 8][4], const float (&p)[kTile / 8][4], __half (*tile)[LD],
+// acc[D/8 n-tiles] += P(16 x 8 NT, given as accumulator fragments) * tile(8 NT x D) (B
+// operand stored with k as rows: transposed ldmatrix). Pass tile + r0 for rows [r0, r0 + 8 NT).
+template <int D, int LD, int NT = kTile / 8>
+__device__ __forceinline__ void mma_pb(float (&acc)[D / 8][4], const float (&p)[NT][4], __half (*tile)[LD],
                                        int lane) {
 #pragma unroll
-    for (int k2 = 0; k2 < kTile / 16; ++k2) {
+    for (int k2 = 0; k2 < NT / 2; ++k2) {
         uint32_t a[4];
         a[0] = pack_half2(p[2 * k2][0], p[2 * k2][1]);
         a[1] = pack_half2(p[2 * k2][2], p[2 * k2][3]);
@@ -102,7 +115,8 @@ __device__ __forceinline__ void mma_pb(float (&acc)[D / 8][4], const float (&p)[
 }  // namespace fa
 
 // Forward. q, k, v, out: fp16 [B*S][H*D]; lse2 fp32 [B*S][H] = log2-sum-exp of the scaled
-// scores (base 2). grid (ceil(S/64), H, B), block 128 (4 warps x 16 query rows).
+// scores (base 2). grid (H, B, ceil(S/64)), block 128 (4 warps x 16 query rows); K/V tiles
+// stream through a two-deep cp.async ring.
 template <int D>
 __global__ void __launch_bounds__(128) flash_fwd_mma_kernel(const __half* __restrict__ q, const __half* __restrict__ k,
                                                             const __half* __restrict__ v, int S, int H, float scale,
@@ -111,31 +125,41 @@ __global__ void __launch_bounds__(128) flash_fwd_mma_kernel(const __half* __rest
     using namespace fa;
     constexpr int LD = D + 8;
     __shared__ __align__(16) __half Qs[kTile][LD];
-    __shared__ __align__(16) __half Ks[kTile][LD];
-    __shared__ __align__(16) __half Vs[kTile][LD];
-    const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+    __shared__ __align__(16) __half Ks[2][kTile][LD];  // K/V tile kt in buffer kt & 1
+    __shared__ __align__(16) __half Vs[2][kTile][LD];
+    // grid (H, B, query tiles): every head and sequence of the longest rows (most key
+    // tiles) is scheduled before any shorter one
+    const int qt = gridDim.z - 1 - blockIdx.z;
+    const int h = blockIdx.x, b = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const long long ld = static_cast<long long>(H) * D;
     const long long base = static_cast<long long>(b) * S;
     const float c = scale * kLog2e;
-    load_tile<D, LD>(Qs, q + (base + qt * kTile) * ld + h * D, ld, S - qt * kTile);
-    __syncthreads();
+    load_tile_async<D, LD>(Qs, q + (base + qt * kTile) * ld + h * D, ld, S - qt * kTile);
+    load_tile_async<D, LD>(Ks[0], k + base * ld + h * D, ld, S);
+    load_tile_async<D, LD>(Vs[0], v + base * ld + h * D, ld, S);
+    cp_async_commit();
     uint32_t qa[D / 16][4];
-    load_a_frags<D, LD>(qa, Qs, warp * 16, lane);
     float o[D / 8][4];
 #pragma unroll
     for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
     const int row0 = qt * kTile + warp * 16 + g, row1 = row0 + 8;
     for (int kt = 0; kt <= qt; ++kt) {
+        if (kt < qt) {  // prefetch tile kt + 1 while tile kt is used
+            load_tile_async<D, LD>(Ks[(kt + 1) & 1], k + (base + (kt + 1) * kTile) * ld + h * D, ld, S - (kt + 1) * kTile);
+            load_tile_async<D, LD>(Vs[(kt + 1) & 1], v + (base + (kt + 1) * kTile) * ld + h * D, ld, S - (kt + 1) * kTile);
+        }
+        cp_async_commit();
+        cp_async_wait<1>();  // all but the newest group: tile kt (and Q) have landed
         __syncthreads();
-        load_tile<D, LD>(Ks, k + (base + kt * kTile) * ld + h * D, ld, S - kt * kTile);
-        load_tile<D, LD>(Vs, v + (base + kt * kTile) * ld + h * D, ld, S - kt * kTile);
-        __syncthreads();
+        if (kt == 0) load_a_frags<D, LD>(qa, Qs, warp * 16, lane);
+        __half (*Kt)[LD] = Ks[kt & 1];
+        __half (*Vt)[LD] = Vs[kt & 1];
         float s[kTile / 8][4];
 #pragma unroll
         for (int i = 0; i < kTile / 8; ++i) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.f;
-        mma_abt<D, LD>(s, qa, Ks, lane);
+        mma_abt<D, LD>(s, qa, Kt, lane);
         float mx0 = m0, mx1 = m1;
 #pragma unroll
         for (int nt = 0; nt < kTile / 8; ++nt)
@@ -170,7 +194,8 @@ __global__ void __launch_bounds__(128) flash_fwd_mma_kernel(const __half* __rest
             l0 += s[nt][0] + s[nt][1];
             l1 += s[nt][2] + s[nt][3];
         }
-        mma_pb<D, LD>(o, s, Vs, lane);
+        mma_pb<D, LD>(o, s, Vt, lane);
+        __syncthreads();  // buffer kt & 1 is refilled by the prefetch issued next iteration
     }
     l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
     l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
@@ -202,59 +227,79 @@ __global__ void attn_rowdot_kernel(const __half* __restrict__ dout, const __half
 }
 
 // dQ for one query tile (4 warps x 16 query rows). dout fp16 [B*S][H*D]. dq fp32 [B*S][H*D],
-// including the softmax scale.
+// including the softmax scale. grid (H, B, ceil(S/64)), longest rows first; K/V tiles stream
+// through a two-deep cp.async ring. Dynamic shared memory: flash_dq_smem<D>() bytes.
+template <int D> constexpr int flash_dq_smem() { return 6 * fa::kTile * (D + 8) * 2; }
 template <int D>
-__global__ void __launch_bounds__(128) flash_bwd_dq_mma_kernel(
+__global__ void __launch_bounds__(128, 4) flash_bwd_dq_mma_kernel(
     const __half* __restrict__ q, const __half* __restrict__ k, const __half* __restrict__ v,
     const __half* __restrict__ dout, const float* __restrict__ lse2, const float* __restrict__ Dd, int S, int H,
     float scale, float* __restrict__ dq) {
     MM_PDL_ENTRY();
     using namespace fa;
     constexpr int LD = D + 8;
-    __shared__ __align__(16) __half Qs[kTile][LD];
-    __shared__ __align__(16) __half Gs[kTile][LD];
-    __shared__ __align__(16) __half Ks[kTile][LD];
-    __shared__ __align__(16) __half Vs[kTile][LD];
-    const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+    extern __shared__ __align__(16) unsigned char fa_smem[];
+    auto tiles = reinterpret_cast<__half (*)[kTile][LD]>(fa_smem);  // Q, dO, K[2], V[2]
+    __half (*Qs)[LD] = tiles[0];
+    __half (*Gs)[LD] = tiles[1];
+    const int qt = gridDim.z - 1 - blockIdx.z, h = blockIdx.x, b = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const long long ld = static_cast<long long>(H) * D;
     const long long base = static_cast<long long>(b) * S;
     const float c = scale * kLog2e;
-    load_tile<D, LD>(Qs, q + (base + qt * kTile) * ld + h * D, ld, S - qt * kTile);
-    load_tile<D, LD>(Gs, dout + (base + qt * kTile) * ld + h * D, ld, S - qt * kTile);
-    __syncthreads();
-    uint32_t qa[D / 16][4], ga[D / 16][4];
-    load_a_frags<D, LD>(qa, Qs, warp * 16, lane);
-    load_a_frags<D, LD>(ga, Gs, warp * 16, lane);
+    load_tile_async<D, LD>(Qs, q + (base + qt * kTile) * ld + h * D, ld, S - qt * kTile);
+    load_tile_async<D, LD>(Gs, dout + (base + qt * kTile) * ld + h * D, ld, S - qt * kTile);
+    load_tile_async<D, LD>(tiles[2], k + base * ld + h * D, ld, S);
+    load_tile_async<D, LD>(tiles[4], v + base * ld + h * D, ld, S);
+    cp_async_commit();
     const int row0 = qt * kTile + warp * 16 + g, row1 = row0 + 8;
     const float L0 = row0 < S ? lse2[(base + row0) * H + h] : 0.f, L1 = row1 < S ? lse2[(base + row1) * H + h] : 0.f;
     const float D0 = row0 < S ? Dd[(base + row0) * H + h] : 0.f, D1 = row1 < S ? Dd[(base + row1) * H + h] : 0.f;
+    uint32_t qa[D / 16][4], ga[D / 16][4];
     float acc[D / 8][4];
 #pragma unroll
     for (int i = 0; i < D / 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
     for (int kt = 0; kt <= qt; ++kt) {
-        __syncthreads();
-        load_tile<D, LD>(Ks, k + (base + kt * kTile) * ld + h * D, ld, S - kt * kTile);
-        load_tile<D, LD>(Vs, v + (base + kt * kTile) * ld + h * D, ld, S - kt * kTile);
-        __syncthreads();
-        float s[kTile / 8][4], dp[kTile / 8][4];
-#pragma unroll
-        for (int i = 0; i < kTile / 8; ++i) {
-            s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.f;
-            dp[i][0] = dp[i][1] = dp[i][2] = dp[i][3] = 0.f;
+        if (kt < qt) {
+            load_tile_async<D, LD>(tiles[2 + ((kt + 1) & 1)], k + (base + (kt + 1) * kTile) * ld + h * D, ld,
+                                   S - (kt + 1) * kTile);
+            load_tile_async<D, LD>(tiles[4 + ((kt + 1) & 1)], v + (base + (kt + 1) * kTile) * ld + h * D, ld,
+                                   S - (kt + 1) * kTile);
         }
-        mma_abt<D, LD>(s, qa, Ks, lane);
-        mma_abt<D, LD>(dp, ga, Vs, lane);
+        cp_async_commit();
+        cp_async_wait<1>();
+        __syncthreads();
+        if (kt == 0) {
+            load_a_frags<D, LD>(qa, Qs, warp * 16, lane);
+            load_a_frags<D, LD>(ga, Gs, warp * 16, lane);
+        }
+        __half (*Ks)[LD] = tiles[2 + (kt & 1)];
+        __half (*Vs)[LD] = tiles[4 + (kt & 1)];
+        // the 64 keys of the tile in two halves of 32 (half the live fragments)
 #pragma unroll
-        for (int nt = 0; nt < kTile / 8; ++nt)
+        for (int hk = 0; hk < 2; ++hk) {
+            constexpr int NT = kTile / 16;
+            float s[NT][4], dp[NT][4];
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int key = kt * kTile + nt * 8 + 2 * t + (e & 1);
-                const int row = e < 2 ? row0 : row1;
-                const float p = (key > row || key >= S || row >= S) ? 0.f : exp2f(s[nt][e] * c - (e < 2 ? L0 : L1));
-                s[nt][e] = p * (dp[nt][e] - (e < 2 ? D0 : D1)) * scale;
+            for (int i = 0; i < NT; ++i) {
+                s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.f;
+                dp[i][0] = dp[i][1] = dp[i][2] = dp[i][3] = 0.f;
             }
-        mma_pb<D, LD>(acc, s, Ks, lane);
+            mma_abt<D, LD, NT>(s, qa, Ks + hk * 32, lane);
+            mma_abt<D, LD, NT>(dp, ga, Vs + hk * 32, lane);
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int key = kt * kTile + hk * 32 + nt * 8 + 2 * t + (e & 1);
+                    const int row = e < 2 ? row0 : row1;
+                    const float p =
+                        (key > row || key >= S || row >= S) ? 0.f : exp2f(s[nt][e] * c - (e < 2 ? L0 : L1));
+                    s[nt][e] = p * (dp[nt][e] - (e < 2 ? D0 : D1)) * scale;
+                }
+            mma_pb<D, LD, NT>(acc, s, Ks + hk * 32, lane);
+        }
+        __syncthreads();
     }
 #pragma unroll
     for (int i = 0; i < D / 8; ++i) {
@@ -264,31 +309,46 @@ __global__ void __launch_bounds__(128) flash_bwd_dq_mma_kernel(
     }
 }
 
-// dK, dV for one key tile (4 warps x 16 keys). dk includes the softmax scale.
+// dK, dV for one key tile (4 warps x 16 keys). dk includes the softmax scale. grid (H, B,
+// ceil(S/64)), key tile = blockIdx.z (the first key tiles meet the most query tiles and
+// are scheduled first); Q/dO tiles and their lse/D rows stream through a two-deep cp.async
+// ring. Dynamic shared memory: flash_dkdv_smem<D>() bytes.
+template <int D> constexpr int flash_dkdv_smem() { return 6 * fa::kTile * (D + 8) * 2 + 4 * fa::kTile * 4; }
 template <int D>
-__global__ void __launch_bounds__(128) flash_bwd_dkdv_mma_kernel(
+__global__ void __launch_bounds__(128, 3) flash_bwd_dkdv_mma_kernel(
     const __half* __restrict__ q, const __half* __restrict__ k, const __half* __restrict__ v,
     const __half* __restrict__ dout, const float* __restrict__ lse2, const float* __restrict__ Dd, int S, int H,
     float scale, float* __restrict__ dk, float* __restrict__ dv) {
     MM_PDL_ENTRY();
     using namespace fa;
     constexpr int LD = D + 8;
-    __shared__ __align__(16) __half Ks[kTile][LD];
-    __shared__ __align__(16) __half Vs[kTile][LD];
-    __shared__ __align__(16) __half Qs[kTile][LD];
-    __shared__ __align__(16) __half Gs[kTile][LD];
-    __shared__ float Ls[kTile], Ds[kTile];
-    const int kt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+    extern __shared__ __align__(16) unsigned char fa_smem[];
+    auto tiles = reinterpret_cast<__half (*)[kTile][LD]>(fa_smem);  // K, V, Q[2], dO[2]
+    float (*Ls)[kTile] = reinterpret_cast<float (*)[kTile]>(fa_smem + 6 * kTile * LD * 2);
+    float (*Ds)[kTile] = Ls + 2;
+    const int kt = blockIdx.z, h = blockIdx.x, b = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const long long ld = static_cast<long long>(H) * D;
     const long long base = static_cast<long long>(b) * S;
     const float c = scale * kLog2e;
-    load_tile<D, LD>(Ks, k + (base + kt * kTile) * ld + h * D, ld, S - kt * kTile);
-    load_tile<D, LD>(Vs, v + (base + kt * kTile) * ld + h * D, ld, S - kt * kTile);
-    __syncthreads();
+    const int ntiles = (S + kTile - 1) / kTile;
+    // query tile qt (its Q, dO, lse and D rows) into ring slot qt & 1
+    auto issue = [&](int qt) {
+        const int sl = qt & 1;
+        load_tile_async<D, LD>(tiles[2 + sl], q + (base + qt * kTile) * ld + h * D, ld, S - qt * kTile);
+        load_tile_async<D, LD>(tiles[4 + sl], dout + (base + qt * kTile) * ld + h * D, ld, S - qt * kTile);
+        for (int e = threadIdx.x; e < kTile; e += blockDim.x) {
+            const int r = qt * kTile + e;
+            const bool ok = r < S;
+            cp_async4(&Ls[sl][e], lse2 + (base + (ok ? r : 0)) * H + h, ok);
+            cp_async4(&Ds[sl][e], Dd + (base + (ok ? r : 0)) * H + h, ok);
+        }
+    };
+    load_tile_async<D, LD>(tiles[0], k + (base + kt * kTile) * ld + h * D, ld, S - kt * kTile);
+    load_tile_async<D, LD>(tiles[1], v + (base + kt * kTile) * ld + h * D, ld, S - kt * kTile);
+    issue(kt);
+    cp_async_commit();
     uint32_t ka[D / 16][4], va[D / 16][4];
-    load_a_frags<D, LD>(ka, Ks, warp * 16, lane);
-    load_a_frags<D, LD>(va, Vs, warp * 16, lane);
     const int key0 = kt * kTile + warp * 16 + g, key1 = key0 + 8;
     float accK[D / 8][4], accV[D / 8][4];
 #pragma unroll
@@ -296,38 +356,45 @@ __global__ void __launch_bounds__(128) flash_bwd_dkdv_mma_kernel(
         accK[i][0] = accK[i][1] = accK[i][2] = accK[i][3] = 0.f;
         accV[i][0] = accV[i][1] = accV[i][2] = accV[i][3] = 0.f;
     }
-    const int ntiles = (S + kTile - 1) / kTile;
     for (int qt = kt; qt < ntiles; ++qt) {
+        if (qt + 1 < ntiles) issue(qt + 1);
+        cp_async_commit();
+        cp_async_wait<1>();
         __syncthreads();
-        load_tile<D, LD>(Qs, q + (base + qt * kTile) * ld + h * D, ld, S - qt * kTile);
-        load_tile<D, LD>(Gs, dout + (base + qt * kTile) * ld + h * D, ld, S - qt * kTile);
-        for (int e = threadIdx.x; e < kTile; e += blockDim.x) {
-            const int r = qt * kTile + e;
-            Ls[e] = r < S ? lse2[(base + r) * H + h] : 0.f;
-            Ds[e] = r < S ? Dd[(base + r) * H + h] : 0.f;
+        if (qt == kt) {
+            load_a_frags<D, LD>(ka, tiles[0], warp * 16, lane);
+            load_a_frags<D, LD>(va, tiles[1], warp * 16, lane);
         }
-        __syncthreads();
-        float st[kTile / 8][4], dpt[kTile / 8][4];
+        const int sl = qt & 1;
+        __half (*Qs)[LD] = tiles[2 + sl];
+        __half (*Gs)[LD] = tiles[4 + sl];
+        // the 64 queries of the tile in two halves of 32 (half the live fragments)
 #pragma unroll
-        for (int i = 0; i < kTile / 8; ++i) {
-            st[i][0] = st[i][1] = st[i][2] = st[i][3] = 0.f;
-            dpt[i][0] = dpt[i][1] = dpt[i][2] = dpt[i][3] = 0.f;
-        }
-        mma_abt<D, LD>(st, ka, Qs, lane);   // S^T: keys x queries
-        mma_abt<D, LD>(dpt, va, Gs, lane);  // dP^T
+        for (int hq = 0; hq < 2; ++hq) {
+            constexpr int NT = kTile / 16;
+            float st[NT][4], dpt[NT][4];
 #pragma unroll
-        for (int nt = 0; nt < kTile / 8; ++nt)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int qi = nt * 8 + 2 * t + (e & 1);
-                const int query = qt * kTile + qi;
-                const int key = e < 2 ? key0 : key1;
-                const float p = (key > query || query >= S || key >= S) ? 0.f : exp2f(st[nt][e] * c - Ls[qi]);
-                st[nt][e] = p;
-                dpt[nt][e] = p * (dpt[nt][e] - Ds[qi]) * scale;
+            for (int i = 0; i < NT; ++i) {
+                st[i][0] = st[i][1] = st[i][2] = st[i][3] = 0.f;
+                dpt[i][0] = dpt[i][1] = dpt[i][2] = dpt[i][3] = 0.f;
             }
-        mma_pb<D, LD>(accV, st, Gs, lane);   // dV += P^T dO
-        mma_pb<D, LD>(accK, dpt, Qs, lane);  // dK += dS^T Q * scale
+            mma_abt<D, LD, NT>(st, ka, Qs + hq * 32, lane);   // S^T: keys x queries
+            mma_abt<D, LD, NT>(dpt, va, Gs + hq * 32, lane);  // dP^T
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int qi = hq * 32 + nt * 8 + 2 * t + (e & 1);
+                    const int query = qt * kTile + qi;
+                    const int key = e < 2 ? key0 : key1;
+                    const float p = (key > query || query >= S || key >= S) ? 0.f : exp2f(st[nt][e] * c - Ls[sl][qi]);
+                    st[nt][e] = p;
+                    dpt[nt][e] = p * (dpt[nt][e] - Ds[sl][qi]) * scale;
+                }
+            mma_pb<D, LD, NT>(accV, st, Gs + hq * 32, lane);   // dV += P^T dO
+            mma_pb<D, LD, NT>(accK, dpt, Qs + hq * 32, lane);  // dK += dS^T Q * scale
+        }
+        __syncthreads();
     }
 #pragma unroll
     for (int i = 0; i < D / 8; ++i) {

@@ -293,7 +293,7 @@ inline void launch_rope_rows(Context& cx,const float* in, long long ldin, int T,
 
 inline void launch_flash_fwd(Context& cx, const LayerBuf& b, int Bc, int S) {
     const Dims& c = cx.c;
-    dim3 grid((S + fa::kTile - 1) / fa::kTile, c.H, Bc);
+    dim3 grid(c.H, Bc, (S + fa::kTile - 1) / fa::kTile);
     const float scale = 1.0f / std::sqrt(static_cast<float>(c.qk()));
     // causal pairs x (qk + dv) multiply-adds
     const double work = 2.0 * Bc * c.H * (S * (S + 1.0) / 2.0) * (c.qk() + c.dv);
@@ -451,17 +451,23 @@ inline void backward_chunk(Context& cx, int Bc, int S) {
         // attention
         launch_rowdot(cx, w.dao16, b.ao, T, c.H, c.dv, w.Dd);
         {
-            dim3 grid((S + fa::kTile - 1) / fa::kTile, c.H, Bc);
+            dim3 grid(c.H, Bc, (S + fa::kTile - 1) / fa::kTile);
             const float scale = 1.0f / std::sqrt(static_cast<float>(qk));
             const double pairs = static_cast<double>(Bc) * c.H * (S * (S + 1.0) / 2.0);
             // dK/dV: S^T, dP^T, dV, dK products; dQ: S, dP, dQ products (2 flops per MAC)
             const double w_kv = pairs * 2.0 * (2 * qk + 2 * c.dv), w_q = pairs * 2.0 * (2 * qk + c.dv);
             if (qk == 64) {
-                MM_LAUNCH_TIMED(kKFlashBwd, w_kv, flash_bwd_dkdv_mma_kernel<64>, grid, 128, 0, b.q, b.k, b.v, w.dao16, b.lse, w.Dd, S, c.H, scale, w.dk, w.dv);
-                MM_LAUNCH_TIMED(kKFlashBwd, w_q, flash_bwd_dq_mma_kernel<64>, grid, 128, 0, b.q, b.k, b.v, w.dao16, b.lse, w.Dd, S, c.H, scale, w.dq);
+                set_dynamic_smem<flash_bwd_dkdv_mma_kernel<64>>(flash_dkdv_smem<64>());
+                set_dynamic_smem<flash_bwd_dq_mma_kernel<64>>(flash_dq_smem<64>());
+                MM_LAUNCH_TIMED(kKFlashBwd, w_kv, flash_bwd_dkdv_mma_kernel<64>, grid, 128, flash_dkdv_smem<64>(), b.q, b.k,
+                                b.v, w.dao16, b.lse, w.Dd, S, c.H, scale, w.dk, w.dv);
+                MM_LAUNCH_TIMED(kKFlashBwd, w_q, flash_bwd_dq_mma_kernel<64>, grid, 128, flash_dq_smem<64>(), b.q, b.k, b.v,
+                                w.dao16, b.lse, w.Dd, S, c.H, scale, w.dq);
             } else {
-                MM_LAUNCH_TIMED(kKFlashBwd, w_kv, flash_bwd_dkdv_mma_kernel<16>, grid, 128, 0, b.q, b.k, b.v, w.dao16, b.lse, w.Dd, S, c.H, scale, w.dk, w.dv);
-                MM_LAUNCH_TIMED(kKFlashBwd, w_q, flash_bwd_dq_mma_kernel<16>, grid, 128, 0, b.q, b.k, b.v, w.dao16, b.lse, w.Dd, S, c.H, scale, w.dq);
+                MM_LAUNCH_TIMED(kKFlashBwd, w_kv, flash_bwd_dkdv_mma_kernel<16>, grid, 128, flash_dkdv_smem<16>(), b.q, b.k,
+                                b.v, w.dao16, b.lse, w.Dd, S, c.H, scale, w.dk, w.dv);
+                MM_LAUNCH_TIMED(kKFlashBwd, w_q, flash_bwd_dq_mma_kernel<16>, grid, 128, flash_dq_smem<16>(), b.q, b.k, b.v,
+                                w.dao16, b.lse, w.Dd, S, c.H, scale, w.dq);
             }
         }
         const int ld_q16 = cx.d16(c.H * qk);

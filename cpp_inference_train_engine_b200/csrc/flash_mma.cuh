@@ -226,15 +226,18 @@ __global__ void attn_rowdot_kernel(const __half* __restrict__ dout, const __half
     Dd[idx] = s;
 }
 
-// dQ for one query tile (4 warps x 16 query rows). dout fp16 [B*S][H*D]. dq fp32 [B*S][H*D],
-// including the softmax scale. grid (H, B, ceil(S/64)), longest rows first; K/V tiles stream
+// dQ for one query tile (4 warps x 16 query rows). dout fp16 [B*S][H*D]. dq16 fp16 [B*S][ld],
+// including the softmax scale, with the inverse RoPE of columns [rope_begin, rope_begin +
+// rope) of every head applied at the row's position (the backward of the query rotation;
+// rope_rows_kernel's arithmetic with the angle negated). grid (H, B, ceil(S/64)), longest rows first; K/V tiles stream
 // through a two-deep cp.async ring. Dynamic shared memory: flash_dq_smem<D>() bytes.
 template <int D> constexpr int flash_dq_smem() { return 6 * fa::kTile * (D + 8) * 2; }
 template <int D>
 __global__ void __launch_bounds__(128, 4) flash_bwd_dq_mma_kernel(
     const __half* __restrict__ q, const __half* __restrict__ k, const __half* __restrict__ v,
     const __half* __restrict__ dout, const float* __restrict__ lse2, const float* __restrict__ Dd, int S, int H,
-    float scale, float* __restrict__ dq) {
+    float scale, __half* __restrict__ dq16, long long ld_dq, const float* __restrict__ cos_t,
+    const float* __restrict__ sin_t, int rope_begin, int rope) {
     MM_PDL_ENTRY();
     using namespace fa;
     constexpr int LD = D + 8;
@@ -301,15 +304,30 @@ __global__ void __launch_bounds__(128, 4) flash_bwd_dq_mma_kernel(
         }
         __syncthreads();
     }
+    const int half_r = rope / 2;
 #pragma unroll
     for (int i = 0; i < D / 8; ++i) {
-        const int col = h * D + i * 8 + 2 * t;
-        if (row0 < S) *reinterpret_cast<float2*>(dq + (base + row0) * ld + col) = make_float2(acc[i][0], acc[i][1]);
-        if (row1 < S) *reinterpret_cast<float2*>(dq + (base + row1) * ld + col) = make_float2(acc[i][2], acc[i][3]);
+        const int cc = i * 8 + 2 * t;  // column pair (cc, cc + 1) within the head
+        const bool rot = cc >= rope_begin && cc < rope_begin + rope;
+        const int pair = (cc - rope_begin) >> 1;
+#pragma unroll
+        for (int hr = 0; hr < 2; ++hr) {
+            const int row = hr ? row1 : row0;
+            if (row >= S) continue;
+            float a = acc[i][2 * hr], bb = acc[i][2 * hr + 1];
+            if (rot) {
+                const float cs = cos_t[row * half_r + pair], sn = -sin_t[row * half_r + pair];
+                const float x0 = a * cs - bb * sn, x1 = a * sn + bb * cs;
+                a = x0;
+                bb = x1;
+            }
+            *reinterpret_cast<__half2*>(dq16 + (base + row) * ld_dq + h * D + cc) = __floats2half2_rn(a, bb);
+        }
     }
 }
 
-// dK, dV for one key tile (4 warps x 16 keys). dk includes the softmax scale. grid (H, B,
+// dK, dV for one key tile (4 warps x 16 keys). dk (fp32) includes the softmax scale; dV
+// goes out in fp16 (dv16, row pitch ld_dv), the operand form its products use. grid (H, B,
 // ceil(S/64)), key tile = blockIdx.z (the first key tiles meet the most query tiles and
 // are scheduled first); Q/dO tiles and their lse/D rows stream through a two-deep cp.async
 // ring. Dynamic shared memory: flash_dkdv_smem<D>() bytes.
@@ -318,7 +336,7 @@ template <int D>
 __global__ void __launch_bounds__(128, 3) flash_bwd_dkdv_mma_kernel(
     const __half* __restrict__ q, const __half* __restrict__ k, const __half* __restrict__ v,
     const __half* __restrict__ dout, const float* __restrict__ lse2, const float* __restrict__ Dd, int S, int H,
-    float scale, float* __restrict__ dk, float* __restrict__ dv) {
+    float scale, float* __restrict__ dk, __half* __restrict__ dv16, long long ld_dv) {
     MM_PDL_ENTRY();
     using namespace fa;
     constexpr int LD = D + 8;
@@ -401,11 +419,11 @@ __global__ void __launch_bounds__(128, 3) flash_bwd_dkdv_mma_kernel(
         const int col = h * D + i * 8 + 2 * t;
         if (key0 < S) {
             *reinterpret_cast<float2*>(dk + (base + key0) * ld + col) = make_float2(accK[i][0], accK[i][1]);
-            *reinterpret_cast<float2*>(dv + (base + key0) * ld + col) = make_float2(accV[i][0], accV[i][1]);
+            *reinterpret_cast<__half2*>(dv16 + (base + key0) * ld_dv + col) = __floats2half2_rn(accV[i][0], accV[i][1]);
         }
         if (key1 < S) {
             *reinterpret_cast<float2*>(dk + (base + key1) * ld + col) = make_float2(accK[i][2], accK[i][3]);
-            *reinterpret_cast<float2*>(dv + (base + key1) * ld + col) = make_float2(accV[i][2], accV[i][3]);
+            *reinterpret_cast<__half2*>(dv16 + (base + key1) * ld_dv + col) = __floats2half2_rn(accV[i][2], accV[i][3]);
         }
     }
 }

@@ -115,9 +115,7 @@ template <class A> void plan_workspace(Context& cx, A& a, int T, bool tape) {
         w.dh2 = a.template take<float>(t * c.d);
         w.dres = a.template take<float>(t * c.d);
         w.dao = a.template take<float>(t * c.aw());
-        w.dq = a.template take<float>(t * c.H * c.qk());
         w.dk = a.template take<float>(t * c.H * c.qk());
-        w.dv = a.template take<float>(t * c.aw());
         w.drope = a.template take<float>(t * c.rope);
         w.drope2 = a.template take<float>(t * c.rope);
         w.dckv = a.template take<float>(t * c.kvr);
@@ -417,11 +415,12 @@ inline void backward_chunk(Context& cx, int Bc, int S) {
         o.alpha_ptr = inv_s;
         gemm(cx, c.V, c.d, T, {w.g16, c.V, true}, {w.h3, ld3, true}, o);  // h_hi = h3[:, :d]
     }
-    launch_rmsnorm_backward(cx, w.x_out, c.d, cx.FinalNorm(), w.dh, c.d, (const float*)nullptr, 0LL, T, c.d, w.dy, c.d, (__half*)nullptr, 0LL, cx.GFinalNorm(), inv_s);
+    // dy (fp32, the residual gradient) and its fp16 copy for the layer's products
+    launch_rmsnorm_backward(cx, w.x_out, c.d, cx.FinalNorm(), w.dh, c.d, (const float*)nullptr, 0LL, T, c.d, w.dy, c.d,
+                            w.dy16, ld_d, cx.GFinalNorm(), inv_s);
     for (int l = c.L - 1; l >= 0; --l) {
         LayerBuf& b = w.layers[l];
         // feed-forward block
-        launch_to_half(cx, w.dy, c.d, T, c.d, w.dy16, ld_d);
         {
             GemmOutSpec o{cx.G(l, kWdown), c.d, kOutF32Acc};
             o.alpha_ptr = inv_s;
@@ -456,27 +455,28 @@ inline void backward_chunk(Context& cx, int Bc, int S) {
             const double pairs = static_cast<double>(Bc) * c.H * (S * (S + 1.0) / 2.0);
             // dK/dV: S^T, dP^T, dV, dK products; dQ: S, dP, dQ products (2 flops per MAC)
             const double w_kv = pairs * 2.0 * (2 * qk + 2 * c.dv), w_q = pairs * 2.0 * (2 * qk + c.dv);
+            const int ld_q16 = cx.d16(c.H * qk), ld_v16 = cx.d16(aw);
             if (qk == 64) {
                 set_dynamic_smem<flash_bwd_dkdv_mma_kernel<64>>(flash_dkdv_smem<64>());
                 set_dynamic_smem<flash_bwd_dq_mma_kernel<64>>(flash_dq_smem<64>());
                 MM_LAUNCH_TIMED(kKFlashBwd, w_kv, flash_bwd_dkdv_mma_kernel<64>, grid, 128, flash_dkdv_smem<64>(), b.q, b.k,
-                                b.v, w.dao16, b.lse, w.Dd, S, c.H, scale, w.dk, w.dv);
+                                b.v, w.dao16, b.lse, w.Dd, S, c.H, scale, w.dk, w.dv16, (long long)ld_v16);
                 MM_LAUNCH_TIMED(kKFlashBwd, w_q, flash_bwd_dq_mma_kernel<64>, grid, 128, flash_dq_smem<64>(), b.q, b.k, b.v,
-                                w.dao16, b.lse, w.Dd, S, c.H, scale, w.dq);
+                                w.dao16, b.lse, w.Dd, S, c.H, scale, w.dq16, (long long)ld_q16, cx.cos_t, cx.sin_t,
+                                c.nope, c.rope);
             } else {
                 MM_LAUNCH_TIMED(kKFlashBwd, w_kv, flash_bwd_dkdv_mma_kernel<16>, grid, 128, flash_dkdv_smem<16>(), b.q, b.k,
-                                b.v, w.dao16, b.lse, w.Dd, S, c.H, scale, w.dk, w.dv);
+                                b.v, w.dao16, b.lse, w.Dd, S, c.H, scale, w.dk, w.dv16, (long long)ld_v16);
                 MM_LAUNCH_TIMED(kKFlashBwd, w_q, flash_bwd_dq_mma_kernel<16>, grid, 128, flash_dq_smem<16>(), b.q, b.k, b.v,
-                                w.dao16, b.lse, w.Dd, S, c.H, scale, w.dq);
+                                w.dao16, b.lse, w.Dd, S, c.H, scale, w.dq16, (long long)ld_q16, cx.cos_t, cx.sin_t,
+                                c.nope, c.rope);
             }
         }
         const int ld_q16 = cx.d16(c.H * qk);
-        launch_rope_rows(cx, w.dq, (c.H * qk), T, S, (const int*)nullptr, c.H, qk, c.nope, c.rope, 1, (float*)nullptr, 0LL, w.dq16, ld_q16);
         const int ld_kn16 = cx.d16(c.H * c.nope);
         MM_LAUNCH(split_dk_kernel, warp_rows_grid(T), 256, 0, w.dk, T, c.H, c.nope, c.rope, w.dkn16, (long long)ld_kn16, w.drope);
         launch_rope_rows(cx, w.drope, c.rope, T, S, (const int*)nullptr, 1, c.rope, 0, c.rope, 1, w.drope2, c.rope, (__half*)nullptr, 0LL);
         const int ld_v16 = cx.d16(aw);
-        launch_to_half(cx, w.dv, aw, T, aw, w.dv16, ld_v16);
         {
             GemmOutSpec o{cx.G(l, kWuk), c.H * c.nope, kOutF32Acc};
             o.alpha_ptr = inv_s;
@@ -510,7 +510,8 @@ inline void backward_chunk(Context& cx, int Bc, int S) {
         }
         // dh = [d raw_cq | d kv_pack] . [W_dq | W_dkv]^T, one product over K = qr + kvw
         gemm(cx, T, c.d, qkv, {w.draw16, ld_qkv16, false}, {cx.prep[l].Wa, cx.prep[l].lda, false}, {w.dh, c.d, kOutF32});
-        launch_rmsnorm_backward(cx, b.x_in, c.d, cx.W(l, kAttnNorm), w.dh, c.d, w.dres, c.d, T, c.d, w.dy, c.d, (__half*)nullptr, 0LL, cx.G(l, kAttnNorm), inv_s);
+        launch_rmsnorm_backward(cx, b.x_in, c.d, cx.W(l, kAttnNorm), w.dh, c.d, w.dres, c.d, T, c.d, w.dy, c.d, w.dy16,
+                                ld_d, cx.G(l, kAttnNorm), inv_s);
     }
     MM_LAUNCH(embed_backward_kernel, warp_rows_grid(T), 256, 0, w.tokens, w.dy, T, c.d, cx.GE(), inv_s);
 }

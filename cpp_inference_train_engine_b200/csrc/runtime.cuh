@@ -158,7 +158,7 @@ struct Workspace {
     float* q_pre;       // [T][H*qk]
     float* knope;       // [T][H*nope]
     // backward scratch (tape only)
-    float *dy, *dgated, *dh2, *dres, *dao, *dq, *dk, *dv, *drope, *drope2, *dckv, *dkvraw, *dh, *dcq, *Dd;
+    float *dy, *dgated, *dh2, *dres, *dao, *dk, *drope, *drope2, *dckv, *dkvraw, *dh, *dcq, *Dd;
     __half *dy16, *dg16, *du16, *dres16, *dq16, *dkn16, *dv16, *dkvp16, *draw16, *g16, *dao16;
     float* norm_part;   // [kNormBlocks][max(d, qr, kv_rank)] RMSNorm weight-gradient partials
 };

@@ -86,9 +86,17 @@ inline int gemm(Context& cx, int M, int N, int K, Opnd A, Opnd B, const GemmOutS
     } else {
         tc = &tensor_map_t(o.out, map_type, N, M, o.ldc, ch, 32);
     }
+    // A grid that fits one wave (the decode-time products, M = batch) has each CTA's whole
+    // K loop on the critical path: a deeper TMA ring keeps more of it in flight.
+    const bool one_wave = tiles * splits <= sm_count();
     if (BN == 256) launch_gemm_bn<256, 4>(cx, ta, tb, *tc, ga);
-    else if (BN == 128) launch_gemm_bn<128, 3>(cx, ta, tb, *tc, ga);
-    else launch_gemm_bn<64, 4>(cx, ta, tb, *tc, ga);
+    else if (BN == 128) {
+        if (one_wave && num_k > 3) launch_gemm_bn<128, 6>(cx, ta, tb, *tc, ga);
+        else launch_gemm_bn<128, 3>(cx, ta, tb, *tc, ga);
+    } else {
+        if (one_wave && num_k > 4) launch_gemm_bn<64, 8>(cx, ta, tb, *tc, ga);
+        else launch_gemm_bn<64, 4>(cx, ta, tb, *tc, ga);
+    }
     if (splits > 1) {
         // partial of split z, row r: part[(z * Mp + r) * n_pad + c]; reduce over a dense view
         const int Mp = ga.split_rows;

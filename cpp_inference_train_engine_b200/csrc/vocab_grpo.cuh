@@ -221,6 +221,7 @@ __device__ __forceinline__ uint32_t float_key(float f) {
 constexpr int kSampleThreads = 512;
 constexpr int kSampleBuckets = 2048;
 constexpr int kSampleCap = 1024;
+constexpr int kSampleCache = 32;  // scores per thread held in registers (rows up to 16384)
 
 // Block-wide inclusive prefix sum of one u64 per thread (blockDim.x = kSampleThreads).
 __device__ __forceinline__ unsigned long long block_scan_incl(unsigned long long v, unsigned long long* warp_tot) {
@@ -252,7 +253,8 @@ __device__ __forceinline__ unsigned long long block_scan_incl(unsigned long long
 // inference.cpp:410-411), so a row of at most 65535 weights sums below 2^64 and every
 // partial sum is exact and independent of the order of addition.
 __device__ __forceinline__ unsigned long long sample_weight_q(float s, float s0, double T) {
-    return __double2ull_rn(exp(static_cast<double>(__fsub_rn(s, s0)) / T) * 281474976710656.0);
+    const double d = static_cast<double>(__fsub_rn(s, s0));
+    return __double2ull_rn(exp(T == 1.0 ? d : d / T) * 281474976710656.0);  // d / 1 == d exactly
 }
 
 // The draw u * total in the same fixed point, with the reference's 24-bit uniform
@@ -339,13 +341,12 @@ __device__ void sample_locate(SampleShared& S, int nb, bool first, uint64_t seed
 // Gathers the scores selected by `in_set` (at most kSampleCap of them), sorts them (score
 // descending, id ascending) and returns the id where their running mass reaches S.s_draw
 // (the last one when none does; `none` when the set is empty).
-template <class Pred>
-__device__ int sample_pick(SampleShared& S, const float* __restrict__ row, int V, float s0, double T, Pred in_set,
-                           int none) {
+// `each(f)` calls f(id, score) for this thread's share of the row.
+template <class Each, class Pred>
+__device__ int sample_pick(SampleShared& S, Each each, float s0, double T, Pred in_set, int none) {
     if (threadIdx.x == 0) S.s_ncand = 0;
     __syncthreads();
-    for (int j = threadIdx.x; j < V; j += blockDim.x) {
-        const float v = row[j];
+    each([&](int j, float v) {
         if (in_set(v)) {
             const int slot = atomicAdd(&S.s_ncand, 1);
             if (slot < kSampleCap) {
@@ -354,7 +355,7 @@ __device__ int sample_pick(SampleShared& S, const float* __restrict__ row, int V
                 S.cand_w[slot] = sample_weight_q(v, s0, T);
             }
         }
-    }
+    });
     __syncthreads();
     const int n = min(S.s_ncand, kSampleCap);
     int np2 = 1;
@@ -443,15 +444,35 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(
     if (active && !active[b]) return;
     const float* row = logits + b * ld;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    // Rows up to kSampleCache * kSampleThreads scores stay in registers across the passes.
+    const bool cached = V <= kSampleCache * kSampleThreads;
+    float vals[kSampleCache];
+    if (cached) {
+#pragma unroll
+        for (int k = 0; k < kSampleCache; ++k) {
+            const int j = threadIdx.x + k * kSampleThreads;
+            vals[k] = j < V ? row[j] : 0.f;
+        }
+    }
+    auto each = [&](auto&& f) {
+        if (cached) {
+#pragma unroll
+            for (int k = 0; k < kSampleCache; ++k) {
+                const int j = threadIdx.x + k * kSampleThreads;
+                if (j < V) f(j, vals[k]);
+            }
+        } else {
+            for (int j = threadIdx.x; j < V; j += kSampleThreads) f(j, row[j]);
+        }
+    };
 
     // maximum with its first index, and minimum
     float mx = -INFINITY, mn = INFINITY;
     int mi = 0x7fffffff;
-    for (int j = threadIdx.x; j < V; j += blockDim.x) {
-        const float v = row[j];
+    each([&](int j, float v) {
         if (v > mx) { mx = v; mi = j; }
         mn = fminf(mn, v);
-    }
+    });
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
         const float ov = __shfl_xor_sync(0xffffffffu, mx, o);
@@ -494,17 +515,16 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(
         };
         for (int i = threadIdx.x; i < kSampleBuckets; i += blockDim.x) { S.hist[i] = 0ull; S.hcount[i] = 0; }
         __syncthreads();
-        for (int j = threadIdx.x; j < V; j += blockDim.x) {
-            const float v = row[j];
+        each([&](int, float v) {
             const int bk = bucket_of(v);
             atomicAdd(&S.hist[bk], sample_weight_q(v, s0, T));
             atomicAdd(&S.hcount[bk], 1);
-        }
+        });
         __syncthreads();
         sample_locate(S, kSampleBuckets, true, seed, k);
         const int chosen = S.s_chosen;
         if (S.hcount[chosen] <= kSampleCap) {
-            const int tok = sample_pick(S, row, V, s0, T, [&](float v) { return bucket_of(v) == chosen; }, best);
+            const int tok = sample_pick(S, each, s0, T, [&](float v) { return bucket_of(v) == chosen; }, best);
             if (threadIdx.x == 0) out[b * out_stride] = static_cast<uint16_t>(tok);
             return;
         }
@@ -574,7 +594,7 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(
         }
         return;
     }
-    const int tok = sample_pick(S, row, V, s0, T, [&](float v) {
+    const int tok = sample_pick(S, each, s0, T, [&](float v) {
         const uint32_t key = float_key(v);
         return (bits >= 32 ? key : (key >> (32 - bits))) == prefix;
     }, best);

@@ -98,71 +98,6 @@ __global__ void advance_pos_kernel(int* pos, int B) {
     if (b < B) pos[b] += 1;
 }
 
-// After the [W_dq | W_dkv] product of one decode step, per row b of y = [raw_cq (qr) |
-// raw latent (kvr) | raw rope key (rope)]: cq16 = RMSNorm(raw_cq) (fp16), and the cache row at
-// position pos[b] = [RMSNorm(raw latent) | RoPE(raw rope key, pos[b])] in fp16 (the
-// rmsnorm_kernel / rope_key_kernel / cache_write_kernel sequence in one pass, same float
-// expressions). One warp per row; qr, kvr and rope multiples of 4, y rows 16-byte aligned.
-__global__ void decode_latent_kernel(const float* __restrict__ y, long long ldy, int qr, int kvr, int rope,
-                                     const float* __restrict__ w_q, const float* __restrict__ w_kv, float eps,
-                                     const int* __restrict__ pos, const float* __restrict__ cos_t,
-                                     const float* __restrict__ sin_t, int B, __half* __restrict__ cq16,
-                                     long long ld_cq, __half* __restrict__ cache, int Sc) {
-    MM_PDL_ENTRY();
-    const int b = warp_row(), lane = threadIdx.x & 31;
-    if (b >= B) return;
-    const float* row = y + b * ldy;
-    const int n4 = (qr + kvr + rope) >> 2;
-    constexpr int MAXV = 4;  // up to 512 values per row
-    float4 v[MAXV];
-    float sq = 0.f, sk = 0.f;
-#pragma unroll
-    for (int k = 0; k < MAXV; ++k) {
-        const int q = k * 32 + lane;
-        if (q < n4) {
-            v[k] = *reinterpret_cast<const float4*>(row + 4 * q);
-            const float s = v[k].x * v[k].x + v[k].y * v[k].y + v[k].z * v[k].z + v[k].w * v[k].w;
-            if (4 * q < qr) sq += s;
-            else if (4 * q < qr + kvr) sk += s;
-        }
-    }
-    sq = warp_sum(sq);
-    sk = warp_sum(sk);
-    const float iq = 1.0f / sqrtf(sq / static_cast<float>(qr) + eps);
-    const float ik = 1.0f / sqrtf(sk / static_cast<float>(kvr) + eps);
-    const int p = pos[b];
-    const bool store_cache = p < Sc;
-    __half* crow = cache + (static_cast<long long>(b) * Sc + p) * (kvr + rope);
-    const int half_r = rope / 2;
-#pragma unroll
-    for (int k = 0; k < MAXV; ++k) {
-        const int q = k * 32 + lane, c = 4 * q;
-        if (q >= n4) continue;
-        float f[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
-        if (c < qr) {
-            const float4 wv = *reinterpret_cast<const float4*>(w_q + c);
-            *reinterpret_cast<uint2*>(cq16 + b * ld_cq + c) =
-                pack_h4(f[0] * iq * wv.x, f[1] * iq * wv.y, f[2] * iq * wv.z, f[3] * iq * wv.w);
-        } else if (c < qr + kvr) {
-            const float4 wv = *reinterpret_cast<const float4*>(w_kv + (c - qr));
-            if (store_cache)
-                *reinterpret_cast<uint2*>(crow + (c - qr)) =
-                    pack_h4(f[0] * ik * wv.x, f[1] * ik * wv.y, f[2] * ik * wv.z, f[3] * ik * wv.w);
-        } else {
-            const int j = c - qr - kvr;  // even: two rotation pairs
-#pragma unroll
-            for (int e = 0; e < 4; e += 2) {
-                const int pair = (j + e) >> 1;
-                const float cs = cos_t[p * half_r + pair], sn = sin_t[p * half_r + pair];
-                const float a = f[e], bb = f[e + 1];
-                f[e] = a * cs - bb * sn;
-                f[e + 1] = a * sn + bb * cs;
-            }
-            if (store_cache) *reinterpret_cast<uint2*>(crow + kvr + j) = pack_h4(f[0], f[1], f[2], f[3]);
-        }
-    }
-}
-
 // One decode step for every row: dec.tok holds the tokens to append at dec.pos.
 inline void decode_step(Context& cx) {
     const Dims& c = cx.c;
@@ -178,9 +113,9 @@ inline void decode_step(Context& cx) {
                                   ld_qr % 4 == 0;
         __half* cache_l = d.cache + static_cast<long long>(l) * B * d.Sc * kvw;
         if (fused_latent) {
-            MM_LAUNCH(decode_latent_kernel, warp_rows_grid(B), 256, 0, d.y, (long long)qrk, c.qr, c.kvr, c.rope,
-                      cx.W(l, kQNorm), cx.W(l, kKvNorm), c.eps, d.pos, cx.cos_t, cx.sin_t, B, d.cq16, (long long)ld_qr,
-                      cache_l, d.Sc);
+            MM_LAUNCH(latent_kernel, warp_rows_grid(B), 256, 0, d.y, (long long)qrk, c.qr, c.kvr, c.rope, cx.W(l, kQNorm),
+                      cx.W(l, kKvNorm), c.eps, B, 1, (const int*)d.pos, 0, cx.cos_t, cx.sin_t, d.cq16, (long long)ld_qr,
+                      (__half*)nullptr, 0LL, (float*)nullptr, cache_l, d.Sc);
         } else {
             launch_rmsnorm(cx, d.y, qrk, cx.W(l, kQNorm), B, c.qr, (float*)nullptr, 0LL, d.cq16, ld_qr);
             launch_rmsnorm(cx, d.y + c.qr, qrk, cx.W(l, kKvNorm), B, c.kvr, (float*)nullptr, 0LL, d.lat16, ld_kvr);

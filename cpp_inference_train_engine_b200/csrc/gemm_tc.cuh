@@ -50,6 +50,12 @@ struct GemmArgs {
     // [n0, n0 + BN/2) and the matching up columns into one accumulator and stores
     // gate * sigmoid(gate) * up for output columns [n0, n0 + BN/2). 0 = off.
     int glu_n;
+    // Adjacent-pair RoPE on an fp16 output: within every rope_period columns, pairs in
+    // [rope_begin, rope_begin + rope_len) are rotated to position row % rope_seq with the
+    // tables rope_cos/rope_sin [positions][rope_len / 2]. Null = off.
+    const float* rope_cos;
+    const float* rope_sin;
+    int rope_seq, rope_period, rope_begin, rope_len;
 };
 
 constexpr int kGemmBM = 128;
@@ -304,6 +310,19 @@ __global__ void __launch_bounds__(192, 1)
                 }
                 __syncwarp();
                 uint8_t* rowp = stage + lane * 128;
+                if (half_out && g.rope_cos && row < g.M) {
+                    const int p = row % g.rope_seq, hr = g.rope_len >> 1;
+#pragma unroll
+                    for (int i = 0; i < 64; i += 2) {
+                        const int cc = (col0 + i) % g.rope_period - g.rope_begin;
+                        if (cc >= 0 && cc < g.rope_len) {
+                            const float cs = g.rope_cos[p * hr + (cc >> 1)], sn = g.rope_sin[p * hr + (cc >> 1)];
+                            const float a = v[i], bb = v[i + 1];
+                            v[i] = a * cs - bb * sn;
+                            v[i + 1] = a * sn + bb * cs;
+                        }
+                    }
+                }
                 if (half_out) {
 #pragma unroll
                     for (int ch = 0; ch < 8; ++ch) {

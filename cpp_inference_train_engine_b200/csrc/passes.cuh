@@ -25,6 +25,77 @@ __global__ void cache_write_kernel(const __half* __restrict__ ckv, long long ldc
     dst[j] = j < kvr ? ckv[t * ldckv + j] : __float2half_rn(k_rope[t * rope + (j - kvr)]);
 }
 
+// After the [W_dq | W_dkv] product, per token row t of y = [raw_cq (qr) | raw latent (kvr)
+// | raw rope key (rope)]: cq16 = RMSNorm(raw_cq) (fp16); the normalised latent (fp16) into
+// ckv16 and/or the cache; the rope key rotated to its position into k_rope32 (fp32) and/or
+// the cache. Row t belongs to sequence t / S at position (pos_base ? pos_base[t / S] : 0) +
+// t % S; its cache row is row0 + t / S (positions >= Sc are not stored). This is the
+// rmsnorm_kernel / rope_key_kernel / cache_write_kernel sequence in one pass with the same
+// float expressions. One warp per row; qr, kvr, rope multiples of 4, 16-byte aligned y rows,
+// qr + kvr + rope <= 512.
+__global__ void latent_kernel(const float* __restrict__ y, long long ldy, int qr, int kvr, int rope,
+                              const float* __restrict__ w_q, const float* __restrict__ w_kv, float eps, int T, int S,
+                              const int* __restrict__ pos_base, int row0, const float* __restrict__ cos_t,
+                              const float* __restrict__ sin_t, __half* __restrict__ cq16, long long ld_cq,
+                              __half* __restrict__ ckv16, long long ld_ckv, float* __restrict__ k_rope32,
+                              __half* __restrict__ cache, int Sc) {
+    MM_PDL_ENTRY();
+    const int t = warp_row(), lane = threadIdx.x & 31;
+    if (t >= T) return;
+    const float* row = y + t * ldy;
+    const int n4 = (qr + kvr + rope) >> 2;
+    constexpr int MAXV = 4;  // up to 512 values per row
+    float4 v[MAXV];
+    float sq = 0.f, sk = 0.f;
+#pragma unroll
+    for (int k = 0; k < MAXV; ++k) {
+        const int q = k * 32 + lane;
+        if (q < n4) {
+            v[k] = *reinterpret_cast<const float4*>(row + 4 * q);
+            const float s = v[k].x * v[k].x + v[k].y * v[k].y + v[k].z * v[k].z + v[k].w * v[k].w;
+            if (4 * q < qr) sq += s;
+            else if (4 * q < qr + kvr) sk += s;
+        }
+    }
+    sq = warp_sum(sq);
+    sk = warp_sum(sk);
+    const float iq = 1.0f / sqrtf(sq / static_cast<float>(qr) + eps);
+    const float ik = 1.0f / sqrtf(sk / static_cast<float>(kvr) + eps);
+    const int seq = t / S;
+    const int p = (pos_base ? pos_base[seq] : 0) + t % S;
+    const bool to_cache = cache && p < Sc;
+    __half* crow = to_cache ? cache + (static_cast<long long>(row0 + seq) * Sc + p) * (kvr + rope) : nullptr;
+    const int half_r = rope / 2;
+#pragma unroll
+    for (int k = 0; k < MAXV; ++k) {
+        const int q = k * 32 + lane, c = 4 * q;
+        if (q >= n4) continue;
+        float f[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
+        if (c < qr) {
+            const float4 wv = *reinterpret_cast<const float4*>(w_q + c);
+            *reinterpret_cast<uint2*>(cq16 + t * ld_cq + c) =
+                pack_h4(f[0] * iq * wv.x, f[1] * iq * wv.y, f[2] * iq * wv.z, f[3] * iq * wv.w);
+        } else if (c < qr + kvr) {
+            const float4 wv = *reinterpret_cast<const float4*>(w_kv + (c - qr));
+            const uint2 h = pack_h4(f[0] * ik * wv.x, f[1] * ik * wv.y, f[2] * ik * wv.z, f[3] * ik * wv.w);
+            if (ckv16) *reinterpret_cast<uint2*>(ckv16 + t * ld_ckv + (c - qr)) = h;
+            if (to_cache) *reinterpret_cast<uint2*>(crow + (c - qr)) = h;
+        } else {
+            const int j = c - qr - kvr;  // even: two rotation pairs
+#pragma unroll
+            for (int e = 0; e < 4; e += 2) {
+                const int pair = (j + e) >> 1;
+                const float cs = cos_t[p * half_r + pair], sn = sin_t[p * half_r + pair];
+                const float a = f[e], bb = f[e + 1];
+                f[e] = a * cs - bb * sn;
+                f[e + 1] = a * sn + bb * cs;
+            }
+            if (k_rope32) *reinterpret_cast<float4*>(k_rope32 + t * rope + j) = make_float4(f[0], f[1], f[2], f[3]);
+            if (to_cache) *reinterpret_cast<uint2*>(crow + kvr + j) = pack_h4(f[0], f[1], f[2], f[3]);
+        }
+    }
+}
+
 // h3 rows for the vocabulary head from fp32 rows in[t * mul + add].
 __global__ void split3_gather_kernel(const float* __restrict__ h, int d, int T, int mul, int add,
                                      __half* __restrict__ h3, long long ld3) {
@@ -107,7 +178,6 @@ template <class A> void plan_workspace(Context& cx, A& a, int T, bool tape) {
     w.coef = a.template take<float>(t);
     w.old_lp = a.template take<float>(t);
     w.ref_lp = a.template take<float>(t);
-    w.q_pre = a.template take<float>(t * c.H * c.qk());
     w.knope = a.template take<float>(t * c.H * c.nope);
     if (tape) {
         w.dy = a.template take<float>(t * c.d);
@@ -324,15 +394,36 @@ inline void forward_chunk(Context& cx, int Bc, int S, bool tape, VocabMode vm, b
         const PrepLayer& pw = cx.prep[l];
         const int qkv = c.qr + kvw;
         gemm(cx, T, qkv, c.d, {b.h, ld_d, false}, {pw.Wa, pw.lda, true}, {b.raw_cq, qkv, kOutF32});
-        launch_rmsnorm(cx, b.raw_cq, qkv, cx.W(l, kQNorm), T, c.qr, (float*)nullptr, 0LL, b.cq, ld_qr);
-        gemm(cx, T, c.H * qk, c.qr, {b.cq, ld_qr, false}, {cx.S(l, kWuq), cx.SL(l, kWuq), true}, {w.q_pre, c.H * qk, kOutF32});
-        launch_rope_rows(cx, w.q_pre, (c.H * qk), T, S, (const int*)nullptr, c.H, qk, c.nope, c.rope, 0, (float*)nullptr, 0LL, b.q, (c.H * qk));
-        launch_rmsnorm(cx, b.kvp, qkv, cx.W(l, kKvNorm), T, c.kvr, (float*)nullptr, 0LL, b.ckv, ld_kvr);
-        MM_LAUNCH(rope_key_kernel, blocks_for((long long)T * (c.rope / 2), 256), 256, 0, b.kvp, (long long)qkv, c.kvr,
-                  c.rope, T, S, (const int*)nullptr, cx.cos_t, cx.sin_t, b.k_rope, (__half*)nullptr, 0LL);
-        if (cache)
-            MM_LAUNCH(cache_write_kernel, blocks_for((long long)T * kvw, 256), 256, 0, b.ckv, (long long)ld_kvr, b.k_rope,
-                      T, S, (const int*)nullptr, row0, cache + (long long)l * cx.dec.B * Sc * kvw, Sc, c.kvr, c.rope);
+        // both latent norms, the rope key and the prefill cache rows in one pass when the
+        // widths allow 16-byte rows
+        const bool fused_latent = c.qr % 4 == 0 && c.kvr % 4 == 0 && c.rope % 4 == 0 && qkv % 4 == 0 && qkv <= 512 &&
+                                  ld_qr % 4 == 0 && ld_kvr % 4 == 0;
+        __half* cache_l = cache ? cache + (long long)l * cx.dec.B * Sc * kvw : nullptr;
+        if (fused_latent)
+            MM_LAUNCH(latent_kernel, warp_rows_grid(T), 256, 0, b.raw_cq, (long long)qkv, c.qr, c.kvr, c.rope,
+                      cx.W(l, kQNorm), cx.W(l, kKvNorm), c.eps, T, S, (const int*)nullptr, row0, cx.cos_t, cx.sin_t,
+                      b.cq, (long long)ld_qr, b.ckv, (long long)ld_kvr, b.k_rope, cache_l, Sc);
+        else
+            launch_rmsnorm(cx, b.raw_cq, qkv, cx.W(l, kQNorm), T, c.qr, (float*)nullptr, 0LL, b.cq, ld_qr);
+        {
+            // q = cq . W_uq with the rope part of every head rotated in the epilogue (fp16)
+            GemmOutSpec o{b.q, c.H * qk, kOutF16};
+            o.rope_cos = cx.cos_t;
+            o.rope_sin = cx.sin_t;
+            o.rope_seq = S;
+            o.rope_period = qk;
+            o.rope_begin = c.nope;
+            o.rope_len = c.rope;
+            gemm(cx, T, c.H * qk, c.qr, {b.cq, ld_qr, false}, {cx.S(l, kWuq), cx.SL(l, kWuq), true}, o);
+        }
+        if (!fused_latent) {
+            launch_rmsnorm(cx, b.kvp, qkv, cx.W(l, kKvNorm), T, c.kvr, (float*)nullptr, 0LL, b.ckv, ld_kvr);
+            MM_LAUNCH(rope_key_kernel, blocks_for((long long)T * (c.rope / 2), 256), 256, 0, b.kvp, (long long)qkv,
+                      c.kvr, c.rope, T, S, (const int*)nullptr, cx.cos_t, cx.sin_t, b.k_rope, (__half*)nullptr, 0LL);
+            if (cache)
+                MM_LAUNCH(cache_write_kernel, blocks_for((long long)T * kvw, 256), 256, 0, b.ckv, (long long)ld_kvr,
+                          b.k_rope, T, S, (const int*)nullptr, row0, cache_l, Sc, c.kvr, c.rope);
+        }
         gemm(cx, T, c.H * c.nope, c.kvr, {b.ckv, ld_kvr, false}, {cx.S(l, kWuk), cx.SL(l, kWuk), true},
              {w.knope, c.H * c.nope, kOutF32});
         launch_assemble_k(cx, w.knope, (c.H * c.nope), b.k_rope, T, b.k, (c.H * qk));

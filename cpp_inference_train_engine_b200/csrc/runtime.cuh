@@ -155,7 +155,6 @@ struct Workspace {
     float* old_lp;      // [T]
     float* ref_lp;      // [T]
     // scratch
-    float* q_pre;       // [T][H*qk]
     float* knope;       // [T][H*nope]
     // backward scratch (tape only)
     float *dy, *dgated, *dh2, *dres, *dao, *dk, *drope, *drope2, *dckv, *dkvraw, *dh, *dcq, *Dd;
@@ -432,6 +431,10 @@ struct GemmOutSpec {
     // SwiGLU output (GemmArgs::glu_n): N = output columns, B holds [gate | up] with the up
     // half glu_n columns after the gate half; fp16 output, B MN-major
     int glu_n = 0;
+    // RoPE on an fp16 output (GemmArgs::rope_cos): position = row % rope_seq
+    const float* rope_cos = nullptr;
+    const float* rope_sin = nullptr;
+    int rope_seq = 1, rope_period = 1, rope_begin = 0, rope_len = 0;
 };
 
 inline int sm_count() {

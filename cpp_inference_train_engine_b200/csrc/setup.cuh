@@ -26,6 +26,9 @@ inline int gemm(Context& cx, int M, int N, int K, Opnd A, Opnd B, const GemmOutS
     GemmOutSpec o = o_in;
     if (o.lse_part && (o.kind != kOutF32 || o.residual || !o.targets || !o.tgt_logit))
         fail(MM_INVALID_ARGUMENT, "log-sum-exp epilogue needs a plain fp32 product with targets");
+    if (o.rope_cos && (o.kind != kOutF16 || o.glu_n || o.rope_len % 2 || o.rope_begin % 2 || o.rope_period < 1 ||
+                       o.rope_seq < 1))
+        fail(MM_INVALID_ARGUMENT, "RoPE epilogue needs a plain fp16 product");
     if (o.glu_n && (o.kind != kOutF16 || o.residual || o.lse_part || !B.mn || o.glu_n < N))
         fail(MM_INVALID_ARGUMENT, "SwiGLU epilogue needs an fp16 product with [gate | up] MN-major weights");
     if (o.residual) {
@@ -53,7 +56,8 @@ inline int gemm(Context& cx, int M, int N, int K, Opnd A, Opnd B, const GemmOutS
                                  : tensor_map(B.p, bf16, K, nb, B.ld, 64, BN);
     GemmArgs ga{M, N, K, A.mn ? 1 : 0, B.mn ? 1 : 0, bf16 ? 1 : 0, o.kind,
                 o.residual, o.ldr, o.alpha, o.alpha_ptr, cx.d_err, 0, 0,
-                o.lse_part, o.targets, o.tgt_logit, (o.lse_part && o.no_store) ? 1 : 0, o.glu_n};
+                o.lse_part, o.targets, o.tgt_logit, (o.lse_part && o.no_store) ? 1 : 0, o.glu_n,
+                o.rope_cos, o.rope_sin, o.rope_seq, o.rope_period, o.rope_begin, o.rope_len};
     // Split-K for accumulating products with few output tiles over a long K (the weight
     // gradients, K = tokens): each K slice stores its fp32 partial, then one reduction adds
     // them in order into the destination.

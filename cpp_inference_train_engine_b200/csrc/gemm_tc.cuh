@@ -38,9 +38,10 @@ struct GemmArgs {
     int k_tiles_per_split;  // split-K: tiles of split z cover k-tiles [z*per, (z+1)*per); 0 = all
     int split_rows;         // split-K: rows of the output map per split (M rounded up to 128)
     // Row log-sum-exp partials (the vocabulary head, fp32 output, no split): per output
-    // tile and row, (max, sum exp(x - max)) over the tile's columns into
-    // lse_part[n_tile * M + row], and the value in column targets[row] into tgt_logit[row]
-    // (written by the one tile holding that column). no_store skips the output itself.
+    // tile, epilogue half (0/1) and row, (max, sum exp(x - max)) over the columns that half
+    // drains into lse_part[(n_tile * 2 + half) * M + row] (max -inf, sum 0 when it drains
+    // none), and the value in column targets[row] into tgt_logit[row] (written by the one
+    // warp holding that column). no_store skips the output itself.
     float2* lse_part;
     const uint16_t* targets;
     float* tgt_logit;
@@ -60,17 +61,21 @@ struct GemmArgs {
 
 constexpr int kGemmBM = 128;
 constexpr int kGemmBK = 64;
-// 32-row x 128-byte staging tiles per epilogue warp: with two, a warp fills one while the
-// TMA store of the other is still reading it (the 256-wide tile, one CTA per SM); the
-// narrower tiles keep one so that two CTAs fit on an SM.
-template <int BN> constexpr int epi_bufs() { return BN == 256 ? 2 : 1; }
+// Epilogue warps: two per TMEM lane quadrant for the 256-wide tile (one CTA per SM; they
+// take alternate column chunks, so a short-K product's epilogue keeps up with its MMAs),
+// one per quadrant for the narrower tiles (two CTAs per SM). Each owns one 32-row x
+// 128-byte staging tile.
+template <int BN> constexpr int epi_warps() { return BN == 256 ? 8 : 4; }
+template <int BN> constexpr int epi_bufs() { return 1; }
 
 template <int BN, int STAGES> struct GemmCfg {
     static constexpr int A_BYTES = kGemmBM * 128;
     static constexpr int B_BYTES = BN * 128;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int EPI_WARPS = epi_warps<BN>();
+    static constexpr int THREADS = 64 + 32 * EPI_WARPS;
     static constexpr int EPI_BUFS = epi_bufs<BN>();
-    static constexpr int EPI_BYTES = 4 * EPI_BUFS * 4096;
+    static constexpr int EPI_BYTES = EPI_WARPS * EPI_BUFS * 4096;
     static constexpr int SMEM = STAGES * STAGE_BYTES + EPI_BYTES + 1024 + 256;
 };
 
@@ -79,7 +84,7 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
 }
 
 template <int BN, int STAGES>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(320, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, GemmArgs g) {
     using C = GemmCfg<BN, STAGES>;
@@ -109,8 +114,8 @@ __global__ void __launch_bounds__(192, 1)
             }
             mbar_init(&acc_full[0], 1);
             mbar_init(&acc_full[1], 1);
-            mbar_init(&acc_empty[0], 4);
-            mbar_init(&acc_empty[1], 4);
+            mbar_init(&acc_empty[0], C::EPI_WARPS);
+            mbar_init(&acc_empty[1], C::EPI_WARPS);
             fence_mbar_init();
             prefetch_tmap(&tmA);
             prefetch_tmap(&tmB);
@@ -193,7 +198,9 @@ __global__ void __launch_bounds__(192, 1)
             tc_commit(&acc_full[buf]);
         }
     } else if (warp >= 2) {
-        const int q = warp & 3;
+        const int q = warp & 3;              // TMEM lane quadrant of this warp
+        const int half = (warp - 2) >> 2;    // which of the quadrant's warps (0 or 1)
+        const int nhalf = C::EPI_WARPS / 4;  // warps per quadrant
         uint8_t* stage_base = epi + (warp - 2) * C::EPI_BUFS * 4096;
         int sbuf = 0;  // staging tile the next chunk fills
         const float alpha = g.alpha * (g.alpha_ptr ? *g.alpha_ptr : 1.0f);
@@ -213,7 +220,12 @@ __global__ void __launch_bounds__(192, 1)
             const uint32_t src = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * BN);
             if (g.glu_n) {
                 // accumulator columns [0, TW) gate, [TW, 2 TW) up; 64 fp16 outputs per staged row
-                for (int c = 0; c < TW; c += 64) {
+                if (half * 64 >= TW) {  // no chunk for this warp: release the accumulator
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&acc_empty[buf]);
+                }
+                for (int c = half * 64; c < TW; c += 64 * nhalf) {
                     uint8_t* stage = stage_base + sbuf * 4096;
                     if (C::EPI_BUFS == 2) sbuf ^= 1;
                     if (lane == 0) {  // the store that last read `stage` is done
@@ -228,7 +240,7 @@ __global__ void __launch_bounds__(192, 1)
                         tmem_ld32_nowait(src + static_cast<uint32_t>(c + 32 * sub), gv);
                         tmem_ld32_nowait(src + static_cast<uint32_t>(TW + c + 32 * sub), uv);
                         tmem_wait_ld();
-                        if (sub == 1 && c + 64 >= TW) {
+                        if (sub == 1 && c + 64 * nhalf >= TW) {
                             tc_fence_before();
                             __syncwarp();
                             if (lane == 0) mbar_arrive(&acc_empty[buf]);
@@ -263,12 +275,17 @@ __global__ void __launch_bounds__(192, 1)
             // online (max, sum of exp) over this tile's columns of the row, and its target
             float run_m = -INFINITY, run_s = 0.f, run_t = 0.f;
             const int tg = (g.lse_part && row < g.M) ? static_cast<int>(g.targets[row]) : -1;
-            for (int c = 0; c < n_mma; c += CH) {
+            if (half * CH >= n_mma) {  // no chunk for this warp: release the accumulator
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&acc_empty[buf]);
+            }
+            for (int c = half * CH; c < n_mma; c += CH * nhalf) {
                 float v[64];
                 tmem_ld32_nowait(src + static_cast<uint32_t>(c), v);
                 if (half_out) tmem_ld32_nowait(src + static_cast<uint32_t>(c + 32), v + 32);
                 tmem_wait_ld();
-                if (c + CH >= n_mma) {
+                if (c + CH * nhalf >= n_mma) {
                     // last read of this accumulator: hand it back to the MMA warp first
                     tc_fence_before();
                     __syncwarp();
@@ -355,8 +372,12 @@ __global__ void __launch_bounds__(192, 1)
                 }
             }
             if (g.lse_part && row < g.M) {
-                g.lse_part[static_cast<long long>(n0 / BN) * g.M + row] = make_float2(run_m, run_s);
-                if (tg >= n0 && tg < n0 + BN) g.tgt_logit[row] = run_t;
+                // one partial per tile and quadrant warp: [n_tile * 2 + half][row]
+                g.lse_part[static_cast<long long>((n0 / BN) * 2 + half) * g.M + row] = make_float2(run_m, run_s);
+                if (nhalf == 1)  // one warp per quadrant: the second slot holds nothing
+                    g.lse_part[static_cast<long long>((n0 / BN) * 2 + 1) * g.M + row] = make_float2(-INFINITY, 0.f);
+                const int rel = tg - n0;  // the warp whose chunks hold the target column writes it
+                if (rel >= 0 && rel < n_mma && ((rel / CH) % nhalf) == half) g.tgt_logit[row] = run_t;
             }
         }
         if (lane == 0) bulk_wait0();

@@ -168,7 +168,7 @@ template <class A> void plan_workspace(Context& cx, A& a, int T, bool tape) {
     w.hf = a.template take<float>(t * c.d);
     w.h3 = a.template take<__half>(t * cx.d16(3 * c.d));
     w.logits = a.template take<float>(t * c.V);
-    w.lse_part = a.template take<float2>(t * ((c.V + 63) / 64));
+    w.lse_part = a.template take<float2>(t * 2 * ((c.V + 63) / 64));
     w.tgt_logit = a.template take<float>(t);
     w.lp = a.template take<float>(t);
     w.lse_v = a.template take<float>(t);
@@ -472,8 +472,8 @@ inline void forward_chunk(Context& cx, int Bc, int S, bool tape, VocabMode vm, b
         }
         const int bn = gemm(cx, T, c.V, 3 * c.d, {w.h3, ld3, false}, {cx.E3(), cx.E3L(), false}, lo);
         if (with_targets)
-            MM_LAUNCH_TIMED(kKLogsoftmax, 8.0 * T * ((c.V + bn - 1) / bn), lse_combine_kernel, blocks_for(T, 256), 256, 0,
-                            w.lse_part, (c.V + bn - 1) / bn, T, w.tgt_logit, w.lp, w.lse_v, cx.d_err);
+            MM_LAUNCH_TIMED(kKLogsoftmax, 16.0 * T * ((c.V + bn - 1) / bn), lse_combine_kernel, blocks_for(T, 256), 256,
+                            0, w.lse_part, 2 * ((c.V + bn - 1) / bn), T, w.tgt_logit, w.lp, w.lse_v, cx.d_err);
     } else {
         MM_LAUNCH(split3_gather_kernel, blocks_for((long long)Bc * c.d, 256), 256, 0, w.hf, c.d, Bc, S, S - 1, w.h3,
                   (long long)ld3);

@@ -144,7 +144,7 @@ struct Workspace {
     float* hf;          // [T][d] final norm output
     __half* h3;         // [T][ld16(3d)]
     float* logits;      // [T][V]
-    float2* lse_part;   // [ceil(V / 64)][T] per-tile (max, sum exp) of the vocabulary head
+    float2* lse_part;   // [2 * ceil(V / 64)][T] per tile and epilogue half (max, sum exp)
     float* tgt_logit;   // [T]
     float* lp;          // [T]
     float* lse_v;       // [T]
@@ -423,7 +423,7 @@ struct GemmOutSpec {
     float alpha = 1.f;
     const float* alpha_ptr = nullptr;
     // row log-sum-exp partials of an fp32 product (GemmArgs::lse_part); gemm() returns the
-    // tile width, so the partials are [ceil(N / width)][M]
+    // tile width, so the partials are [2 * ceil(N / width)][M]
     float2* lse_part = nullptr;
     const uint16_t* targets = nullptr;
     float* tgt_logit = nullptr;
@@ -500,7 +500,7 @@ inline void launch_gemm_bn(Context& cx, const CUtensorMap& ta, const CUtensorMap
     const int per_sm = std::max(1, std::min(512 / (2 * BN), (227 * 1024) / C::SMEM));
     dim3 grid(static_cast<unsigned>(std::min<long long>(tiles, static_cast<long long>(sm_count()) * per_sm)));
     cudaEvent_t t0 = cx.prof_begin();
-    launch_k(cx.stream, gemm_tc_kernel<BN, STAGES>, grid, dim3(192), C::SMEM, ta, tb, tc, ga);
+    launch_k(cx.stream, gemm_tc_kernel<BN, STAGES>, grid, dim3(C::THREADS), C::SMEM, ta, tb, tc, ga);
     const double flops = 2.0 * ga.M * static_cast<double>(ga.N) * ga.K;
     if (t0) {
         char key[96];

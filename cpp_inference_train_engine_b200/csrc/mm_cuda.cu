@@ -149,7 +149,9 @@ void mm_cuda_destroy(mm_cuda_ctx* h) {
     if (h->cx.stream) cudaStreamSynchronize(h->cx.stream);
     if (h->cx.nccl_comm) {
         try {
-            mm::nccl().commDestroy(static_cast<ncclComm_t>(h->cx.nccl_comm));
+            ncclComm_t comm = static_cast<ncclComm_t>(h->cx.nccl_comm);
+            const ncclResult_t r = mm::nccl().commDestroy(comm);
+            if (r == ncclInProgress && h->cx.nccl_nonblocking) mm::nccl_settle(comm, 30.0, "ncclCommDestroy");
         } catch (...) {
         }
     }
@@ -408,15 +410,43 @@ int mm_cuda_init_comm(mm_cuda_ctx* h, int rank, int world, const char id[128]) {
         if (world == 1) return;
         ncclUniqueId uid;
         std::memcpy(&uid, id, sizeof(uid));
-        ncclComm_t comm;
-        MM_NCCL_CHECK(mm::nccl().commInitRank(&comm, world, uid, rank));
-        cx.nccl_comm = comm;
+        mm::nccl_init(cx, world, uid, rank);
         cx.rank = rank;
         cx.world = world;
     });
 }
 
 int64_t mm_cuda_kernel_launches(const mm_cuda_ctx* h) { return h ? h->cx.launches : -1; }
+
+namespace mm {
+// Waits on an mbarrier nothing arrives at for at most `polls` polls, then records a wait
+// timeout in the error word and returns: the same bounded-wait exit as a stalled GEMM pipeline.
+__global__ void wait_probe_kernel(uint32_t polls, int* err) {
+    MM_PDL_ENTRY();
+    __shared__ uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        bool ok = false;
+        for (uint32_t i = 0; i < polls && !ok; ++i) {
+            ok = mbar_try_wait(&bar, 0);
+            if (i > 64) __nanosleep(32);
+        }
+        if (!ok) raise_error(err, kErrWaitTimeout);
+    }
+}
+}  // namespace mm
+
+int mm_cuda_selftest_wait_timeout(mm_cuda_ctx* h, uint32_t polls) {
+    return guarded(h, [&](mm::Context& cx) {
+        if (polls < 1 || polls > (1u << 22)) mm::fail(MM_INVALID_ARGUMENT, "polls must be in [1, 2^22]");
+        MM_LAUNCH(mm::wait_probe_kernel, 1, 32, 0, polls, cx.d_err);
+        mm::check_device(cx, "wait self-test");
+    });
+}
 
 // ---------------------------------------------------------------- include/mm_cuda_kernels.h
 

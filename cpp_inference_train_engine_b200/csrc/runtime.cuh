@@ -291,6 +291,7 @@ class Context {
 
     // NCCL
     void* nccl_comm = nullptr;
+    bool nccl_nonblocking = false;  // communicator created with blocking = 0
     int rank = 0, world = 1;
 
     // timing

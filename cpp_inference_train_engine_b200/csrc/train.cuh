@@ -4,6 +4,9 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <chrono>
+#include <thread>
+
 #include "decode.cuh"
 
 namespace mm {
@@ -18,6 +21,10 @@ struct Nccl {
     ncclResult_t (*allReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t, cudaStream_t) = nullptr;
     ncclResult_t (*commDestroy)(ncclComm_t) = nullptr;
     const char* (*getErrorString)(ncclResult_t) = nullptr;
+    // non-blocking initialisation with a deadline (present in NCCL >= 2.14)
+    ncclResult_t (*commInitRankConfig)(ncclComm_t*, int, ncclUniqueId, int, ncclConfig_t*) = nullptr;
+    ncclResult_t (*commGetAsyncError)(ncclComm_t, ncclResult_t*) = nullptr;
+    ncclResult_t (*commAbort)(ncclComm_t) = nullptr;
 };
 inline Nccl& nccl() {
     static Nccl n;
@@ -31,6 +38,9 @@ inline Nccl& nccl() {
         n.getErrorString = reinterpret_cast<decltype(n.getErrorString)>(dlsym(n.lib, "ncclGetErrorString"));
         if (!n.getUniqueId || !n.commInitRank || !n.allReduce || !n.commDestroy || !n.getErrorString)
             fail(MM_UNSUPPORTED, "libnccl.so.2 lacks the expected symbols");
+        n.commInitRankConfig = reinterpret_cast<decltype(n.commInitRankConfig)>(dlsym(n.lib, "ncclCommInitRankConfig"));
+        n.commGetAsyncError = reinterpret_cast<decltype(n.commGetAsyncError)>(dlsym(n.lib, "ncclCommGetAsyncError"));
+        n.commAbort = reinterpret_cast<decltype(n.commAbort)>(dlsym(n.lib, "ncclCommAbort"));
     }
     return n;
 }
@@ -40,9 +50,63 @@ inline Nccl& nccl() {
         if (r_ != ncclSuccess) ::mm::fail(MM_GPU_ERROR, std::string(#x) + ": " + ::mm::nccl().getErrorString(r_)); \
     } while (0)
 
+// Seconds a communicator may take to form (MM_NCCL_INIT_TIMEOUT, default 300): a rank
+// that never joins turns into a gpu_error instead of a hang.
+inline double nccl_init_timeout() {
+    const char* e = std::getenv("MM_NCCL_INIT_TIMEOUT");
+    const double v = e ? std::atof(e) : 0.0;
+    return v > 0 ? v : 300.0;
+}
+
+// Waits, up to `seconds`, for a non-blocking communicator's pending operation; false on
+// timeout, fails on an NCCL error.
+inline bool nccl_settle(ncclComm_t comm, double seconds, const char* what) {
+    const auto t0 = std::chrono::steady_clock::now();
+    while (true) {
+        ncclResult_t st = ncclSuccess;
+        MM_NCCL_CHECK(nccl().commGetAsyncError(comm, &st));
+        if (st == ncclSuccess) return true;
+        if (st != ncclInProgress) fail(MM_GPU_ERROR, std::string(what) + ": " + nccl().getErrorString(st));
+        if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > seconds) return false;
+        std::this_thread::sleep_for(std::chrono::milliseconds(1));
+    }
+}
+
+// ncclCommInitRank with a deadline: non-blocking initialisation polled until it completes,
+// aborted (gpu_error) when the other ranks do not join in time. Blocking when the library
+// lacks the non-blocking entry points.
+inline void nccl_init(Context& cx, int world, const ncclUniqueId& uid, int rank) {
+    Nccl& n = nccl();
+    ncclComm_t comm = nullptr;
+    if (!n.commInitRankConfig || !n.commGetAsyncError || !n.commAbort) {
+        MM_NCCL_CHECK(n.commInitRank(&comm, world, uid, rank));
+        cx.nccl_comm = comm;
+        return;
+    }
+    ncclConfig_t config = NCCL_CONFIG_INITIALIZER;
+    config.blocking = 0;
+    const ncclResult_t r = n.commInitRankConfig(&comm, world, uid, rank, &config);
+    if (r != ncclSuccess && r != ncclInProgress)
+        fail(MM_GPU_ERROR, std::string("ncclCommInitRankConfig: ") + n.getErrorString(r));
+    const double limit = nccl_init_timeout();
+    if (!nccl_settle(comm, limit, "ncclCommInitRankConfig")) {
+        n.commAbort(comm);
+        fail(MM_GPU_ERROR, "NCCL communicator did not form within " + std::to_string(static_cast<int>(limit)) +
+                               " s (a rank did not join)");
+    }
+    cx.nccl_comm = comm;
+    cx.nccl_nonblocking = true;
+}
+
 inline void allreduce(Context& cx, void* buf, size_t count, ncclDataType_t t, ncclRedOp_t op) {
     if (cx.world <= 1 || !cx.nccl_comm) return;
-    MM_NCCL_CHECK(nccl().allReduce(buf, buf, count, t, op, static_cast<ncclComm_t>(cx.nccl_comm), cx.stream));
+    ncclComm_t comm = static_cast<ncclComm_t>(cx.nccl_comm);
+    const ncclResult_t r = nccl().allReduce(buf, buf, count, t, op, comm, cx.stream);
+    if (r == ncclInProgress && cx.nccl_nonblocking) {
+        if (!nccl_settle(comm, nccl_init_timeout(), "ncclAllReduce")) fail(MM_GPU_ERROR, "ncclAllReduce was not enqueued");
+        return;
+    }
+    if (r != ncclSuccess) fail(MM_GPU_ERROR, std::string("ncclAllReduce: ") + nccl().getErrorString(r));
 }
 
 // ------------------------------------------------------------------ timing

@@ -122,6 +122,7 @@ def lib():
         "mm_cuda_decode_attention": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int64, _vp, ctypes.c_int,
                                                     ctypes.c_int, ctypes.c_float, _vp]),
         "mm_cuda_profile_gemm_shapes": (ctypes.c_int64, [_vp, ctypes.c_char_p, ctypes.c_int64]),
+        "mm_cuda_selftest_wait_timeout": (ctypes.c_int, [_vp, ctypes.c_uint32]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)
@@ -397,6 +398,11 @@ class CudaExecution:
         """Kernel-level latent decode attention on device pointers (mm_cuda_kernels.h)."""
         self._check(lib().mm_cuda_decode_attention(self.h, q_ptr, cache_ptr, cache_seq_stride,
                                                    pos_ptr, batch, splits, scale, out_ptr))
+
+    def selftest_wait_timeout(self, polls: int = 1 << 12):
+        """Runs the bounded-wait failure path (mm_cuda_selftest_wait_timeout): raises
+        EngineError(gpu_error) and leaves this execution unusable."""
+        self._check(lib().mm_cuda_selftest_wait_timeout(self.h, polls))
 
     def gemm_shapes(self):
         """Per-shape GEMM timing collected while profiling: list of dicts."""

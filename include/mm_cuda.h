@@ -181,7 +181,10 @@ int mm_cuda_grpo_step(mm_cuda_ctx* policy, mm_cuda_ctx* reference, const uint16_
 
 /* ---------------------------------------------------------------- data parallel */
 
-/* NCCL bootstrap: rank 0 creates the id (128 bytes), every rank attaches with it. */
+/* NCCL bootstrap: rank 0 creates the id (128 bytes), every rank attaches with it. The
+ * communicator is formed without blocking and polled: when the other ranks have not joined
+ * within MM_NCCL_INIT_TIMEOUT seconds (default 300) it is aborted and the call returns
+ * MM_GPU_ERROR instead of hanging. */
 int mm_cuda_nccl_unique_id(char out[128]);
 int mm_cuda_init_comm(mm_cuda_ctx* ctx, int rank, int world, const char id[128]);
 

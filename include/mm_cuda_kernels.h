@@ -74,6 +74,15 @@ int64_t mm_cuda_profile_gemm_shapes(mm_cuda_ctx* ctx, char* buf, int64_t cap);
 /* The context's CUDA stream (cudaStream_t), for events recorded by a caller. */
 int mm_cuda_stream(mm_cuda_ctx* ctx, void** stream);
 
+/* Self-test of the bounded-wait failure path (no reference counterpart; the reference's
+ * backends report device failures as gpu_error and mark the execution unusable,
+ * mps_backend.mm:1050-1065). Launches one kernel that waits on an mbarrier no thread
+ * arrives at for at most `polls` polls (1 <= polls <= 2^22), after which it records a wait
+ * timeout in the context's device error word and returns: no trap, no fault. The call
+ * returns MM_GPU_ERROR ("device wait timed out") and the context is unusable afterwards,
+ * exactly as after a GEMM whose pipeline stalled. */
+int mm_cuda_selftest_wait_timeout(mm_cuda_ctx* ctx, uint32_t polls);
+
 #ifdef __cplusplus
 }
 #endif

@@ -109,3 +109,41 @@ def test_two_gloo_ranks_match_one_process():
         assert abs(r["loss"] - loss) <= 1e-9 * max(1.0, abs(loss))
         assert abs(r["kl"] - kl) <= 1e-9 * max(1.0, abs(kl))
         np.testing.assert_allclose(r["grad"], flat, rtol=0, atol=1e-6 * np.abs(flat).max())
+
+
+def _failing_worker(rank, port, out):
+    """Rank 1 leaves right after the group forms; rank 0 then bootstraps NCCL through it."""
+    import datetime
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import torch.distributed as dist
+    dist.init_process_group("gloo", rank=rank, world_size=WORLD, timeout=datetime.timedelta(seconds=10))
+    if rank == 1:
+        os._exit(0)  # a rank that dies between steps, with no collective in flight
+    import time
+    t0 = time.time()
+    try:
+        D.broadcast_unique_id(rank, lambda: bytes(128))
+        out[rank] = ("completed", time.time() - t0)
+    except Exception as e:  # the peer is gone: the bootstrap must fail, not hang
+        out[rank] = ("error " + type(e).__name__, time.time() - t0)
+
+
+def test_rank_failure_is_reported_not_hung():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as m:
+        out = m.dict()
+        port = _free_port()
+        procs = [ctx.Process(target=_failing_worker, args=(r, port, out)) for r in range(WORLD)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(120)
+        alive = [p.is_alive() for p in procs]
+        for p in procs:
+            if p.is_alive():
+                p.kill()
+        assert not any(alive), "a rank hung after its peer left"
+        status, seconds = out[0]
+    assert status.startswith("error"), status
+    assert seconds < 60

@@ -221,7 +221,8 @@ def main():
 
     def one_step(step_idx):
         # The rollout seeds advance per update like the trainer's Rng(seed) stream.
-        s = (seeds + np.uint64(step_idx) * np.uint64(0x9E3779B97F4A7C15)).astype(np.uint64)
+        with np.errstate(over="ignore"):  # arithmetic mod 2^64 is intended
+            s = (seeds + np.uint64(step_idx) * np.uint64(0x9E3779B97F4A7C15)).astype(np.uint64)
         r = pol.rollout(prompts, args.new_tokens, seq, s, 1.0)
         out = pol.grpo_step(refm, r["input"], r["target"], r["mask"], r["old_lp"], rewards,
                             args.group, n_total=n_total, clip=0.2, klc=0.04, learning_rate=1e-5)

@@ -1,0 +1,278 @@
+// Causal attention forward on the 5th-generation tensor cores for 64-wide heads (the
+// 35.8M model: qk = 48 nope + 16 rope, dv = 64), the teacher-forced passes of
+// ops::attention (ops.cpp:109-140). Output and per-row base-2 log-sum-exp are those of
+// flash_fwd_mma_kernel, so either backward consumes them.
+//
+// One CTA per (head, sequence, 128-query tile), 10 warps:
+//   warp 8   TMA: Q once, then K tiles into a 2-deep ring and V tiles into one buffer;
+//   warp 9   one thread issues tcgen05.mma: S = Q K^T (128 x 128, fp32 in TMEM columns
+//            [0, 128)), then O_j = P_j V_j (128 x 64, TMEM columns [128, 192));
+//   warps 0-7 softmax, two warps per TMEM lane quadrant (lane = query row): warp w reads
+//            key columns [64 (w / 4), +64) of its rows. Pass 1 takes the row maximum (the
+//            two halves exchange theirs through shared memory), pass 2 writes
+//            P = exp2(S - max) as fp16 into its 64-key half of a 128-byte-swizzled shared
+//            tile (the A operand of P V), then the warp folds value columns
+//            [32 (w / 4), +32) of O_j into registers with the online-softmax correction.
+// Only the diagonal key tile is masked (keys after the query or past the sequence end).
+// Every mbarrier wait is bounded; a timeout sets the device error word and the CTA unwinds
+// and frees its tensor memory. 96 KB of shared memory and 256 TMEM columns: two CTAs per SM.
+#pragma once
+#include "common.cuh"
+
+namespace mm {
+
+namespace fatc {
+constexpr int kRows = 128;                 // queries per CTA and keys per tile
+constexpr int kD = 64;                     // qk and value width
+constexpr int kTileBytes = kRows * kD * 2; // one 128 x 64 fp16 tile, 128-byte rows
+constexpr int kSoftmaxWarps = 8;
+constexpr int kThreads = 32 * (kSoftmaxWarps + 2);
+// Q, K[2], V, P (two 64-key halves), then barriers and the row exchange of the two softmax
+// halves: maxima [parity][half][row] and sums [half][row]
+constexpr int kSmem = 6 * kTileBytes + 1024 + 256 + 6 * kRows * 4;
+constexpr uint32_t kTmemCols = 256;
+constexpr int kColS = 0, kColO = 128;
+}  // namespace fatc
+
+// q, k, v, out: fp16 [T][H * 64] (row pitch H * 64), T = sequences * S, viewed through the
+// tensor maps tmQ/tmK/tmV (box {64, 128}, 128-byte swizzle); lse2 fp32 [T][H].
+// grid (H, sequences, ceil(S / 128)); the longest query tiles are scheduled first.
+__global__ void __launch_bounds__(fatc::kThreads, 2)
+    flash_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                        const __grid_constant__ CUtensorMap tmV, int S, int H, float scale,
+                        __half* __restrict__ out, float* __restrict__ lse2, int* err) {
+    using namespace fatc;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~static_cast<uintptr_t>(1023));
+    uint8_t* sQ = smem;
+    uint8_t* sK = smem + kTileBytes;      // [2]
+    uint8_t* sV = smem + 3 * kTileBytes;
+    uint8_t* sP = smem + 4 * kTileBytes;  // keys [0, 64) then [64, 128)
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 6 * kTileBytes);
+    uint64_t* q_full = bars + 0;
+    uint64_t* k_full = bars + 1;   // [2]
+    uint64_t* k_empty = bars + 3;  // [2]
+    uint64_t* v_full = bars + 5;
+    uint64_t* v_empty = bars + 6;
+    uint64_t* s_full = bars + 7;
+    uint64_t* s_empty = bars + 8;  // softmax warps
+    uint64_t* p_full = bars + 9;   // softmax warps
+    uint64_t* p_empty = bars + 10;
+    uint64_t* o_full = bars + 11;
+    uint64_t* o_empty = bars + 12; // softmax warps
+    uint64_t* xbar = bars + 13;    // [4] the two softmax warps of a lane quadrant
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
+    float* xchg = reinterpret_cast<float*>(smem + 6 * kTileBytes + 256);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int h = blockIdx.x, b = blockIdx.y;
+    const int qt = gridDim.z - 1 - blockIdx.z;
+    const int nk = qt + 1;  // key tiles at or below the diagonal
+    const int row_base = b * S;
+
+    if (warp == 8) {
+        if (lane == 0) {
+            mbar_init(q_full, 1);
+            mbar_init(&k_full[0], 1);
+            mbar_init(&k_full[1], 1);
+            mbar_init(&k_empty[0], 1);
+            mbar_init(&k_empty[1], 1);
+            mbar_init(v_full, 1);
+            mbar_init(v_empty, 1);
+            mbar_init(s_full, 1);
+            mbar_init(s_empty, kSoftmaxWarps);
+            mbar_init(p_full, kSoftmaxWarps);
+            mbar_init(p_empty, 1);
+            mbar_init(o_full, 1);
+            mbar_init(o_empty, kSoftmaxWarps);
+            for (int i = 0; i < 4; ++i) mbar_init(&xbar[i], 2);
+            fence_mbar_init();
+            prefetch_tmap(&tmQ);
+            prefetch_tmap(&tmK);
+            prefetch_tmap(&tmV);
+        }
+        __syncwarp();
+        tmem_alloc(tmem_slot, kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    MM_PDL_ENTRY();
+
+    if (warp == 8) {
+        if (lane == 0) {
+            bool ok = true;
+            mbar_arrive_expect_tx(q_full, kTileBytes);
+            tma_load_2d(sQ, &tmQ, q_full, h * kD, row_base + qt * kRows);
+            for (int j = 0; j < nk && ok; ++j) {
+                const int s = j & 1, u = j >> 1;
+                if (!mbar_wait_bounded(&k_empty[s], (u & 1) ^ 1, err)) { ok = false; break; }
+                mbar_arrive_expect_tx(&k_full[s], kTileBytes);
+                tma_load_2d(sK + s * kTileBytes, &tmK, &k_full[s], h * kD, row_base + j * kRows);
+                if (!mbar_wait_bounded(v_empty, (j & 1) ^ 1, err)) { ok = false; break; }
+                mbar_arrive_expect_tx(v_full, kTileBytes);
+                tma_load_2d(sV, &tmV, v_full, h * kD, row_base + j * kRows);
+            }
+        }
+    } else if (warp == 9) {
+        if (lane == 0) {
+            const uint32_t id_s = umma_idesc_f16(false, false, false, kRows, kRows);  // Q K^T, both K-major
+            const uint32_t id_o = umma_idesc_f16(false, false, true, kRows, kD);      // P V, V MN-major
+            const uint32_t aq = smem_u32(sQ), ap = smem_u32(sP), bv = smem_u32(sV);
+            bool ok = mbar_wait_bounded(q_full, 0, err);
+            for (int j = 0; j < nk && ok; ++j) {
+                const int s = j & 1, u = j >> 1;
+                if (!mbar_wait_bounded(&k_full[s], u & 1, err)) { ok = false; break; }
+                if (!mbar_wait_bounded(s_empty, (j & 1) ^ 1, err)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t bk = smem_u32(sK + s * kTileBytes);
+#pragma unroll
+                for (int k = 0; k < kD / 16; ++k)
+                    tc_mma_f16(tmem + kColS, umma_desc_sw128(aq + k * 32, 16, 1024),
+                               umma_desc_sw128(bk + k * 32, 16, 1024), id_s, k ? 1u : 0u);
+                tc_commit(s_full);
+                tc_commit(&k_empty[s]);
+                if (!mbar_wait_bounded(p_full, j & 1, err)) { ok = false; break; }
+                if (!mbar_wait_bounded(v_full, j & 1, err)) { ok = false; break; }
+                if (!mbar_wait_bounded(o_empty, (j & 1) ^ 1, err)) { ok = false; break; }
+                tc_fence_after();
+#pragma unroll
+                for (int k = 0; k < kRows / 16; ++k)
+                    tc_mma_f16(tmem + kColO, umma_desc_sw128(ap + (k >> 2) * kTileBytes + (k & 3) * 32, 16, 1024),
+                               umma_desc_sw128(bv + k * 2048, 8192, 1024), id_o, k ? 1u : 0u);
+                tc_commit(o_full);
+                tc_commit(v_empty);
+                tc_commit(p_empty);
+            }
+        }
+    } else {
+        // softmax: thread = query row r of the tile (TMEM lane r), key/value half hh
+        const int q = warp & 3, hh = warp >> 2;
+        const int r = q * 32 + lane;
+        const int qpos = qt * kRows + r;
+        const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
+        const float cs = scale * 1.4426950408889634f;
+        uint8_t* prow = sP + hh * kTileBytes + r * 128;
+        float acc[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) acc[i] = 0.f;
+        float m_run = -INFINITY, l_run = 0.f;
+        bool ok = true;
+        for (int j = 0; j < nk && ok; ++j) {
+            if (!mbar_wait_bounded(s_full, j & 1, err)) { ok = false; break; }
+            tc_fence_after();
+            const bool diag = j == qt;
+            // diagonal tile: columns after the query or past the sequence end are masked
+            const int lim = diag ? min(qpos, S - 1) - j * kRows - hh * 64 : 63;
+            float mx = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+                float v[32];
+                tmem_ld32_nowait(lane_base + kColS + hh * 64 + c * 32, v);
+                tmem_wait_ld();
+                if (diag) {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i)
+                        if (c * 32 + i <= lim) mx = fmaxf(mx, v[i]);
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) mx = fmaxf(mx, v[i]);
+                }
+            }
+            float* xm = xchg + (j & 1) * 2 * kRows;
+            xm[hh * kRows + r] = mx;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&xbar[q]);
+            if (!mbar_wait_bounded(&xbar[q], j & 1, err)) { ok = false; break; }
+            mx = fmaxf(mx, xm[(hh ^ 1) * kRows + r]) * cs;  // cs > 0: max commutes with the scale
+            const float m_new = fmaxf(m_run, mx);
+            const float base = m_new == -INFINITY ? 0.f : m_new;
+            const float corr = fast_exp2(m_run - base);
+            if (!mbar_wait_bounded(p_empty, (j & 1) ^ 1, err)) { ok = false; break; }
+            float ls = 0.f;
+#pragma unroll 1
+            for (int c = 0; c < 2; ++c) {
+                float v[32];
+                tmem_ld32_nowait(lane_base + kColS + hh * 64 + c * 32, v);
+                tmem_wait_ld();
+                uint32_t w[16];
+#pragma unroll
+                for (int i = 0; i < 32; i += 2) {
+                    float p0 = fast_exp2(fmaf(v[i], cs, -base));
+                    float p1 = fast_exp2(fmaf(v[i + 1], cs, -base));
+                    if (diag) {
+                        if (c * 32 + i > lim) p0 = 0.f;
+                        if (c * 32 + i + 1 > lim) p1 = 0.f;
+                    }
+                    ls += p0 + p1;
+                    const __half2 hp = __floats2half2_rn(p0, p1);
+                    w[i >> 1] = *reinterpret_cast<const uint32_t*>(&hp);
+                }
+                // keys [32c, 32c + 32) of this half: four 16-byte chunks, 128-byte swizzle
+#pragma unroll
+                for (int q4 = 0; q4 < 4; ++q4) {
+                    const int cc = c * 4 + q4;
+                    *reinterpret_cast<uint4*>(prow + ((cc ^ (r & 7)) << 4)) =
+                        make_uint4(w[4 * q4], w[4 * q4 + 1], w[4 * q4 + 2], w[4 * q4 + 3]);
+                }
+            }
+            tc_fence_before();
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(s_empty);
+                mbar_arrive(p_full);
+            }
+            if (!mbar_wait_bounded(o_full, j & 1, err)) { ok = false; break; }
+            tc_fence_after();
+            {
+                float o[32];
+                tmem_ld32_nowait(lane_base + kColO + hh * 32, o);
+                tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 32; ++i) acc[i] = acc[i] * corr + o[i];
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(o_empty);
+            l_run = l_run * corr + ls;
+            m_run = m_new;
+        }
+        // the row sum is the two halves' sums (same maxima, same corrections)
+        float* xl = xchg + 2 * 2 * kRows;
+        if (ok) {
+            xl[hh * kRows + r] = l_run;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&xbar[q]);
+            ok = mbar_wait_bounded(&xbar[q], nk & 1, err);
+        }
+        if (ok && qpos < S) {
+            const float l = l_run + xl[(hh ^ 1) * kRows + r];
+            const float inv = 1.f / l;
+            __half* dst = out + (static_cast<long long>(row_base) + qpos) * (static_cast<long long>(H) * kD) + h * kD +
+                          hh * 32;
+#pragma unroll
+            for (int i = 0; i < 32; i += 8) {
+                const __half2 h0 = __floats2half2_rn(acc[i] * inv, acc[i + 1] * inv);
+                const __half2 h1 = __floats2half2_rn(acc[i + 2] * inv, acc[i + 3] * inv);
+                const __half2 h2 = __floats2half2_rn(acc[i + 4] * inv, acc[i + 5] * inv);
+                const __half2 h3 = __floats2half2_rn(acc[i + 6] * inv, acc[i + 7] * inv);
+                *reinterpret_cast<uint4*>(dst + i) =
+                    make_uint4(*reinterpret_cast<const uint32_t*>(&h0), *reinterpret_cast<const uint32_t*>(&h1),
+                               *reinterpret_cast<const uint32_t*>(&h2), *reinterpret_cast<const uint32_t*>(&h3));
+            }
+            if (hh == 0) lse2[(static_cast<long long>(row_base) + qpos) * H + h] = m_run + log2f(l);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 8) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+}  // namespace mm

@@ -481,6 +481,59 @@ int mm_cuda_gemm_f16(mm_cuda_ctx* h, int M, int N, int K, const void* a, int64_t
     });
 }
 
+int mm_cuda_bench_gemm(mm_cuda_ctx* h, int reps, int M, int N, int K, const void* a, int64_t lda, int a_mn,
+                       const void* b, int64_t ldb, int b_mn, void* out, int64_t ldc, int out_kind,
+                       float* ms_per_launch) {
+    return guarded(h, [&](mm::Context& cx) {
+        if (reps < 1 || reps > 4096 || M < 1 || N < 1 || K < 1 || !a || !b || !out || out_kind < 0 ||
+            out_kind > 3 || !ms_per_launch)
+            mm::fail(MM_INVALID_ARGUMENT, "invalid GEMM arguments");
+        mm::GemmOutSpec o{out, ldc, out_kind};
+        const mm::Opnd A{a, lda, a_mn != 0}, B{b, ldb, b_mn != 0};
+        // one eager launch sets kernel attributes and sizes the split-K staging
+        mm::gemm(cx, M, N, K, A, B, o);
+        mm::check_device(cx, "gemm");
+        const bool prof = cx.profiling;
+        const long long before = cx.launches;
+        cx.profiling = false;
+        cudaGraph_t g = nullptr;
+        cudaGraphExec_t ge = nullptr;
+        cudaEvent_t e0 = nullptr, e1 = nullptr;
+        MM_CUDA_CHECK(cudaStreamBeginCapture(cx.stream, cudaStreamCaptureModeThreadLocal));
+        try {
+            for (int r = 0; r < reps; ++r) mm::gemm(cx, M, N, K, A, B, o);
+        } catch (...) {
+            cudaStreamEndCapture(cx.stream, &g);
+            if (g) cudaGraphDestroy(g);
+            cx.profiling = prof;
+            throw;
+        }
+        const cudaError_t ce = cudaStreamEndCapture(cx.stream, &g);
+        cx.profiling = prof;
+        const long long per_replay = cx.launches - before;
+        if (ce != cudaSuccess || !g) mm::fail(MM_GPU_ERROR, std::string("GEMM graph capture: ") + cudaGetErrorString(ce));
+        const cudaError_t ie = cudaGraphInstantiate(&ge, g, 0);
+        cudaGraphDestroy(g);
+        if (ie != cudaSuccess) mm::fail(MM_GPU_ERROR, std::string("GEMM graph instantiate: ") + cudaGetErrorString(ie));
+        float ms = 0.f;
+        cudaError_t e = cudaGraphLaunch(ge, cx.stream);  // warm replay
+        if (e == cudaSuccess) e = cudaEventCreate(&e0);
+        if (e == cudaSuccess) e = cudaEventCreate(&e1);
+        if (e == cudaSuccess) e = cudaEventRecord(e0, cx.stream);
+        if (e == cudaSuccess) e = cudaGraphLaunch(ge, cx.stream);
+        if (e == cudaSuccess) e = cudaEventRecord(e1, cx.stream);
+        if (e == cudaSuccess) e = cudaEventSynchronize(e1);
+        if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, e0, e1);
+        if (e0) cudaEventDestroy(e0);
+        if (e1) cudaEventDestroy(e1);
+        cudaGraphExecDestroy(ge);
+        if (e != cudaSuccess) mm::fail(MM_GPU_ERROR, std::string("GEMM graph replay: ") + cudaGetErrorString(e));
+        cx.launches = before + 2 * per_replay;
+        mm::check_device(cx, "gemm");
+        *ms_per_launch = ms / static_cast<float>(reps);
+    });
+}
+
 int mm_cuda_decode_attention(mm_cuda_ctx* h, const float* q, const void* cache, int64_t cache_seq_stride,
                              const int32_t* pos, int batch, int splits, float scale, void* out) {
     return guarded(h, [&](mm::Context& cx) {

@@ -49,6 +49,13 @@ inline int gemm(Context& cx, int M, int N, int K, Opnd A, Opnd B, const GemmOutS
     if (o.glu_n) BN = 256;  // 128 gate + 128 up columns per tile
     else if (N >= 256 && (split_candidate || tiles_m * ((N + 255) / 256) >= 148)) BN = 256;
     else if (tiles_m * ((N + 127) / 128) >= 120 && N > 64) BN = 128;
+    // MM_GEMM_BN (64, 128 or 256) pins the tile width of every plain product, for tuning.
+    static const int forced_bn = [] {
+        const char* e = std::getenv("MM_GEMM_BN");
+        const int v = e ? std::atoi(e) : 0;
+        return v == 64 || v == 128 || v == 256 ? v : 0;
+    }();
+    if (forced_bn && !o.glu_n) BN = forced_bn;
     const int nb = o.glu_n ? o.glu_n + N : N;  // columns of B
     const CUtensorMap& ta = A.mn ? tensor_map(A.p, bf16, M, K, A.ld, 64, 64)
                                  : tensor_map(A.p, bf16, K, M, A.ld, 64, kGemmBM);

@@ -218,35 +218,36 @@ __device__ __forceinline__ uint32_t float_key(float f) {
     return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
-constexpr int kSampleThreads = 512;
-constexpr int kSampleBuckets = 2048;
-constexpr int kSampleCap = 1024;
-constexpr int kSampleCache = 32;  // scores per thread held in registers (rows up to 16384)
+// One block of kSampleThreads per row. Shared memory per row: an equal-width bucket
+// histogram (later reused for the candidates) and per-bucket exponential bases.
+constexpr int kSampleThreads = 256;
+constexpr int kSampleBuckets = 512;
+constexpr int kSampleRadixBits = 9;  // key bits fixed per fallback round (512 buckets)
+constexpr int kSampleCap = 384;      // candidates ranked exactly in shared memory
+constexpr int kSampleBatch = 2;      // row loads in flight per thread (more unrolling overflows the i-cache)
 
-// Block-wide inclusive prefix sum of one u64 per thread (blockDim.x = kSampleThreads).
-__device__ __forceinline__ unsigned long long block_scan_incl(unsigned long long v, unsigned long long* warp_tot) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        const unsigned long long n = __shfl_up_sync(0xffffffffu, v, o);
-        if (lane >= o) v += n;
-    }
-    if (lane == 31) warp_tot[warp] = v;
-    __syncthreads();
-    if (warp == 0) {
-        unsigned long long t = lane < (kSampleThreads >> 5) ? warp_tot[lane] : 0ull;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const unsigned long long n = __shfl_up_sync(0xffffffffu, t, o);
-            if (lane >= o) t += n;
-        }
-        if (lane < (kSampleThreads >> 5)) warp_tot[lane] = t;
-    }
-    __syncthreads();
-    const unsigned long long before = warp > 0 ? warp_tot[warp - 1] : 0ull;
-    __syncthreads();  // warp_tot is reused by the next scan
-    return v + before;
-}
+struct SampleShared {
+    union {
+        // bucket mass in 2^-48 fixed point as three 16-bit limbs summed with 32-bit shared
+        // atomics (no sum overflows: weights <= 2^48, at most 65535 of them)
+        struct {
+            unsigned lo[kSampleBuckets], mid[kSampleBuckets], hi[kSampleBuckets];
+            unsigned count[kSampleBuckets];
+        } h;
+        struct {
+            unsigned long long w[kSampleCap];
+            uint32_t key[kSampleCap];
+            int id[kSampleCap];
+        } c;
+    };
+    double xb[kSampleBuckets];     // centre x_b of bucket b in units of s - s0
+    double ebase[kSampleBuckets];  // exp(x_b) * 2^48
+    float red_f[kSampleThreads / 32], red_g[kSampleThreads / 32];
+    int red_i[kSampleThreads / 32];
+    uint32_t red_k[kSampleThreads / 32];
+    unsigned long long draw;
+    int chosen, ncand;
+};
 
 // Sampling weight in 2^-48 fixed point: w = exp(double(s - s0) / T) <= 1 (s0 is the row
 // maximum; the float difference and the double division are those of sample_token,
@@ -266,166 +267,174 @@ __device__ __forceinline__ unsigned long long sample_draw(uint64_t seed, int k, 
     return (hi << 39) | (lo >> 25);
 }
 
-// Adds q to hist[bucket] and 1 to hcount[bucket], one atomic per distinct bucket of the
-// warp (scores crowd into few key buckets, so per-lane atomics would serialise).
-__device__ __forceinline__ void warp_bucket_add(unsigned long long* hist, int* hcount, int bucket,
-                                                unsigned long long q, bool valid) {
-    const unsigned active = __ballot_sync(0xffffffffu, valid);
-    if (!valid) return;
-    const unsigned peers = __match_any_sync(active, bucket);
-    unsigned long long sum = 0;
-    for (unsigned m = peers; m; m &= m - 1) sum += __shfl_sync(peers, q, __ffs(m) - 1);
-    if ((threadIdx.x & 31) == __ffs(peers) - 1) {
-        atomicAdd(&hist[bucket], sum);
-        atomicAdd(&hcount[bucket], __popc(peers));
-    }
+__device__ __forceinline__ void sample_hist_add(SampleShared& S, int bk, unsigned long long w) {
+    atomicAdd(&S.h.lo[bk], static_cast<unsigned>(w & 0xffffu));
+    atomicAdd(&S.h.mid[bk], static_cast<unsigned>((w >> 16) & 0xffffu));
+    atomicAdd(&S.h.hi[bk], static_cast<unsigned>(w >> 32));
+    atomicAdd(&S.h.count[bk], 1u);
+}
+__device__ __forceinline__ unsigned long long sample_hist_mass(const SampleShared& S, int bk) {
+    return (static_cast<unsigned long long>(S.h.hi[bk]) << 32) + (static_cast<unsigned long long>(S.h.mid[bk]) << 16) +
+           S.h.lo[bk];
+}
+__device__ __forceinline__ void sample_hist_clear(SampleShared& S) {
+    for (int i = threadIdx.x; i < kSampleBuckets; i += kSampleThreads)
+        S.h.lo[i] = S.h.mid[i] = S.h.hi[i] = S.h.count[i] = 0u;
 }
 
-struct SampleShared {
-    unsigned long long hist[kSampleBuckets];
-    int hcount[kSampleBuckets];
-    uint32_t cand_key[kSampleCap];
-    int cand_id[kSampleCap];
-    unsigned long long cand_w[kSampleCap];
-    float red_f[32], red_g[32];
-    int red_i[32];
-    unsigned long long warp_tot[32];
-    unsigned long long s_draw;
-    uint32_t s_prefix;
-    int s_bits, s_ncand, s_chosen, s_last;
+// Weights of one row. At temperature 1 with equal-width buckets at most 0.1 wide (score
+// range <= 51.2), w = exp(x_b) * exp(x - x_b) with exp(x_b) from a per-bucket table and
+// exp(d), |d| <= 0.0501, from its Taylor series to degree 8 (truncation below 6e-18
+// relative): a weight agrees with the directly computed double exponential to within a
+// few units of the last place before the rounding to 2^-48. Otherwise sample_weight_q.
+struct SampleRowWeight {
+    float s0, scale;
+    double T;
+    bool poly;
+    const double* xb;
+    const double* ebase;
+    __device__ __forceinline__ int bucket(float v) const {
+        const float p = fminf(__fmul_rn(__fsub_rn(s0, v), scale), static_cast<float>(kSampleBuckets - 1));
+        return kSampleBuckets - 1 - static_cast<int>(p);
+    }
+    __device__ __forceinline__ unsigned long long operator()(float v, int b) const {
+        if (!poly) return sample_weight_q(v, s0, T);
+        const double d = static_cast<double>(__fsub_rn(v, s0)) - xb[b];
+        double p = 1.0 / 40320.0;
+        p = fma(p, d, 1.0 / 5040.0);
+        p = fma(p, d, 1.0 / 720.0);
+        p = fma(p, d, 1.0 / 120.0);
+        p = fma(p, d, 1.0 / 24.0);
+        p = fma(p, d, 1.0 / 6.0);
+        p = fma(p, d, 0.5);
+        p = fma(p, d, 1.0);
+        p = fma(p, d, 1.0);
+        return __double2ull_rn(ebase[b] * p);
+    }
 };
 
-// Scan of the bucket masses from the highest bucket (highest scores) down. With `first`,
-// the draw is derived from the row total. Leaves in S.s_chosen the bucket where the running
-// mass first reaches the draw and in S.s_draw the part of the draw left inside it.
-__device__ void sample_locate(SampleShared& S, int nb, bool first, uint64_t seed, int k) {
-    constexpr int PER = kSampleBuckets / kSampleThreads;  // buckets per thread
-    // thread t owns descending positions [t*PER, t*PER + PER); position p <-> bucket nb-1-p
+// Warp 0 scans the histogram in descending bucket order (lane L owns positions
+// [16L, 16L + 16), position p <-> bucket nb - 1 - p). With `first` the draw comes from the
+// row total, otherwise S.draw is the part left inside the previously fixed prefix. Leaves in
+// S.chosen the bucket where the running mass first reaches the draw and in S.draw the part
+// of it inside that bucket; when every weight rounded to zero below the draw, the lowest
+// non-empty bucket with S.draw = ~0. Called by warp 0 only.
+__device__ __forceinline__ void sample_locate(SampleShared& S, int nb, bool first, uint64_t seed, int k) {
+    constexpr int PER = kSampleBuckets / 32;
+    const int lane = threadIdx.x & 31;
     unsigned long long mine = 0;
 #pragma unroll
     for (int e = 0; e < PER; ++e) {
-        const int bk = nb - 1 - (static_cast<int>(threadIdx.x) * PER + e);
-        if (bk >= 0) mine += S.hist[bk];
+        const int bk = nb - 1 - (lane * PER + e);
+        if (bk >= 0) mine += sample_hist_mass(S, bk);
     }
-    const unsigned long long incl = block_scan_incl(mine, S.warp_tot);
-    if (first) {
-        if (threadIdx.x == kSampleThreads - 1) S.s_draw = sample_draw(seed, k, incl);
-        __syncthreads();
+    unsigned long long incl = mine;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const unsigned long long n = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += n;
     }
-    if (threadIdx.x == 0) { S.s_chosen = -1; S.s_last = 0x7fffffff; }
-    __syncthreads();
-    const unsigned long long draw = S.s_draw;
-    unsigned long long run = incl - mine;  // mass of all higher buckets
-    int last_here = 0x7fffffff;
-    __syncthreads();  // every thread has read the draw before it is rewritten
+    const unsigned long long draw = first ? sample_draw(seed, k, __shfl_sync(0xffffffffu, incl, 31)) : S.draw;
+    unsigned long long run = incl - mine, rem = 0;
+    int found = -1, last_here = 0x7fffffff;
 #pragma unroll
     for (int e = 0; e < PER; ++e) {
-        const int bk = nb - 1 - (static_cast<int>(threadIdx.x) * PER + e);
-        if (bk < 0 || S.hcount[bk] == 0) continue;
+        const int bk = nb - 1 - (lane * PER + e);
+        if (bk < 0 || S.h.count[bk] == 0) continue;
         last_here = bk;
-        if (run < draw && run + S.hist[bk] >= draw) {
-            S.s_chosen = bk;
-            S.s_draw = draw - run;
+        const unsigned long long m = sample_hist_mass(S, bk);
+        if (found < 0 && run < draw && run + m >= draw) {
+            found = bk;
+            rem = draw - run;
         }
-        run += S.hist[bk];
+        run += m;
     }
-    if (last_here != 0x7fffffff) atomicMin(&S.s_last, last_here);
-    __syncthreads();
-    if (threadIdx.x == 0 && S.s_chosen < 0) {
-        S.s_chosen = S.s_last;  // only when every weight rounded to zero below the draw
-        S.s_draw = ~0ull;
+    const unsigned hit = __ballot_sync(0xffffffffu, found >= 0);
+    if (hit) {
+        if (lane == __ffs(hit) - 1) {
+            S.chosen = found;
+            S.draw = rem;
+        }
+        return;
     }
-    __syncthreads();
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) last_here = min(last_here, __shfl_xor_sync(0xffffffffu, last_here, o));
+    if (lane == 0) {
+        S.chosen = last_here;
+        S.draw = ~0ull;
+    }
 }
 
-// Gathers the scores selected by `in_set` (at most kSampleCap of them), sorts them (score
-// descending, id ascending) and returns the id where their running mass reaches S.s_draw
-// (the last one when none does; `none` when the set is empty).
-// `each(f)` calls f(id, score) for this thread's share of the row.
+// Among the scores selected by `in_set` (at most kSampleCap, gathered into shared memory)
+// ordered by score descending then id ascending, the id where the running mass first
+// reaches S.draw (the last one when none does; `none` when the set is empty). Ranks by
+// counting: the mass before candidate i is the sum over the candidates ordered before it.
+// Called by the whole block.
 template <class Each, class Pred>
-__device__ int sample_pick(SampleShared& S, Each each, float s0, double T, Pred in_set, int none) {
-    if (threadIdx.x == 0) S.s_ncand = 0;
+__device__ int sample_pick(SampleShared& S, Each each, const SampleRowWeight& wt, Pred in_set, int none) {
+    const unsigned long long rem = S.draw;
+    __syncthreads();  // every thread has read the draw and the chosen bucket
+    if (threadIdx.x == 0) { S.ncand = 0; S.chosen = -1; }
     __syncthreads();
     each([&](int j, float v) {
         if (in_set(v)) {
-            const int slot = atomicAdd(&S.s_ncand, 1);
+            const int slot = atomicAdd(&S.ncand, 1);
             if (slot < kSampleCap) {
-                S.cand_key[slot] = float_key(v);
-                S.cand_id[slot] = j;
-                S.cand_w[slot] = sample_weight_q(v, s0, T);
+                S.c.key[slot] = float_key(v);
+                S.c.id[slot] = j;
+                S.c.w[slot] = wt(v, wt.poly ? wt.bucket(v) : 0);
             }
         }
     });
     __syncthreads();
-    const int n = min(S.s_ncand, kSampleCap);
-    int np2 = 1;
-    while (np2 < n) np2 <<= 1;
-    // bitonic sort of the candidates (padded to a power of two): key descending, id ascending
-    for (int i = n + threadIdx.x; i < np2; i += blockDim.x) {
-        S.cand_key[i] = 0;
-        S.cand_id[i] = 0x7fffffff;
-        S.cand_w[i] = 0ull;
-    }
-    __syncthreads();
-    for (int size = 2; size <= np2; size <<= 1) {
-        for (int stride = size >> 1; stride > 0; stride >>= 1) {
-            for (int i = threadIdx.x; i < np2; i += blockDim.x) {
-                const int jx = i ^ stride;
-                if (jx > i) {
-                    const bool desc = (i & size) == 0;
-                    const bool i_before = S.cand_key[i] > S.cand_key[jx] ||
-                                          (S.cand_key[i] == S.cand_key[jx] && S.cand_id[i] < S.cand_id[jx]);
-                    if (desc != i_before) {
-                        const uint32_t tk = S.cand_key[i]; S.cand_key[i] = S.cand_key[jx]; S.cand_key[jx] = tk;
-                        const int ti = S.cand_id[i]; S.cand_id[i] = S.cand_id[jx]; S.cand_id[jx] = ti;
-                        const unsigned long long tw = S.cand_w[i]; S.cand_w[i] = S.cand_w[jx]; S.cand_w[jx] = tw;
-                    }
-                }
-            }
-            __syncthreads();
+    const int n = min(S.ncand, kSampleCap);
+    if (n == 0) return none;
+    uint32_t last_key = 0xffffffffu;
+    int last_id = -1;
+    for (int i = threadIdx.x; i < n; i += kSampleThreads) {
+        const uint32_t ki = S.c.key[i];
+        const int ii = S.c.id[i];
+        unsigned long long before = 0;
+        for (int j = 0; j < n; ++j) {
+            const uint32_t kj = S.c.key[j];
+            if (kj > ki || (kj == ki && S.c.id[j] < ii)) before += S.c.w[j];
         }
+        if (before < rem && before + S.c.w[i] >= rem) S.chosen = ii;
+        if (ki < last_key || (ki == last_key && ii > last_id)) { last_key = ki; last_id = ii; }
     }
-    // first sorted candidate whose running sum reaches the remaining draw
-    const unsigned long long rem = S.s_draw;
-    constexpr int CPT = kSampleCap / kSampleThreads;  // candidates per thread
-    unsigned long long mine = 0;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll
-    for (int e = 0; e < CPT; ++e) {
-        const int i = threadIdx.x * CPT + e;
-        if (i < n) mine += S.cand_w[i];
+    for (int o = 16; o > 0; o >>= 1) {
+        const uint32_t ok = __shfl_xor_sync(0xffffffffu, last_key, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, last_id, o);
+        if (ok < last_key || (ok == last_key && oi > last_id)) { last_key = ok; last_id = oi; }
     }
-    const unsigned long long incl = block_scan_incl(mine, S.warp_tot);
-    if (threadIdx.x == 0) S.s_chosen = 0x7fffffff;
+    if (lane == 0) { S.red_k[warp] = last_key; S.red_i[warp] = last_id; }
     __syncthreads();
-    unsigned long long run = incl - mine;
-#pragma unroll
-    for (int e = 0; e < CPT; ++e) {
-        const int i = threadIdx.x * CPT + e;
-        if (i < n) {
-            run += S.cand_w[i];
-            if (run >= rem) { atomicMin(&S.s_chosen, i); break; }
-        }
-    }
-    __syncthreads();
-    const int i = S.s_chosen == 0x7fffffff ? n - 1 : S.s_chosen;
-    return n > 0 ? S.cand_id[i] : none;
+    if (S.chosen >= 0) return S.chosen;
+    uint32_t bk = S.red_k[0];
+    int bi = S.red_i[0];
+    for (int w = 1; w < kSampleThreads / 32; ++w)
+        if (S.red_k[w] < bk || (S.red_k[w] == bk && S.red_i[w] > bi)) { bk = S.red_k[w]; bi = S.red_i[w]; }
+    return bi;
 }
 
 // One block per sequence row of logits [B][ld] (vocab V <= 65535). Greedy when
 // temperature == 0 (first index of the maximum). Otherwise the inverse CDF of
-// sample_token with top_p = 1: scores sorted descending (ties: lower id first), weights
-// w = exp(double(s - s0) / T), draw = u * sum(w) with the reference's 24-bit uniform u,
-// first position whose running sum reaches the draw. Weights are summed in exact 2^-48
-// fixed point (the sampled token equals the reference's except when the draw falls within
-// ~1e-10 of a CDF boundary). The sorted order is found without a full sort:
-//  1. one pass histograms the weights over 2048 buckets of equal score width between the
+// sample_token with top_p = 1 (inference.cpp:345-426): scores sorted descending (ties:
+// lower id first), weights w = exp(double(s - s0) / T), draw = u * sum(w) with the
+// reference's 24-bit uniform u, first position whose running sum reaches the draw. Weights
+// are summed in exact 2^-48 fixed point (the sampled token equals the reference's except
+// when the draw falls within ~1e-10 of a CDF boundary). The sorted order is found without
+// a full sort:
+//  1. one pass histograms the weights over 512 buckets of equal score width between the
 //     row minimum and maximum (an order-preserving map: a higher score never lands in a
-//     lower bucket, and equal scores share one), so a row of 16384 spreads ~8 per bucket;
-//  2. a block scan over the buckets, highest first, locates the bucket holding the crossing;
-//  3. that bucket's scores are sorted in shared memory and a block scan finds the crossing.
+//     lower bucket, and equal scores share one), so a row of 16384 spreads ~32 per bucket;
+//  2. a warp scan over the buckets, highest first, locates the bucket holding the crossing;
+//  3. that bucket's scores are ranked in shared memory and the crossing read off.
 // When the crossing bucket holds more than kSampleCap scores (a row of near-identical
 // scores beside a distant maximum), the buckets are rebuilt from the order-preserving
-// integer key of each score instead, 11 bits at a time, until the selected prefix holds at
+// integer key of each score instead, 9 bits at a time, until the selected prefix holds at
 // most kSampleCap scores (or all 32 bits are fixed).
 // Rows with active[b] == 0 are skipped. The draw index of row b is draw_index[b] (or 0) +
 // draw_offset + *counter (when given); the token goes to out[b * out_stride + *counter]
@@ -437,32 +446,39 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(
     long long out_stride) {
     MM_PDL_ENTRY();
     __shared__ SampleShared S;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int b = blockIdx.x;
     const int step = counter ? *counter : 0;
     out += step;
     draw_offset += step;
-    const int b = blockIdx.x;
     if (active && !active[b]) return;
     const float* row = logits + b * ld;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    // Rows up to kSampleCache * kSampleThreads scores stay in registers across the passes.
-    const bool cached = V <= kSampleCache * kSampleThreads;
-    float vals[kSampleCache];
-    if (cached) {
-#pragma unroll
-        for (int k = 0; k < kSampleCache; ++k) {
-            const int j = threadIdx.x + k * kSampleThreads;
-            vals[k] = j < V ? row[j] : 0.f;
-        }
-    }
+    const bool vec = (V & 3) == 0 && (ld & 3) == 0 && (reinterpret_cast<uintptr_t>(logits) & 15) == 0;
     auto each = [&](auto&& f) {
-        if (cached) {
+        if (vec) {
+            // kSampleBatch 16-byte loads in flight per thread before any is used
+            const float4* r4 = reinterpret_cast<const float4*>(row);
+            const int n4 = V >> 2;
+            for (int base = 0; base < n4; base += kSampleThreads * kSampleBatch) {
+                float4 x[kSampleBatch];
 #pragma unroll
-            for (int k = 0; k < kSampleCache; ++k) {
-                const int j = threadIdx.x + k * kSampleThreads;
-                if (j < V) f(j, vals[k]);
+                for (int u = 0; u < kSampleBatch; ++u) {
+                    const int j4 = base + u * kSampleThreads + tid;
+                    x[u] = j4 < n4 ? r4[j4] : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+#pragma unroll
+                for (int u = 0; u < kSampleBatch; ++u) {
+                    const int j4 = base + u * kSampleThreads + tid;
+                    if (j4 < n4) {
+                        f(4 * j4, x[u].x);
+                        f(4 * j4 + 1, x[u].y);
+                        f(4 * j4 + 2, x[u].z);
+                        f(4 * j4 + 3, x[u].w);
+                    }
+                }
             }
         } else {
-            for (int j = threadIdx.x; j < V; j += kSampleThreads) f(j, row[j]);
+            for (int j = tid; j < V; j += kSampleThreads) f(j, row[j]);
         }
     };
 
@@ -470,7 +486,7 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(
     float mx = -INFINITY, mn = INFINITY;
     int mi = 0x7fffffff;
     each([&](int j, float v) {
-        if (v > mx) { mx = v; mi = j; }
+        if (v > mx || (v == mx && j < mi)) { mx = v; mi = j; }
         mn = fminf(mn, v);
     });
 #pragma unroll
@@ -482,22 +498,14 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(
     }
     if (lane == 0) { S.red_f[warp] = mx; S.red_i[warp] = mi; S.red_g[warp] = mn; }
     __syncthreads();
-    if (threadIdx.x == 0) {
-        float bm = S.red_f[0], bn = S.red_g[0];
-        int bi = S.red_i[0];
-        for (int w = 1; w < nw; ++w) {
-            if (S.red_f[w] > bm || (S.red_f[w] == bm && S.red_i[w] < bi)) { bm = S.red_f[w]; bi = S.red_i[w]; }
-            bn = fminf(bn, S.red_g[w]);
-        }
-        S.red_f[0] = bm;
-        S.red_i[0] = bi;
-        S.red_g[0] = bn;
+    float s0 = S.red_f[0], smin = S.red_g[0];
+    int best = S.red_i[0];
+    for (int w = 1; w < kSampleThreads / 32; ++w) {
+        if (S.red_f[w] > s0 || (S.red_f[w] == s0 && S.red_i[w] < best)) { s0 = S.red_f[w]; best = S.red_i[w]; }
+        smin = fminf(smin, S.red_g[w]);
     }
-    __syncthreads();
-    const float s0 = S.red_f[0], smin = S.red_g[0];
-    const int best = S.red_i[0];
     if (temperature == 0.f) {
-        if (threadIdx.x == 0) out[b * out_stride] = static_cast<uint16_t>(best);
+        if (tid == 0) out[b * out_stride] = static_cast<uint16_t>(best);
         return;
     }
     const double T = static_cast<double>(temperature);
@@ -508,99 +516,92 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(
     const float range = __fsub_rn(s0, smin);
     float scale = range > 0.f ? __fdiv_rn(static_cast<float>(kSampleBuckets), range) : 0.f;
     if (!(scale <= 3.0e38f)) scale = 0.f;
+    // bucket half-width 0.5 / scale <= 0.05
+    const SampleRowWeight wt{s0, scale, T, T == 1.0 && scale >= 10.f, S.xb, S.ebase};
     if (scale > 0.f) {
-        auto bucket_of = [&](float v) {
-            const float p = fminf(__fmul_rn(__fsub_rn(s0, v), scale), static_cast<float>(kSampleBuckets - 1));
-            return kSampleBuckets - 1 - static_cast<int>(p);
-        };
-        for (int i = threadIdx.x; i < kSampleBuckets; i += blockDim.x) { S.hist[i] = 0ull; S.hcount[i] = 0; }
+        sample_hist_clear(S);
+        if (wt.poly) {
+            const double inv = 1.0 / static_cast<double>(scale);
+            for (int i = tid; i < kSampleBuckets; i += kSampleThreads) {
+                const double x = -(static_cast<double>(kSampleBuckets - i) - 0.5) * inv;
+                S.xb[i] = x;
+                S.ebase[i] = exp(x) * 281474976710656.0;
+            }
+        }
         __syncthreads();
         each([&](int, float v) {
-            const int bk = bucket_of(v);
-            atomicAdd(&S.hist[bk], sample_weight_q(v, s0, T));
-            atomicAdd(&S.hcount[bk], 1);
+            const int bk = wt.bucket(v);
+            sample_hist_add(S, bk, wt(v, bk));
         });
         __syncthreads();
-        sample_locate(S, kSampleBuckets, true, seed, k);
-        const int chosen = S.s_chosen;
-        if (S.hcount[chosen] <= kSampleCap) {
-            const int tok = sample_pick(S, each, s0, T, [&](float v) { return bucket_of(v) == chosen; }, best);
-            if (threadIdx.x == 0) out[b * out_stride] = static_cast<uint16_t>(tok);
+        if (warp == 0) sample_locate(S, kSampleBuckets, true, seed, k);
+        __syncthreads();
+        const int chosen = S.chosen;
+        if (S.h.count[chosen] <= static_cast<unsigned>(kSampleCap)) {
+            const int tok = sample_pick(S, each, wt, [&](float v) { return wt.bucket(v) == chosen; }, best);
+            if (tid == 0) out[b * out_stride] = static_cast<uint16_t>(tok);
             return;
         }
-        __syncthreads();
+        __syncthreads();  // every thread has read the count before the histogram is cleared
     }
 
-    // fallback: buckets of the order-preserving key, refined 11 bits at a time
-    if (threadIdx.x == 0) { S.s_prefix = 0; S.s_bits = 0; }
-    __syncthreads();
+    // fallback: buckets of the order-preserving key, refined kSampleRadixBits at a time
+    uint32_t prefix = 0;
+    int bits = 0;
+    unsigned ncand = 0;
     bool first = true;
     while (true) {
-        const int bits = S.s_bits;
-        const uint32_t prefix = S.s_prefix;
-        const int width = min(11, 32 - bits);
+        const int width = min(kSampleRadixBits, 32 - bits);
         const int nb = 1 << width;
-        for (int i = threadIdx.x; i < kSampleBuckets; i += blockDim.x) { S.hist[i] = 0ull; S.hcount[i] = 0; }
+        sample_hist_clear(S);
         __syncthreads();
-        for (int j0 = 0; j0 < V; j0 += blockDim.x) {
-            const int j = j0 + threadIdx.x;
-            bool valid = j < V;
-            const float v = valid ? row[j] : 0.f;
+        each([&](int, float v) {
             const uint32_t key = float_key(v);
-            if (bits > 0) valid = valid && (key >> (32 - bits)) == prefix;
+            if (bits > 0 && (key >> (32 - bits)) != prefix) return;
             const int bk = static_cast<int>((key >> (32 - bits - width)) & (nb - 1));
-            const unsigned long long q = valid ? sample_weight_q(v, s0, T) : 0ull;
-            warp_bucket_add(S.hist, S.hcount, bk, q, valid);
-        }
+            sample_hist_add(S, bk, wt(v, wt.poly ? wt.bucket(v) : 0));
+        });
         __syncthreads();
-        sample_locate(S, nb, first, seed, k);
+        if (warp == 0) sample_locate(S, nb, first, seed, k);
+        __syncthreads();
         first = false;
-        if (threadIdx.x == 0) {
-            const int chosen = S.s_chosen;
-            S.s_prefix = (prefix << width) | static_cast<uint32_t>(chosen);
-            S.s_bits = bits + width;
-            S.s_ncand = S.hcount[chosen];
-        }
-        __syncthreads();
-        if (S.s_ncand <= kSampleCap || S.s_bits >= 32) break;
+        const int chosen = S.chosen;
+        prefix = (prefix << width) | static_cast<uint32_t>(chosen);
+        bits += width;
+        ncand = S.h.count[chosen];
+        __syncthreads();  // every thread has read the count before the next clear
+        if (ncand <= static_cast<unsigned>(kSampleCap) || bits >= 32) break;
     }
-    const int bits = S.s_bits;
-    const uint32_t prefix = S.s_prefix;
-    const int ncand = S.s_ncand;
-    __syncthreads();
-    if (ncand > kSampleCap) {
+    if (ncand > static_cast<unsigned>(kSampleCap)) {
         // More than kSampleCap scores share one exact value (every key bit fixed): equal
         // weights w, ordered by id, so the crossing is position m = ceil(rem / w) - 1 among
-        // them, found by an id-ordered block scan over the row.
+        // them, found by an id-ordered scan of warp 0 over the row.
+        if (warp != 0) return;
         const uint32_t u = (prefix & 0x80000000u) ? (prefix & 0x7fffffffu) : ~prefix;
-        const unsigned long long w = sample_weight_q(__uint_as_float(u), s0, T);
-        const unsigned long long rem = S.s_draw;
-        long long m = ncand - 1;
+        const float fv = __uint_as_float(u);
+        const unsigned long long w = wt(fv, wt.poly ? wt.bucket(fv) : 0);
+        const unsigned long long rem = S.draw;
+        long long m = static_cast<long long>(ncand) - 1;
         if (w > 0 && rem <= static_cast<unsigned long long>(ncand) * w) m = static_cast<long long>((rem + w - 1) / w) - 1;
-        m = max(0LL, min(m, static_cast<long long>(ncand - 1)));
+        m = max(0LL, min(m, static_cast<long long>(ncand) - 1));
         long long seen = 0;
-        for (int j0 = 0; j0 < V; j0 += blockDim.x) {
-            const int j = j0 + threadIdx.x;
-            const int hit = (j < V && float_key(row[j]) == prefix) ? 1 : 0;
-            const unsigned long long incl = block_scan_incl(static_cast<unsigned long long>(hit), S.warp_tot);
-            const long long before = seen + static_cast<long long>(incl) - hit;
+        for (int j0 = 0; j0 < V; j0 += 32) {
+            const int j = j0 + lane;
+            const bool hit = j < V && float_key(row[j]) == prefix;
+            const unsigned mask = __ballot_sync(0xffffffffu, hit);
+            const long long before = seen + __popc(mask & ((1u << lane) - 1u));
             if (hit && before == m) out[b * out_stride] = static_cast<uint16_t>(j);
-            // the block's count for this chunk is the last thread's inclusive sum
-            if (threadIdx.x == kSampleThreads - 1) S.s_last = static_cast<int>(incl);
-            __syncthreads();
-            seen += S.s_last;
-            __syncthreads();
+            seen += __popc(mask);
             if (seen > m) break;
         }
         return;
     }
-    const int tok = sample_pick(S, each, s0, T, [&](float v) {
+    const int tok = sample_pick(S, each, wt, [&](float v) {
         const uint32_t key = float_key(v);
         return (bits >= 32 ? key : (key >> (32 - bits))) == prefix;
     }, best);
-    if (threadIdx.x == 0) out[b * out_stride] = static_cast<uint16_t>(tok);
+    if (tid == 0) out[b * out_stride] = static_cast<uint16_t>(tok);
 }
-
 } // namespace mm
 
 namespace mm {

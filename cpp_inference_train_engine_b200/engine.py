@@ -123,6 +123,10 @@ def lib():
                                                     ctypes.c_int, ctypes.c_float, _vp]),
         "mm_cuda_profile_gemm_shapes": (ctypes.c_int64, [_vp, ctypes.c_char_p, ctypes.c_int64]),
         "mm_cuda_selftest_wait_timeout": (ctypes.c_int, [_vp, ctypes.c_uint32]),
+        "mm_cuda_bench_gemm": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                              _vp, ctypes.c_int64, ctypes.c_int, _vp, ctypes.c_int64,
+                                              ctypes.c_int, _vp, ctypes.c_int64, ctypes.c_int,
+                                              ctypes.POINTER(ctypes.c_float)]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)
@@ -392,6 +396,14 @@ class CudaExecution:
         self._check(lib().mm_cuda_gemm_f16(self.h, M, N, K, a_ptr, lda, int(a_mn), b_ptr, ldb,
                                            int(b_mn), out_ptr, ldc, out_kind, alpha,
                                            residual_ptr, ldr, int(bf16)))
+
+    def bench_gemm(self, reps, M, N, K, a_ptr, lda, a_mn, b_ptr, ldb, b_mn, out_ptr, ldc, out_kind):
+        """Device milliseconds per launch of `reps` back-to-back launches of one product,
+        replayed from a CUDA graph (mm_cuda_bench_gemm)."""
+        ms = ctypes.c_float(0.0)
+        self._check(lib().mm_cuda_bench_gemm(self.h, reps, M, N, K, a_ptr, lda, int(a_mn), b_ptr, ldb,
+                                             int(b_mn), out_ptr, ldc, out_kind, ctypes.byref(ms)))
+        return float(ms.value)
 
     def decode_attention(self, q_ptr, cache_ptr, cache_seq_stride, pos_ptr, batch, splits, scale,
                          out_ptr):

@@ -1,8 +1,11 @@
 """Microbenchmark of the tcgen05 GEMM at one shape through the kernel-level entry point
 (mm_cuda_gemm_f16 in include/mm_cuda_kernels.h).
 
-Device time per launch comes from the library's own CUDA-event profile (events recorded on
-the library stream around every GEMM launch), so host gaps between calls do not count.
+Device time per launch: by default `--iters` launches are captured in one CUDA graph and
+replayed back to back (mm_cuda_bench_gemm), as the engine's passes issue them, so neither
+host launch cost nor a synchronisation per call is counted. `--eager` instead times each
+call of mm_cuda_gemm_f16 with the library's CUDA-event profile (events around every
+launch; each call also waits for completion, so short products read long).
 The default shape is the vocabulary head of one 32,640-token teacher-forced chunk:
 [T, 3d] x [V, 3d]^T with K = 3 * 512 (the fp32-accurate three-term split), fp32 output.
 
@@ -20,6 +23,7 @@ def main(argv=None):
     ap.add_argument("--out", default="f32", choices=["f32", "f16", "acc"])
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--eager", action="store_true", help="time each eager call instead")
     args = ap.parse_args(argv)
 
     import torch
@@ -42,6 +46,14 @@ def main(argv=None):
         ex.gemm(M, N, K, A.data_ptr(), A.shape[1], args.a_mn, B.data_ptr(), B.shape[1],
                 args.b_mn, C.data_ptr(), N, kind)
 
+    if not args.eager:
+        ms = ex.bench_gemm(args.iters, M, N, K, A.data_ptr(), A.shape[1], args.a_mn, B.data_ptr(),
+                           B.shape[1], args.b_mn, C.data_ptr(), N, kind)
+        print(json.dumps({"shape": [M, N, K], "a_mn": args.a_mn, "b_mn": args.b_mn, "out": args.out,
+                          "graph_launches": args.iters, "ms_per_launch": ms,
+                          "tflops": 2.0 * M * N * K / (ms / 1e3) / 1e12}))
+        ex.close()
+        return
     for _ in range(args.warmup):
         run()
     ex.profile(1)

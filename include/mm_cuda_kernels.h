@@ -83,6 +83,14 @@ int mm_cuda_stream(mm_cuda_ctx* ctx, void** stream);
  * exactly as after a GEMM whose pipeline stalled. */
 int mm_cuda_selftest_wait_timeout(mm_cuda_ctx* ctx, uint32_t polls);
 
+/* Measurement entry (no reference counterpart): the product of mm_cuda_gemm_f16 (fp32
+ * store, accumulate, fp16 or bf16 output, no residual) launched `reps` times back to back
+ * inside one CUDA graph, so that consecutive launches overlap as in the engine's own
+ * passes; *ms_per_launch receives the device time of one replay divided by reps. */
+int mm_cuda_bench_gemm(mm_cuda_ctx* ctx, int reps, int M, int N, int K, const void* a, int64_t lda,
+                       int a_mn, const void* b, int64_t ldb, int b_mn, void* out, int64_t ldc,
+                       int out_kind, float* ms_per_launch);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,5 +1,7 @@
 """Batched latent-cache decode and the on-device sampler against the reference's
 CpuDecoder and sample_token."""
+import dataclasses
+
 import numpy as np
 import pytest
 
@@ -76,9 +78,11 @@ def test_36m_decode_split_and_wide_batches(B, P, steps):
 
 def test_sampler_matches_reference_sample_token():
     require_gpu()
-    execs = {264: E.CudaExecution(TINY), 16384: E.CudaExecution(MLA36M)}
+    # 261: a vocabulary that is not a multiple of 4 takes the scalar row loads
+    execs = {264: E.CudaExecution(TINY), 16384: E.CudaExecution(MLA36M),
+             261: E.CudaExecution(dataclasses.replace(TINY, vocab_size=261))}
     rng = np.random.default_rng(7)
-    for V in (264, 16384):
+    for V in (264, 261, 16384):
         ex = execs[V]
         B = 64
         logits = (rng.normal(size=(B, V)) * rng.uniform(0.2, 3, size=(B, 1))).astype(np.float32)

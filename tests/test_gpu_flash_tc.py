@@ -1,0 +1,77 @@
+"""The tcgen05 attention forward (64-wide heads of the 35.8M model) on sequences of several
+128-query tiles, ragged last tile included: teacher-forced log-probabilities against the
+reference's CPU build (2e-3 absolute, as the other model tests), and log-probabilities and
+the weighted-NLL gradient against the same engine with the forward on the mma.sync kernel
+(MM_FLASH_TC=0, a separate process): 3e-3 absolute and 3e-4 mean absolute on log-probs,
+1e-2 relative on the gradient (both paths round P to fp16, normalised per 128-key tile here
+and per 64-key tile there, and the difference grows through the ten layers)."""
+import os
+import subprocess
+import sys
+import textwrap
+
+import numpy as np
+import pytest
+
+import cpp_inference_train_engine_b200 as E
+from cpp_inference_train_engine_b200.config import MLA36M
+from oracle import ref
+from tests.gpu_util import ROOT, rel, require_gpu
+
+pytestmark = pytest.mark.gpu
+
+B, S = 3, 300  # query tiles of 128, 128 and 44 rows
+
+
+def _batch():
+    rng = np.random.default_rng(21)
+    x = rng.integers(0, 16384, (B, S)).astype(np.uint16)
+    t = rng.integers(0, 16384, (B, S)).astype(np.uint16)
+    coef = (rng.normal(size=(B, S)) * 1e-3).astype(np.float32)
+    return x, t, coef
+
+
+_RUN = textwrap.dedent("""
+    import sys
+    import numpy as np
+    import cpp_inference_train_engine_b200 as E
+    from cpp_inference_train_engine_b200.config import MLA36M
+    from tests.test_gpu_flash_tc import _batch, B, S
+    x, t, coef = _batch()
+    ex = E.make_execution(MLA36M, E.init_params(MLA36M, 5), optimizer=E.AdamWConfig())
+    lp = ex.log_probabilities(x, t, B, S)
+    ex.zero_grad()
+    ex.accumulate(x, t, coef, B, S)
+    g = ex.synchronize_to_host(params=False, grads=True)["grads"]
+    np.savez(sys.argv[1], lp=lp, g=g)
+""")
+
+
+def _run(path, tc):
+    env = dict(os.environ, PYTHONPATH=ROOT, MM_FLASH_TC="1" if tc else "0")
+    out = subprocess.run([sys.executable, "-c", _RUN, path], cwd=ROOT, env=env, capture_output=True,
+                         text=True, timeout=600)
+    assert out.returncode == 0, out.stdout + out.stderr
+    return np.load(path)
+
+
+def test_tc_forward_matches_mma_forward(tmp_path):
+    require_gpu()
+    a = _run(str(tmp_path / "tc.npz"), True)
+    b = _run(str(tmp_path / "mma.npz"), False)
+    d = np.abs(a["lp"] - b["lp"])
+    assert d.max() < 3e-3 and d.mean() < 3e-4, (d.max(), d.mean())
+    assert rel(a["g"], b["g"]) < 1e-2
+
+
+def test_36m_multi_tile_log_probs_match_reference():
+    require_gpu()
+    if not ref.available():
+        pytest.skip("oracle/_ref not built")
+    W = E.init_params(MLA36M, 0)
+    s = ref.Session(MLA36M, 0)
+    ex = E.make_execution(MLA36M, W)
+    x, t, _ = _batch()
+    want = s.log_probs(x, t, np.ones((B, S), np.float32), B, S)
+    got = ex.log_probabilities(x, t, B, S)
+    assert np.abs(got - want).max() < 2e-3

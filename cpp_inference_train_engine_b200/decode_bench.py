@@ -13,6 +13,11 @@ Attention mode times one launch of the split latent attention (mm_cuda_decode_at
 over a synthetic fp16 cache of --ctx positions per row:
 
     python -m cpp_inference_train_engine_b200.decode_bench --attention --batch 2048 --ctx 256
+
+Sample mode times the exact sampler (mm_cuda_sample) on synthetic Gaussian logits of
+standard deviation --logit-sd over the 16384-word vocabulary, per launch:
+
+    python -m cpp_inference_train_engine_b200.decode_bench --sample --batch 2048 --temperature 1.0
 """
 import argparse
 import json
@@ -63,6 +68,32 @@ def attention(args):
     ex.close()
 
 
+def sample(args):
+    import numpy as np
+
+    import cpp_inference_train_engine_b200 as E
+    ex = E.CudaExecution(E.MLA36M)
+    rng = np.random.default_rng(0)
+    V = E.MLA36M.vocab_size
+    for B in args.batch:
+        logits = (rng.normal(size=(B, V)) * args.logit_sd).astype(np.float32)
+        seeds = rng.integers(0, 2 ** 63, B).astype(np.uint64)
+        draws = rng.integers(0, 300, B).astype(np.int32)
+        for temp in args.temperature:
+            for _ in range(args.warmup):
+                ex.sample(logits, temp, seeds, draws)
+            ex.profile(1)
+            for _ in range(args.iters):
+                ex.sample(logits, temp, seeds, draws)
+            ms, n, _ = ex.profile(0)["k_sample"]
+            peak, src = _peak_hbm()
+            us = ms / max(n, 1) * 1e3
+            print(json.dumps({"kernel": "sample", "batch": B, "vocab": V, "temperature": temp,
+                              "logit_sd": args.logit_sd, "us": us,
+                              "hbm_frac": 4.0 * B * V / (us / 1e6) / 1e9 / peak, "peak_source": src}))
+    ex.close()
+
+
 def decode(args):
     import numpy as np
 
@@ -102,6 +133,8 @@ def decode(args):
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--attention", action="store_true")
+    ap.add_argument("--sample", action="store_true")
+    ap.add_argument("--logit-sd", type=float, default=1.0)
     ap.add_argument("--batch", type=lambda s: [int(x) for x in s.split(",")], default=[1, 16, 64])
     ap.add_argument("--prompt", type=int, default=1024)
     ap.add_argument("--new", type=int, default=128)
@@ -111,7 +144,12 @@ def main(argv=None):
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=2)
     args = ap.parse_args(argv)
-    attention(args) if args.attention else decode(args)
+    if args.attention:
+        attention(args)
+    elif args.sample:
+        sample(args)
+    else:
+        decode(args)
 
 
 if __name__ == "__main__":

@@ -223,16 +223,56 @@ __global__ void split3_rows_kernel(const float* __restrict__ h, long long ldh, i
     h3[t * ld3 + 2 * d + j] = hi;
 }
 
-// Embedding gradient from the input gather (model.cpp:238-240): dE[tok] += s * dy[t].
-__global__ void embed_backward_kernel(const uint16_t* __restrict__ tokens, const float* __restrict__ dy,
-                                      int T, int d, float* __restrict__ dE,
-                                      const float* __restrict__ grad_scale) {
+// Embedding gradient from the input gather (model.cpp:238-240): dE[tok] += s * dy[t], made
+// independent of the order in which tokens sharing an id arrive: each row's sum is taken
+// exactly in 64-bit fixed point (integer additions commute), then converted once. The unit
+// is 2^-k with k from the chunk's max |dy| (m < 2^e) and token count (T < 2^et),
+// k = 62 - e - et, so |q| < 2^(62 - et) and no sum of T terms reaches 2^62.
+__device__ __forceinline__ int embed_fixed_shift(unsigned int max_bits, int T) {
+    const float m = __uint_as_float(max_bits);
+    if (!(m > 0.f) || !isfinite(m)) return 0;
+    int e = 0, et = 0;
+    frexpf(m, &e);
+    frexpf(static_cast<float>(T), &et);
+    return 62 - e - et;
+}
+// dy rows in fixed point into acc[V][d]; a non-finite dy sets *nonfinite instead.
+__global__ void embed_grad_fixed_kernel(const uint16_t* __restrict__ tokens, const float* __restrict__ dy, int T,
+                                        int d, unsigned long long* __restrict__ acc,
+                                        const unsigned int* __restrict__ max_bits, int* __restrict__ nonfinite) {
     MM_PDL_ENTRY();
     const int t = warp_row(), lane = threadIdx.x & 31;
     if (t >= T) return;
+    const int k = embed_fixed_shift(*max_bits, T);
+    const long long row = static_cast<long long>(tokens[t]) * d;
+    for (int j = lane; j < d; j += 32) {
+        const float v = dy[static_cast<long long>(t) * d + j];
+        if (!isfinite(v)) {
+            *nonfinite = 1;
+            continue;
+        }
+        const long long q = __double2ll_rn(ldexp(static_cast<double>(v), k));
+        if (q) atomicAdd(&acc[row + j], static_cast<unsigned long long>(q));
+    }
+}
+// dE += s * acc * 2^-k over every entry, clearing acc for the next chunk; a non-finite input
+// is passed on as a NaN in dE[0] (the optimizer's finiteness check reports it).
+__global__ void embed_grad_convert_kernel(unsigned long long* __restrict__ acc, long long n, int T,
+                                          const unsigned int* __restrict__ max_bits,
+                                          const int* __restrict__ nonfinite, const float* __restrict__ grad_scale,
+                                          float* __restrict__ dE) {
+    MM_PDL_ENTRY();
+    const int k = embed_fixed_shift(*max_bits, T);
     const float s = grad_scale ? *grad_scale : 1.0f;
-    const int tok = tokens[t];
-    for (int j = lane; j < d; j += 32) atomicAdd(&dE[static_cast<long long>(tok) * d + j], dy[t * d + j] * s);
+    for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const long long q = static_cast<long long>(acc[i]);
+        if (q) {
+            dE[i] += static_cast<float>(ldexp(static_cast<double>(q), -k)) * s;
+            acc[i] = 0ull;
+        }
+    }
+    if (blockIdx.x == 0 && threadIdx.x == 0 && *nonfinite) dE[0] = __int_as_float(0x7fc00000);
 }
 
 // Key gradient split (model.cpp:204-215): dk_nope (fp16, per head) and the rope-key

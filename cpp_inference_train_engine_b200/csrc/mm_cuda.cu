@@ -368,8 +368,11 @@ int mm_cuda_grpo_coefficients(mm_cuda_ctx* h, const float* lp, const float* old_
         MM_CUDA_CHECK(cudaMemsetAsync(cx.d_sums, 0, sizeof(mm::GrpoSums), cx.stream));
         MM_LAUNCH(mm::advantages_kernel, mm::blocks_for(n / group_size, 128), 128, 0, d_rew, n / group_size, group_size,
                   1e-6f, d_adv, cx.d_any);
-        MM_LAUNCH(mm::grpo_coef_kernel, mm::blocks_for(T, 256), 256, 0, d_lp, d_old, d_ref, d_mask, d_adv, d_sup,
-                  static_cast<int>(T), seq, static_cast<double>(n_total), clip, klc, d_coef, cx.d_sums);
+        const unsigned nb = mm::blocks_for(T, 256);
+        double2* part = static_cast<double2*>(cx.sums_part.get(sizeof(double2) * nb));
+        MM_LAUNCH(mm::grpo_coef_kernel, nb, 256, 0, d_lp, d_old, d_ref, d_mask, d_adv, d_sup,
+                  static_cast<int>(T), seq, static_cast<double>(n_total), clip, klc, d_coef, cx.d_sums, part);
+        MM_LAUNCH(mm::grpo_sums_kernel, 1, 32, 0, part, static_cast<int>(nb), cx.d_sums);
         mm::GrpoSums sums{};
         MM_CUDA_CHECK(cudaMemcpyAsync(coefficients, d_coef, T * 4, cudaMemcpyDeviceToHost, cx.stream));
         if (advantages) MM_CUDA_CHECK(cudaMemcpyAsync(advantages, d_adv, n * 4, cudaMemcpyDeviceToHost, cx.stream));

@@ -624,7 +624,21 @@ inline void backward_chunk(Context& cx, int Bc, int S) {
         launch_rmsnorm_backward(cx, b.x_in, c.d, cx.W(l, kAttnNorm), w.dh, c.d, w.dres, c.d, T, c.d, w.dy, c.d, w.dy16,
                                 ld_d, cx.G(l, kAttnNorm), inv_s);
     }
-    MM_LAUNCH(embed_backward_kernel, warp_rows_grid(T), 256, 0, w.tokens, w.dy, T, c.d, cx.GE(), inv_s);
+    // embedding-gather gradient, summed per vocabulary row in 64-bit fixed point (the
+    // accumulator is zero between chunks: the conversion clears what it consumes)
+    const long long nE = static_cast<long long>(c.V) * c.d;
+    const size_t acc_bytes = sizeof(unsigned long long) * static_cast<size_t>(nE);
+    const bool fresh = cx.emb_acc.cap < acc_bytes + 256;
+    char* eb = static_cast<char*>(cx.emb_acc.get(acc_bytes + 256));
+    auto* acc = reinterpret_cast<unsigned long long*>(eb);
+    auto* max_bits = reinterpret_cast<unsigned int*>(eb + acc_bytes);
+    int* nonfinite = reinterpret_cast<int*>(eb + acc_bytes + 4);
+    if (fresh) MM_CUDA_CHECK(cudaMemsetAsync(acc, 0, acc_bytes, cx.stream));
+    MM_CUDA_CHECK(cudaMemsetAsync(max_bits, 0, 8, cx.stream));
+    MM_LAUNCH(absmax_kernel, blocks_for(static_cast<long long>(T) * c.d, 256), 256, 0, w.dy, T * c.d, max_bits);
+    MM_LAUNCH(embed_grad_fixed_kernel, warp_rows_grid(T), 256, 0, w.tokens, w.dy, T, c.d, acc, max_bits, nonfinite);
+    MM_LAUNCH(embed_grad_convert_kernel, static_cast<unsigned>(sm_count() * 8), 256, 0, acc, nE, T, max_bits, nonfinite,
+              inv_s, cx.GE());
 }
 
 } // namespace mm

@@ -286,6 +286,8 @@ class Context {
     Arena ws_arena;
     Staging stage;
     Staging splitk;  // split-K partials of the GEMM
+    Staging emb_acc; // fixed-point embedding-gather gradient [V][d] (+ max |dy|, non-finite flag)
+    Staging sums_part;  // per-block GRPO loss/kl partials (double2)
     DecodeState dec;
     int dec_len = 0;  // positions filled in the decode session (0: no session)
 

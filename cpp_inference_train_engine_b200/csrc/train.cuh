@@ -257,8 +257,11 @@ inline mm_step_result grpo_step(Context& pc, Context& rc, const uint16_t* input,
         }
         PhaseTimer t(pc, kPhBackward);
         MM_CUDA_CHECK(cudaMemsetAsync(&pc.d_sums->max_coef_bits, 0, 4, pc.stream));
-        MM_LAUNCH_CX(pc, grpo_coef_kernel, blocks_for(T, 256), 256, 0, w.lp, w.old_lp, w.ref_lp, w.mask, d_adv + r0,
-                     d_sup + r0, static_cast<int>(T), S, static_cast<double>(n_total), clip, klc, w.coef, pc.d_sums);
+        const unsigned nb = blocks_for(T, 256);
+        double2* part = static_cast<double2*>(pc.sums_part.get(sizeof(double2) * nb));
+        MM_LAUNCH_CX(pc, grpo_coef_kernel, nb, 256, 0, w.lp, w.old_lp, w.ref_lp, w.mask, d_adv + r0,
+                     d_sup + r0, static_cast<int>(T), S, static_cast<double>(n_total), clip, klc, w.coef, pc.d_sums, part);
+        MM_LAUNCH_CX(pc, grpo_sums_kernel, 1, 32, 0, part, static_cast<int>(nb), pc.d_sums);
         MM_LAUNCH_CX(pc, grad_scale_kernel, 1, 1, 0, pc.d_sums, pc.d_scale);
         backward_chunk(pc, bc, S);
     }

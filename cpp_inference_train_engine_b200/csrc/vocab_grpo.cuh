@@ -110,13 +110,15 @@ struct GrpoSums {
 };
 
 // Per token t of a chunk (rows t in [0, T), sequence = t / S): when mask[t] != 0,
-// coef[t] = nll_coefficient / (n_total * supervised[seq]) in float, and loss/kl sums
-// (objective/denominator) accumulate in double. Masked tokens get coef 0.
+// coef[t] = nll_coefficient / (n_total * supervised[seq]) in float, and the block's loss/kl
+// sums (objective/denominator, in double) go to part[block] for grpo_sums_kernel. Masked
+// tokens get coef 0.
 __global__ void grpo_coef_kernel(const float* __restrict__ lp, const float* __restrict__ old_lp,
                                  const float* __restrict__ ref_lp, const float* __restrict__ mask,
                                  const float* __restrict__ adv, const int* __restrict__ supervised,
                                  int T, int S, double n_total, float clip, float klc,
-                                 float* __restrict__ coef, GrpoSums* __restrict__ sums) {
+                                 float* __restrict__ coef, GrpoSums* __restrict__ sums,
+                                 double2* __restrict__ part) {
     MM_PDL_ENTRY();
     __shared__ double sl[32], sk[32];
     const int t = blockIdx.x * blockDim.x + threadIdx.x;
@@ -164,9 +166,22 @@ __global__ void grpo_coef_kernel(const float* __restrict__ lp, const float* __re
             a += sl[w];
             b += sk[w];
         }
-        atomicAdd(&sums->loss, a);
-        atomicAdd(&sums->kl, b);
+        part[blockIdx.x] = make_double2(a, b);
     }
+}
+
+// Adds grpo_coef_kernel's per-block (loss, kl) partials into the sums in block order, so
+// the reported objective does not depend on the order in which blocks finish.
+__global__ void grpo_sums_kernel(const double2* __restrict__ part, int nblocks, GrpoSums* __restrict__ sums) {
+    MM_PDL_ENTRY();
+    if (blockIdx.x != 0 || threadIdx.x != 0) return;
+    double a = 0.0, b = 0.0;
+    for (int i = 0; i < nblocks; ++i) {
+        a += part[i].x;
+        b += part[i].y;
+    }
+    sums->loss += a;
+    sums->kl += b;
 }
 
 // scale = 2^-floor(log2(max|coef|)) so that the largest scaled coefficient lies in [1, 2);

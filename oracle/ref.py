@@ -15,6 +15,9 @@ import numpy as np
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "_ref", "libmini_mla_ref.so")
+# The same reference sources with sessions on the sm_100a backend through its reference-side
+# adapter (`make -C oracle cuda`): the reference's own Execution-API drivers on the GPU.
+CUDA_LIB_PATH = os.path.join(_HERE, "_ref", "libmini_mla_ref_cuda.so")
 
 _u16p = ctypes.POINTER(ctypes.c_uint16)
 _f32p = ctypes.POINTER(ctypes.c_float)
@@ -22,19 +25,20 @@ _f64p = ctypes.POINTER(ctypes.c_double)
 _i32p = ctypes.POINTER(ctypes.c_int)
 _u64p = ctypes.POINTER(ctypes.c_uint64)
 
-_lib = None
+_libs = {}
 
 
-def available() -> bool:
-    return os.path.exists(LIB_PATH)
+def available(backend: str = "cpu") -> bool:
+    return os.path.exists(CUDA_LIB_PATH if backend == "cuda" else LIB_PATH)
 
 
-def lib():
-    global _lib
-    if _lib is None:
-        if not available():
-            raise RuntimeError(f"reference oracle not built: {LIB_PATH} (run make -C oracle)")
-        L = ctypes.CDLL(LIB_PATH)
+def lib(backend: str = "cpu"):
+    L = _libs.get(backend)
+    if L is None:
+        path = CUDA_LIB_PATH if backend == "cuda" else LIB_PATH
+        if not os.path.exists(path):
+            raise RuntimeError(f"reference oracle not built: {path} (run make -C oracle)")
+        L = ctypes.CDLL(path)
         L.ref_last_error.restype = ctypes.c_char_p
         L.ref_session_create.restype = ctypes.c_void_p
         L.ref_session_create.argtypes = [ctypes.POINTER(ctypes.c_int), ctypes.c_float,
@@ -80,8 +84,8 @@ def lib():
                                       ctypes.c_int, ctypes.c_int, _u16p, _u16p, _f32p, _f32p,
                                       _f32p, ctypes.c_float, ctypes.c_float, ctypes.c_float,
                                       _f64p, _f64p, _f64p, _i32p, _f32p, _f32p]
-        _lib = L
-    return _lib
+        _libs[backend] = L
+    return L
 
 
 def _p(a, t):
@@ -94,17 +98,19 @@ class RefError(RuntimeError):
         self.code = code
 
 
-def _check(rc: int):
+def _check(rc: int, L=None):
     if rc != 0:
-        raise RefError(rc, lib().ref_last_error().decode())
+        raise RefError(rc, (L or lib()).ref_last_error().decode())
 
 
 class Session:
     """Model + optional AdamW Optimizer + ``make_execution("cpu")``
-    (src/model/model.cpp:20-75, src/train/optimizer.cpp:53-72, src/infer/inference.cpp:314-329)."""
+    (src/model/model.cpp:20-75, src/train/optimizer.cpp:53-72, src/infer/inference.cpp:314-329);
+    with backend="cuda" the execution is the sm_100a backend's reference-side adapter
+    (make_cuda_execution) and the same reference code drives the GPU."""
 
-    def __init__(self, cfg, seed: int, optimizer=None):
-        L = lib()
+    def __init__(self, cfg, seed: int, optimizer=None, backend: str = "cpu"):
+        L = self.L = lib(backend)
         ints = (ctypes.c_int * 11)(*cfg.int_fields())
         opt = np.asarray(optimizer if optimizer is not None else [0.9, 0.95, 1e-8, 0.1, 1.0],
                          dtype=np.float32)
@@ -117,7 +123,7 @@ class Session:
 
     def close(self):
         if self.h:
-            lib().ref_session_destroy(self.h)
+            self.L.ref_session_destroy(self.h)
             self.h = None
 
     def __del__(self):
@@ -128,13 +134,13 @@ class Session:
 
     def _read(self, which):
         out = np.empty(self.n, np.float32)
-        _check(lib().ref_session_read(self.h, which, _p(out, _f32p)))
+        _check(self.L.ref_session_read(self.h, which, _p(out, _f32p)), self.L)
         return out
 
     def _write(self, which, arr):
         a = np.ascontiguousarray(arr, dtype=np.float32)
         assert a.size == self.n
-        _check(lib().ref_session_write(self.h, which, _p(a, _f32p)))
+        _check(self.L.ref_session_write(self.h, which, _p(a, _f32p)), self.L)
 
     def params(self):
         return self._read(0)
@@ -157,16 +163,16 @@ class Session:
 
     @property
     def steps(self):
-        return int(lib().ref_session_steps(self.h))
+        return int(self.L.ref_session_steps(self.h))
 
     @steps.setter
     def steps(self, s):
-        lib().ref_session_set_steps(self.h, s)
+        self.L.ref_session_set_steps(self.h, s)
 
     def forward(self, tokens, batch, seq):
         t = np.ascontiguousarray(tokens, np.uint16).reshape(-1)
         out = np.empty((batch * seq, self.cfg.vocab_size), np.float32)
-        _check(lib().ref_forward(self.h, _p(t, _u16p), batch, seq, _p(out, _f32p)))
+        _check(self.L.ref_forward(self.h, _p(t, _u16p), batch, seq, _p(out, _f32p)), self.L)
         return out
 
     def log_probs(self, inp, tgt, mask, batch, seq):
@@ -174,12 +180,12 @@ class Session:
         t = np.ascontiguousarray(tgt, np.uint16).reshape(-1)
         m = np.ascontiguousarray(mask, np.float32).reshape(-1)
         out = np.empty(batch * seq, np.float32)
-        _check(lib().ref_log_probs(self.h, _p(i, _u16p), _p(t, _u16p), _p(m, _f32p), batch, seq,
-                                   _p(out, _f32p)))
+        _check(self.L.ref_log_probs(self.h, _p(i, _u16p), _p(t, _u16p), _p(m, _f32p), batch, seq,
+                                   _p(out, _f32p)), self.L)
         return out
 
     def zero_grad(self):
-        _check(lib().ref_zero_grad(self.h))
+        _check(self.L.ref_zero_grad(self.h), self.L)
 
     def accumulate(self, inp, tgt, mask, coef, batch, seq):
         i = np.ascontiguousarray(inp, np.uint16).reshape(-1)
@@ -187,24 +193,24 @@ class Session:
         m = np.ascontiguousarray(mask, np.float32).reshape(-1)
         c = np.ascontiguousarray(coef, np.float32).reshape(-1)
         loss = ctypes.c_double()
-        _check(lib().ref_accumulate(self.h, _p(i, _u16p), _p(t, _u16p), _p(m, _f32p),
-                                    _p(c, _f32p), batch, seq, ctypes.byref(loss)))
+        _check(self.L.ref_accumulate(self.h, _p(i, _u16p), _p(t, _u16p), _p(m, _f32p),
+                                    _p(c, _f32p), batch, seq, ctypes.byref(loss)), self.L)
         return loss.value
 
     def update(self, lr):
         norm = ctypes.c_double()
-        _check(lib().ref_update(self.h, lr, ctypes.byref(norm)))
+        _check(self.L.ref_update(self.h, lr, ctypes.byref(norm)), self.L)
         return norm.value
 
     def prefill(self, ids):
         a = np.ascontiguousarray(ids, np.uint16)
         out = np.empty(self.cfg.vocab_size, np.float32)
-        _check(lib().ref_prefill(self.h, _p(a, _u16p), a.size, _p(out, _f32p)))
+        _check(self.L.ref_prefill(self.h, _p(a, _u16p), a.size, _p(out, _f32p)), self.L)
         return out
 
     def decode(self, token):
         out = np.empty(self.cfg.vocab_size, np.float32)
-        _check(lib().ref_decode(self.h, int(token), _p(out, _f32p)))
+        _check(self.L.ref_decode(self.h, int(token), _p(out, _f32p)), self.L)
         return out
 
     def rollout(self, prompt, completion_tokens, sequence, eos, pad, seed, temperature=1.0):
@@ -216,9 +222,9 @@ class Session:
         tgt = np.zeros(sequence, np.uint16)
         mask = np.zeros(sequence, np.float32)
         old = np.zeros(sequence, np.float32)
-        _check(lib().ref_rollout(self.h, _p(p, _u16p), p.size, completion_tokens, sequence, eos,
+        _check(self.L.ref_rollout(self.h, _p(p, _u16p), p.size, completion_tokens, sequence, eos,
                                  pad, seed, temperature, _p(toks, _u16p), ctypes.byref(n),
-                                 _p(inp, _u16p), _p(tgt, _u16p), _p(mask, _f32p), _p(old, _f32p)))
+                                 _p(inp, _u16p), _p(tgt, _u16p), _p(mask, _f32p), _p(old, _f32p)), self.L)
         return dict(tokens=toks[: n.value].copy(), input=inp, target=tgt, mask=mask, old_lp=old)
 
 
@@ -235,11 +241,11 @@ def grpo_update(policy: Session, reference: Session, group_size, inp, tgt, mask,
     skipped = ctypes.c_int()
     adv = np.zeros(n, np.float32)
     coef = np.zeros((n, seq), np.float32)
-    _check(lib().ref_grpo_update(policy.h, reference.h, n, group_size, seq, _p(i, _u16p),
+    _check(policy.L.ref_grpo_update(policy.h, reference.h, n, group_size, seq, _p(i, _u16p),
                                  _p(t, _u16p), _p(m, _f32p), _p(o, _f32p), _p(r, _f32p), clip,
                                  klc, lr, ctypes.byref(loss), ctypes.byref(kl),
                                  ctypes.byref(norm), ctypes.byref(skipped), _p(adv, _f32p),
-                                 _p(coef, _f32p)))
+                                 _p(coef, _f32p)), policy.L)
     return dict(loss=loss.value, kl=kl.value, grad_norm=norm.value, skipped=bool(skipped.value),
                 advantages=adv, coefficients=coef)
 

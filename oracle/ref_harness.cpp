@@ -24,6 +24,15 @@
 
 using namespace mini_mla;
 
+#ifdef MM_REF_EXECUTION_CUDA
+// Built a second time (libmini_mla_ref_cuda.so) with sessions on the sm_100a backend through
+// its reference-side adapter (cpp_inference_train_engine_b200/reference_adapter), so the
+// drivers below run the reference's own Execution-API sequences on the GPU.
+namespace mini_mla {
+Result<std::unique_ptr<Execution>> make_cuda_execution(Model&, Optimizer*, int device);
+}
+#endif
+
 namespace {
 thread_local std::string g_last_error;
 
@@ -103,7 +112,11 @@ void* ref_session_create(const int* cfg, float eps, float theta, std::uint64_t s
             return nullptr;
         }
     }
+#ifdef MM_REF_EXECUTION_CUDA
+    auto e = make_cuda_execution(*s->model, s->optimizer.get(), 0);
+#else
     auto e = make_execution(*s->model, s->optimizer.get(), "cpu", "fp32");
+#endif
     if (!e) {
         fail(e.error());
         delete s;
@@ -122,6 +135,8 @@ std::int64_t ref_session_param_count(void* h) {
 // which: 0 weights, 1 gradients, 2 first moments, 3 second moments. Registry order.
 int ref_session_read(void* h, int which, float* out) {
     auto* s = static_cast<Session*>(h);
+    if (auto st = s->execution->synchronize_to_host(); !st)  // device results to the host Model
+        return fail(st.error());
     std::size_t off = 0;
     for (std::size_t i = 0; i < s->model->parameters().size(); ++i) {
         const auto& p = s->model->parameters()[i];

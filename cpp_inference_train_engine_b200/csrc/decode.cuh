@@ -12,9 +12,20 @@ constexpr int kMaxDecodeSplits = 16;
 // Context splits of the latent decode attention (one warp per row and split): enough warps
 // for ~8 per SM when the batch alone does not provide them, at least 4 tiles of 16
 // positions per split.
+// Warps the split latent attention aims for per launch (MM_DECODE_TARGET_WARPS, for tuning).
+inline int decode_target_warps() {
+    static const int v = [] {
+        const char* e = std::getenv("MM_DECODE_TARGET_WARPS");
+        const int x = e ? std::atoi(e) : 0;
+        return x > 0 ? x : dec::kTargetWarps;
+    }();
+    return v;
+}
+
 inline int decode_splits(int B, int ctx) {
-    if (B >= dec::kTargetWarps) return 1;
-    const int want = (dec::kTargetWarps + B - 1) / B;
+    const int target = decode_target_warps();
+    if (B >= target) return 1;
+    const int want = (target + B - 1) / B;
     const int by_len = std::max(1, (ctx + 63) / 64);
     return std::max(1, std::min(std::min(want, by_len), kMaxDecodeSplits));
 }
@@ -61,7 +72,7 @@ inline void ensure_decode(Context& cx, int B, int Sc, int max_new) {
         d.draw = a.template take<int>(B);
         d.out_tok = a.template take<uint16_t>(static_cast<long long>(B) * std::max(max_new, 1));
         // flash-decoding partials (max, sum, O[kv_rank]) per split and head
-        d.part = a.template take<float>(B >= dec::kTargetWarps ? 1 : static_cast<long long>(B) * kMaxDecodeSplits * c.H * (c.kvr + 2));
+        d.part = a.template take<float>(B >= decode_target_warps() ? 1 : static_cast<long long>(B) * kMaxDecodeSplits * c.H * (c.kvr + 2));
         d.step = a.template take<int>(1);
     };
     d.drop_graph();

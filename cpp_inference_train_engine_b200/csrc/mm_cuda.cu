@@ -396,6 +396,17 @@ int mm_cuda_grpo_step(mm_cuda_ctx* policy, mm_cuda_ctx* reference, const uint16_
     });
 }
 
+int mm_cuda_dpo_step(mm_cuda_ctx* policy, mm_cuda_ctx* reference, const uint16_t* input, const uint16_t* target,
+                     const float* mask, int n, int seq, int64_t n_total, float beta, float lr, mm_step_result* out,
+                     double* margins) {
+    if (!reference) return MM_INVALID_ARGUMENT;
+    return guarded(policy, [&](mm::Context& cx) {
+        if (!input || !target || !mask || !out) mm::fail(MM_INVALID_ARGUMENT, "null DPO buffer");
+        if (reference->cx.unusable) mm::fail(MM_GPU_ERROR, "reference execution is unusable");
+        *out = mm::dpo_step(cx, reference->cx, input, target, mask, n, seq, n_total, beta, lr, margins);
+    });
+}
+
 int mm_cuda_nccl_unique_id(char out[128]) {
     try {
         ncclUniqueId id;

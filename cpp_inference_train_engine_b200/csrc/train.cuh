@@ -279,6 +279,76 @@ inline mm_step_result grpo_step(Context& pc, Context& rc, const uint16_t* input,
     return res;
 }
 
+// ------------------------------------------------------------------ DPO update
+// The DPO update (trainer.cpp:765-783 with preference_objective :107-121 and Execution::step)
+// over n preference pairs: rows 2p (chosen) and 2p + 1 (rejected) of the [2n][S] batch. Per
+// chunk of whole pairs: the frozen reference's log-probs, the policy's taped forward,
+// dpo_coef_kernel (coefficients over the n_total pairs of the update across ranks), the
+// backward; then the gradient all-reduce and AdamW. loss = sum of pair losses / n_total and
+// kl = sum of pair margins / n_total, both summed over ranks; margins (host [n], may be null)
+// receives each local pair's margin.
+inline mm_step_result dpo_step(Context& pc, Context& rc, const uint16_t* input, const uint16_t* target,
+                               const float* mask, int n, int S, long long n_total, float beta, float lr,
+                               double* margins) {
+    if (!pc.trainable) fail(MM_INVALID_ARGUMENT, "policy context must be trainable");
+    if (pc.device != rc.device) fail(MM_INVALID_ARGUMENT, "policy and reference must share a device");
+    if (n < 1 || S < 1 || S > pc.c.maxS || n_total < n) fail(MM_INVALID_ARGUMENT, "Invalid preference batch");
+    if (!std::isfinite(beta) || beta <= 0) fail(MM_INVALID_ARGUMENT, "Invalid DPO beta");
+    const long long NS = 2LL * n * S;
+    for (long long i = 0; i < NS; ++i) {
+        if (mask[i] != 0.f && mask[i] != 1.f) fail(MM_INVALID_ARGUMENT, "Loss mask must contain zero or one");
+        if (input[i] >= pc.c.V || target[i] >= pc.c.V) fail(MM_INVALID_ARGUMENT, "Input token exceeds vocabulary");
+    }
+    MM_CUDA_CHECK(cudaMemsetAsync(pc.g, 0, sizeof(float) * pc.P_dev, pc.stream));
+    MM_CUDA_CHECK(cudaMemsetAsync(pc.d_sums, 0, sizeof(GrpoSums), pc.stream));
+    double2* part = static_cast<double2*>(pc.sums_part.get(sizeof(double2) * static_cast<size_t>(n) +
+                                                            sizeof(double) * static_cast<size_t>(n)));
+    double* d_margins = reinterpret_cast<double*>(part + n);
+    const int per = std::max(1, chunk_tokens_default() / (2 * S));  // pairs per chunk
+    ensure_workspace(pc, 2 * std::min(n, per) * S, true);
+    ensure_workspace(rc, 2 * std::min(n, per) * S, rc.ws.tape);
+    Workspace& w = pc.ws;
+    for (int p0 = 0; p0 < n; p0 += per) {
+        const int bp = std::min(per, n - p0), rows = 2 * bp;
+        const long long T = static_cast<long long>(rows) * S, off = 2LL * p0 * S;
+        {
+            PhaseTimer t(pc, kPhLogprob);
+            MM_CUDA_CHECK(cudaMemcpyAsync(rc.ws.tokens, input + off, T * 2, cudaMemcpyHostToDevice, rc.stream));
+            MM_CUDA_CHECK(cudaMemcpyAsync(rc.ws.targets, target + off, T * 2, cudaMemcpyHostToDevice, rc.stream));
+            forward_chunk(rc, rows, S, false, kVocabAll, true, nullptr, 0, 0, nullptr);
+            MM_CUDA_CHECK(cudaMemcpyAsync(w.tokens, input + off, T * 2, cudaMemcpyHostToDevice, pc.stream));
+            MM_CUDA_CHECK(cudaMemcpyAsync(w.targets, target + off, T * 2, cudaMemcpyHostToDevice, pc.stream));
+            MM_CUDA_CHECK(cudaMemcpyAsync(w.mask, mask + off, T * 4, cudaMemcpyHostToDevice, pc.stream));
+            // the reference's log-probs reach the policy stream only after its forward completes
+            MM_CUDA_CHECK(cudaStreamSynchronize(rc.stream));
+            MM_CUDA_CHECK(cudaMemcpyAsync(w.ref_lp, rc.ws.lp, T * 4, cudaMemcpyDeviceToDevice, pc.stream));
+            forward_chunk(pc, rows, S, true, kVocabAll, true, nullptr, 0, 0, nullptr);
+        }
+        PhaseTimer t(pc, kPhBackward);
+        MM_LAUNCH_CX(pc, dpo_coef_kernel, bp, 256, 0, w.lp, w.ref_lp, w.mask, S, beta, static_cast<float>(n_total),
+                     static_cast<double>(n_total), w.coef, part + p0, d_margins + p0);
+        MM_CUDA_CHECK(cudaMemsetAsync(&pc.d_sums->max_coef_bits, 0, 4, pc.stream));
+        MM_LAUNCH_CX(pc, absmax_kernel, blocks_for(T, 256), 256, 0, w.coef, static_cast<int>(T),
+                     &pc.d_sums->max_coef_bits);
+        MM_LAUNCH_CX(pc, grad_scale_kernel, 1, 1, 0, pc.d_sums, pc.d_scale);
+        backward_chunk(pc, rows, S);
+    }
+    check_device(rc, "reference log_probabilities");
+    check_device(pc, "dpo backward");
+    MM_LAUNCH_CX(pc, grpo_sums_kernel, 1, 32, 0, part, n, pc.d_sums);
+    if (margins) MM_CUDA_CHECK(cudaMemcpyAsync(margins, d_margins, sizeof(double) * n, cudaMemcpyDeviceToHost, pc.stream));
+    allreduce(pc, pc.d_sums, 2, ncclFloat64, ncclSum);
+    GrpoSums sums{};
+    MM_CUDA_CHECK(cudaMemcpyAsync(&sums, pc.d_sums, sizeof(GrpoSums), cudaMemcpyDeviceToHost, pc.stream));
+    MM_CUDA_CHECK(cudaStreamSynchronize(pc.stream));
+    if (!std::isfinite(sums.loss)) fail(MM_NUMERICAL_ERROR, "Nonfinite logits or loss");
+    mm_step_result res{};
+    res.grad_norm = adamw_update(pc, lr);
+    res.loss = sums.loss;
+    res.kl = sums.kl / static_cast<double>(n_total);
+    return res;
+}
+
 __global__ void column_gather_kernel(const uint16_t* __restrict__ src, long long stride, int col, int B,
                                      uint16_t* __restrict__ dst) {
     MM_PDL_ENTRY();

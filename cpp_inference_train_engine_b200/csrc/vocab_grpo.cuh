@@ -170,6 +170,53 @@ __global__ void grpo_coef_kernel(const float* __restrict__ lp, const float* __re
     }
 }
 
+// DPO on a preference pair (trainer.cpp:107-121, 345-350, 765-783): rows 2p (chosen) and
+// 2p + 1 (rejected) of a chunk, S positions each. One block per pair: the masked sums of the
+// policy and reference log-probs in double (fixed-order block reduction), then
+// dpo_objective -- margin = (chosen - rejected) - (ref_chosen - ref_rejected), z = beta * margin,
+// loss = max(-z, 0) + log1p(exp(-|z|)), scale = beta * sigmoid(float(-z)) -- and the per-token
+// coefficients mask * (+-scale / pairs) (float, as the reference's coefficient loop).
+// part[p] = (loss / pairs, margin) for an ordered sum; the pair's margin also to margins[p].
+__global__ void dpo_coef_kernel(const float* __restrict__ lp, const float* __restrict__ ref_lp,
+                                const float* __restrict__ mask, int S, float beta, float pairs,
+                                double pairs_d, float* __restrict__ coef, double2* __restrict__ part,
+                                double* __restrict__ margins) {
+    MM_PDL_ENTRY();
+    __shared__ double red[4][32];
+    const int p = blockIdx.x;
+    const long long base = 2LL * p * S;
+    double a[4] = {0.0, 0.0, 0.0, 0.0};  // chosen, rejected, ref chosen, ref rejected
+    for (int t = threadIdx.x; t < 2 * S; t += blockDim.x) {
+        if (mask[base + t] == 0.f) continue;
+        const int r = t < S ? 0 : 1;
+        a[r] += static_cast<double>(lp[base + t]);
+        a[2 + r] += static_cast<double>(ref_lp[base + t]);
+    }
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        a[i] = warp_sum(a[i]);
+        if (lane == 0) red[i][warp] = a[i];
+    }
+    __syncthreads();
+    double sum[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        sum[i] = 0.0;
+        for (int w = 0; w < nw; ++w) sum[i] += red[i][w];
+    }
+    const double margin = (sum[0] - sum[1]) - (sum[2] - sum[3]);
+    const double z = static_cast<double>(beta) * margin;
+    const double loss = fmax(-z, 0.0) + log1p(exp(-fabs(z)));
+    const float scale = beta * sigmoid_ref(static_cast<float>(-z));
+    const float cc = scale / pairs, cr = -scale / pairs;
+    for (int t = threadIdx.x; t < 2 * S; t += blockDim.x) coef[base + t] = mask[base + t] * (t < S ? cc : cr);
+    if (threadIdx.x == 0) {
+        part[p] = make_double2(loss / pairs_d, margin);
+        if (margins) margins[p] = margin;
+    }
+}
+
 // Adds grpo_coef_kernel's per-block (loss, kl) partials into the sums in block order, so
 // the reported objective does not depend on the order in which blocks finish.
 __global__ void grpo_sums_kernel(const double2* __restrict__ part, int nblocks, GrpoSums* __restrict__ sums) {

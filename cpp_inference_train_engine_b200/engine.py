@@ -110,6 +110,9 @@ def lib():
                                              ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                              ctypes.c_int64, ctypes.c_float, ctypes.c_float,
                                              ctypes.c_float, ctypes.POINTER(StepResult)]),
+        "mm_cuda_dpo_step": (ctypes.c_int, [_vp, _vp, _u16p, _u16p, _f32p, ctypes.c_int, ctypes.c_int,
+                                            ctypes.c_int64, ctypes.c_float, ctypes.c_float,
+                                            ctypes.POINTER(StepResult), ctypes.POINTER(ctypes.c_double)]),
         "mm_cuda_nccl_unique_id": (ctypes.c_int, [ctypes.c_char_p]),
         "mm_cuda_init_comm": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, ctypes.c_char_p]),
         "mm_cuda_kernel_launches": (ctypes.c_int64, [_vp]),
@@ -377,6 +380,25 @@ class CudaExecution:
                                             ctypes.byref(res)))
         return {"loss": res.loss, "kl": res.kl, "grad_norm": res.grad_norm,
                 "skipped": bool(res.skipped)}
+
+    def dpo_step(self, reference: "CudaExecution", inp, tgt, mask, beta=0.1, n_total=None,
+                 learning_rate=1e-5):
+        """One DPO update (mm_cuda_dpo_step) over preference pairs: rows 2p (chosen) and 2p + 1
+        (rejected) of [2n, seq] arrays. Returns loss, mean margin, pre-clip gradient norm and the
+        per-pair margins."""
+        i = np.ascontiguousarray(inp, np.uint16)
+        t = np.ascontiguousarray(tgt, np.uint16)
+        m = np.ascontiguousarray(mask, np.float32)
+        rows, seq = i.shape
+        if rows % 2 or t.shape != i.shape or m.shape != i.shape:
+            raise EngineError(1, "preference pairs need [2n, seq] input, target and mask")
+        n = rows // 2
+        res = StepResult()
+        margins = np.empty(n, np.float64)
+        self._check(lib().mm_cuda_dpo_step(self.h, reference.h, _p(i, _u16p), _p(t, _u16p), _p(m, _f32p), n,
+                                           seq, n_total or n, beta, learning_rate, ctypes.byref(res),
+                                           margins.ctypes.data_as(ctypes.POINTER(ctypes.c_double))))
+        return {"loss": res.loss, "margin": res.kl, "grad_norm": res.grad_norm, "margins": margins}
 
     # ------------------------------------------------------------------ data parallel
     @staticmethod

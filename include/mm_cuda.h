@@ -179,6 +179,18 @@ int mm_cuda_grpo_step(mm_cuda_ctx* policy, mm_cuda_ctx* reference, const uint16_
                       float clip, float kl_coefficient, float learning_rate,
                       mm_step_result* out);
 
+/* One DPO update (trainer.cpp:765-783: preference_objective :107-121 and dpo_objective
+ * :345-350 per pair, then Execution::step) over n local preference pairs: rows 2p (chosen)
+ * and 2p + 1 (rejected) of input/target/mask [2n][seq] (completion_batch layout, mask 1 on
+ * completion tokens). The frozen reference forward on `reference`, the policy forward, the
+ * per-pair objective and signed coefficients (+-scale / n_total), the backward, the gradient
+ * all-reduce and AdamW at learning_rate. out->loss = sum of pair losses / n_total,
+ * out->kl = mean margin over the n_total pairs, out->grad_norm = pre-clip norm. margins
+ * (host [n], may be NULL) receives each local pair's margin. n_total = pairs over all ranks. */
+int mm_cuda_dpo_step(mm_cuda_ctx* policy, mm_cuda_ctx* reference, const uint16_t* input,
+                     const uint16_t* target, const float* mask, int n, int seq, int64_t n_total,
+                     float beta, float learning_rate, mm_step_result* out, double* margins);
+
 /* ---------------------------------------------------------------- data parallel */
 
 /* NCCL bootstrap: rank 0 creates the id (128 bytes), every rank attaches with it. The

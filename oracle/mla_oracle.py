@@ -401,6 +401,46 @@ def grpo_objective(lp, old, ref, adv, clip, klc):
     return obj, kl, coef
 
 
+# ---------------------------------------------------------------- DPO (trainer.cpp)
+def dpo_objective(chosen, rejected, ref_chosen, ref_rejected, beta):
+    """dpo_objective (src/train/trainer.cpp:345-350): (loss, margin, chosen and rejected
+    float32 coefficients); the loss is the stable softplus of -beta * margin in double."""
+    margin = (chosen - rejected) - (ref_chosen - ref_rejected)
+    z = float(F32(beta)) * margin
+    loss = max(-z, 0.0) + math.log1p(math.exp(-abs(z)))
+    scale = F32(beta) * _sigmoid_scalar(-z)
+    return loss, margin, float(scale), float(-scale)
+
+
+def _sigmoid_scalar(x):
+    """ops::sigmoid (src/model/ops.cpp:65-70) on one float, with the float exponential
+    taken as the correctly rounded value of the double one."""
+    x = float(F32(x))
+    if x >= 0:
+        return F32(1) / (F32(1) + F32(math.exp(-x)))
+    e = F32(math.exp(x))
+    return e / (F32(1) + e)
+
+
+def dpo_coefficients(lp, ref_lp, mask, beta):
+    """The DPO coefficient loop (trainer.cpp:765-783 with preference_objective :107-121) over
+    pairs [2n, S] (rows 2p chosen, 2p + 1 rejected): (loss, margins, float32 coefficients)."""
+    n = lp.shape[0] // 2
+    coef = np.zeros_like(mask, dtype=F32)
+    loss, margins = 0.0, []
+    for p in range(n):
+        c, r = 2 * p, 2 * p + 1
+        sums = [float(np.sum(lp[c][mask[c] != 0], dtype=np.float64)), float(np.sum(lp[r][mask[r] != 0], dtype=np.float64)),
+                float(np.sum(ref_lp[c][mask[c] != 0], dtype=np.float64)),
+                float(np.sum(ref_lp[r][mask[r] != 0], dtype=np.float64))]
+        lo, margin, cc, cr = dpo_objective(sums[0], sums[1], sums[2], sums[3], beta)
+        loss += lo / n
+        margins.append(margin)
+        coef[c] = mask[c] * (F32(cc) / F32(n))
+        coef[r] = mask[r] * (F32(cr) / F32(n))
+    return loss, np.array(margins), coef
+
+
 def group_advantages(rewards, eps=1e-6):
     """group_advantages (src/train/trainer.cpp:371-385): population std in double."""
     r = [float(F32(x)) for x in rewards]

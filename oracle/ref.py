@@ -80,6 +80,9 @@ def lib(backend: str = "cpu"):
         L.ref_rollout.argtypes = [ctypes.c_void_p, _u16p, ctypes.c_int, ctypes.c_int,
                                   ctypes.c_int, ctypes.c_uint16, ctypes.c_uint16, ctypes.c_uint64,
                                   ctypes.c_float, _u16p, _i32p, _u16p, _u16p, _f32p, _f32p]
+        L.ref_dpo_objective.argtypes = [ctypes.c_double] * 4 + [ctypes.c_float, _f64p, _f64p, _f32p, _f32p]
+        L.ref_dpo_update.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, _u16p, _u16p,
+                                     _f32p, ctypes.c_float, ctypes.c_float, _f64p, _f64p, _f64p]
         L.ref_grpo_update.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
                                       ctypes.c_int, ctypes.c_int, _u16p, _u16p, _f32p, _f32p,
                                       _f32p, ctypes.c_float, ctypes.c_float, ctypes.c_float,
@@ -310,3 +313,28 @@ class Rng:
 
     def normal(self):
         return float(lib().ref_rng_normal(ctypes.byref(self.state)))
+
+
+def dpo_objective(chosen, rejected, ref_chosen, ref_rejected, beta):
+    """dpo_objective (src/train/trainer.cpp:345-350): (loss, margin, chosen, rejected coefficients)."""
+    loss, margin = ctypes.c_double(), ctypes.c_double()
+    cc, cr = ctypes.c_float(), ctypes.c_float()
+    _check(lib().ref_dpo_objective(chosen, rejected, ref_chosen, ref_rejected, beta, ctypes.byref(loss),
+                                   ctypes.byref(margin), ctypes.byref(cc), ctypes.byref(cr)))
+    return loss.value, margin.value, cc.value, cr.value
+
+
+def dpo_update(policy: Session, reference: Session, inp, tgt, mask, beta, lr):
+    """DPO update body of src/train/trainer.cpp:765-783 (restated over the public API); pair p is
+    rows 2p (chosen) and 2p + 1 (rejected) of [2n, seq] arrays."""
+    rows, seq = inp.shape
+    n = rows // 2
+    i = np.ascontiguousarray(inp, np.uint16)
+    t = np.ascontiguousarray(tgt, np.uint16)
+    m = np.ascontiguousarray(mask, np.float32)
+    loss, norm = ctypes.c_double(), ctypes.c_double()
+    margins = np.zeros(n, np.float64)
+    _check(policy.L.ref_dpo_update(policy.h, reference.h, n, seq, _p(i, _u16p), _p(t, _u16p), _p(m, _f32p),
+                                   beta, lr, ctypes.byref(loss), ctypes.byref(norm), _p(margins, _f64p)),
+           policy.L)
+    return dict(loss=loss.value, grad_norm=norm.value, margins=margins)

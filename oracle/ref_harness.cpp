@@ -6,10 +6,11 @@
 // Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg load it, as the
 // checker and as the timed CPU baseline.
 //
-// Two functions restate file-local reference code that is not reachable through a
+// Three functions restate file-local reference code that is not reachable through a
 // public symbol:
-//   * ref_rollout   <- rollout()             src/train/trainer.cpp:187-213
+//   * ref_rollout     <- rollout()             src/train/trainer.cpp:187-213
 //   * ref_grpo_update <- the GRPO update body src/train/trainer.cpp:814-847 + 848-883
+//   * ref_dpo_update  <- the DPO update body  src/train/trainer.cpp:765-783 (+ :107-121)
 // Both call only the reference's public API, step for step as those lines do.
 #include "mini_mla/execution.hpp"
 #include "mini_mla/inference.hpp"
@@ -477,6 +478,73 @@ int ref_grpo_update(void* policy, void* reference, int n_rollouts, int group_siz
     }
     for (std::size_t i = 0; i < coefficients.size(); ++i)
         std::memcpy(out_coefficients + i * S, coefficients[i].data(), S * 4);
+    std::vector<GradientBatch> jobs;
+    for (std::size_t i = 0; i < batches.size(); ++i)
+        jobs.push_back({&batches[i], coefficients[i]});
+    auto r = ps->execution->step(jobs, lr);
+    if (!r)
+        return fail(r.error());
+    *grad_norm = r.value().gradient_norm;
+    return 0;
+}
+
+// dpo_objective (src/train/trainer.cpp:345-350).
+int ref_dpo_objective(double chosen, double rejected, double ref_chosen, double ref_rejected, float beta,
+                      double* loss, double* margin, float* chosen_coef, float* rejected_coef) {
+    auto o = dpo_objective(chosen, rejected, ref_chosen, ref_rejected, beta);
+    *loss = o.loss;
+    *margin = o.margin;
+    *chosen_coef = o.chosen_nll_coefficient;
+    *rejected_coef = o.rejected_nll_coefficient;
+    return 0;
+}
+
+// The DPO update body restated from src/train/trainer.cpp:765-783 over the public API:
+// per pair preference_objective (:107-121: both executions' log-probabilities, masked sums in
+// double, dpo_objective), loss += objective.loss / pairs, coefficients = mask * (+-scale) /
+// pairs; then Execution::step (:848-883). Pair p is rows 2p (chosen) and 2p + 1 (rejected)
+// of the flat [2 n_pairs][sequence] arrays. margins receives each pair's margin.
+int ref_dpo_update(void* policy, void* reference, int n_pairs, int sequence, const std::uint16_t* input,
+                   const std::uint16_t* target, const float* mask, float beta, float lr, double* loss,
+                   double* grad_norm, double* margins) {
+    auto* ps = static_cast<Session*>(policy);
+    auto* rs = static_cast<Session*>(reference);
+    if (n_pairs < 1)
+        return fail_msg("no preference pairs");
+    auto S = static_cast<std::size_t>(sequence);
+    std::vector<Batch> batches;
+    std::vector<std::vector<float>> coefficients;
+    *loss = 0;
+    for (int p = 0; p < n_pairs; ++p) {
+        const std::size_t off = 2 * static_cast<std::size_t>(p) * S;
+        auto b = make_batch(input + off, target + off, mask + off, 2, sequence);
+        auto pl = ps->execution->log_probabilities(b);
+        if (!pl)
+            return fail(pl.error());
+        auto rl = rs->execution->log_probabilities(b);
+        if (!rl)
+            return fail(rl.error());
+        double chosen = 0, rejected = 0, ref_chosen = 0, ref_rejected = 0;
+        for (std::size_t t = 0; t < b.target.size(); ++t)
+            if (b.mask[t] != 0) {
+                if (t < S) {
+                    chosen += pl.value()[t];
+                    ref_chosen += rl.value()[t];
+                } else {
+                    rejected += pl.value()[t];
+                    ref_rejected += rl.value()[t];
+                }
+            }
+        auto objective = dpo_objective(chosen, rejected, ref_chosen, ref_rejected, beta);
+        *loss += objective.loss / n_pairs;
+        margins[p] = objective.margin;
+        auto c = b.mask;
+        for (std::size_t t = 0; t < c.size(); ++t)
+            c[t] *= (t < S ? objective.chosen_nll_coefficient : objective.rejected_nll_coefficient) /
+                    static_cast<float>(n_pairs);
+        batches.push_back(std::move(b));
+        coefficients.push_back(std::move(c));
+    }
     std::vector<GradientBatch> jobs;
     for (std::size_t i = 0; i < batches.size(); ++i)
         jobs.push_back({&batches[i], coefficients[i]});

@@ -217,3 +217,43 @@ def test_tiny_grpo_update_matches_reference():
     loss, kl, coef = O.grpo_coefficients(lp, old, lp, mask, adv, 0.2, 0.04)
     assert abs(loss - out["loss"]) < 1e-5 and abs(kl - out["kl"]) < 1e-6
     assert np.abs(coef - out["coefficients"]).max() < 1e-6
+
+
+@needs_ref
+def test_dpo_objective_matches_reference():
+    rng = np.random.default_rng(4)
+    for k in range(300):
+        c, r, rc, rr = rng.normal(-40, 15, 4)
+        beta = [0.1, 0.5, 2.0][k % 3]
+        if k % 10 == 0:  # large margins exercise the stable softplus branches
+            c += 400 * (1 if k % 20 else -1)
+        want = ref.dpo_objective(c, r, rc, rr, beta)
+        got = O.dpo_objective(c, r, rc, rr, beta)
+        assert got[0] == pytest.approx(want[0], rel=1e-12, abs=1e-300)
+        assert got[1] == want[1]
+        assert np.float32(got[2]) == np.float32(want[2]) and np.float32(got[3]) == np.float32(want[3])
+
+
+@needs_ref
+def test_tiny_dpo_update_matches_reference():
+    """Preference pairs through the reference's DPO update body (restated over its public API)
+    against the numpy restatement's objective and coefficients on the same log-probs."""
+    cfg = TINY
+    opt = [0.9, 0.95, 1e-8, 0.1, 1.0]
+    pol = ref.Session(cfg, 0, optimizer=opt)
+    refm = ref.Session(cfg, 1)
+    rng = np.random.default_rng(8)
+    n, S = 3, 32
+    inp = rng.integers(0, 256, (2 * n, S)).astype(np.uint16)
+    tgt = rng.integers(0, 256, (2 * n, S)).astype(np.uint16)
+    mask = np.zeros((2 * n, S), np.float32)
+    for row in range(2 * n):
+        mask[row, 10:10 + 4 + 3 * row] = 1
+    ones = np.ones((2 * n, S), np.float32)
+    lp = pol.log_probs(inp, tgt, ones, 2 * n, S).reshape(2 * n, S)
+    rl = refm.log_probs(inp, tgt, ones, 2 * n, S).reshape(2 * n, S)
+    loss, margins, _ = O.dpo_coefficients(lp, rl, mask, 0.1)
+    out = ref.dpo_update(pol, refm, inp, tgt, mask, 0.1, 1e-3)
+    assert abs(out["loss"] - loss) < 1e-12 * max(1.0, abs(loss))
+    np.testing.assert_allclose(out["margins"], margins, rtol=0, atol=1e-9)
+    assert pol.steps == 1

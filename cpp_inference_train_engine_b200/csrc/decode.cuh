@@ -74,6 +74,7 @@ inline void ensure_decode(Context& cx, int B, int Sc, int max_new) {
         // flash-decoding partials (max, sum, O[kv_rank]) per split and head
         d.part = a.template take<float>(B >= decode_target_warps() ? 1 : static_cast<long long>(B) * kMaxDecodeSplits * c.H * (c.kvr + 2));
         d.step = a.template take<int>(1);
+        d.active = a.template take<int>(B);
     };
     d.drop_graph();
     d.B = B;
@@ -101,6 +102,18 @@ inline void prefill_rows(Context& cx, const uint16_t* d_prompts, int B, int P, i
     }
     std::vector<int> pos(B, P);
     MM_CUDA_CHECK(cudaMemcpyAsync(d.pos, pos.data(), sizeof(int) * B, cudaMemcpyHostToDevice, cx.stream));
+}
+
+// Serving: free slots decode a dummy token at position 0 of their own cache row, so their
+// positions never run past the row (the step advances every row).
+__global__ void serve_prepare_kernel(int* __restrict__ pos, uint16_t* __restrict__ tok, const int* __restrict__ active,
+                                     int B) {
+    MM_PDL_ENTRY();
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b < B && !active[b]) {
+        pos[b] = 0;
+        tok[b] = 0;
+    }
 }
 
 __global__ void advance_pos_kernel(int* pos, int B) {

@@ -277,6 +277,7 @@ int mm_cuda_prefill_batch(mm_cuda_ctx* h, const uint16_t* prompts, int batch, in
             mm::fail(MM_INVALID_ARGUMENT, "Prompt exceeds context or is empty");
         check_tokens(cx, prompts, static_cast<long long>(batch) * prompt_len);
         mm::ensure_decode(cx, batch, cx.c.maxS, 1);
+        cx.serving = false;  // the decode state now holds this batch
         uint16_t* d = static_cast<uint16_t*>(cx.stage.get(static_cast<size_t>(batch) * prompt_len * 2));
         MM_CUDA_CHECK(cudaMemcpyAsync(d, prompts, static_cast<size_t>(batch) * prompt_len * 2, cudaMemcpyHostToDevice, cx.stream));
         mm::prefill_rows(cx, d, batch, prompt_len, mm::chunk_tokens_default());
@@ -299,6 +300,99 @@ int mm_cuda_decode_batch(mm_cuda_ctx* h, const uint16_t* tokens, int batch, floa
             MM_CUDA_CHECK(cudaMemcpyAsync(logits, cx.dec.logits, sizeof(float) * batch * cx.c.V, cudaMemcpyDeviceToHost, cx.stream));
         cx.dec_len += 1;
         mm::check_device(cx, "decode");
+    });
+}
+
+int mm_cuda_serve_open(mm_cuda_ctx* h, int slots, int max_context) {
+    return guarded(h, [&](mm::Context& cx) {
+        if (slots < 1 || max_context < 2 || max_context > cx.c.maxS)
+            mm::fail(MM_INVALID_ARGUMENT, "Invalid serving slots or context");
+        mm::ensure_decode(cx, slots, max_context, 1);
+        MM_CUDA_CHECK(cudaMemsetAsync(cx.dec.pos, 0, sizeof(int) * slots, cx.stream));
+        cx.serve_pos.assign(static_cast<size_t>(slots), -1);
+        cx.serving = true;
+        cx.dec_len = 1;
+        mm::check_device(cx, "serve_open");
+    });
+}
+
+int mm_cuda_serve_admit(mm_cuda_ctx* h, int slot, const uint16_t* prompt, int len, int max_new, float temperature,
+                        uint64_t seed, uint16_t* first, float* logits) {
+    return guarded(h, [&](mm::Context& cx) {
+        mm::DecodeState& d = cx.dec;
+        if (!cx.serving) mm::fail(MM_INVALID_ARGUMENT, "No serving session");
+        if (slot < 0 || slot >= d.B || cx.serve_pos[slot] >= 0) mm::fail(MM_INVALID_ARGUMENT, "Slot is not free");
+        if (!prompt || !first || len < 1 || max_new < 1 || len + max_new > cx.c.maxS || len + max_new - 1 > d.Sc)
+            mm::fail(MM_INVALID_ARGUMENT, "Prompt plus requested tokens exceeds context");
+        if (!std::isfinite(temperature) || temperature < 0) mm::fail(MM_INVALID_ARGUMENT, "Invalid generation settings");
+        check_tokens(cx, prompt, len);
+        char* base = static_cast<char*>(cx.stage.get(mm::round_up(len * 2LL, 256) + 256));
+        uint16_t* d_prompt = reinterpret_cast<uint16_t*>(base);
+        uint64_t* d_seed = reinterpret_cast<uint64_t*>(base + mm::round_up(len * 2LL, 256));
+        int* d_draw = reinterpret_cast<int*>(d_seed + 1);
+        int* d_len = d_draw + 1;
+        uint16_t* d_first = reinterpret_cast<uint16_t*>(d_len + 1);
+        const int zero = 0;
+        MM_CUDA_CHECK(cudaMemcpyAsync(d_prompt, prompt, len * 2LL, cudaMemcpyHostToDevice, cx.stream));
+        MM_CUDA_CHECK(cudaMemcpyAsync(d_seed, &seed, 8, cudaMemcpyHostToDevice, cx.stream));
+        MM_CUDA_CHECK(cudaMemcpyAsync(d_draw, &zero, 4, cudaMemcpyHostToDevice, cx.stream));
+        MM_CUDA_CHECK(cudaMemcpyAsync(d_len, &len, 4, cudaMemcpyHostToDevice, cx.stream));
+        // the prompt's cache rows of this slot only, and its last-position logits
+        mm::ensure_workspace(cx, len, cx.ws.tape);
+        MM_CUDA_CHECK(cudaMemcpyAsync(cx.ws.tokens, d_prompt, len * 2LL, cudaMemcpyDeviceToDevice, cx.stream));
+        float* row_logits = d.logits + static_cast<long long>(slot) * cx.c.V;
+        mm::forward_chunk(cx, 1, len, false, mm::kVocabLast, false, d.cache, d.Sc, slot, row_logits);
+        MM_CUDA_CHECK(cudaMemcpyAsync(d.pos + slot, d_len, 4, cudaMemcpyDeviceToDevice, cx.stream));
+        // first token: draw 0 of Rng(seed) (generate_tokens, inference.cpp:469-579)
+        mm::launch_sample(cx, row_logits, 1, temperature, d_seed, d_draw, 0, nullptr, d_first, 1);
+        MM_CUDA_CHECK(cudaMemcpyAsync(first, d_first, 2, cudaMemcpyDeviceToHost, cx.stream));
+        if (logits)
+            MM_CUDA_CHECK(cudaMemcpyAsync(logits, row_logits, sizeof(float) * cx.c.V, cudaMemcpyDeviceToHost, cx.stream));
+        mm::check_device(cx, "serve_admit");
+        cx.serve_pos[slot] = len;
+    });
+}
+
+int mm_cuda_serve_step(mm_cuda_ctx* h, const uint16_t* tokens, const int32_t* active, float temperature,
+                       const uint64_t* seeds, const int32_t* draw_index, uint16_t* next, float* logits) {
+    return guarded(h, [&](mm::Context& cx) {
+        mm::DecodeState& d = cx.dec;
+        if (!cx.serving) mm::fail(MM_INVALID_ARGUMENT, "No serving session");
+        if (!tokens || !active || !seeds || !draw_index || !next) mm::fail(MM_INVALID_ARGUMENT, "null serving buffer");
+        if (!std::isfinite(temperature) || temperature < 0) mm::fail(MM_INVALID_ARGUMENT, "Invalid generation settings");
+        const int B = d.B;
+        int longest = 1;
+        for (int b = 0; b < B; ++b) {
+            if (!active[b]) continue;
+            if (cx.serve_pos[b] < 1) mm::fail(MM_INVALID_ARGUMENT, "Active slot holds no request");
+            if (cx.serve_pos[b] >= d.Sc || cx.serve_pos[b] >= cx.c.maxS)
+                mm::fail(MM_INVALID_ARGUMENT, "Decode requires available context");
+            if (tokens[b] >= cx.c.V) mm::fail(MM_INVALID_ARGUMENT, "Input token exceeds vocabulary");
+            longest = std::max(longest, cx.serve_pos[b] + 1);
+        }
+        std::vector<int> act(static_cast<size_t>(B));
+        for (int b = 0; b < B; ++b) act[b] = active[b] ? 1 : 0;
+        MM_CUDA_CHECK(cudaMemcpyAsync(d.tok, tokens, sizeof(uint16_t) * B, cudaMemcpyHostToDevice, cx.stream));
+        MM_CUDA_CHECK(cudaMemcpyAsync(d.active, act.data(), sizeof(int) * B, cudaMemcpyHostToDevice, cx.stream));
+        MM_CUDA_CHECK(cudaMemcpyAsync(d.seeds, seeds, sizeof(uint64_t) * B, cudaMemcpyHostToDevice, cx.stream));
+        MM_CUDA_CHECK(cudaMemcpyAsync(d.draw, draw_index, sizeof(int) * B, cudaMemcpyHostToDevice, cx.stream));
+        MM_LAUNCH(mm::serve_prepare_kernel, mm::blocks_for(B, 256), 256, 0, d.pos, d.tok, d.active, B);
+        cx.dec_len = longest - 1;  // cache entries before this step's write (the split heuristic)
+        mm::decode_step(cx);
+        mm::launch_sample(cx, d.logits, B, temperature, d.seeds, d.draw, 0, d.active, d.out_tok, 1);
+        MM_CUDA_CHECK(cudaMemcpyAsync(next, d.out_tok, sizeof(uint16_t) * B, cudaMemcpyDeviceToHost, cx.stream));
+        if (logits)
+            MM_CUDA_CHECK(cudaMemcpyAsync(logits, d.logits, sizeof(float) * B * cx.c.V, cudaMemcpyDeviceToHost, cx.stream));
+        mm::check_device(cx, "serve_step");
+        for (int b = 0; b < B; ++b)
+            if (act[b]) cx.serve_pos[b] += 1;
+    });
+}
+
+int mm_cuda_serve_release(mm_cuda_ctx* h, int slot) {
+    return guarded(h, [&](mm::Context& cx) {
+        if (!cx.serving || slot < 0 || slot >= cx.dec.B) mm::fail(MM_INVALID_ARGUMENT, "No such serving slot");
+        cx.serve_pos[slot] = -1;
     });
 }
 

@@ -191,6 +191,7 @@ struct DecodeState {
     uint16_t* out_tok;        // [B][max_new]
     float* part;              // [B][splits][H][kv_rank + 2] decode-attention partials
     int* step;                // device step counter of the rollout loop
+    int* active;              // [B] serving: 1 for slots holding a request
     int max_new = 0;
     Arena arena;
     // one captured rollout decode step (decode_sample_step), valid for the buffers above
@@ -290,6 +291,10 @@ class Context {
     Staging sums_part;  // per-block GRPO loss/kl partials (double2)
     DecodeState dec;
     int dec_len = 0;  // positions filled in the decode session (0: no session)
+    // continuous-batching serving session over dec (mm_cuda_serve_*): next position of
+    // each slot on the host, -1 for a free slot
+    bool serving = false;
+    std::vector<int> serve_pos;
 
     // NCCL
     void* nccl_comm = nullptr;

@@ -370,6 +370,7 @@ inline void rollout(Context& cx, const uint16_t* prompts, int n, int P, int comp
         if (prompts[i] >= c.V) fail(MM_INVALID_ARGUMENT, "Input token exceeds vocabulary");
     const int Sc = P + length - 1;
     ensure_decode(cx, n, Sc, completion);
+    cx.serving = false;  // the decode state now holds the rollout batch
     DecodeState& d = cx.dec;
     uint16_t* d_prompts = static_cast<uint16_t*>(cx.stage.get(static_cast<size_t>(n) * P * 2));
     MM_CUDA_CHECK(cudaMemcpyAsync(d_prompts, prompts, static_cast<size_t>(n) * P * 2, cudaMemcpyHostToDevice, cx.stream));

@@ -113,6 +113,11 @@ def lib():
         "mm_cuda_dpo_step": (ctypes.c_int, [_vp, _vp, _u16p, _u16p, _f32p, ctypes.c_int, ctypes.c_int,
                                             ctypes.c_int64, ctypes.c_float, ctypes.c_float,
                                             ctypes.POINTER(StepResult), ctypes.POINTER(ctypes.c_double)]),
+        "mm_cuda_serve_open": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int]),
+        "mm_cuda_serve_admit": (ctypes.c_int, [_vp, ctypes.c_int, _u16p, ctypes.c_int, ctypes.c_int,
+                                               ctypes.c_float, ctypes.c_uint64, _u16p, _f32p]),
+        "mm_cuda_serve_step": (ctypes.c_int, [_vp, _u16p, _i32p, ctypes.c_float, _u64p, _i32p, _u16p, _f32p]),
+        "mm_cuda_serve_release": (ctypes.c_int, [_vp, ctypes.c_int]),
         "mm_cuda_nccl_unique_id": (ctypes.c_int, [ctypes.c_char_p]),
         "mm_cuda_init_comm": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, ctypes.c_char_p]),
         "mm_cuda_kernel_launches": (ctypes.c_int64, [_vp]),
@@ -399,6 +404,35 @@ class CudaExecution:
                                            seq, n_total or n, beta, learning_rate, ctypes.byref(res),
                                            margins.ctypes.data_as(ctypes.POINTER(ctypes.c_double))))
         return {"loss": res.loss, "margin": res.kl, "grad_norm": res.grad_norm, "margins": margins}
+
+    # ------------------------------------------------------------------ serving
+    def serve_open(self, slots: int, max_context: int):
+        """Opens a continuous-batching session of `slots` requests (mm_cuda_serve_open)."""
+        self._check(lib().mm_cuda_serve_open(self.h, slots, max_context))
+
+    def serve_admit(self, slot, prompt, max_new, temperature=0.0, seed=0, with_logits=False):
+        """Prefills `prompt` into `slot`; returns the first token (and its logits)."""
+        p = np.ascontiguousarray(prompt, np.uint16).reshape(-1)
+        first = np.zeros(1, np.uint16)
+        lg = np.empty(self.cfg.vocab_size, np.float32) if with_logits else None
+        self._check(lib().mm_cuda_serve_admit(self.h, slot, _p(p, _u16p), p.size, max_new, temperature,
+                                              int(seed), _p(first, _u16p), _p(lg, _f32p)))
+        return (int(first[0]), lg) if with_logits else int(first[0])
+
+    def serve_step(self, tokens, active, temperature, seeds, draw_index, with_logits=False):
+        """One decode step of the active slots; returns the next token of every slot."""
+        t = np.ascontiguousarray(tokens, np.uint16)
+        a = np.ascontiguousarray(active, np.int32)
+        s = np.ascontiguousarray(seeds, np.uint64)
+        d = np.ascontiguousarray(draw_index, np.int32)
+        nxt = np.zeros(t.size, np.uint16)
+        lg = np.empty((t.size, self.cfg.vocab_size), np.float32) if with_logits else None
+        self._check(lib().mm_cuda_serve_step(self.h, _p(t, _u16p), _p(a, _i32p), temperature, _p(s, _u64p),
+                                             _p(d, _i32p), _p(nxt, _u16p), _p(lg, _f32p)))
+        return (nxt, lg) if with_logits else nxt
+
+    def serve_release(self, slot: int):
+        self._check(lib().mm_cuda_serve_release(self.h, slot))
 
     # ------------------------------------------------------------------ data parallel
     @staticmethod

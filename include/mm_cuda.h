@@ -135,6 +135,28 @@ int mm_cuda_prefill_batch(mm_cuda_ctx* ctx, const uint16_t* prompts, int batch, 
  * row's next position and returns logits [batch][vocab] (may be NULL). */
 int mm_cuda_decode_batch(mm_cuda_ctx* ctx, const uint16_t* tokens, int batch, float* logits);
 
+/* ---------------------------------------------------------------- serving (continuous batching) */
+
+/* InferenceEngine::generate_tokens (inference.cpp:469-579) for many requests at once: `slots`
+ * independent latent-cache rows of max_context positions, each holding one request between
+ * admit and release; requests join and leave while the others keep decoding. Opening a
+ * session replaces the batched decode/rollout state (and a later prefill_batch or rollout
+ * replaces the session). */
+int mm_cuda_serve_open(mm_cuda_ctx* ctx, int slots, int max_context);
+/* Prefills `prompt` into a free slot (that slot's cache rows only) and samples the request's
+ * first token, draw 0 of Rng(seed) at `temperature` (0 = greedy), into *first; logits (may be
+ * NULL) receives the last prompt position's logits [vocab]. len + max_new must fit the
+ * model's context and the session's. */
+int mm_cuda_serve_admit(mm_cuda_ctx* ctx, int slot, const uint16_t* prompt, int len, int max_new,
+                        float temperature, uint64_t seed, uint16_t* first, float* logits);
+/* One decode step of every active slot (active[s] != 0): appends tokens[s] at the slot's next
+ * position and samples next[s] with draw draw_index[s] of Rng(seeds[s]); logits (may be NULL)
+ * receives [slots][vocab]. Inactive slots are left as they are. */
+int mm_cuda_serve_step(mm_cuda_ctx* ctx, const uint16_t* tokens, const int32_t* active, float temperature,
+                       const uint64_t* seeds, const int32_t* draw_index, uint16_t* next, float* logits);
+/* Frees a slot for the next request. */
+int mm_cuda_serve_release(mm_cuda_ctx* ctx, int slot);
+
 /* sample_token with top_p = 1, top_k = 0, repetition penalty 1, no bans
  * (inference.cpp:345-426) on host logits [batch][vocab]: row b uses draw `draw_index[b]`
  * of Rng(seeds[b]) (temperature 0 = greedy, no draw). */

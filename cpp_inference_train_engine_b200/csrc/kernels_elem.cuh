@@ -181,8 +181,13 @@ __global__ void swiglu_kernel(const __half* __restrict__ gate, const __half* __r
 }
 
 // SwiGLU backward (ops.cpp:78-87) to fp16 dgate/dup.
+__device__ __forceinline__ float to_float(float v) { return v; }
+__device__ __forceinline__ float to_float(__half v) { return __half2float(v); }
+
+// dy in fp32 or fp16 (the scaled backward carries it in fp16)
+template <class DY>
 __global__ void swiglu_backward_kernel(const __half* __restrict__ gate, const __half* __restrict__ up,
-                                       long long ld, const float* __restrict__ dy, long long lddy,
+                                       long long ld, const DY* __restrict__ dy, long long lddy,
                                        int T, int n, __half* __restrict__ dg, __half* __restrict__ du,
                                        long long ldo) {
     MM_PDL_ENTRY();
@@ -190,7 +195,7 @@ __global__ void swiglu_backward_kernel(const __half* __restrict__ gate, const __
     if (idx >= static_cast<long long>(T) * n) return;
     const int t = static_cast<int>(idx / n), j = static_cast<int>(idx % n);
     const float x = __half2float(gate[t * ld + j]), u = __half2float(up[t * ld + j]);
-    const float g = dy[t * lddy + j];
+    const float g = to_float(dy[t * lddy + j]);
     const float s = sigmoid_ref(x);
     dg[t * ldo + j] = __float2half_rn(g * u * (s + x * s * (1.f - s)));
     du[t * ldo + j] = __float2half_rn(g * x * s);

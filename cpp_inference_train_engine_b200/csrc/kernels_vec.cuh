@@ -212,6 +212,29 @@ __global__ void swiglu_backward_v8_kernel(const __half* __restrict__ gate, const
     *reinterpret_cast<uint4*>(du + t * ldo + c) = pack_h8(b);
 }
 
+// swiglu_backward_v8_kernel with dy in fp16.
+__global__ void swiglu_backward_h8_kernel(const __half* __restrict__ gate, const __half* __restrict__ up,
+                                          long long ld, const __half* __restrict__ dy, long long lddy, int T, int n,
+                                          __half* __restrict__ dg, __half* __restrict__ du, long long ldo) {
+    MM_PDL_ENTRY();
+    const int nv = n >> 3;
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= T * nv) return;
+    const int t = i / nv, c = (i - t * nv) << 3;
+    float x[8], u[8], g[8], a[8], b[8];
+    unpack_h8(*reinterpret_cast<const uint4*>(gate + t * ld + c), x);
+    unpack_h8(*reinterpret_cast<const uint4*>(up + t * ld + c), u);
+    unpack_h8(*reinterpret_cast<const uint4*>(dy + t * lddy + c), g);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const float s = sigmoid_ref(x[k]);
+        a[k] = g[k] * u[k] * (s + x[k] * s * (1.f - s));
+        b[k] = g[k] * x[k] * s;
+    }
+    *reinterpret_cast<uint4*>(dg + t * ldo + c) = pack_h8(a);
+    *reinterpret_cast<uint4*>(du + t * ldo + c) = pack_h8(b);
+}
+
 // fp32 -> fp16, 4 columns per thread.
 __global__ void to_half_v4_kernel(const float* __restrict__ in, long long ldin, int T, int n, __half* __restrict__ out,
                                   long long ldo) {

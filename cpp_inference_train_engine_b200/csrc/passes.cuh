@@ -182,7 +182,7 @@ template <class A> void plan_workspace(Context& cx, A& a, int T, bool tape) {
     w.knope = a.template take<float>(t * c.H * c.nope);
     if (tape) {
         w.dy = a.template take<float>(t * c.d);
-        w.dgated = a.template take<float>(t * c.dff);
+        w.dgated16 = a.template take<__half>(t * cx.d16(c.dff));
         w.dh2 = a.template take<float>(t * c.d);
         w.dres = a.template take<float>(t * c.d);
         w.dao = a.template take<float>(t * c.aw());
@@ -299,8 +299,18 @@ inline void launch_swiglu_backward(Context& cx, const __half* gate, const __half
         MM_LAUNCH(swiglu_backward_v8_kernel, blocks_for(static_cast<long long>(T) * (n / 8), 256), 256, 0, gate, up,
                   ld, dy, lddy, T, n, dg, du, ldo);
     else
-        MM_LAUNCH(swiglu_backward_kernel, blocks_for(static_cast<long long>(T) * n, 256), 256, 0, gate, up, ld, dy,
+        MM_LAUNCH(swiglu_backward_kernel<float>, blocks_for(static_cast<long long>(T) * n, 256), 256, 0, gate, up, ld, dy,
                   lddy, T, n, dg, du, ldo);
+}
+inline void launch_swiglu_backward(Context& cx, const __half* gate, const __half* up, long long ld, const __half* dy,
+                                   long long lddy, int T, int n, __half* dg, __half* du, long long ldo) {
+    if (n % 8 == 0 && ld % 8 == 0 && ldo % 8 == 0 && lddy % 8 == 0 && al16(gate) && al16(up) && al16(dy) && al16(dg) &&
+        al16(du))
+        MM_LAUNCH(swiglu_backward_h8_kernel, blocks_for(static_cast<long long>(T) * (n / 8), 256), 256, 0, gate, up,
+                  ld, dy, lddy, T, n, dg, du, ldo);
+    else
+        MM_LAUNCH(swiglu_backward_kernel<__half>, blocks_for(static_cast<long long>(T) * n, 256), 256, 0, gate, up, ld,
+                  dy, lddy, T, n, dg, du, ldo);
 }
 
 inline void launch_to_half(Context& cx, const float* in, long long ldin, int T, int n, __half* out, long long ldo) {
@@ -537,10 +547,12 @@ inline void backward_chunk(Context& cx, int Bc, int S) {
             o.alpha_ptr = inv_s;
             gemm(cx, c.dff, c.d, T, {b.gated, ld_ff, true}, {w.dy16, ld_d, true}, o);
         }
-        gemm(cx, T, c.dff, c.d, {w.dy16, ld_d, false}, {cx.S(l, kWdown), cx.SL(l, kWdown), false}, {w.dgated, c.dff, kOutF32});
+        // dH in fp16 (scaled like every backward operand), read once by the SwiGLU backward
+        gemm(cx, T, c.dff, c.d, {w.dy16, ld_d, false}, {cx.S(l, kWdown), cx.SL(l, kWdown), false},
+             {w.dgated16, ld_ff, kOutF16});
         const int ld_gu = cx.d16(2 * c.dff);
         const PrepLayer& pw = cx.prep[l];
-        launch_swiglu_backward(cx, b.gate, b.up, ld_gu, w.dgated, c.dff, T, c.dff, w.dg16, w.du16, ld_gu);
+        launch_swiglu_backward(cx, b.gate, b.up, ld_gu, w.dgated16, ld_ff, T, c.dff, w.dg16, w.du16, ld_gu);
         {
             GemmOutSpec o{cx.G(l, kWgate), c.dff, kOutF32Acc};
             o.alpha_ptr = inv_s;

@@ -157,7 +157,8 @@ struct Workspace {
     // scratch
     float* knope;       // [T][H*nope]
     // backward scratch (tape only)
-    float *dy, *dgated, *dh2, *dres, *dao, *dk, *drope, *drope2, *dckv, *dkvraw, *dh, *dcq, *Dd;
+    __half* dgated16;  // [T][ld16(dff)]
+    float *dy, *dh2, *dres, *dao, *dk, *drope, *drope2, *dckv, *dkvraw, *dh, *dcq, *Dd;
     __half *dy16, *dg16, *du16, *dres16, *dq16, *dkn16, *dv16, *dkvp16, *draw16, *g16, *dao16;
     float* norm_part;   // [kNormBlocks][max(d, qr, kv_rank)] RMSNorm weight-gradient partials
 };

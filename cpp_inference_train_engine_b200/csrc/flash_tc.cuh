@@ -275,4 +275,222 @@ __global__ void __launch_bounds__(fatc::kThreads, 2)
     }
 }
 
+
+namespace fadq {
+constexpr int kRows = 128;                  // queries per CTA
+constexpr int kKeys = 64;                   // keys per tile
+constexpr int kD = 64;
+constexpr int kQBytes = kRows * kD * 2;     // 16 KB
+constexpr int kKBytes = kKeys * kD * 2;     // 8 KB
+constexpr int kSoftmaxWarps = 8;
+constexpr int kThreads = 32 * (kSoftmaxWarps + 2);
+// Q, dO, K[2], V[2], dS [128 queries][64 keys], then barriers
+constexpr int kSmem = 2 * kQBytes + 4 * kKBytes + kQBytes + 1024 + 256;
+constexpr uint32_t kTmemCols = 128;
+constexpr int kColS = 0, kColDP = 64, kColDQ = 0;  // dQ_j reuses S's columns once S is consumed
+}  // namespace fadq
+
+// dQ of causal attention on the tensor cores (the backward of ops::attention, ops.cpp:143-172):
+// one CTA per (head, sequence, 128-query tile), 64-key tiles at or below the diagonal.
+// warp 8 TMA (Q and dO once, K and V tiles into a 2-deep ring), warp 9 tcgen05.mma
+// (S = Q K^T and dP = dO V^T into TMEM, then dQ_j = dS K_j), warps 0-7 one thread per query
+// row and 32-key half: P = exp2(S c - lse2) from the forward's base-2 log-sum-exp,
+// dS = P (dP - D) scale in fp16 into the A operand of dQ_j, dQ accumulated in registers.
+// The epilogue applies the inverse query RoPE and writes fp16 dq16, as
+// flash_bwd_dq_mma_kernel does. 82 KB of shared memory, 128 TMEM columns: two CTAs per SM.
+__global__ void __launch_bounds__(fadq::kThreads, 2)
+    flash_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmDO,
+                           const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                           const float* __restrict__ lse2, const float* __restrict__ Dd, int S, int H, float scale,
+                           __half* __restrict__ dq16, long long ld_dq, const float* __restrict__ cos_t,
+                           const float* __restrict__ sin_t, int rope_begin, int rope, int* err) {
+    using namespace fadq;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~static_cast<uintptr_t>(1023));
+    uint8_t* sQ = smem;
+    uint8_t* sG = smem + kQBytes;              // dO
+    uint8_t* sK = smem + 2 * kQBytes;          // [2]
+    uint8_t* sV = sK + 2 * kKBytes;            // [2]
+    uint8_t* sDS = sV + 2 * kKBytes;           // [128][64] fp16
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sDS + kQBytes);
+    uint64_t* q_full = bars + 0;
+    uint64_t* kv_full = bars + 1;   // [2]
+    uint64_t* kv_empty = bars + 3;  // [2]
+    uint64_t* s_full = bars + 5;
+    uint64_t* ds_full = bars + 6;   // softmax warps
+    uint64_t* dq_full = bars + 7;
+    uint64_t* dq_empty = bars + 8;  // softmax warps
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 9);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int h = blockIdx.x, b = blockIdx.y;
+    const int qt = gridDim.z - 1 - blockIdx.z;
+    const int nk = min(2 * qt + 2, (S + kKeys - 1) / kKeys);  // key tiles at or below the diagonal
+    const int row_base = b * S;
+
+    if (warp == 8) {
+        if (lane == 0) {
+            mbar_init(q_full, 1);
+            mbar_init(&kv_full[0], 1);
+            mbar_init(&kv_full[1], 1);
+            mbar_init(&kv_empty[0], 1);
+            mbar_init(&kv_empty[1], 1);
+            mbar_init(s_full, 1);
+            mbar_init(ds_full, kSoftmaxWarps);
+            mbar_init(dq_full, 1);
+            mbar_init(dq_empty, kSoftmaxWarps);
+            fence_mbar_init();
+            prefetch_tmap(&tmQ);
+            prefetch_tmap(&tmDO);
+            prefetch_tmap(&tmK);
+            prefetch_tmap(&tmV);
+        }
+        __syncwarp();
+        tmem_alloc(tmem_slot, kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    MM_PDL_ENTRY();
+
+    if (warp == 8) {
+        if (lane == 0) {
+            mbar_arrive_expect_tx(q_full, 2 * kQBytes);
+            tma_load_2d(sQ, &tmQ, q_full, h * kD, row_base + qt * kRows);
+            tma_load_2d(sG, &tmDO, q_full, h * kD, row_base + qt * kRows);
+            for (int j = 0; j < nk; ++j) {
+                const int s = j & 1, u = j >> 1;
+                if (!mbar_wait_bounded(&kv_empty[s], (u & 1) ^ 1, err)) break;
+                mbar_arrive_expect_tx(&kv_full[s], 2 * kKBytes);
+                tma_load_2d(sK + s * kKBytes, &tmK, &kv_full[s], h * kD, row_base + j * kKeys);
+                tma_load_2d(sV + s * kKBytes, &tmV, &kv_full[s], h * kD, row_base + j * kKeys);
+            }
+        }
+    } else if (warp == 9) {
+        if (lane == 0) {
+            const uint32_t id_s = umma_idesc_f16(false, false, false, kRows, kKeys);  // Q K^T, dO V^T
+            const uint32_t id_q = umma_idesc_f16(false, false, true, kRows, kD);     // dS K, K MN-major
+            const uint32_t aq = smem_u32(sQ), ag = smem_u32(sG), ads = smem_u32(sDS);
+            bool ok = mbar_wait_bounded(q_full, 0, err);
+            for (int j = 0; j < nk && ok; ++j) {
+                const int s = j & 1, u = j >> 1;
+                if (!mbar_wait_bounded(&kv_full[s], u & 1, err)) { ok = false; break; }
+                if (j > 0 && !mbar_wait_bounded(dq_empty, (j - 1) & 1, err)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t bk = smem_u32(sK + s * kKBytes), bv = smem_u32(sV + s * kKBytes);
+#pragma unroll
+                for (int k = 0; k < kD / 16; ++k) {
+                    tc_mma_f16(tmem + kColS, umma_desc_sw128(aq + k * 32, 16, 1024),
+                               umma_desc_sw128(bk + k * 32, 16, 1024), id_s, k ? 1u : 0u);
+                    tc_mma_f16(tmem + kColDP, umma_desc_sw128(ag + k * 32, 16, 1024),
+                               umma_desc_sw128(bv + k * 32, 16, 1024), id_s, k ? 1u : 0u);
+                }
+                tc_commit(s_full);
+                if (!mbar_wait_bounded(ds_full, j & 1, err)) { ok = false; break; }
+                tc_fence_after();
+#pragma unroll
+                for (int k = 0; k < kKeys / 16; ++k)
+                    tc_mma_f16(tmem + kColDQ, umma_desc_sw128(ads + k * 32, 16, 1024),
+                               umma_desc_sw128(bk + k * 2048, 8192, 1024), id_q, k ? 1u : 0u);
+                tc_commit(dq_full);
+                tc_commit(&kv_empty[s]);
+            }
+        }
+    } else {
+        // thread = query row r (TMEM lane r), key half hh of each 64-key tile, dQ columns [32 hh, +32)
+        const int q = warp & 3, hh = warp >> 2;
+        const int r = q * 32 + lane;
+        const int qpos = qt * kRows + r;
+        const bool row_ok = qpos < S;
+        const float L = row_ok ? lse2[(static_cast<long long>(row_base) + qpos) * H + h] : 0.f;
+        const float D = row_ok ? Dd[(static_cast<long long>(row_base) + qpos) * H + h] : 0.f;
+        const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
+        const float cs = scale * 1.4426950408889634f;
+        uint8_t* drow = sDS + r * 128;
+        float acc[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) acc[i] = 0.f;
+        bool ok = true;
+        for (int j = 0; j < nk && ok; ++j) {
+            if (!mbar_wait_bounded(s_full, j & 1, err)) { ok = false; break; }
+            tc_fence_after();
+            const int key0 = j * kKeys + hh * 32;
+            // last key of this half the row may attend (causal, inside the sequence)
+            const int lim = row_ok ? min(qpos, S - 1) - key0 : -1;
+#pragma unroll 1
+            for (int c = 0; c < 2; ++c) {
+                float sv[16], dp[16];
+                tmem_ld16(lane_base + kColS + hh * 32 + c * 16, sv);
+                tmem_ld16(lane_base + kColDP + hh * 32 + c * 16, dp);
+                uint32_t w[8];
+#pragma unroll
+                for (int i = 0; i < 16; i += 2) {
+                    const float p0 = c * 16 + i <= lim ? fast_exp2(fmaf(sv[i], cs, -L)) : 0.f;
+                    const float p1 = c * 16 + i + 1 <= lim ? fast_exp2(fmaf(sv[i + 1], cs, -L)) : 0.f;
+                    const __half2 hv = __floats2half2_rn(p0 * (dp[i] - D) * scale, p1 * (dp[i + 1] - D) * scale);
+                    w[i >> 1] = *reinterpret_cast<const uint32_t*>(&hv);
+                }
+                // keys [32 hh + 16 c, +16): two 16-byte chunks of the 128-byte row, swizzled
+#pragma unroll
+                for (int q2 = 0; q2 < 2; ++q2) {
+                    const int cc = hh * 4 + c * 2 + q2;
+                    *reinterpret_cast<uint4*>(drow + ((cc ^ (r & 7)) << 4)) =
+                        make_uint4(w[4 * q2], w[4 * q2 + 1], w[4 * q2 + 2], w[4 * q2 + 3]);
+                }
+            }
+            tc_fence_before();
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(ds_full);
+            if (!mbar_wait_bounded(dq_full, j & 1, err)) { ok = false; break; }
+            tc_fence_after();
+            {
+                float o[32];
+                tmem_ld32_nowait(lane_base + kColDQ + hh * 32, o);
+                tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 32; ++i) acc[i] += o[i];
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(dq_empty);
+        }
+        if (ok && row_ok) {
+            // inverse RoPE of the query rotation on columns [rope_begin, rope_begin + rope)
+            const int half_r = rope / 2;
+#pragma unroll
+            for (int i = 0; i < 32; i += 2) {
+                const int cc = hh * 32 + i;
+                if (cc >= rope_begin && cc < rope_begin + rope) {
+                    const int pair = (cc - rope_begin) >> 1;
+                    const float cn = cos_t[qpos * half_r + pair], sn = -sin_t[qpos * half_r + pair];
+                    const float a = acc[i], bb = acc[i + 1];
+                    acc[i] = a * cn - bb * sn;
+                    acc[i + 1] = a * sn + bb * cn;
+                }
+            }
+            __half* dst = dq16 + (static_cast<long long>(row_base) + qpos) * ld_dq + h * kD + hh * 32;
+#pragma unroll
+            for (int i = 0; i < 32; i += 8) {
+                const __half2 h0 = __floats2half2_rn(acc[i], acc[i + 1]);
+                const __half2 h1 = __floats2half2_rn(acc[i + 2], acc[i + 3]);
+                const __half2 h2 = __floats2half2_rn(acc[i + 4], acc[i + 5]);
+                const __half2 h3 = __floats2half2_rn(acc[i + 6], acc[i + 7]);
+                *reinterpret_cast<uint4*>(dst + i) =
+                    make_uint4(*reinterpret_cast<const uint32_t*>(&h0), *reinterpret_cast<const uint32_t*>(&h1),
+                               *reinterpret_cast<const uint32_t*>(&h2), *reinterpret_cast<const uint32_t*>(&h3));
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 8) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
 }  // namespace mm

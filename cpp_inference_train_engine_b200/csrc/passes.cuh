@@ -584,9 +584,23 @@ inline void backward_chunk(Context& cx, int Bc, int S) {
                 set_dynamic_smem<flash_bwd_dq_mma_kernel<64>>(flash_dq_smem<64>());
                 MM_LAUNCH_TIMED(kKFlashBwd, w_kv, flash_bwd_dkdv_mma_kernel<64>, grid, 128, flash_dkdv_smem<64>(), b.q, b.k,
                                 b.v, w.dao16, b.lse, w.Dd, S, c.H, scale, w.dk, w.dv16, (long long)ld_v16);
-                MM_LAUNCH_TIMED(kKFlashBwd, w_q, flash_bwd_dq_mma_kernel<64>, grid, 128, flash_dq_smem<64>(), b.q, b.k, b.v,
-                                w.dao16, b.lse, w.Dd, S, c.H, scale, w.dq16, (long long)ld_q16, cx.cos_t, cx.sin_t,
-                                c.nope, c.rope);
+                if (c.dv == 64 && flash_tc_enabled()) {
+                    // tcgen05 dQ: Q/dO tiles of 128 rows, K/V tiles of 64 keys through TMA
+                    const long long T64 = static_cast<long long>(Bc) * S, wd = static_cast<long long>(c.H) * 64;
+                    const CUtensorMap& tq = tensor_map(b.q, false, wd, T64, wd, 64, fadq::kRows);
+                    const CUtensorMap& tg = tensor_map(w.dao16, false, wd, T64, wd, 64, fadq::kRows);
+                    const CUtensorMap& tk = tensor_map(b.k, false, wd, T64, wd, 64, fadq::kKeys);
+                    const CUtensorMap& tv = tensor_map(b.v, false, wd, T64, wd, 64, fadq::kKeys);
+                    set_dynamic_smem<flash_bwd_dq_tc_kernel>(fadq::kSmem);
+                    dim3 gq(c.H, Bc, (S + fadq::kRows - 1) / fadq::kRows);
+                    MM_LAUNCH_TIMED(kKFlashBwd, w_q, flash_bwd_dq_tc_kernel, gq, fadq::kThreads, fadq::kSmem, tq, tg, tk,
+                                    tv, b.lse, w.Dd, S, c.H, scale, w.dq16, (long long)ld_q16, cx.cos_t, cx.sin_t,
+                                    c.nope, c.rope, cx.d_err);
+                } else {
+                    MM_LAUNCH_TIMED(kKFlashBwd, w_q, flash_bwd_dq_mma_kernel<64>, grid, 128, flash_dq_smem<64>(), b.q, b.k,
+                                    b.v, w.dao16, b.lse, w.Dd, S, c.H, scale, w.dq16, (long long)ld_q16, cx.cos_t,
+                                    cx.sin_t, c.nope, c.rope);
+                }
             } else {
                 MM_LAUNCH_TIMED(kKFlashBwd, w_kv, flash_bwd_dkdv_mma_kernel<16>, grid, 128, flash_dkdv_smem<16>(), b.q, b.k,
                                 b.v, w.dao16, b.lse, w.Dd, S, c.H, scale, w.dk, w.dv16, (long long)ld_v16);

@@ -1,8 +1,8 @@
-"""The tcgen05 attention forward (64-wide heads of the 35.8M model) on sequences of several
+"""The tcgen05 attention forward and backward dQ (64-wide heads of the 35.8M model) on sequences of several
 128-query tiles, ragged last tile included: teacher-forced log-probabilities against the
 reference's CPU build (2e-3 absolute, as the other model tests), and log-probabilities and
-the weighted-NLL gradient against the same engine with the forward on the mma.sync kernel
-(MM_FLASH_TC=0, a separate process): 3e-3 absolute and 3e-4 mean absolute on log-probs,
+the weighted-NLL gradient against the same engine with the forward and dQ on the mma.sync
+kernels (MM_FLASH_TC=0, a separate process): 3e-3 absolute and 3e-4 mean absolute on log-probs,
 1e-2 relative on the gradient (both paths round P to fp16, normalised per 128-key tile here
 and per 64-key tile there, and the difference grows through the ten layers)."""
 import os

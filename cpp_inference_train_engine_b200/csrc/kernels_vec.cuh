@@ -152,21 +152,23 @@ __global__ void __launch_bounds__(256) rmsnorm_backward_v4_kernel(
     }
 }
 
-// dw[j] += scale * sum_r part[r][j] in a fixed order: block (32, 8) covers 32 columns,
-// row group y sums rows y, y + 8, ... and the 8 group sums are added in order.
+// dw[j] += scale * sum_r part[r][j] in a fixed order: block (32, kColsumGroups) covers 32
+// columns, row group y sums rows y, y + kColsumGroups, ... and the group sums are added in
+// order (many short row walks in flight instead of a few long ones).
+constexpr int kColsumGroups = 32;
 __global__ void colsum_kernel(const float* __restrict__ part, int rows, int n, const float* __restrict__ scale,
                               float* __restrict__ dw) {
     MM_PDL_ENTRY();
-    __shared__ float grp[8][33];
+    __shared__ float grp[kColsumGroups][33];
     const int j = blockIdx.x * 32 + threadIdx.x;
     float s = 0.f;
     if (j < n)
-        for (int r = threadIdx.y; r < rows; r += 8) s += part[static_cast<long long>(r) * n + j];
+        for (int r = threadIdx.y; r < rows; r += kColsumGroups) s += part[static_cast<long long>(r) * n + j];
     grp[threadIdx.y][threadIdx.x] = s;
     __syncthreads();
     if (threadIdx.y == 0 && j < n) {
         float t = grp[0][threadIdx.x];
-        for (int y = 1; y < 8; ++y) t += grp[y][threadIdx.x];
+        for (int y = 1; y < kColsumGroups; ++y) t += grp[y][threadIdx.x];
         dw[j] += t * (scale ? *scale : 1.0f);
     }
 }

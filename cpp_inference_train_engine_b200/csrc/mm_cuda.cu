@@ -251,7 +251,7 @@ int mm_cuda_accumulate(mm_cuda_ctx* h, const uint16_t* input, const uint16_t* ta
             lp.resize(static_cast<size_t>(T));
             MM_CUDA_CHECK(cudaMemcpyAsync(lp.data(), w.lp, T * 4, cudaMemcpyDeviceToHost, cx.stream));
             MM_CUDA_CHECK(cudaMemsetAsync(&cx.d_sums->max_coef_bits, 0, 4, cx.stream));
-            MM_LAUNCH(mm::absmax_kernel, mm::blocks_for(T, 256), 256, 0, w.coef, static_cast<int>(T),
+            MM_LAUNCH(mm::absmax_kernel, std::min<unsigned>(mm::blocks_for(T, 1024), mm::sm_count() * 4), 256, 0, w.coef, T,
                       &cx.d_sums->max_coef_bits);
             MM_LAUNCH(mm::grad_scale_kernel, 1, 1, 0, cx.d_sums, cx.d_scale);
             mm::backward_chunk(cx, bc, seq);

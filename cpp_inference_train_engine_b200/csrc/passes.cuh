@@ -280,7 +280,7 @@ inline void launch_rmsnorm_backward(Context& cx, const float* x, long long ldx, 
     else
         MM_LAUNCH(rmsnorm_backward_v4_kernel<8>, kNormBlocks, 256, smem, x, ldx, w, dy, lddy, add, ldadd, T, n, eps,
                   dx32, lddx, dx16, lddx16, cx.ws.norm_part);
-    MM_LAUNCH(colsum_kernel, (n + 31) / 32, dim3(32, 8), 0, cx.ws.norm_part, kNormBlocks, n, scale, dw);
+    MM_LAUNCH(colsum_kernel, (n + 31) / 32, dim3(32, kColsumGroups), 0, cx.ws.norm_part, kNormBlocks, n, scale, dw);
 }
 
 inline void launch_swiglu(Context& cx, const __half* gate, const __half* up, long long ld, int T, int n, __half* out,
@@ -661,7 +661,7 @@ inline void backward_chunk(Context& cx, int Bc, int S) {
     int* nonfinite = reinterpret_cast<int*>(eb + acc_bytes + 4);
     if (fresh) MM_CUDA_CHECK(cudaMemsetAsync(acc, 0, acc_bytes, cx.stream));
     MM_CUDA_CHECK(cudaMemsetAsync(max_bits, 0, 8, cx.stream));
-    MM_LAUNCH(absmax_kernel, blocks_for(static_cast<long long>(T) * c.d, 256), 256, 0, w.dy, T * c.d, max_bits);
+    MM_LAUNCH(absmax_kernel, static_cast<unsigned>(sm_count() * 4), 256, 0, w.dy, static_cast<long long>(T) * c.d, max_bits);
     MM_LAUNCH(embed_grad_fixed_kernel, warp_rows_grid(T), 256, 0, w.tokens, w.dy, T, c.d, acc, max_bits, nonfinite);
     MM_LAUNCH(embed_grad_convert_kernel, static_cast<unsigned>(sm_count() * 8), 256, 0, acc, nE, T, max_bits, nonfinite,
               inv_s, cx.GE());

@@ -328,7 +328,7 @@ inline mm_step_result dpo_step(Context& pc, Context& rc, const uint16_t* input, 
         MM_LAUNCH_CX(pc, dpo_coef_kernel, bp, 256, 0, w.lp, w.ref_lp, w.mask, S, beta, static_cast<float>(n_total),
                      static_cast<double>(n_total), w.coef, part + p0, d_margins + p0);
         MM_CUDA_CHECK(cudaMemsetAsync(&pc.d_sums->max_coef_bits, 0, 4, pc.stream));
-        MM_LAUNCH_CX(pc, absmax_kernel, blocks_for(T, 256), 256, 0, w.coef, static_cast<int>(T),
+        MM_LAUNCH_CX(pc, absmax_kernel, std::min<unsigned>(blocks_for(T, 1024), sm_count() * 4), 256, 0, w.coef, T,
                      &pc.d_sums->max_coef_bits);
         MM_LAUNCH_CX(pc, grad_scale_kernel, 1, 1, 0, pc.d_sums, pc.d_scale);
         backward_chunk(pc, rows, S);

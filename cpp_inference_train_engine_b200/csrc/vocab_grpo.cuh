@@ -667,12 +667,31 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(
 } // namespace mm
 
 namespace mm {
-// max |x| over n floats, as float bits into *out (atomicMax on non-negative floats).
-__global__ void absmax_kernel(const float* __restrict__ x, int n, unsigned int* __restrict__ out) {
+// max |x| over n floats (NaN ignored), as float bits into *out: grid-stride 16-byte loads,
+// a block maximum, one atomicMax per block (the bits of non-negative floats order like them).
+__global__ void absmax_kernel(const float* __restrict__ x, long long n, unsigned int* __restrict__ out) {
     MM_PDL_ENTRY();
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    float v = i < n ? fabsf(x[i]) : 0.f;
-    v = warp_max(v);
-    if ((threadIdx.x & 31) == 0 && v > 0.f) atomicMax(out, __float_as_uint(v));
+    __shared__ float red[32];
+    float m = 0.f;
+    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+    const long long i0 = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if ((reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+        const long long n4 = n >> 2;
+        const float4* x4 = reinterpret_cast<const float4*>(x);
+        for (long long i = i0; i < n4; i += stride) {
+            const float4 v = x4[i];
+            m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+        }
+        for (long long i = (n4 << 2) + i0; i < n; i += stride) m = fmaxf(m, fabsf(x[i]));
+    } else {
+        for (long long i = i0; i < n; i += stride) m = fmaxf(m, fabsf(x[i]));
+    }
+    m = warp_max(m);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w) m = fmaxf(m, red[w]);
+        if (m > 0.f) atomicMax(out, __float_as_uint(m));
+    }
 }
 } // namespace mm

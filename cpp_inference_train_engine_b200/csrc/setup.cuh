@@ -72,8 +72,18 @@ inline int gemm(Context& cx, int M, int N, int K, Opnd A, Opnd B, const GemmOutS
     const int num_k = (K + kGemmBK - 1) / kGemmBK;
     int splits = 1;
     if (!o.glu_n && o.kind == kOutF32Acc && !o.residual && tiles < sm_count() && num_k >= 32 && N % 4 == 0) {
-        splits = static_cast<int>(std::min<long long>((2LL * sm_count() + tiles - 1) / tiles, num_k / 8));
-        splits = std::max(1, std::min(splits, 32));
+        // the split count whose waves of (tile, split) units cost least per split: time ~
+        // ceil(tiles * s / SMs) / s (a nearly empty last wave costs as much as a full one);
+        // ties go to fewer splits (less partial traffic)
+        const int cap = static_cast<int>(std::min<long long>(32, num_k / 8));
+        double best = 2.0;
+        for (int s = 1; s <= cap; ++s) {
+            const double cost = static_cast<double>((tiles * s + sm_count() - 1) / sm_count()) / s;
+            if (cost < best - 1e-12) {
+                best = cost;
+                splits = s;
+            }
+        }
     }
     // Output map: 32-row x 128-byte boxes; fp32 partials of split z occupy rows
     // [z * Mp, z * Mp + M) with Mp = M rounded up to whole 128-row tiles, so a tile's

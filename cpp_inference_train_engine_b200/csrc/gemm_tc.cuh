@@ -57,7 +57,44 @@ struct GemmArgs {
     const float* rope_cos;
     const float* rope_sin;
     int rope_seq, rope_period, rope_begin, rope_len;
+    // With glu_n: also store the fp16 pre-activations, gate columns through the map tmD and
+    // up columns through tmE (the training forward keeps them for the backward).
+    int glu_pre;
+    // SwiGLU backward in the epilogue of dH (fp16 out, dglu_n = N = d_ff): with gate and up
+    // read from dglu_gu (row pitch dglu_ld, up at column offset dglu_n), stores d gate
+    // through tmC and d up through tmD. 0 = off.
+    const __half* dglu_gu;
+    long long dglu_ld;
+    int dglu_n;
 };
+
+__device__ __forceinline__ uint32_t pack_half2(float a, float b) {
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// 64 fp16 values (32 packed words) of one staged 128-byte row, 128-byte swizzled.
+__device__ __forceinline__ void stage_row_words(uint8_t* rowp, int lane, const uint32_t (&w)[32]) {
+#pragma unroll
+    for (int cc = 0; cc < 8; ++cc)
+        *reinterpret_cast<uint4*>(rowp + ((cc ^ (lane & 7)) << 4)) =
+            make_uint4(w[4 * cc], w[4 * cc + 1], w[4 * cc + 2], w[4 * cc + 3]);
+}
+
+// One 32-row x 64-column fp16 tile from a warp's staging buffer to global through `map`,
+// after the previous store from that buffer has finished reading it.
+__device__ __forceinline__ void stage_and_store(uint8_t* stage, int lane, const uint32_t (&w)[32],
+                                                const CUtensorMap* map, int x, int y) {
+    if (lane == 0) bulk_wait_read0();
+    __syncwarp();
+    stage_row_words(stage + lane * 128, lane, w);
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+        tma_store_2d(map, stage, x, y);
+        bulk_commit();
+    }
+}
 
 constexpr int kGemmBM = 128;
 constexpr int kGemmBK = 64;
@@ -82,7 +119,8 @@ template <int BN, int STAGES> struct GemmCfg {
 template <int BN, int STAGES>
 __global__ void __launch_bounds__(320, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const __grid_constant__ CUtensorMap tmC, GemmArgs g) {
+                   const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmD,
+                   const __grid_constant__ CUtensorMap tmE, GemmArgs g) {
     using C = GemmCfg<BN, STAGES>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -222,6 +260,36 @@ __global__ void __launch_bounds__(320, 1)
                     if (lane == 0) mbar_arrive(&acc_empty[buf]);
                 }
                 for (int c = half * 64; c < TW; c += 64 * nhalf) {
+                    if (g.glu_pre) {
+                        // the fp16 pre-activations first: gate columns, then up columns, each
+                        // read from tensor memory into the warp's staging tile
+#pragma unroll 1
+                        for (int part = 0; part < 2; ++part) {
+                            if (lane == 0) bulk_wait_read0();
+                            __syncwarp();
+                            uint8_t* rowp = stage_base + lane * 128;
+#pragma unroll
+                            for (int sub = 0; sub < 2; ++sub) {
+                                float t[32];
+                                tmem_ld32_nowait(src + static_cast<uint32_t>(part * TW + c + 32 * sub), t);
+                                tmem_wait_ld();
+#pragma unroll
+                                for (int ch = 0; ch < 4; ++ch) {
+                                    const float* f = t + 8 * ch;
+                                    const int cc = sub * 4 + ch;
+                                    *reinterpret_cast<uint4*>(rowp + ((cc ^ (lane & 7)) << 4)) =
+                                        make_uint4(pack_half2(f[0] * alpha, f[1] * alpha), pack_half2(f[2] * alpha, f[3] * alpha),
+                                                   pack_half2(f[4] * alpha, f[5] * alpha), pack_half2(f[6] * alpha, f[7] * alpha));
+                                }
+                            }
+                            fence_proxy_async_smem();
+                            __syncwarp();
+                            if (lane == 0) {
+                                tma_store_2d(part ? &tmE : &tmD, stage_base, n0 + c, map_row0);
+                                bulk_commit();
+                            }
+                        }
+                    }
                     uint8_t* stage = stage_base + sbuf * 4096;
                     if (C::EPI_BUFS == 2) sbuf ^= 1;
                     if (lane == 0) {  // the store that last read `stage` is done
@@ -252,8 +320,7 @@ __global__ void __launch_bounds__(320, 1)
                                 const float ga = gv[i] * alpha, gb = gv[i + 1] * alpha;
                                 const float a = __fdividef(ga, 1.f + __expf(-ga)) * (uv[i] * alpha);
                                 const float b = __fdividef(gb, 1.f + __expf(-gb)) * (uv[i + 1] * alpha);
-                                const __half2 h = __floats2half2_rn(a, b);
-                                w[e] = *reinterpret_cast<const uint32_t*>(&h);
+                                w[e] = pack_half2(a, b);
                             }
                             const int cc = sub * 4 + ch;
                             *reinterpret_cast<uint4*>(rowp + ((cc ^ (lane & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
@@ -295,6 +362,52 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll
                     for (int i = 0; i < 32; ++i)
                         if (col0 + i < g.N) v[i] += r[i];
+                }
+                if (g.dglu_n) {
+                    // v = dh of columns [col0, col0 + 64) of this row; x = gate, u = up from the
+                    // forward: d gate = dh u s (1 + x (1 - s)), d up = dh x s, s = sigmoid(x).
+                    // d gate goes straight into the staging tile, d up waits packed for it.
+                    const __half* gr = g.dglu_gu + static_cast<long long>(row < g.M ? row : 0) * g.dglu_ld;
+                    uint32_t du[32];
+                    if (lane == 0) bulk_wait_read0();
+                    __syncwarp();
+                    uint8_t* rowp = stage_base + lane * 128;
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        // 8 columns at a time; the barrier keeps the next group's loads behind
+                        // this group's math (registers)
+                        if (j) asm volatile("" ::: "memory");
+                        const int col = col0 + 8 * j;
+                        const bool in = row < g.M && col < g.N;  // N % 8 == 0
+                        const uint4 xq = in ? *reinterpret_cast<const uint4*>(gr + col) : make_uint4(0, 0, 0, 0);
+                        const uint4 uq = in ? *reinterpret_cast<const uint4*>(gr + g.dglu_n + col) : make_uint4(0, 0, 0, 0);
+                        const uint32_t xw[4] = {xq.x, xq.y, xq.z, xq.w};
+                        const uint32_t uw[4] = {uq.x, uq.y, uq.z, uq.w};
+                        uint32_t da[4];
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const float x0 = __half2float(__ushort_as_half(static_cast<unsigned short>(xw[e] & 0xFFFFu)));
+                            const float x1 = __half2float(__ushort_as_half(static_cast<unsigned short>(xw[e] >> 16)));
+                            const float u0 = __half2float(__ushort_as_half(static_cast<unsigned short>(uw[e] & 0xFFFFu)));
+                            const float u1 = __half2float(__ushort_as_half(static_cast<unsigned short>(uw[e] >> 16)));
+                            const int i = 8 * j + 2 * e;
+                            // sigmoid on the SFU (the results are rounded to fp16)
+                            const float s0 = __fdividef(1.f, 1.f + __expf(-x0));
+                            const float s1 = __fdividef(1.f, 1.f + __expf(-x1));
+                            da[e] = pack_half2(v[i] * u0 * (s0 + x0 * s0 * (1.f - s0)),
+                                               v[i + 1] * u1 * (s1 + x1 * s1 * (1.f - s1)));
+                            du[4 * j + e] = pack_half2(v[i] * x0 * s0, v[i + 1] * x1 * s1);
+                        }
+                        *reinterpret_cast<uint4*>(rowp + ((j ^ (lane & 7)) << 4)) = make_uint4(da[0], da[1], da[2], da[3]);
+                    }
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_2d(&tmC, stage_base, col0, map_row0);
+                        bulk_commit();
+                    }
+                    stage_and_store(stage_base, lane, du, &tmD, col0, map_row0);
+                    continue;
                 }
                 if (g.lse_part) {  // fp32 output: 32 columns per chunk
                     float cm = -INFINITY;

@@ -379,6 +379,16 @@ inline bool flash_tc_enabled() {
     return on;
 }
 
+// MM_FUSED_SWIGLU=0 keeps the training SwiGLU (forward with tape, backward) as separate
+// elementwise kernels around plain products (for comparison).
+inline bool swiglu_fused_enabled() {
+    static const bool on = [] {
+        const char* e = std::getenv("MM_FUSED_SWIGLU");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
 inline void launch_flash_fwd(Context& cx, const LayerBuf& b, int Bc, int S) {
     const Dims& c = cx.c;
     dim3 grid(c.H, Bc, (S + fa::kTile - 1) / fa::kTile);
@@ -468,13 +478,18 @@ inline void forward_chunk(Context& cx, int Bc, int S, bool tape, VocabMode vm, b
         // feed-forward block
         launch_rmsnorm(cx, res, c.d, cx.W(l, kFfnNorm), T, c.d, (float*)nullptr, 0LL, b.h2, ld_d);
         const int ld_gu = cx.d16(2 * c.dff);
-        if (tape || c.dff % 8) {
+        if (c.dff % 8 || (tape && !swiglu_fused_enabled())) {
             // the backward needs gate and up themselves
             gemm(cx, T, 2 * c.dff, c.d, {b.h2, ld_d, false}, {pw.Wgu, pw.ldgu, true}, {b.gate, ld_gu, kOutF16});
             launch_swiglu(cx, b.gate, b.up, ld_gu, T, c.dff, b.gated, ld_ff);
         } else {
+            // SwiGLU in the product's epilogue; with tape it also stores gate and up for the backward
             GemmOutSpec o{b.gated, ld_ff, kOutF16};
             o.glu_n = c.dff;
+            if (tape) {
+                o.pre_gate = b.gate;
+                o.pre_ld = ld_gu;
+            }
             gemm(cx, T, c.dff, c.d, {b.h2, ld_d, false}, {pw.Wgu, pw.ldgu, true}, o);
         }
         {
@@ -547,12 +562,22 @@ inline void backward_chunk(Context& cx, int Bc, int S) {
             o.alpha_ptr = inv_s;
             gemm(cx, c.dff, c.d, T, {b.gated, ld_ff, true}, {w.dy16, ld_d, true}, o);
         }
-        // dH in fp16 (scaled like every backward operand), read once by the SwiGLU backward
-        gemm(cx, T, c.dff, c.d, {w.dy16, ld_d, false}, {cx.S(l, kWdown), cx.SL(l, kWdown), false},
-             {w.dgated16, ld_ff, kOutF16});
         const int ld_gu = cx.d16(2 * c.dff);
         const PrepLayer& pw = cx.prep[l];
-        launch_swiglu_backward(cx, b.gate, b.up, ld_gu, w.dgated16, ld_ff, T, c.dff, w.dg16, w.du16, ld_gu);
+        if (c.dff % 8 == 0 && swiglu_fused_enabled()) {
+            // dH = dY W_down^T with the SwiGLU backward in its epilogue: [d gate | d up] in fp16
+            // (scaled like every backward operand) straight from the fp32 accumulator
+            GemmOutSpec o{w.dg16, ld_gu, kOutF16};
+            o.dglu_gu = b.gate;
+            o.dglu_ld = ld_gu;
+            o.dglu_up = w.du16;
+            gemm(cx, T, c.dff, c.d, {w.dy16, ld_d, false}, {cx.S(l, kWdown), cx.SL(l, kWdown), false}, o);
+        } else {
+            // dH in fp16, read once by the SwiGLU backward
+            gemm(cx, T, c.dff, c.d, {w.dy16, ld_d, false}, {cx.S(l, kWdown), cx.SL(l, kWdown), false},
+                 {w.dgated16, ld_ff, kOutF16});
+            launch_swiglu_backward(cx, b.gate, b.up, ld_gu, w.dgated16, ld_ff, T, c.dff, w.dg16, w.du16, ld_gu);
+        }
         {
             GemmOutSpec o{cx.G(l, kWgate), c.dff, kOutF32Acc};
             o.alpha_ptr = inv_s;

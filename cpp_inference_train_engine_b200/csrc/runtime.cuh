@@ -444,6 +444,15 @@ struct GemmOutSpec {
     const float* rope_cos = nullptr;
     const float* rope_sin = nullptr;
     int rope_seq = 1, rope_period = 1, rope_begin = 0, rope_len = 0;
+    // with glu_n: also store the fp16 pre-activations, gate at pre_gate[r][c] and up at
+    // pre_gate[r][glu_n + c] (row pitch pre_ld)
+    __half* pre_gate = nullptr;
+    long long pre_ld = 0;
+    // SwiGLU backward of dH (fp16 product, N = d_ff): out receives d gate and dglu_up d up
+    // (both row pitch ldc), from gate / up at dglu_gu[r][c] / dglu_gu[r][N + c] (pitch dglu_ld)
+    const __half* dglu_gu = nullptr;
+    long long dglu_ld = 0;
+    __half* dglu_up = nullptr;
 };
 
 inline int sm_count() {
@@ -497,7 +506,7 @@ inline void set_dynamic_smem(int bytes) {
 
 template <int BN, int STAGES>
 inline void launch_gemm_bn(Context& cx, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
-                           const GemmArgs& ga) {
+                           const CUtensorMap& td, const CUtensorMap& te, const GemmArgs& ga) {
     using C = GemmCfg<BN, STAGES>;
     set_dynamic_smem<gemm_tc_kernel<BN, STAGES>>(C::SMEM);
     const long long num_k = (ga.K + kGemmBK - 1) / kGemmBK;
@@ -509,7 +518,7 @@ inline void launch_gemm_bn(Context& cx, const CUtensorMap& ta, const CUtensorMap
     const int per_sm = std::max(1, std::min(512 / (2 * BN), (227 * 1024) / C::SMEM));
     dim3 grid(static_cast<unsigned>(std::min<long long>(tiles, static_cast<long long>(sm_count()) * per_sm)));
     cudaEvent_t t0 = cx.prof_begin();
-    launch_k(cx.stream, gemm_tc_kernel<BN, STAGES>, grid, dim3(C::THREADS), C::SMEM, ta, tb, tc, ga);
+    launch_k(cx.stream, gemm_tc_kernel<BN, STAGES>, grid, dim3(C::THREADS), C::SMEM, ta, tb, tc, td, te, ga);
     const double flops = 2.0 * ga.M * static_cast<double>(ga.N) * ga.K;
     if (t0) {
         char key[96];

@@ -31,6 +31,11 @@ inline int gemm(Context& cx, int M, int N, int K, Opnd A, Opnd B, const GemmOutS
         fail(MM_INVALID_ARGUMENT, "RoPE epilogue needs a plain fp16 product");
     if (o.glu_n && (o.kind != kOutF16 || o.residual || o.lse_part || !B.mn || o.glu_n < N))
         fail(MM_INVALID_ARGUMENT, "SwiGLU epilogue needs an fp16 product with [gate | up] MN-major weights");
+    if (o.pre_gate && (!o.glu_n || o.glu_n != N || N % 8 || o.pre_ld % 8 || o.pre_ld < 2 * N))
+        fail(MM_INVALID_ARGUMENT, "pre-activation stores need the SwiGLU epilogue over all d_ff columns");
+    if (o.dglu_gu && (o.kind != kOutF16 || o.residual || o.lse_part || o.glu_n || o.rope_cos || !o.dglu_up ||
+                      N % 8 || o.ldc % 8 || o.dglu_ld % 8 || o.dglu_ld < 2 * N))
+        fail(MM_INVALID_ARGUMENT, "SwiGLU-backward epilogue needs a plain fp16 product, N % 8 == 0");
     if (o.residual) {
         // out = alpha * A B + residual  ==  out := residual, then out += alpha * A B through the
         // TMA reduce-add epilogue (the residual moves as one coalesced device copy).
@@ -64,7 +69,8 @@ inline int gemm(Context& cx, int M, int N, int K, Opnd A, Opnd B, const GemmOutS
     GemmArgs ga{M, N, K, A.mn ? 1 : 0, B.mn ? 1 : 0, bf16 ? 1 : 0, o.kind,
                 o.residual, o.ldr, o.alpha, o.alpha_ptr, cx.d_err, 0, 0,
                 o.lse_part, o.targets, o.tgt_logit, (o.lse_part && o.no_store) ? 1 : 0, o.glu_n,
-                o.rope_cos, o.rope_sin, o.rope_seq, o.rope_period, o.rope_begin, o.rope_len};
+                o.rope_cos, o.rope_sin, o.rope_seq, o.rope_period, o.rope_begin, o.rope_len,
+                o.pre_gate ? 1 : 0, o.dglu_gu, o.dglu_ld, o.dglu_gu ? N : 0};
     // Split-K for accumulating products with few output tiles over a long K (the weight
     // gradients, K = tokens): each K slice stores its fp32 partial, then one reduction adds
     // them in order into the destination.
@@ -110,13 +116,22 @@ inline int gemm(Context& cx, int M, int N, int K, Opnd A, Opnd B, const GemmOutS
     // A grid that fits one wave (the decode-time products, M = batch) has each CTA's whole
     // K loop on the critical path: a deeper TMA ring keeps more of it in flight.
     const bool one_wave = tiles * splits <= sm_count();
-    if (BN == 256) launch_gemm_bn<256, 4>(cx, ta, tb, *tc, ga);
+    // auxiliary fp16 outputs of the SwiGLU epilogues: 64-column x 32-row boxes like tc
+    const CUtensorMap* td = tc;
+    const CUtensorMap* te = tc;
+    if (o.pre_gate) {
+        td = &tensor_map_t(o.pre_gate, kMapF16, N, M, o.pre_ld, 64, 32);
+        te = &tensor_map_t(o.pre_gate + o.glu_n, kMapF16, N, M, o.pre_ld, 64, 32);
+    } else if (o.dglu_gu) {
+        td = &tensor_map_t(o.dglu_up, kMapF16, N, M, o.ldc, 64, 32);
+    }
+    if (BN == 256) launch_gemm_bn<256, 4>(cx, ta, tb, *tc, *td, *te, ga);
     else if (BN == 128) {
-        if (one_wave && num_k > 3) launch_gemm_bn<128, 6>(cx, ta, tb, *tc, ga);
-        else launch_gemm_bn<128, 3>(cx, ta, tb, *tc, ga);
+        if (one_wave && num_k > 3) launch_gemm_bn<128, 6>(cx, ta, tb, *tc, *td, *te, ga);
+        else launch_gemm_bn<128, 3>(cx, ta, tb, *tc, *td, *te, ga);
     } else {
-        if (one_wave && num_k > 4) launch_gemm_bn<64, 8>(cx, ta, tb, *tc, ga);
-        else launch_gemm_bn<64, 4>(cx, ta, tb, *tc, ga);
+        if (one_wave && num_k > 4) launch_gemm_bn<64, 8>(cx, ta, tb, *tc, *td, *te, ga);
+        else launch_gemm_bn<64, 4>(cx, ta, tb, *tc, *td, *te, ga);
     }
     if (splits > 1) {
         // partial of split z, row r: part[(z * Mp + r) * n_pad + c]; reduce over a dense view

@@ -22,7 +22,9 @@ from tests.gpu_util import ROOT, rel, require_gpu
 
 pytestmark = pytest.mark.gpu
 
-B, S = 4, 264  # query tiles of 128, 128 and 8 rows; M = 1,056 rows (9 row tiles, ragged)
+# query tiles of 128, 128 and 8 rows; M = 4,224 rows: 33 row tiles, enough for the 256-wide
+# tiles the full-size chunks use (the last tile of d_ff = 1,360 is 80 columns wide)
+B, S = 16, 264
 
 _RUN = textwrap.dedent("""
     import sys

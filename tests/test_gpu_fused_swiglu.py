@@ -88,7 +88,8 @@ def test_tape_pass_log_probs_equal_pass_without_tape():
     ref.close()
     assert r["kl"] == 0.0, r["kl"]
     adv = np.concatenate([O.group_advantages(rewards[g:g + G]) for g in range(0, n, G)])
-    want, kl, _ = O.grpo_coefficients(old, old, old, mask, adv, 0.2, 0.04)
+    o2 = np.asarray(old, np.float32).reshape(n, S2)
+    want, kl, _ = O.grpo_coefficients(o2, o2, o2, mask, adv, 0.2, 0.04)
     assert kl == 0.0
     # advantages in float on both sides, sums in double in different orders
     assert abs(r["loss"] - want) <= 1e-6 * max(1.0, abs(want)), (r["loss"], want)

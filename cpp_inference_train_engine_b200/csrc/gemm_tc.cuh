@@ -103,7 +103,6 @@ constexpr int kGemmBK = 64;
 // one per quadrant for the narrower tiles (two CTAs per SM). Each owns one 32-row x
 // 128-byte staging tile.
 template <int BN> constexpr int epi_warps() { return BN == 256 ? 8 : 4; }
-template <int BN> constexpr int epi_bufs() { return 1; }
 
 template <int BN, int STAGES> struct GemmCfg {
     static constexpr int A_BYTES = kGemmBM * 128;
@@ -111,10 +110,262 @@ template <int BN, int STAGES> struct GemmCfg {
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int EPI_WARPS = epi_warps<BN>();
     static constexpr int THREADS = 64 + 32 * EPI_WARPS;
-    static constexpr int EPI_BUFS = epi_bufs<BN>();
-    static constexpr int EPI_BYTES = EPI_WARPS * EPI_BUFS * 4096;
+    static constexpr int EPI_BYTES = EPI_WARPS * 4096;
     static constexpr int SMEM = STAGES * STAGE_BYTES + EPI_BYTES + 1024 + 256;
 };
+
+// Drains one finished accumulator tile (tensor memory columns from `src`, which already
+// points at this warp's lane quadrant q) into global memory: the warp takes column chunks
+// half, half + nhalf, ... of CH columns. Right after its last read of the accumulator the
+// warp arrives on the mbarrier at shared::cluster address `release_bar` (the MMA issuer's
+// "accumulator free" barrier, possibly in the peer CTA).
+__device__ __forceinline__ void gemm_release_acc(uint32_t release_bar, int lane) {
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive_cluster(release_bar);
+}
+template <int BN, int EPI_WARPS>
+__device__ __forceinline__ void gemm_drain_tile(const GemmArgs g, const CUtensorMap& tmC, const CUtensorMap& tmD,
+                                                const CUtensorMap& tmE, uint8_t* stage_base, uint32_t src, int m0,
+                                                int n0, int map_row0, int q, int half, int lane, float alpha,
+                                                uint32_t release_bar) {
+    constexpr int nhalf = EPI_WARPS / 4;  // warps per quadrant
+    const bool half_out = g.out_kind >= kOutF16;
+    const int CH = half_out ? 64 : 32;  // columns per 128-byte staged row
+    const int TW = g.glu_n ? BN / 2 : BN;
+    const int n_mma = min(BN, ((g.N - n0) + 15) / 16 * 16);
+    const int row0 = m0 + q * 32;
+    const int row = row0 + lane;
+    if (g.glu_n) {
+        // accumulator columns [0, TW) gate, [TW, 2 TW) up; 64 fp16 outputs per staged row
+        if (half * 64 >= TW) {  // no chunk for this warp: release the accumulator
+            gemm_release_acc(release_bar, lane);
+        }
+        for (int c = half * 64; c < TW; c += 64 * nhalf) {
+            if (g.glu_pre) {
+                // the fp16 pre-activations first: gate columns, then up columns, each
+                // read from tensor memory into the warp's staging tile
+#pragma unroll 1
+                for (int part = 0; part < 2; ++part) {
+                    if (lane == 0) bulk_wait_read0();
+                    __syncwarp();
+                    uint8_t* rowp = stage_base + lane * 128;
+#pragma unroll
+                    for (int sub = 0; sub < 2; ++sub) {
+                        float t[32];
+                        tmem_ld32_nowait(src + static_cast<uint32_t>(part * TW + c + 32 * sub), t);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int ch = 0; ch < 4; ++ch) {
+                            const float* f = t + 8 * ch;
+                            const int cc = sub * 4 + ch;
+                            *reinterpret_cast<uint4*>(rowp + ((cc ^ (lane & 7)) << 4)) =
+                                make_uint4(pack_half2(f[0] * alpha, f[1] * alpha), pack_half2(f[2] * alpha, f[3] * alpha),
+                                           pack_half2(f[4] * alpha, f[5] * alpha), pack_half2(f[6] * alpha, f[7] * alpha));
+                        }
+                    }
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_2d(part ? &tmE : &tmD, stage_base, n0 + c, map_row0);
+                        bulk_commit();
+                    }
+                }
+            }
+            uint8_t* stage = stage_base;
+            if (lane == 0) bulk_wait_read0();  // the store that last read `stage` is done
+            __syncwarp();
+            uint8_t* rowp = stage + lane * 128;
+#pragma unroll
+            for (int sub = 0; sub < 2; ++sub) {
+                float gv[32], uv[32];
+                tmem_ld32_nowait(src + static_cast<uint32_t>(c + 32 * sub), gv);
+                tmem_ld32_nowait(src + static_cast<uint32_t>(TW + c + 32 * sub), uv);
+                tmem_wait_ld();
+                if (sub == 1 && c + 64 * nhalf >= TW) {
+                    gemm_release_acc(release_bar, lane);
+                }
+#pragma unroll
+                for (int ch = 0; ch < 4; ++ch) {
+                    uint32_t w[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const int i = ch * 8 + 2 * e;
+                        // g * sigmoid(g) = g / (1 + e^-g), branch-free on the SFU
+                        // (the result is rounded to fp16)
+                        const float ga = gv[i] * alpha, gb = gv[i + 1] * alpha;
+                        const float a = __fdividef(ga, 1.f + __expf(-ga)) * (uv[i] * alpha);
+                        const float b = __fdividef(gb, 1.f + __expf(-gb)) * (uv[i + 1] * alpha);
+                        w[e] = pack_half2(a, b);
+                    }
+                    const int cc = sub * 4 + ch;
+                    *reinterpret_cast<uint4*>(rowp + ((cc ^ (lane & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+                }
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                tma_store_2d(&tmC, stage, n0 + c, map_row0);
+                bulk_commit();
+            }
+        }
+        return;
+    }
+    // online (max, sum of exp) over this tile's columns of the row, and its target
+    float run_m = -INFINITY, run_s = 0.f, run_t = 0.f;
+    const int tg = (g.lse_part && row < g.M) ? static_cast<int>(g.targets[row]) : -1;
+    if (half * CH >= n_mma) {  // no chunk for this warp: release the accumulator
+        gemm_release_acc(release_bar, lane);
+    }
+    for (int c = half * CH; c < n_mma; c += CH * nhalf) {
+        if (g.dglu_n) {
+            // SwiGLU backward of dH columns [col0, col0 + 64) of this row, 32 at a time from
+            // tensor memory; x = gate, u = up from the forward: d gate = dh u s (1 + x (1 - s)),
+            // d up = dh x s, s = sigmoid(x). d gate goes straight into the staging tile, d up
+            // waits packed until that tile is stored.
+            const int col0 = n0 + c;
+            const __half* gr = g.dglu_gu + static_cast<long long>(row < g.M ? row : 0) * g.dglu_ld;
+            uint32_t du[32];
+            if (lane == 0) bulk_wait_read0();
+            __syncwarp();
+            uint8_t* rowp = stage_base + lane * 128;
+#pragma unroll
+            for (int hf = 0; hf < 2; ++hf) {
+                float t[32];
+                tmem_ld32_nowait(src + static_cast<uint32_t>(c + 32 * hf), t);
+                tmem_wait_ld();
+                if (hf == 1 && c + CH * nhalf >= n_mma) gemm_release_acc(release_bar, lane);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    // 8 columns at a time; the barrier keeps the next group's loads behind this
+                    // group's math (registers)
+                    asm volatile("" ::: "memory");
+                    const int col = col0 + 32 * hf + 8 * j;
+                    const bool in = row < g.M && col < g.N;  // N % 8 == 0
+                    const uint4 xq = in ? *reinterpret_cast<const uint4*>(gr + col) : make_uint4(0, 0, 0, 0);
+                    const uint4 uq = in ? *reinterpret_cast<const uint4*>(gr + g.dglu_n + col) : make_uint4(0, 0, 0, 0);
+                    const uint32_t xw[4] = {xq.x, xq.y, xq.z, xq.w};
+                    const uint32_t uw[4] = {uq.x, uq.y, uq.z, uq.w};
+                    uint32_t da[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const float x0 = __half2float(__ushort_as_half(static_cast<unsigned short>(xw[e] & 0xFFFFu)));
+                        const float x1 = __half2float(__ushort_as_half(static_cast<unsigned short>(xw[e] >> 16)));
+                        const float u0 = __half2float(__ushort_as_half(static_cast<unsigned short>(uw[e] & 0xFFFFu)));
+                        const float u1 = __half2float(__ushort_as_half(static_cast<unsigned short>(uw[e] >> 16)));
+                        const float d0 = t[8 * j + 2 * e] * alpha, d1 = t[8 * j + 2 * e + 1] * alpha;
+                        // sigmoid on the SFU (the results are rounded to fp16)
+                        const float s0 = __fdividef(1.f, 1.f + __expf(-x0));
+                        const float s1 = __fdividef(1.f, 1.f + __expf(-x1));
+                        da[e] = pack_half2(d0 * u0 * (s0 + x0 * s0 * (1.f - s0)), d1 * u1 * (s1 + x1 * s1 * (1.f - s1)));
+                        du[16 * hf + 4 * j + e] = pack_half2(d0 * x0 * s0, d1 * x1 * s1);
+                    }
+                    const int cc = 4 * hf + j;
+                    *reinterpret_cast<uint4*>(rowp + ((cc ^ (lane & 7)) << 4)) = make_uint4(da[0], da[1], da[2], da[3]);
+                }
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                tma_store_2d(&tmC, stage_base, col0, map_row0);
+                bulk_commit();
+            }
+            stage_and_store(stage_base, lane, du, &tmD, col0, map_row0);
+            continue;
+        }
+        float v[64];
+        tmem_ld32_nowait(src + static_cast<uint32_t>(c), v);
+        if (half_out) tmem_ld32_nowait(src + static_cast<uint32_t>(c + 32), v + 32);
+        tmem_wait_ld();
+        if (c + CH * nhalf >= n_mma) {
+            // last read of this accumulator: hand it back to the MMA warp first
+            gemm_release_acc(release_bar, lane);
+        }
+        const int col0 = n0 + c;
+#pragma unroll
+        for (int i = 0; i < 64; ++i) v[i] *= alpha;
+        if (g.residual && row < g.M) {
+            const float* r = g.residual + static_cast<long long>(row) * g.ldr + col0;
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+                if (col0 + i < g.N) v[i] += r[i];
+        }
+        if (g.lse_part) {  // fp32 output: 32 columns per chunk
+            float cm = -INFINITY;
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+                if (col0 + i < g.N) cm = fmaxf(cm, v[i]);
+            const float nm = fmaxf(run_m, cm);  // finite: every chunk holds a column < N
+            float add = 0.f;
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+                if (col0 + i < g.N) add += __expf(v[i] - nm);
+            run_s = (run_m == -INFINITY ? 0.f : run_s * __expf(run_m - nm)) + add;
+            run_m = nm;
+            const int rel = tg - col0;
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+                if (rel == i) run_t = v[i];
+            if (g.no_store) continue;
+        }
+        // the store issued last (from this staging tile) has finished reading it
+        uint8_t* stage = stage_base;
+        if (lane == 0) bulk_wait_read0();
+        __syncwarp();
+        uint8_t* rowp = stage + lane * 128;
+        if (half_out && g.rope_cos && row < g.M) {
+            const int p = row % g.rope_seq, hr = g.rope_len >> 1;
+#pragma unroll
+            for (int i = 0; i < 64; i += 2) {
+                const int cc = (col0 + i) % g.rope_period - g.rope_begin;
+                if (cc >= 0 && cc < g.rope_len) {
+                    const float cs = g.rope_cos[p * hr + (cc >> 1)], sn = g.rope_sin[p * hr + (cc >> 1)];
+                    const float a = v[i], bb = v[i + 1];
+                    v[i] = a * cs - bb * sn;
+                    v[i + 1] = a * sn + bb * cs;
+                }
+            }
+        }
+        if (half_out) {
+#pragma unroll
+            for (int ch = 0; ch < 8; ++ch) {
+                uint32_t w[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float a = v[ch * 8 + 2 * e], b = v[ch * 8 + 2 * e + 1];
+                    if (g.out_kind == kOutF16) {
+                        const __half2 h = __floats2half2_rn(a, b);
+                        w[e] = *reinterpret_cast<const uint32_t*>(&h);
+                    } else {
+                        const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+                        w[e] = *reinterpret_cast<const uint32_t*>(&h);
+                    }
+                }
+                *reinterpret_cast<uint4*>(rowp + ((ch ^ (lane & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+        } else {
+#pragma unroll
+            for (int ch = 0; ch < 8; ++ch)
+                *reinterpret_cast<float4*>(rowp + ((ch ^ (lane & 7)) << 4)) =
+                    make_float4(v[4 * ch], v[4 * ch + 1], v[4 * ch + 2], v[4 * ch + 3]);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+            if (g.out_kind == kOutF32Acc) tma_reduce_add_2d(&tmC, stage, col0, map_row0);
+            else tma_store_2d(&tmC, stage, col0, map_row0);
+            bulk_commit();
+        }
+    }
+    if (g.lse_part && row < g.M) {
+        // one partial per tile and quadrant warp: [n_tile * 2 + half][row]
+        g.lse_part[static_cast<long long>((n0 / BN) * 2 + half) * g.M + row] = make_float2(run_m, run_s);
+        if (nhalf == 1)  // one warp per quadrant: the second slot holds nothing
+            g.lse_part[static_cast<long long>((n0 / BN) * 2 + 1) * g.M + row] = make_float2(-INFINITY, 0.f);
+        const int rel = tg - n0;  // the warp whose chunks hold the target column writes it
+        if (rel >= 0 && rel < n_mma && ((rel / CH) % nhalf) == half) g.tgt_logit[row] = run_t;
+    }
+}
 
 template <int BN, int STAGES>
 __global__ void __launch_bounds__(320, 1)
@@ -232,262 +483,21 @@ __global__ void __launch_bounds__(320, 1)
             tc_commit(&acc_full[buf]);
         }
     } else if (warp >= 2) {
-        const int q = warp & 3;              // TMEM lane quadrant of this warp
-        const int half = (warp - 2) >> 2;    // which of the quadrant's warps (0 or 1)
-        const int nhalf = C::EPI_WARPS / 4;  // warps per quadrant
-        uint8_t* stage_base = epi + (warp - 2) * C::EPI_BUFS * 4096;
-        int sbuf = 0;  // staging tile the next chunk fills
+        const int q = warp & 3;            // TMEM lane quadrant of this warp
+        const int half = (warp - 2) >> 2;  // which of the quadrant's warps (0 or 1)
+        uint8_t* stage_base = epi + (warp - 2) * 4096;
         const float alpha = g.alpha * (g.alpha_ptr ? *g.alpha_ptr : 1.0f);
-        const bool half_out = g.out_kind >= kOutF16;
-        const int CH = half_out ? 64 : 32;  // columns per 128-byte staged row
         int j = 0;
         for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++j) {
             const int z = tile / (tiles_n * tiles_m), mn = tile % (tiles_n * tiles_m);
             const int m0 = (mn / tiles_n) * kGemmBM, n0 = (mn % tiles_n) * TW;
-            const int n_mma = min(BN, ((g.N - n0) + 15) / 16 * 16);
             const int buf = j & 1;
             if (!mbar_wait_bounded(&acc_full[buf], (j >> 1) & 1, g.err)) break;
             tc_fence_after();
-            const int row0 = m0 + q * 32;
-            const int row = row0 + lane;
-            const int map_row0 = row0 + (g.k_tiles_per_split > 0 ? z * g.split_rows : 0);
+            const int map_row0 = m0 + q * 32 + (g.k_tiles_per_split > 0 ? z * g.split_rows : 0);
             const uint32_t src = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * BN);
-            if (g.glu_n) {
-                // accumulator columns [0, TW) gate, [TW, 2 TW) up; 64 fp16 outputs per staged row
-                if (half * 64 >= TW) {  // no chunk for this warp: release the accumulator
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&acc_empty[buf]);
-                }
-                for (int c = half * 64; c < TW; c += 64 * nhalf) {
-                    if (g.glu_pre) {
-                        // the fp16 pre-activations first: gate columns, then up columns, each
-                        // read from tensor memory into the warp's staging tile
-#pragma unroll 1
-                        for (int part = 0; part < 2; ++part) {
-                            if (lane == 0) bulk_wait_read0();
-                            __syncwarp();
-                            uint8_t* rowp = stage_base + lane * 128;
-#pragma unroll
-                            for (int sub = 0; sub < 2; ++sub) {
-                                float t[32];
-                                tmem_ld32_nowait(src + static_cast<uint32_t>(part * TW + c + 32 * sub), t);
-                                tmem_wait_ld();
-#pragma unroll
-                                for (int ch = 0; ch < 4; ++ch) {
-                                    const float* f = t + 8 * ch;
-                                    const int cc = sub * 4 + ch;
-                                    *reinterpret_cast<uint4*>(rowp + ((cc ^ (lane & 7)) << 4)) =
-                                        make_uint4(pack_half2(f[0] * alpha, f[1] * alpha), pack_half2(f[2] * alpha, f[3] * alpha),
-                                                   pack_half2(f[4] * alpha, f[5] * alpha), pack_half2(f[6] * alpha, f[7] * alpha));
-                                }
-                            }
-                            fence_proxy_async_smem();
-                            __syncwarp();
-                            if (lane == 0) {
-                                tma_store_2d(part ? &tmE : &tmD, stage_base, n0 + c, map_row0);
-                                bulk_commit();
-                            }
-                        }
-                    }
-                    uint8_t* stage = stage_base + sbuf * 4096;
-                    if (C::EPI_BUFS == 2) sbuf ^= 1;
-                    if (lane == 0) {  // the store that last read `stage` is done
-                        if (C::EPI_BUFS == 2) bulk_wait_read1();
-                        else bulk_wait_read0();
-                    }
-                    __syncwarp();
-                    uint8_t* rowp = stage + lane * 128;
-#pragma unroll
-                    for (int sub = 0; sub < 2; ++sub) {
-                        float gv[32], uv[32];
-                        tmem_ld32_nowait(src + static_cast<uint32_t>(c + 32 * sub), gv);
-                        tmem_ld32_nowait(src + static_cast<uint32_t>(TW + c + 32 * sub), uv);
-                        tmem_wait_ld();
-                        if (sub == 1 && c + 64 * nhalf >= TW) {
-                            tc_fence_before();
-                            __syncwarp();
-                            if (lane == 0) mbar_arrive(&acc_empty[buf]);
-                        }
-#pragma unroll
-                        for (int ch = 0; ch < 4; ++ch) {
-                            uint32_t w[4];
-#pragma unroll
-                            for (int e = 0; e < 4; ++e) {
-                                const int i = ch * 8 + 2 * e;
-                                // g * sigmoid(g) = g / (1 + e^-g), branch-free on the SFU
-                                // (the result is rounded to fp16)
-                                const float ga = gv[i] * alpha, gb = gv[i + 1] * alpha;
-                                const float a = __fdividef(ga, 1.f + __expf(-ga)) * (uv[i] * alpha);
-                                const float b = __fdividef(gb, 1.f + __expf(-gb)) * (uv[i + 1] * alpha);
-                                w[e] = pack_half2(a, b);
-                            }
-                            const int cc = sub * 4 + ch;
-                            *reinterpret_cast<uint4*>(rowp + ((cc ^ (lane & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
-                        }
-                    }
-                    fence_proxy_async_smem();
-                    __syncwarp();
-                    if (lane == 0) {
-                        tma_store_2d(&tmC, stage, n0 + c, map_row0);
-                        bulk_commit();
-                    }
-                }
-                continue;
-            }
-            // online (max, sum of exp) over this tile's columns of the row, and its target
-            float run_m = -INFINITY, run_s = 0.f, run_t = 0.f;
-            const int tg = (g.lse_part && row < g.M) ? static_cast<int>(g.targets[row]) : -1;
-            if (half * CH >= n_mma) {  // no chunk for this warp: release the accumulator
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&acc_empty[buf]);
-            }
-            for (int c = half * CH; c < n_mma; c += CH * nhalf) {
-                float v[64];
-                tmem_ld32_nowait(src + static_cast<uint32_t>(c), v);
-                if (half_out) tmem_ld32_nowait(src + static_cast<uint32_t>(c + 32), v + 32);
-                tmem_wait_ld();
-                if (c + CH * nhalf >= n_mma) {
-                    // last read of this accumulator: hand it back to the MMA warp first
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&acc_empty[buf]);
-                }
-                const int col0 = n0 + c;
-#pragma unroll
-                for (int i = 0; i < 64; ++i) v[i] *= alpha;
-                if (g.residual && row < g.M) {
-                    const float* r = g.residual + static_cast<long long>(row) * g.ldr + col0;
-#pragma unroll
-                    for (int i = 0; i < 32; ++i)
-                        if (col0 + i < g.N) v[i] += r[i];
-                }
-                if (g.dglu_n) {
-                    // v = dh of columns [col0, col0 + 64) of this row; x = gate, u = up from the
-                    // forward: d gate = dh u s (1 + x (1 - s)), d up = dh x s, s = sigmoid(x).
-                    // d gate goes straight into the staging tile, d up waits packed for it.
-                    const __half* gr = g.dglu_gu + static_cast<long long>(row < g.M ? row : 0) * g.dglu_ld;
-                    uint32_t du[32];
-                    if (lane == 0) bulk_wait_read0();
-                    __syncwarp();
-                    uint8_t* rowp = stage_base + lane * 128;
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        // 8 columns at a time; the barrier keeps the next group's loads behind
-                        // this group's math (registers)
-                        if (j) asm volatile("" ::: "memory");
-                        const int col = col0 + 8 * j;
-                        const bool in = row < g.M && col < g.N;  // N % 8 == 0
-                        const uint4 xq = in ? *reinterpret_cast<const uint4*>(gr + col) : make_uint4(0, 0, 0, 0);
-                        const uint4 uq = in ? *reinterpret_cast<const uint4*>(gr + g.dglu_n + col) : make_uint4(0, 0, 0, 0);
-                        const uint32_t xw[4] = {xq.x, xq.y, xq.z, xq.w};
-                        const uint32_t uw[4] = {uq.x, uq.y, uq.z, uq.w};
-                        uint32_t da[4];
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const float x0 = __half2float(__ushort_as_half(static_cast<unsigned short>(xw[e] & 0xFFFFu)));
-                            const float x1 = __half2float(__ushort_as_half(static_cast<unsigned short>(xw[e] >> 16)));
-                            const float u0 = __half2float(__ushort_as_half(static_cast<unsigned short>(uw[e] & 0xFFFFu)));
-                            const float u1 = __half2float(__ushort_as_half(static_cast<unsigned short>(uw[e] >> 16)));
-                            const int i = 8 * j + 2 * e;
-                            // sigmoid on the SFU (the results are rounded to fp16)
-                            const float s0 = __fdividef(1.f, 1.f + __expf(-x0));
-                            const float s1 = __fdividef(1.f, 1.f + __expf(-x1));
-                            da[e] = pack_half2(v[i] * u0 * (s0 + x0 * s0 * (1.f - s0)),
-                                               v[i + 1] * u1 * (s1 + x1 * s1 * (1.f - s1)));
-                            du[4 * j + e] = pack_half2(v[i] * x0 * s0, v[i + 1] * x1 * s1);
-                        }
-                        *reinterpret_cast<uint4*>(rowp + ((j ^ (lane & 7)) << 4)) = make_uint4(da[0], da[1], da[2], da[3]);
-                    }
-                    fence_proxy_async_smem();
-                    __syncwarp();
-                    if (lane == 0) {
-                        tma_store_2d(&tmC, stage_base, col0, map_row0);
-                        bulk_commit();
-                    }
-                    stage_and_store(stage_base, lane, du, &tmD, col0, map_row0);
-                    continue;
-                }
-                if (g.lse_part) {  // fp32 output: 32 columns per chunk
-                    float cm = -INFINITY;
-#pragma unroll
-                    for (int i = 0; i < 32; ++i)
-                        if (col0 + i < g.N) cm = fmaxf(cm, v[i]);
-                    const float nm = fmaxf(run_m, cm);  // finite: every chunk holds a column < N
-                    float add = 0.f;
-#pragma unroll
-                    for (int i = 0; i < 32; ++i)
-                        if (col0 + i < g.N) add += __expf(v[i] - nm);
-                    run_s = (run_m == -INFINITY ? 0.f : run_s * __expf(run_m - nm)) + add;
-                    run_m = nm;
-                    const int rel = tg - col0;
-#pragma unroll
-                    for (int i = 0; i < 32; ++i)
-                        if (rel == i) run_t = v[i];
-                    if (g.no_store) continue;
-                }
-                // the store issued two chunks ago (from this staging tile) has finished reading it
-                uint8_t* stage = stage_base + sbuf * 4096;
-                if (C::EPI_BUFS == 2) sbuf ^= 1;
-                if (lane == 0) {
-                    if (C::EPI_BUFS == 2) bulk_wait_read1();
-                    else bulk_wait_read0();
-                }
-                __syncwarp();
-                uint8_t* rowp = stage + lane * 128;
-                if (half_out && g.rope_cos && row < g.M) {
-                    const int p = row % g.rope_seq, hr = g.rope_len >> 1;
-#pragma unroll
-                    for (int i = 0; i < 64; i += 2) {
-                        const int cc = (col0 + i) % g.rope_period - g.rope_begin;
-                        if (cc >= 0 && cc < g.rope_len) {
-                            const float cs = g.rope_cos[p * hr + (cc >> 1)], sn = g.rope_sin[p * hr + (cc >> 1)];
-                            const float a = v[i], bb = v[i + 1];
-                            v[i] = a * cs - bb * sn;
-                            v[i + 1] = a * sn + bb * cs;
-                        }
-                    }
-                }
-                if (half_out) {
-#pragma unroll
-                    for (int ch = 0; ch < 8; ++ch) {
-                        uint32_t w[4];
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const float a = v[ch * 8 + 2 * e], b = v[ch * 8 + 2 * e + 1];
-                            if (g.out_kind == kOutF16) {
-                                const __half2 h = __floats2half2_rn(a, b);
-                                w[e] = *reinterpret_cast<const uint32_t*>(&h);
-                            } else {
-                                const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
-                                w[e] = *reinterpret_cast<const uint32_t*>(&h);
-                            }
-                        }
-                        *reinterpret_cast<uint4*>(rowp + ((ch ^ (lane & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
-                    }
-                } else {
-#pragma unroll
-                    for (int ch = 0; ch < 8; ++ch)
-                        *reinterpret_cast<float4*>(rowp + ((ch ^ (lane & 7)) << 4)) =
-                            make_float4(v[4 * ch], v[4 * ch + 1], v[4 * ch + 2], v[4 * ch + 3]);
-                }
-                fence_proxy_async_smem();
-                __syncwarp();
-                if (lane == 0) {
-                    if (g.out_kind == kOutF32Acc) tma_reduce_add_2d(&tmC, stage, col0, map_row0);
-                    else tma_store_2d(&tmC, stage, col0, map_row0);
-                    bulk_commit();
-                }
-            }
-            if (g.lse_part && row < g.M) {
-                // one partial per tile and quadrant warp: [n_tile * 2 + half][row]
-                g.lse_part[static_cast<long long>((n0 / BN) * 2 + half) * g.M + row] = make_float2(run_m, run_s);
-                if (nhalf == 1)  // one warp per quadrant: the second slot holds nothing
-                    g.lse_part[static_cast<long long>((n0 / BN) * 2 + 1) * g.M + row] = make_float2(-INFINITY, 0.f);
-                const int rel = tg - n0;  // the warp whose chunks hold the target column writes it
-                if (rel >= 0 && rel < n_mma && ((rel / CH) % nhalf) == half) g.tgt_logit[row] = run_t;
-            }
+            gemm_drain_tile<BN, C::EPI_WARPS>(g, tmC, tmD, tmE, stage_base, src, m0, n0, map_row0, q, half, lane,
+                                              alpha, smem_u32(&acc_empty[buf]));
         }
         if (lane == 0) bulk_wait0();
         __syncwarp();
@@ -497,6 +507,167 @@ __global__ void __launch_bounds__(320, 1)
     if (warp == 0) {
         tc_fence_after();
         tmem_dealloc(tmem, 2 * BN);
+    }
+}
+
+// ------------------------------------------------------------------ CTA-pair variant
+// The same product on pairs of CTAs (clusters of 2, tcgen05 cta_group::2) for the large
+// 256-wide-tile products: a pair computes a 256-row x 256-column accumulator (TW output
+// columns). CTA r of the pair loads rows [m0 + 128 r, +128) of A and 128 of the tile's B
+// columns (columns [n0 + 128 r, +128); with SwiGLU the gate columns in CTA 0 and the up
+// columns in CTA 1) into its own shared memory; the leader (rank 0) issues one M = 256,
+// N = 256 MMA per 16-deep K step over both CTAs' operands, and each CTA's tensor memory holds
+// its own 128 rows x 256 columns, which its epilogue warps drain exactly as in the
+// single-CTA kernel. Per SM a 64-deep K step moves 32 KB for 128 x 256 outputs (48 KB with
+// one CTA), so a 6-stage ring fits and hides 1.5x the load latency at the same MMA rate.
+// Barriers: full[s] (leader: its producer expects both CTAs' bytes, both CTAs' loads count
+// on it), empty[s] and acc_full[b] (every CTA: the leader's commits are multicast to both),
+// acc_empty[b] (leader: all 16 epilogue warps of the pair arrive). Every wait is bounded;
+// both CTAs always reach the final cluster barrier and free their tensor memory together.
+constexpr int kPairStages = 6;
+struct PairCfg {
+    static constexpr int A_BYTES = kGemmBM * 128;  // 128 rows x 64 K
+    static constexpr int B_BYTES = 128 * 128;      // 128 columns x 64 K
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int EPI_WARPS = 8;
+    static constexpr int THREADS = 64 + 32 * EPI_WARPS;
+    static constexpr int EPI_BYTES = EPI_WARPS * 4096;
+    static constexpr int SMEM = kPairStages * STAGE_BYTES + EPI_BYTES + 1024 + 256;
+};
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
+    gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmD,
+                        const __grid_constant__ CUtensorMap tmE, GemmArgs g) {
+    using C = PairCfg;
+    constexpr int BN = 256;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~static_cast<uintptr_t>(1023));
+    uint8_t* epi = smem + kPairStages * C::STAGE_BYTES;
+    uint64_t* full = reinterpret_cast<uint64_t*>(epi + C::EPI_BYTES);
+    uint64_t* empty = full + kPairStages;
+    uint64_t* acc_full = empty + kPairStages;  // [2] leader's MMAs -> both epilogues
+    uint64_t* acc_empty = acc_full + 2;        // [2] both epilogues -> leader (16 warp arrivals)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const int pair = static_cast<int>(blockIdx.x >> 1), npairs = static_cast<int>(gridDim.x >> 1);
+    const int num_k = (g.K + kGemmBK - 1) / kGemmBK;
+    const int TW = g.glu_n ? BN / 2 : BN;  // output columns per tile
+    const int tiles_n = (g.N + TW - 1) / TW, tiles_m = (g.M + 2 * kGemmBM - 1) / (2 * kGemmBM);
+    const int tiles = tiles_n * tiles_m;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            for (int s = 0; s < kPairStages; ++s) {
+                mbar_init(&full[s], 1);
+                mbar_init(&empty[s], 1);
+            }
+            mbar_init(&acc_full[0], 1);
+            mbar_init(&acc_full[1], 1);
+            mbar_init(&acc_empty[0], 2 * C::EPI_WARPS);
+            mbar_init(&acc_empty[1], 2 * C::EPI_WARPS);
+            fence_mbar_init();
+            prefetch_tmap(&tmA);
+            prefetch_tmap(&tmB);
+            prefetch_tmap(&tmC);
+        }
+        __syncwarp();
+        tmem_alloc_pair(tmem_slot, 2 * BN);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync_all();  // both CTAs' barriers exist before any load or arrive crosses the pair
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    MM_PDL_ENTRY();
+
+    if (warp == 0 && lane == 0) {
+        int it = 0;  // ring position across tiles
+        bool ok = true;
+        for (int tile = pair; tile < tiles && ok; tile += npairs) {
+            const int m0 = (tile / tiles_n) * (2 * kGemmBM) + kGemmBM * static_cast<int>(rank);
+            const int n0 = (tile % tiles_n) * TW;
+            const int nb = g.glu_n ? (rank == 0 ? n0 : g.glu_n + n0) : n0 + 128 * static_cast<int>(rank);
+            for (int kt = 0; kt < num_k; ++kt, ++it) {
+                const int s = it % kPairStages;
+                const uint32_t ph = (it / kPairStages) & 1;
+                if (!mbar_wait_bounded(&empty[s], ph ^ 1, g.err)) { ok = false; break; }
+                uint8_t* sa = smem + s * C::STAGE_BYTES;
+                uint8_t* sb = sa + C::A_BYTES;
+                if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * C::STAGE_BYTES);
+                const uint32_t fb = mapa_shared(smem_u32(&full[s]), 0);
+                const int k0 = kt * kGemmBK;
+                if (!g.a_mn) {
+                    tma_load_2d_pair(sa, &tmA, fb, k0, m0);
+                } else {
+                    tma_load_2d_pair(sa, &tmA, fb, m0, k0);
+                    tma_load_2d_pair(sa + 8192, &tmA, fb, m0 + 64, k0);
+                }
+                if (!g.b_mn) {
+                    tma_load_2d_pair(sb, &tmB, fb, k0, nb);
+                } else {
+                    tma_load_2d_pair(sb, &tmB, fb, nb, k0);
+                    tma_load_2d_pair(sb + 8192, &tmB, fb, nb + 64, k0);
+                }
+            }
+        }
+    } else if (warp == 1 && lane == 0 && rank == 0) {
+        int it = 0, j = 0;
+        bool ok = true;
+        const uint32_t idesc = umma_idesc_f16(g.bf16 != 0, g.a_mn != 0, g.b_mn != 0, 2 * kGemmBM, BN);
+        for (int tile = pair; tile < tiles && ok; tile += npairs, ++j) {
+            const int buf = j & 1;
+            if (!mbar_wait_bounded_cluster(&acc_empty[buf], ((j >> 1) & 1) ^ 1, g.err)) break;
+            tc_fence_after();
+            const uint32_t dst = tmem + static_cast<uint32_t>(buf * BN);
+            for (int kt = 0; kt < num_k; ++kt, ++it) {
+                const int s = it % kPairStages;
+                const uint32_t ph = (it / kPairStages) & 1;
+                if (!mbar_wait_bounded(&full[s], ph, g.err)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t sa = smem_u32(smem + s * C::STAGE_BYTES);
+                const uint32_t sb = sa + C::A_BYTES;
+#pragma unroll
+                for (int k = 0; k < kGemmBK / 16; ++k) {
+                    const uint64_t ad = g.a_mn ? umma_desc_sw128(sa + k * 2048, 8192, 1024)
+                                               : umma_desc_sw128(sa + k * 32, 16, 1024);
+                    const uint64_t bd = g.b_mn ? umma_desc_sw128(sb + k * 2048, 8192, 1024)
+                                               : umma_desc_sw128(sb + k * 32, 16, 1024);
+                    tc_mma_f16_pair(dst, ad, bd, idesc, (kt != 0 || k != 0) ? 1u : 0u);
+                }
+                tc_commit_pair(&empty[s], 0x3);
+            }
+            tc_commit_pair(&acc_full[buf], 0x3);
+        }
+    } else if (warp >= 2) {
+        const int q = warp & 3;            // TMEM lane quadrant of this warp
+        const int half = (warp - 2) >> 2;  // which of the quadrant's warps (0 or 1)
+        uint8_t* stage_base = epi + (warp - 2) * 4096;
+        const float alpha = g.alpha * (g.alpha_ptr ? *g.alpha_ptr : 1.0f);
+        int j = 0;
+        for (int tile = pair; tile < tiles; tile += npairs, ++j) {
+            const int m0 = (tile / tiles_n) * (2 * kGemmBM) + kGemmBM * static_cast<int>(rank);
+            const int n0 = (tile % tiles_n) * TW;
+            const int buf = j & 1;
+            if (!mbar_wait_bounded(&acc_full[buf], (j >> 1) & 1, g.err)) break;
+            tc_fence_after();
+            const uint32_t src = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * BN);
+            gemm_drain_tile<BN, C::EPI_WARPS>(g, tmC, tmD, tmE, stage_base, src, m0, n0, m0 + q * 32, q, half, lane,
+                                              alpha, mapa_shared(smem_u32(&acc_empty[buf]), 0));
+        }
+        if (lane == 0) bulk_wait0();
+        __syncwarp();
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync_all();  // neither CTA leaves while the other may still signal its barriers
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem, 2 * BN);
     }
 }
 

@@ -530,6 +530,55 @@ inline void launch_gemm_bn(Context& cx, const CUtensorMap& ta, const CUtensorMap
     ++cx.launches;
 }
 
+// MM_GEMM_PAIR=0 keeps every product on the single-CTA kernel (for comparison).
+inline bool pair_gemm_enabled() {
+    static const bool on = [] {
+        const char* e = std::getenv("MM_GEMM_PAIR");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
+// CTA pairs of gemm_tc_pair_kernel that can be resident at once on this device (0 when the
+// cluster launch does not fit).
+inline int pair_gemm_slots() {
+    static int slots = -1;
+    if (slots < 0) {
+        set_dynamic_smem<gemm_tc_pair_kernel>(PairCfg::SMEM);
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2 * 74);
+        cfg.blockDim = dim3(PairCfg::THREADS);
+        cfg.dynamicSmemBytes = PairCfg::SMEM;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, gemm_tc_pair_kernel, &cfg) != cudaSuccess) {
+            cudaGetLastError();
+            n = 0;
+        }
+        slots = n;
+    }
+    return slots;
+}
+
+// The CTA-pair product: one persistent cluster per resident pair slot, 256-row tiles.
+inline void launch_gemm_pair(Context& cx, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
+                             const CUtensorMap& td, const CUtensorMap& te, const GemmArgs& ga) {
+    set_dynamic_smem<gemm_tc_pair_kernel>(PairCfg::SMEM);
+    const int tw = ga.glu_n ? 128 : 256;
+    const long long tiles = static_cast<long long>((ga.N + tw - 1) / tw) * ((ga.M + 255) / 256);
+    dim3 grid(static_cast<unsigned>(2 * std::min<long long>(tiles, pair_gemm_slots())));
+    cudaEvent_t t0 = cx.prof_begin();
+    launch_k(cx.stream, gemm_tc_pair_kernel, grid, dim3(PairCfg::THREADS), PairCfg::SMEM, ta, tb, tc, td, te, ga);
+    const double flops = 2.0 * ga.M * static_cast<double>(ga.N) * ga.K;
+    if (t0) {
+        char key[96];
+        std::snprintf(key, sizeof key, "M%d N%d K%d a%s b%s pair out%d", ga.M, ga.N, ga.K, ga.a_mn ? "mn" : "k",
+                      ga.b_mn ? "mn" : "k", ga.out_kind);
+        cx.prof_shape(key, t0, flops);
+    }
+    cx.prof_end(kKGemm, t0, flops);
+    ++cx.launches;
+}
+
 // D[M,N] = alpha * A * B (+ residual | += D). bf16 selects bf16 operands.
 int gemm(Context& cx, int M, int N, int K, Opnd A, Opnd B, const GemmOutSpec& o, bool bf16 = false);
 

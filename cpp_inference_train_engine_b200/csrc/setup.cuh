@@ -125,7 +125,13 @@ inline int gemm(Context& cx, int M, int N, int K, Opnd A, Opnd B, const GemmOutS
     } else if (o.dglu_gu) {
         td = &tensor_map_t(o.dglu_up, kMapF16, N, M, o.ldc, 64, 32);
     }
-    if (BN == 256) launch_gemm_bn<256, 4>(cx, ta, tb, *tc, *td, *te, ga);
+    // Large 256-wide products run on CTA pairs: at least one full wave of 256 x 256 tiles.
+    const long long pair_tiles = static_cast<long long>((M + 255) / 256) * ((N + (o.glu_n ? 127 : 255)) / (o.glu_n ? 128 : 256));
+    if (BN == 256 && splits == 1 && pair_gemm_enabled() && pair_gemm_slots() > 0 && pair_tiles >= pair_gemm_slots()) {
+        // the B tile of each CTA is 128 columns: K-major B boxes are 128 rows high
+        const CUtensorMap& tb2 = B.mn ? tb : tensor_map(B.p, bf16, K, nb, B.ld, 64, 128);
+        launch_gemm_pair(cx, ta, tb2, *tc, *td, *te, ga);
+    } else if (BN == 256) launch_gemm_bn<256, 4>(cx, ta, tb, *tc, *td, *te, ga);
     else if (BN == 128) {
         if (one_wave && num_k > 3) launch_gemm_bn<128, 6>(cx, ta, tb, *tc, *td, *te, ga);
         else launch_gemm_bn<128, 3>(cx, ta, tb, *tc, *td, *te, ga);

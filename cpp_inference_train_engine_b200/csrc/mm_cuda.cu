@@ -578,6 +578,8 @@ int mm_cuda_gemm_f16(mm_cuda_ctx* h, int M, int N, int K, const void* a, int64_t
                      int64_t ldb, int b_mn, void* out, int64_t ldc, int out_kind, float alpha, const float* residual,
                      int64_t ldr, int bf16) {
     return guarded(h, [&](mm::Context& cx) {
+        // inputs written on any stream (the caller's) are complete before this stream reads them
+        MM_CUDA_CHECK(cudaDeviceSynchronize());
         if (M < 1 || N < 1 || K < 1 || !a || !b || !out || out_kind < 0 || out_kind > 3)
             mm::fail(MM_INVALID_ARGUMENT, "invalid GEMM arguments");
         mm::GemmOutSpec o{out, ldc, out_kind};
@@ -593,6 +595,8 @@ int mm_cuda_bench_gemm(mm_cuda_ctx* h, int reps, int M, int N, int K, const void
                        const void* b, int64_t ldb, int b_mn, void* out, int64_t ldc, int out_kind,
                        float* ms_per_launch) {
     return guarded(h, [&](mm::Context& cx) {
+        // inputs written on any stream (the caller's) are complete before this stream reads them
+        MM_CUDA_CHECK(cudaDeviceSynchronize());
         if (reps < 1 || reps > 4096 || M < 1 || N < 1 || K < 1 || !a || !b || !out || out_kind < 0 ||
             out_kind > 3 || !ms_per_launch)
             mm::fail(MM_INVALID_ARGUMENT, "invalid GEMM arguments");
@@ -645,6 +649,8 @@ int mm_cuda_bench_gemm(mm_cuda_ctx* h, int reps, int M, int N, int K, const void
 int mm_cuda_decode_attention(mm_cuda_ctx* h, const float* q, const void* cache, int64_t cache_seq_stride,
                              const int32_t* pos, int batch, int splits, float scale, void* out) {
     return guarded(h, [&](mm::Context& cx) {
+        // inputs written on any stream (the caller's) are complete before this stream reads them
+        MM_CUDA_CHECK(cudaDeviceSynchronize());
         if (!q || !cache || !pos || !out || batch < 1 || splits < 1 || splits > mm::kMaxDecodeSplits ||
             cache_seq_stride < mm::dec::W)
             mm::fail(MM_INVALID_ARGUMENT, "invalid decode attention arguments");

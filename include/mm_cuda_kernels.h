@@ -3,6 +3,8 @@
  * for the parity tests and the benchmark's timing. They have no counterpart in the
  * reference's Execution interface (the reference's GPU path is MPSGraph programs,
  * src/backends/mps_backend.mm:1597-1738); they expose single kernels of the same path.
+ * Each entry first waits for all work already submitted to the device, so inputs written on
+ * any stream are complete before they are read.
  */
 #ifndef MM_CUDA_KERNELS_H
 #define MM_CUDA_KERNELS_H

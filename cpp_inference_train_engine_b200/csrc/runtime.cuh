@@ -295,6 +295,10 @@ class Context {
     // continuous-batching serving session over dec (mm_cuda_serve_*): next position of
     // each slot on the host, -1 for a free slot
     bool serving = false;
+    // false while this context's products run beside another stream's (the frozen
+    // reference's forward overlapping the policy's backward): CTA-pair products need two free
+    // SMs of one TPC at once and stall behind the other stream's CTAs, so they stay single
+    bool pair_ok = true;
     std::vector<int> serve_pos;
 
     // NCCL

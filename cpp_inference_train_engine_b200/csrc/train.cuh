@@ -245,7 +245,9 @@ inline mm_step_result grpo_step(Context& pc, Context& rc, const uint16_t* input,
             PhaseTimer t(pc, kPhLogprob);
             MM_CUDA_CHECK(cudaMemcpyAsync(rc.ws.tokens, input + off, T * 2, cudaMemcpyHostToDevice, rc.stream));
             MM_CUDA_CHECK(cudaMemcpyAsync(rc.ws.targets, target + off, T * 2, cudaMemcpyHostToDevice, rc.stream));
+            rc.pair_ok = false;  // runs beside the policy's backward on its own stream
             forward_chunk(rc, bc, S, false, kVocabAll, true, nullptr, 0, 0, nullptr);
+            rc.pair_ok = true;
             MM_CUDA_CHECK(cudaMemcpyAsync(w.tokens, input + off, T * 2, cudaMemcpyHostToDevice, pc.stream));
             MM_CUDA_CHECK(cudaMemcpyAsync(w.targets, target + off, T * 2, cudaMemcpyHostToDevice, pc.stream));
             MM_CUDA_CHECK(cudaMemcpyAsync(w.mask, mask + off, T * 4, cudaMemcpyHostToDevice, pc.stream));
@@ -315,7 +317,9 @@ inline mm_step_result dpo_step(Context& pc, Context& rc, const uint16_t* input, 
             PhaseTimer t(pc, kPhLogprob);
             MM_CUDA_CHECK(cudaMemcpyAsync(rc.ws.tokens, input + off, T * 2, cudaMemcpyHostToDevice, rc.stream));
             MM_CUDA_CHECK(cudaMemcpyAsync(rc.ws.targets, target + off, T * 2, cudaMemcpyHostToDevice, rc.stream));
+            rc.pair_ok = false;  // runs beside the policy's backward on its own stream
             forward_chunk(rc, rows, S, false, kVocabAll, true, nullptr, 0, 0, nullptr);
+            rc.pair_ok = true;
             MM_CUDA_CHECK(cudaMemcpyAsync(w.tokens, input + off, T * 2, cudaMemcpyHostToDevice, pc.stream));
             MM_CUDA_CHECK(cudaMemcpyAsync(w.targets, target + off, T * 2, cudaMemcpyHostToDevice, pc.stream));
             MM_CUDA_CHECK(cudaMemcpyAsync(w.mask, mask + off, T * 4, cudaMemcpyHostToDevice, pc.stream));

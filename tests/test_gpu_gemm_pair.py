@@ -3,7 +3,7 @@
 product of the same fp16 operands (ragged M and N included), and the 35.8M model's
 teacher-forced log-probabilities and weighted-NLL gradient, whose vocabulary head
 (log-sum-exp epilogue), SwiGLU forward (with pre-activation stores) and SwiGLU backward
-products run on it at 4,224 tokens, against the same engine with every product on the
+products run on it at 8,448 tokens, against the same engine with every product on the
 single-CTA kernel (MM_GEMM_PAIR=0, a separate process)."""
 import os
 import subprocess
@@ -17,8 +17,9 @@ from tests.gpu_util import ROOT, rel, require_gpu
 
 pytestmark = pytest.mark.gpu
 
-# (M, N, K): at least one full wave of pair tiles, so the pair kernel is chosen
-PAIR_SHAPES = [(4096, 4096, 512), (4224, 1360, 512), (2048, 16384, 1536), (4100, 2056, 200)]
+# (M, N, K): chunk-sized (M >= 8192) with at least one full wave of pair tiles, so the pair
+# kernel is chosen; ragged M (8320 = 32.5 x 256), N (1360, 2056) and K (200)
+PAIR_SHAPES = [(8192, 4096, 512), (8320, 1360, 512), (8192, 8192, 1536), (8200, 2056, 200)]
 
 
 @pytest.fixture(scope="module")
@@ -67,7 +68,7 @@ _RUN = textwrap.dedent("""
     import numpy as np
     import cpp_inference_train_engine_b200 as E
     from cpp_inference_train_engine_b200.config import MLA36M
-    B, S = 16, 264
+    B, S = 32, 264
     rng = np.random.default_rng(41)
     x = rng.integers(0, 16384, (B, S)).astype(np.uint16)
     t = rng.integers(0, 16384, (B, S)).astype(np.uint16)

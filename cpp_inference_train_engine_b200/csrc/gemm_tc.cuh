@@ -124,7 +124,13 @@ __device__ __forceinline__ void gemm_release_acc(uint32_t release_bar, int lane)
     __syncwarp();
     if (lane == 0) mbar_arrive_cluster(release_bar);
 }
-template <int BN, int EPI_WARPS>
+// Epilogue families, one kernel instantiation each, so the common products carry none of
+// the SwiGLU paths' registers: kEpiPlain (store / accumulate / residual / log-sum-exp
+// partials / RoPE), kEpiGlu (SwiGLU, optionally with the pre-activations), kEpiDglu (SwiGLU
+// backward of dH).
+enum GemmEpi : int { kEpiPlain = 0, kEpiGlu = 1, kEpiDglu = 2 };
+
+template <int BN, int EPI_WARPS, int EPI>
 __device__ __forceinline__ void gemm_drain_tile(const GemmArgs g, const CUtensorMap& tmC, const CUtensorMap& tmD,
                                                 const CUtensorMap& tmE, uint8_t* stage_base, uint32_t src, int m0,
                                                 int n0, int map_row0, int q, int half, int lane, float alpha,
@@ -132,11 +138,11 @@ __device__ __forceinline__ void gemm_drain_tile(const GemmArgs g, const CUtensor
     constexpr int nhalf = EPI_WARPS / 4;  // warps per quadrant
     const bool half_out = g.out_kind >= kOutF16;
     const int CH = half_out ? 64 : 32;  // columns per 128-byte staged row
-    const int TW = g.glu_n ? BN / 2 : BN;
+    const int TW = EPI == kEpiGlu ? BN / 2 : BN;
     const int n_mma = min(BN, ((g.N - n0) + 15) / 16 * 16);
     const int row0 = m0 + q * 32;
     const int row = row0 + lane;
-    if (g.glu_n) {
+    if constexpr (EPI == kEpiGlu) {
         // accumulator columns [0, TW) gate, [TW, 2 TW) up; 64 fp16 outputs per staged row
         if (half * 64 >= TW) {  // no chunk for this warp: release the accumulator
             gemm_release_acc(release_bar, lane);
@@ -218,7 +224,7 @@ __device__ __forceinline__ void gemm_drain_tile(const GemmArgs g, const CUtensor
         gemm_release_acc(release_bar, lane);
     }
     for (int c = half * CH; c < n_mma; c += CH * nhalf) {
-        if (g.dglu_n) {
+        if constexpr (EPI == kEpiDglu) {
             // SwiGLU backward of dH columns [col0, col0 + 64) of this row, 32 at a time from
             // tensor memory; x = gate, u = up from the forward: d gate = dh u s (1 + x (1 - s)),
             // d up = dh x s, s = sigmoid(x). d gate goes straight into the staging tile, d up
@@ -367,7 +373,7 @@ __device__ __forceinline__ void gemm_drain_tile(const GemmArgs g, const CUtensor
     }
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int EPI>
 __global__ void __launch_bounds__(320, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmD,
@@ -387,7 +393,7 @@ __global__ void __launch_bounds__(320, 1)
     const int num_k = (g.K + kGemmBK - 1) / kGemmBK;
     const int per = g.k_tiles_per_split > 0 ? g.k_tiles_per_split : num_k;
     const int splits = (num_k + per - 1) / per;
-    const int TW = g.glu_n ? BN / 2 : BN;  // output columns per tile
+    const int TW = EPI == kEpiGlu ? BN / 2 : BN;  // output columns per tile
     const int tiles_n = (g.N + TW - 1) / TW, tiles_m = (g.M + kGemmBM - 1) / kGemmBM;
     const int tiles = tiles_n * tiles_m * splits;
 
@@ -443,7 +449,7 @@ __global__ void __launch_bounds__(320, 1)
                 } else {
 #pragma unroll
                     for (int j = 0; j < BN / 64; ++j) {
-                        const int col = !g.glu_n ? n0 + 64 * j
+                        const int col = EPI != kEpiGlu ? n0 + 64 * j
                                                  : (j < BN / 128 ? n0 + 64 * j : g.glu_n + n0 + 64 * (j - BN / 128));
                         tma_load_2d(sb + j * 8192, &tmB, &full[s], col, k0);
                     }
@@ -457,7 +463,7 @@ __global__ void __launch_bounds__(320, 1)
             const int z = tile / (tiles_n * tiles_m), mn = tile % (tiles_n * tiles_m);
             const int n0 = (mn % tiles_n) * TW;
             const int kb = z * per, ke = min(num_k, kb + per);
-            const int n_mma = g.glu_n ? BN : min(BN, ((g.N - n0) + 15) / 16 * 16);
+            const int n_mma = EPI == kEpiGlu ? BN : min(BN, ((g.N - n0) + 15) / 16 * 16);
             const uint32_t idesc = umma_idesc_f16(g.bf16 != 0, g.a_mn != 0, g.b_mn != 0, kGemmBM, n_mma);
             const int buf = j & 1;
             if (!mbar_wait_bounded(&acc_empty[buf], ((j >> 1) & 1) ^ 1, g.err)) break;
@@ -496,7 +502,7 @@ __global__ void __launch_bounds__(320, 1)
             tc_fence_after();
             const int map_row0 = m0 + q * 32 + (g.k_tiles_per_split > 0 ? z * g.split_rows : 0);
             const uint32_t src = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * BN);
-            gemm_drain_tile<BN, C::EPI_WARPS>(g, tmC, tmD, tmE, stage_base, src, m0, n0, map_row0, q, half, lane,
+            gemm_drain_tile<BN, C::EPI_WARPS, EPI>(g, tmC, tmD, tmE, stage_base, src, m0, n0, map_row0, q, half, lane,
                                               alpha, smem_u32(&acc_empty[buf]));
         }
         if (lane == 0) bulk_wait0();
@@ -535,6 +541,7 @@ struct PairCfg {
     static constexpr int SMEM = kPairStages * STAGE_BYTES + EPI_BYTES + 1024 + 256;
 };
 
+template <int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
     gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmD,
@@ -555,7 +562,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
     const uint32_t rank = cluster_ctarank();
     const int pair = static_cast<int>(blockIdx.x >> 1), npairs = static_cast<int>(gridDim.x >> 1);
     const int num_k = (g.K + kGemmBK - 1) / kGemmBK;
-    const int TW = g.glu_n ? BN / 2 : BN;  // output columns per tile
+    const int TW = EPI == kEpiGlu ? BN / 2 : BN;  // output columns per tile
     const int tiles_n = (g.N + TW - 1) / TW, tiles_m = (g.M + 2 * kGemmBM - 1) / (2 * kGemmBM);
     const int tiles = tiles_n * tiles_m;
 
@@ -591,7 +598,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
         for (int tile = pair; tile < tiles && ok; tile += npairs) {
             const int m0 = (tile / tiles_n) * (2 * kGemmBM) + kGemmBM * static_cast<int>(rank);
             const int n0 = (tile % tiles_n) * TW;
-            const int nb = g.glu_n ? (rank == 0 ? n0 : g.glu_n + n0) : n0 + 128 * static_cast<int>(rank);
+            const int nb = EPI == kEpiGlu ? (rank == 0 ? n0 : g.glu_n + n0) : n0 + 128 * static_cast<int>(rank);
             for (int kt = 0; kt < num_k; ++kt, ++it) {
                 const int s = it % kPairStages;
                 const uint32_t ph = (it / kPairStages) & 1;
@@ -656,7 +663,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
             if (!mbar_wait_bounded(&acc_full[buf], (j >> 1) & 1, g.err)) break;
             tc_fence_after();
             const uint32_t src = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * BN);
-            gemm_drain_tile<BN, C::EPI_WARPS>(g, tmC, tmD, tmE, stage_base, src, m0, n0, m0 + q * 32, q, half, lane,
+            gemm_drain_tile<BN, C::EPI_WARPS, EPI>(g, tmC, tmD, tmE, stage_base, src, m0, n0, m0 + q * 32, q, half, lane,
                                               alpha, mapa_shared(smem_u32(&acc_empty[buf]), 0));
         }
         if (lane == 0) bulk_wait0();

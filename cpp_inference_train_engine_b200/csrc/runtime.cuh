@@ -508,11 +508,11 @@ inline void set_dynamic_smem(int bytes) {
     done.fetch_or(bit);
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int EPI = kEpiPlain>
 inline void launch_gemm_bn(Context& cx, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
                            const CUtensorMap& td, const CUtensorMap& te, const GemmArgs& ga) {
     using C = GemmCfg<BN, STAGES>;
-    set_dynamic_smem<gemm_tc_kernel<BN, STAGES>>(C::SMEM);
+    set_dynamic_smem<gemm_tc_kernel<BN, STAGES, EPI>>(C::SMEM);
     const long long num_k = (ga.K + kGemmBK - 1) / kGemmBK;
     const long long per = ga.k_tiles_per_split > 0 ? ga.k_tiles_per_split : num_k;
     const int tw = ga.glu_n ? BN / 2 : BN;
@@ -522,7 +522,7 @@ inline void launch_gemm_bn(Context& cx, const CUtensorMap& ta, const CUtensorMap
     const int per_sm = std::max(1, std::min(512 / (2 * BN), (227 * 1024) / C::SMEM));
     dim3 grid(static_cast<unsigned>(std::min<long long>(tiles, static_cast<long long>(sm_count()) * per_sm)));
     cudaEvent_t t0 = cx.prof_begin();
-    launch_k(cx.stream, gemm_tc_kernel<BN, STAGES>, grid, dim3(C::THREADS), C::SMEM, ta, tb, tc, td, te, ga);
+    launch_k(cx.stream, gemm_tc_kernel<BN, STAGES, EPI>, grid, dim3(C::THREADS), C::SMEM, ta, tb, tc, td, te, ga);
     const double flops = 2.0 * ga.M * static_cast<double>(ga.N) * ga.K;
     if (t0) {
         char key[96];
@@ -548,13 +548,13 @@ inline bool pair_gemm_enabled() {
 inline int pair_gemm_slots() {
     static int slots = -1;
     if (slots < 0) {
-        set_dynamic_smem<gemm_tc_pair_kernel>(PairCfg::SMEM);
+        set_dynamic_smem<gemm_tc_pair_kernel<kEpiPlain>>(PairCfg::SMEM);
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(2 * 74);
         cfg.blockDim = dim3(PairCfg::THREADS);
         cfg.dynamicSmemBytes = PairCfg::SMEM;
         int n = 0;
-        if (cudaOccupancyMaxActiveClusters(&n, gemm_tc_pair_kernel, &cfg) != cudaSuccess) {
+        if (cudaOccupancyMaxActiveClusters(&n, gemm_tc_pair_kernel<kEpiPlain>, &cfg) != cudaSuccess) {
             cudaGetLastError();
             n = 0;
         }
@@ -564,14 +564,15 @@ inline int pair_gemm_slots() {
 }
 
 // The CTA-pair product: one persistent cluster per resident pair slot, 256-row tiles.
+template <int EPI>
 inline void launch_gemm_pair(Context& cx, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
                              const CUtensorMap& td, const CUtensorMap& te, const GemmArgs& ga) {
-    set_dynamic_smem<gemm_tc_pair_kernel>(PairCfg::SMEM);
+    set_dynamic_smem<gemm_tc_pair_kernel<EPI>>(PairCfg::SMEM);
     const int tw = ga.glu_n ? 128 : 256;
     const long long tiles = static_cast<long long>((ga.N + tw - 1) / tw) * ((ga.M + 255) / 256);
     dim3 grid(static_cast<unsigned>(2 * std::min<long long>(tiles, pair_gemm_slots())));
     cudaEvent_t t0 = cx.prof_begin();
-    launch_k(cx.stream, gemm_tc_pair_kernel, grid, dim3(PairCfg::THREADS), PairCfg::SMEM, ta, tb, tc, td, te, ga);
+    launch_k(cx.stream, gemm_tc_pair_kernel<EPI>, grid, dim3(PairCfg::THREADS), PairCfg::SMEM, ta, tb, tc, td, te, ga);
     const double flops = 2.0 * ga.M * static_cast<double>(ga.N) * ga.K;
     if (t0) {
         char key[96];

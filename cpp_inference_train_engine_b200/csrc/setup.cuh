@@ -51,7 +51,7 @@ inline int gemm(Context& cx, int M, int N, int K, Opnd A, Opnd B, const GemmOutS
     const bool split_candidate = o.kind == kOutF32Acc && num_k_all >= 32 && N % 4 == 0 &&
                                  tiles_m * ((N + 63) / 64) < sm_count();
     int BN = 64;
-    if (o.glu_n) BN = 256;  // 128 gate + 128 up columns per tile
+    if (o.glu_n || o.dglu_gu) BN = 256;  // SwiGLU: 128 gate + 128 up columns per tile; both on 256-wide tiles only
     else if (N >= 256 && (split_candidate || tiles_m * ((N + 255) / 256) >= 148)) BN = 256;
     else if (tiles_m * ((N + 127) / 128) >= 120 && N > 64) BN = 128;
     // MM_GEMM_BN (64, 128 or 256) pins the tile width of every plain product, for tuning.
@@ -60,7 +60,7 @@ inline int gemm(Context& cx, int M, int N, int K, Opnd A, Opnd B, const GemmOutS
         const int v = e ? std::atoi(e) : 0;
         return v == 64 || v == 128 || v == 256 ? v : 0;
     }();
-    if (forced_bn && !o.glu_n) BN = forced_bn;
+    if (forced_bn && !o.glu_n && !o.dglu_gu) BN = forced_bn;
     const int nb = o.glu_n ? o.glu_n + N : N;  // columns of B
     const CUtensorMap& ta = A.mn ? tensor_map(A.p, bf16, M, K, A.ld, 64, 64)
                                  : tensor_map(A.p, bf16, K, M, A.ld, 64, kGemmBM);
@@ -133,8 +133,12 @@ inline int gemm(Context& cx, int M, int N, int K, Opnd A, Opnd B, const GemmOutS
         pair_tiles >= pair_gemm_slots()) {
         // the B tile of each CTA is 128 columns: K-major B boxes are 128 rows high
         const CUtensorMap& tb2 = B.mn ? tb : tensor_map(B.p, bf16, K, nb, B.ld, 64, 128);
-        launch_gemm_pair(cx, ta, tb2, *tc, *td, *te, ga);
-    } else if (BN == 256) launch_gemm_bn<256, 4>(cx, ta, tb, *tc, *td, *te, ga);
+        if (o.glu_n) launch_gemm_pair<kEpiGlu>(cx, ta, tb2, *tc, *td, *te, ga);
+        else if (o.dglu_gu) launch_gemm_pair<kEpiDglu>(cx, ta, tb2, *tc, *td, *te, ga);
+        else launch_gemm_pair<kEpiPlain>(cx, ta, tb2, *tc, *td, *te, ga);
+    } else if (o.glu_n) launch_gemm_bn<256, 4, kEpiGlu>(cx, ta, tb, *tc, *td, *te, ga);
+    else if (o.dglu_gu) launch_gemm_bn<256, 4, kEpiDglu>(cx, ta, tb, *tc, *td, *te, ga);
+    else if (BN == 256) launch_gemm_bn<256, 4>(cx, ta, tb, *tc, *td, *te, ga);
     else if (BN == 128) {
         if (one_wave && num_k > 3) launch_gemm_bn<128, 6>(cx, ta, tb, *tc, *td, *te, ga);
         else launch_gemm_bn<128, 3>(cx, ta, tb, *tc, *td, *te, ga);

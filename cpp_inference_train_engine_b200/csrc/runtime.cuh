@@ -543,6 +543,17 @@ inline bool pair_gemm_enabled() {
     return on;
 }
 
+// Smallest M (rows) a product needs to run on CTA pairs; MM_GEMM_PAIR_MIN_M overrides the
+// default of 8192 (for measurements).
+inline int pair_gemm_min_m() {
+    static const int m = [] {
+        const char* e = std::getenv("MM_GEMM_PAIR_MIN_M");
+        const int v = e ? std::atoi(e) : 0;
+        return v > 0 ? v : 8192;
+    }();
+    return m;
+}
+
 // CTA pairs of gemm_tc_pair_kernel that can be resident at once on this device (0 when the
 // cluster launch does not fit).
 inline int pair_gemm_slots() {

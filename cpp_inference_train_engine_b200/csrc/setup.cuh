@@ -129,7 +129,7 @@ inline int gemm(Context& cx, int M, int N, int K, Opnd A, Opnd B, const GemmOutS
     // short products lose more to the cluster launch than they gain), at least one full wave
     // of 256 x 256 tiles, and no other stream's products running beside them.
     const long long pair_tiles = static_cast<long long>((M + 255) / 256) * ((N + (o.glu_n ? 127 : 255)) / (o.glu_n ? 128 : 256));
-    if (BN == 256 && splits == 1 && M >= 8192 && cx.pair_ok && pair_gemm_enabled() && pair_gemm_slots() > 0 &&
+    if (BN == 256 && splits == 1 && M >= pair_gemm_min_m() && cx.pair_ok && pair_gemm_enabled() && pair_gemm_slots() > 0 &&
         pair_tiles >= pair_gemm_slots()) {
         // the B tile of each CTA is 128 columns: K-major B boxes are 128 rows high
         const CUtensorMap& tb2 = B.mn ? tb : tensor_map(B.p, bf16, K, nb, B.ld, 64, 128);

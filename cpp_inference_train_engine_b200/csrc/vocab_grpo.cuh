@@ -335,6 +335,13 @@ __device__ __forceinline__ void sample_hist_add(SampleShared& S, int bk, unsigne
     atomicAdd(&S.h.hi[bk], static_cast<unsigned>(w >> 32));
     atomicAdd(&S.h.count[bk], 1u);
 }
+// The first round's form: masses only. Its candidate count comes from the gather that ranks
+// the crossing bucket (sample_pick), which reports an overflow instead.
+__device__ __forceinline__ void sample_hist_add_mass(SampleShared& S, int bk, unsigned long long w) {
+    atomicAdd(&S.h.lo[bk], static_cast<unsigned>(w & 0xffffu));
+    atomicAdd(&S.h.mid[bk], static_cast<unsigned>((w >> 16) & 0xffffu));
+    atomicAdd(&S.h.hi[bk], static_cast<unsigned>(w >> 32));
+}
 __device__ __forceinline__ unsigned long long sample_hist_mass(const SampleShared& S, int bk) {
     return (static_cast<unsigned long long>(S.h.hi[bk]) << 32) + (static_cast<unsigned long long>(S.h.mid[bk]) << 16) +
            S.h.lo[bk];
@@ -380,8 +387,11 @@ struct SampleRowWeight {
 // row total, otherwise S.draw is the part left inside the previously fixed prefix. Leaves in
 // S.chosen the bucket where the running mass first reaches the draw and in S.draw the part
 // of it inside that bucket; when every weight rounded to zero below the draw, the lowest
-// non-empty bucket with S.draw = ~0. Called by warp 0 only.
-__device__ __forceinline__ void sample_locate(SampleShared& S, int nb, bool first, uint64_t seed, int k) {
+// non-empty bucket with S.draw = ~0 (`counted`: emptiness from the counts, else from the
+// masses; the first round's draw is below the row total, so it always finds a crossing).
+// Called by warp 0 only.
+__device__ __forceinline__ void sample_locate(SampleShared& S, int nb, bool first, uint64_t seed, int k,
+                                              bool counted) {
     constexpr int PER = kSampleBuckets / 32;
     const int lane = threadIdx.x & 31;
     unsigned long long mine = 0;
@@ -402,9 +412,11 @@ __device__ __forceinline__ void sample_locate(SampleShared& S, int nb, bool firs
 #pragma unroll
     for (int e = 0; e < PER; ++e) {
         const int bk = nb - 1 - (lane * PER + e);
-        if (bk < 0 || S.h.count[bk] == 0) continue;
-        last_here = bk;
+        if (bk < 0) continue;
         const unsigned long long m = sample_hist_mass(S, bk);
+        // without counts an empty bucket is one of zero mass, which can never hold the crossing
+        if (counted ? S.h.count[bk] == 0 : m == 0) continue;
+        last_here = bk;
         if (found < 0 && run < draw && run + m >= draw) {
             found = bk;
             rem = draw - run;
@@ -431,7 +443,8 @@ __device__ __forceinline__ void sample_locate(SampleShared& S, int nb, bool firs
 // ordered by score descending then id ascending, the id where the running mass first
 // reaches S.draw (the last one when none does; `none` when the set is empty). Ranks by
 // counting: the mass before candidate i is the sum over the candidates ordered before it.
-// Called by the whole block.
+// kSamplePickOverflow when the set holds more than kSampleCap scores. Called by the whole block.
+constexpr int kSamplePickOverflow = -2;
 template <class Each, class Pred>
 __device__ int sample_pick(SampleShared& S, Each each, const SampleRowWeight& wt, Pred in_set, int none) {
     const unsigned long long rem = S.draw;
@@ -449,7 +462,8 @@ __device__ int sample_pick(SampleShared& S, Each each, const SampleRowWeight& wt
         }
     });
     __syncthreads();
-    const int n = min(S.ncand, kSampleCap);
+    if (S.ncand > kSampleCap) return kSamplePickOverflow;
+    const int n = S.ncand;
     if (n == 0) return none;
     uint32_t last_key = 0xffffffffu;
     int last_id = -1;
@@ -593,18 +607,19 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(
         __syncthreads();
         each([&](int, float v) {
             const int bk = wt.bucket(v);
-            sample_hist_add(S, bk, wt(v, bk));
+            sample_hist_add_mass(S, bk, wt(v, bk));
         });
         __syncthreads();
-        if (warp == 0) sample_locate(S, kSampleBuckets, true, seed, k);
+        if (warp == 0) sample_locate(S, kSampleBuckets, true, seed, k, false);
         __syncthreads();
         const int chosen = S.chosen;
-        if (S.h.count[chosen] <= static_cast<unsigned>(kSampleCap)) {
-            const int tok = sample_pick(S, each, wt, [&](float v) { return wt.bucket(v) == chosen; }, best);
+        const int tok = sample_pick(S, each, wt, [&](float v) { return wt.bucket(v) == chosen; }, best);
+        if (tok != kSamplePickOverflow) {
             if (tid == 0) out[b * out_stride] = static_cast<uint16_t>(tok);
             return;
         }
-        __syncthreads();  // every thread has read the count before the histogram is cleared
+        // more than kSampleCap scores in the crossing bucket: every thread has passed the
+        // gather's barrier, so the histogram (which the candidates share) may be rebuilt
     }
 
     // fallback: buckets of the order-preserving key, refined kSampleRadixBits at a time
@@ -624,7 +639,7 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(
             sample_hist_add(S, bk, wt(v, wt.poly ? wt.bucket(v) : 0));
         });
         __syncthreads();
-        if (warp == 0) sample_locate(S, nb, first, seed, k);
+        if (warp == 0) sample_locate(S, nb, first, seed, k, true);
         __syncthreads();
         first = false;
         const int chosen = S.chosen;

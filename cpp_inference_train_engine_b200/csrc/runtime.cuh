@@ -543,13 +543,13 @@ inline bool pair_gemm_enabled() {
     return on;
 }
 
-// Smallest M (rows) a product needs to run on CTA pairs; MM_GEMM_PAIR_MIN_M overrides the
-// default of 8192 (for measurements).
+// Smallest M (rows) a product needs to run on CTA pairs (the 2,048-row decode step's
+// vocabulary head and SwiGLU products gain ~1% of the step); MM_GEMM_PAIR_MIN_M overrides it.
 inline int pair_gemm_min_m() {
     static const int m = [] {
         const char* e = std::getenv("MM_GEMM_PAIR_MIN_M");
         const int v = e ? std::atoi(e) : 0;
-        return v > 0 ? v : 8192;
+        return v > 0 ? v : 2048;
     }();
     return m;
 }

@@ -125,9 +125,8 @@ inline int gemm(Context& cx, int M, int N, int K, Opnd A, Opnd B, const GemmOutS
     } else if (o.dglu_gu) {
         td = &tensor_map_t(o.dglu_up, kMapF16, N, M, o.ldc, 64, 32);
     }
-    // Large 256-wide products run on CTA pairs: chunk-sized (M >= 8192; the decode step's
-    // short products lose more to the cluster launch than they gain), at least one full wave
-    // of 256 x 256 tiles, and no other stream's products running beside them.
+    // Large 256-wide products run on CTA pairs: M >= pair_gemm_min_m(), at least one full
+    // wave of 256 x 256 tiles, and no other stream's products running beside them.
     const long long pair_tiles = static_cast<long long>((M + 255) / 256) * ((N + (o.glu_n ? 127 : 255)) / (o.glu_n ? 128 : 256));
     if (BN == 256 && splits == 1 && M >= pair_gemm_min_m() && cx.pair_ok && pair_gemm_enabled() && pair_gemm_slots() > 0 &&
         pair_tiles >= pair_gemm_slots()) {

@@ -94,8 +94,14 @@ __global__ void __launch_bounds__(256) rmsnorm_backward_v4_kernel(
     for (int t = blockIdx.x * warps + warp; t < T; t += gridDim.x * warps) {
         const float* xr = x + t * ldx;
         const float* gr = dy + t * lddy;
-        float4 xv[MAXV], gv[MAXV];
+        float4 xv[MAXV], gv[MAXV], av[MAXV];
         float sq = 0.f, dot = 0.f;
+        // the added gradient is loaded with x and dy, so its latency hides behind theirs
+#pragma unroll
+        for (int k = 0; k < MAXV; ++k) {
+            const int j = (k * 32 + lane) * 4;
+            av[k] = (add && j < n) ? ld_f4(add + t * ldadd + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
 #pragma unroll
         for (int k = 0; k < MAXV; ++k) {
             const int j = (k * 32 + lane) * 4;
@@ -118,11 +124,10 @@ __global__ void __launch_bounds__(256) rmsnorm_backward_v4_kernel(
                 float4 o = make_float4(gv[k].x * wv[k].x * inv - xv[k].x * corr, gv[k].y * wv[k].y * inv - xv[k].y * corr,
                                        gv[k].z * wv[k].z * inv - xv[k].z * corr, gv[k].w * wv[k].w * inv - xv[k].w * corr);
                 if (add) {
-                    const float4 a = ld_f4(add + t * ldadd + j);
-                    o.x += a.x;
-                    o.y += a.y;
-                    o.z += a.z;
-                    o.w += a.w;
+                    o.x += av[k].x;
+                    o.y += av[k].y;
+                    o.z += av[k].z;
+                    o.w += av[k].w;
                 }
                 if (dx32) st_f4(dx32 + t * lddx + j, o);
                 if (dx16) *reinterpret_cast<uint2*>(dx16 + t * lddx16 + j) = pack_h4(o.x, o.y, o.z, o.w);

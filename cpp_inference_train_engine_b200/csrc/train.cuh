@@ -164,6 +164,25 @@ inline bool decode_graphs_enabled() {
     return v != 0;
 }
 
+// The frozen reference's forward of one chunk. By default it runs on its own stream beside
+// the policy's backward of the previous chunk, with single-CTA products (CTA pairs need both
+// SMs of a TPC free at once and stall behind the other stream's CTAs); MM_REF_OVERLAP=0 runs
+// it after that backward instead, on CTA pairs where they apply.
+inline bool ref_overlap_enabled() {
+    static const bool on = [] {
+        const char* e = std::getenv("MM_REF_OVERLAP");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+inline void reference_forward(Context& pc, Context& rc, int rows, int S) {
+    const bool overlap = ref_overlap_enabled();
+    if (!overlap) MM_CUDA_CHECK(cudaStreamSynchronize(pc.stream));
+    rc.pair_ok = !overlap;
+    forward_chunk(rc, rows, S, false, kVocabAll, true, nullptr, 0, 0, nullptr);
+    rc.pair_ok = true;
+}
+
 inline int chunk_tokens_default() {
     static int v = [] {
         const char* e = std::getenv("MM_CHUNK_TOKENS");
@@ -245,9 +264,7 @@ inline mm_step_result grpo_step(Context& pc, Context& rc, const uint16_t* input,
             PhaseTimer t(pc, kPhLogprob);
             MM_CUDA_CHECK(cudaMemcpyAsync(rc.ws.tokens, input + off, T * 2, cudaMemcpyHostToDevice, rc.stream));
             MM_CUDA_CHECK(cudaMemcpyAsync(rc.ws.targets, target + off, T * 2, cudaMemcpyHostToDevice, rc.stream));
-            rc.pair_ok = false;  // runs beside the policy's backward on its own stream
-            forward_chunk(rc, bc, S, false, kVocabAll, true, nullptr, 0, 0, nullptr);
-            rc.pair_ok = true;
+            reference_forward(pc, rc, bc, S);
             MM_CUDA_CHECK(cudaMemcpyAsync(w.tokens, input + off, T * 2, cudaMemcpyHostToDevice, pc.stream));
             MM_CUDA_CHECK(cudaMemcpyAsync(w.targets, target + off, T * 2, cudaMemcpyHostToDevice, pc.stream));
             MM_CUDA_CHECK(cudaMemcpyAsync(w.mask, mask + off, T * 4, cudaMemcpyHostToDevice, pc.stream));
@@ -317,9 +334,7 @@ inline mm_step_result dpo_step(Context& pc, Context& rc, const uint16_t* input, 
             PhaseTimer t(pc, kPhLogprob);
             MM_CUDA_CHECK(cudaMemcpyAsync(rc.ws.tokens, input + off, T * 2, cudaMemcpyHostToDevice, rc.stream));
             MM_CUDA_CHECK(cudaMemcpyAsync(rc.ws.targets, target + off, T * 2, cudaMemcpyHostToDevice, rc.stream));
-            rc.pair_ok = false;  // runs beside the policy's backward on its own stream
-            forward_chunk(rc, rows, S, false, kVocabAll, true, nullptr, 0, 0, nullptr);
-            rc.pair_ok = true;
+            reference_forward(pc, rc, rows, S);
             MM_CUDA_CHECK(cudaMemcpyAsync(w.tokens, input + off, T * 2, cudaMemcpyHostToDevice, pc.stream));
             MM_CUDA_CHECK(cudaMemcpyAsync(w.targets, target + off, T * 2, cudaMemcpyHostToDevice, pc.stream));
             MM_CUDA_CHECK(cudaMemcpyAsync(w.mask, mask + off, T * 4, cudaMemcpyHostToDevice, pc.stream));

@@ -658,8 +658,11 @@ int mm_cuda_decode_attention(mm_cuda_ctx* h, const float* q, const void* cache, 
         if (splits > 1)
             part = static_cast<float*>(cx.stage.get(sizeof(float) * static_cast<size_t>(batch) * splits * mm::dec::H *
                                                     (mm::dec::KV + 2)));
+        // device time of the launch(es) alone, for the profile (the synchronisation above is not in it)
+        cudaEvent_t t0 = cx.prof_begin();
         mm::launch_decode_attention(cx, q, static_cast<const __half*>(cache), cache_seq_stride, pos, batch, splits, scale,
                                     static_cast<__half*>(out), part);
+        cx.prof_end(mm::kKDecodeAttn, t0);
         mm::check_device(cx, "decode_attention");
     });
 }

@@ -39,7 +39,6 @@ def attention(args):
     import cpp_inference_train_engine_b200 as E
     H, KV, W = 8, 128, 144
     ex = E.CudaExecution(E.MLA36M)
-    stream = torch.cuda.ExternalStream(ex.stream)
     g = torch.Generator(device="cuda").manual_seed(1)
     for B in args.batch:
         Sc = args.ctx
@@ -49,17 +48,18 @@ def attention(args):
         out = torch.empty(B, H * KV, device="cuda", dtype=torch.half)
         splits = args.splits or (1 if B >= 1184 else max(1, min((1184 + B - 1) // B, (args.ctx + 63) // 64, 16)))
         torch.cuda.synchronize()
-        times = []
-        for it in range(args.warmup + args.iters):
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
+        # device time of the kernel launches alone, from the library's per-launch events (each
+        # call first waits for all earlier device work, which a pair of events around the
+        # call would count)
+        for _ in range(args.warmup):
             ex.decode_attention(q.data_ptr(), cache.data_ptr(), Sc * W, pos.data_ptr(), B, splits, 0.125,
                                 out.data_ptr())
-            e1.record(stream)
-            torch.cuda.synchronize()
-            if it >= args.warmup:
-                times.append(e0.elapsed_time(e1))
-        ms = sorted(times)[len(times) // 2]
+        ex.profile(1)
+        for _ in range(args.iters):
+            ex.decode_attention(q.data_ptr(), cache.data_ptr(), Sc * W, pos.data_ptr(), B, splits, 0.125,
+                                out.data_ptr())
+        tot, calls, _ = ex.profile(0)["k_decode_attention"]
+        ms = tot / max(calls, 1)
         byts = B * args.ctx * W * 2 + B * H * W * 4 + B * H * KV * 2
         peak, src = _peak_hbm()
         print(json.dumps({"kernel": "decode_attention", "batch": B, "ctx": args.ctx, "splits": splits,

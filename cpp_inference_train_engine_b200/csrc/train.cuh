@@ -178,9 +178,12 @@ inline bool ref_overlap_enabled() {
 inline void reference_forward(Context& pc, Context& rc, int rows, int S) {
     const bool overlap = ref_overlap_enabled();
     if (!overlap) MM_CUDA_CHECK(cudaStreamSynchronize(pc.stream));
+    struct Restore {  // pair products allowed again however the forward ends
+        Context& c;
+        ~Restore() { c.pair_ok = true; }
+    } restore{rc};
     rc.pair_ok = !overlap;
     forward_chunk(rc, rows, S, false, kVocabAll, true, nullptr, 0, 0, nullptr);
-    rc.pair_ok = true;
 }
 
 inline int chunk_tokens_default() {

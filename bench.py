@@ -1,9 +1,9 @@
 #!/usr/bin/env python3
-"""Benchmark: one full online GRPO step of the 35.8M-parameter MLA model:
-256 prompts x group 8 = 2048 rollouts, prompt 128 tokens, 256 new tokens at temperature 1
-(sequence 384), Bernoulli(0.3) rewards, clip 0.2, KL 0.04, AdamW lr 1e-5 on fp32 master
-weights with fp16 tensor-core compute. Random-init weights (seed 0) and synthetic prompt ids;
-the frozen reference model equals the initial policy.
+"""Benchmark: one full online GRPO step of the 35.8M-parameter MLA model: 256 prompts x
+group 8 = 2048 rollouts, prompt 128 tokens, 256 new tokens at temperature 1 (sequence 384),
+Bernoulli(0.3) rewards, clip 0.2, KL 0.04, AdamW lr 1e-5 on fp32 master weights with fp16
+tensor-core compute. Random-init weights (seed 0) and synthetic prompt ids; the frozen
+reference model equals the initial policy.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
@@ -14,20 +14,39 @@ fused objective + backward, gradient all-reduce, AdamW). Rollouts are sharded ov
 
 Printed once by rank 0: a JSON line with value = generated rollout tokens per second of
 device step time (whole job), e2e = the same through the public API with host buffers,
-ms_per_step, roofline of the dominant kernel class, the reference CPU baseline, clocks.
+ms_per_step, the roofline of the dominant kernel class (algorithmic FLOPs) and of the decode
+phase (algorithmic HBM bytes), a fixed-input GRPO update whose loss / grad norm must not
+depend on the rank count, the reference CPU baseline, clocks.
+
+--impl reference times the reference engine's own CPU path (oracle/_ref, OpenBLAS on every
+host core) on a bounded sample of the same workload; only rank 0 works, and it touches no GPU.
 """
-from __future__ import annotations
-
-import argparse
-import json
 import os
-import statistics
-import subprocess
 import sys
-import threading
-import time
 
-import numpy as np
+
+def _host_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
+
+
+if "reference" in sys.argv[1:] or "--impl=reference" in sys.argv[1:]:
+    # Before numpy (and the OpenBLAS it bundles, which the reference build calls) loads: a
+    # launcher that set OMP_NUM_THREADS=1 for its workers must not leave the CPU baseline on
+    # one thread.
+    os.environ["OPENBLAS_NUM_THREADS"] = str(_host_threads())
+    os.environ["OMP_NUM_THREADS"] = str(_host_threads())
+
+import argparse  # noqa: E402
+import json  # noqa: E402
+import statistics  # noqa: E402
+import subprocess  # noqa: E402
+import threading  # noqa: E402
+import time  # noqa: E402
+
+import numpy as np  # noqa: E402
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
@@ -45,8 +64,11 @@ def parse():
     ap.add_argument("--group", type=int, default=8)
     ap.add_argument("--prompt-len", type=int, default=128)
     ap.add_argument("--new-tokens", type=int, default=256)
-    ap.add_argument("--cpu-rollouts", type=int, default=2,
-                    help="rollouts in the bounded CPU-baseline sample")
+    ap.add_argument("--cpu-rollouts", type=int, default=8,
+                    help="rollouts (one group) in the bounded CPU-baseline sample of the GPU arm")
+    ap.add_argument("--reference-budget", type=float, default=240.0,
+                    help="seconds the --impl reference run may take (sizes its per-step sample)")
+    ap.add_argument("--no-fixed-check", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--gemm-shapes", action="store_true",
                     help="print per-shape GEMM device time to stderr")
@@ -113,52 +135,96 @@ def peaks():
 
 
 # ---------------------------------------------------------------------------- CPU baseline
-def cpu_baseline(args, steps=1):
-    """The reference engine's own CPU path (oracle/_ref, OpenBLAS on all host cores) on a
-    bounded sample of the same workload: `cpu_rollouts` rollouts of the same prompt shape
-    and length, then their GRPO update. Returns tokens/s per step."""
-    from cpp_inference_train_engine_b200.config import MLA36M, AdamWConfig
-    from cpp_inference_train_engine_b200.rng import grpo_workload
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+class CpuSample:
+    """The reference engine's own CPU path (oracle/_ref, OpenBLAS) on a bounded sample of the
+    workload: `n` rollouts of one prompt (one group) with the workload's prompt length and new
+    tokens, then their GRPO update. Each run() returns generated tokens per second."""
+
+    def __init__(self, args, n):
+        from cpp_inference_train_engine_b200.config import MLA36M, AdamWConfig
+        from cpp_inference_train_engine_b200.rng import grpo_workload
+        from oracle import ref
+        self.ref, self.cfg, self.args, self.n = ref, MLA36M, args, n
+        prompts, seeds, rewards = grpo_workload(1, n, args.prompt_len, MLA36M.vocab_size, 0.3)
+        rewards[0], rewards[-1] = 1.0, 0.0
+        self.prompts, self.seeds, self.rewards = prompts, seeds, rewards
+        self.seq = args.prompt_len + args.new_tokens
+        self.pol = ref.Session(MLA36M, 0, optimizer=AdamWConfig().as_list())
+        self.refm = ref.Session(MLA36M, 0)
+
+    def run(self):
+        a, c, r = self.args, self.cfg, self.ref
+        t0 = time.perf_counter()
+        rolls = [self.pol.rollout(self.prompts[i], a.new_tokens, self.seq, c.eos_id, c.pad_id, int(self.seeds[i]))
+                 for i in range(self.n)]
+        stack = lambda k: np.stack([x[k] for x in rolls])  # noqa: E731
+        r.grpo_update(self.pol, self.refm, self.n, stack("input"), stack("target"), stack("mask"),
+                      stack("old_lp"), self.rewards, 0.2, 0.04, 1e-5)
+        dt = time.perf_counter() - t0
+        return sum(len(x["tokens"]) for x in rolls) / dt, dt
+
+    def describe(self):
+        threads = os.environ.get("OPENBLAS_NUM_THREADS", str(_host_threads()))
+        return (f"one group of {self.n} rollouts (prompt {self.args.prompt_len}, {self.args.new_tokens} new "
+                f"tokens, S={self.seq}) + their GRPO update, reference CPU build, OpenBLAS 0.3.30 "
+                f"(numpy-bundled) on {threads} threads; host: {cpu_model()}")
+
+
+def cpu_baseline(args):
+    """The GPU arm's reported CPU baseline (rank 0, one GPU): one timed group of rollouts."""
     from oracle import ref
     if not ref.available():
-        return None, "oracle/_ref not built"
-    n = args.cpu_rollouts
-    prompts, seeds, rewards = grpo_workload(1, n, args.prompt_len, MLA36M.vocab_size, 0.3)
-    rewards[0], rewards[-1] = 1.0, 0.0
-    seq = args.prompt_len + args.new_tokens
-    pol = ref.Session(MLA36M, 0, optimizer=AdamWConfig().as_list())
-    refm = ref.Session(MLA36M, 0)
-    rates = []
-    for _ in range(steps):
-        t0 = time.perf_counter()
-        rolls = [pol.rollout(prompts[i], args.new_tokens, seq, MLA36M.eos_id, MLA36M.pad_id,
-                             int(seeds[i])) for i in range(n)]
-        stack = lambda k: np.stack([r[k] for r in rolls])
-        ref.grpo_update(pol, refm, n, stack("input"), stack("target"), stack("mask"),
-                        stack("old_lp"), rewards, 0.2, 0.04, 1e-5)
-        dt = time.perf_counter() - t0
-        rates.append(sum(len(r["tokens"]) for r in rolls) / dt)
-    sample = (f"{n} rollouts (prompt {args.prompt_len}, {args.new_tokens} new tokens, S={seq}) "
-              f"+ their GRPO update (group {n}), reference CPU build, OpenBLAS")
-    return {"value": statistics.median(rates), "unit": "tok/s", "cores": os.cpu_count(),
-            "kind": "reference", "sample": sample}, None
+        return None
+    smp = CpuSample(args, args.cpu_rollouts)
+    rate, _ = smp.run()
+    return {"value": rate, "unit": "tok/s", "cores": int(os.environ.get("OPENBLAS_NUM_THREADS", _host_threads())),
+            "host_threads": _host_threads(), "cpu_model": cpu_model(), "kind": "reference",
+            "sample": smp.describe()}
 
 
 def run_reference(args, rank, world):
+    """--impl reference: rank 0 alone times the reference CPU path; the sample per step is one
+    group of 8, 4 or 2 rollouts, the largest whose W + K steps fit the time budget."""
     if rank != 0:
         return
-    for _ in range(max(args.warmup, 0)):
-        pass  # the bounded sample has no warm-up state to build; W is honoured by step count
-    res, err = cpu_baseline(args, steps=args.steps)
-    if res is None:
-        print(json.dumps({"impl": "reference", "unavailable": err}))
+    from oracle import ref
+    if not ref.available():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref (the reference CPU build) is not built"}))
         return
-    line = {"metric": METRIC, "value": res["value"], "unit": "tok/s", "n_gpus": world,
+    probe = CpuSample(args, 2)
+    _, dt = probe.run()  # untimed: first-touch of the weights, thread pool start-up
+    per_rollout = dt / 2
+    steps = max(args.warmup, 0) + args.steps
+    n = 2
+    for g in (8, 4):
+        if steps * g * per_rollout <= args.reference_budget:
+            n = g
+            break
+    smp = probe if n == 2 else CpuSample(args, n)
+    for _ in range(max(args.warmup, 0)):
+        smp.run()
+    rates = [smp.run()[0] for _ in range(args.steps)]
+    value = statistics.median(rates)
+    res = {"value": value, "unit": "tok/s", "cores": int(os.environ["OPENBLAS_NUM_THREADS"]),
+           "host_threads": _host_threads(), "cpu_model": cpu_model(), "kind": "reference",
+           "sample": smp.describe()}
+    line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "impl": "reference",
             "higher_is_better": True, "dtype": "f32", "data": "synthetic",
             "config": workload_config(args, world),
             "cpu_baseline": res,
-            "e2e": {"value": res["value"], "unit": "tok/s", "h2d_bytes_per_step": 0,
+            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     print(json.dumps(line))
 
@@ -173,26 +239,56 @@ def workload_config(args, world):
 
 
 # ---------------------------------------------------------------------------- ours
+def fixed_batch(args, cfg, n_total, prompts_all):
+    """A teacher-forced GRPO batch for the whole job, the same on every rank count: each
+    rollout is its prompt followed by new_tokens fixed ids (np.random seed 6), laid out as
+    completion_batch does (trainer.cpp:386-408)."""
+    seq = args.prompt_len + args.new_tokens
+    comp = np.random.default_rng(6).integers(0, cfg.vocab_size - 8, (n_total, args.new_tokens)).astype(np.uint16)
+    ids = np.concatenate([prompts_all, comp], axis=1)
+    inp = np.full((n_total, seq), cfg.pad_id, np.uint16)
+    tgt = np.full((n_total, seq), cfg.pad_id, np.uint16)
+    mask = np.zeros((n_total, seq), np.float32)
+    inp[:, :seq - 1] = ids[:, :-1]
+    tgt[:, :seq - 1] = ids[:, 1:]
+    mask[:, args.prompt_len - 1:seq - 1] = 1
+    return inp, tgt, mask
+
+
+def gemm_algorithmic_flops(cfg, rollouts, seq, prompt_len):
+    """Algorithmic tensor-core work of one step's event-timed products on one rank: every
+    teacher-forced token passes the model's matrices (2 x 27,374,720 flops) and the vocabulary
+    head (2 x d x V) five times (old-policy, frozen-reference and policy forwards, the backward
+    at twice a forward), and every prompt token passes the matrices once in the prefill. The
+    fp32-accurate head's three fp16 terms count once: their extra work is an implementation
+    cost, not algorithmic work. Attention is its own kernel class."""
+    mats = 0
+    for _, (r, c), role in cfg.parameter_shapes()[2:]:
+        if role != "norm_scale":
+            mats += r * c
+    model = 2.0 * mats
+    vocab = 2.0 * cfg.d_model * cfg.vocab_size
+    return rollouts * seq * 5 * (model + vocab) + rollouts * prompt_len * model
+
+
+def decode_algorithmic_bytes(cfg, n_params, rollouts, prompt_len, new_tokens):
+    """HBM bytes one rank's rollout decode must move: per decode step the fp16 weights once
+    (2 x P) and every row's latent cache, (kv rank + rope) fp16 values per cached position and
+    layer; decode step k (1 <= k < new_tokens) attends prompt_len + k positions."""
+    kv = 2 * (cfg.kv_lora_rank + cfg.head_dim_rope) * cfg.n_layers
+    return sum(2.0 * n_params + rollouts * (prompt_len + k) * kv for k in range(1, new_tokens))
+
+
 def main():
     args = parse()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    dist = None
-    if world > 1:
-        import datetime
-
-        import torch
-        import torch.distributed as dist
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
-                                device_id=torch.device("cuda", local))
     if args.impl == "reference":
-        run_reference(args, rank, world)
-        if dist:
-            dist.barrier()
-            dist.destroy_process_group()
+        run_reference(args, rank, world)  # CPU only: no process group, no GPU
         return
+
+    import datetime
 
     import torch
 
@@ -201,6 +297,15 @@ def main():
     from cpp_inference_train_engine_b200.config import MLA36M, AdamWConfig
     from cpp_inference_train_engine_b200.rng import grpo_workload
 
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        # harness only (barriers, max over ranks of the timings); the engine's own NCCL
+        # communicator is bootstrapped by distributed.init_comm without torch
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+
     cfg = MLA36M
     n_total = args.prompts * args.group
     try:
@@ -208,9 +313,9 @@ def main():
     except ValueError as e:
         raise SystemExit(str(e))
     seq = args.prompt_len + args.new_tokens
-    prompts, seeds, rewards = grpo_workload(args.prompts, args.group, args.prompt_len,
-                                            cfg.vocab_size, 0.3)
-    prompts, seeds, rewards = prompts[sl].copy(), seeds[sl].copy(), rewards[sl].copy()
+    prompts_all, seeds, rewards_all = grpo_workload(args.prompts, args.group, args.prompt_len,
+                                                    cfg.vocab_size, 0.3)
+    prompts, seeds, rewards = prompts_all[sl].copy(), seeds[sl].copy(), rewards_all[sl].copy()
 
     W = E.init_params(cfg, 0)
     pol = E.make_execution(cfg, W, optimizer=AdamWConfig(), device=local)
@@ -218,6 +323,28 @@ def main():
     if world > 1:
         D.init_comm(pol, rank, world)
     stream = torch.cuda.ExternalStream(pol.stream, device=local)
+
+    def barrier():
+        torch.cuda.synchronize(local)
+        if dist:
+            dist.barrier()
+
+    fixed = None
+    if not args.no_fixed_check:
+        # One GRPO update on a fixed teacher-forced batch of the whole job: its loss and
+        # pre-clip gradient norm are global sums, so they must not depend on the rank count.
+        inp, tgt, mask = fixed_batch(args, cfg, n_total, prompts_all)
+        inp, tgt, mask = inp[sl].copy(), tgt[sl].copy(), mask[sl].copy()
+        R = inp.shape[0]
+        lp = pol.log_probabilities(inp, tgt, R, seq).reshape(R, seq)
+        phase = np.arange(n_total * seq, dtype=np.float64).reshape(n_total, seq)[sl]
+        old = (lp + 0.3 * np.sin(phase) * mask).astype(np.float32)
+        out = pol.grpo_step(refm, inp, tgt, mask, old, rewards, args.group, n_total=n_total,
+                            clip=0.2, klc=0.04, learning_rate=1e-5)
+        fixed = {"loss": out["loss"], "kl": out["kl"], "grad_norm": out["grad_norm"],
+                 "batch": f"{n_total} x {seq} teacher-forced, fixed ids (seed 6), old = lp + 0.3 sin"}
+        pol.upload(W)  # back to the initial weights, zero moments, step 0
+        barrier()
 
     def one_step(step_idx):
         # The rollout seeds advance per update like the trainer's Rng(seed) stream.
@@ -227,11 +354,6 @@ def main():
         out = pol.grpo_step(refm, r["input"], r["target"], r["mask"], r["old_lp"], rewards,
                             args.group, n_total=n_total, clip=0.2, klc=0.04, learning_rate=1e-5)
         return r, out
-
-    def barrier():
-        torch.cuda.synchronize(local)
-        if dist:
-            dist.barrier()
 
     for i in range(args.warmup):
         one_step(i)
@@ -274,13 +396,14 @@ def main():
     launches = pol.kernel_launches + refm.kernel_launches - launches0
     dev_ms = sum(prof_p[k][0] for k in ("prefill", "decode", "sample", "logprob", "backward",
                                         "adamw", "allreduce")) + prof_r["logprob"][0]
+    decode_ms = (prof_p["decode"][0] + prof_p["sample"][0]) / args.steps
     if dist:
-        t = torch.tensor([e2e_ms, dev_ms, float(toks)], device=f"cuda:{local}", dtype=torch.float64)
+        t = torch.tensor([e2e_ms, dev_ms, float(toks), decode_ms], device=f"cuda:{local}", dtype=torch.float64)
         mx = t.clone()
         dist.all_reduce(mx, op=dist.ReduceOp.MAX)
         sm = t.clone()
         dist.all_reduce(sm, op=dist.ReduceOp.SUM)
-        e2e_ms, dev_ms, toks = float(mx[0]), float(mx[1]), int(sm[2])
+        e2e_ms, dev_ms, toks, decode_ms = float(mx[0]), float(mx[1]), int(sm[2]), float(mx[3])
     if rank == 0:
         pk = peaks()
         kern = {}
@@ -291,23 +414,40 @@ def main():
             work = prof_p[k][2] + prof_r[k][2]
             kern[k] = {"ms": ms, "launches": n, "work": work}
         top = max(kern, key=lambda k: kern[k]["ms"])
+        R = prompts.shape[0]
+        if top == "k_gemm":
+            work = gemm_algorithmic_flops(cfg, R, seq, args.prompt_len) * args.steps
+            how = ("algorithmic flops: rollouts x S x 5 x (2 x 27,374,720 + 2 d V) + prompt tokens x "
+                   "2 x 27,374,720, over the class's event-timed launches")
+        else:
+            work = kern[top]["work"]
+            how = "work as counted per launch"
         tensor = top in ("k_gemm", "k_flash_fwd", "k_flash_bwd")
         sec = kern[top]["ms"] / 1e3
-        achieved = (kern[top]["work"] / sec / 1e12) if tensor else (kern[top]["work"] / sec / 1e9)
+        achieved = (work / sec / 1e12) if tensor else (work / sec / 1e9)
         peak = pk["tflops"] if tensor else pk["hbm_gbs"]
         roofline = {"kernel": top, "bound": "tensor" if tensor else "hbm",
                     "achieved": achieved, "peak": peak, "unit": "TFLOP/s" if tensor else "GB/s",
-                    "frac": achieved / peak, "peak_source": pk["source"] + " (sustained)",
-                    "launches": kern[top]["launches"],
+                    "frac": achieved / peak, "peak_source": pk["source"] + " (sustained bf16)",
+                    "work": how, "launches": kern[top]["launches"],
                     "avg_launch_us": 1e3 * kern[top]["ms"] / max(kern[top]["launches"], 1),
-                    "traffic": None}
+                    # DRAM bytes of one vocabulary-head launch (the class's largest shape),
+                    # single-launch ncu capture at M = 8,192 scaled to this chunk's M
+                    "traffic": vocab_head_traffic(seq, R),
+                    "traffic_kernel": "gemm_tc_pair_kernel, vocabulary head M x 16384 x 1536"}
+        dec_bytes = decode_algorithmic_bytes(cfg, pol.n_params, R, args.prompt_len, args.new_tokens)
+        dec_gbs = dec_bytes / (decode_ms / 1e3) / 1e9 if decode_ms else None
+        roofline_decode = {"phase": "rollout decode + sampling (per rank, slowest rank's time)",
+                           "bound": "hbm", "achieved": dec_gbs, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                           "frac": dec_gbs / pk["hbm_gbs"] if dec_gbs else None,
+                           "bytes_per_step": dec_bytes, "ms_per_step": decode_ms,
+                           "work": "sum over decode steps of 2 P (fp16 weights) + rows x ctx x 2,880 B"}
         phases = {k: round(prof_p[k][0] / args.steps, 3) for k in
                   ("prefill", "decode", "sample", "logprob", "backward", "adamw", "allreduce")}
         phases["reference_logprob"] = round(prof_r["logprob"][0] / args.steps, 3)
-        decode_ms = (prof_p["decode"][0] + prof_p["sample"][0] + prof_p["prefill"][0]) / args.steps
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
-            cpu, _ = cpu_baseline(args, steps=1)
+            cpu = cpu_baseline(args)
         line = {
             "metric": METRIC, "value": toks / (dev_ms / 1e3), "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": dev_ms / args.steps,
@@ -318,11 +458,12 @@ def main():
                     "ms_per_step": e2e_ms / args.steps,
                     "h2d_bytes_per_step": h2d // args.steps, "d2h_bytes_per_step": d2h // args.steps},
             "rollout_tokens_per_step": toks // args.steps,
-            "rollout_decode_tok_s": toks / (decode_ms * args.steps / 1e3) if decode_ms else None,
             "phases_ms_per_step": phases,
             "kernels": {k: {"ms_per_step": round(v["ms"] / args.steps, 3),
                             "launches_per_step": v["launches"] // args.steps} for k, v in kern.items()},
             "roofline": roofline,
+            "roofline_decode": roofline_decode,
+            "fixed_update": fixed,
             "cpu_baseline": cpu,
             "gpu_launches": launches,
             "clocks": clocks.summary(),
@@ -335,6 +476,15 @@ def main():
     if dist:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def vocab_head_traffic(seq, rollouts):
+    """DRAM bytes of one vocabulary-head launch of the teacher-forced pass at this workload's
+    chunk size: the committed single-launch capture of the CTA-pair kernel (912 MB read and
+    written at M = 8,192 tokens, logits stored) scaled by M, since both its logits stream and
+    its operand re-reads grow with the number of M-tiles."""
+    chunk = min(rollouts, max(1, 196608 // seq)) * seq
+    return 911.9e6 * chunk / 8192.0
 
 
 if __name__ == "__main__":

@@ -673,22 +673,36 @@ int mm_decode_attention_noalloc(const float* q, const void* cache, int64_t cache
         cache_seq_stride < mm::dec::W)
         return MM_INVALID_ARGUMENT;
     if (splits > 1 && static_cast<long long>(batch) * splits > kStaticPartialSlots) return MM_INVALID_ARGUMENT;
-    float* part = static_partials_address();
-    if (!part) return MM_GPU_ERROR;
+    // the static array is read only by the split combine; one split writes `out` directly
+    float* part = nullptr;
+    if (splits > 1 && !(part = static_partials_address())) return MM_GPU_ERROR;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     try {
         mm::set_dynamic_smem<mm::decode_attention_row_kernel>(mm::dec::kRowSmem);
     } catch (...) {
         return MM_GPU_ERROR;
     }
-    mm::decode_attention_row_kernel<<<mm::blocks_for(static_cast<long long>(batch) * splits, mm::dec::kWarps),
-                                      32 * mm::dec::kWarps, mm::dec::kRowSmem, s>>>(
-        q, static_cast<const __half*>(cache), cache_seq_stride, pos, batch, splits, scale, static_cast<__half*>(out),
-        part, static_cast<const float*>(nullptr), static_cast<const float*>(nullptr));
-    if (splits > 1)
-        mm::decode_attention_combine_kernel<<<mm::blocks_for(static_cast<long long>(batch) * mm::dec::H * 32, 128), 128, 0, s>>>(
-            part, splits, batch, static_cast<__half*>(out));
-    if (cudaGetLastError() != cudaSuccess) return MM_GPU_ERROR;
+    // Launch errors are taken from the launches themselves, not cudaGetLastError, so an error
+    // an earlier call left pending stays with its owner and does not fail this call.
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(mm::blocks_for(static_cast<long long>(batch) * splits, mm::dec::kWarps));
+    cfg.blockDim = dim3(32 * mm::dec::kWarps);
+    cfg.dynamicSmemBytes = mm::dec::kRowSmem;
+    cfg.stream = s;
+    if (cudaLaunchKernelEx(&cfg, mm::decode_attention_row_kernel, q, static_cast<const __half*>(cache),
+                           static_cast<long long>(cache_seq_stride), static_cast<const int*>(pos), batch, splits, scale,
+                           static_cast<__half*>(out), part, static_cast<const float*>(nullptr),
+                           static_cast<const float*>(nullptr)) != cudaSuccess)
+        return MM_GPU_ERROR;
+    if (splits > 1) {
+        cudaLaunchConfig_t cc = {};
+        cc.gridDim = dim3(mm::blocks_for(static_cast<long long>(batch) * mm::dec::H * 32, 128));
+        cc.blockDim = dim3(128);
+        cc.stream = s;
+        if (cudaLaunchKernelEx(&cc, mm::decode_attention_combine_kernel, static_cast<const float*>(part), splits, batch,
+                               static_cast<__half*>(out)) != cudaSuccess)
+            return MM_GPU_ERROR;
+    }
     if (cudaStreamSynchronize(s) != cudaSuccess) return MM_GPU_ERROR;
     return MM_OK;
 }

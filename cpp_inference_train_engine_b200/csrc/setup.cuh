@@ -330,7 +330,7 @@ inline void create_context(Context& cx, const mm_model_desc& desc, int device, b
         cx.d_nonfinite_out = a.template take<int>(1);
         cx.d_sums = a.template take<GrpoSums>(1);
         cx.d_scale = a.template take<float>(2);
-        cx.d_any = a.template take<int>(1);
+        cx.d_any = a.template take<int>(2);  // [flag, a rank's batch was invalid]
         cx.d_one = a.template take<float>(1);
     };
     Sizer s2;

@@ -109,6 +109,70 @@ inline void allreduce(Context& cx, void* buf, size_t count, ncclDataType_t t, nc
     if (r != ncclSuccess) fail(MM_GPU_ERROR, std::string("ncclAllReduce: ") + nccl().getErrorString(r));
 }
 
+// Waits for the context stream once a collective has been enqueued on it. With several
+// ranks on a non-blocking communicator the wait is bounded: the stream and the
+// communicator's asynchronous error are polled, and a collective that has not completed
+// within MM_NCCL_INIT_TIMEOUT seconds (a peer stopped, or took a different path) aborts the
+// communicator, marks the context unusable and fails with gpu_error instead of hanging.
+inline void sync_collective(Context& cx) {
+    if (cx.world <= 1 || !cx.nccl_comm || !cx.nccl_nonblocking) {
+        MM_CUDA_CHECK(cudaStreamSynchronize(cx.stream));
+        return;
+    }
+    ncclComm_t comm = static_cast<ncclComm_t>(cx.nccl_comm);
+    const double limit = nccl_init_timeout();
+    const auto t0 = std::chrono::steady_clock::now();
+    for (long long polls = 0;; ++polls) {
+        const cudaError_t e = cudaStreamQuery(cx.stream);
+        if (e == cudaSuccess) return;
+        if (e != cudaErrorNotReady) MM_CUDA_CHECK(e);
+        ncclResult_t st = ncclSuccess;
+        nccl().commGetAsyncError(comm, &st);
+        const double waited = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+        if ((st != ncclSuccess && st != ncclInProgress) || waited > limit) {
+            nccl().commAbort(comm);
+            cx.nccl_comm = nullptr;
+            cx.unusable = true;
+            if (st != ncclSuccess && st != ncclInProgress)
+                fail(MM_GPU_ERROR, std::string("collective failed: ") + nccl().getErrorString(st));
+            fail(MM_GPU_ERROR, "collective did not complete within " + std::to_string(static_cast<int>(limit)) +
+                                   " s (a peer rank stopped or diverged); communicator aborted");
+        }
+        if (polls < 2000)
+            std::this_thread::yield();
+        else
+            std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
+}
+
+// First failed host-side check of a batch: the code and message to report. On several ranks
+// the status travels with the step's first collective, so every rank fails together instead
+// of the others blocking in a collective the failing rank never joins.
+struct BatchCheck {
+    int code = 0;
+    std::string msg;
+    void set(int c, const char* m) {
+        if (!code) {
+            code = c;
+            msg = m;
+        }
+    }
+};
+
+// Max-reduces [flag0, invalid] over the ranks (flag0 as computed on the device, invalid =
+// this rank's BatchCheck) and fails on every rank when any rank's batch was invalid.
+// Returns the reduced flag0.
+inline int reduce_flag_and_check(Context& cx, int* d_flags, const BatchCheck& bad) {
+    MM_CUDA_CHECK(cudaMemsetAsync(d_flags + 1, bad.code ? 1 : 0, 4, cx.stream));
+    allreduce(cx, d_flags, 2, ncclInt32, ncclMax);
+    int flags[2] = {0, 0};
+    MM_CUDA_CHECK(cudaMemcpyAsync(flags, d_flags, 8, cudaMemcpyDeviceToHost, cx.stream));
+    sync_collective(cx);
+    if (bad.code) fail(bad.code, bad.msg);
+    if (flags[1]) fail(MM_INVALID_ARGUMENT, "a peer rank rejected its batch");
+    return flags[0];
+}
+
 // ------------------------------------------------------------------ timing
 struct PhaseTimer {
     Context& cx;
@@ -145,7 +209,7 @@ inline double adamw_update(Context& cx, float lr) {
     MM_CUDA_CHECK(cudaMemcpyAsync(&flags[0], cx.d_nonfinite, 4, cudaMemcpyDeviceToHost, cx.stream));
     MM_CUDA_CHECK(cudaMemcpyAsync(&flags[1], cx.d_nonfinite_out, 4, cudaMemcpyDeviceToHost, cx.stream));
     MM_CUDA_CHECK(cudaMemcpyAsync(&norm, cx.d_norm, 8, cudaMemcpyDeviceToHost, cx.stream));
-    MM_CUDA_CHECK(cudaStreamSynchronize(cx.stream));
+    sync_collective(cx);
     if (flags[0]) fail(MM_NUMERICAL_ERROR, "Nonfinite gradient before optimizer update");
     cx.steps = next;
     refresh_derived(cx, false);
@@ -220,41 +284,65 @@ inline void log_probs_host(Context& cx, const uint16_t* input, const uint16_t* t
 }
 
 // ------------------------------------------------------------------ GRPO update
+// Records, on `from`, the point after which `to` may proceed (cudaStreamWaitEvent) — used
+// so the frozen reference's next forward never overwrites log-probs a pending copy on the
+// policy stream still reads.
+struct StreamOrder {
+    cudaEvent_t ev = nullptr;
+    bool recorded = false;
+    StreamOrder() { MM_CUDA_CHECK(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming)); }
+    ~StreamOrder() { cudaEventDestroy(ev); }
+    void record(cudaStream_t from) {
+        MM_CUDA_CHECK(cudaEventRecord(ev, from));
+        recorded = true;
+    }
+    void wait(cudaStream_t to) {
+        if (recorded) MM_CUDA_CHECK(cudaStreamWaitEvent(to, ev, 0));
+    }
+};
+
 inline mm_step_result grpo_step(Context& pc, Context& rc, const uint16_t* input, const uint16_t* target,
                                 const float* mask, const float* old_lp, const float* rewards, int n, int S, int G,
                                 long long n_total, float clip, float klc, float lr) {
     if (!pc.trainable) fail(MM_INVALID_ARGUMENT, "policy context must be trainable");
     if (pc.device != rc.device) fail(MM_INVALID_ARGUMENT, "policy and reference must share a device");
+    BatchCheck bad;
     if (n < 1 || G < 2 || n % G || S < 1 || S > pc.c.maxS || n_total < n)
-        fail(MM_INVALID_ARGUMENT, "rollouts must form whole groups within the context");
-    if (!std::isfinite(clip) || clip <= 0 || clip >= 1 || !std::isfinite(klc) || klc < 0)
-        fail(MM_NUMERICAL_ERROR, "Invalid or unbounded GRPO token statistics");
-    const long long NS = static_cast<long long>(n) * S;
-    std::vector<int> sup(n, 0);
-    for (int i = 0; i < n; ++i) {
-        for (int t = 0; t < S; ++t) {
-            const float mv = mask[static_cast<long long>(i) * S + t];
-            if (mv != 0.f && mv != 1.f) fail(MM_INVALID_ARGUMENT, "Loss mask must contain zero or one");
-            sup[i] += mv == 1.f ? 1 : 0;
+        bad.set(MM_INVALID_ARGUMENT, "rollouts must form whole groups within the context");
+    else if (!std::isfinite(clip) || clip <= 0 || clip >= 1 || !std::isfinite(klc) || klc < 0)
+        bad.set(MM_NUMERICAL_ERROR, "Invalid or unbounded GRPO token statistics");
+    std::vector<int> sup(std::max(n, 0), 0);
+    if (!bad.code) {
+        const long long NS = static_cast<long long>(n) * S;
+        for (int i = 0; i < n && !bad.code; ++i) {
+            for (int t = 0; t < S; ++t) {
+                const float mv = mask[static_cast<long long>(i) * S + t];
+                if (mv != 0.f && mv != 1.f) {
+                    bad.set(MM_INVALID_ARGUMENT, "Loss mask must contain zero or one");
+                    break;
+                }
+                sup[i] += mv == 1.f ? 1 : 0;
+            }
+            if (!bad.code && sup[i] == 0) bad.set(MM_INVALID_ARGUMENT, "Batch has no supervised tokens");
         }
-        if (sup[i] == 0) fail(MM_INVALID_ARGUMENT, "Batch has no supervised tokens");
+        for (long long i = 0; i < NS && !bad.code; ++i)
+            if (input[i] >= pc.c.V || target[i] >= pc.c.V) bad.set(MM_INVALID_ARGUMENT, "Input token exceeds vocabulary");
+        for (int i = 0; i < n && !bad.code; ++i)
+            if (!std::isfinite(rewards[i])) bad.set(MM_INVALID_ARGUMENT, "Invalid reward group");
     }
-    for (long long i = 0; i < NS; ++i)
-        if (input[i] >= pc.c.V || target[i] >= pc.c.V) fail(MM_INVALID_ARGUMENT, "Input token exceeds vocabulary");
-    for (int i = 0; i < n; ++i)
-        if (!std::isfinite(rewards[i])) fail(MM_INVALID_ARGUMENT, "Invalid reward group");
-    char* base = static_cast<char*>(pc.stage.get(static_cast<size_t>(n) * 16 + 1024));
+    if (bad.code && pc.world <= 1) fail(bad.code, bad.msg);
+    char* base = static_cast<char*>(pc.stage.get(static_cast<size_t>(std::max(n, 1)) * 16 + 1024));
     float* d_rew = reinterpret_cast<float*>(base);
     float* d_adv = reinterpret_cast<float*>(base + round_up(n * 4LL, 256));
     int* d_sup = reinterpret_cast<int*>(base + 2 * round_up(n * 4LL, 256));
-    MM_CUDA_CHECK(cudaMemcpyAsync(d_rew, rewards, n * 4, cudaMemcpyHostToDevice, pc.stream));
-    MM_CUDA_CHECK(cudaMemcpyAsync(d_sup, sup.data(), n * 4, cudaMemcpyHostToDevice, pc.stream));
-    MM_CUDA_CHECK(cudaMemsetAsync(pc.d_any, 0, 4, pc.stream));
-    MM_LAUNCH_CX(pc, advantages_kernel, blocks_for(n / G, 128), 128, 0, d_rew, n / G, G, 1e-6f, d_adv, pc.d_any);
-    allreduce(pc, pc.d_any, 1, ncclInt32, ncclMax);
-    int any = 0;
-    MM_CUDA_CHECK(cudaMemcpyAsync(&any, pc.d_any, 4, cudaMemcpyDeviceToHost, pc.stream));
-    MM_CUDA_CHECK(cudaStreamSynchronize(pc.stream));
+    MM_CUDA_CHECK(cudaMemsetAsync(pc.d_any, 0, 8, pc.stream));
+    if (!bad.code) {
+        MM_CUDA_CHECK(cudaMemcpyAsync(d_rew, rewards, n * 4, cudaMemcpyHostToDevice, pc.stream));
+        MM_CUDA_CHECK(cudaMemcpyAsync(d_sup, sup.data(), n * 4, cudaMemcpyHostToDevice, pc.stream));
+        MM_LAUNCH_CX(pc, advantages_kernel, blocks_for(n / G, 128), 128, 0, d_rew, n / G, G, 1e-6f, d_adv, pc.d_any);
+    }
+    // the global skip rule (trainer.cpp:818-820) and every rank's batch check in one collective
+    const int any = reduce_flag_and_check(pc, pc.d_any, bad);
     mm_step_result res{};
     if (!any) {
         res.skipped = 1;
@@ -266,11 +354,15 @@ inline mm_step_result grpo_step(Context& pc, Context& rc, const uint16_t* input,
     ensure_workspace(pc, std::min(n, per) * S, true);
     ensure_workspace(rc, std::min(n, per) * S, rc.ws.tape);
     Workspace& w = pc.ws;
+    StreamOrder ref_lp_copied;
     for (int r0 = 0; r0 < n; r0 += per) {
         const int bc = std::min(per, n - r0);
         const long long T = static_cast<long long>(bc) * S, off = static_cast<long long>(r0) * S;
         {
             PhaseTimer t(pc, kPhLogprob);
+            // the previous chunk's log-probs must have left rc.ws.lp before this forward
+            // rewrites it (the copy is queued on the policy stream behind its backward)
+            ref_lp_copied.wait(rc.stream);
             MM_CUDA_CHECK(cudaMemcpyAsync(rc.ws.tokens, input + off, T * 2, cudaMemcpyHostToDevice, rc.stream));
             MM_CUDA_CHECK(cudaMemcpyAsync(rc.ws.targets, target + off, T * 2, cudaMemcpyHostToDevice, rc.stream));
             reference_forward(pc, rc, bc, S);
@@ -281,6 +373,7 @@ inline mm_step_result grpo_step(Context& pc, Context& rc, const uint16_t* input,
             // the reference's log-probs reach the policy stream only after its forward completes
             MM_CUDA_CHECK(cudaStreamSynchronize(rc.stream));
             MM_CUDA_CHECK(cudaMemcpyAsync(w.ref_lp, rc.ws.lp, T * 4, cudaMemcpyDeviceToDevice, pc.stream));
+            ref_lp_copied.record(pc.stream);
             forward_chunk(pc, bc, S, true, kVocabAll, true, nullptr, 0, 0, nullptr);
         }
         PhaseTimer t(pc, kPhBackward);
@@ -298,9 +391,15 @@ inline mm_step_result grpo_step(Context& pc, Context& rc, const uint16_t* input,
     GrpoSums sums{};
     MM_CUDA_CHECK(cudaMemcpyAsync(&sums, pc.d_sums, sizeof(GrpoSums), cudaMemcpyDeviceToHost, pc.stream));
     MM_CUDA_CHECK(cudaStreamSynchronize(pc.stream));
-    if (sums.rejected) fail(MM_NUMERICAL_ERROR, "Invalid or unbounded GRPO token statistics");
-    allreduce(pc, pc.d_sums, 2, ncclFloat64, ncclSum);
+    if (sums.rejected && pc.world <= 1) fail(MM_NUMERICAL_ERROR, "Invalid or unbounded GRPO token statistics");
+    // loss and kl sums, and every rank's rejected-token count, in one collective: a rejection
+    // anywhere fails the step on every rank before the gradient all-reduce
+    const double rejected = sums.rejected ? 1.0 : 0.0;
+    MM_CUDA_CHECK(cudaMemcpyAsync(&pc.d_sums->rejected_ranks, &rejected, 8, cudaMemcpyHostToDevice, pc.stream));
+    allreduce(pc, pc.d_sums, 3, ncclFloat64, ncclSum);
     MM_CUDA_CHECK(cudaMemcpyAsync(&sums, pc.d_sums, sizeof(GrpoSums), cudaMemcpyDeviceToHost, pc.stream));
+    sync_collective(pc);
+    if (sums.rejected_ranks != 0) fail(MM_NUMERICAL_ERROR, "Invalid or unbounded GRPO token statistics");
     res.grad_norm = adamw_update(pc, lr);
     res.loss = sums.loss;
     res.kl = sums.kl;
@@ -320,12 +419,20 @@ inline mm_step_result dpo_step(Context& pc, Context& rc, const uint16_t* input, 
                                double* margins) {
     if (!pc.trainable) fail(MM_INVALID_ARGUMENT, "policy context must be trainable");
     if (pc.device != rc.device) fail(MM_INVALID_ARGUMENT, "policy and reference must share a device");
-    if (n < 1 || S < 1 || S > pc.c.maxS || n_total < n) fail(MM_INVALID_ARGUMENT, "Invalid preference batch");
-    if (!std::isfinite(beta) || beta <= 0) fail(MM_INVALID_ARGUMENT, "Invalid DPO beta");
-    const long long NS = 2LL * n * S;
-    for (long long i = 0; i < NS; ++i) {
-        if (mask[i] != 0.f && mask[i] != 1.f) fail(MM_INVALID_ARGUMENT, "Loss mask must contain zero or one");
-        if (input[i] >= pc.c.V || target[i] >= pc.c.V) fail(MM_INVALID_ARGUMENT, "Input token exceeds vocabulary");
+    BatchCheck bad;
+    if (n < 1 || S < 1 || S > pc.c.maxS || n_total < n) bad.set(MM_INVALID_ARGUMENT, "Invalid preference batch");
+    else if (!std::isfinite(beta) || beta <= 0) bad.set(MM_INVALID_ARGUMENT, "Invalid DPO beta");
+    if (!bad.code) {
+        const long long NS = 2LL * n * S;
+        for (long long i = 0; i < NS && !bad.code; ++i) {
+            if (mask[i] != 0.f && mask[i] != 1.f) bad.set(MM_INVALID_ARGUMENT, "Loss mask must contain zero or one");
+            else if (input[i] >= pc.c.V || target[i] >= pc.c.V) bad.set(MM_INVALID_ARGUMENT, "Input token exceeds vocabulary");
+        }
+    }
+    if (bad.code && pc.world <= 1) fail(bad.code, bad.msg);
+    if (pc.world > 1) {  // every rank's batch check, before any rank starts the passes
+        MM_CUDA_CHECK(cudaMemsetAsync(pc.d_any, 0, 8, pc.stream));
+        reduce_flag_and_check(pc, pc.d_any, bad);
     }
     MM_CUDA_CHECK(cudaMemsetAsync(pc.g, 0, sizeof(float) * pc.P_dev, pc.stream));
     MM_CUDA_CHECK(cudaMemsetAsync(pc.d_sums, 0, sizeof(GrpoSums), pc.stream));
@@ -336,11 +443,13 @@ inline mm_step_result dpo_step(Context& pc, Context& rc, const uint16_t* input, 
     ensure_workspace(pc, 2 * std::min(n, per) * S, true);
     ensure_workspace(rc, 2 * std::min(n, per) * S, rc.ws.tape);
     Workspace& w = pc.ws;
+    StreamOrder ref_lp_copied;
     for (int p0 = 0; p0 < n; p0 += per) {
         const int bp = std::min(per, n - p0), rows = 2 * bp;
         const long long T = static_cast<long long>(rows) * S, off = 2LL * p0 * S;
         {
             PhaseTimer t(pc, kPhLogprob);
+            ref_lp_copied.wait(rc.stream);  // the previous chunk's copy out of rc.ws.lp is done
             MM_CUDA_CHECK(cudaMemcpyAsync(rc.ws.tokens, input + off, T * 2, cudaMemcpyHostToDevice, rc.stream));
             MM_CUDA_CHECK(cudaMemcpyAsync(rc.ws.targets, target + off, T * 2, cudaMemcpyHostToDevice, rc.stream));
             reference_forward(pc, rc, rows, S);
@@ -350,6 +459,7 @@ inline mm_step_result dpo_step(Context& pc, Context& rc, const uint16_t* input, 
             // the reference's log-probs reach the policy stream only after its forward completes
             MM_CUDA_CHECK(cudaStreamSynchronize(rc.stream));
             MM_CUDA_CHECK(cudaMemcpyAsync(w.ref_lp, rc.ws.lp, T * 4, cudaMemcpyDeviceToDevice, pc.stream));
+            ref_lp_copied.record(pc.stream);
             forward_chunk(pc, rows, S, true, kVocabAll, true, nullptr, 0, 0, nullptr);
         }
         PhaseTimer t(pc, kPhBackward);
@@ -368,7 +478,7 @@ inline mm_step_result dpo_step(Context& pc, Context& rc, const uint16_t* input, 
     allreduce(pc, pc.d_sums, 2, ncclFloat64, ncclSum);
     GrpoSums sums{};
     MM_CUDA_CHECK(cudaMemcpyAsync(&sums, pc.d_sums, sizeof(GrpoSums), cudaMemcpyDeviceToHost, pc.stream));
-    MM_CUDA_CHECK(cudaStreamSynchronize(pc.stream));
+    sync_collective(pc);
     if (!std::isfinite(sums.loss)) fail(MM_NUMERICAL_ERROR, "Nonfinite logits or loss");
     mm_step_result res{};
     res.grad_norm = adamw_update(pc, lr);

@@ -105,12 +105,13 @@ __global__ void vocab_grad_kernel(const float* __restrict__ logits, long long ld
 
 struct GrpoSums {
     double loss, kl;
+    double rejected_ranks;       // ranks that rejected a token, summed across ranks
     unsigned int max_coef_bits;  // max |coef| of the current chunk, as float bits
-    int rejected;
+    int rejected;                // tokens this rank rejected
 };
 
 // Per token t of a chunk (rows t in [0, T), sequence = t / S): when mask[t] != 0,
-// coef[t] = nll_coefficient / (n_total * supervised[seq]) in float, and the block's loss/kl
+// coef[t] = float(float(nll_coefficient) / (n_total * supervised[seq])), and the block's loss/kl
 // sums (objective/denominator, in double) go to part[block] for grpo_sums_kernel. Masked
 // tokens get coef 0.
 __global__ void grpo_coef_kernel(const float* __restrict__ lp, const float* __restrict__ old_lp,
@@ -144,8 +145,10 @@ __global__ void grpo_coef_kernel(const float* __restrict__ lp, const float* __re
                 const double den = n_total * static_cast<double>(supervised[t / S]);
                 lo = obj / den;
                 kl = k3 / den;
-                cf = static_cast<float>(c / den);
-                if (!isfinite(obj) || !isfinite(c)) atomicAdd(&sums->rejected, 1);
+                // grpo_objective hands back the coefficient as a float (trainer.cpp:368-369),
+                // which the loop divides by the double denominator and rounds again (:842-843)
+                cf = static_cast<float>(static_cast<double>(static_cast<float>(c)) / den);
+                if (!isfinite(obj) || !(fabs(c) <= 3.4028234663852886e38)) atomicAdd(&sums->rejected, 1);
             }
         }
         coef[t] = cf;

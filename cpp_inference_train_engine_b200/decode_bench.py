@@ -5,9 +5,9 @@ pass: B random prompts of --prompt ids, prefill, then --new tokens per row (gree
 temperature sampling), and reports the decode phase (all steps after the first token,
 which comes from the prefill logits) as tokens/s and against the HBM roofline of
 2·P weight bytes (fp16) plus B·ctx·2880 cache bytes (latent 128 + rope 16 in fp16 over 10
-layers) per step, ctx averaged over the steps. BASELINE config 2 is
-``--batch 1,16,64 --prompt 1024 --new 128``; config 4's decode is ``--batch 2048 --prompt 128
---new 256``.
+layers) per step, ctx averaged over the steps. Decode-only after long prompts is
+``--batch 1,16,64 --prompt 1024 --new 128``; the full GRPO step's rollout decode is
+``--batch 2048 --prompt 128 --new 256``.
 
 Attention mode times one launch of the split latent attention (mm_cuda_decode_attention)
 over a synthetic fp16 cache of --ctx positions per row:

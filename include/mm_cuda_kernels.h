@@ -49,8 +49,14 @@ int mm_cuda_decode_attention(mm_cuda_ctx* ctx, const float* q, const void* cache
  * has finished the work. No context, cudaMalloc, cudaFree or allocating library routine is
  * involved: the split partials live in one static device array of 256 (row, split) slots
  * (1,064,960 bytes) that every GPU loading this library holds until the process exits.
- *   - The first call on a device resolves that array's device address (with the device
- *     current); make this first call before any stream capture on that device.
+ *   - The first call with splits > 1 on a device resolves that array's device address
+ *     (cudaGetSymbolAddress, with the device current) and caches it for the process. Under
+ *     lazy module loading that first call is also when the driver loads this library's
+ *     device code and the array, which allocates: make it at start-up, before any stream
+ *     capture, like any other set-up. After cudaDeviceReset the cached address is stale:
+ *     a process that resets a device must be restarted before calling this again.
+ *   - Launch failures are read from the launches themselves; an error an earlier call left
+ *     pending is neither reported nor cleared here.
  *   - Returns MM_INVALID_ARGUMENT when splits > 1 and batch * splits > 256 (the array's
  *     capacity), for splits outside [1, 16], a null pointer or a row stride below 144;
  *     MM_GPU_ERROR when a CUDA call fails.

@@ -396,9 +396,13 @@ def grpo_objective(lp, old, ref, adv, clip, klc):
     ed = math.exp(delta)
     kl = ed - delta - 1
     obj = -min(ratio * adv, clipped * adv) + klc * kl
-    active = ratio <= 1 + clip if adv >= 0 else ratio >= 1 - clip
+    # 1 + clip and 1 - clip are float sums in the reference (trainer.cpp:363)
+    active = ratio <= float(F32(1.0 + clip)) if adv >= 0 else ratio >= float(F32(1.0 - clip))
     coef = (ratio * adv if active else 0.0) + klc * (ed - 1)
-    return obj, kl, coef
+    if not math.isfinite(obj) or abs(coef) > float(np.finfo(F32).max):
+        return None
+    # the objective hands back the coefficient as a float (trainer.cpp:368-369)
+    return obj, kl, float(F32(coef))
 
 
 # ---------------------------------------------------------------- DPO (trainer.cpp)
@@ -480,6 +484,7 @@ def grpo_coefficients(lp, old, ref, mask, advantages, clip, klc, n_total=None):
                 raise ValueError("Invalid or unbounded GRPO token statistics")
             loss += o[0] / den
             kl += o[1] / den
+            # float coefficient / double denominator, rounded to float (trainer.cpp:842-843)
             coef[i, t] = F32(o[2] / den)
     return loss, kl, coef
 

@@ -1,5 +1,5 @@
 """Data-parallel GRPO on CPU ranks (gloo, world size 2), no GPU: the rollout sharding, the
-NCCL unique-id bootstrap over torch.distributed, and the algebra of the sharded update that
+NCCL unique-id bootstrap over the engine's TCP rendezvous, and the algebra of the sharded update that
 the engine runs on device — each rank's coefficients divided by the global rollout count,
 gradients and loss/KL summed over ranks, the skip flag OR-ed — against one process over the
 whole batch (oracle restatement of trainer.cpp:784-891 on the tiny model)."""
@@ -61,7 +61,8 @@ def _worker(rank, port, out):
     try:
         sl = D.rollout_shard(N, G, rank, WORLD)
         from cpp_inference_train_engine_b200.engine import CudaExecution
-        uid = D.broadcast_unique_id(rank, CudaExecution.nccl_unique_id)
+        uid = D.exchange_unique_id(rank, WORLD, CudaExecution.nccl_unique_id, "127.0.0.1", port + 1,
+                                   timeout=60)
         ids = [None] * WORLD
         dist.all_gather_object(ids, uid)
         loss, kl, flat, any_nz = _grpo(np.arange(N)[sl], N)
@@ -112,20 +113,24 @@ def test_two_gloo_ranks_match_one_process():
 
 
 def _failing_worker(rank, port, out):
-    """Rank 1 leaves right after the group forms; rank 0 then bootstraps NCCL through it."""
-    import datetime
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
-    import torch.distributed as dist
-    dist.init_process_group("gloo", rank=rank, world_size=WORLD, timeout=datetime.timedelta(seconds=10))
+    """Rank 1 exits before the bootstrap; rank 0 then serves the NCCL id to nobody."""
     if rank == 1:
         os._exit(0)  # a rank that dies between steps, with no collective in flight
     import time
     t0 = time.time()
     try:
-        D.broadcast_unique_id(rank, lambda: bytes(128))
+        D.exchange_unique_id(rank, WORLD, lambda: bytes(128), "127.0.0.1", port, timeout=10)
         out[rank] = ("completed", time.time() - t0)
     except Exception as e:  # the peer is gone: the bootstrap must fail, not hang
         out[rank] = ("error " + type(e).__name__, time.time() - t0)
+
+
+def test_rendezvous_without_rank0_fails_in_time():
+    import time
+    t0 = time.time()
+    with pytest.raises(RuntimeError):
+        D.exchange_unique_id(1, 2, lambda: bytes(128), "127.0.0.1", _free_port(), timeout=2)
+    assert time.time() - t0 < 30
 
 
 def test_rank_failure_is_reported_not_hung():

@@ -211,12 +211,21 @@ def test_tiny_grpo_update_matches_reference():
     rewards = np.array([1.0 if O.Rng(3 + i).uniform() < 0.5 else 0.0 for i in range(8)],
                        np.float32)
     rewards[:2] = [0, 1]
+    # the reference's own current and frozen log-probs, as its update body computes them
+    n = len(rolls)
+    cur = pol.log_probs(inp, tgt, mask, n, S).reshape(n, S)
+    frozen = refm.log_probs(inp, tgt, mask, n, S).reshape(n, S)
     out = ref.grpo_update(pol, refm, G, inp, tgt, mask, old, rewards, 0.2, 0.04, 1e-4)
     adv = np.concatenate([O.group_advantages(rewards[g * G:(g + 1) * G]) for g in range(2)])
     assert np.array_equal(adv, out["advantages"])
     loss, kl, coef = O.grpo_coefficients(lp, old, lp, mask, adv, 0.2, 0.04)
     assert abs(loss - out["loss"]) < 1e-5 and abs(kl - out["kl"]) < 1e-6
-    assert np.abs(coef - out["coefficients"]).max() < 1e-6
+    # on the reference's own log-probs the restated coefficients are the reference's, bit for
+    # bit (float objective coefficient / double denominator, trainer.cpp:842-843)
+    loss, kl, coef = O.grpo_coefficients(cur, old, frozen, mask, adv, 0.2, 0.04)
+    assert np.array_equal(coef, out["coefficients"])
+    assert loss == pytest.approx(out["loss"], rel=1e-12, abs=1e-15)
+    assert kl == pytest.approx(out["kl"], rel=1e-12, abs=1e-15)
 
 
 @needs_ref

@@ -4,8 +4,9 @@ entry point (mm_cuda_decode_attention), through the C ABI.
 Some callers cannot allocate device memory while they run -- a server that gave all of it to
 its own pool at start-up, a plugin host that only lends input and output buffers -- so this
 entry point keeps its split partials in a static device array instead. Two calls in a row
-must match the allocating entry point within this suite's decode-attention tolerance, and
-a split plan larger than the static array must be refused.
+must match the allocating entry point within this suite's decode-attention tolerance, a
+call after the first must leave the device's free memory unchanged, and a split plan larger
+than the static array must be refused.
 """
 import ctypes
 
@@ -61,6 +62,25 @@ def test_noalloc_matches_allocating_entry_point_twice():
         assert rc == 0, rc
         err = (got.float() - want.float()).abs().max().item()
         assert err < 2e-2 * max(1.0, want.float().abs().max().item()), (call, err)
+
+
+def test_noalloc_call_allocates_nothing():
+    require_gpu()
+    import torch
+    f = noalloc_fn()
+    q, cache, pos, Sc = case(32, 700, 11)
+    out = torch.zeros(32, H * KV, device="cuda", dtype=torch.half)
+    stream = torch.cuda.current_stream().cuda_stream
+    # the first call is the set-up (module load, symbol address); later calls allocate nothing
+    assert f(q.data_ptr(), cache.data_ptr(), Sc * W, pos.data_ptr(), 32, 8, 0.125, out.data_ptr(), stream) == 0
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    for _ in range(3):
+        assert f(q.data_ptr(), cache.data_ptr(), Sc * W, pos.data_ptr(), 32, 8, 0.125, out.data_ptr(),
+                 stream) == 0
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0, (free0, free1)
 
 
 def test_noalloc_rejects_plans_beyond_its_static_scratch():

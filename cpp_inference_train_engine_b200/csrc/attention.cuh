@@ -107,25 +107,25 @@ constexpr int kTargetWarps = 148 * 8;
 // With cos_t/sin_t, the rope part of each head's query is rotated to position pos[b] as
 // it is loaded (the step's query comes straight from the W_uq product).
 // Launch: ceil(B * nsplit / kWarps) blocks of 128 threads, dec::kRowSmem dynamic smem.
-__global__ void __launch_bounds__(128) decode_attention_row_kernel(
-    const float* __restrict__ qf, const __half* __restrict__ cache, long long cache_seq_stride,
-    const int* __restrict__ pos, int B, int nsplit, float scale, __half* __restrict__ ctx, float* __restrict__ part,
-    const float* __restrict__ cos_t, const float* __restrict__ sin_t) {
-    MM_PDL_ENTRY();
+// One work item of the split latent decode attention for one warp: row b, context split sp
+// of nsplit. `mine` is the warp's kWarpSmem bytes of shared memory. With nsplit == 1 the
+// normalised context goes to ctx; otherwise the split's partial (max, sum, O) goes to
+// part[(b * nsplit + sp) * H * (KV + 2)].
+__device__ __forceinline__ void decode_attention_item(const float* __restrict__ qf, const __half* __restrict__ cache,
+                                                      long long cache_seq_stride, const int* __restrict__ pos, int b,
+                                                      int sp, int nsplit, float scale, __half* __restrict__ ctx,
+                                                      float* __restrict__ part, const float* __restrict__ cos_t,
+                                                      const float* __restrict__ sin_t, unsigned char* mine) {
     using namespace dec;
     using fa::ldsm_x4;
     using fa::ldsm_x4_t;
     using fa::mma16816;
-    extern __shared__ __align__(16) unsigned char row_smem[];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-    const int item = blockIdx.x * kWarps + warp;
-    if (item >= B * nsplit) return;  // no block-wide barrier follows
-    const int b = item / nsplit, sp = item - b * nsplit;
-    unsigned char* mine = row_smem + warp * kWarpSmem;
+    const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const long long item = static_cast<long long>(b) * nsplit + sp;
     auto ring = reinterpret_cast<__half (*)[16][LDQ]>(mine);
     auto Qs = reinterpret_cast<__half (*)[LDQ]>(mine + kRingBytes);
     auto Pw = reinterpret_cast<__half (*)[LDP]>(mine + kRingBytes + H * LDQ * 2);
-    const int n = pos[b] + 1;
+    const int n = __ldcg(pos + b) + 1;
     const int tiles = (n + 15) / 16;
     const int per = (tiles + nsplit - 1) / nsplit;
     const int t_begin = sp * per, t_end = min(tiles, t_begin + per);
@@ -149,7 +149,7 @@ __global__ void __launch_bounds__(128) decode_attention_row_kernel(
     const float4* q4 = reinterpret_cast<const float4*>(qf + static_cast<long long>(b) * H * W);
     const int p = n - 1;  // position of this step's token
     for (int e = lane; e < H * W / 4; e += 32) {
-        float4 v = q4[e];
+        float4 v = __ldcg(q4 + e);
         const int hh = (4 * e) / W, c = (4 * e) % W;
         if (cos_t && c >= KV) {  // adjacent-pair RoPE of the rope query (rope_rows_kernel's arithmetic)
             float* f = reinterpret_cast<float*>(&v);
@@ -265,6 +265,22 @@ __global__ void __launch_bounds__(128) decode_attention_row_kernel(
     }
 }
 
+
+__global__ void __launch_bounds__(128) decode_attention_row_kernel(
+    const float* __restrict__ qf, const __half* __restrict__ cache, long long cache_seq_stride,
+    const int* __restrict__ pos, int B, int nsplit, float scale, __half* __restrict__ ctx, float* __restrict__ part,
+    const float* __restrict__ cos_t, const float* __restrict__ sin_t) {
+    MM_PDL_ENTRY();
+    using namespace dec;
+    extern __shared__ __align__(16) unsigned char row_smem[];
+    const int warp = threadIdx.x >> 5;
+    const int item = blockIdx.x * kWarps + warp;
+    if (item >= B * nsplit) return;  // no block-wide barrier follows
+    const int b = item / nsplit, sp = item - b * nsplit;
+    decode_attention_item(qf, cache, cache_seq_stride, pos, b, sp, nsplit, scale, ctx, part, cos_t, sin_t,
+                          row_smem + warp * kWarpSmem);
+}
+
 // Merges the nsplit partials of decode_attention_row_kernel: one warp per (row, head),
 // 4 context columns per lane; grid ceil(B * H / 4), block 128.
 __global__ void decode_attention_combine_kernel(const float* __restrict__ part, int nsplit, int B,
@@ -296,6 +312,59 @@ __global__ void decode_attention_combine_kernel(const float* __restrict__ part, 
     __half* out = ctx + static_cast<long long>(b) * H * KV + hh * KV + 4 * lane;
     *reinterpret_cast<__half2*>(out) = __floats2half2_rn(o0 * inv, o1 * inv);
     *reinterpret_cast<__half2*>(out + 2) = __floats2half2_rn(o2 * inv, o3 * inv);
+}
+
+// Merges the nsplit partials of row b (all H heads) into ctx with one warp, in one pass over
+// the splits with every head's state in registers (lane = 4 context columns of each head):
+// the loads of one split, all heads, are independent and in flight together. Running
+// maximum per head, sums rescaled when it rises (the same result as the combine kernel's
+// two passes up to rounding). The partials were written by other warps (other CTAs), so
+// they are read from L2.
+__device__ __forceinline__ void decode_attention_merge_row(const float* __restrict__ part, int nsplit, int b,
+                                                           __half* __restrict__ ctx) {
+    using namespace dec;
+    const int lane = threadIdx.x & 31;
+    const long long stride = static_cast<long long>(H) * (KV + 2);
+    const float* pb = part + static_cast<long long>(b) * nsplit * stride;
+    float M[H], L[H], o[H][4];
+#pragma unroll
+    for (int hh = 0; hh < H; ++hh) {
+        M[hh] = -INFINITY;
+        L[hh] = 0.f;
+        o[hh][0] = o[hh][1] = o[hh][2] = o[hh][3] = 0.f;
+    }
+    for (int sp = 0; sp < nsplit; ++sp) {
+        const float* ps = pb + sp * stride;
+        float2 ml[H];
+        float4 ov[H];
+#pragma unroll
+        for (int hh = 0; hh < H; ++hh) {
+            ml[hh] = __ldcg(reinterpret_cast<const float2*>(ps + hh * (KV + 2)));
+            const float2 a = __ldcg(reinterpret_cast<const float2*>(ps + hh * (KV + 2) + 2 + 4 * lane));
+            const float2 c = __ldcg(reinterpret_cast<const float2*>(ps + hh * (KV + 2) + 4 + 4 * lane));
+            ov[hh] = make_float4(a.x, a.y, c.x, c.y);
+        }
+#pragma unroll
+        for (int hh = 0; hh < H; ++hh) {
+            const float m = ml[hh].x;
+            if (m == -INFINITY) continue;
+            const float nm = fmaxf(M[hh], m);
+            const float fo = exp2f(M[hh] - nm), fn = exp2f(m - nm);  // fo = 0 while empty
+            L[hh] = L[hh] * fo + fn * ml[hh].y;
+            o[hh][0] = o[hh][0] * fo + fn * ov[hh].x;
+            o[hh][1] = o[hh][1] * fo + fn * ov[hh].y;
+            o[hh][2] = o[hh][2] * fo + fn * ov[hh].z;
+            o[hh][3] = o[hh][3] * fo + fn * ov[hh].w;
+            M[hh] = nm;
+        }
+    }
+#pragma unroll
+    for (int hh = 0; hh < H; ++hh) {
+        const float inv = 1.f / L[hh];
+        __half* out = ctx + static_cast<long long>(b) * H * KV + hh * KV + 4 * lane;
+        *reinterpret_cast<__half2*>(out) = __floats2half2_rn(o[hh][0] * inv, o[hh][1] * inv);
+        *reinterpret_cast<__half2*>(out + 2) = __floats2half2_rn(o[hh][2] * inv, o[hh][3] * inv);
+    }
 }
 
 } // namespace mm

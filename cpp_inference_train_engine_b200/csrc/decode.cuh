@@ -2,9 +2,13 @@
 // absorbed form), on-device sampling (sample_token, inference.cpp:345-426) and the batched
 // rollout() of trainer.cpp:187-213.
 #pragma once
+#include "decode_mk.cuh"
 #include "passes.cuh"
 
 namespace mm {
+
+// Timestamps one traced fused decode step can record (start, every barrier, end).
+constexpr int kMkTraceSlots = 320;
 
 // Context splits of the tensor-core decode attention: enough CTAs for ~2 per SM when the
 // batch alone does not provide them, at least 4 tiles of 16 positions per split.
@@ -75,6 +79,10 @@ inline void ensure_decode(Context& cx, int B, int Sc, int max_new) {
         d.part = a.template take<float>(B >= decode_target_warps() ? 1 : static_cast<long long>(B) * kMaxDecodeSplits * c.H * (c.kvr + 2));
         d.step = a.template take<int>(1);
         d.active = a.template take<int>(B);
+        d.mk_part = a.template take<float>(static_cast<long long>(mk::kMaxKs) * B * c.d);
+        d.mk_cnt = a.template take<int>(B);
+        d.mk_bar = a.template take<unsigned>(1);
+        d.mk_trace = a.template take<unsigned long long>(kMkTraceSlots);
     };
     d.drop_graph();
     d.B = B;
@@ -85,6 +93,118 @@ inline void ensure_decode(Context& cx, int B, int Sc, int max_new) {
     d.arena.release();
     d.arena.reserve(sz.used() + 4096);
     plan(d.arena);
+    MM_CUDA_CHECK(cudaMemsetAsync(d.mk_cnt, 0, sizeof(int) * B, cx.stream));
+}
+
+// The fused decode step (decode_mk_kernel) runs for the 35.8M model's shapes unless
+// MM_DECODE_MK=0 (then every layer is its own chain of launches; same arithmetic up to the
+// order of fp32 additions).
+inline bool decode_mk_enabled(const Context& cx) {
+    static const bool on = [] {
+        const char* e = std::getenv("MM_DECODE_MK");
+        return !(e && e[0] == '0');
+    }();
+    // rows up to which the fused step is used (MM_DECODE_MK_MAX_ROWS): beyond it the step is
+    // dominated by the latent attention and the products' work, not by launch latency
+    static const int max_rows = [] {
+        const char* e = std::getenv("MM_DECODE_MK_MAX_ROWS");
+        const int v = e ? std::atoi(e) : 0;
+        return v > 0 ? v : 512;
+    }();
+    const Dims& c = cx.c;
+    return on && cx.dec.B <= max_rows && c.d == mk::D && c.qr == mk::QR && c.kvr == mk::KVR && c.rope == mk::ROPE && c.H == mk::H &&
+           c.dff == mk::DFF && c.L <= mk::kMaxLayers && c.nope + c.rope == 64;
+}
+
+// Launches decode_mk_kernel for the rows of cx.dec: embedding of dec.tok through the h3 rows
+// of the vocabulary head, cache rows written at dec.pos, positions advanced. One CTA per SM
+// (cooperative launch, so every CTA is resident for the grid barriers).
+inline void launch_decode_mk(Context& cx) {
+    const Dims& c = cx.c;
+    DecodeState& d = cx.dec;
+    const int B = d.B;
+    const int G = sm_count();
+    MkParams p{};
+    p.a_h16 = tensor_map(d.h16, false, mk::D, B, cx.d16(c.d), 64, 128);
+    p.a_cq16 = tensor_map(d.cq16, false, mk::QR, B, cx.d16(c.qr), 64, 128);
+    p.a_ctx16 = tensor_map(d.ctx16, false, mk::HKV, B, mk::HKV, 64, 128);
+    p.a_h2 = tensor_map(d.h2, false, mk::D, B, cx.d16(c.d), 64, 128);
+    p.a_gated = tensor_map(d.gated, false, mk::DFF, B, cx.d16(c.dff), 64, 128);
+    for (int l = 0; l < c.L; ++l) {
+        const PrepLayer& w = cx.prep[l];
+        p.wa[l] = tensor_map(w.Wa, false, mk::QKV, mk::D, w.lda, 64, 64);
+        p.wq[l] = tensor_map(w.Wq, false, mk::QW, mk::QR, w.ldq, 64, 64);
+        p.wo[l] = tensor_map(w.Wo, false, mk::D, mk::HKV, w.ldo, 64, 64);
+        p.wgu[l] = tensor_map(w.Wgu, false, 2 * mk::DFF, mk::D, w.ldgu, 64, 64);
+        p.wdown[l] = tensor_map(cx.S(l, kWdown), false, mk::D, mk::DFF, cx.SL(l, kWdown), 64, 64);
+        const void* wb[5] = {w.Wa, w.Wq, w.Wo, w.Wgu, cx.S(l, kWdown)};
+        const long long wn[5] = {2LL * mk::D * w.lda, 2LL * mk::QR * w.ldq, 2LL * mk::HKV * w.ldo,
+                                 2LL * mk::D * w.ldgu, 2LL * mk::DFF * cx.SL(l, kWdown)};
+        for (int k = 0; k < 5; ++k) {
+            p.wbase[l][k] = wb[k];
+            p.wbytes[l][k] = wn[k];
+        }
+        p.attn_norm[l] = cx.W(l, kAttnNorm);
+        p.ffn_norm[l] = cx.W(l, kFfnNorm);
+        p.q_norm[l] = cx.W(l, kQNorm);
+        p.kv_norm[l] = cx.W(l, kKvNorm);
+    }
+    p.final_norm = cx.FinalNorm();
+    p.E = cx.E();
+    p.tok = d.tok;
+    p.V = c.V;
+    p.B = B;
+    p.L = c.L;
+    p.Sc = d.Sc;
+    // context splits: as many as keep every (row, split) item in one wave of the grid's warps
+    // (about two 16-position tiles per split)
+    p.ns = std::max(1, std::min(std::min(kMaxDecodeSplits, G * mk::kWarps / B), (cx.dec_len + 1 + 31) / 32));
+    // K splits of the residual products: about one wave of (split, m-tile, n-tile) units
+    const int MT = (B + 127) / 128;
+    auto pick = [&](int nk, int maxks, int& ks, int& per) {
+        const int want = std::max(1, std::min(maxks, G / (MT * (mk::D / 128))));
+        per = (nk + want - 1) / want;
+        ks = (nk + per - 1) / per;
+    };
+    pick(mk::HKV / 64, 4, p.ks_o, p.per_o);
+    pick((mk::DFF + 63) / 64, mk::kMaxKs, p.ks_d, p.per_d);
+    p.eps = c.eps;
+    p.scale = 1.0f / std::sqrt(static_cast<float>(c.qk()));
+    p.x = d.x;
+    p.h16 = d.h16;
+    p.cq16 = d.cq16;
+    p.qf = d.qf;
+    p.ctx16 = d.ctx16;
+    p.h2 = d.h2;
+    p.gated = d.gated;
+    p.h3 = d.h3;
+    p.ld3 = cx.d16(3 * c.d);
+    p.part = d.mk_part;
+    p.attn_part = d.part;
+    p.attn_cnt = d.mk_cnt;
+    p.cache = d.cache;
+    p.pos = d.pos;
+    p.cos_t = cx.cos_t;
+    p.sin_t = cx.sin_t;
+    p.bar = d.mk_bar;
+    p.err = cx.d_err;
+    p.trace = d.mk_trace_on ? d.mk_trace : nullptr;
+    set_dynamic_smem<decode_mk_kernel>(mk::kSmem);
+    MM_CUDA_CHECK(cudaMemsetAsync(d.mk_bar, 0, sizeof(unsigned), cx.stream));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(G);
+    cfg.blockDim = dim3(mk::kThreads);
+    cfg.dynamicSmemBytes = mk::kSmem;
+    cfg.stream = cx.stream;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeCooperative;
+    at[0].val.cooperative = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    cudaEvent_t t0 = cx.prof_begin();
+    MM_CUDA_CHECK(cudaLaunchKernelEx(&cfg, decode_mk_kernel, p));
+    cx.prof_end(kKOther, t0);
+    ++cx.launches;
 }
 
 // Prefill of rows [0, B) from device prompts [B][P] (already in ws-independent storage):
@@ -128,6 +248,13 @@ inline void decode_step(Context& cx) {
     DecodeState& d = cx.dec;
     const int B = d.B, kvw = c.kvw(), qrk = c.qr + kvw;
     const int ld_d = cx.d16(c.d), ld_qr = cx.d16(c.qr), ld_kvr = cx.d16(c.kvr);
+    if (decode_mk_enabled(cx)) {
+        launch_decode_mk(cx);  // every layer, the final norm and the positions' advance
+        GemmOutSpec lo{d.logits, c.V, kOutF32};
+        lo.alpha = 1.0f / kVocabScale;
+        gemm(cx, B, c.V, 3 * c.d, {d.h3, cx.d16(3 * c.d), false}, {cx.E3(), cx.E3L(), false}, lo);
+        return;
+    }
     MM_LAUNCH(embed_kernel, warp_rows_grid(B), 256, 0, d.tok, cx.E(), d.x, B, c.d, c.V, cx.d_err);
     for (int l = 0; l < c.L; ++l) {
         const PrepLayer& p = cx.prep[l];

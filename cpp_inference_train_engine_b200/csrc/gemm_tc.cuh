@@ -66,7 +66,19 @@ struct GemmArgs {
     const __half* dglu_gu;
     long long dglu_ld;
     int dglu_n;
+    // B K-row wrap (MN-major B only): A's k-block at k reads B rows k % b_k_wrap, so
+    // A = [hi | lo] over K = 2 b_k_wrap against the same weights gives the two-term product;
+    // with b_k3, B holds [W_hi; W_lo] (2 b_k_wrap rows) and k in [2 w, 3 w) reads rows k - w,
+    // so A = [hi | lo | hi] gives hi.W_hi + lo.W_hi + hi.W_lo. 0 = off.
+    int b_k_wrap;
+    int b_k3;
 };
+
+__device__ __forceinline__ int gemm_b_row(const GemmArgs& g, int k0) {
+    if (!g.b_k_wrap) return k0;
+    if (g.b_k3 && k0 >= 2 * g.b_k_wrap) return k0 - g.b_k_wrap;
+    return k0 % g.b_k_wrap;
+}
 
 __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
     const __half2 h = __floats2half2_rn(a, b);
@@ -447,11 +459,12 @@ __global__ void __launch_bounds__(320, 1)
                 if (!g.b_mn) {
                     tma_load_2d(sb, &tmB, &full[s], k0, n0);
                 } else {
+                    const int kB = gemm_b_row(g, k0);
 #pragma unroll
                     for (int j = 0; j < BN / 64; ++j) {
                         const int col = EPI != kEpiGlu ? n0 + 64 * j
                                                  : (j < BN / 128 ? n0 + 64 * j : g.glu_n + n0 + 64 * (j - BN / 128));
-                        tma_load_2d(sb + j * 8192, &tmB, &full[s], col, k0);
+                        tma_load_2d(sb + j * 8192, &tmB, &full[s], col, kB);
                     }
                 }
             }
@@ -617,8 +630,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
                 if (!g.b_mn) {
                     tma_load_2d_pair(sb, &tmB, fb, k0, nb);
                 } else {
-                    tma_load_2d_pair(sb, &tmB, fb, nb, k0);
-                    tma_load_2d_pair(sb + 8192, &tmB, fb, nb + 64, k0);
+                    const int kB = gemm_b_row(g, k0);
+                    tma_load_2d_pair(sb, &tmB, fb, nb, kB);
+                    tma_load_2d_pair(sb + 8192, &tmB, fb, nb + 64, kB);
                 }
             }
         }

@@ -30,7 +30,8 @@ __global__ void embed_kernel(const uint16_t* __restrict__ tokens, const float* _
 // fp16 y, and the row's inverse rms for the backward pass.
 __global__ void rmsnorm_kernel(const float* __restrict__ x, long long ldx, const float* __restrict__ w,
                                int T, int n, float eps, float* __restrict__ y32, long long ld32,
-                               __half* __restrict__ y16, long long ld16, float* __restrict__ inv_out) {
+                               __half* __restrict__ y16, long long ld16, float* __restrict__ inv_out,
+                               int split16 = 0) {
     MM_PDL_ENTRY();
     const int t = warp_row(), lane = threadIdx.x & 31;
     if (t >= T) return;
@@ -43,7 +44,12 @@ __global__ void rmsnorm_kernel(const float* __restrict__ x, long long ldx, const
     for (int j = lane; j < n; j += 32) {
         const float v = xr[j] * inv * w[j];
         if (y32) y32[t * ld32 + j] = v;
-        if (y16) y16[t * ld16 + j] = __float2half_rn(v);
+        if (y16) {
+            const __half hi = __float2half_rn(v);
+            y16[t * ld16 + j] = hi;
+            if (split16) y16[t * ld16 + n + j] = __float2half_rn(v - __half2float(hi));
+            if (split16 == 2) y16[t * ld16 + 2 * n + j] = hi;
+        }
     }
 }
 

@@ -39,7 +39,7 @@ __device__ __forceinline__ void unpack_h8(uint4 u, float* f) {
 template <int MAXV>
 __global__ void rmsnorm_v4_kernel(const float* __restrict__ x, long long ldx, const float* __restrict__ w, int T,
                                   int n, float eps, float* __restrict__ y32, long long ld32, __half* __restrict__ y16,
-                                  long long ld16, float* __restrict__ inv_out) {
+                                  long long ld16, float* __restrict__ inv_out, int split16 = 0) {
     MM_PDL_ENTRY();
     const int t = warp_row(), lane = threadIdx.x & 31;
     if (t >= T) return;
@@ -65,7 +65,16 @@ __global__ void rmsnorm_v4_kernel(const float* __restrict__ x, long long ldx, co
             const float4 o = make_float4(v[k].x * inv * wv.x, v[k].y * inv * wv.y, v[k].z * inv * wv.z,
                                          v[k].w * inv * wv.w);
             if (y32) st_f4(y32 + t * ld32 + j, o);
-            if (y16) *reinterpret_cast<uint2*>(y16 + t * ld16 + j) = pack_h4(o.x, o.y, o.z, o.w);
+            if (y16) {
+                const uint2 hi = pack_h4(o.x, o.y, o.z, o.w);
+                *reinterpret_cast<uint2*>(y16 + t * ld16 + j) = hi;
+                if (split16) {  // [hi | lo (| hi)]: lo = fp16(y - hi) at column n + j
+                    const __half2 a = *reinterpret_cast<const __half2*>(&hi.x), b = *reinterpret_cast<const __half2*>(&hi.y);
+                    *reinterpret_cast<uint2*>(y16 + t * ld16 + n + j) =
+                        pack_h4(o.x - __low2float(a), o.y - __high2float(a), o.z - __low2float(b), o.w - __high2float(b));
+                    if (split16 == 2) *reinterpret_cast<uint2*>(y16 + t * ld16 + 2 * n + j) = hi;
+                }
+            }
         }
     }
 }

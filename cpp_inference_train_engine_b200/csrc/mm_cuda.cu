@@ -727,6 +727,18 @@ int64_t mm_cuda_profile_gemm_shapes(mm_cuda_ctx* h, char* buf, int64_t cap) {
     return static_cast<int64_t>(text.size());
 }
 
+int mm_cuda_decode_trace(mm_cuda_ctx* h, int enable, uint64_t* out_ns, int cap, int* count) {
+    return guarded(h, [&](mm::Context& cx) {
+        if (enable >= 0) cx.dec.mk_trace_on = enable != 0;
+        if (count) *count = 0;
+        if (!out_ns || cap <= 0 || !cx.dec.mk_trace) return;
+        const int n = std::min(cap, mm::kMkTraceSlots);
+        MM_CUDA_CHECK(cudaMemcpyAsync(out_ns, cx.dec.mk_trace, sizeof(uint64_t) * n, cudaMemcpyDeviceToHost, cx.stream));
+        MM_CUDA_CHECK(cudaStreamSynchronize(cx.stream));
+        if (count) *count = n;
+    });
+}
+
 int mm_cuda_stream(mm_cuda_ctx* h, void** stream) {
     return guarded(h, [&](mm::Context& cx) { *stream = cx.stream; });
 }

@@ -142,7 +142,9 @@ __global__ void shadow_refresh_kernel(const ParamDesc* __restrict__ params, cons
 //   Wa  [d][q_rank + kv_rank + rope]      = [W_dq | W_dkv]
 //   Wq  [q_rank][H*(kv_rank + rope)]      per head: [W_uq_nope,h . W_uk,h^T | W_uq_rope,h]
 //   Wo  [H*kv_rank][d]                    per head: W_uv,h . W_o,h
-//   Wgu [d][2*d_ff]                       = [W_gate | W_up]
+//   Wgu [2 d][2*d_ff]                     = [W_gate | W_up] in fp16 (rows [0, d)), then the
+//                                           rounding residual fp16(W - fp16(W)) (rows [d, 2d)):
+//                                           the teacher-forced FFN's three-term product reads both
 struct PrepArgs {
     const float *w_dq, *w_dkv, *w_uq, *w_uk, *w_uv, *w_o, *w_gate, *w_up;
     __half *Wa, *Wq, *Wo, *Wgu;
@@ -198,7 +200,9 @@ __global__ void decode_prep_kernel(PrepArgs a) {
         {
             const int r = static_cast<int>(j / (2 * a.dff)), c = static_cast<int>(j % (2 * a.dff));
             const float v = c < a.dff ? a.w_gate[r * a.dff + c] : a.w_up[r * a.dff + (c - a.dff)];
-            a.Wgu[static_cast<long long>(r) * a.ldgu + c] = __float2half_rn(v);
+            const __half hi = __float2half_rn(v);
+            a.Wgu[static_cast<long long>(r) * a.ldgu + c] = hi;
+            a.Wgu[static_cast<long long>(a.d + r) * a.ldgu + c] = __float2half_rn(v - __half2float(hi));
         }
     }
 }

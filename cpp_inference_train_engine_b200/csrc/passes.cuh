@@ -159,7 +159,7 @@ template <class A> void plan_workspace(Context& cx, A& a, int T, bool tape) {
         b.ao = a.template take<__half>(t * c.aw());
         b.lse = a.template take<float>(t * c.H);
         b.res = a.template take<float>(t * c.d);
-        b.h2 = a.template take<__half>(t * cx.d16(c.d));
+        b.h2 = a.template take<__half>(t * 3 * cx.d16(c.d));  // [hi | lo | hi] rows (ffn_terms)
         // [gate | up] from one product with [W_gate | W_up], row pitch ld16(2 d_ff)
         b.gate = a.template take<__half>(t * cx.d16(2 * c.dff));
         b.up = b.gate ? b.gate + c.dff : nullptr;
@@ -244,19 +244,40 @@ inline unsigned warp_rows_grid(int rows) { return blocks_for(static_cast<long lo
 inline bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 inline bool al8(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 7) == 0; }
 
+// Terms of the teacher-forced passes' [W_gate | W_up] product (MM_FFN_EXACT): 3 (default)
+// hi(x).hi(W) + lo(x).hi(W) + hi(x).lo(W), 2 without the weights' residual, 1 = plain fp16.
+// The FFN's input and weights in fp16 are the largest sources of the teacher-forced
+// log-probabilities' deviation from the fp32 reference (about a third of it). Needs d % 64 == 0
+// (the weight-row wrap falls on whole 64-wide k-blocks).
+inline int ffn_terms(const Context& cx) {
+    static const int v = [] {
+        const char* e = std::getenv("MM_FFN_EXACT");
+        if (!e) return 3;
+        const int x = std::atoi(e);
+        return x <= 0 ? 1 : std::min(x, 3);
+    }();
+    return cx.c.d % 64 == 0 ? v : 1;
+}
+
+// split16: the fp16 output is the two-term [hi | lo] row (lo = fp16(y - hi) at column n of
+// the same row), or with split16 == 2 the three-term [hi | lo | hi] row, so a product over
+// K = 2n or 3n against the weights (and their residual) reads y to about 2^-22 relative
+// instead of fp16's 2^-11.
 inline void launch_rmsnorm(Context& cx, const float* x, long long ldx, const float* w, int T, int n, float* y32,
-                           long long ld32, __half* y16, long long ld16) {
+                           long long ld32, __half* y16, long long ld16, int split16 = 0) {
     const float eps = cx.c.eps;
     const bool vec = n % 4 == 0 && n <= 1024 && ldx % 4 == 0 && al16(x) && al16(w) &&
                      (!y32 || (ld32 % 4 == 0 && al16(y32))) && (!y16 || (ld16 % 4 == 0 && al8(y16)));
+    const int sp = split16;
     if (vec && n <= 512)
         MM_LAUNCH(rmsnorm_v4_kernel<4>, warp_rows_grid(T), 256, 0, x, ldx, w, T, n, eps, y32, ld32, y16, ld16,
-                  (float*)nullptr);
+                  (float*)nullptr, sp);
     else if (vec)
         MM_LAUNCH(rmsnorm_v4_kernel<8>, warp_rows_grid(T), 256, 0, x, ldx, w, T, n, eps, y32, ld32, y16, ld16,
-                  (float*)nullptr);
+                  (float*)nullptr, sp);
     else
-        MM_LAUNCH(rmsnorm_kernel, warp_rows_grid(T), 256, 0, x, ldx, w, T, n, eps, y32, ld32, y16, ld16, (float*)nullptr);
+        MM_LAUNCH(rmsnorm_kernel, warp_rows_grid(T), 256, 0, x, ldx, w, T, n, eps, y32, ld32, y16, ld16, (float*)nullptr,
+                  sp);
 }
 
 // dx = RMSNorm backward (+ add); dw += scale * sum over rows (fixed-order reduction when
@@ -475,22 +496,31 @@ inline void forward_chunk(Context& cx, int Bc, int S, bool tape, VocabMode vm, b
             o.ldr = c.d;
             gemm(cx, T, c.d, c.aw(), {b.ao, c.aw(), false}, {cx.S(l, kWo), cx.SL(l, kWo), true}, o);
         }
-        // feed-forward block
-        launch_rmsnorm(cx, res, c.d, cx.W(l, kFfnNorm), T, c.d, (float*)nullptr, 0LL, b.h2, ld_d);
+        // feed-forward block: the [W_gate | W_up] product in ffn_terms(cx) fp16 terms, its input
+        // written by the norm as [hi | lo | hi] and the weight rows wrapped onto [W_hi; W_lo]
+        const int nt = ffn_terms(cx);
+        const long long ld_h2 = nt * static_cast<long long>(ld_d);
+        launch_rmsnorm(cx, res, c.d, cx.W(l, kFfnNorm), T, c.d, (float*)nullptr, 0LL, b.h2, ld_h2, nt - 1);
         const int ld_gu = cx.d16(2 * c.dff);
+        const int k_gu = nt * c.d;
         if (c.dff % 8 || (tape && !swiglu_fused_enabled())) {
             // the backward needs gate and up themselves
-            gemm(cx, T, 2 * c.dff, c.d, {b.h2, ld_d, false}, {pw.Wgu, pw.ldgu, true}, {b.gate, ld_gu, kOutF16});
+            GemmOutSpec o{b.gate, ld_gu, kOutF16};
+            if (nt > 1) o.b_k_wrap = c.d;
+            o.b_k3 = nt == 3;
+            gemm(cx, T, 2 * c.dff, k_gu, {b.h2, ld_h2, false}, {pw.Wgu, pw.ldgu, true}, o);
             launch_swiglu(cx, b.gate, b.up, ld_gu, T, c.dff, b.gated, ld_ff);
         } else {
             // SwiGLU in the product's epilogue; with tape it also stores gate and up for the backward
             GemmOutSpec o{b.gated, ld_ff, kOutF16};
             o.glu_n = c.dff;
+            if (nt > 1) o.b_k_wrap = c.d;
+            o.b_k3 = nt == 3;
             if (tape) {
                 o.pre_gate = b.gate;
                 o.pre_ld = ld_gu;
             }
-            gemm(cx, T, c.dff, c.d, {b.h2, ld_d, false}, {pw.Wgu, pw.ldgu, true}, o);
+            gemm(cx, T, c.dff, k_gu, {b.h2, ld_h2, false}, {pw.Wgu, pw.ldgu, true}, o);
         }
         {
             GemmOutSpec o{x_next, c.d, tape ? kOutF32 : kOutF32Acc};
@@ -579,11 +609,13 @@ inline void backward_chunk(Context& cx, int Bc, int S) {
             launch_swiglu_backward(cx, b.gate, b.up, ld_gu, w.dgated16, ld_ff, T, c.dff, w.dg16, w.du16, ld_gu);
         }
         {
+            // the weight gradients read the fp16 high part of the FFN input
+            const long long ld_h2 = ffn_terms(cx) * static_cast<long long>(ld_d);
             GemmOutSpec o{cx.G(l, kWgate), c.dff, kOutF32Acc};
             o.alpha_ptr = inv_s;
-            gemm(cx, c.d, c.dff, T, {b.h2, ld_d, true}, {w.dg16, ld_gu, true}, o);
+            gemm(cx, c.d, c.dff, T, {b.h2, ld_h2, true}, {w.dg16, ld_gu, true}, o);
             o.out = cx.G(l, kWup);
-            gemm(cx, c.d, c.dff, T, {b.h2, ld_d, true}, {w.du16, ld_gu, true}, o);
+            gemm(cx, c.d, c.dff, T, {b.h2, ld_h2, true}, {w.du16, ld_gu, true}, o);
         }
         // dh2 = [dg | du] . [W_gate | W_up]^T, one product over K = 2 d_ff
         gemm(cx, T, c.d, 2 * c.dff, {w.dg16, ld_gu, false}, {pw.Wgu, pw.ldgu, false}, {w.dh2, c.d, kOutF32});

@@ -193,6 +193,13 @@ struct DecodeState {
     float* part;              // [B][splits][H][kv_rank + 2] decode-attention partials
     int* step;                // device step counter of the rollout loop
     int* active;              // [B] serving: 1 for slots holding a request
+    // fused decode step (decode_mk_kernel): split-K partials [6][B][d], per-row attention
+    // arrival counters [B] (zero between uses) and the grid barrier's arrival counter
+    float* mk_part = nullptr;
+    int* mk_cnt = nullptr;
+    unsigned* mk_bar = nullptr;
+    unsigned long long* mk_trace = nullptr;  // [kMkTraceSlots] phase timestamps when tracing
+    bool mk_trace_on = false;
     int max_new = 0;
     Arena arena;
     // one captured rollout decode step (decode_sample_step), valid for the buffers above
@@ -457,6 +464,10 @@ struct GemmOutSpec {
     const __half* dglu_gu = nullptr;
     long long dglu_ld = 0;
     __half* dglu_up = nullptr;
+    // split A (GemmArgs::b_k_wrap, b_k3): two-term, B (MN-major) has b_k_wrap rows and
+    // K = 2 b_k_wrap; three-term, B holds [hi; lo] of b_k_wrap rows each and K = 3 b_k_wrap
+    int b_k_wrap = 0;
+    bool b_k3 = false;
 };
 
 inline int sm_count() {

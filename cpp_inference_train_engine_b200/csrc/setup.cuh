@@ -61,16 +61,19 @@ inline int gemm(Context& cx, int M, int N, int K, Opnd A, Opnd B, const GemmOutS
         return v == 64 || v == 128 || v == 256 ? v : 0;
     }();
     if (forced_bn && !o.glu_n && !o.dglu_gu) BN = forced_bn;
+    if (o.b_k_wrap && (!B.mn || o.b_k_wrap % kGemmBK || K != (o.b_k3 ? 3 : 2) * o.b_k_wrap))
+        fail(MM_INVALID_ARGUMENT, "split A needs MN-major B and K = 2 or 3 times the 64-aligned wrap");
     const int nb = o.glu_n ? o.glu_n + N : N;  // columns of B
+    const int kb_rows = o.b_k_wrap ? (o.b_k3 ? 2 : 1) * o.b_k_wrap : K;  // rows of B
     const CUtensorMap& ta = A.mn ? tensor_map(A.p, bf16, M, K, A.ld, 64, 64)
                                  : tensor_map(A.p, bf16, K, M, A.ld, 64, kGemmBM);
-    const CUtensorMap& tb = B.mn ? tensor_map(B.p, bf16, nb, K, B.ld, 64, 64)
+    const CUtensorMap& tb = B.mn ? tensor_map(B.p, bf16, nb, kb_rows, B.ld, 64, 64)
                                  : tensor_map(B.p, bf16, K, nb, B.ld, 64, BN);
     GemmArgs ga{M, N, K, A.mn ? 1 : 0, B.mn ? 1 : 0, bf16 ? 1 : 0, o.kind,
                 o.residual, o.ldr, o.alpha, o.alpha_ptr, cx.d_err, 0, 0,
                 o.lse_part, o.targets, o.tgt_logit, (o.lse_part && o.no_store) ? 1 : 0, o.glu_n,
                 o.rope_cos, o.rope_sin, o.rope_seq, o.rope_period, o.rope_begin, o.rope_len,
-                o.pre_gate ? 1 : 0, o.dglu_gu, o.dglu_ld, o.dglu_gu ? N : 0};
+                o.pre_gate ? 1 : 0, o.dglu_gu, o.dglu_ld, o.dglu_gu ? N : 0, o.b_k_wrap, o.b_k3 ? 1 : 0};
     // Split-K for accumulating products with few output tiles over a long K (the weight
     // gradients, K = tokens): each K slice stores its fp32 partial, then one reduction adds
     // them in order into the destination.
@@ -299,7 +302,7 @@ inline void create_context(Context& cx, const mm_model_desc& desc, int device, b
             p.Wa = a.template take<__half>(static_cast<long long>(c.d) * lda);
             p.Wq = a.template take<__half>(static_cast<long long>(c.qr) * ldq);
             p.Wo = a.template take<__half>(static_cast<long long>(c.H) * c.kvr * ldo);
-            p.Wgu = a.template take<__half>(static_cast<long long>(c.d) * ldgu);
+            p.Wgu = a.template take<__half>(2LL * c.d * ldgu);  // [hi; lo] rows
         }
     };
     Sizer sz;

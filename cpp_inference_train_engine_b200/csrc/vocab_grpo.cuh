@@ -56,20 +56,38 @@ __global__ void logsoftmax_rows_kernel(const float* __restrict__ logits, long lo
 }
 
 // Combines the per-tile (max, sum exp) partials of the vocabulary GEMM's log-sum-exp
-// epilogue, part[j * T + t] for j < ntiles: lse[t] = M + log(sum_j s_j exp(m_j - M)) with the
-// sum in double, lp[t] = target logit - lse[t]. One thread per row.
+// epilogue, part[j * T + t] for j < ntiles: lse[t] = M + log(sum_j s_j exp(m_j - M)),
+// lp[t] = target logit - lse[t]. One thread per row and a single pass over the partials:
+// groups of 8 are loaded together (streaming loads: the partials are read once), the running
+// maximum is raised group by group with the sum rescaled, each group's 8 terms are added in
+// float and the groups in double (the reference sums in double, ops.cpp:195-201). A partial
+// that drained no column carries (-inf, 0) and adds nothing.
 __global__ void lse_combine_kernel(const float2* __restrict__ part, int ntiles, int T,
                                    const float* __restrict__ tgt_logit, float* __restrict__ lp,
                                    float* __restrict__ lse, int* err) {
     MM_PDL_ENTRY();
     const int t = blockIdx.x * blockDim.x + threadIdx.x;
     if (t >= T) return;
+    const float2* p = part + t;
     float mx = -INFINITY;
-    for (int j = 0; j < ntiles; ++j) mx = fmaxf(mx, part[static_cast<long long>(j) * T + t].x);
     double z = 0.0;
-    for (int j = 0; j < ntiles; ++j) {
-        const float2 p = part[static_cast<long long>(j) * T + t];
-        z += static_cast<double>(p.y) * static_cast<double>(__expf(p.x - mx));
+    constexpr int U = 8;
+    for (int j = 0; j < ntiles; j += U) {
+        float2 v[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+            v[u] = j + u < ntiles ? __ldcs(p + static_cast<long long>(j + u) * T) : make_float2(-INFINITY, 0.f);
+        float cm = v[0].x;
+#pragma unroll
+        for (int u = 1; u < U; ++u) cm = fmaxf(cm, v[u].x);
+        if (cm > mx) {
+            z *= static_cast<double>(__expf(mx - cm));  // 0 while nothing was added (mx = -inf)
+            mx = cm;
+        }
+        float s = 0.f;
+#pragma unroll
+        for (int u = 0; u < U; ++u) s += v[u].x == -INFINITY ? 0.f : v[u].y * __expf(v[u].x - mx);
+        z += static_cast<double>(s);
     }
     const double l = log(z) + static_cast<double>(mx);
     if (lse) lse[t] = static_cast<float>(l);

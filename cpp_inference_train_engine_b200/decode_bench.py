@@ -113,11 +113,35 @@ def decode(args):
         seeds = np.array([r1.next() for _ in range(B)], np.uint64)
         S = args.prompt + args.new
         for temp in args.temperature:
+            if args.trace:
+                ex.decode_trace(1)
             for it in range(args.warmup + 1):
                 if it == args.warmup:
                     ex.profile(1)
                 ex.rollout(prompts, args.new, S, seeds, temp, with_batches=False)
             prof = ex.profile(0)
+            if args.trace:
+                raw = ex.decode_trace_raw()
+                ph = ex.decode_trace(0)
+                kinds = ["wa", "wq", "wo", "wgu", "wdown"]
+                inner = {k: [0.0, 0.0] for k in kinds}
+                for g in range(5 * cfg.n_layers):
+                    a, b, c = raw[128 + 3 * g: 131 + 3 * g]
+                    if a > 0 and b > a and c > b:
+                        inner[kinds[g % 5]][0] += (b - a) / 1e3
+                        inner[kinds[g % 5]][1] += (c - b) / 1e3
+                print(json.dumps({"mode": "decode_trace_inner", "batch": B,
+                                  "load_mma_us": {k: round(v[0], 2) for k, v in inner.items()},
+                                  "epilogue_us": {k: round(v[1], 2) for k, v in inner.items()}}))
+                names = ["embed"] + [f"{n}{l}" for l in range(cfg.n_layers) for n in
+                                     ("wa", "wq", "attn", "wo", "norm2", "wgu", "wdown", "norm1")]
+                per = {}
+                for n, us in zip(names, ph):
+                    key = n.rstrip("0123456789")
+                    per[key] = per.get(key, 0.0) + us
+                print(json.dumps({"mode": "decode_trace", "batch": B, "phases": len(ph), "total_us": sum(ph),
+                                  "by_kind_us": {k: round(v, 2) for k, v in per.items()},
+                                  "layer0_us": [round(x, 2) for x in ph[1:9]]}))
             ms = prof["decode"][0] + prof["sample"][0]
             steps = args.new - 1
             ctx = args.prompt + (args.new - 1) / 2.0  # mean positions attended per step
@@ -143,6 +167,8 @@ def main(argv=None):
     ap.add_argument("--splits", type=int, default=0)
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=2)
+    ap.add_argument("--trace", action="store_true",
+                    help="print the fused decode step's per-phase times (device global timer)")
     args = ap.parse_args(argv)
     if args.attention:
         attention(args)

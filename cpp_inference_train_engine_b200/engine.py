@@ -126,6 +126,7 @@ def lib():
                                             ctypes.c_int, _vp, ctypes.c_int64, ctypes.c_int,
                                             ctypes.c_float, _vp, ctypes.c_int64, ctypes.c_int]),
         "mm_cuda_profile": (ctypes.c_int, [_vp, ctypes.c_int, _f64p, _i64p, _f64p]),
+        "mm_cuda_decode_trace": (ctypes.c_int, [_vp, ctypes.c_int, _u64p, ctypes.c_int, _i32p]),
         "mm_cuda_stream": (ctypes.c_int, [_vp, ctypes.POINTER(_vp)]),
         "mm_cuda_decode_attention": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int64, _vp, ctypes.c_int,
                                                     ctypes.c_int, ctypes.c_float, _vp]),
@@ -486,6 +487,24 @@ class CudaExecution:
                         "calls": int(parts["calls"]), "ms": float(parts["ms"]),
                         "tflops": float(parts["tflops"])})
         return sorted(out, key=lambda r: -r["ms"])
+
+    def decode_trace(self, enable: int = -1):
+        """Phase trace of the fused decode step (mm_cuda_decode_trace): with enable 1/0 turns it
+        on/off; returns the last traced step's phase durations in microseconds."""
+        buf = np.zeros(320, np.uint64)
+        n = ctypes.c_int32()
+        self._check(lib().mm_cuda_decode_trace(self.h, enable, _p(buf, _u64p), buf.size, ctypes.byref(n)))
+        t = buf[:min(n.value, 128)].astype(np.int64)
+        t = t[t > 0]
+        return (np.diff(t) / 1e3).tolist() if t.size > 1 else []
+
+    def decode_trace_raw(self):
+        """The raw timestamps (ns) of the last traced fused decode step: [0, 128) start, barriers,
+        end; [128, 320) per GEMM phase g: producer start, accumulator ready, epilogue done."""
+        buf = np.zeros(320, np.uint64)
+        n = ctypes.c_int32()
+        self._check(lib().mm_cuda_decode_trace(self.h, -1, _p(buf, _u64p), buf.size, ctypes.byref(n)))
+        return buf[:n.value].astype(np.int64)
 
     def profile(self, enable: int = -1):
         """{tag: (device ms, launches, algorithmic work)}; see PROFILE_TAGS."""

@@ -79,6 +79,13 @@ int mm_cuda_profile(mm_cuda_ctx* ctx, int enable, double* ms, int64_t* calls, do
  * calls= ms= tflops="), NUL-terminated into buf. Returns the full length, or -(1 + code). */
 int64_t mm_cuda_profile_gemm_shapes(mm_cuda_ctx* ctx, char* buf, int64_t cap);
 
+/* Phase trace of the fused rollout decode step (no reference counterpart; the reference
+ * logs per-update counters only, execution.hpp:25-27): while enabled (enable = 1; 0 turns it
+ * off, -1 leaves it) every fused step records the device global timer (ns) at its start,
+ * after each of its grid barriers and at its end. out_ns (cap entries) receives the last
+ * step's record; *count the entries copied. Tracing adds one timer read per barrier. */
+int mm_cuda_decode_trace(mm_cuda_ctx* ctx, int enable, uint64_t* out_ns, int cap, int* count);
+
 /* The context's CUDA stream (cudaStream_t), for events recorded by a caller. */
 int mm_cuda_stream(mm_cuda_ctx* ctx, void** stream);
 

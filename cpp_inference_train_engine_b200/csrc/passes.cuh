@@ -498,7 +498,8 @@ inline void forward_chunk(Context& cx, int Bc, int S, bool tape, VocabMode vm, b
         }
         // feed-forward block: the [W_gate | W_up] product in ffn_terms(cx) fp16 terms, its input
         // written by the norm as [hi | lo | hi] and the weight rows wrapped onto [W_hi; W_lo]
-        const int nt = ffn_terms(cx);
+        // (the rollout prefill, kVocabLast, yields no log-probabilities: one term)
+        const int nt = vm == kVocabLast ? 1 : ffn_terms(cx);
         const long long ld_h2 = nt * static_cast<long long>(ld_d);
         launch_rmsnorm(cx, res, c.d, cx.W(l, kFfnNorm), T, c.d, (float*)nullptr, 0LL, b.h2, ld_h2, nt - 1);
         const int ld_gu = cx.d16(2 * c.dff);

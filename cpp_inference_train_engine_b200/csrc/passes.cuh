@@ -548,7 +548,7 @@ inline void forward_chunk(Context& cx, int Bc, int S, bool tape, VocabMode vm, b
         }
         const int bn = gemm(cx, T, c.V, 3 * c.d, {w.h3, ld3, false}, {cx.E3(), cx.E3L(), false}, lo);
         if (with_targets)
-            MM_LAUNCH_TIMED(kKLogsoftmax, 16.0 * T * ((c.V + bn - 1) / bn), lse_combine_kernel, blocks_for(T, 256), 256,
+            MM_LAUNCH_TIMED(kKLogsoftmax, 16.0 * T * ((c.V + bn - 1) / bn), lse_combine_kernel, blocks_for(T, kLseRows), 256,
                             0, w.lse_part, 2 * ((c.V + bn - 1) / bn), T, w.tgt_logit, w.lp, w.lse_v, cx.d_err);
     } else {
         MM_LAUNCH(split3_gather_kernel, blocks_for((long long)Bc * c.d, 256), 256, 0, w.hf, c.d, Bc, S, S - 1, w.h3,

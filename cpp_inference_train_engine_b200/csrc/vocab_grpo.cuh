@@ -57,39 +57,57 @@ __global__ void logsoftmax_rows_kernel(const float* __restrict__ logits, long lo
 
 // Combines the per-tile (max, sum exp) partials of the vocabulary GEMM's log-sum-exp
 // epilogue, part[j * T + t] for j < ntiles: lse[t] = M + log(sum_j s_j exp(m_j - M)),
-// lp[t] = target logit - lse[t]. One thread per row and a single pass over the partials:
-// groups of 8 are loaded together (streaming loads: the partials are read once), the running
-// maximum is raised group by group with the sum rescaled, each group's 8 terms are added in
-// float and the groups in double (the reference sums in double, ops.cpp:195-201). A partial
-// that drained no column carries (-inf, 0) and adds nothing.
-__global__ void lse_combine_kernel(const float2* __restrict__ part, int ntiles, int T,
-                                   const float* __restrict__ tgt_logit, float* __restrict__ lp,
-                                   float* __restrict__ lse, int* err) {
+// lp[t] = target logit - lse[t]. A block of 256 threads takes 64 rows; the four 64-thread
+// groups each merge a quarter of every row's partials (groups of 8 loaded together with
+// streaming loads: the partials are read once, 32 consecutive rows per warp load), with the
+// running maximum raised group by group and the sum rescaled, 8 terms added in float and the
+// groups in double (the reference sums in double, ops.cpp:195-201); the quarters are then
+// merged in shared memory in a fixed order. A partial that drained no column carries
+// (-inf, 0) and adds nothing.
+constexpr int kLseRows = 64;
+__global__ void __launch_bounds__(256) lse_combine_kernel(const float2* __restrict__ part, int ntiles, int T,
+                                                          const float* __restrict__ tgt_logit, float* __restrict__ lp,
+                                                          float* __restrict__ lse, int* err) {
     MM_PDL_ENTRY();
-    const int t = blockIdx.x * blockDim.x + threadIdx.x;
-    if (t >= T) return;
-    const float2* p = part + t;
+    __shared__ float sm[4][kLseRows];
+    __shared__ double sz[4][kLseRows];
+    const int q = threadIdx.x / kLseRows, r = threadIdx.x % kLseRows;
+    const int t = blockIdx.x * kLseRows + r;
+    const int per = (ntiles + 3) / 4;
+    const int j0 = q * per, j1 = min(ntiles, j0 + per);
     float mx = -INFINITY;
     double z = 0.0;
-    constexpr int U = 8;
-    for (int j = 0; j < ntiles; j += U) {
-        float2 v[U];
+    if (t < T) {
+        const float2* p = part + t;
+        constexpr int U = 8;
+        for (int j = j0; j < j1; j += U) {
+            float2 v[U];
 #pragma unroll
-        for (int u = 0; u < U; ++u)
-            v[u] = j + u < ntiles ? __ldcs(p + static_cast<long long>(j + u) * T) : make_float2(-INFINITY, 0.f);
-        float cm = v[0].x;
+            for (int u = 0; u < U; ++u)
+                v[u] = j + u < j1 ? __ldcs(p + static_cast<long long>(j + u) * T) : make_float2(-INFINITY, 0.f);
+            float cm = v[0].x;
 #pragma unroll
-        for (int u = 1; u < U; ++u) cm = fmaxf(cm, v[u].x);
-        if (cm > mx) {
-            z *= static_cast<double>(__expf(mx - cm));  // 0 while nothing was added (mx = -inf)
-            mx = cm;
+            for (int u = 1; u < U; ++u) cm = fmaxf(cm, v[u].x);
+            if (cm > mx) {
+                z *= static_cast<double>(__expf(mx - cm));  // 0 while nothing was added (mx = -inf)
+                mx = cm;
+            }
+            float s = 0.f;
+#pragma unroll
+            for (int u = 0; u < U; ++u) s += v[u].x == -INFINITY ? 0.f : v[u].y * __expf(v[u].x - mx);
+            z += static_cast<double>(s);
         }
-        float s = 0.f;
-#pragma unroll
-        for (int u = 0; u < U; ++u) s += v[u].x == -INFINITY ? 0.f : v[u].y * __expf(v[u].x - mx);
-        z += static_cast<double>(s);
     }
-    const double l = log(z) + static_cast<double>(mx);
+    sm[q][r] = mx;
+    sz[q][r] = z;
+    __syncthreads();
+    if (q != 0 || t >= T) return;
+    float M = sm[0][r];
+    for (int g = 1; g < 4; ++g) M = fmaxf(M, sm[g][r]);
+    double Z = 0.0;
+    for (int g = 0; g < 4; ++g)
+        if (sm[g][r] != -INFINITY) Z += sz[g][r] * static_cast<double>(__expf(sm[g][r] - M));
+    const double l = log(Z) + static_cast<double>(M);
     if (lse) lse[t] = static_cast<float>(l);
     if (lp) {
         const double v = static_cast<double>(tgt_logit[t]) - l;

@@ -84,6 +84,15 @@ def case_grpo_chunks():
                       and np.array_equal(mask, r["mask"][i]))
     noise = np.random.default_rng(5).normal(0, 0.3, r["old_lp"].shape).astype(np.float32)
     old = (r["old_lp"] + noise * r["mask"]).astype(np.float32)
+    # A token whose ratio sits on a clip edge (within the engines' log-prob difference, max
+    # ~2e-3) is clipped in one engine and not in the other, which adds or removes that token's
+    # whole gradient: no tolerance covers that step. Such tokens move 1e-2 off the edge, judged
+    # on the policy's own teacher-forced log-probs (the update's lp).
+    lp = pol.log_probabilities(r["input"], r["target"], N_ROLL, SEQ).reshape(N_ROLL, SEQ)
+    for edge in (np.log(1.2), np.log(0.8)):
+        d = lp.astype(np.float64) - old - edge
+        near = (r["mask"] > 0) & (np.abs(d) < 5e-3)
+        old = np.where(near, old + np.where(d >= 0, -1e-2, 1e-2), old).astype(np.float32)
     rewards = np.array([1.0 if rr.uniform() < 0.3 else 0.0 for _ in range(N_ROLL)], np.float32)
     rewards[0], rewards[1], rewards[G], rewards[G + 1] = 1.0, 0.0, 0.0, 1.0
     # both clip branches (advantage sign x ratio outside [1 - eps, 1 + eps]) on the policy's lp

@@ -6,6 +6,13 @@ tensor-core compute. Random-init weights (seed 0) and synthetic prompt ids; the 
 reference model equals the initial policy.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py --workload mla1b [--gpus N] ...
+
+--workload mla1b runs the scaled model instead (24 blocks, width 2048, 16 heads, query rank
+768, kv rank 512, SwiGLU 5632, tied 32,768-token vocabulary, 1.14 B parameters): 128 prompts
+x group 16 = 2048 rollouts, prompt 512, 1536 new tokens (context 2048), N(0, 1) rewards. It
+has no CPU baseline (the reference's CPU path would take days per step) and no fixed-input
+check by default.
 
 One step = rollout (prefill + 256 batched decode steps with on-device sampling + the
 old-policy log-prob pass) and the GRPO update (reference-model log-probs, policy forward +
@@ -60,10 +67,11 @@ def parse():
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--prompts", type=int, default=256, help="prompts per step (whole job)")
-    ap.add_argument("--group", type=int, default=8)
-    ap.add_argument("--prompt-len", type=int, default=128)
-    ap.add_argument("--new-tokens", type=int, default=256)
+    ap.add_argument("--workload", default="mla36m", choices=["mla36m", "mla1b"])
+    ap.add_argument("--prompts", type=int, default=None, help="prompts per step (whole job)")
+    ap.add_argument("--group", type=int, default=None)
+    ap.add_argument("--prompt-len", type=int, default=None)
+    ap.add_argument("--new-tokens", type=int, default=None)
     ap.add_argument("--cpu-rollouts", type=int, default=8,
                     help="rollouts (one group) in the bounded CPU-baseline sample of the GPU arm")
     ap.add_argument("--reference-budget", type=float, default=240.0,
@@ -72,7 +80,24 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--gemm-shapes", action="store_true",
                     help="print per-shape GEMM device time to stderr")
-    return ap.parse_args()
+    args = ap.parse_args()
+    dflt = WORKLOADS[args.workload]
+    for k in ("prompts", "group", "prompt_len", "new_tokens"):
+        if getattr(args, k) is None:
+            setattr(args, k, dflt[k])
+    return args
+
+
+# prompts, group, prompt length, new tokens, reward (Bernoulli p; None = N(0, 1)), learning rate
+WORKLOADS = {
+    "mla36m": {"prompts": 256, "group": 8, "prompt_len": 128, "new_tokens": 256, "p_reward": 0.3, "lr": 1e-5},
+    "mla1b": {"prompts": 128, "group": 16, "prompt_len": 512, "new_tokens": 1536, "p_reward": None, "lr": 1e-5},
+}
+
+
+def model_config(args):
+    from cpp_inference_train_engine_b200.config import MLA1B, MLA36M
+    return MLA36M if args.workload == "mla36m" else MLA1B
 
 
 # ---------------------------------------------------------------------------- clocks
@@ -198,6 +223,10 @@ def run_reference(args, rank, world):
     group of 8, 4 or 2 rollouts, the largest whose W + K steps fit the time budget."""
     if rank != 0:
         return
+    if args.workload != "mla36m":
+        print(json.dumps({"impl": "reference", "unavailable": "the reference's CPU path takes days per step "
+                          "of the 1.14 B model (2048 rollouts x 2048 positions); no CPU sample is run"}))
+        return
     from oracle import ref
     if not ref.available():
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref (the reference CPU build) is not built"}))
@@ -231,11 +260,16 @@ def run_reference(args, rank, world):
 
 def workload_config(args, world):
     n = args.prompts * args.group
-    return {"workload": "grpo_step_mla36m", "rollouts": n, "prompts": args.prompts,
+    w = WORKLOADS[args.workload]
+    cfg = model_config(args)
+    seq = args.prompt_len + args.new_tokens
+    cache_gb = n * seq * (cfg.kv_lora_rank + cfg.head_dim_rope) * 2 * cfg.n_layers / 1e9
+    return {"workload": "grpo_step_" + args.workload, "rollouts": n, "prompts": args.prompts,
             "group": args.group, "prompt_len": args.prompt_len, "new_tokens": args.new_tokens,
-            "sequence": args.prompt_len + args.new_tokens, "temperature": 1.0,
-            "reward": "bernoulli(0.3)", "clip": 0.2, "kl": 0.04, "lr": 1e-5,
-            "parallelism": f"dp{world}", "l2": "inputs larger than L2 (cache 2.3 GB, logits)"}
+            "sequence": seq, "temperature": 1.0,
+            "reward": "normal(0,1)" if w["p_reward"] is None else f"bernoulli({w['p_reward']})",
+            "clip": 0.2, "kl": 0.04, "lr": w["lr"],
+            "parallelism": f"dp{world}", "l2": f"inputs larger than L2 (cache {cache_gb:.1f} GB, logits)"}
 
 
 # ---------------------------------------------------------------------------- ours
@@ -257,7 +291,8 @@ def fixed_batch(args, cfg, n_total, prompts_all):
 
 def gemm_algorithmic_flops(cfg, rollouts, seq, prompt_len):
     """Algorithmic tensor-core work of one step's event-timed products on one rank: every
-    teacher-forced token passes the model's matrices (2 x 27,374,720 flops) and the vocabulary
+    teacher-forced token passes the model's matrices (2 x their entries: 2 x 27,374,720
+    flops for the 35.8M model) and the vocabulary
     head (2 x d x V) five times (old-policy, frozen-reference and policy forwards, the backward
     at twice a forward), and every prompt token passes the matrices once in the prefill. The
     fp32-accurate head's three fp16 terms count once: their extra work is an implementation
@@ -306,7 +341,8 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
                                 device_id=torch.device("cuda", local))
 
-    cfg = MLA36M
+    cfg = model_config(args)
+    wl = WORKLOADS[args.workload]
     n_total = args.prompts * args.group
     try:
         sl = D.rollout_shard(n_total, args.group, rank, world)
@@ -314,7 +350,7 @@ def main():
         raise SystemExit(str(e))
     seq = args.prompt_len + args.new_tokens
     prompts_all, seeds, rewards_all = grpo_workload(args.prompts, args.group, args.prompt_len,
-                                                    cfg.vocab_size, 0.3)
+                                                    cfg.vocab_size, wl["p_reward"])
     prompts, seeds, rewards = prompts_all[sl].copy(), seeds[sl].copy(), rewards_all[sl].copy()
 
     W = E.init_params(cfg, 0)
@@ -330,7 +366,7 @@ def main():
             dist.barrier()
 
     fixed = None
-    if not args.no_fixed_check:
+    if not args.no_fixed_check and args.workload == "mla36m":
         # One GRPO update on a fixed teacher-forced batch of the whole job: its loss and
         # pre-clip gradient norm are global sums, so they must not depend on the rank count.
         inp, tgt, mask = fixed_batch(args, cfg, n_total, prompts_all)
@@ -340,7 +376,7 @@ def main():
         phase = np.arange(n_total * seq, dtype=np.float64).reshape(n_total, seq)[sl]
         old = (lp + 0.3 * np.sin(phase) * mask).astype(np.float32)
         out = pol.grpo_step(refm, inp, tgt, mask, old, rewards, args.group, n_total=n_total,
-                            clip=0.2, klc=0.04, learning_rate=1e-5)
+                            clip=0.2, klc=0.04, learning_rate=wl["lr"])
         fixed = {"loss": out["loss"], "kl": out["kl"], "grad_norm": out["grad_norm"],
                  "batch": f"{n_total} x {seq} teacher-forced, fixed ids (seed 6), old = lp + 0.3 sin"}
         pol.upload(W)  # back to the initial weights, zero moments, step 0
@@ -352,7 +388,7 @@ def main():
             s = (seeds + np.uint64(step_idx) * np.uint64(0x9E3779B97F4A7C15)).astype(np.uint64)
         r = pol.rollout(prompts, args.new_tokens, seq, s, 1.0)
         out = pol.grpo_step(refm, r["input"], r["target"], r["mask"], r["old_lp"], rewards,
-                            args.group, n_total=n_total, clip=0.2, klc=0.04, learning_rate=1e-5)
+                            args.group, n_total=n_total, clip=0.2, klc=0.04, learning_rate=wl["lr"])
         return r, out
 
     for i in range(args.warmup):
@@ -417,8 +453,8 @@ def main():
         R = prompts.shape[0]
         if top == "k_gemm":
             work = gemm_algorithmic_flops(cfg, R, seq, args.prompt_len) * args.steps
-            how = ("algorithmic flops: rollouts x S x 5 x (2 x 27,374,720 + 2 d V) + prompt tokens x "
-                   "2 x 27,374,720, over the class's event-timed launches")
+            how = ("algorithmic flops: rollouts x S x 5 x (2 x matrix entries + 2 d V) + prompt tokens x "
+                   "2 x matrix entries, over the class's event-timed launches")
         else:
             work = kern[top]["work"]
             how = "work as counted per launch"
@@ -433,7 +469,7 @@ def main():
                     "avg_launch_us": 1e3 * kern[top]["ms"] / max(kern[top]["launches"], 1),
                     # DRAM bytes of one vocabulary-head launch (the class's largest shape),
                     # single-launch ncu capture at M = 8,192 scaled to this chunk's M
-                    "traffic": vocab_head_traffic(seq, R),
+                    "traffic": vocab_head_traffic(seq, R) if args.workload == "mla36m" else None,
                     "traffic_kernel": "gemm_tc_pair_kernel, vocabulary head M x 16384 x 1536"}
         dec_bytes = decode_algorithmic_bytes(cfg, pol.n_params, R, args.prompt_len, args.new_tokens)
         dec_gbs = dec_bytes / (decode_ms / 1e3) / 1e9 if decode_ms else None
@@ -441,12 +477,12 @@ def main():
                            "bound": "hbm", "achieved": dec_gbs, "peak": pk["hbm_gbs"], "unit": "GB/s",
                            "frac": dec_gbs / pk["hbm_gbs"] if dec_gbs else None,
                            "bytes_per_step": dec_bytes, "ms_per_step": decode_ms,
-                           "work": "sum over decode steps of 2 P (fp16 weights) + rows x ctx x 2,880 B"}
+                           "work": "sum over decode steps of 2 P (fp16 weights) + rows x ctx x 2 (kv + rope) L B"}
         phases = {k: round(prof_p[k][0] / args.steps, 3) for k in
                   ("prefill", "decode", "sample", "logprob", "backward", "adamw", "allreduce")}
         phases["reference_logprob"] = round(prof_r["logprob"][0] / args.steps, 3)
         cpu = None
-        if world == 1 and not args.no_cpu_baseline:
+        if world == 1 and not args.no_cpu_baseline and args.workload == "mla36m":
             cpu = cpu_baseline(args)
         line = {
             "metric": METRIC, "value": toks / (dev_ms / 1e3), "unit": "tok/s", "n_gpus": world,

@@ -95,6 +95,16 @@ MLA36M = ModelConfig(vocab_size=16384, max_sequence_length=2048, n_layers=10, d_
                      q_lora_rank=192, kv_lora_rank=128, d_ff=1360)
 
 
+# The scaled MLA model of the multi-GPU GRPO workload: 24 blocks, width 2048, 16 heads, query
+# rank 768, kv rank 512, SwiGLU 5632, tied 32,768-token vocabulary, context 2048. Its head
+# widths are this backend's choice (nope 96 + rope 32 = value 128, so query/key and value
+# heads have the same width): 1,144,651,776 parameters. The reference's validator caps
+# models at 1e9 parameters (src/model/config.cpp:44-46); this backend does not.
+MLA1B = ModelConfig(vocab_size=32768, max_sequence_length=2048, n_layers=24, d_model=2048,
+                    n_heads=16, head_dim_nope=96, head_dim_rope=32, head_dim_value=128,
+                    q_lora_rank=768, kv_lora_rank=512, d_ff=5632)
+
+
 @dataclasses.dataclass(frozen=True)
 class AdamWConfig:
     """OptimizerConfig defaults (include/mini_mla/optimizer.hpp:5-14)."""

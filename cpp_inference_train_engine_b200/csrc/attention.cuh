@@ -12,7 +12,12 @@ namespace mm {
 // Absorbed latent decode attention for one new token per sequence.
 // qf fp32 [B][H][KV + R]: per head the absorbed query (W_uk folded in) then the rotated
 // rope query. Cache: fp16 [B][max_seq][KV + R] for this layer. Positions 0..pos[b]
-// (inclusive) are attended. ctx out fp16 [B][H*KV]. grid B, block 32*H.
+// (inclusive) are attended. ctx out fp16 [B][H*KV]. grid B, block 32*H, dynamic shared
+// memory decode_attention_smem<KV, R>(H) bytes.
+template <int KV, int R>
+constexpr size_t decode_attention_smem(int H) {
+    return sizeof(float) * (static_cast<size_t>(H) * (KV + R) + 32 * (KV + R + 1));
+}
 template <int KV, int R>
 __global__ void decode_attention_kernel(const float* __restrict__ qf, const __half* __restrict__ cache,
                                         long long cache_seq_stride, const int* __restrict__ pos,
@@ -20,8 +25,8 @@ __global__ void decode_attention_kernel(const float* __restrict__ qf, const __ha
     MM_PDL_ENTRY();
     constexpr int W = KV + R;
     constexpr int TILE = 32;
-    __shared__ float Cs[TILE][W + 1];
-    extern __shared__ float qsm[];  // [H][W]
+    extern __shared__ float qsm[];  // [H][W], then the cache tile [TILE][W + 1]
+    float (*Cs)[W + 1] = reinterpret_cast<float (*)[W + 1]>(qsm + H * W);
     const int b = blockIdx.x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n = pos[b] + 1;
@@ -365,6 +370,236 @@ __device__ __forceinline__ void decode_attention_merge_row(const float* __restri
         *reinterpret_cast<__half2*>(out) = __floats2half2_rn(o[hh][0] * inv, o[hh][1] * inv);
         *reinterpret_cast<__half2*>(out + 2) = __floats2half2_rn(o[hh][2] * inv, o[hh][3] * inv);
     }
+}
+
+// Tensor-core form for 16 heads over a [512 latent | 32 rope] cache row (the 2,048-wide
+// model). All heads of a row attend over the same cache rows (multi-query form), so one CTA
+// of 4 warps takes a (row, context split) work item and streams 32-position tiles of the
+// row's cache through a cp.async ring (zero-filled past the row's length):
+//   scores  S[16 heads x 32 positions] = Q[16 x 544] C^T: warp w takes positions 8w..8w+7
+//           (A = the row's queries from shared memory, B = the cache tile, 34 k-steps),
+//   softmax thread i owns head i / 8 and 4 positions: running max and sum per head in the
+//           base-2 domain, P in fp16, the per-head rescale factor shared,
+//   output  O^T[512 x 16] += C^T[512 x 32] P^T: warp w accumulates latent columns
+//           [128 w, 128 w + 128) for all 16 heads (8 x 2 m16n8 tiles in registers), A = the
+//           cache tile through transposed ldmatrix, B = P.
+// Arithmetic as the 8-head form: fp16 operands (queries pre-scaled by scale * log2 e),
+// fp32 accumulation, fp16 probabilities. With nsplit == 1 the normalised context goes to ctx
+// (fp16 [B][16 * 512]); otherwise (max, sum, O[512]) per head goes to part for
+// decode_attention_wide_combine_kernel.
+namespace decw {
+constexpr int H = 16, KV = 512, R = 32, W = KV + R;
+constexpr int kTile = 32;               // cached positions per tile
+constexpr int LD = W + 8;               // padded rows: conflict-free ldmatrix
+constexpr int LDP = kTile + 8;
+constexpr int kStages = 2;
+constexpr int kThreads = 128;
+constexpr int kQBytes = H * LD * 2;
+constexpr int kTileBytes = kTile * LD * 2;
+constexpr int kSmem = kQBytes + kStages * kTileBytes + H * kTile * 4 + H * LDP * 2 + 3 * H * 4;
+// work items (CTAs) wanted in flight for the whole batch when choosing context splits
+constexpr int kTargetItems = 148 * 4;
+}  // namespace decw
+
+__global__ void __launch_bounds__(decw::kThreads, 2) decode_attention_wide_kernel(
+    const float* __restrict__ qf, const __half* __restrict__ cache, long long cache_seq_stride,
+    const int* __restrict__ pos, int B, int nsplit, float scale, __half* __restrict__ ctx, float* __restrict__ part) {
+    MM_PDL_ENTRY();
+    using namespace decw;
+    using fa::ldsm_x4;
+    using fa::ldsm_x4_t;
+    using fa::mma16816;
+    extern __shared__ __align__(16) unsigned char wide_smem[];
+    auto Qs = reinterpret_cast<__half (*)[LD]>(wide_smem);
+    auto ring = reinterpret_cast<__half (*)[kTile][LD]>(wide_smem + kQBytes);
+    auto Ss = reinterpret_cast<float (*)[kTile]>(wide_smem + kQBytes + kStages * kTileBytes);
+    auto Ps = reinterpret_cast<__half (*)[LDP]>(wide_smem + kQBytes + kStages * kTileBytes + H * kTile * 4);
+    float* corr_s = reinterpret_cast<float*>(wide_smem + kQBytes + kStages * kTileBytes + H * kTile * 4 + H * LDP * 2);
+    float* m_s = corr_s + H;
+    float* l_s = m_s + H;
+    const int item = blockIdx.x;
+    if (item >= B * nsplit) return;
+    const int b = item / nsplit, sp = item - b * nsplit;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
+    const int n = __ldcg(pos + b) + 1;
+    const int tiles = (n + kTile - 1) / kTile;
+    const int per = (tiles + nsplit - 1) / nsplit;
+    const int t_begin = sp * per, t_end = min(tiles, t_begin + per);
+    const __half* cb = cache + static_cast<long long>(b) * cache_seq_stride;
+    auto issue = [&](int j) {
+        const int tile = t_begin + j;
+        if (tile < t_end) {
+            const int p0 = tile * kTile;
+            for (int e = tid; e < kTile * (W / 8); e += kThreads) {
+                const int r = e / (W / 8), cc = (e % (W / 8)) * 8;
+                const bool ok = p0 + r < n;
+                cp_async16(&ring[j % kStages][r][cc], cb + static_cast<long long>(ok ? p0 + r : 0) * W + cc, ok);
+            }
+        }
+        cp_async_commit();
+    };
+#pragma unroll
+    for (int j = 0; j < kStages - 1; ++j) issue(j);
+    // the row's queries (rope part already rotated), pre-scaled into the base-2 domain
+    const float qscale = scale * fa::kLog2e;
+    const float4* q4 = reinterpret_cast<const float4*>(qf + static_cast<long long>(b) * H * W);
+    for (int e = tid; e < H * W / 4; e += kThreads) {
+        const float4 v = __ldcg(q4 + e);
+        const int hh = (4 * e) / W, c = (4 * e) % W;
+        *reinterpret_cast<__half2*>(&Qs[hh][c]) = __floats2half2_rn(v.x * qscale, v.y * qscale);
+        *reinterpret_cast<__half2*>(&Qs[hh][c + 2]) = __floats2half2_rn(v.z * qscale, v.w * qscale);
+    }
+    float acc[8][2][4];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int k = 0; k < 2; ++k) acc[i][k][0] = acc[i][k][1] = acc[i][k][2] = acc[i][k][3] = 0.f;
+    // softmax state of head tid / 8 (replicated over its 8 threads)
+    const int sh = tid >> 3, sq = (tid & 7) * 4;
+    float m_run = -INFINITY, l_run = 0.f;
+    for (int j = 0;; ++j) {
+        const int tile = t_begin + j;
+        if (tile >= t_end) break;
+        const int p0 = tile * kTile;
+        cp_async_wait<kStages - 2>();
+        __syncthreads();  // tile j (and the queries) visible; every warp is done with tile j - 1
+        issue(j + kStages - 1);
+        __half (*Ct)[LD] = ring[j % kStages];
+        // scores of positions 8 warp .. 8 warp + 7 for all 16 heads
+        {
+            float s[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int kk = 0; kk < W / 16; kk += 2) {
+                uint32_t cbf[4];  // k-steps kk and kk + 1 of the 8 positions
+                ldsm_x4(cbf, &Ct[8 * warp + (lane & 7)][kk * 16 + (lane >> 3) * 8]);
+                uint32_t a[4];
+                ldsm_x4(a, &Qs[lane & 15][kk * 16 + (lane >> 4) * 8]);
+                mma16816(s, a, cbf[0], cbf[1]);
+                ldsm_x4(a, &Qs[lane & 15][(kk + 1) * 16 + (lane >> 4) * 8]);
+                mma16816(s, a, cbf[2], cbf[3]);
+            }
+            const int q0 = 8 * warp + 2 * t;
+            const bool v0 = p0 + q0 < n, v1 = p0 + q0 + 1 < n;
+            Ss[g][q0] = v0 ? s[0] : -INFINITY;
+            Ss[g][q0 + 1] = v1 ? s[1] : -INFINITY;
+            Ss[g + 8][q0] = v0 ? s[2] : -INFINITY;
+            Ss[g + 8][q0 + 1] = v1 ? s[3] : -INFINITY;
+        }
+        __syncthreads();
+        // online softmax: thread tid owns positions sq..sq+3 of head sh
+        {
+            const float4 sv = *reinterpret_cast<const float4*>(&Ss[sh][sq]);
+            float mx = fmaxf(fmaxf(sv.x, sv.y), fmaxf(sv.z, sv.w));
+#pragma unroll
+            for (int o = 1; o < 8; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+            const float mn = fmaxf(m_run, mx);  // finite: position p0 is valid
+            const float cf = exp2f(m_run - mn);
+            const float e0 = exp2f(sv.x - mn), e1 = exp2f(sv.y - mn), e2 = exp2f(sv.z - mn), e3 = exp2f(sv.w - mn);
+            float ps = (e0 + e1) + (e2 + e3);
+#pragma unroll
+            for (int o = 1; o < 8; o <<= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+            l_run = l_run * cf + ps;
+            m_run = mn;
+            *reinterpret_cast<__half2*>(&Ps[sh][sq]) = __floats2half2_rn(e0, e1);
+            *reinterpret_cast<__half2*>(&Ps[sh][sq + 2]) = __floats2half2_rn(e2, e3);
+            if ((tid & 7) == 0) corr_s[sh] = cf;
+        }
+        __syncthreads();
+        // rescale this warp's accumulators, then O^T += C^T P^T over the tile's 32 positions
+        {
+            const float c00 = corr_s[2 * t], c01 = corr_s[2 * t + 1], c10 = corr_s[8 + 2 * t], c11 = corr_s[9 + 2 * t];
+#pragma unroll
+            for (int mt = 0; mt < 8; ++mt) {
+                acc[mt][0][0] *= c00; acc[mt][0][1] *= c01; acc[mt][0][2] *= c00; acc[mt][0][3] *= c01;
+                acc[mt][1][0] *= c10; acc[mt][1][1] *= c11; acc[mt][1][2] *= c10; acc[mt][1][3] *= c11;
+            }
+#pragma unroll
+            for (int ks = 0; ks < kTile / 16; ++ks) {
+                uint32_t bp[4];  // heads 0-7 (bp[0], bp[1]) and 8-15 (bp[2], bp[3])
+                ldsm_x4(bp, &Ps[(lane & 7) + ((lane >> 4) << 3)][16 * ks + ((lane >> 3) & 1) * 8]);
+#pragma unroll
+                for (int mt = 0; mt < 8; ++mt) {
+                    uint32_t a[4];
+                    ldsm_x4_t(a, &Ct[16 * ks + (lane & 7) + ((lane >> 4) << 3)][128 * warp + mt * 16 + ((lane >> 3) & 1) * 8]);
+                    mma16816(acc[mt][0], a, bp[0], bp[1]);
+                    mma16816(acc[mt][1], a, bp[2], bp[3]);
+                }
+            }
+        }
+    }
+    cp_async_wait<0>();
+    if ((tid & 7) == 0) {
+        m_s[sh] = m_run;
+        l_s[sh] = l_run;
+    }
+    __syncthreads();
+    const int h0 = 2 * t, h1 = 2 * t + 1, h2 = 8 + 2 * t, h3 = 9 + 2 * t;
+    if (nsplit == 1) {
+        const float i0 = 1.f / l_s[h0], i1 = 1.f / l_s[h1], i2 = 1.f / l_s[h2], i3 = 1.f / l_s[h3];
+        __half* o = ctx + static_cast<long long>(b) * H * KV + 128 * warp;
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt) {
+            const int c = mt * 16 + g;
+            o[h0 * KV + c] = __float2half_rn(acc[mt][0][0] * i0);
+            o[h1 * KV + c] = __float2half_rn(acc[mt][0][1] * i1);
+            o[h0 * KV + c + 8] = __float2half_rn(acc[mt][0][2] * i0);
+            o[h1 * KV + c + 8] = __float2half_rn(acc[mt][0][3] * i1);
+            o[h2 * KV + c] = __float2half_rn(acc[mt][1][0] * i2);
+            o[h3 * KV + c] = __float2half_rn(acc[mt][1][1] * i3);
+            o[h2 * KV + c + 8] = __float2half_rn(acc[mt][1][2] * i2);
+            o[h3 * KV + c + 8] = __float2half_rn(acc[mt][1][3] * i3);
+        }
+    } else {
+        float* pp = part + static_cast<long long>(item) * H * (KV + 2);
+        if (tid < H) {
+            pp[tid * (KV + 2)] = m_s[tid];
+            pp[tid * (KV + 2) + 1] = l_s[tid];
+        }
+        float* o = pp + 2 + 128 * warp;
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt) {
+            const int c = mt * 16 + g;
+            o[h0 * (KV + 2) + c] = acc[mt][0][0];
+            o[h1 * (KV + 2) + c] = acc[mt][0][1];
+            o[h0 * (KV + 2) + c + 8] = acc[mt][0][2];
+            o[h1 * (KV + 2) + c + 8] = acc[mt][0][3];
+            o[h2 * (KV + 2) + c] = acc[mt][1][0];
+            o[h3 * (KV + 2) + c] = acc[mt][1][1];
+            o[h2 * (KV + 2) + c + 8] = acc[mt][1][2];
+            o[h3 * (KV + 2) + c + 8] = acc[mt][1][3];
+        }
+    }
+}
+
+// Merges the nsplit partials of decode_attention_wide_kernel: one warp per (row, head),
+// 16 context columns per lane; grid ceil(B * 16 / 4), block 128.
+__global__ void decode_attention_wide_combine_kernel(const float* __restrict__ part, int nsplit, int B,
+                                                     __half* __restrict__ ctx) {
+    MM_PDL_ENTRY();
+    using namespace decw;
+    const int wid = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (wid >= B * H) return;
+    const int b = wid / H, hh = wid % H;
+    const float* pb = part + static_cast<long long>(b) * nsplit * H * (KV + 2) + hh * (KV + 2);
+    const long long stride = static_cast<long long>(H) * (KV + 2);
+    float M = -INFINITY;
+    for (int s = 0; s < nsplit; ++s) M = fmaxf(M, pb[s * stride]);
+    float L = 0.f, o[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) o[i] = 0.f;
+    for (int s = 0; s < nsplit; ++s) {
+        const float* ps = pb + s * stride;
+        const float m = ps[0];
+        if (m == -INFINITY) continue;
+        const float f = exp2f(m - M);
+        L += f * ps[1];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) o[i] += f * ps[2 + 32 * i + lane];
+    }
+    const float inv = 1.f / L;
+    __half* out = ctx + static_cast<long long>(b) * H * KV + hh * KV + lane;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) out[32 * i] = __float2half_rn(o[i] * inv);
 }
 
 } // namespace mm

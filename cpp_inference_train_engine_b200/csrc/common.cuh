@@ -9,6 +9,9 @@
 
 namespace mm {
 
+// Heads per decode row the generic latent attention's shared memory is sized for.
+constexpr int kMaxDecodeHeads = 64;
+
 // Bits of the per-context device error word. A kernel that gives up on a wait sets one
 // and returns; the host reads the word after each call and reports gpu_error.
 enum DeviceError : int {

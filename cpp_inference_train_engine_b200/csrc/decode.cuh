@@ -47,6 +47,25 @@ inline void launch_decode_attention(Context& cx, const float* q, const __half* c
                   ns, B, out);
 }
 
+// Context splits of the 16-head tensor-core form: enough (row, split) work items for
+// decw::kTargetItems CTAs, at least 4 tiles of 32 positions per split.
+inline int decode_splits_wide(int B, int ctx) {
+    if (B >= decw::kTargetItems) return 1;
+    const int want = (decw::kTargetItems + B - 1) / B;
+    const int by_len = std::max(1, (ctx + 127) / 128);
+    return std::max(1, std::min(std::min(want, by_len), kMaxDecodeSplits));
+}
+
+// MM_WIDE_ATTENTION=0 keeps the 2,048-wide model's decode attention on the CUDA-core form
+// (for comparison).
+inline bool wide_attention_enabled() {
+    static const bool on = [] {
+        const char* e = std::getenv("MM_WIDE_ATTENTION");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
 inline void ensure_decode(Context& cx, int B, int Sc, int max_new) {
     DecodeState& d = cx.dec;
     if (d.B == B && d.Sc >= Sc && d.max_new >= max_new && d.arena.capacity()) return;
@@ -76,7 +95,8 @@ inline void ensure_decode(Context& cx, int B, int Sc, int max_new) {
         d.draw = a.template take<int>(B);
         d.out_tok = a.template take<uint16_t>(static_cast<long long>(B) * std::max(max_new, 1));
         // flash-decoding partials (max, sum, O[kv_rank]) per split and head
-        d.part = a.template take<float>(B >= decode_target_warps() ? 1 : static_cast<long long>(B) * kMaxDecodeSplits * c.H * (c.kvr + 2));
+        d.part = a.template take<float>(B >= std::max(decode_target_warps(), decw::kTargetItems)
+                                            ? 1 : static_cast<long long>(B) * kMaxDecodeSplits * c.H * (c.kvr + 2));
         d.step = a.template take<int>(1);
         d.active = a.template take<int>(B);
         d.mk_part = a.template take<float>(static_cast<long long>(mk::kMaxKs) * B * c.d);
@@ -90,6 +110,11 @@ inline void ensure_decode(Context& cx, int B, int Sc, int max_new) {
     d.max_new = max_new;
     Sizer sz;
     plan(sz);
+    // and the teacher-forced workspace makes room for the cache (the next pass re-creates it)
+    if (!d.arena.fits(sz.used() + 4096) && cx.ws_arena.capacity()) {
+        cx.ws_arena.release();
+        cx.ws.T = 0;
+    }
     d.arena.release();
     d.arena.reserve(sz.used() + 4096);
     plan(d.arena);
@@ -283,7 +308,6 @@ inline void decode_step(Context& cx) {
                              (__half*)nullptr, 0LL);
         {
             const float scale = 1.0f / std::sqrt(static_cast<float>(c.qk()));
-            const size_t smem = sizeof(float) * c.H * kvw;
             // cache rows read once (fp16) + absorbed queries in (fp32) + context out (fp16)
             const double bytes = static_cast<double>(B) * ((cx.dec_len + 1.0) * kvw * 2 + c.H * kvw * 4.0 + c.H * c.kvr * 2.0);
             if (mma_attn) {
@@ -292,12 +316,31 @@ inline void decode_step(Context& cx) {
                 launch_decode_attention(cx, d.qf, cache_l, (long long)d.Sc * kvw, d.pos, B, ns, scale, d.ctx16, d.part,
                                         cx.cos_t, cx.sin_t);
                 cx.prof_end(kKDecodeAttn, t0, bytes);
-            } else if (c.kvr == 128)
-                MM_LAUNCH_TIMED(kKDecodeAttn, bytes, (decode_attention_kernel<128, 16>), B, 32 * c.H, smem, d.qf2, cache_l,
-                                (long long)d.Sc * kvw, d.pos, c.H, scale, d.ctx16);
-            else
-                MM_LAUNCH_TIMED(kKDecodeAttn, bytes, (decode_attention_kernel<8, 4>), B, 32 * c.H, smem, d.qf2, cache_l,
-                                (long long)d.Sc * kvw, d.pos, c.H, scale, d.ctx16);
+            } else if (c.kvr == decw::KV && c.rope == decw::R && c.H == decw::H && wide_attention_enabled()) {
+                const int ns = decode_splits_wide(B, cx.dec_len + 1);
+                cudaEvent_t t0 = cx.prof_begin();
+                set_dynamic_smem<decode_attention_wide_kernel>(decw::kSmem);
+                MM_LAUNCH(decode_attention_wide_kernel, B * ns, decw::kThreads, decw::kSmem, d.qf2, cache_l,
+                          (long long)d.Sc * kvw, d.pos, B, ns, scale, d.ctx16, d.part);
+                if (ns > 1)
+                    MM_LAUNCH(decode_attention_wide_combine_kernel, blocks_for(static_cast<long long>(B) * decw::H * 32, 128),
+                              128, 0, d.part, ns, B, d.ctx16);
+                cx.prof_end(kKDecodeAttn, t0, bytes);
+            } else if (c.kvr == 512) {
+                set_dynamic_smem<decode_attention_kernel<512, 32>>(decode_attention_smem<512, 32>(kMaxDecodeHeads));
+                MM_LAUNCH_TIMED(kKDecodeAttn, bytes, (decode_attention_kernel<512, 32>), B, 32 * c.H,
+                                (decode_attention_smem<512, 32>(c.H)), d.qf2, cache_l, (long long)d.Sc * kvw, d.pos, c.H,
+                                scale, d.ctx16);
+            } else if (c.kvr == 128) {
+                set_dynamic_smem<decode_attention_kernel<128, 16>>(decode_attention_smem<128, 16>(kMaxDecodeHeads));
+                MM_LAUNCH_TIMED(kKDecodeAttn, bytes, (decode_attention_kernel<128, 16>), B, 32 * c.H,
+                                (decode_attention_smem<128, 16>(c.H)), d.qf2, cache_l, (long long)d.Sc * kvw, d.pos, c.H,
+                                scale, d.ctx16);
+            } else {
+                MM_LAUNCH_TIMED(kKDecodeAttn, bytes, (decode_attention_kernel<8, 4>), B, 32 * c.H,
+                                (decode_attention_smem<8, 4>(c.H)), d.qf2, cache_l, (long long)d.Sc * kvw, d.pos, c.H,
+                                scale, d.ctx16);
+            }
         }
         {
             GemmOutSpec o{d.x, c.d, kOutF32Acc};  // residual stream updated in place

@@ -116,7 +116,9 @@ __device__ __forceinline__ void mma_pb(float (&acc)[D / 8][4], const float (&p)[
 
 // Forward. q, k, v, out: fp16 [B*S][H*D]; lse2 fp32 [B*S][H] = log2-sum-exp of the scaled
 // scores (base 2). grid (H, B, ceil(S/64)), block 128 (4 warps x 16 query rows); K/V tiles
-// stream through a two-deep cp.async ring.
+// stream through a two-deep cp.async ring. Dynamic shared memory: flash_fwd_smem<D>() bytes
+// (87 KB at D = 128).
+template <int D> constexpr int flash_fwd_smem() { return 5 * fa::kTile * (D + 8) * 2; }
 template <int D>
 __global__ void __launch_bounds__(128) flash_fwd_mma_kernel(const __half* __restrict__ q, const __half* __restrict__ k,
                                                             const __half* __restrict__ v, int S, int H, float scale,
@@ -124,9 +126,11 @@ __global__ void __launch_bounds__(128) flash_fwd_mma_kernel(const __half* __rest
     MM_PDL_ENTRY();
     using namespace fa;
     constexpr int LD = D + 8;
-    __shared__ __align__(16) __half Qs[kTile][LD];
-    __shared__ __align__(16) __half Ks[2][kTile][LD];  // K/V tile kt in buffer kt & 1
-    __shared__ __align__(16) __half Vs[2][kTile][LD];
+    extern __shared__ __align__(16) unsigned char fa_smem[];
+    auto tiles = reinterpret_cast<__half (*)[kTile][LD]>(fa_smem);
+    __half (*Qs)[LD] = tiles[0];
+    __half (*Ks)[kTile][LD] = tiles + 1;  // K/V tile kt in buffer kt & 1
+    __half (*Vs)[kTile][LD] = tiles + 3;
     // grid (H, B, query tiles): every head and sequence of the longest rows (most key
     // tiles) is scheduled before any shorter one
     const int qt = gridDim.z - 1 - blockIdx.z;
@@ -233,7 +237,7 @@ __global__ void attn_rowdot_kernel(const __half* __restrict__ dout, const __half
 // through a two-deep cp.async ring. Dynamic shared memory: flash_dq_smem<D>() bytes.
 template <int D> constexpr int flash_dq_smem() { return 6 * fa::kTile * (D + 8) * 2; }
 template <int D>
-__global__ void __launch_bounds__(128, 4) flash_bwd_dq_mma_kernel(
+__global__ void __launch_bounds__(128, D >= 128 ? 1 : 4) flash_bwd_dq_mma_kernel(
     const __half* __restrict__ q, const __half* __restrict__ k, const __half* __restrict__ v,
     const __half* __restrict__ dout, const float* __restrict__ lse2, const float* __restrict__ Dd, int S, int H,
     float scale, __half* __restrict__ dq16, long long ld_dq, const float* __restrict__ cos_t,
@@ -333,7 +337,7 @@ __global__ void __launch_bounds__(128, 4) flash_bwd_dq_mma_kernel(
 // ring. Dynamic shared memory: flash_dkdv_smem<D>() bytes.
 template <int D> constexpr int flash_dkdv_smem() { return 6 * fa::kTile * (D + 8) * 2 + 4 * fa::kTile * 4; }
 template <int D>
-__global__ void __launch_bounds__(128, 3) flash_bwd_dkdv_mma_kernel(
+__global__ void __launch_bounds__(128, D >= 128 ? 1 : 3) flash_bwd_dkdv_mma_kernel(
     const __half* __restrict__ q, const __half* __restrict__ k, const __half* __restrict__ v,
     const __half* __restrict__ dout, const float* __restrict__ lse2, const float* __restrict__ Dd, int S, int H,
     float scale, float* __restrict__ dk, __half* __restrict__ dv16, long long ld_dv) {

@@ -192,7 +192,7 @@ int mm_cuda_forward_logits(mm_cuda_ctx* h, const uint16_t* tokens, int batch, in
         if (!tokens || !logits || batch < 1 || seq < 1 || seq > cx.c.maxS)
             mm::fail(MM_INVALID_ARGUMENT, "Input batch or sequence shape is invalid");
         check_tokens(cx, tokens, static_cast<long long>(batch) * seq);
-        const int per = std::max(1, mm::chunk_tokens_default() / seq);
+        const int per = std::max(1, mm::chunk_tokens(cx) / seq);
         mm::ensure_workspace(cx, std::min(batch, per) * seq, cx.ws.tape);
         for (int r0 = 0; r0 < batch; r0 += per) {
             const int bc = std::min(per, batch - r0);
@@ -236,7 +236,7 @@ int mm_cuda_accumulate(mm_cuda_ctx* h, const uint16_t* input, const uint16_t* ta
         check_tokens(cx, target, N);
         for (long long i = 0; i < N; ++i)
             if (!std::isfinite(coef[i])) mm::fail(MM_INVALID_ARGUMENT, "Invalid target or loss coefficient");
-        const int per = std::max(1, mm::chunk_tokens_default() / seq);
+        const int per = std::max(1, mm::chunk_tokens(cx) / seq);
         mm::ensure_workspace(cx, std::min(batch, per) * seq, true);
         mm::Workspace& w = cx.ws;
         double total = 0;
@@ -280,7 +280,7 @@ int mm_cuda_prefill_batch(mm_cuda_ctx* h, const uint16_t* prompts, int batch, in
         cx.serving = false;  // the decode state now holds this batch
         uint16_t* d = static_cast<uint16_t*>(cx.stage.get(static_cast<size_t>(batch) * prompt_len * 2));
         MM_CUDA_CHECK(cudaMemcpyAsync(d, prompts, static_cast<size_t>(batch) * prompt_len * 2, cudaMemcpyHostToDevice, cx.stream));
-        mm::prefill_rows(cx, d, batch, prompt_len, mm::chunk_tokens_default());
+        mm::prefill_rows(cx, d, batch, prompt_len, mm::chunk_tokens(cx));
         if (logits)
             MM_CUDA_CHECK(cudaMemcpyAsync(logits, cx.dec.logits, sizeof(float) * batch * cx.c.V, cudaMemcpyDeviceToHost, cx.stream));
         cx.dec_len = prompt_len;

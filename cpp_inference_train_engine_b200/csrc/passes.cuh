@@ -218,6 +218,14 @@ inline void ensure_workspace(Context& cx, int T, bool tape) {
     MM_CUDA_CHECK(cudaStreamSynchronize(cx.stream));
     Sizer sz;
     plan_workspace(cx, sz, T, tape);
+    // the rollout's latent cache makes room for a training chunk (tape) when both do not
+    // fit: 109 GB of cache for 2,048 rows of the 2,048-context 1.1B model. No tape pass runs
+    // inside a rollout, whose outputs are on the host by the time one does.
+    if (tape && !cx.ws_arena.fits(sz.used() + 4096) && !cx.serving && cx.dec.arena.capacity()) {
+        cx.dec.drop_graph();
+        cx.dec.arena.release();
+        cx.dec.B = 0;
+    }
     cx.ws_arena.release();
     cx.ws_arena.reserve(sz.used() + 4096);
     plan_workspace(cx, cx.ws_arena, T, tape);
@@ -426,8 +434,17 @@ inline void launch_flash_fwd(Context& cx, const LayerBuf& b, int Bc, int S) {
         dim3 gt(c.H, Bc, (S + fatc::kRows - 1) / fatc::kRows);
         MM_LAUNCH_TIMED(kKFlashFwd, work, flash_fwd_tc_kernel, gt, fatc::kThreads, fatc::kSmem, tq, tk, tv, S, c.H,
                         scale, b.ao, b.lse, cx.d_err);
-    } else if (c.qk() == 64) MM_LAUNCH_TIMED(kKFlashFwd, work, flash_fwd_mma_kernel<64>, grid, 128, 0, b.q, b.k, b.v, S, c.H, scale, b.ao, b.lse);
-    else MM_LAUNCH_TIMED(kKFlashFwd, work, flash_fwd_mma_kernel<16>, grid, 128, 0, b.q, b.k, b.v, S, c.H, scale, b.ao, b.lse);
+    } else if (c.qk() == 64) {
+        MM_LAUNCH_TIMED(kKFlashFwd, work, flash_fwd_mma_kernel<64>, grid, 128, flash_fwd_smem<64>(), b.q, b.k, b.v, S,
+                        c.H, scale, b.ao, b.lse);
+    } else if (c.qk() == 128) {
+        set_dynamic_smem<flash_fwd_mma_kernel<128>>(flash_fwd_smem<128>());
+        MM_LAUNCH_TIMED(kKFlashFwd, work, flash_fwd_mma_kernel<128>, grid, 128, flash_fwd_smem<128>(), b.q, b.k, b.v, S,
+                        c.H, scale, b.ao, b.lse);
+    } else {
+        MM_LAUNCH_TIMED(kKFlashFwd, work, flash_fwd_mma_kernel<16>, grid, 128, flash_fwd_smem<16>(), b.q, b.k, b.v, S,
+                        c.H, scale, b.ao, b.lse);
+    }
 }
 
 enum VocabMode { kVocabNone, kVocabAll, kVocabLast };
@@ -659,6 +676,14 @@ inline void backward_chunk(Context& cx, int Bc, int S) {
                                     b.v, w.dao16, b.lse, w.Dd, S, c.H, scale, w.dq16, (long long)ld_q16, cx.cos_t,
                                     cx.sin_t, c.nope, c.rope);
                 }
+            } else if (qk == 128) {
+                set_dynamic_smem<flash_bwd_dkdv_mma_kernel<128>>(flash_dkdv_smem<128>());
+                set_dynamic_smem<flash_bwd_dq_mma_kernel<128>>(flash_dq_smem<128>());
+                MM_LAUNCH_TIMED(kKFlashBwd, w_kv, flash_bwd_dkdv_mma_kernel<128>, grid, 128, flash_dkdv_smem<128>(), b.q,
+                                b.k, b.v, w.dao16, b.lse, w.Dd, S, c.H, scale, w.dk, w.dv16, (long long)ld_v16);
+                MM_LAUNCH_TIMED(kKFlashBwd, w_q, flash_bwd_dq_mma_kernel<128>, grid, 128, flash_dq_smem<128>(), b.q, b.k,
+                                b.v, w.dao16, b.lse, w.Dd, S, c.H, scale, w.dq16, (long long)ld_q16, cx.cos_t, cx.sin_t,
+                                c.nope, c.rope);
             } else {
                 MM_LAUNCH_TIMED(kKFlashBwd, w_kv, flash_bwd_dkdv_mma_kernel<16>, grid, 128, flash_dkdv_smem<16>(), b.q, b.k,
                                 b.v, w.dao16, b.lse, w.Dd, S, c.H, scale, w.dk, w.dv16, (long long)ld_v16);

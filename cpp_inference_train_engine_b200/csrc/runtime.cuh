@@ -72,6 +72,13 @@ class Arena {
         return reinterpret_cast<T*>(static_cast<char*>(base_) + off);
     }
     void reset() { used_ = 0; }
+    // Whether `bytes` more fit on the device now (with 1 GB to spare), counting this arena's
+    // own block as free when it is about to be replaced.
+    bool fits(size_t bytes) const {
+        size_t fr = 0, total = 0;
+        if (cudaMemGetInfo(&fr, &total) != cudaSuccess) return true;
+        return bytes + (1ull << 30) <= fr + cap_;
+    }
     void release() {
         if (base_) cudaFree(base_);
         base_ = nullptr;
@@ -293,6 +300,7 @@ class Context {
 
     Workspace ws;
     Arena ws_arena;
+    int chunk_cap = 0;  // tokens per chunk this model's workspace allows (chunk_tokens)
     Staging stage;
     Staging splitk;  // split-K partials of the GEMM
     Staging emb_acc; // fixed-point embedding-gather gradient [V][d] (+ max |dy|, non-finite flag)

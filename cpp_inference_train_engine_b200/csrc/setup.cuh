@@ -185,10 +185,11 @@ inline void validate_dims(const Dims& c) {
         fail(MM_INVALID_ARGUMENT, "Invalid vocabulary/layer/head count, d_model divisibility, or odd RoPE dimension");
     if (!std::isfinite(c.eps) || c.eps <= 0 || !std::isfinite(c.theta) || c.theta <= 1)
         fail(MM_INVALID_ARGUMENT, "Invalid normalization epsilon or RoPE theta");
-    const bool att_ok = (c.qk() == 16 && c.dv == 16) || (c.qk() == 64 && c.dv == 64);
-    if (!att_ok) fail(MM_UNSUPPORTED, "attention kernels are built for (qk, dv) = (16, 16) or (64, 64)");
-    const bool dec_ok = (c.kvr == 8 && c.rope == 4) || (c.kvr == 128 && c.rope == 16);
-    if (!dec_ok) fail(MM_UNSUPPORTED, "decode attention is built for (kv_rank, rope) = (8, 4) or (128, 16)");
+    const bool att_ok = c.qk() == c.dv && (c.qk() == 16 || c.qk() == 64 || c.qk() == 128);
+    if (!att_ok) fail(MM_UNSUPPORTED, "attention kernels are built for qk = dv in {16, 64, 128}");
+    const bool dec_ok = (c.kvr == 8 && c.rope == 4) || (c.kvr == 128 && c.rope == 16) || (c.kvr == 512 && c.rope == 32);
+    if (!dec_ok) fail(MM_UNSUPPORTED, "decode attention is built for (kv_rank, rope) = (8, 4), (128, 16) or (512, 32)");
+    if (c.H > kMaxDecodeHeads) fail(MM_UNSUPPORTED, "decode attention is built for at most 64 heads");
 }
 
 inline long long parameter_count(const Dims& c) {

@@ -265,11 +265,42 @@ inline int chunk_tokens_default() {
     return v;
 }
 
+// Tokens per chunk for this model: the default, capped (unless MM_CHUNK_TOKENS is set) so
+// that the policy's workspace with tape stays within 45 % of the device's memory. The cap
+// depends only on the model and the device, never on what is free at the time, so the
+// chunking (and with it the update's rounding) is the same on every run and rank. The 35.8M
+// model (~360 KB per token) keeps 196,608; the 2,048-wide 1.1B model (~2.4 MB) gets ~34 K.
+inline int chunk_tokens(Context& cx) {
+    static const bool pinned = std::getenv("MM_CHUNK_TOKENS") != nullptr;
+    if (pinned) return chunk_tokens_default();
+    if (!cx.chunk_cap) {
+        constexpr int kProbe = 4096;
+        const int T0 = cx.ws.T;
+        const bool tape0 = cx.ws.tape;
+        Sizer a, b;
+        plan_workspace(cx, a, kProbe, true);
+        plan_workspace(cx, b, 2 * kProbe, true);
+        const double per_token = static_cast<double>(b.used() - a.used()) / kProbe;
+        size_t fr = 0, total = 0;
+        MM_CUDA_CHECK(cudaMemGetInfo(&fr, &total));
+        cx.chunk_cap = static_cast<int>(std::min(2.0e9, 0.45 * static_cast<double>(total) / per_token));
+        // plan_workspace leaves the chunk's buffer table pointing nowhere: restore it
+        if (cx.ws_arena.capacity()) {
+            cx.ws_arena.reset();
+            plan_workspace(cx, cx.ws_arena, T0, tape0);
+        } else {
+            cx.ws.T = 0;
+            cx.ws.tape = tape0;
+        }
+    }
+    return std::max(1, std::min(chunk_tokens_default(), cx.chunk_cap));
+}
+
 // Teacher-forced log-probabilities of host batches [B][S] (Execution::log_probabilities),
 // chunked over whole sequences. Result into host `out` [B*S].
 inline void log_probs_host(Context& cx, const uint16_t* input, const uint16_t* target, int B, int S, float* out) {
     PhaseTimer t(cx, kPhLogprob);
-    const int per = std::max(1, chunk_tokens_default() / S);
+    const int per = std::max(1, chunk_tokens(cx) / S);
     ensure_workspace(cx, std::min(B, per) * S, cx.ws.tape);
     Workspace& w = cx.ws;
     for (int r0 = 0; r0 < B; r0 += per) {
@@ -350,7 +381,7 @@ inline mm_step_result grpo_step(Context& pc, Context& rc, const uint16_t* input,
     }
     MM_CUDA_CHECK(cudaMemsetAsync(pc.g, 0, sizeof(float) * pc.P_dev, pc.stream));
     MM_CUDA_CHECK(cudaMemsetAsync(pc.d_sums, 0, sizeof(GrpoSums), pc.stream));
-    const int per = std::max(1, chunk_tokens_default() / S);
+    const int per = std::max(1, chunk_tokens(pc) / S);
     ensure_workspace(pc, std::min(n, per) * S, true);
     ensure_workspace(rc, std::min(n, per) * S, rc.ws.tape);
     Workspace& w = pc.ws;
@@ -439,7 +470,7 @@ inline mm_step_result dpo_step(Context& pc, Context& rc, const uint16_t* input, 
     double2* part = static_cast<double2*>(pc.sums_part.get(sizeof(double2) * static_cast<size_t>(n) +
                                                             sizeof(double) * static_cast<size_t>(n)));
     double* d_margins = reinterpret_cast<double*>(part + n);
-    const int per = std::max(1, chunk_tokens_default() / (2 * S));  // pairs per chunk
+    const int per = std::max(1, chunk_tokens(pc) / (2 * S));  // pairs per chunk
     ensure_workspace(pc, 2 * std::min(n, per) * S, true);
     ensure_workspace(rc, 2 * std::min(n, per) * S, rc.ws.tape);
     Workspace& w = pc.ws;
@@ -515,7 +546,7 @@ inline void rollout(Context& cx, const uint16_t* prompts, int n, int P, int comp
     MM_CUDA_CHECK(cudaMemcpyAsync(d.seeds, seeds, static_cast<size_t>(n) * 8, cudaMemcpyHostToDevice, cx.stream));
     {
         PhaseTimer t(cx, kPhPrefill);
-        prefill_rows(cx, d_prompts, n, P, chunk_tokens_default());
+        prefill_rows(cx, d_prompts, n, P, chunk_tokens(cx));
     }
     MM_CUDA_CHECK(cudaMemsetAsync(d.step, 0, sizeof(int), cx.stream));
     {

@@ -98,11 +98,12 @@ def decode(args):
     import numpy as np
 
     import cpp_inference_train_engine_b200 as E
-    from cpp_inference_train_engine_b200.config import MLA36M
+    from cpp_inference_train_engine_b200.config import MLA1B, MLA36M
     from cpp_inference_train_engine_b200.rng import Rng
 
-    cfg = MLA36M
+    cfg = MLA36M if args.model == "mla36m" else MLA1B
     P = E.parameter_count(cfg)
+    kv_bytes = 2.0 * (cfg.kv_lora_rank + cfg.head_dim_rope) * cfg.n_layers  # per row and position
     ex = E.make_execution(cfg, E.init_params(cfg, 0))
     peak, src = _peak_hbm()
     for B in args.batch:
@@ -119,7 +120,14 @@ def decode(args):
                 if it == args.warmup:
                     ex.profile(1)
                 ex.rollout(prompts, args.new, S, seeds, temp, with_batches=False)
+            if args.gemm_shapes:
+                for row in ex.gemm_shapes()[:20]:
+                    print(json.dumps({"gemm_shape": row["shape"], "ms": row["ms"], "calls": row["calls"],
+                                      "tflops": row["tflops"]}))
             prof = ex.profile(0)
+            if args.gemm_shapes:
+                print(json.dumps({"mode": "phases", "batch": B,
+                                  "ms": {k: round(v[0], 3) for k, v in prof.items() if v[0]}}))
             if args.trace:
                 raw = ex.decode_trace_raw()
                 ph = ex.decode_trace(0)
@@ -145,7 +153,7 @@ def decode(args):
             ms = prof["decode"][0] + prof["sample"][0]
             steps = args.new - 1
             ctx = args.prompt + (args.new - 1) / 2.0  # mean positions attended per step
-            byts = steps * (2.0 * P + B * ctx * 2880.0)
+            byts = steps * (2.0 * P + B * ctx * kv_bytes)
             print(json.dumps({"mode": "decode", "batch": B, "prompt": args.prompt, "new": args.new,
                               "temperature": temp, "decode_ms": ms, "ms_per_step": ms / steps,
                               "tok_s": B * steps / (ms / 1e3),
@@ -167,6 +175,8 @@ def main(argv=None):
     ap.add_argument("--splits", type=int, default=0)
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=2)
+    ap.add_argument("--model", default="mla36m", choices=["mla36m", "mla1b"])
+    ap.add_argument("--gemm-shapes", action="store_true", help="per-shape GEMM device time of the timed run")
     ap.add_argument("--trace", action="store_true",
                     help="print the fused decode step's per-phase times (device global timer)")
     args = ap.parse_args(argv)

@@ -40,9 +40,10 @@ class Rng:
                      np.cos(np.float32(2.0 * np.pi) * u2))
 
 
-def grpo_workload(n_prompts: int, group: int, prompt_len: int, vocab: int, p_reward: float):
-    """Config-4 style synthetic GRPO inputs: prompts [n_prompts*group, prompt_len] (each
-    prompt repeated for its group), per-rollout seeds, Bernoulli(p_reward) rewards."""
+def grpo_workload(n_prompts: int, group: int, prompt_len: int, vocab: int, p_reward):
+    """Synthetic GRPO inputs: prompts [n_prompts*group, prompt_len] (each prompt repeated for
+    its group), per-rollout seeds, Bernoulli(p_reward) rewards (N(0, 1) when p_reward is
+    None)."""
     pr = Rng(2)
     base = np.array([[pr.bounded(vocab) for _ in range(prompt_len)] for _ in range(n_prompts)],
                     np.uint16)
@@ -50,6 +51,9 @@ def grpo_workload(n_prompts: int, group: int, prompt_len: int, vocab: int, p_rew
     sr = Rng(1)
     seeds = np.array([sr.next() for _ in range(n_prompts * group)], np.uint64)
     rr = Rng(3)
-    rewards = np.array([1.0 if rr.uniform() < p_reward else 0.0
-                        for _ in range(n_prompts * group)], np.float32)
+    if p_reward is None:
+        rewards = np.array([rr.normal() for _ in range(n_prompts * group)], np.float32)
+    else:
+        rewards = np.array([1.0 if rr.uniform() < p_reward else 0.0
+                            for _ in range(n_prompts * group)], np.float32)
     return prompts, seeds, rewards

@@ -59,6 +59,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "GRPO rollout tok/s + step time, 35.8M MLA, 1/2/4/8 B200; % HBM roofline"
+METRIC_MLA1B = "GRPO rollout tok/s + step time, scaled 1.14B MLA (context 2048), 1/2/4/8 B200; % HBM roofline"
 
 
 def parse():
@@ -248,7 +249,7 @@ def run_reference(args, rank, world):
     res = {"value": value, "unit": "tok/s", "cores": int(os.environ["OPENBLAS_NUM_THREADS"]),
            "host_threads": _host_threads(), "cpu_model": cpu_model(), "kind": "reference",
            "sample": smp.describe()}
-    line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
+    line = {"metric": METRIC if args.workload == "mla36m" else METRIC_MLA1B, "value": value, "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "impl": "reference",
             "higher_is_better": True, "dtype": "f32", "data": "synthetic",
             "config": workload_config(args, world),
@@ -485,7 +486,7 @@ def main():
         if world == 1 and not args.no_cpu_baseline and args.workload == "mla36m":
             cpu = cpu_baseline(args)
         line = {
-            "metric": METRIC, "value": toks / (dev_ms / 1e3), "unit": "tok/s", "n_gpus": world,
+            "metric": METRIC if args.workload == "mla36m" else METRIC_MLA1B, "value": toks / (dev_ms / 1e3), "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": dev_ms / args.steps,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "fp16 tensor-core compute, fp32 master/accumulate", "data": "synthetic",

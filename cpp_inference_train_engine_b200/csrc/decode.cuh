@@ -114,6 +114,7 @@ inline void ensure_decode(Context& cx, int B, int Sc, int max_new) {
     if (!d.arena.fits(sz.used() + 4096) && cx.ws_arena.capacity()) {
         cx.ws_arena.release();
         cx.ws.T = 0;
+        cx.ws.tape = false;  // a released workspace holds no tape: the next request plans its own
     }
     d.arena.release();
     d.arena.reserve(sz.used() + 4096);
@@ -238,7 +239,7 @@ inline void launch_decode_mk(Context& cx) {
 inline void prefill_rows(Context& cx, const uint16_t* d_prompts, int B, int P, int chunk_tokens) {
     DecodeState& d = cx.dec;
     const int per = std::max(1, chunk_tokens / P);
-    ensure_workspace(cx, std::min(B, per) * P, cx.ws.tape);
+    ensure_workspace(cx, std::min(B, per) * P, false);  // reuses a larger workspace with tape
     for (int r0 = 0; r0 < B; r0 += per) {
         const int bc = std::min(per, B - r0);
         MM_CUDA_CHECK(cudaMemcpyAsync(cx.ws.tokens, d_prompts + static_cast<long long>(r0) * P,

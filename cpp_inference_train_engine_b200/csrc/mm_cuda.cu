@@ -193,7 +193,7 @@ int mm_cuda_forward_logits(mm_cuda_ctx* h, const uint16_t* tokens, int batch, in
             mm::fail(MM_INVALID_ARGUMENT, "Input batch or sequence shape is invalid");
         check_tokens(cx, tokens, static_cast<long long>(batch) * seq);
         const int per = std::max(1, mm::chunk_tokens(cx) / seq);
-        mm::ensure_workspace(cx, std::min(batch, per) * seq, cx.ws.tape);
+        mm::ensure_workspace(cx, std::min(batch, per) * seq, false);
         for (int r0 = 0; r0 < batch; r0 += per) {
             const int bc = std::min(per, batch - r0);
             const long long T = static_cast<long long>(bc) * seq;

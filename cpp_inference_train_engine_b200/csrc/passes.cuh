@@ -219,12 +219,13 @@ inline void ensure_workspace(Context& cx, int T, bool tape) {
     Sizer sz;
     plan_workspace(cx, sz, T, tape);
     // the rollout's latent cache makes room for a training chunk (tape) when both do not
-    // fit: 109 GB of cache for 2,048 rows of the 2,048-context 1.1B model. No tape pass runs
-    // inside a rollout, whose outputs are on the host by the time one does.
-    if (tape && !cx.ws_arena.fits(sz.used() + 4096) && !cx.serving && cx.dec.arena.capacity()) {
+    // fit: 109 GB of cache for 2,048 rows of the 2,048-context 1.1B model. Never while a
+    // rollout or a serving session holds the cache.
+    if (tape && !cx.ws_arena.fits(sz.used() + 4096) && !cx.serving && !cx.dec.in_use && cx.dec.arena.capacity()) {
         cx.dec.drop_graph();
         cx.dec.arena.release();
         cx.dec.B = 0;
+        cx.dec_len = 0;  // a later decode without a new prefill fails cleanly
     }
     cx.ws_arena.release();
     cx.ws_arena.reserve(sz.used() + 4096);

@@ -209,6 +209,8 @@ struct DecodeState {
     bool mk_trace_on = false;
     int max_new = 0;
     Arena arena;
+    // set for the whole of a rollout: a workspace request inside it never takes the arena
+    bool in_use = false;
     // one captured rollout decode step (decode_sample_step), valid for the buffers above
     cudaGraphExec_t graph = nullptr;
     long long graph_launches = 0;  // kernels per replay

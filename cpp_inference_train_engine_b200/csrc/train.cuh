@@ -301,7 +301,7 @@ inline int chunk_tokens(Context& cx) {
 inline void log_probs_host(Context& cx, const uint16_t* input, const uint16_t* target, int B, int S, float* out) {
     PhaseTimer t(cx, kPhLogprob);
     const int per = std::max(1, chunk_tokens(cx) / S);
-    ensure_workspace(cx, std::min(B, per) * S, cx.ws.tape);
+    ensure_workspace(cx, std::min(B, per) * S, false);  // reuses a larger workspace with tape
     Workspace& w = cx.ws;
     for (int r0 = 0; r0 < B; r0 += per) {
         const int bc = std::min(per, B - r0);
@@ -539,6 +539,11 @@ inline void rollout(Context& cx, const uint16_t* prompts, int n, int P, int comp
         if (prompts[i] >= c.V) fail(MM_INVALID_ARGUMENT, "Input token exceeds vocabulary");
     const int Sc = P + length - 1;
     ensure_decode(cx, n, Sc, completion);
+    struct InUse {  // the cache is written from the prefill on: no workspace request may free it
+        bool& f;
+        explicit InUse(bool& x) : f(x) { f = true; }
+        ~InUse() { f = false; }
+    } in_use(cx.dec.in_use);
     cx.serving = false;  // the decode state now holds the rollout batch
     DecodeState& d = cx.dec;
     uint16_t* d_prompts = static_cast<uint16_t*>(cx.stage.get(static_cast<size_t>(n) * P * 2));

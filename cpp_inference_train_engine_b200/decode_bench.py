@@ -98,10 +98,16 @@ def decode(args):
     import numpy as np
 
     import cpp_inference_train_engine_b200 as E
-    from cpp_inference_train_engine_b200.config import MLA1B, MLA36M
+    from cpp_inference_train_engine_b200.config import MLA1B, MLA36M, ModelConfig
     from cpp_inference_train_engine_b200.rng import Rng
 
-    cfg = MLA36M if args.model == "mla36m" else MLA1B
+    # MLA1B's attention shapes (16 heads, kv rank 512, rope 32) on 2 layers of width 256: a
+    # small device footprint for single-kernel captures of its decode attention
+    MLA1B_ATTN = ModelConfig(vocab_size=2048, max_sequence_length=2048, n_layers=2, d_model=256, n_heads=16,
+                             head_dim_nope=96, head_dim_rope=32, head_dim_value=128, q_lora_rank=192,
+                             kv_lora_rank=512, d_ff=512)
+
+    cfg = {"mla36m": MLA36M, "mla1b": MLA1B, "mla1b-attn": MLA1B_ATTN}[args.model]
     P = E.parameter_count(cfg)
     kv_bytes = 2.0 * (cfg.kv_lora_rank + cfg.head_dim_rope) * cfg.n_layers  # per row and position
     ex = E.make_execution(cfg, E.init_params(cfg, 0))
@@ -158,7 +164,11 @@ def decode(args):
                               "temperature": temp, "decode_ms": ms, "ms_per_step": ms / steps,
                               "tok_s": B * steps / (ms / 1e3),
                               "hbm_roofline_frac": byts / (ms / 1e3) / 1e9 / peak, "peak_source": src,
-                              "prefill_ms": prof["prefill"][0]}))
+                              "prefill_ms": prof["prefill"][0],
+                              # event-timed launches only (eager steps; graph replays are not)
+                              "attention": {"ms": prof["k_decode_attention"][0],
+                                            "launches": prof["k_decode_attention"][1],
+                                            "gbs": prof["k_decode_attention"][2] / max(prof["k_decode_attention"][0], 1e-9) / 1e6}}))
     ex.close()
 
 
@@ -175,7 +185,7 @@ def main(argv=None):
     ap.add_argument("--splits", type=int, default=0)
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=2)
-    ap.add_argument("--model", default="mla36m", choices=["mla36m", "mla1b"])
+    ap.add_argument("--model", default="mla36m", choices=["mla36m", "mla1b", "mla1b-attn"])
     ap.add_argument("--gemm-shapes", action="store_true", help="per-shape GEMM device time of the timed run")
     ap.add_argument("--trace", action="store_true",
                     help="print the fused decode step's per-phase times (device global timer)")

@@ -275,6 +275,28 @@ __device__ __forceinline__ void mk_gemm_phase(const MkParams& p, const MkPipe& p
         for (int u = blockIdx.x; u < units; u += gridDim.x, ++acc_j) {
             const MkUnit t = unit_of(u);
             const int buf = acc_j & 1;
+            const int r = t.m0 + q * 32 + lane;
+            const bool live = r < p.B;
+            // what the latent epilogue reads besides the accumulator, fetched while the MMAs
+            // run: the norm weights (into L1) and, for the kv unit, the row's position and its
+            // rope table entries (registers)
+            int ps = 0;
+            bool in = false;
+            float cs[mk::ROPE / 2], sn[mk::ROPE / 2];
+            if constexpr (EPI == kMkLatent) {
+                const float* w = t.nt == 0 ? p.q_norm[l] : p.kv_norm[l];
+                const int nw = t.nt == 0 ? mk::QR : mk::KVR;
+                if (q * 32 + lane < nw / 32) prefetch_l1(w + 32 * (q * 32 + lane));
+                if (t.nt == 1) {
+                    ps = live ? __ldcg(p.pos + r) : 0;
+                    in = live && ps >= 0 && ps < p.Sc;
+#pragma unroll
+                    for (int h = 0; h < mk::ROPE / 2; ++h) {
+                        cs[h] = in ? p.cos_t[ps * (mk::ROPE / 2) + h] : 0.f;
+                        sn[h] = in ? p.sin_t[ps * (mk::ROPE / 2) + h] : 0.f;
+                    }
+                }
+            }
             if (!mbar_wait_bounded(&pp.acc_full[buf], (acc_j >> 1) & 1, p.err)) {
                 *pp.s_abort = 1;
                 break;
@@ -282,8 +304,6 @@ __device__ __forceinline__ void mk_gemm_phase(const MkParams& p, const MkPipe& p
             tc_fence_after();
             if (u == static_cast<int>(blockIdx.x) && warp == 4 && lane == 0) mk_stamp(p, kMkStampBase + 3 * gidx + 1);
             const uint32_t src = pp.tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * mk::kAccStride);
-            const int r = t.m0 + q * 32 + lane;
-            const bool live = r < p.B;
             float v[32];
             if constexpr (EPI == kMkLatent) {
                 // whole-row norms by one thread: tensor-memory reads in batches of 96 columns
@@ -325,17 +345,8 @@ __device__ __forceinline__ void mk_gemm_phase(const MkParams& p, const MkPipe& p
                     }
                 } else {
                     const float* w = p.kv_norm[l];
-                    const int ps = live ? __ldcg(p.pos + r) : 0;
-                    const bool in = live && ps >= 0 && ps < p.Sc;
                     if (live && !in) raise_error(p.err, kErrBadIndex);
                     __half* o = p.cache + ((static_cast<long long>(l) * p.B + r) * p.Sc + (in ? ps : 0)) * mk::KVW;
-                    // the rope tables of this row's position, fetched while tensor memory is read
-                    float cs[mk::ROPE / 2], sn[mk::ROPE / 2];
-#pragma unroll
-                    for (int h = 0; h < mk::ROPE / 2; ++h) {
-                        cs[h] = in ? p.cos_t[ps * (mk::ROPE / 2) + h] : 0.f;
-                        sn[h] = in ? p.sin_t[ps * (mk::ROPE / 2) + h] : 0.f;
-                    }
                     for (int c = 0; c < mk::KVW; c += 96) {  // columns [0, 96), [96, 192): latent 128 | rope 16
                         tmem_ld32_nowait(src + c, b3);
                         tmem_ld32_nowait(src + c + 32, b3 + 32);

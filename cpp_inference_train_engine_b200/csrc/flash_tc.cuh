@@ -1,6 +1,6 @@
-// Causal attention forward on the 5th-generation tensor cores for 64-wide heads (the
-// 35.8M model: qk = 48 nope + 16 rope, dv = 64), the teacher-forced passes of
-// ops::attention (ops.cpp:109-140). Output and per-row base-2 log-sum-exp are those of
+// Causal attention forward on the 5th-generation tensor cores for 64- and 128-wide heads (the
+// 35.8M model: qk = 48 nope + 16 rope = dv = 64; the scaled model: 96 + 32 = dv = 128), the
+// teacher-forced passes of ops::attention (ops.cpp:109-140). Output and per-row base-2 log-sum-exp are those of
 // flash_fwd_mma_kernel, so either backward consumes them.
 //
 // One CTA per (head, sequence, 128-query tile), 10 warps:
@@ -23,25 +23,33 @@ namespace mm {
 
 namespace fatc {
 constexpr int kRows = 128;                 // queries per CTA and keys per tile
-constexpr int kD = 64;                     // qk and value width
-constexpr int kTileBytes = kRows * kD * 2; // one 128 x 64 fp16 tile, 128-byte rows
+constexpr int kSub = kRows * 64 * 2;       // one 128 x 64 fp16 box, 128-byte rows
 constexpr int kSoftmaxWarps = 8;
 constexpr int kThreads = 32 * (kSoftmaxWarps + 2);
+// A 128-row tile of width D: D / 64 boxes of 64 columns, one after the other.
+template <int D> constexpr int tile_bytes() { return (D / 64) * kSub; }
 // Q, K[2], V, P (two 64-key halves), then barriers and the row exchange of the two softmax
-// halves: maxima [parity][half][row] and sums [half][row]
-constexpr int kSmem = 6 * kTileBytes + 1024 + 256 + 6 * kRows * 4;
+// halves: maxima [parity][half][row] and sums [half][row]. 96 KB at D = 64, 160 KB at 128.
+template <int D> constexpr int smem_bytes() { return 4 * tile_bytes<D>() + 2 * kSub + 1024 + 256 + 6 * kRows * 4; }
 constexpr uint32_t kTmemCols = 256;
-constexpr int kColS = 0, kColO = 128;
+constexpr int kColS = 0, kColO = 128;      // S: 128 key columns; O: D value columns
 }  // namespace fatc
 
-// q, k, v, out: fp16 [T][H * 64] (row pitch H * 64), T = sequences * S, viewed through the
-// tensor maps tmQ/tmK/tmV (box {64, 128}, 128-byte swizzle); lse2 fp32 [T][H].
-// grid (H, sequences, ceil(S / 128)); the longest query tiles are scheduled first.
-__global__ void __launch_bounds__(fatc::kThreads, 2)
+// q, k, v, out: fp16 [T][H * D] (row pitch H * D), D = 64 or 128 (qk = dv), T = sequences * S,
+// viewed through the tensor maps tmQ/tmK/tmV (box {64, 128}, 128-byte swizzle: a tile is D / 64
+// boxes); lse2 fp32 [T][H]. grid (H, sequences, ceil(S / 128)); the longest query tiles are
+// scheduled first. At D = 128 the softmax warps fold 64 value columns each and one CTA fits
+// per SM (160 KB of shared memory).
+template <int D>
+__global__ void __launch_bounds__(fatc::kThreads, D == 64 ? 2 : 1)
     flash_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV, int S, int H, float scale,
                         __half* __restrict__ out, float* __restrict__ lse2, int* err) {
     using namespace fatc;
+    static_assert(D == 64 || D == 128, "64- or 128-wide heads");
+    constexpr int kD = D;
+    constexpr int kTileBytes = tile_bytes<D>();
+    constexpr int kBoxes = D / 64;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~static_cast<uintptr_t>(1023));
@@ -49,7 +57,7 @@ __global__ void __launch_bounds__(fatc::kThreads, 2)
     uint8_t* sK = smem + kTileBytes;      // [2]
     uint8_t* sV = smem + 3 * kTileBytes;
     uint8_t* sP = smem + 4 * kTileBytes;  // keys [0, 64) then [64, 128)
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 6 * kTileBytes);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 4 * kTileBytes + 2 * kSub);
     uint64_t* q_full = bars + 0;
     uint64_t* k_full = bars + 1;   // [2]
     uint64_t* k_empty = bars + 3;  // [2]
@@ -63,7 +71,7 @@ __global__ void __launch_bounds__(fatc::kThreads, 2)
     uint64_t* o_empty = bars + 12; // softmax warps
     uint64_t* xbar = bars + 13;    // [4] the two softmax warps of a lane quadrant
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
-    float* xchg = reinterpret_cast<float*>(smem + 6 * kTileBytes + 256);
+    float* xchg = reinterpret_cast<float*>(smem + 4 * kTileBytes + 2 * kSub + 256);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int h = blockIdx.x, b = blockIdx.y;
@@ -106,15 +114,19 @@ __global__ void __launch_bounds__(fatc::kThreads, 2)
         if (lane == 0) {
             bool ok = true;
             mbar_arrive_expect_tx(q_full, kTileBytes);
-            tma_load_2d(sQ, &tmQ, q_full, h * kD, row_base + qt * kRows);
+#pragma unroll
+            for (int x = 0; x < kBoxes; ++x) tma_load_2d(sQ + x * kSub, &tmQ, q_full, h * kD + 64 * x, row_base + qt * kRows);
             for (int j = 0; j < nk && ok; ++j) {
                 const int s = j & 1, u = j >> 1;
                 if (!mbar_wait_bounded(&k_empty[s], (u & 1) ^ 1, err)) { ok = false; break; }
                 mbar_arrive_expect_tx(&k_full[s], kTileBytes);
-                tma_load_2d(sK + s * kTileBytes, &tmK, &k_full[s], h * kD, row_base + j * kRows);
+#pragma unroll
+                for (int x = 0; x < kBoxes; ++x)
+                    tma_load_2d(sK + s * kTileBytes + x * kSub, &tmK, &k_full[s], h * kD + 64 * x, row_base + j * kRows);
                 if (!mbar_wait_bounded(v_empty, (j & 1) ^ 1, err)) { ok = false; break; }
                 mbar_arrive_expect_tx(v_full, kTileBytes);
-                tma_load_2d(sV, &tmV, v_full, h * kD, row_base + j * kRows);
+#pragma unroll
+                for (int x = 0; x < kBoxes; ++x) tma_load_2d(sV + x * kSub, &tmV, v_full, h * kD + 64 * x, row_base + j * kRows);
             }
         }
     } else if (warp == 9) {
@@ -130,9 +142,9 @@ __global__ void __launch_bounds__(fatc::kThreads, 2)
                 tc_fence_after();
                 const uint32_t bk = smem_u32(sK + s * kTileBytes);
 #pragma unroll
-                for (int k = 0; k < kD / 16; ++k)
-                    tc_mma_f16(tmem + kColS, umma_desc_sw128(aq + k * 32, 16, 1024),
-                               umma_desc_sw128(bk + k * 32, 16, 1024), id_s, k ? 1u : 0u);
+                for (int k = 0; k < kD / 16; ++k)  // k-steps 4x..4x+3 in box x
+                    tc_mma_f16(tmem + kColS, umma_desc_sw128(aq + (k >> 2) * kSub + (k & 3) * 32, 16, 1024),
+                               umma_desc_sw128(bk + (k >> 2) * kSub + (k & 3) * 32, 16, 1024), id_s, k ? 1u : 0u);
                 tc_commit(s_full);
                 tc_commit(&k_empty[s]);
                 if (!mbar_wait_bounded(p_full, j & 1, err)) { ok = false; break; }
@@ -141,8 +153,9 @@ __global__ void __launch_bounds__(fatc::kThreads, 2)
                 tc_fence_after();
 #pragma unroll
                 for (int k = 0; k < kRows / 16; ++k)
-                    tc_mma_f16(tmem + kColO, umma_desc_sw128(ap + (k >> 2) * kTileBytes + (k & 3) * 32, 16, 1024),
-                               umma_desc_sw128(bv + k * 2048, 8192, 1024), id_o, k ? 1u : 0u);
+                    // V MN-major: 16 keys = 2048 B down a box; the next 64 value columns one box on
+                    tc_mma_f16(tmem + kColO, umma_desc_sw128(ap + (k >> 2) * kSub + (k & 3) * 32, 16, 1024),
+                               umma_desc_sw128(bv + k * 2048, D == 64 ? 8192 : kSub, 1024), id_o, k ? 1u : 0u);
                 tc_commit(o_full);
                 tc_commit(v_empty);
                 tc_commit(p_empty);
@@ -155,10 +168,11 @@ __global__ void __launch_bounds__(fatc::kThreads, 2)
         const int qpos = qt * kRows + r;
         const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
         const float cs = scale * 1.4426950408889634f;
-        uint8_t* prow = sP + hh * kTileBytes + r * 128;
-        float acc[32];
+        uint8_t* prow = sP + hh * kSub + r * 128;
+        constexpr int kHalf = kD / 2;  // value columns this warp folds
+        float acc[kHalf];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) acc[i] = 0.f;
+        for (int i = 0; i < kHalf; ++i) acc[i] = 0.f;
         float m_run = -INFINITY, l_run = 0.f;
         bool ok = true;
         for (int j = 0; j < nk && ok; ++j) {
@@ -228,12 +242,13 @@ __global__ void __launch_bounds__(fatc::kThreads, 2)
             }
             if (!mbar_wait_bounded(o_full, j & 1, err)) { ok = false; break; }
             tc_fence_after();
-            {
+#pragma unroll
+            for (int oc = 0; oc < kHalf; oc += 32) {
                 float o[32];
-                tmem_ld32_nowait(lane_base + kColO + hh * 32, o);
+                tmem_ld32_nowait(lane_base + kColO + hh * kHalf + oc, o);
                 tmem_wait_ld();
 #pragma unroll
-                for (int i = 0; i < 32; ++i) acc[i] = acc[i] * corr + o[i];
+                for (int i = 0; i < 32; ++i) acc[oc + i] = acc[oc + i] * corr + o[i];
             }
             tc_fence_before();
             __syncwarp();
@@ -253,9 +268,9 @@ __global__ void __launch_bounds__(fatc::kThreads, 2)
             const float l = l_run + xl[(hh ^ 1) * kRows + r];
             const float inv = 1.f / l;
             __half* dst = out + (static_cast<long long>(row_base) + qpos) * (static_cast<long long>(H) * kD) + h * kD +
-                          hh * 32;
+                          hh * kHalf;
 #pragma unroll
-            for (int i = 0; i < 32; i += 8) {
+            for (int i = 0; i < kHalf; i += 8) {
                 const __half2 h0 = __floats2half2_rn(acc[i] * inv, acc[i + 1] * inv);
                 const __half2 h1 = __floats2half2_rn(acc[i + 2] * inv, acc[i + 3] * inv);
                 const __half2 h2 = __floats2half2_rn(acc[i + 4] * inv, acc[i + 5] * inv);

@@ -247,6 +247,16 @@ __device__ __forceinline__ void gemm_drain_tile(const GemmArgs g, const CUtensor
             if (lane == 0) bulk_wait_read0();
             __syncwarp();
             uint8_t* rowp = stage_base + lane * 128;
+            if (row < g.M && col0 < g.N) {
+                // this row's 64 gate and 64 up values (128 B each, at most two lines apiece),
+                // requested before anything waits on them; addresses inside the row only
+                prefetch_l1(gr + col0);
+                prefetch_l1(gr + g.dglu_n + col0);
+                if (col0 + 32 < g.N) {
+                    prefetch_l1(gr + col0 + 32);
+                    prefetch_l1(gr + g.dglu_n + col0 + 32);
+                }
+            }
 #pragma unroll
             for (int hf = 0; hf < 2; ++hf) {
                 float t[32];
@@ -255,8 +265,8 @@ __device__ __forceinline__ void gemm_drain_tile(const GemmArgs g, const CUtensor
                 if (hf == 1 && c + CH * nhalf >= n_mma) gemm_release_acc(release_bar, lane);
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
-                    // 8 columns at a time; the barrier keeps the next group's loads behind this
-                    // group's math (registers)
+                    // 8 columns at a time (L1 hits after the prefetch above); the barrier keeps
+                    // the next group's loads behind this group's math (registers)
                     asm volatile("" ::: "memory");
                     const int col = col0 + 32 * hf + 8 * j;
                     const bool in = row < g.M && col < g.N;  // N % 8 == 0

@@ -400,7 +400,7 @@ inline void launch_rope_rows(Context& cx,const float* in, long long ldin, int T,
                   cx.cos_t, cx.sin_t, inverse, out32, ld32, out16, ld16);
 }
 
-// MM_FLASH_TC=0 keeps the 64-wide forward on the mma.sync kernel (for comparison).
+// MM_FLASH_TC=0 keeps the 64- and 128-wide forward on the mma.sync kernels (for comparison).
 inline bool flash_tc_enabled() {
     static const bool on = [] {
         const char* e = std::getenv("MM_FLASH_TC");
@@ -425,16 +425,23 @@ inline void launch_flash_fwd(Context& cx, const LayerBuf& b, int Bc, int S) {
     const float scale = 1.0f / std::sqrt(static_cast<float>(c.qk()));
     // causal pairs x (qk + dv) multiply-adds
     const double work = 2.0 * Bc * c.H * (S * (S + 1.0) / 2.0) * (c.qk() + c.dv);
-    if (c.qk() == 64 && c.dv == 64 && flash_tc_enabled()) {
-        // tcgen05 forward: Q, K, V tiles of 128 rows x 64 through TMA
-        const long long T = static_cast<long long>(Bc) * S, wd = static_cast<long long>(c.H) * 64;
+    if ((c.qk() == 64 || c.qk() == 128) && c.dv == c.qk() && flash_tc_enabled()) {
+        // tcgen05 forward: Q, K, V tiles of 128 rows x qk through TMA (boxes of 64 columns)
+        const int D = c.qk();
+        const long long T = static_cast<long long>(Bc) * S, wd = static_cast<long long>(c.H) * D;
         const CUtensorMap& tq = tensor_map(b.q, false, wd, T, wd, 64, fatc::kRows);
         const CUtensorMap& tk = tensor_map(b.k, false, wd, T, wd, 64, fatc::kRows);
         const CUtensorMap& tv = tensor_map(b.v, false, wd, T, wd, 64, fatc::kRows);
-        set_dynamic_smem<flash_fwd_tc_kernel>(fatc::kSmem);
         dim3 gt(c.H, Bc, (S + fatc::kRows - 1) / fatc::kRows);
-        MM_LAUNCH_TIMED(kKFlashFwd, work, flash_fwd_tc_kernel, gt, fatc::kThreads, fatc::kSmem, tq, tk, tv, S, c.H,
-                        scale, b.ao, b.lse, cx.d_err);
+        if (D == 64) {
+            set_dynamic_smem<flash_fwd_tc_kernel<64>>(fatc::smem_bytes<64>());
+            MM_LAUNCH_TIMED(kKFlashFwd, work, flash_fwd_tc_kernel<64>, gt, fatc::kThreads, fatc::smem_bytes<64>(), tq, tk,
+                            tv, S, c.H, scale, b.ao, b.lse, cx.d_err);
+        } else {
+            set_dynamic_smem<flash_fwd_tc_kernel<128>>(fatc::smem_bytes<128>());
+            MM_LAUNCH_TIMED(kKFlashFwd, work, flash_fwd_tc_kernel<128>, gt, fatc::kThreads, fatc::smem_bytes<128>(), tq,
+                            tk, tv, S, c.H, scale, b.ao, b.lse, cx.d_err);
+        }
     } else if (c.qk() == 64) {
         MM_LAUNCH_TIMED(kKFlashFwd, work, flash_fwd_mma_kernel<64>, grid, 128, flash_fwd_smem<64>(), b.q, b.k, b.v, S,
                         c.H, scale, b.ao, b.lse);

@@ -98,6 +98,8 @@ constexpr int kStages = 2;  // cache tiles per warp ring: one computing, one lan
 // per warp: a tile ring, its row's query (fp16) and P
 constexpr int kRingBytes = kStages * 16 * LDQ * 2;
 constexpr int kWarpSmem = kRingBytes + H * LDQ * 2 + H * LDP * 2;
+// the same with a STAGES-deep ring (the fused decode step gives its warps a deeper one)
+template <int STAGES> constexpr int warp_smem() { return STAGES * 16 * LDQ * 2 + H * LDQ * 2 + H * LDP * 2; }
 constexpr int kRowSmem = kWarps * kWarpSmem;
 // warps wanted in flight for the whole batch (8 per SM) when choosing context splits
 constexpr int kTargetWarps = 148 * 8;
@@ -115,7 +117,9 @@ constexpr int kTargetWarps = 148 * 8;
 // One work item of the split latent decode attention for one warp: row b, context split sp
 // of nsplit. `mine` is the warp's kWarpSmem bytes of shared memory. With nsplit == 1 the
 // normalised context goes to ctx; otherwise the split's partial (max, sum, O) goes to
-// part[(b * nsplit + sp) * H * (KV + 2)].
+// part[(b * nsplit + sp) * H * (KV + 2)]. STAGES cache tiles in the warp's ring (the
+// standalone kernel: dec::kStages; `mine` holds dec::warp_smem<STAGES>() bytes).
+template <int STAGES = dec::kStages>
 __device__ __forceinline__ void decode_attention_item(const float* __restrict__ qf, const __half* __restrict__ cache,
                                                       long long cache_seq_stride, const int* __restrict__ pos, int b,
                                                       int sp, int nsplit, float scale, __half* __restrict__ ctx,
@@ -127,9 +131,10 @@ __device__ __forceinline__ void decode_attention_item(const float* __restrict__ 
     using fa::mma16816;
     const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const long long item = static_cast<long long>(b) * nsplit + sp;
+    constexpr int kRing = STAGES * 16 * LDQ * 2;
     auto ring = reinterpret_cast<__half (*)[16][LDQ]>(mine);
-    auto Qs = reinterpret_cast<__half (*)[LDQ]>(mine + kRingBytes);
-    auto Pw = reinterpret_cast<__half (*)[LDP]>(mine + kRingBytes + H * LDQ * 2);
+    auto Qs = reinterpret_cast<__half (*)[LDQ]>(mine + kRing);
+    auto Pw = reinterpret_cast<__half (*)[LDP]>(mine + kRing + H * LDQ * 2);
     const int n = __ldcg(pos + b) + 1;
     const int tiles = (n + 15) / 16;
     const int per = (tiles + nsplit - 1) / nsplit;
@@ -142,13 +147,13 @@ __device__ __forceinline__ void decode_attention_item(const float* __restrict__ 
             for (int e = lane; e < 16 * (W / 8); e += 32) {
                 const int r = e / (W / 8), cc = (e % (W / 8)) * 8;
                 const bool ok = p0 + r < n;
-                cp_async16(&ring[j % kStages][r][cc], cb + static_cast<long long>(ok ? p0 + r : 0) * W + cc, ok);
+                cp_async16(&ring[j % STAGES][r][cc], cb + static_cast<long long>(ok ? p0 + r : 0) * W + cc, ok);
             }
         }
         cp_async_commit();
     };
 #pragma unroll
-    for (int j = 0; j < kStages - 1; ++j) issue(j);
+    for (int j = 0; j < STAGES - 1; ++j) issue(j);
     // the row's absorbed queries, pre-scaled into the base-2 domain, as fp16
     const float qscale = scale * fa::kLog2e;
     const float4* q4 = reinterpret_cast<const float4*>(qf + static_cast<long long>(b) * H * W);
@@ -187,10 +192,10 @@ __device__ __forceinline__ void decode_attention_item(const float* __restrict__ 
         const int tile = t_begin + j;
         if (tile >= t_end) break;
         const int p0 = tile * 16;
-        issue(j + kStages - 1);
-        cp_async_wait<kStages - 1>();
+        issue(j + STAGES - 1);
+        cp_async_wait<STAGES - 1>();
         __syncwarp();
-        __half (*Ct)[LDQ] = ring[j % kStages];
+        __half (*Ct)[LDQ] = ring[j % STAGES];
         float s[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int kk = 0; kk < W / 16; ++kk) {

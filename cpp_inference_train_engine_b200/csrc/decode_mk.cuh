@@ -47,7 +47,11 @@ constexpr int kBChunk = 64 * 128;   // 64 k x 64 n, fp16
 constexpr int kBChunks = 3;
 constexpr int kStageBytes = kABytes + kBChunks * kBChunk;
 constexpr int kRingBytes = kStages * kStageBytes;
-constexpr int kAttnBytes = kWarps * dec::kWarpSmem;
+// the attention phase reuses the ring's shared memory: each warp a 2-deep cache-tile ring
+// (deeper rings, up to 4 tiles in flight per item, measured no faster: the phase is bound by
+// its chain of dependent reads and the split merge, not by the tile loads)
+constexpr int kAttnStages = 2;
+constexpr int kAttnBytes = kWarps * dec::warp_smem<kAttnStages>();
 constexpr int kDataBytes = kRingBytes > kAttnBytes ? kRingBytes : kAttnBytes;
 constexpr int kSmem = kDataBytes + 1024 + 256;
 constexpr int kTmemCols = 512;
@@ -508,8 +512,9 @@ __device__ __forceinline__ void mk_attention_phase(const MkParams& p, int l, uin
     const int items = p.B * p.ns;
     for (int it = blockIdx.x * mk::kWarps + warp; it < items; it += gridDim.x * mk::kWarps) {
         const int b = it / p.ns, sp = it - b * p.ns;
-        decode_attention_item(p.qf, cache_l, static_cast<long long>(p.Sc) * mk::KVW, p.pos, b, sp, p.ns, p.scale,
-                              p.ctx16, p.attn_part, p.cos_t, p.sin_t, smem + warp * dec::kWarpSmem);
+        decode_attention_item<mk::kAttnStages>(p.qf, cache_l, static_cast<long long>(p.Sc) * mk::KVW, p.pos, b, sp,
+                                               p.ns, p.scale, p.ctx16, p.attn_part, p.cos_t, p.sin_t,
+                                               smem + warp * dec::warp_smem<mk::kAttnStages>());
         if (p.ns > 1) {
             __threadfence();
             __syncwarp();

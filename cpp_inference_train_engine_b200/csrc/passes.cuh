@@ -112,6 +112,107 @@ __global__ void split3_gather_kernel(const float* __restrict__ h, int d, int T, 
     h3[t * ld3 + 2 * d + j] = hi;
 }
 
+// The vocabulary head's rows of an update, compacted: h3 row i = the three-term split of hf
+// row sel[i] ([hi | lo | hi], as split3_gather_v4_kernel) and sel_tgt[i] its target.
+// 4 columns per thread (d % 4 == 0, 8-byte aligned h3 rows).
+__global__ void split3_select_v4_kernel(const float* __restrict__ h, int d, const int* __restrict__ sel, int n,
+                                        const uint16_t* __restrict__ targets, __half* __restrict__ h3, long long ld3,
+                                        uint16_t* __restrict__ sel_tgt) {
+    MM_PDL_ENTRY();
+    const int nv = d >> 2;
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n * nv) return;
+    const int t = i / nv, j = (i - t * nv) << 2;
+    const int src = sel[t];
+    if (j == 0) sel_tgt[t] = targets[src];
+    const float4 v = *reinterpret_cast<const float4*>(h + static_cast<long long>(src) * d + j);
+    const float f[4] = {v.x, v.y, v.z, v.w};
+    __half hi[4], lo[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        hi[k] = __float2half_rn(f[k]);
+        lo[k] = __float2half_rn(f[k] - __half2float(hi[k]));
+    }
+    __half* row = h3 + t * ld3;
+    const uint2 H = *reinterpret_cast<const uint2*>(hi), L = *reinterpret_cast<const uint2*>(lo);
+    *reinterpret_cast<uint2*>(row + j) = H;
+    *reinterpret_cast<uint2*>(row + d + j) = L;
+    *reinterpret_cast<uint2*>(row + 2 * d + j) = H;
+}
+
+// Row selection (mask != 0) in ascending order, in two launches of 1024-row blocks:
+// select_count_kernel counts each block's rows, select_write_kernel writes each block's
+// selected rows after the rows of the blocks before it.
+constexpr int kSelectBlock = 1024;
+__global__ void __launch_bounds__(kSelectBlock) select_count_kernel(const float* __restrict__ mask, int T,
+                                                                    int* __restrict__ counts) {
+    MM_PDL_ENTRY();
+    const int t = blockIdx.x * kSelectBlock + threadIdx.x;
+    const int c = __syncthreads_count(t < T && mask[t] != 0.f);
+    if (threadIdx.x == 0) counts[blockIdx.x] = c;
+}
+__global__ void __launch_bounds__(kSelectBlock) select_write_kernel(const float* __restrict__ mask, int T,
+                                                                    const int* __restrict__ counts,
+                                                                    int* __restrict__ sel) {
+    MM_PDL_ENTRY();
+    __shared__ int part[32], wcnt[32], woff[32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int before = 0;  // rows selected by the blocks before this one
+    for (int b = threadIdx.x; b < static_cast<int>(blockIdx.x); b += kSelectBlock) before += counts[b];
+    before = __reduce_add_sync(0xffffffffu, before);
+    const int t = blockIdx.x * kSelectBlock + threadIdx.x;
+    const bool f = t < T && mask[t] != 0.f;
+    const unsigned bal = __ballot_sync(0xffffffffu, f);
+    if (lane == 0) {
+        part[warp] = before;
+        wcnt[warp] = __popc(bal);
+    }
+    __syncthreads();
+    if (warp == 0) {
+        const int base = __reduce_add_sync(0xffffffffu, part[lane]);
+        int c = wcnt[lane], x = c;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, x, o);
+            if (lane >= o) x += y;
+        }
+        woff[lane] = base + x - c;  // exclusive prefix of the warps' counts
+    }
+    __syncthreads();
+    if (f) sel[woff[warp] + __popc(bal & ((1u << lane) - 1u))] = t;
+}
+
+// lp / lse of compacted row i to row sel[i] (the other rows were cleared).
+__global__ void scatter_lp_kernel(const int* __restrict__ sel, int n, const float* __restrict__ lp_c,
+                                  const float* __restrict__ lse_c, float* __restrict__ lp, float* __restrict__ lse) {
+    MM_PDL_ENTRY();
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    lp[sel[i]] = lp_c[i];
+    lse[sel[i]] = lse_c[i];
+}
+
+// coef of row sel[i] into compacted row i.
+__global__ void gather_coef_kernel(const int* __restrict__ sel, int n, const float* __restrict__ coef,
+                                   float* __restrict__ coef_c) {
+    MM_PDL_ENTRY();
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) coef_c[i] = coef[sel[i]];
+}
+
+// fp32 rows [n][d] to rows sel[i] of a [T][d] array whose other rows were cleared; 4 columns
+// per thread (d % 4 == 0, 16-byte aligned rows).
+__global__ void scatter_rows_v4_kernel(const float* __restrict__ src, const int* __restrict__ sel, int n, int d,
+                                       float* __restrict__ dst) {
+    MM_PDL_ENTRY();
+    const int nv = d >> 2;
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n * nv) return;
+    const int t = i / nv, j = (i - t * nv) << 2;
+    *reinterpret_cast<float4*>(dst + static_cast<long long>(sel[t]) * d + j) =
+        *reinterpret_cast<const float4*>(src + static_cast<long long>(t) * d + j);
+}
+
 // split3_gather_kernel, 4 columns per thread (d % 4 == 0, 8-byte aligned h3 rows).
 __global__ void split3_gather_v4_kernel(const float* __restrict__ h, int d, int T, int mul, int add,
                                         __half* __restrict__ h3, long long ld3) {
@@ -179,6 +280,12 @@ template <class A> void plan_workspace(Context& cx, A& a, int T, bool tape) {
     w.coef = a.template take<float>(t);
     w.old_lp = a.template take<float>(t);
     w.ref_lp = a.template take<float>(t);
+    w.sel = a.template take<int>(t);
+    w.sel_counts = a.template take<int>((t + kSelectBlock - 1) / kSelectBlock);
+    w.sel_tgt = a.template take<uint16_t>(t);
+    w.sel_lp = a.template take<float>(t);
+    w.sel_lse = a.template take<float>(t);
+    w.sel_coef = a.template take<float>(t);
     w.knope = a.template take<float>(t * c.H * c.nope);
     if (tape) {
         w.dy = a.template take<float>(t * c.d);
@@ -372,6 +479,17 @@ inline void launch_split3(Context& cx, const float* h, int d, int T, int mul, in
                   ld3);
 }
 
+// The workspace's row selection from its mask (already on cx.stream), nsel = the caller's
+// count of the same rows.
+inline void select_rows(Context& cx, int T, int nsel) {
+    Workspace& w = cx.ws;
+    w.nsel = nsel;
+    if (nsel <= 0 || nsel >= T) return;
+    const int nb = (T + kSelectBlock - 1) / kSelectBlock;
+    MM_LAUNCH(select_count_kernel, nb, kSelectBlock, 0, w.mask, T, w.sel_counts);
+    MM_LAUNCH(select_write_kernel, nb, kSelectBlock, 0, w.mask, T, w.sel_counts, w.sel);
+}
+
 inline void launch_rowdot(Context& cx, const __half* dout, const __half* out, int T, int H, int DV, float* Dd) {
     if (DV % 8 == 0 && al16(dout) && al16(out))
         MM_LAUNCH(attn_rowdot_v8_kernel, blocks_for(static_cast<long long>(T) * H, 256), 256, 0, dout, out, T, H, DV, Dd);
@@ -456,6 +574,17 @@ inline void launch_flash_fwd(Context& cx, const LayerBuf& b, int Bc, int S) {
 }
 
 enum VocabMode { kVocabNone, kVocabAll, kVocabLast };
+
+// Whether the vocabulary head of a T-row chunk runs on its nsel selected rows only (set by
+// the GRPO update for the rows with mask != 0; needs d % 4 == 0 for the row kernels).
+// MM_VOCAB_ROWS=all keeps every row (for comparison).
+inline bool vocab_rows_compact(const Context& cx, long long T) {
+    static const bool on = [] {
+        const char* e = std::getenv("MM_VOCAB_ROWS");
+        return !(e && std::strcmp(e, "all") == 0);
+    }();
+    return on && cx.ws.nsel > 0 && cx.ws.nsel < T && cx.c.d % 4 == 0;
+}
 
 // Forward over ws.tokens [Bc*S]. tape: keep every layer's activations. cache: write the
 // latent/rope cache of rows [row0, row0 + Bc) (prefill). Vocabulary head:
@@ -561,20 +690,34 @@ inline void forward_chunk(Context& cx, int Bc, int S, bool tape, VocabMode vm, b
     GemmOutSpec lo{nullptr, c.V, kOutF32};
     lo.alpha = 1.0f / kVocabScale;
     if (vm == kVocabAll) {
-        launch_split3(cx, w.hf, c.d, T, 1, 0, w.h3, ld3);
+        // an update's passes (nsel set) run the head on the rows it uses only
+        const bool compact = with_targets && vocab_rows_compact(cx, T);
+        const int M = compact ? w.nsel : T;
+        if (compact)
+            MM_LAUNCH(split3_select_v4_kernel, blocks_for(static_cast<long long>(M) * (c.d / 4), 256), 256, 0, w.hf, c.d,
+                      w.sel, M, w.targets, w.h3, (long long)ld3, w.sel_tgt);
+        else
+            launch_split3(cx, w.hf, c.d, T, 1, 0, w.h3, ld3);
         lo.out = w.logits;
         if (with_targets) {
             // log-softmax fused into the product: per-tile row partials, then one combine;
             // the logits themselves are stored only for the backward (tape)
             lo.lse_part = w.lse_part;
-            lo.targets = w.targets;
+            lo.targets = compact ? w.sel_tgt : w.targets;
             lo.tgt_logit = w.tgt_logit;
             lo.no_store = !tape;
         }
-        const int bn = gemm(cx, T, c.V, 3 * c.d, {w.h3, ld3, false}, {cx.E3(), cx.E3L(), false}, lo);
-        if (with_targets)
-            MM_LAUNCH_TIMED(kKLogsoftmax, 16.0 * T * ((c.V + bn - 1) / bn), lse_combine_kernel, blocks_for(T, kLseRows), 256,
-                            0, w.lse_part, 2 * ((c.V + bn - 1) / bn), T, w.tgt_logit, w.lp, w.lse_v, cx.d_err);
+        const int bn = gemm(cx, M, c.V, 3 * c.d, {w.h3, ld3, false}, {cx.E3(), cx.E3L(), false}, lo);
+        if (with_targets) {
+            MM_LAUNCH_TIMED(kKLogsoftmax, 16.0 * M * ((c.V + bn - 1) / bn), lse_combine_kernel, blocks_for(M, kLseRows), 256,
+                            0, w.lse_part, 2 * ((c.V + bn - 1) / bn), M, w.tgt_logit, compact ? w.sel_lp : w.lp,
+                            compact ? w.sel_lse : w.lse_v, cx.d_err);
+            if (compact) {  // rows outside the selection (mask 0) are never read: zero
+                MM_CUDA_CHECK(cudaMemsetAsync(w.lp, 0, sizeof(float) * T, cx.stream));
+                MM_CUDA_CHECK(cudaMemsetAsync(w.lse_v, 0, sizeof(float) * T, cx.stream));
+                MM_LAUNCH(scatter_lp_kernel, blocks_for(M, 256), 256, 0, w.sel, M, w.sel_lp, w.sel_lse, w.lp, w.lse_v);
+            }
+        }
     } else {
         MM_LAUNCH(split3_gather_kernel, blocks_for((long long)Bc * c.d, 256), 256, 0, w.hf, c.d, Bc, S, S - 1, w.h3,
                   (long long)ld3);
@@ -595,17 +738,32 @@ inline void backward_chunk(Context& cx, int Bc, int S) {
     const int ld_d = cx.d16(c.d), ld_qr = cx.d16(c.qr), ld_kvr = cx.d16(c.kvr), ld_ff = cx.d16(c.dff);
     const int ld3 = cx.d16(3 * c.d);
     const float* inv_s = cx.d_scale + 1;
-    // vocabulary head: g = s * coef * (softmax - onehot)
-    launch_vocab_grad(cx, w.logits, c.V, c.V, w.targets, w.lse_v, w.coef, cx.d_scale, T, w.g16, c.V);
+    // vocabulary head: g = s * coef * (softmax - onehot), on the forward's selected rows when
+    // it ran on those only (the other rows' coef is 0: their g, dH and dE terms are zero)
+    const bool compact = vocab_rows_compact(cx, T);
+    const int M = compact ? w.nsel : T;
+    if (compact) {
+        MM_LAUNCH(gather_coef_kernel, blocks_for(M, 256), 256, 0, w.sel, M, w.coef, w.sel_coef);
+        launch_vocab_grad(cx, w.logits, c.V, c.V, w.sel_tgt, w.sel_lse, w.sel_coef, cx.d_scale, M, w.g16, c.V);
+    } else {
+        launch_vocab_grad(cx, w.logits, c.V, c.V, w.targets, w.lse_v, w.coef, cx.d_scale, T, w.g16, c.V);
+    }
     {
-        GemmOutSpec o{w.dh, c.d, kOutF32};
+        // dH of the selected rows into dy (free until the final norm's backward writes it),
+        // then scattered into the cleared dH
+        GemmOutSpec o{compact ? w.dy : w.dh, c.d, kOutF32};
         o.alpha = 1.0f / kVocabScale;  // E3's hi part holds 64 * E
-        gemm(cx, T, c.d, c.V, {w.g16, c.V, false}, {cx.E3(), cx.E3L(), true}, o);
+        gemm(cx, M, c.d, c.V, {w.g16, c.V, false}, {cx.E3(), cx.E3L(), true}, o);
+        if (compact) {
+            MM_CUDA_CHECK(cudaMemsetAsync(w.dh, 0, sizeof(float) * T * c.d, cx.stream));
+            MM_LAUNCH(scatter_rows_v4_kernel, blocks_for(static_cast<long long>(M) * (c.d / 4), 256), 256, 0, w.dy, w.sel,
+                      M, c.d, w.dh);
+        }
     }
     {
         GemmOutSpec o{cx.GE(), c.d, kOutF32Acc};
         o.alpha_ptr = inv_s;
-        gemm(cx, c.V, c.d, T, {w.g16, c.V, true}, {w.h3, ld3, true}, o);  // h_hi = h3[:, :d]
+        gemm(cx, c.V, c.d, M, {w.g16, c.V, true}, {w.h3, ld3, true}, o);  // h_hi = h3[:, :d]
     }
     // dy (fp32, the residual gradient) and its fp16 copy for the layer's products
     launch_rmsnorm_backward(cx, w.x_out, c.d, cx.FinalNorm(), w.dh, c.d, (const float*)nullptr, 0LL, T, c.d, w.dy, c.d,

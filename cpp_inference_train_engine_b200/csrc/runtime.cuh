@@ -168,6 +168,14 @@ struct Workspace {
     float *dy, *dh2, *dres, *dao, *dk, *drope, *drope2, *dckv, *dkvraw, *dh, *dcq, *Dd;
     __half *dy16, *dg16, *du16, *dres16, *dq16, *dkn16, *dv16, *dkvp16, *draw16, *g16, *dao16;
     float* norm_part;   // [kNormBlocks][max(d, qr, kv_rank)] RMSNorm weight-gradient partials
+    // Rows whose log-probabilities the update uses (mask != 0): with 0 < nsel < T the
+    // vocabulary head and its backward run on these rows only (h3, logits, lse partials and
+    // the vocabulary gradient hold nsel compacted rows). nsel < 0: every row.
+    int nsel = -1;
+    int* sel;            // [T] row of compacted row i
+    int* sel_counts;     // [ceil(T / 1024)] selected rows per 1024-row block
+    uint16_t* sel_tgt;   // [T] target of compacted row i
+    float *sel_lp, *sel_lse, *sel_coef;  // [T] per compacted row
 };
 
 // Blocks of the RMSNorm backward (2 per SM): one weight-gradient partial row each.

@@ -386,9 +386,17 @@ inline mm_step_result grpo_step(Context& pc, Context& rc, const uint16_t* input,
     ensure_workspace(rc, std::min(n, per) * S, rc.ws.tape);
     Workspace& w = pc.ws;
     StreamOrder ref_lp_copied;
+    // the rows whose log-probabilities the update uses (mask != 0), per chunk: both models'
+    // vocabulary heads and the policy's vocabulary backward run on these only
+    struct Selection {
+        Context &p, &r;
+        ~Selection() { p.ws.nsel = r.ws.nsel = -1; }
+    } selection{pc, rc};
     for (int r0 = 0; r0 < n; r0 += per) {
         const int bc = std::min(per, n - r0);
         const long long T = static_cast<long long>(bc) * S, off = static_cast<long long>(r0) * S;
+        int nsel = 0;  // the GEMMs' row count; the devices list the rows themselves
+        for (long long i = 0; i < T; ++i) nsel += mask[off + i] != 0.f;
         {
             PhaseTimer t(pc, kPhLogprob);
             // the previous chunk's log-probs must have left rc.ws.lp before this forward
@@ -396,11 +404,14 @@ inline mm_step_result grpo_step(Context& pc, Context& rc, const uint16_t* input,
             ref_lp_copied.wait(rc.stream);
             MM_CUDA_CHECK(cudaMemcpyAsync(rc.ws.tokens, input + off, T * 2, cudaMemcpyHostToDevice, rc.stream));
             MM_CUDA_CHECK(cudaMemcpyAsync(rc.ws.targets, target + off, T * 2, cudaMemcpyHostToDevice, rc.stream));
+            MM_CUDA_CHECK(cudaMemcpyAsync(rc.ws.mask, mask + off, T * 4, cudaMemcpyHostToDevice, rc.stream));
+            select_rows(rc, static_cast<int>(T), nsel);
             reference_forward(pc, rc, bc, S);
             MM_CUDA_CHECK(cudaMemcpyAsync(w.tokens, input + off, T * 2, cudaMemcpyHostToDevice, pc.stream));
             MM_CUDA_CHECK(cudaMemcpyAsync(w.targets, target + off, T * 2, cudaMemcpyHostToDevice, pc.stream));
             MM_CUDA_CHECK(cudaMemcpyAsync(w.mask, mask + off, T * 4, cudaMemcpyHostToDevice, pc.stream));
             MM_CUDA_CHECK(cudaMemcpyAsync(w.old_lp, old_lp + off, T * 4, cudaMemcpyHostToDevice, pc.stream));
+            select_rows(pc, static_cast<int>(T), nsel);
             // the reference's log-probs reach the policy stream only after its forward completes
             MM_CUDA_CHECK(cudaStreamSynchronize(rc.stream));
             MM_CUDA_CHECK(cudaMemcpyAsync(w.ref_lp, rc.ws.lp, T * 4, cudaMemcpyDeviceToDevice, pc.stream));

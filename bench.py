@@ -471,7 +471,7 @@ def main():
                     # DRAM bytes of one vocabulary-head launch (the class's largest shape),
                     # single-launch ncu capture at M = 8,192 scaled to this chunk's M
                     "traffic": vocab_head_traffic(seq, R) if args.workload == "mla36m" else None,
-                    "traffic_kernel": "gemm_tc_pair_kernel, vocabulary head M x 16384 x 1536"}
+                    "traffic_kernel": "gemm_tc_pair_kernel, vocabulary head M x 16384 x 1536, log-sum-exp epilogue, no store"}
         dec_bytes = decode_algorithmic_bytes(cfg, pol.n_params, R, args.prompt_len, args.new_tokens)
         dec_gbs = dec_bytes / (decode_ms / 1e3) / 1e9 if decode_ms else None
         roofline_decode = {"phase": "rollout decode + sampling (per rank, slowest rank's time)",
@@ -516,12 +516,12 @@ def main():
 
 
 def vocab_head_traffic(seq, rollouts):
-    """DRAM bytes of one vocabulary-head launch of the teacher-forced pass at this workload's
-    chunk size: the committed single-launch capture of the CTA-pair kernel (912 MB read and
-    written at M = 8,192 tokens, logits stored) scaled by M, since both its logits stream and
-    its operand re-reads grow with the number of M-tiles."""
+    """DRAM bytes of one vocabulary-head launch at this workload's chunk size: the committed
+    single-launch capture of the CTA-pair kernel with the log-sum-exp epilogue and no logits
+    store (76.8 MB read + 8.4 MB written at M = 8,192; operands read 1.02x), scaled by M, as
+    its partials and the re-reads of B grow with the number of M-tiles."""
     chunk = min(rollouts, max(1, 196608 // seq)) * seq
-    return 911.9e6 * chunk / 8192.0
+    return 85.2e6 * chunk / 8192.0
 
 
 if __name__ == "__main__":

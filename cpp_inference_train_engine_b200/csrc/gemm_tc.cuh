@@ -72,6 +72,12 @@ struct GemmArgs {
     // so A = [hi | lo | hi] gives hi.W_hi + lo.W_hi + hi.W_lo. 0 = off.
     int b_k_wrap;
     int b_k3;
+    // Weighted-NLL gradient of recomputed logits (the vocabulary backward, fp16 output): the
+    // product's value v (after alpha) of row r, column c becomes
+    // vg_coef[r] * vg_scale[0] * (exp(v - vg_lse[r]) - (c == targets[r])). Null = off.
+    const float* vg_lse;
+    const float* vg_coef;
+    const float* vg_scale;
 };
 
 __device__ __forceinline__ int gemm_b_row(const GemmArgs& g, int k0) {
@@ -317,6 +323,13 @@ __device__ __forceinline__ void gemm_drain_tile(const GemmArgs g, const CUtensor
 #pragma unroll
             for (int i = 0; i < 32; ++i)
                 if (col0 + i < g.N) v[i] += r[i];
+        }
+        if (g.vg_lse && row < g.M) {
+            // coef * (softmax - onehot) of this row's recomputed logits (vocab_grad's arithmetic)
+            const float L = g.vg_lse[row], cf = g.vg_coef[row] * *g.vg_scale;
+            const int rel = static_cast<int>(g.targets[row]) - col0;
+#pragma unroll
+            for (int i = 0; i < 64; ++i) v[i] = cf * (__expf(v[i] - L) - (i == rel ? 1.f : 0.f));
         }
         if (g.lse_part) {  // fp32 output: 32 columns per chunk
             float cm = -INFINITY;

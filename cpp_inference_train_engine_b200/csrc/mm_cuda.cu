@@ -598,9 +598,44 @@ int mm_cuda_bench_gemm(mm_cuda_ctx* h, int reps, int M, int N, int K, const void
         // inputs written on any stream (the caller's) are complete before this stream reads them
         MM_CUDA_CHECK(cudaDeviceSynchronize());
         if (reps < 1 || reps > 4096 || M < 1 || N < 1 || K < 1 || !a || !b || !out || out_kind < 0 ||
-            out_kind > 3 || !ms_per_launch)
+            out_kind > 5 || !ms_per_launch)
             mm::fail(MM_INVALID_ARGUMENT, "invalid GEMM arguments");
-        mm::GemmOutSpec o{out, ldc, out_kind};
+        mm::GemmOutSpec o{out, ldc, out_kind <= 3 ? out_kind : (out_kind == 4 ? mm::kOutF32 : mm::kOutF16)};
+        // the vocabulary head's epilogues: per-row inputs and outputs in one scratch block
+        struct Scratch {
+            void* p = nullptr;
+            ~Scratch() { if (p) cudaFree(p); }
+        } scratch;
+        if (out_kind >= 4) {
+            const size_t parts = 2ull * ((N + 63) / 64) * M;  // float2 partials, any tile width
+            const size_t bytes = parts * 8 + 4ull * M * 4 + 16;
+            MM_CUDA_CHECK(cudaMalloc(&scratch.p, bytes));
+            MM_CUDA_CHECK(cudaMemsetAsync(scratch.p, 0, bytes, cx.stream));
+            char* q = static_cast<char*>(scratch.p);
+            float2* lse_part = reinterpret_cast<float2*>(q);
+            uint16_t* targets = reinterpret_cast<uint16_t*>(q + parts * 8);
+            float* row_a = reinterpret_cast<float*>(q + parts * 8 + 4ull * M);      // tgt_logit / lse
+            float* row_b = reinterpret_cast<float*>(q + parts * 8 + 8ull * M);      // coef
+            float* scale = reinterpret_cast<float*>(q + parts * 8 + 12ull * M);
+            std::vector<uint16_t> t(M);
+            for (int r = 0; r < M; ++r) t[r] = static_cast<uint16_t>(r % std::min(N, 65536));
+            const float one = 1.f;
+            std::vector<float> ones(M, 1.f);
+            MM_CUDA_CHECK(cudaMemcpyAsync(targets, t.data(), 2ull * M, cudaMemcpyHostToDevice, cx.stream));
+            MM_CUDA_CHECK(cudaMemcpyAsync(row_b, ones.data(), 4ull * M, cudaMemcpyHostToDevice, cx.stream));
+            MM_CUDA_CHECK(cudaMemcpyAsync(scale, &one, 4, cudaMemcpyHostToDevice, cx.stream));
+            MM_CUDA_CHECK(cudaStreamSynchronize(cx.stream));
+            o.targets = targets;
+            if (out_kind == 4) {
+                o.lse_part = lse_part;
+                o.tgt_logit = row_a;
+                o.no_store = true;
+            } else {
+                o.vg_lse = row_a;
+                o.vg_coef = row_b;
+                o.vg_scale = scale;
+            }
+        }
         const mm::Opnd A{a, lda, a_mn != 0}, B{b, ldb, b_mn != 0};
         // one eager launch sets kernel attributes and sizes the split-K staging
         mm::gemm(cx, M, N, K, A, B, o);

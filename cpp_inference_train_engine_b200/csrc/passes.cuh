@@ -575,6 +575,18 @@ inline void launch_flash_fwd(Context& cx, const LayerBuf& b, int Bc, int S) {
 
 enum VocabMode { kVocabNone, kVocabAll, kVocabLast };
 
+// The vocabulary backward recomputes the logit tiles (the same three-term product as the
+// forward, hence the same values) with the weighted-NLL gradient in the product's epilogue,
+// so no [T][V] logits are ever stored. MM_VOCAB_RECOMPUTE=0: the tape pass stores fp32
+// logits and vocab_grad_v4_kernel reads them (for comparison).
+inline bool vocab_recompute_enabled() {
+    static const bool on = [] {
+        const char* e = std::getenv("MM_VOCAB_RECOMPUTE");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
 // Whether the vocabulary head of a T-row chunk runs on its nsel selected rows only (set by
 // the GRPO update for the rows with mask != 0; needs d % 4 == 0 for the row kernels).
 // MM_VOCAB_ROWS=all keeps every row (for comparison).
@@ -701,11 +713,12 @@ inline void forward_chunk(Context& cx, int Bc, int S, bool tape, VocabMode vm, b
         lo.out = w.logits;
         if (with_targets) {
             // log-softmax fused into the product: per-tile row partials, then one combine;
-            // the logits themselves are stored only for the backward (tape)
+            // the logits are never stored (the backward recomputes them), except for the
+            // backward with stored logits (MM_VOCAB_RECOMPUTE=0)
             lo.lse_part = w.lse_part;
             lo.targets = compact ? w.sel_tgt : w.targets;
             lo.tgt_logit = w.tgt_logit;
-            lo.no_store = !tape;
+            lo.no_store = !tape || vocab_recompute_enabled();
         }
         const int bn = gemm(cx, M, c.V, 3 * c.d, {w.h3, ld3, false}, {cx.E3(), cx.E3L(), false}, lo);
         if (with_targets) {
@@ -742,11 +755,21 @@ inline void backward_chunk(Context& cx, int Bc, int S) {
     // it ran on those only (the other rows' coef is 0: their g, dH and dE terms are zero)
     const bool compact = vocab_rows_compact(cx, T);
     const int M = compact ? w.nsel : T;
-    if (compact) {
-        MM_LAUNCH(gather_coef_kernel, blocks_for(M, 256), 256, 0, w.sel, M, w.coef, w.sel_coef);
-        launch_vocab_grad(cx, w.logits, c.V, c.V, w.sel_tgt, w.sel_lse, w.sel_coef, cx.d_scale, M, w.g16, c.V);
+    if (compact) MM_LAUNCH(gather_coef_kernel, blocks_for(M, 256), 256, 0, w.sel, M, w.coef, w.sel_coef);
+    const uint16_t* tgt = compact ? w.sel_tgt : w.targets;
+    const float* lse = compact ? w.sel_lse : w.lse_v;
+    const float* cf = compact ? w.sel_coef : w.coef;
+    if (vocab_recompute_enabled()) {
+        // the forward's logit tiles again (h3 still holds its rows), gradient in the epilogue
+        GemmOutSpec o{w.g16, c.V, kOutF16};
+        o.alpha = 1.0f / kVocabScale;
+        o.targets = tgt;
+        o.vg_lse = lse;
+        o.vg_coef = cf;
+        o.vg_scale = cx.d_scale;
+        gemm(cx, M, c.V, 3 * c.d, {w.h3, ld3, false}, {cx.E3(), cx.E3L(), false}, o);
     } else {
-        launch_vocab_grad(cx, w.logits, c.V, c.V, w.targets, w.lse_v, w.coef, cx.d_scale, T, w.g16, c.V);
+        launch_vocab_grad(cx, w.logits, c.V, c.V, tgt, lse, cf, cx.d_scale, M, w.g16, c.V);
     }
     {
         // dH of the selected rows into dy (free until the final norm's backward writes it),

@@ -486,6 +486,11 @@ struct GemmOutSpec {
     // K = 2 b_k_wrap; three-term, B holds [hi; lo] of b_k_wrap rows each and K = 3 b_k_wrap
     int b_k_wrap = 0;
     bool b_k3 = false;
+    // weighted-NLL gradient of the recomputed logits (GemmArgs::vg_lse): fp16 product, per row
+    // log-sum-exp, coefficient and target (targets), device scale vg_scale[0]
+    const float* vg_lse = nullptr;
+    const float* vg_coef = nullptr;
+    const float* vg_scale = nullptr;
 };
 
 inline int sm_count() {

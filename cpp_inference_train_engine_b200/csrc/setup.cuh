@@ -36,6 +36,9 @@ inline int gemm(Context& cx, int M, int N, int K, Opnd A, Opnd B, const GemmOutS
     if (o.dglu_gu && (o.kind != kOutF16 || o.residual || o.lse_part || o.glu_n || o.rope_cos || !o.dglu_up ||
                       N % 8 || o.ldc % 8 || o.dglu_ld % 8 || o.dglu_ld < 2 * N))
         fail(MM_INVALID_ARGUMENT, "SwiGLU-backward epilogue needs a plain fp16 product, N % 8 == 0");
+    if (o.vg_lse && (o.kind != kOutF16 || o.residual || o.lse_part || o.glu_n || o.dglu_gu || o.rope_cos ||
+                     !o.targets || !o.vg_coef || !o.vg_scale))
+        fail(MM_INVALID_ARGUMENT, "vocabulary-gradient epilogue needs a plain fp16 product with targets");
     if (o.residual) {
         // out = alpha * A B + residual  ==  out := residual, then out += alpha * A B through the
         // TMA reduce-add epilogue (the residual moves as one coalesced device copy).
@@ -73,7 +76,8 @@ inline int gemm(Context& cx, int M, int N, int K, Opnd A, Opnd B, const GemmOutS
                 o.residual, o.ldr, o.alpha, o.alpha_ptr, cx.d_err, 0, 0,
                 o.lse_part, o.targets, o.tgt_logit, (o.lse_part && o.no_store) ? 1 : 0, o.glu_n,
                 o.rope_cos, o.rope_sin, o.rope_seq, o.rope_period, o.rope_begin, o.rope_len,
-                o.pre_gate ? 1 : 0, o.dglu_gu, o.dglu_ld, o.dglu_gu ? N : 0, o.b_k_wrap, o.b_k3 ? 1 : 0};
+                o.pre_gate ? 1 : 0, o.dglu_gu, o.dglu_ld, o.dglu_gu ? N : 0, o.b_k_wrap, o.b_k3 ? 1 : 0,
+                o.vg_lse, o.vg_coef, o.vg_scale};
     // Split-K for accumulating products with few output tiles over a long K (the weight
     // gradients, K = tokens): each K slice stores its fp32 partial, then one reduction adds
     // them in order into the destination.

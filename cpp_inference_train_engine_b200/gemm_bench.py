@@ -20,7 +20,9 @@ def main(argv=None):
     ap.add_argument("--shape", default="32640,16384,1536", help="M,N,K")
     ap.add_argument("--a-mn", type=int, default=0, help="A stored [K][M] (1) or [M][K] (0)")
     ap.add_argument("--b-mn", type=int, default=0, help="B stored [K][N] (1) or [N][K] (0)")
-    ap.add_argument("--out", default="f32", choices=["f32", "f16", "acc"])
+    ap.add_argument("--out", default="f32", choices=["f32", "f16", "acc", "lse", "vgrad"],
+                    help="lse: the vocabulary head's log-sum-exp epilogue, no store; vgrad: its "
+                         "backward's gradient epilogue, fp16 out (graph mode only)")
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--eager", action="store_true", help="time each eager call instead")
@@ -31,7 +33,7 @@ def main(argv=None):
     import cpp_inference_train_engine_b200 as E
 
     M, N, K = (int(v) for v in args.shape.split(","))
-    kind = {"f32": 0, "acc": 1, "f16": 2}[args.out]
+    kind = {"f32": 0, "acc": 1, "f16": 2, "lse": 4, "vgrad": 5}[args.out]
     ex = E.CudaExecution(E.TINY)
     g = torch.Generator(device="cuda").manual_seed(M + 3 * N + 7 * K)
     pad = (K + 7) // 8 * 8
@@ -39,7 +41,7 @@ def main(argv=None):
          else torch.randn(M, pad, device="cuda", generator=g)).half()
     B = (torch.randn(K, (N + 7) // 8 * 8, device="cuda", generator=g) if args.b_mn
          else torch.randn(N, pad, device="cuda", generator=g)).half()
-    C = torch.zeros(M, N, device="cuda", dtype=torch.half if kind == 2 else torch.float32)
+    C = torch.zeros(M, N, device="cuda", dtype=torch.half if kind in (2, 5) else torch.float32)
     torch.cuda.synchronize()
 
     def run():

@@ -101,7 +101,11 @@ int mm_cuda_selftest_wait_timeout(mm_cuda_ctx* ctx, uint32_t polls);
 /* Measurement entry (no reference counterpart): the product of mm_cuda_gemm_f16 (fp32
  * store, accumulate, fp16 or bf16 output, no residual) launched `reps` times back to back
  * inside one CUDA graph, so that consecutive launches overlap as in the engine's own
- * passes; *ms_per_launch receives the device time of one replay divided by reps. */
+ * passes; *ms_per_launch receives the device time of one replay divided by reps.
+ * out_kind 4 and 5 time the vocabulary head's two epilogues instead: 4 the forward's
+ * row log-sum-exp partials and target logits with no store (fp32 product; `out` unused but
+ * non-NULL), 5 the backward's weighted-NLL gradient of the recomputed logits into fp16 `out`
+ * (row log-sum-exp 0, coefficient 1, targets row % N: the arithmetic, not a gradient). */
 int mm_cuda_bench_gemm(mm_cuda_ctx* ctx, int reps, int M, int N, int K, const void* a, int64_t lda,
                        int a_mn, const void* b, int64_t ldb, int b_mn, void* out, int64_t ldc,
                        int out_kind, float* ms_per_launch);

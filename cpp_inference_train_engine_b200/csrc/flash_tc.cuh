@@ -37,13 +37,16 @@ constexpr int kColS = 0, kColO = 128;      // S: 128 key columns; O: D value col
 
 // q, k, v, out: fp16 [T][H * D] (row pitch H * D), D = 64 or 128 (qk = dv), T = sequences * S,
 // viewed through the tensor maps tmQ/tmK/tmV (box {64, 128}, 128-byte swizzle: a tile is D / 64
-// boxes); lse2 fp32 [T][H]. grid (H, sequences, ceil(S / 128)); the longest query tiles are
-// scheduled first. At D = 128 the softmax warps fold 64 value columns each and one CTA fits
-// per SM (160 KB of shared memory).
+// boxes); lse2 fp32 [T][H]. Persistent: a 1-D grid of at most the resident CTAs (two per SM
+// at D = 64, one at 128: 160 KB of shared memory) walks the work items (query tile, sequence,
+// head), longest query tiles first, round robin; barrier phases run on across items (the
+// producer loads the next item's Q as soon as the MMA warp has issued the current item's last
+// S product), so the setup (barriers, tensor memory) is paid once per CTA. At D = 128 the
+// softmax warps fold 64 value columns each.
 template <int D>
 __global__ void __launch_bounds__(fatc::kThreads, D == 64 ? 2 : 1)
     flash_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                        const __grid_constant__ CUtensorMap tmV, int S, int H, float scale,
+                        const __grid_constant__ CUtensorMap tmV, int S, int H, int nseq, float scale,
                         __half* __restrict__ out, float* __restrict__ lse2, int* err) {
     using namespace fatc;
     static_assert(D == 64 || D == 128, "64- or 128-wide heads");
@@ -71,17 +74,23 @@ __global__ void __launch_bounds__(fatc::kThreads, D == 64 ? 2 : 1)
     uint64_t* o_empty = bars + 12; // softmax warps
     uint64_t* xbar = bars + 13;    // [4] the two softmax warps of a lane quadrant
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
+    uint64_t* q_empty = bars + 18;  // the MMA warp: the item's S products have read Q
     float* xchg = reinterpret_cast<float*>(smem + 4 * kTileBytes + 2 * kSub + 256);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int h = blockIdx.x, b = blockIdx.y;
-    const int qt = gridDim.z - 1 - blockIdx.z;
-    const int nk = qt + 1;  // key tiles at or below the diagonal
-    const int row_base = b * S;
+    // persistent: work item i = (query tile, sequence, head), longest query tiles first
+    const int qtiles = (S + kRows - 1) / kRows, hs = H * nseq, items = hs * qtiles;
+    auto item_of = [&](int i, int& h, int& b, int& qt) {
+        qt = qtiles - 1 - i / hs;
+        const int r = i - (qtiles - 1 - qt) * hs;
+        b = r / H;
+        h = r - b * H;
+    };
 
     if (warp == 8) {
         if (lane == 0) {
             mbar_init(q_full, 1);
+            mbar_init(q_empty, 1);
             mbar_init(&k_full[0], 1);
             mbar_init(&k_full[1], 1);
             mbar_init(&k_empty[0], 1);
@@ -113,20 +122,28 @@ __global__ void __launch_bounds__(fatc::kThreads, D == 64 ? 2 : 1)
     if (warp == 8) {
         if (lane == 0) {
             bool ok = true;
-            mbar_arrive_expect_tx(q_full, kTileBytes);
+            int kc = 0;  // key tiles loaded so far (ring position)
+            for (int it = blockIdx.x, n = 0; it < items && ok; it += gridDim.x, ++n) {
+                int h, b, qt;
+                item_of(it, h, b, qt);
+                const int row_base = b * S;
+                // the previous item's S products have read Q
+                if (!mbar_wait_bounded(q_empty, (n & 1) ^ 1, err)) { ok = false; break; }
+                mbar_arrive_expect_tx(q_full, kTileBytes);
 #pragma unroll
-            for (int x = 0; x < kBoxes; ++x) tma_load_2d(sQ + x * kSub, &tmQ, q_full, h * kD + 64 * x, row_base + qt * kRows);
-            for (int j = 0; j < nk && ok; ++j) {
-                const int s = j & 1, u = j >> 1;
-                if (!mbar_wait_bounded(&k_empty[s], (u & 1) ^ 1, err)) { ok = false; break; }
-                mbar_arrive_expect_tx(&k_full[s], kTileBytes);
+                for (int x = 0; x < kBoxes; ++x) tma_load_2d(sQ + x * kSub, &tmQ, q_full, h * kD + 64 * x, row_base + qt * kRows);
+                for (int j = 0; j <= qt; ++j, ++kc) {
+                    const int s = kc & 1, u = kc >> 1;
+                    if (!mbar_wait_bounded(&k_empty[s], (u & 1) ^ 1, err)) { ok = false; break; }
+                    mbar_arrive_expect_tx(&k_full[s], kTileBytes);
 #pragma unroll
-                for (int x = 0; x < kBoxes; ++x)
-                    tma_load_2d(sK + s * kTileBytes + x * kSub, &tmK, &k_full[s], h * kD + 64 * x, row_base + j * kRows);
-                if (!mbar_wait_bounded(v_empty, (j & 1) ^ 1, err)) { ok = false; break; }
-                mbar_arrive_expect_tx(v_full, kTileBytes);
+                    for (int x = 0; x < kBoxes; ++x)
+                        tma_load_2d(sK + s * kTileBytes + x * kSub, &tmK, &k_full[s], h * kD + 64 * x, row_base + j * kRows);
+                    if (!mbar_wait_bounded(v_empty, (kc & 1) ^ 1, err)) { ok = false; break; }
+                    mbar_arrive_expect_tx(v_full, kTileBytes);
 #pragma unroll
-                for (int x = 0; x < kBoxes; ++x) tma_load_2d(sV + x * kSub, &tmV, v_full, h * kD + 64 * x, row_base + j * kRows);
+                    for (int x = 0; x < kBoxes; ++x) tma_load_2d(sV + x * kSub, &tmV, v_full, h * kD + 64 * x, row_base + j * kRows);
+                }
             }
         }
     } else if (warp == 9) {
@@ -134,152 +151,169 @@ __global__ void __launch_bounds__(fatc::kThreads, D == 64 ? 2 : 1)
             const uint32_t id_s = umma_idesc_f16(false, false, false, kRows, kRows);  // Q K^T, both K-major
             const uint32_t id_o = umma_idesc_f16(false, false, true, kRows, kD);      // P V, V MN-major
             const uint32_t aq = smem_u32(sQ), ap = smem_u32(sP), bv = smem_u32(sV);
-            bool ok = mbar_wait_bounded(q_full, 0, err);
-            for (int j = 0; j < nk && ok; ++j) {
-                const int s = j & 1, u = j >> 1;
-                if (!mbar_wait_bounded(&k_full[s], u & 1, err)) { ok = false; break; }
-                if (!mbar_wait_bounded(s_empty, (j & 1) ^ 1, err)) { ok = false; break; }
-                tc_fence_after();
-                const uint32_t bk = smem_u32(sK + s * kTileBytes);
+            bool ok = true;
+            int kc = 0;
+            for (int it = blockIdx.x, n = 0; it < items && ok; it += gridDim.x, ++n) {
+                int h, b, qt;
+                item_of(it, h, b, qt);
+                if (!mbar_wait_bounded(q_full, n & 1, err)) { ok = false; break; }
+                for (int j = 0; j <= qt; ++j, ++kc) {
+                    const int s = kc & 1, u = kc >> 1;
+                    if (!mbar_wait_bounded(&k_full[s], u & 1, err)) { ok = false; break; }
+                    if (!mbar_wait_bounded(s_empty, (kc & 1) ^ 1, err)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t bk = smem_u32(sK + s * kTileBytes);
 #pragma unroll
-                for (int k = 0; k < kD / 16; ++k)  // k-steps 4x..4x+3 in box x
-                    tc_mma_f16(tmem + kColS, umma_desc_sw128(aq + (k >> 2) * kSub + (k & 3) * 32, 16, 1024),
-                               umma_desc_sw128(bk + (k >> 2) * kSub + (k & 3) * 32, 16, 1024), id_s, k ? 1u : 0u);
-                tc_commit(s_full);
-                tc_commit(&k_empty[s]);
-                if (!mbar_wait_bounded(p_full, j & 1, err)) { ok = false; break; }
-                if (!mbar_wait_bounded(v_full, j & 1, err)) { ok = false; break; }
-                if (!mbar_wait_bounded(o_empty, (j & 1) ^ 1, err)) { ok = false; break; }
-                tc_fence_after();
+                    for (int k = 0; k < kD / 16; ++k)  // k-steps 4x..4x+3 in box x
+                        tc_mma_f16(tmem + kColS, umma_desc_sw128(aq + (k >> 2) * kSub + (k & 3) * 32, 16, 1024),
+                                   umma_desc_sw128(bk + (k >> 2) * kSub + (k & 3) * 32, 16, 1024), id_s, k ? 1u : 0u);
+                    tc_commit(s_full);
+                    tc_commit(&k_empty[s]);
+                    if (j == qt) tc_commit(q_empty);  // the item's last read of Q
+                    if (!mbar_wait_bounded(p_full, kc & 1, err)) { ok = false; break; }
+                    if (!mbar_wait_bounded(v_full, kc & 1, err)) { ok = false; break; }
+                    if (!mbar_wait_bounded(o_empty, (kc & 1) ^ 1, err)) { ok = false; break; }
+                    tc_fence_after();
 #pragma unroll
-                for (int k = 0; k < kRows / 16; ++k)
-                    // V MN-major: 16 keys = 2048 B down a box; the next 64 value columns one box on
-                    tc_mma_f16(tmem + kColO, umma_desc_sw128(ap + (k >> 2) * kSub + (k & 3) * 32, 16, 1024),
-                               umma_desc_sw128(bv + k * 2048, D == 64 ? 8192 : kSub, 1024), id_o, k ? 1u : 0u);
-                tc_commit(o_full);
-                tc_commit(v_empty);
-                tc_commit(p_empty);
+                    for (int k = 0; k < kRows / 16; ++k)
+                        // V MN-major: 16 keys = 2048 B down a box; the next 64 value columns one box on
+                        tc_mma_f16(tmem + kColO, umma_desc_sw128(ap + (k >> 2) * kSub + (k & 3) * 32, 16, 1024),
+                                   umma_desc_sw128(bv + k * 2048, D == 64 ? 8192 : kSub, 1024), id_o, k ? 1u : 0u);
+                    tc_commit(o_full);
+                    tc_commit(v_empty);
+                    tc_commit(p_empty);
+                }
             }
         }
     } else {
         // softmax: thread = query row r of the tile (TMEM lane r), key/value half hh
         const int q = warp & 3, hh = warp >> 2;
         const int r = q * 32 + lane;
-        const int qpos = qt * kRows + r;
         const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
         const float cs = scale * 1.4426950408889634f;
         uint8_t* prow = sP + hh * kSub + r * 128;
         constexpr int kHalf = kD / 2;  // value columns this warp folds
-        float acc[kHalf];
-#pragma unroll
-        for (int i = 0; i < kHalf; ++i) acc[i] = 0.f;
-        float m_run = -INFINITY, l_run = 0.f;
         bool ok = true;
-        for (int j = 0; j < nk && ok; ++j) {
-            if (!mbar_wait_bounded(s_full, j & 1, err)) { ok = false; break; }
-            tc_fence_after();
-            const bool diag = j == qt;
-            // diagonal tile: columns after the query or past the sequence end are masked
-            const int lim = diag ? min(qpos, S - 1) - j * kRows - hh * 64 : 63;
-            float mx = -INFINITY;
+        int kc = 0;  // key tiles consumed so far (barrier phases)
+        int xc = 0;  // uses of this quadrant's exchange barrier so far
+        for (int it = blockIdx.x; it < items && ok; it += gridDim.x) {
+            int h, b, qt;
+            item_of(it, h, b, qt);
+            const int nk = qt + 1;  // key tiles at or below the diagonal
+            const int row_base = b * S;
+            const int qpos = qt * kRows + r;
+            float acc[kHalf];
 #pragma unroll
-            for (int c = 0; c < 2; ++c) {
-                float v[32];
-                tmem_ld32_nowait(lane_base + kColS + hh * 64 + c * 32, v);
-                tmem_wait_ld();
-                if (diag) {
+            for (int i = 0; i < kHalf; ++i) acc[i] = 0.f;
+            float m_run = -INFINITY, l_run = 0.f;
+            for (int j = 0; j < nk; ++j, ++kc) {
+                if (!mbar_wait_bounded(s_full, kc & 1, err)) { ok = false; break; }
+                tc_fence_after();
+                const bool diag = j == qt;
+                // diagonal tile: columns after the query or past the sequence end are masked
+                const int lim = diag ? min(qpos, S - 1) - j * kRows - hh * 64 : 63;
+                float mx = -INFINITY;
 #pragma unroll
-                    for (int i = 0; i < 32; ++i)
-                        if (c * 32 + i <= lim) mx = fmaxf(mx, v[i]);
-                } else {
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) mx = fmaxf(mx, v[i]);
-                }
-            }
-            float* xm = xchg + (j & 1) * 2 * kRows;
-            xm[hh * kRows + r] = mx;
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&xbar[q]);
-            if (!mbar_wait_bounded(&xbar[q], j & 1, err)) { ok = false; break; }
-            mx = fmaxf(mx, xm[(hh ^ 1) * kRows + r]) * cs;  // cs > 0: max commutes with the scale
-            const float m_new = fmaxf(m_run, mx);
-            const float base = m_new == -INFINITY ? 0.f : m_new;
-            const float corr = fast_exp2(m_run - base);
-            if (!mbar_wait_bounded(p_empty, (j & 1) ^ 1, err)) { ok = false; break; }
-            float ls = 0.f;
-#pragma unroll 1
-            for (int c = 0; c < 2; ++c) {
-                float v[32];
-                tmem_ld32_nowait(lane_base + kColS + hh * 64 + c * 32, v);
-                tmem_wait_ld();
-                uint32_t w[16];
-#pragma unroll
-                for (int i = 0; i < 32; i += 2) {
-                    float p0 = fast_exp2(fmaf(v[i], cs, -base));
-                    float p1 = fast_exp2(fmaf(v[i + 1], cs, -base));
+                for (int c = 0; c < 2; ++c) {
+                    float v[32];
+                    tmem_ld32_nowait(lane_base + kColS + hh * 64 + c * 32, v);
+                    tmem_wait_ld();
                     if (diag) {
-                        if (c * 32 + i > lim) p0 = 0.f;
-                        if (c * 32 + i + 1 > lim) p1 = 0.f;
+#pragma unroll
+                        for (int i = 0; i < 32; ++i)
+                            if (c * 32 + i <= lim) mx = fmaxf(mx, v[i]);
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) mx = fmaxf(mx, v[i]);
                     }
-                    ls += p0 + p1;
-                    const __half2 hp = __floats2half2_rn(p0, p1);
-                    w[i >> 1] = *reinterpret_cast<const uint32_t*>(&hp);
                 }
-                // keys [32c, 32c + 32) of this half: four 16-byte chunks, 128-byte swizzle
+                float* xm = xchg + (kc & 1) * 2 * kRows;
+                xm[hh * kRows + r] = mx;
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&xbar[q]);
+                if (!mbar_wait_bounded(&xbar[q], xc & 1, err)) { ok = false; break; }
+                ++xc;
+                mx = fmaxf(mx, xm[(hh ^ 1) * kRows + r]) * cs;  // cs > 0: max commutes with the scale
+                const float m_new = fmaxf(m_run, mx);
+                const float base = m_new == -INFINITY ? 0.f : m_new;
+                const float corr = fast_exp2(m_run - base);
+                if (!mbar_wait_bounded(p_empty, (kc & 1) ^ 1, err)) { ok = false; break; }
+                float ls = 0.f;
+#pragma unroll 1
+                for (int c = 0; c < 2; ++c) {
+                    float v[32];
+                    tmem_ld32_nowait(lane_base + kColS + hh * 64 + c * 32, v);
+                    tmem_wait_ld();
+                    uint32_t w[16];
 #pragma unroll
-                for (int q4 = 0; q4 < 4; ++q4) {
-                    const int cc = c * 4 + q4;
-                    *reinterpret_cast<uint4*>(prow + ((cc ^ (r & 7)) << 4)) =
-                        make_uint4(w[4 * q4], w[4 * q4 + 1], w[4 * q4 + 2], w[4 * q4 + 3]);
+                    for (int i = 0; i < 32; i += 2) {
+                        float p0 = fast_exp2(fmaf(v[i], cs, -base));
+                        float p1 = fast_exp2(fmaf(v[i + 1], cs, -base));
+                        if (diag) {
+                            if (c * 32 + i > lim) p0 = 0.f;
+                            if (c * 32 + i + 1 > lim) p1 = 0.f;
+                        }
+                        ls += p0 + p1;
+                        const __half2 hp = __floats2half2_rn(p0, p1);
+                        w[i >> 1] = *reinterpret_cast<const uint32_t*>(&hp);
+                    }
+                    // keys [32c, 32c + 32) of this half: four 16-byte chunks, 128-byte swizzle
+#pragma unroll
+                    for (int q4 = 0; q4 < 4; ++q4) {
+                        const int cc = c * 4 + q4;
+                        *reinterpret_cast<uint4*>(prow + ((cc ^ (r & 7)) << 4)) =
+                            make_uint4(w[4 * q4], w[4 * q4 + 1], w[4 * q4 + 2], w[4 * q4 + 3]);
+                    }
                 }
-            }
-            tc_fence_before();
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(s_empty);
-                mbar_arrive(p_full);
-            }
-            if (!mbar_wait_bounded(o_full, j & 1, err)) { ok = false; break; }
-            tc_fence_after();
+                tc_fence_before();
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(s_empty);
+                    mbar_arrive(p_full);
+                }
+                if (!mbar_wait_bounded(o_full, kc & 1, err)) { ok = false; break; }
+                tc_fence_after();
 #pragma unroll
-            for (int oc = 0; oc < kHalf; oc += 32) {
-                float o[32];
-                tmem_ld32_nowait(lane_base + kColO + hh * kHalf + oc, o);
-                tmem_wait_ld();
+                for (int oc = 0; oc < kHalf; oc += 32) {
+                    float o[32];
+                    tmem_ld32_nowait(lane_base + kColO + hh * kHalf + oc, o);
+                    tmem_wait_ld();
 #pragma unroll
-                for (int i = 0; i < 32; ++i) acc[oc + i] = acc[oc + i] * corr + o[i];
+                    for (int i = 0; i < 32; ++i) acc[oc + i] = acc[oc + i] * corr + o[i];
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(o_empty);
+                l_run = l_run * corr + ls;
+                m_run = m_new;
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(o_empty);
-            l_run = l_run * corr + ls;
-            m_run = m_new;
-        }
-        // the row sum is the two halves' sums (same maxima, same corrections)
-        float* xl = xchg + 2 * 2 * kRows;
-        if (ok) {
+            if (!ok) break;
+            // the row sum is the two halves' sums (same maxima, same corrections)
+            float* xl = xchg + 2 * 2 * kRows;
             xl[hh * kRows + r] = l_run;
             __syncwarp();
             if (lane == 0) mbar_arrive(&xbar[q]);
-            ok = mbar_wait_bounded(&xbar[q], nk & 1, err);
-        }
-        if (ok && qpos < S) {
-            const float l = l_run + xl[(hh ^ 1) * kRows + r];
-            const float inv = 1.f / l;
-            __half* dst = out + (static_cast<long long>(row_base) + qpos) * (static_cast<long long>(H) * kD) + h * kD +
-                          hh * kHalf;
+            if (!mbar_wait_bounded(&xbar[q], xc & 1, err)) { ok = false; break; }
+            ++xc;
+            if (qpos < S) {
+                const float l = l_run + xl[(hh ^ 1) * kRows + r];
+                const float inv = 1.f / l;
+                __half* dst = out + (static_cast<long long>(row_base) + qpos) * (static_cast<long long>(H) * kD) + h * kD +
+                              hh * kHalf;
 #pragma unroll
-            for (int i = 0; i < kHalf; i += 8) {
-                const __half2 h0 = __floats2half2_rn(acc[i] * inv, acc[i + 1] * inv);
-                const __half2 h1 = __floats2half2_rn(acc[i + 2] * inv, acc[i + 3] * inv);
-                const __half2 h2 = __floats2half2_rn(acc[i + 4] * inv, acc[i + 5] * inv);
-                const __half2 h3 = __floats2half2_rn(acc[i + 6] * inv, acc[i + 7] * inv);
-                *reinterpret_cast<uint4*>(dst + i) =
-                    make_uint4(*reinterpret_cast<const uint32_t*>(&h0), *reinterpret_cast<const uint32_t*>(&h1),
-                               *reinterpret_cast<const uint32_t*>(&h2), *reinterpret_cast<const uint32_t*>(&h3));
+                for (int i = 0; i < kHalf; i += 8) {
+                    const __half2 h0 = __floats2half2_rn(acc[i] * inv, acc[i + 1] * inv);
+                    const __half2 h1 = __floats2half2_rn(acc[i + 2] * inv, acc[i + 3] * inv);
+                    const __half2 h2 = __floats2half2_rn(acc[i + 4] * inv, acc[i + 5] * inv);
+                    const __half2 h3 = __floats2half2_rn(acc[i + 6] * inv, acc[i + 7] * inv);
+                    *reinterpret_cast<uint4*>(dst + i) =
+                        make_uint4(*reinterpret_cast<const uint32_t*>(&h0), *reinterpret_cast<const uint32_t*>(&h1),
+                                   *reinterpret_cast<const uint32_t*>(&h2), *reinterpret_cast<const uint32_t*>(&h3));
+                }
+                if (hh == 0) lse2[(static_cast<long long>(row_base) + qpos) * H + h] = m_run + log2f(l);
             }
-            if (hh == 0) lse2[(static_cast<long long>(row_base) + qpos) * H + h] = m_run + log2f(l);
+            // the partner half reads xl before its next exchange, which this warp waits for
         }
     }
     tc_fence_before();

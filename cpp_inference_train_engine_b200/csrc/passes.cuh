@@ -550,15 +550,22 @@ inline void launch_flash_fwd(Context& cx, const LayerBuf& b, int Bc, int S) {
         const CUtensorMap& tq = tensor_map(b.q, false, wd, T, wd, 64, fatc::kRows);
         const CUtensorMap& tk = tensor_map(b.k, false, wd, T, wd, 64, fatc::kRows);
         const CUtensorMap& tv = tensor_map(b.v, false, wd, T, wd, 64, fatc::kRows);
-        dim3 gt(c.H, Bc, (S + fatc::kRows - 1) / fatc::kRows);
+        // persistent: the resident CTAs walk every (query tile, sequence, head) item
+        const long long items = static_cast<long long>(c.H) * Bc * ((S + fatc::kRows - 1) / fatc::kRows);
+        const int resident = sm_count() * (D == 64 ? 2 : 1);
+        static const bool persistent = [] {
+            const char* e = std::getenv("MM_FLASH_PERSISTENT");  // 0: one item per CTA (comparison)
+            return !(e && e[0] == '0');
+        }();
+        const int gt = static_cast<int>(persistent ? std::min<long long>(items, resident) : items);
         if (D == 64) {
             set_dynamic_smem<flash_fwd_tc_kernel<64>>(fatc::smem_bytes<64>());
             MM_LAUNCH_TIMED(kKFlashFwd, work, flash_fwd_tc_kernel<64>, gt, fatc::kThreads, fatc::smem_bytes<64>(), tq, tk,
-                            tv, S, c.H, scale, b.ao, b.lse, cx.d_err);
+                            tv, S, c.H, Bc, scale, b.ao, b.lse, cx.d_err);
         } else {
             set_dynamic_smem<flash_fwd_tc_kernel<128>>(fatc::smem_bytes<128>());
             MM_LAUNCH_TIMED(kKFlashFwd, work, flash_fwd_tc_kernel<128>, gt, fatc::kThreads, fatc::smem_bytes<128>(), tq,
-                            tk, tv, S, c.H, scale, b.ao, b.lse, cx.d_err);
+                            tk, tv, S, c.H, Bc, scale, b.ao, b.lse, cx.d_err);
         }
     } else if (c.qk() == 64) {
         MM_LAUNCH_TIMED(kKFlashFwd, work, flash_fwd_mma_kernel<64>, grid, 128, flash_fwd_smem<64>(), b.q, b.k, b.v, S,

@@ -118,13 +118,15 @@ constexpr int kTargetWarps = 148 * 8;
 // of nsplit. `mine` is the warp's kWarpSmem bytes of shared memory. With nsplit == 1 the
 // normalised context goes to ctx; otherwise the split's partial (max, sum, O) goes to
 // part[(b * nsplit + sp) * H * (KV + 2)]. STAGES cache tiles in the warp's ring (the
-// standalone kernel: dec::kStages; `mine` holds dec::warp_smem<STAGES>() bytes).
+// standalone kernel: dec::kStages; `mine` holds dec::warp_smem<STAGES>() bytes). qrow
+// (optional): a per-row factor of the queries (the fused step's q-latent RMSNorm scale).
 template <int STAGES = dec::kStages>
 __device__ __forceinline__ void decode_attention_item(const float* __restrict__ qf, const __half* __restrict__ cache,
                                                       long long cache_seq_stride, const int* __restrict__ pos, int b,
                                                       int sp, int nsplit, float scale, __half* __restrict__ ctx,
                                                       float* __restrict__ part, const float* __restrict__ cos_t,
-                                                      const float* __restrict__ sin_t, unsigned char* mine) {
+                                                      const float* __restrict__ sin_t, unsigned char* mine,
+                                                      const float* __restrict__ qrow = nullptr) {
     using namespace dec;
     using fa::ldsm_x4;
     using fa::ldsm_x4_t;
@@ -154,8 +156,9 @@ __device__ __forceinline__ void decode_attention_item(const float* __restrict__ 
     };
 #pragma unroll
     for (int j = 0; j < STAGES - 1; ++j) issue(j);
-    // the row's absorbed queries, pre-scaled into the base-2 domain, as fp16
-    const float qscale = scale * fa::kLog2e;
+    // the row's absorbed queries, pre-scaled into the base-2 domain (and by the row factor
+    // qrow[b] when the queries come unnormalised), as fp16
+    const float qscale = scale * fa::kLog2e * (qrow ? __ldcg(qrow + b) : 1.f);
     const float4* q4 = reinterpret_cast<const float4*>(qf + static_cast<long long>(b) * H * W);
     const int p = n - 1;  // position of this step's token
     for (int e = lane; e < H * W / 4; e += 32) {

@@ -101,6 +101,7 @@ inline void ensure_decode(Context& cx, int B, int Sc, int max_new) {
         d.active = a.template take<int>(B);
         d.mk_part = a.template take<float>(static_cast<long long>(mk::kMaxKs) * B * c.d);
         d.mk_cnt = a.template take<int>(B);
+        d.mk_qs = a.template take<float>(B);
         d.mk_bar = a.template take<unsigned>(1);
         d.mk_trace = a.template take<unsigned long long>(kMkTraceSlots);
     };
@@ -137,9 +138,8 @@ inline bool decode_mk_enabled(const Context& cx) {
         const int v = e ? std::atoi(e) : 0;
         return v > 0 ? v : 512;
     }();
-    const Dims& c = cx.c;
-    return on && cx.dec.B <= max_rows && c.d == mk::D && c.qr == mk::QR && c.kvr == mk::KVR && c.rope == mk::ROPE && c.H == mk::H &&
-           c.dff == mk::DFF && c.L <= mk::kMaxLayers && c.nope + c.rope == 64;
+    // (the folded query weights exist for that shape only)
+    return on && cx.dec.B <= max_rows && mk_shape(cx.c) && cx.prep[0].Wf;
 }
 
 // Launches decode_mk_kernel for the rows of cx.dec: embedding of dec.tok through the h3 rows
@@ -152,19 +152,18 @@ inline void launch_decode_mk(Context& cx) {
     const int G = sm_count();
     MkParams p{};
     p.a_h16 = tensor_map(d.h16, false, mk::D, B, cx.d16(c.d), 64, 128);
-    p.a_cq16 = tensor_map(d.cq16, false, mk::QR, B, cx.d16(c.qr), 64, 128);
     p.a_ctx16 = tensor_map(d.ctx16, false, mk::HKV, B, mk::HKV, 64, 128);
     p.a_h2 = tensor_map(d.h2, false, mk::D, B, cx.d16(c.d), 64, 128);
     p.a_gated = tensor_map(d.gated, false, mk::DFF, B, cx.d16(c.dff), 64, 128);
     for (int l = 0; l < c.L; ++l) {
         const PrepLayer& w = cx.prep[l];
         p.wa[l] = tensor_map(w.Wa, false, mk::QKV, mk::D, w.lda, 64, 64);
-        p.wq[l] = tensor_map(w.Wq, false, mk::QW, mk::QR, w.ldq, 64, 64);
+        p.wf[l] = tensor_map(w.Wf, false, mk::QW, mk::D, w.ldf, 64, 64);
         p.wo[l] = tensor_map(w.Wo, false, mk::D, mk::HKV, w.ldo, 64, 64);
         p.wgu[l] = tensor_map(w.Wgu, false, 2 * mk::DFF, mk::D, w.ldgu, 64, 64);
         p.wdown[l] = tensor_map(cx.S(l, kWdown), false, mk::D, mk::DFF, cx.SL(l, kWdown), 64, 64);
-        const void* wb[5] = {w.Wa, w.Wq, w.Wo, w.Wgu, cx.S(l, kWdown)};
-        const long long wn[5] = {2LL * mk::D * w.lda, 2LL * mk::QR * w.ldq, 2LL * mk::HKV * w.ldo,
+        const void* wb[5] = {w.Wa, w.Wf, w.Wo, w.Wgu, cx.S(l, kWdown)};
+        const long long wn[5] = {2LL * mk::D * w.lda, 2LL * mk::D * w.ldf, 2LL * mk::HKV * w.ldo,
                                  2LL * mk::D * w.ldgu, 2LL * mk::DFF * cx.SL(l, kWdown)};
         for (int k = 0; k < 5; ++k) {
             p.wbase[l][k] = wb[k];
@@ -198,7 +197,7 @@ inline void launch_decode_mk(Context& cx) {
     p.scale = 1.0f / std::sqrt(static_cast<float>(c.qk()));
     p.x = d.x;
     p.h16 = d.h16;
-    p.cq16 = d.cq16;
+    p.qs = d.mk_qs;
     p.qf = d.qf;
     p.ctx16 = d.ctx16;
     p.h2 = d.h2;

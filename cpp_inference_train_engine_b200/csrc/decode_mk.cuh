@@ -63,8 +63,9 @@ static_assert(dec::H == H && dec::KV == KVR && dec::R == ROPE, "latent attention
 // Everything one fused decode step reads and writes. The tensor maps: K-major activation
 // maps (box 64 x 128 rows) and MN-major weight maps (box 64 x 64) per layer.
 struct MkParams {
-    CUtensorMap a_h16, a_cq16, a_ctx16, a_h2, a_gated;
-    CUtensorMap wa[mk::kMaxLayers], wq[mk::kMaxLayers], wo[mk::kMaxLayers], wgu[mk::kMaxLayers],
+    CUtensorMap a_h16, a_ctx16, a_h2, a_gated;
+    // wf: the query weights W_dq . diag(g_q) . Wq folded for the latent phase [D][QW]
+    CUtensorMap wa[mk::kMaxLayers], wf[mk::kMaxLayers], wo[mk::kMaxLayers], wgu[mk::kMaxLayers],
         wdown[mk::kMaxLayers];
     const float* attn_norm[mk::kMaxLayers];
     const float* ffn_norm[mk::kMaxLayers];
@@ -80,8 +81,8 @@ struct MkParams {
     float eps, scale;
     float* x;                // [B][D] residual stream
     __half* h16;             // [B][D] normed layer input
-    __half* cq16;            // [B][QR] normed q latent
-    float* qf;               // [B][QW] absorbed query
+    float* qs;               // [B] the q latent's RMSNorm scale 1 / rms (the query's row factor)
+    float* qf;               // [B][QW] absorbed query before its row factor
     __half* ctx16;           // [B][HKV]
     __half* h2;              // [B][D]
     __half* gated;           // [B][DFF]
@@ -170,13 +171,14 @@ struct MkUnit {
 
 template <int EPI>
 __device__ __forceinline__ int mk_b_col(int nt, int j) {
-    if constexpr (EPI == kMkLatent) return nt * mk::QR + 64 * j;     // q: 0,64,128; kv: 192,256,320
+    // latent units: q 0,64,128 and kv 192,256,320 of Wa; then 192-column tiles of Wf
+    if constexpr (EPI == kMkLatent) return nt < 2 ? nt * mk::QR + 64 * j : (nt - 2) * mk::QR + 64 * j;
     if constexpr (EPI == kMkGlu) return j == 0 ? 64 * nt : mk::DFF + 64 * nt;  // gate, up
     return 128 * nt + 64 * j;
 }
 template <int EPI> __host__ __device__ constexpr int mk_chunks() { return EPI == kMkLatent ? 3 : 2; }
 template <int EPI> __device__ __forceinline__ int mk_n_mma(int nt) {
-    if constexpr (EPI == kMkLatent) return nt == 0 ? mk::QR : mk::KVW;
+    if constexpr (EPI == kMkLatent) return nt == 1 ? mk::KVW : mk::QR;
     return 128;
 }
 
@@ -241,7 +243,9 @@ __device__ __forceinline__ void mk_gemm_phase(const MkParams& p, const MkPipe& p
                     mbar_arrive_expect_tx(&pp.full[s], mk::kABytes + CH * mk::kBChunk);
                     tma_load_2d(sa, ta, &pp.full[s], kb * 64, t.m0);
 #pragma unroll
-                    for (int j = 0; j < CH; ++j) tma_load_2d(sb + j * mk::kBChunk, tb, &pp.full[s], mk_b_col<EPI>(t.nt, j), kb * 64);
+                    for (int j = 0; j < CH; ++j)
+                        tma_load_2d(sb + j * mk::kBChunk, (EPI == kMkLatent && t.nt >= 2) ? &p.wf[l] : tb, &pp.full[s],
+                                    mk_b_col<EPI>(t.nt, j), kb * 64);
                 }
             }
             if (!ok) *pp.s_abort = 1;
@@ -281,17 +285,14 @@ __device__ __forceinline__ void mk_gemm_phase(const MkParams& p, const MkPipe& p
             const int buf = acc_j & 1;
             const int r = t.m0 + q * 32 + lane;
             const bool live = r < p.B;
-            // what the latent epilogue reads besides the accumulator, fetched while the MMAs
-            // run: the norm weights (into L1) and, for the kv unit, the row's position and its
-            // rope table entries (registers)
+            // what the kv unit's epilogue reads besides the accumulator, fetched while the MMAs
+            // run: its norm weights (into L1), the row's position and its rope table entries
             int ps = 0;
             bool in = false;
             float cs[mk::ROPE / 2], sn[mk::ROPE / 2];
             if constexpr (EPI == kMkLatent) {
-                const float* w = t.nt == 0 ? p.q_norm[l] : p.kv_norm[l];
-                const int nw = t.nt == 0 ? mk::QR : mk::KVR;
-                if (q * 32 + lane < nw / 32) prefetch_l1(w + 32 * (q * 32 + lane));
                 if (t.nt == 1) {
+                    if (q * 32 + lane < mk::KVR / 32) prefetch_l1(p.kv_norm[l] + 32 * (q * 32 + lane));
                     ps = live ? __ldcg(p.pos + r) : 0;
                     in = live && ps >= 0 && ps < p.Sc;
 #pragma unroll
@@ -310,6 +311,22 @@ __device__ __forceinline__ void mk_gemm_phase(const MkParams& p, const MkPipe& p
             const uint32_t src = pp.tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * mk::kAccStride);
             float v[32];
             if constexpr (EPI == kMkLatent) {
+              if (t.nt >= 2) {
+                // query columns [192 (nt - 2), +192) of h . Wf in fp32; their row factor is qs
+                float* o = p.qf + static_cast<long long>(r) * mk::QW + mk::QR * (t.nt - 2);
+#pragma unroll 1
+                for (int c = 0; c < mk::QR; c += 32) {
+                    tmem_ld32_nowait(src + c, v);
+                    tmem_wait_ld();
+                    if (live) {
+#pragma unroll
+                        for (int e = 0; e < 8; ++e)
+                            *reinterpret_cast<float4*>(o + c + 4 * e) =
+                                make_float4(v[4 * e], v[4 * e + 1], v[4 * e + 2], v[4 * e + 3]);
+                    }
+                    __syncwarp();
+                }
+              } else {
                 // whole-row norms by one thread: tensor-memory reads in batches of 96 columns
                 // (three 32-column loads per wait)
                 float b3[96];
@@ -327,26 +344,8 @@ __device__ __forceinline__ void mk_gemm_phase(const MkParams& p, const MkPipe& p
                 }
                 const float inv = 1.0f / sqrtf(ss / static_cast<float>(nn) + p.eps);
                 if (t.nt == 0) {
-                    const float* w = p.q_norm[l];
-                    __half* o = p.cq16 + static_cast<long long>(r) * mk::QR;
-                    for (int c = 0; c < mk::QR; c += 96) {
-                        tmem_ld32_nowait(src + c, b3);
-                        tmem_ld32_nowait(src + c + 32, b3 + 32);
-                        tmem_ld32_nowait(src + c + 64, b3 + 64);
-                        tmem_wait_ld();
-                        if (live) {
-#pragma unroll
-                            for (int e = 0; e < 12; ++e) {
-                                const float4 w0 = *reinterpret_cast<const float4*>(w + c + 8 * e);
-                                const float4 w1 = *reinterpret_cast<const float4*>(w + c + 8 * e + 4);
-                                const float* f = b3 + 8 * e;
-                                *reinterpret_cast<uint4*>(o + c + 8 * e) = make_uint4(
-                                    pack_half2(f[0] * inv * w0.x, f[1] * inv * w0.y), pack_half2(f[2] * inv * w0.z, f[3] * inv * w0.w),
-                                    pack_half2(f[4] * inv * w1.x, f[5] * inv * w1.y), pack_half2(f[6] * inv * w1.z, f[7] * inv * w1.w));
-                            }
-                        }
-                        __syncwarp();
-                    }
+                    // the query's row factor (g_q is folded into Wf)
+                    if (live) p.qs[r] = inv;
                 } else {
                     const float* w = p.kv_norm[l];
                     if (live && !in) raise_error(p.err, kErrBadIndex);
@@ -383,6 +382,7 @@ __device__ __forceinline__ void mk_gemm_phase(const MkParams& p, const MkPipe& p
                         __syncwarp();
                     }
                 }
+              }
             } else if constexpr (EPI == kMkGlu) {
                 __half* o = p.gated + static_cast<long long>(r) * mk::DFF + 64 * t.nt;
 #pragma unroll 1
@@ -514,7 +514,7 @@ __device__ __forceinline__ void mk_attention_phase(const MkParams& p, int l, uin
         const int b = it / p.ns, sp = it - b * p.ns;
         decode_attention_item<mk::kAttnStages>(p.qf, cache_l, static_cast<long long>(p.Sc) * mk::KVW, p.pos, b, sp,
                                                p.ns, p.scale, p.ctx16, p.attn_part, p.cos_t, p.sin_t,
-                                               smem + warp * dec::warp_smem<mk::kAttnStages>());
+                                               smem + warp * dec::warp_smem<mk::kAttnStages>(), p.qs);
         if (p.ns > 1) {
             __threadfence();
             __syncwarp();
@@ -580,13 +580,12 @@ __global__ void __launch_bounds__(mk::kThreads, 1) decode_mk_kernel(const __grid
     mk_trace(p, tk);
     if (threadIdx.x == 0) {
         prefetch_tmap(&p.a_h16);
-        prefetch_tmap(&p.a_cq16);
         prefetch_tmap(&p.a_ctx16);
         prefetch_tmap(&p.a_h2);
         prefetch_tmap(&p.a_gated);
         for (int l = 0; l < p.L; ++l) {
             prefetch_tmap(&p.wa[l]);
-            prefetch_tmap(&p.wq[l]);
+            prefetch_tmap(&p.wf[l]);
             prefetch_tmap(&p.wo[l]);
             prefetch_tmap(&p.wgu[l]);
             prefetch_tmap(&p.wdown[l]);
@@ -600,30 +599,27 @@ __global__ void __launch_bounds__(mk::kThreads, 1) decode_mk_kernel(const __grid
             mk_trace(p, tk);
         for (int l = 0; l < p.L; ++l) {
             if (l > 0) mk_prefetch_layer(p, l + 1);
-            mk_gemm_phase<kMkLatent>(p, pp, &p.a_h16, &p.wa[l], 2, mk::D / 64, 1, mk::D / 64, l, prod_it, mma_it, acc_j,
-                                     5 * l);
-            if (!mk_sync(p, epoch, s_abort)) return;
-            mk_trace(p, tk);
-            mk_gemm_phase<kMkF32>(p, pp, &p.a_cq16, &p.wq[l], mk::QW / 128, mk::QR / 64, 1, mk::QR / 64, l, prod_it,
-                                  mma_it, acc_j, 5 * l + 1);
+            // the latent phase also computes the queries (h . Wf; 6 tiles of 192 columns)
+            mk_gemm_phase<kMkLatent>(p, pp, &p.a_h16, &p.wa[l], 2 + mk::QW / mk::QR, mk::D / 64, 1, mk::D / 64, l,
+                                     prod_it, mma_it, acc_j, 4 * l);
             if (!mk_sync(p, epoch, s_abort)) return;
             mk_trace(p, tk);
             mk_attention_phase(p, l, smem);
             if (!mk_sync(p, epoch, s_abort)) return;
             mk_trace(p, tk);
             mk_gemm_phase<kMkPartial>(p, pp, &p.a_ctx16, &p.wo[l], mk::D / 128, mk::HKV / 64, p.ks_o, p.per_o, l,
-                                      prod_it, mma_it, acc_j, 5 * l + 2);
+                                      prod_it, mma_it, acc_j, 4 * l + 1);
             if (!mk_sync(p, epoch, s_abort)) return;
             mk_trace(p, tk);
             mk_rows_phase(p, 1, p.ks_o, p.ffn_norm[l], p.h2);
             if (!mk_sync(p, epoch, s_abort)) return;
             mk_trace(p, tk);
             mk_gemm_phase<kMkGlu>(p, pp, &p.a_h2, &p.wgu[l], (mk::DFF + 63) / 64, mk::D / 64, 1, mk::D / 64, l, prod_it,
-                                  mma_it, acc_j, 5 * l + 3);
+                                  mma_it, acc_j, 4 * l + 2);
             if (!mk_sync(p, epoch, s_abort)) return;
             mk_trace(p, tk);
             mk_gemm_phase<kMkPartial>(p, pp, &p.a_gated, &p.wdown[l], mk::D / 128, (mk::DFF + 63) / 64, p.ks_d, p.per_d,
-                                      l, prod_it, mma_it, acc_j, 5 * l + 4);
+                                      l, prod_it, mma_it, acc_j, 4 * l + 3);
             if (!mk_sync(p, epoch, s_abort)) return;
             mk_trace(p, tk);
             const bool last = l + 1 == p.L;

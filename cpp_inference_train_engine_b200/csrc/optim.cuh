@@ -207,4 +207,52 @@ __global__ void decode_prep_kernel(PrepArgs a) {
     }
 }
 
+// The absorbed query weights in fp32, [qr][H * (kvr + rope)]: per head the nope query folded
+// into the latent (W_uq,nope,h . W_uk,h^T) and the rope query columns, the sums of
+// decode_prep_kernel's Wq before its fp16 rounding. Grid-stride over the entries.
+__global__ void absorbed_wq32_kernel(PrepArgs a, float* __restrict__ wq32) {
+    MM_PDL_ENTRY();
+    const int qk = a.nope + a.rope, kvw = a.kvr + a.rope;
+    const long long n = static_cast<long long>(a.qr) * a.H * kvw;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int r = static_cast<int>(i / (a.H * kvw)), c = static_cast<int>(i % (a.H * kvw));
+        const int h = c / kvw, e = c % kvw;
+        float v;
+        if (e < a.kvr) {
+            float s = 0.f;
+            for (int k = 0; k < a.nope; ++k)
+                s += a.w_uq[r * a.H * qk + h * qk + k] * a.w_uk[e * a.H * a.nope + h * a.nope + k];
+            v = s;
+        } else {
+            v = a.w_uq[r * a.H * qk + h * qk + a.nope + (e - a.kvr)];
+        }
+        wq32[i] = v;
+    }
+}
+
+// The fused decode step's query weights: Wf = W_dq . diag(g_q) . Wq, [d][n] fp16 (row pitch
+// ldf), so that the absorbed query of a row is rms_q^-1 * (h . Wf) with rms_q the q latent's
+// RMS (its RMSNorm is a per-row scalar times diag(g_q)). fp32 sums over k in order; 16 x 16
+// output tiles with their operand tiles in shared memory. grid (ceil(n / 16), ceil(d / 16)).
+__global__ void fold_wq_kernel(const float* __restrict__ w_dq, const float* __restrict__ g_q,
+                               const float* __restrict__ wq32, int d, int qr, int n, __half* __restrict__ wf,
+                               int ldf) {
+    MM_PDL_ENTRY();
+    __shared__ float sa[16][17], sb[16][17];
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+    const int row = blockIdx.y * 16 + ty, col = blockIdx.x * 16 + tx;
+    float acc = 0.f;
+    for (int k0 = 0; k0 < qr; k0 += 16) {
+        const int ka = k0 + tx, kb = k0 + ty;
+        sa[ty][tx] = (row < d && ka < qr) ? w_dq[static_cast<long long>(row) * qr + ka] * g_q[ka] : 0.f;
+        sb[ty][tx] = (kb < qr && col < n) ? wq32[static_cast<long long>(kb) * n + col] : 0.f;
+        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < 16; ++k) acc += sa[ty][k] * sb[k][tx];
+        __syncthreads();
+    }
+    if (row < d && col < n) wf[static_cast<long long>(row) * ldf + col] = __float2half_rn(acc);
+}
+
 } // namespace mm

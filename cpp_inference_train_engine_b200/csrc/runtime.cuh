@@ -210,6 +210,7 @@ struct DecodeState {
     int* active;              // [B] serving: 1 for slots holding a request
     // fused decode step (decode_mk_kernel): split-K partials [6][B][d], per-row attention
     // arrival counters [B] (zero between uses) and the grid barrier's arrival counter
+    float* mk_qs = nullptr;   // [B] the fused step's query row factor (q-latent RMSNorm scale)
     float* mk_part = nullptr;
     int* mk_cnt = nullptr;
     unsigned* mk_bar = nullptr;
@@ -234,6 +235,9 @@ struct DecodeState {
 struct PrepLayer {
     __half *Wa, *Wq, *Wo, *Wgu;
     int lda, ldq, ldo, ldgu;
+    // the fused decode step's query weights W_dq . diag(g_q) . Wq [d][ldf] (its shape only)
+    __half* Wf = nullptr;
+    int ldf = 0;
 };
 
 // Device-time accounting while profiling is on: event pairs recorded on the context's
@@ -278,6 +282,7 @@ class Context {
     mm_adamw_desc opt{0.9f, 0.95f, 1e-8f, 0.1f, 1.0f};
     uint64_t steps = 0;
     cudaStream_t stream = nullptr;
+    float* wq32 = nullptr;  // [qr][H * kvw] scratch of the query-weight fold (fused decode shape only)
     std::string last_error;
     bool unusable = false;
     long long launches = 0;

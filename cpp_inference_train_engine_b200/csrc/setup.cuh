@@ -2,8 +2,16 @@
 // weight copies.
 #pragma once
 #include "runtime.cuh"
+#include "decode_mk.cuh"
 
 namespace mm {
+
+// The model shape the fused decode step (decode_mk_kernel) is built for: the 35.8M model.
+inline bool mk_shape(const Dims& c) {
+    return c.d == mk::D && c.qr == mk::QR && c.kvr == mk::KVR && c.rope == mk::ROPE && c.H == mk::H &&
+           c.dff == mk::DFF && c.L <= mk::kMaxLayers && c.nope + c.rope == 64;
+}
+
 
 // out[r][c] += alpha * (*alpha_ptr) * sum_z part[z][r][c], z in order (deterministic
 // split-K); split z's partial starts at part + z * split_stride.
@@ -308,7 +316,12 @@ inline void create_context(Context& cx, const mm_model_desc& desc, int device, b
             p.Wq = a.template take<__half>(static_cast<long long>(c.qr) * ldq);
             p.Wo = a.template take<__half>(static_cast<long long>(c.H) * c.kvr * ldo);
             p.Wgu = a.template take<__half>(2LL * c.d * ldgu);  // [hi; lo] rows
+            if (mk_shape(c)) {
+                p.ldf = static_cast<int>(round_up(static_cast<long long>(c.H) * c.kvw(), 8));
+                p.Wf = a.template take<__half>(static_cast<long long>(c.d) * p.ldf);
+            }
         }
+        if (mk_shape(c)) cx.wq32 = a.template take<float>(static_cast<long long>(c.qr) * c.H * c.kvw());
     };
     Sizer sz;
     plan(sz);
@@ -385,6 +398,14 @@ inline void refresh_derived(Context& cx, bool shadows) {
         a.H = c.H; a.dff = c.dff;
         launch_k(cx.stream, decode_prep_kernel, dim3(592), dim3(256), 0, a);
         ++cx.launches;
+        if (p.Wf) {  // the fused decode step's query weights, from the fp32 sums
+            const int n = c.H * c.kvw();
+            launch_k(cx.stream, absorbed_wq32_kernel, dim3(148), dim3(256), 0, a, cx.wq32);
+            launch_k(cx.stream, fold_wq_kernel, dim3((n + 15) / 16, (c.d + 15) / 16), dim3(256), 0,
+                     (const float*)cx.W(l, kWdq), (const float*)cx.W(l, kQNorm), (const float*)cx.wq32, c.d, c.qr, n,
+                     p.Wf, p.ldf);
+            cx.launches += 2;
+        }
     }
 }
 

@@ -137,25 +137,27 @@ def decode(args):
             if args.trace:
                 raw = ex.decode_trace_raw()
                 ph = ex.decode_trace(0)
-                kinds = ["wa", "wq", "wo", "wgu", "wdown"]
+                # the fused step's four products per layer (the latent phase also makes the
+                # queries) and its seven phases per layer
+                kinds = ["wa", "wo", "wgu", "wdown"]
                 inner = {k: [0.0, 0.0] for k in kinds}
-                for g in range(5 * cfg.n_layers):
+                for g in range(4 * cfg.n_layers):
                     a, b, c = raw[128 + 3 * g: 131 + 3 * g]
                     if a > 0 and b > a and c > b:
-                        inner[kinds[g % 5]][0] += (b - a) / 1e3
-                        inner[kinds[g % 5]][1] += (c - b) / 1e3
+                        inner[kinds[g % 4]][0] += (b - a) / 1e3
+                        inner[kinds[g % 4]][1] += (c - b) / 1e3
                 print(json.dumps({"mode": "decode_trace_inner", "batch": B,
                                   "load_mma_us": {k: round(v[0], 2) for k, v in inner.items()},
                                   "epilogue_us": {k: round(v[1], 2) for k, v in inner.items()}}))
                 names = ["embed"] + [f"{n}{l}" for l in range(cfg.n_layers) for n in
-                                     ("wa", "wq", "attn", "wo", "norm2", "wgu", "wdown", "norm1")]
+                                     ("wa", "attn", "wo", "norm2", "wgu", "wdown", "norm1")]
                 per = {}
                 for n, us in zip(names, ph):
                     key = n.rstrip("0123456789")
                     per[key] = per.get(key, 0.0) + us
                 print(json.dumps({"mode": "decode_trace", "batch": B, "phases": len(ph), "total_us": sum(ph),
                                   "by_kind_us": {k: round(v, 2) for k, v in per.items()},
-                                  "layer0_us": [round(x, 2) for x in ph[1:9]]}))
+                                  "layer0_us": [round(x, 2) for x in ph[1:8]]}))
             ms = prof["decode"][0] + prof["sample"][0]
             steps = args.new - 1
             ctx = args.prompt + (args.new - 1) / 2.0  # mean positions attended per step

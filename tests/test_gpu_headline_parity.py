@@ -15,7 +15,7 @@ path (oracle/_ref) on identical seeded weights and tokens.
   frozen reference seed 1, rewards N(0, 1) in groups of 8: log-probs within 2e-3 absolute,
   loss / KL / gradient norm within 1e-3 relative.
 * Decode after 1,024-token prompts, 128 teacher-forced greedy steps, at 64 rows and at 2,048
-  rows (the size at which the step's vocabulary head and SwiGLU product run on CTA pairs):
+  rows (the size at which the step's vocabulary head runs on CTA pairs):
   the greedy token equals the reference decoder's wherever its top-2 margin exceeds 1e-3.
 """
 import json

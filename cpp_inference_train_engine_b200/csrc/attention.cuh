@@ -126,7 +126,8 @@ __device__ __forceinline__ void decode_attention_item(const float* __restrict__ 
                                                       int sp, int nsplit, float scale, __half* __restrict__ ctx,
                                                       float* __restrict__ part, const float* __restrict__ cos_t,
                                                       const float* __restrict__ sin_t, unsigned char* mine,
-                                                      const float* __restrict__ qrow = nullptr) {
+                                                      const float* __restrict__ qrow = nullptr,
+                                                      unsigned long long* stamps = nullptr) {
     using namespace dec;
     using fa::ldsm_x4;
     using fa::ldsm_x4_t;
@@ -158,27 +159,46 @@ __device__ __forceinline__ void decode_attention_item(const float* __restrict__ 
     for (int j = 0; j < STAGES - 1; ++j) issue(j);
     // the row's absorbed queries, pre-scaled into the base-2 domain (and by the row factor
     // qrow[b] when the queries come unnormalised), as fp16
-    const float qscale = scale * fa::kLog2e * (qrow ? __ldcg(qrow + b) : 1.f);
     const float4* q4 = reinterpret_cast<const float4*>(qf + static_cast<long long>(b) * H * W);
     const int p = n - 1;  // position of this step's token
-    for (int e = lane; e < H * W / 4; e += 32) {
-        float4 v = __ldcg(q4 + e);
-        const int hh = (4 * e) / W, c = (4 * e) % W;
-        if (cos_t && c >= KV) {  // adjacent-pair RoPE of the rope query (rope_rows_kernel's arithmetic)
-            float* f = reinterpret_cast<float*>(&v);
+    // every load first (the lane's 9 query float4s, the row factor and the rope tables its rope
+    // float4 needs), so they are in flight together, then the rotation and the fp16 stores
+    constexpr int NQ = H * W / 4 / 32;
+    static_assert(H * W / 4 == NQ * 32, "whole float4s per lane");
+    float4 v[NQ];
+    float cs[NQ][2], sn[NQ][2];
 #pragma unroll
-            for (int k = 0; k < 4; k += 2) {
-                const int pair = (c - KV + k) >> 1;
-                const float cs = cos_t[p * (R / 2) + pair], sn = sin_t[p * (R / 2) + pair];
-                const float a = f[k], bb = f[k + 1];
-                f[k] = a * cs - bb * sn;
-                f[k + 1] = a * sn + bb * cs;
+    for (int i = 0; i < NQ; ++i) v[i] = __ldcg(q4 + lane + 32 * i);
+    const float qscale = scale * fa::kLog2e * (qrow ? __ldcg(qrow + b) : 1.f);
+#pragma unroll
+    for (int i = 0; i < NQ; ++i) {
+        const int c = (4 * (lane + 32 * i)) % W;
+        const bool rope = cos_t && c >= KV;
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const int pair = rope ? (c - KV) / 2 + k : 0;
+            cs[i][k] = rope ? cos_t[p * (R / 2) + pair] : 1.f;
+            sn[i][k] = rope ? sin_t[p * (R / 2) + pair] : 0.f;
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < NQ; ++i) {
+        const int e = lane + 32 * i;
+        const int hh = (4 * e) / W, c = (4 * e) % W;
+        float* f = reinterpret_cast<float*>(&v[i]);
+        if (cos_t && c >= KV) {  // adjacent-pair RoPE of the rope query (rope_rows_kernel's arithmetic)
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+                const float a = f[2 * k], bb = f[2 * k + 1];
+                f[2 * k] = a * cs[i][k] - bb * sn[i][k];
+                f[2 * k + 1] = a * sn[i][k] + bb * cs[i][k];
             }
         }
-        *reinterpret_cast<__half2*>(&Qs[hh][c]) = __floats2half2_rn(v.x * qscale, v.y * qscale);
-        *reinterpret_cast<__half2*>(&Qs[hh][c + 2]) = __floats2half2_rn(v.z * qscale, v.w * qscale);
+        *reinterpret_cast<__half2*>(&Qs[hh][c]) = __floats2half2_rn(f[0] * qscale, f[1] * qscale);
+        *reinterpret_cast<__half2*>(&Qs[hh][c + 2]) = __floats2half2_rn(f[2] * qscale, f[3] * qscale);
     }
     __syncwarp();
+    if (stamps && lane == 0) asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(stamps[0]));
     uint32_t qb[W / 16][2];
 #pragma unroll
     for (int kk = 0; kk < W / 16; ++kk) {
@@ -244,6 +264,7 @@ __device__ __forceinline__ void decode_attention_item(const float* __restrict__ 
         __syncwarp();
     }
     cp_async_wait<0>();
+    if (stamps && lane == 0) asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(stamps[1]));
 #pragma unroll
     for (int o = 4; o < 32; o <<= 1) {
         l0 += __shfl_xor_sync(0xffffffffu, l0, o);

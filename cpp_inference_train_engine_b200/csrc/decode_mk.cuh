@@ -207,6 +207,9 @@ __device__ __forceinline__ void mk_stamp(const MkParams& p, int slot) {
 // Trace slots of the GEMM phases' inner stamps (CTA 0's first unit): per GEMM phase g,
 // [kMkStampBase + 3 g] producer start, + 1 accumulator ready (epilogue), + 2 epilogue done.
 constexpr int kMkStampBase = 128;
+// Trace slots of the attention phases: per layer l, [kMkAttnStamp + 4 l] CTA 0 warp 0's first
+// item starts, + 1 its queries are in registers, + 2 its cache tiles are done, + 3 merged.
+constexpr int kMkAttnStamp = 256;
 
 template <int EPI>
 __device__ __forceinline__ void mk_gemm_phase(const MkParams& p, const MkPipe& pp, const CUtensorMap* ta,
@@ -512,9 +515,14 @@ __device__ __forceinline__ void mk_attention_phase(const MkParams& p, int l, uin
     const int items = p.B * p.ns;
     for (int it = blockIdx.x * mk::kWarps + warp; it < items; it += gridDim.x * mk::kWarps) {
         const int b = it / p.ns, sp = it - b * p.ns;
+        // trace: CTA 0's warp 0 stamps its first item (start, queries ready, tiles done, merged)
+        unsigned long long* st = (p.trace && blockIdx.x == 0 && warp == 0 && it == 0) ? p.trace + kMkAttnStamp + 4 * l
+                                                                                        : nullptr;
+        if (st && lane == 0) asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(st[0]));
         decode_attention_item<mk::kAttnStages>(p.qf, cache_l, static_cast<long long>(p.Sc) * mk::KVW, p.pos, b, sp,
                                                p.ns, p.scale, p.ctx16, p.attn_part, p.cos_t, p.sin_t,
-                                               smem + warp * dec::warp_smem<mk::kAttnStages>(), p.qs);
+                                               smem + warp * dec::warp_smem<mk::kAttnStages>(), p.qs,
+                                               st ? st + 1 : nullptr);
         if (p.ns > 1) {
             __threadfence();
             __syncwarp();
@@ -527,6 +535,7 @@ __device__ __forceinline__ void mk_attention_phase(const MkParams& p, int l, uin
                 if (lane == 0) atomicExch(p.attn_cnt + b, 0);
             }
         }
+        if (st && lane == 0) asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(st[3]));
         __syncwarp();
     }
     // the warps' generic shared-memory use ends before the next phase's TMA writes there

@@ -146,6 +146,17 @@ def decode(args):
                     if a > 0 and b > a and c > b:
                         inner[kinds[g % 4]][0] += (b - a) / 1e3
                         inner[kinds[g % 4]][1] += (c - b) / 1e3
+                # the attention phases: CTA 0 warp 0's first item per layer
+                att = [0.0, 0.0, 0.0]
+                for l in range(cfg.n_layers):
+                    st = raw[256 + 4 * l: 260 + 4 * l]
+                    if len(st) == 4 and all(x > 0 for x in st) and st[0] <= st[1] <= st[2] <= st[3]:
+                        for k in range(3):
+                            att[k] += (st[k + 1] - st[k]) / 1e3
+                print(json.dumps({"mode": "decode_trace_attention", "batch": B,
+                                  "us_over_layers": {"to_queries_ready": round(att[0], 2),
+                                                     "cache_tiles": round(att[1], 2),
+                                                     "partial_and_merge": round(att[2], 2)}}))
                 print(json.dumps({"mode": "decode_trace_inner", "batch": B,
                                   "load_mma_us": {k: round(v[0], 2) for k, v in inner.items()},
                                   "epilogue_us": {k: round(v[1], 2) for k, v in inner.items()}}))

@@ -500,7 +500,9 @@ class CudaExecution:
 
     def decode_trace_raw(self):
         """The raw timestamps (ns) of the last traced fused decode step: [0, 128) start, barriers,
-        end; [128, 320) per GEMM phase g: producer start, accumulator ready, epilogue done."""
+        end; [128, 256) per GEMM phase g: producer start, accumulator ready, epilogue done;
+        [256, 320) per layer l (4 l): CTA 0 warp 0's first attention item starts, its queries are
+        ready, its cache tiles are done, its row is merged."""
         buf = np.zeros(320, np.uint64)
         n = ctypes.c_int32()
         self._check(lib().mm_cuda_decode_trace(self.h, -1, _p(buf, _u64p), buf.size, ctypes.byref(n)))

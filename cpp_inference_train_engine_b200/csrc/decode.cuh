@@ -182,9 +182,11 @@ inline void launch_decode_mk(Context& cx) {
     p.B = B;
     p.L = c.L;
     p.Sc = d.Sc;
-    // context splits: as many as keep every (row, split) item in one wave of the grid's warps
-    // (about two 16-position tiles per split)
-    p.ns = std::max(1, std::min(std::min(kMaxDecodeSplits, G * mk::kWarps / B), (cx.dec_len + 1 + 31) / 32));
+    // context splits: as many as keep every (row, split) item within half the grid's warps (at
+    // least two 16-position tiles per split): the merge of the splits costs more than the
+    // longer per-item tile loop (512 rows, 128 + 64 tokens: 0.675 ms per step with 1 split per
+    // row, 0.694 with 2; 64 and 256 rows unchanged)
+    p.ns = std::max(1, std::min(std::min(kMaxDecodeSplits, G * mk::kWarps / (2 * B)), (cx.dec_len + 1 + 31) / 32));
     // K splits of the residual products: about one wave of (split, m-tile, n-tile) units
     const int MT = (B + 127) / 128;
     auto pick = [&](int nk, int maxks, int& ks, int& per) {
